@@ -1,0 +1,262 @@
+/*
+ * up_sm100.h — C ABI of libunpopped_sm100.so, the sm_100a (B200) execution backend for Unpopped's lifted
+ * kernel families: row reductions (sum, max, argmax), inclusive/exclusive scans, row gather, int4
+ * group-wise dequant and the W4A16 GEMM.
+ *
+ * The reference (Unpopped, Rust) has no execution step of its own: its `Backend` trait
+ * (crates/unpopped/src/backend.rs:668-835) lowers a `KernelPlan` to kernel source and its oracle
+ * (crates/unpopped/src/oracle/plan_eval.rs) evaluates plans on the CPU. This library is what a Rust
+ * `unpopped-cuda-sm100` crate binds through `extern "C"`: the dtype answer of `Backend::supports_dtype`
+ * (backend.rs:779), the plan classification behind `Backend::lower` (backend.rs:708) and the launch of
+ * the kernel the plan lowered to, on caller-owned device buffers.
+ *
+ * Conventions
+ *  - Every entry point returns an `up_status` (an int). 0 is success. Values 1 and 2 follow the C ABI the
+ *    reference's C99 emitter gives its kernels (crates/unpopped-cpu-c/src/kernel.rs:7-18: 1 = out of
+ *    bounds, 2 = zero step); the rest extend it. No entry point aborts or traps on caller input.
+ *  - Pointers are device pointers unless a parameter says "host". Launches are stream-ordered on the
+ *    `stream` argument (a cudaStream_t; NULL is the legacy default stream) and return once enqueued.
+ *  - Device-side waits (scan look-back, split-K fix-up) are bounded. A wait that runs out sets an error
+ *    word in the caller's workspace; `up_sm100_workspace_status` reports it as UP_ERR_DEVICE_TIMEOUT.
+ *  - Elements are addressed as `ptr + base + sum(coord[d] * stride[d])`, in elements, as in the
+ *    reference's `TypedBuffer` (crates/unpopped/src/oracle/buffers.rs:16) and the C99 emitter's buffer
+ *    arguments (crates/unpopped-cpu-c/src/base.rs:81-86).
+ */
+#ifndef UP_SM100_H
+#define UP_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define UP_SM100_ABI_VERSION 1
+#define UP_MAX_RANK 8
+
+/* Status codes. */
+typedef enum up_status {
+  UP_OK = 0,
+  UP_ERR_OOB = 1,              /* an extent or offset leaves its buffer (cpu-c ABI value 1) */
+  UP_ERR_ZERO_STEP = 2,        /* a zero loop step (cpu-c ABI value 2) */
+  UP_ERR_UNSUPPORTED = 3,      /* the backend declines this dtype / shape / op (LowerError) */
+  UP_ERR_DEVICE_TIMEOUT = 4,   /* a bounded device-side wait ran out */
+  UP_ERR_CUDA = 5,             /* a CUDA runtime/driver call failed */
+  UP_ERR_COMM = 6,             /* a collective failed */
+  UP_ERR_INVALID = 7           /* a null pointer, a negative extent or a too-small workspace */
+} up_status;
+
+/* ElementKind, by ordinal in the reference enum (crates/unpopped-vocab/src/element.rs:1052-1206). */
+typedef enum up_element_kind {
+  UP_EK_F16 = 0, UP_EK_BF16 = 1, UP_EK_F32 = 2, UP_EK_F32_STRICT = 3, UP_EK_F64 = 4,
+  UP_EK_I8 = 5, UP_EK_I16 = 6, UP_EK_U8 = 7, UP_EK_U16 = 8, UP_EK_I32 = 9, UP_EK_I64 = 10,
+  UP_EK_BOOL = 11, UP_EK_FP8_E4M3FN = 12, UP_EK_FP8_E4M3FNUZ = 13, UP_EK_FP8_E5M2 = 14,
+  UP_EK_F8_E8M0 = 15, UP_EK_F8_E6M2 = 16, UP_EK_FP8_E5M2FNUZ = 17, UP_EK_I4 = 18, UP_EK_U4 = 19,
+  UP_EK_B1 = 20, UP_EK_COMPLEX64 = 21, UP_EK_COMPLEX128 = 22, UP_EK_U32 = 23, UP_EK_U64 = 24,
+  UP_EK_F4_E2M1 = 25, UP_EK_F6_E2M3 = 26, UP_EK_F6_E3M2 = 27,
+  UP_EK_COUNT = 28
+} up_element_kind;
+
+/* ReduceOp, by ordinal in the reference enum (crates/unpopped/src/ir.rs:1700-1742). */
+typedef enum up_reduce_op {
+  UP_OP_SUM = 0, UP_OP_MEAN = 1, UP_OP_MAX = 2, UP_OP_MIN = 3, UP_OP_PROD = 4, UP_OP_AND = 5,
+  UP_OP_OR = 6, UP_OP_XOR = 7, UP_OP_MAXNUM = 8, UP_OP_MINNUM = 9, UP_OP_ARGMAX = 10, UP_OP_ARGMIN = 11
+} up_reduce_op;
+
+/* OobPolicy (crates/unpopped/src/ir.rs:2582-2599): what an out-of-range gather index writes. The load
+ * address is always clamped in range; the policy only decides the store. */
+typedef enum up_oob_policy { UP_OOB_SKIP = 0, UP_OOB_CLAMP = 1, UP_OOB_ZERO_FILL = 2 } up_oob_policy;
+
+/* Accumulation policy of a float Sum (crates/unpopped/src/ir.rs:2447-2476, docs/accum-policies.md).
+ *  UP_ACCUM_AUTO: f64 accumulator in the launched lift's documented order (logical thread t of a block of
+ *                 B folds t, t+B, t+2B, ... ascending; then acc[t] += acc[t+s] for s = B/2 .. 1; one
+ *                 rounding at the store) — crates/unpopped/src/kernel_lift/block_reduce.rs:13-23.
+ *                 Bit-exact and reproducible for a given B.
+ *  UP_ACCUM_F32:  f32 accumulator in this library's fixed order (deterministic; error <= 2^-20 sum|x|). */
+typedef enum up_accum { UP_ACCUM_AUTO = 0, UP_ACCUM_F32 = 1 } up_accum;
+
+/* Schedule kind of a plan (crates/unpopped/src/plan/types.rs:14-150), plus the kernel-layer entry
+ * (`Backend::lower_kernel`, backend.rs:726-745) for the dequant GEMM. */
+typedef enum up_schedule {
+  UP_SCHED_VECTORIZED = 0, UP_SCHED_SCALAR = 1, UP_SCHED_STRIDED = 2, UP_SCHED_REDUCTION = 3,
+  UP_SCHED_ROW_REDUCE = 4, UP_SCHED_CONTRACTION = 5, UP_SCHED_SCAN = 6, UP_SCHED_WINDOW = 7,
+  UP_SCHED_KERNEL_FN = 100
+} up_schedule;
+
+/* Kernel ids: what `up_sm100_classify` maps a plan to and `up_sm100_launch` runs. */
+typedef enum up_kernel_id {
+  UP_K_NONE = -1,
+  UP_K_ROW_SUM_F32 = 1,
+  UP_K_ROW_MAX_ARGMAX_BF16 = 2,
+  UP_K_SCAN_I32 = 3,
+  UP_K_GATHER_ROWS = 4,
+  UP_K_DEQUANT_I4 = 5,
+  UP_K_W4A16_GEMM = 6
+} up_kernel_id;
+
+/* A buffer argument: the reference's TypedBuffer / OperandDesc. `base` and `stride` count elements
+ * (for I4/U4: nibbles; packing is two per byte, low nibble = even index, tests/sub_byte_packing.rs:24-40). */
+typedef struct up_tensor {
+  void* ptr;
+  int32_t dtype; /* up_element_kind */
+  int32_t rank;
+  int64_t shape[UP_MAX_RANK];
+  int64_t stride[UP_MAX_RANK];
+  int64_t base;
+} up_tensor;
+
+/* The parts of a reference `KernelPlan` (plan/types.rs:170-270) the classifier reads. */
+typedef struct up_plan_desc {
+  int32_t schedule;      /* up_schedule */
+  int32_t op;            /* up_reduce_op: the Reduction / Scan op */
+  int32_t dtype;         /* plan.dtype, the compute dtype */
+  int32_t out_dtype;     /* plan.out_dtype (ArgMax requires I64; I32 is this library's extension) */
+  uint32_t axes_mask;    /* Reduction axes; 0 = the legacy last-axis default (ir.rs:2094-2097) */
+  int32_t keepdim;
+  int32_t identity_body; /* 1 when the body is Input(0) and the post is Reduced(0) */
+  int32_t accum;         /* up_accum for a float Sum */
+  int32_t scan_axis;     /* Scan: the scanned axis */
+  int32_t exclusive;     /* Scan */
+  int32_t reverse;       /* Scan */
+  int32_t has_read_index;/* Strided with a data-dependent read (a gather) */
+  int32_t gather_axis;   /* ReadIndex::Indexed{axis} (ir.rs:2620-2669) */
+  int32_t oob;           /* up_oob_policy */
+  int32_t index_dtype;   /* up_element_kind of the index operand */
+  int32_t n_operands;    /* inputs then outputs, at most 8 */
+  up_tensor operands[8]; /* shapes/strides/dtypes only; ptr may be NULL */
+  char target[32];       /* TargetId token, e.g. "cuda:sm_100a" or "cuda:sm100a" */
+} up_plan_desc;
+
+/* What `Backend::lower` returns (`GeneratedKernel{name, source}` + launch metadata), or why it refused
+ * (`LowerError`, backend.rs:386-440). */
+typedef enum up_lower_error {
+  UP_LOWER_OK = 0, UP_LOWER_UNSUPPORTED_DTYPE = 1, UP_LOWER_UNSUPPORTED_SCHEDULE = 2,
+  UP_LOWER_UNSUPPORTED_OP = 3, UP_LOWER_UNSUPPORTED_PLAN_SHAPE = 4, UP_LOWER_INADMISSIBLE_PLAN = 5,
+  UP_LOWER_UNSUPPORTED_KERNEL = 6
+} up_lower_error;
+
+typedef struct up_lowered {
+  int32_t kernel_id;     /* up_kernel_id */
+  int32_t lower_error;   /* up_lower_error */
+  char name[64];         /* entry symbol, e.g. "up_sm100_scan_i32" */
+  char detail[160];      /* the refusal's detail text */
+  int64_t scalars[8];    /* launch scalars `up_sm100_launch` expects for this kernel */
+  int32_t n_scalars;
+} up_lowered;
+
+/* ---- Backend seam ------------------------------------------------------------------------------- */
+
+/* UP_SM100_ABI_VERSION of the loaded library. */
+int up_sm100_version(void);
+
+/* `Backend::name` / `Backend::provider` (backend.rs:668-690): "cuda_sm100" / "unpopped-cuda-sm100". */
+const char* up_sm100_name(void);
+const char* up_sm100_provider(void);
+
+/* `Backend::supports_dtype(dtype, target)` (backend.rs:779): 0 Supported, 1 Unsupported,
+ * 2 NotExpressible (DtypeSupport, backend.rs:645-666). Targets "cuda:sm_100a" and "cuda:sm100a" (and
+ * "cuda:sm100") are this backend's; any other target answers Unsupported. */
+int up_sm100_supports_dtype(int dtype, const char* target);
+
+/* `Backend::lower` (backend.rs:708) restricted to what this backend maps: fills `out` with the kernel id,
+ * entry symbol and launch scalars, or with the LowerError that refuses the plan. Returns UP_OK when a
+ * kernel was chosen, UP_ERR_UNSUPPORTED when the plan is refused, UP_ERR_INVALID on a null argument. */
+int up_sm100_classify(const up_plan_desc* plan, up_lowered* out);
+
+/* ---- Generic launch ------------------------------------------------------------------------------ */
+
+/* Workspace bytes `up_sm100_launch(id, ...)` needs (0 when none). The workspace must be zero-filled
+ * once before its first use (`cudaMemset`); the kernels leave it ready for the next launch. */
+int up_sm100_workspace_bytes(int kernel_id, const up_tensor* ins, int n_in, const up_tensor* outs,
+                             int n_out, const int64_t* scalars, int n_scalars, size_t* bytes);
+
+/* Launch kernel `kernel_id` on tensor descriptors. Operand order and scalars per kernel:
+ *  ROW_SUM_F32:          ins {x f32 [rows, cols]}, outs {sum f32 [rows]};
+ *                        scalars {accum (up_accum), block B (AUTO only; power of two, 1..1024)}
+ *  ROW_MAX_ARGMAX_BF16:  ins {x bf16 [rows, cols]}, outs {max f32 [rows] | ptr NULL,
+ *                        argmax i32 or i64 [rows] | ptr NULL}
+ *  SCAN_I32:             ins {x i32 [rows, k]}, outs {y i32 [rows, k]};
+ *                        scalars {op (SUM|MAX|MIN), exclusive, reverse}
+ *  GATHER_ROWS:          ins {table [V, D] (any dtype), ids i32/i64/u32 [N]}, outs {out [N, D]};
+ *                        scalars {oob (up_oob_policy)}
+ *  DEQUANT_I4:           ins {w i4 [N, K], scale f16 [N, K/group]}, outs {out bf16 [N, K]};
+ *                        scalars {group}
+ *  W4A16_GEMM:           ins {w i4 [N, K], scale f16 [N, K/group], x bf16 [M, K]},
+ *                        outs {out bf16 [M, N]}; scalars {group}
+ */
+int up_sm100_launch(int kernel_id, const up_tensor* ins, int n_in, const up_tensor* outs, int n_out,
+                    const int64_t* scalars, int n_scalars, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+/* Waits for `stream`, then reads and clears the device error word of a workspace: UP_OK, or
+ * UP_ERR_DEVICE_TIMEOUT when a bounded wait ran out during an earlier launch on it. */
+int up_sm100_workspace_status(void* workspace, void* stream);
+
+/* ---- Typed entry points (what the generic launch dispatches to) ------------------------------------ */
+
+/* Row sum of a row-major f32 matrix (`ReduceOp::Sum` over the last axis, `Access::Reduction`,
+ * ir.rs:2080-2135; oracle fold oracle/plan_eval.rs:501-651). `row_stride` in elements (>= cols). */
+int up_sm100_row_sum_f32(const float* x, int64_t rows, int64_t cols, int64_t row_stride, float* out,
+                         int accum, int block, void* stream);
+
+/* Row max and argmax of a row-major bf16 matrix: Max is NaN-propagating (oracle/plan_contract.rs:179-210),
+ * ArgMax is the first index of the extreme with NaN the greatest value (plan_contract.rs:213-245).
+ * Either output may be NULL; `argmax_i64` and `argmax_i32` may both be given. */
+int up_sm100_row_max_argmax_bf16(const uint16_t* x, int64_t rows, int64_t cols, int64_t row_stride,
+                                 float* max_out, int32_t* argmax_i32, int64_t* argmax_i64, void* stream);
+
+/* Scan of `rows` independent rows of `k` int32 (`Access::Scan`, ir.rs:2153-2195; oracle
+ * oracle/plan_window.rs:10-238): op SUM (wrapping), MAX or MIN; `exclusive` writes the prefix before
+ * the element (the first is the identity: 0, INT32_MIN, INT32_MAX); `reverse` runs from the row's end.
+ * `carry_in` (device pointer to one int32, or NULL) is combined in front of every row — the carry of a
+ * scan sharded over several GPUs. Single-pass decoupled look-back; `workspace` from
+ * up_sm100_scan_workspace_bytes, zero-filled before its first use. */
+int up_sm100_scan_i32(const int32_t* x, int32_t* y, int64_t rows, int64_t k, int op, int exclusive,
+                      int reverse, const int32_t* carry_in, void* workspace, size_t workspace_bytes,
+                      void* stream);
+size_t up_sm100_scan_workspace_bytes(int64_t rows, int64_t k);
+
+/* Fold of a whole int32 array to one value (the first pass of a scan sharded over GPUs): SUM (wrapping),
+ * MAX or MIN, written to `total` (device, one int32). Deterministic. */
+int up_sm100_reduce_i32(const int32_t* x, int64_t n, int op, int32_t* total, void* stream);
+
+/* Row gather `out[n, :] = table[ids[n], :]` (ReadIndex::Indexed on axis 0, ir.rs:2620-2669; oracle
+ * oracle/plan_eval.rs:363-385): the row is copied bit for bit; an id outside [0, table_rows) writes
+ * nothing (SKIP), zeros (ZERO_FILL) or the clamped row (CLAMP). `row_bytes` is the row size in bytes;
+ * `index_dtype` is UP_EK_I32, UP_EK_I64 or UP_EK_U32. */
+int up_sm100_gather_rows(const void* table, int64_t table_rows, int64_t row_bytes, const void* ids,
+                         int index_dtype, int64_t n, int oob, void* out, void* stream);
+
+/* Group-wise int4 dequant: out[n][k] = bf16(w[n][k] * scale[n][k / group]) with one rounding (RNE).
+ * `w` is [N, K] i4 packed two per byte along K (low nibble first), `scale` f16 [N, K/group]. */
+int up_sm100_dequant_i4_bf16(const uint8_t* w, const uint16_t* scale, int64_t n, int64_t k,
+                             int64_t group, uint16_t* out, void* stream);
+
+/* W4A16 GEMM: out[m][n] = bf16( sum_k x[m][k] * w[n][k] * scale[n][k / group] ), f32 accumulation on
+ * the tcgen05 tensor cores (TMEM accumulator, per-group scale applied in f32). `x` bf16 [M, K]
+ * row-major, `out` bf16 [M, N] row-major, M <= 16 per call tile, K % group == 0, group % 128 == 0,
+ * N % 128 == 0. `workspace` from up_sm100_w4a16_workspace_bytes (split-K partials and counters),
+ * zero-filled before its first use. */
+int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, const uint16_t* x, int64_t m,
+                        int64_t n, int64_t k, int64_t group, uint16_t* out, void* workspace,
+                        size_t workspace_bytes, void* stream);
+size_t up_sm100_w4a16_workspace_bytes(int64_t m, int64_t n, int64_t k, int64_t group);
+
+/* ---- Test and tuning hooks ----------------------------------------------------------------------- */
+
+/* Bound, in nanoseconds, of every device-side wait (default 1e9). */
+void up_sm100_set_wait_limit_ns(uint64_t ns);
+/* When nonzero, the next scan launches make tile 0 withhold its look-back flag, so every other tile's wait
+ * runs out: the host-visible error path of a bounded wait, without hanging or faulting the GPU. */
+void up_sm100_set_test_withhold_flag(int enable);
+/* Number of kernels this library has launched since load (all entry points). */
+uint64_t up_sm100_launch_count(void);
+/* Last CUDA error text seen by the library (static storage). */
+const char* up_sm100_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* UP_SM100_H */

@@ -1,0 +1,208 @@
+"""ctypes wrapper of the CPU oracle restatement (``up_oracle.c``).
+
+TEST INFRASTRUCTURE ONLY: the parity tests, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
+leg use it as the checker (and the timed CPU baseline). The product library never imports it.
+All arrays are numpy; raw bf16/f16 travel as ``uint16``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liborc.so")
+
+OP_SUM, OP_MAX, OP_MIN = 0, 2, 3
+OOB_SKIP, OOB_CLAMP, OOB_ZERO_FILL = 0, 1, 2
+EK_I32, EK_I64, EK_U32 = 9, 10, 23
+
+_lib = None
+
+
+def build(force: bool = False) -> str:
+    """Compile liborc.so with the committed Makefile (gcc, strict FP, OpenMP)."""
+    if force or not os.path.exists(_LIB_PATH) or (
+        os.path.getmtime(_LIB_PATH) < os.path.getmtime(os.path.join(_HERE, "up_oracle.c"))
+    ):
+        subprocess.run(["make", "-s", "-C", _HERE, "liborc.so"], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        L = ctypes.CDLL(_LIB_PATH)
+        P, I64, I = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+        L.orc_row_sum_f32.argtypes = [P, I64, I64, I64, P, I]
+        L.orc_row_sum_f32_documented.argtypes = [P, I64, I64, I64, I64, P, I]
+        L.orc_row_max_argmax_bf16.argtypes = [P, I64, I64, I64, P, P, I]
+        L.orc_scan_i32.argtypes = [P, P, I64, I64, I, I, I, ctypes.c_int32, I]
+        L.orc_scan_i32_chunked.argtypes = [P, P, I64, I, I, I]
+        L.orc_reduce_i32.argtypes = [P, I64, I]
+        L.orc_reduce_i32.restype = ctypes.c_int32
+        L.orc_scan_identity_i32.argtypes = [I]
+        L.orc_scan_identity_i32.restype = ctypes.c_int32
+        L.orc_gather_rows.argtypes = [P, I64, I64, P, I, I64, I, P, I]
+        L.orc_dequant_i4_bf16.argtypes = [P, P, I64, I64, I64, P, I]
+        L.orc_w4a16.argtypes = [P, P, P, I64, I64, I64, I64, P, P, P, I]
+        L.orc_dequant_gemm_kat.argtypes = [P, I, P, P, P, I64, I64, I64, I64, P]
+        L.orc_f32_to_bf16.argtypes = [ctypes.c_float]
+        L.orc_f32_to_bf16.restype = ctypes.c_uint16
+        L.orc_f64_to_bf16.argtypes = [ctypes.c_double]
+        L.orc_f64_to_bf16.restype = ctypes.c_uint16
+        L.orc_f32_to_f16.argtypes = [ctypes.c_float]
+        L.orc_f32_to_f16.restype = ctypes.c_uint16
+        L.orc_f16_to_f64.argtypes = [ctypes.c_uint16]
+        L.orc_f16_to_f64.restype = ctypes.c_double
+        L.orc_bf16_to_f64.argtypes = [ctypes.c_uint16]
+        L.orc_bf16_to_f64.restype = ctypes.c_double
+        L.orc_f64_to_f32_odd.argtypes = [ctypes.c_double]
+        L.orc_f64_to_f32_odd.restype = ctypes.c_float
+        L.orc_i4_value.argtypes = [P, I64]
+        L.orc_i4_value.restype = I
+        L.orc_max_threads.restype = I
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"], "oracle inputs must be C-contiguous"
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def max_threads() -> int:
+    return int(lib().orc_max_threads())
+
+
+def row_sum_f32(x: np.ndarray, threads: int = 1) -> np.ndarray:
+    """Serial f64 fold, one rounding (oracle/plan_eval.rs:501-651)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, cols = x.shape
+    out = np.empty(rows, np.float32)
+    lib().orc_row_sum_f32(_p(x), rows, cols, cols, _p(out), threads)
+    return out
+
+
+def row_sum_f32_documented(x: np.ndarray, block: int, threads: int = 1) -> np.ndarray:
+    """The launched lift's documented f64 order for a block of ``block`` threads."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, cols = x.shape
+    out = np.empty(rows, np.float32)
+    lib().orc_row_sum_f32_documented(_p(x), rows, cols, cols, block, _p(out), threads)
+    return out
+
+
+def row_max_argmax_bf16(x_bits: np.ndarray, threads: int = 1):
+    """(max as f32, argmax as i64) per row of a bf16 matrix given as uint16 bits."""
+    x = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    rows, cols = x.shape
+    mx = np.empty(rows, np.float32)
+    am = np.empty(rows, np.int64)
+    lib().orc_row_max_argmax_bf16(_p(x), rows, cols, cols, _p(mx), _p(am), threads)
+    return mx, am
+
+
+def scan_i32(x: np.ndarray, op: int, exclusive: bool, reverse: bool = False, carry=None,
+             threads: int = 1) -> np.ndarray:
+    """Row scans of an int32 [rows, k] (or 1-D) array (oracle/plan_window.rs:10-238)."""
+    x = np.ascontiguousarray(x, dtype=np.int32)
+    shape = x.shape
+    x2 = x.reshape(1, -1) if x.ndim == 1 else x.reshape(-1, shape[-1])
+    y = np.empty_like(x2)
+    c = lib().orc_scan_identity_i32(op) if carry is None else int(np.int32(carry))
+    lib().orc_scan_i32(_p(x2), _p(y), x2.shape[0], x2.shape[1], op, int(exclusive), int(reverse),
+                       c, threads)
+    return y.reshape(shape)
+
+
+def scan_i32_chunked(x: np.ndarray, op: int, exclusive: bool, threads: int) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.int32).reshape(-1)
+    y = np.empty_like(x)
+    lib().orc_scan_i32_chunked(_p(x), _p(y), x.size, op, int(exclusive), threads)
+    return y
+
+
+def reduce_i32(x: np.ndarray, op: int) -> int:
+    x = np.ascontiguousarray(x, dtype=np.int32).reshape(-1)
+    return int(lib().orc_reduce_i32(_p(x), x.size, op))
+
+
+def scan_identity_i32(op: int) -> int:
+    return int(lib().orc_scan_identity_i32(op))
+
+
+def gather_rows(table: np.ndarray, ids: np.ndarray, oob: int, out: np.ndarray | None = None,
+                threads: int = 1) -> np.ndarray:
+    """Row gather with an OOB policy; ``out`` (pre-filled) is updated in place for Skip."""
+    table = np.ascontiguousarray(table)
+    ids = np.ascontiguousarray(ids)
+    ek = {np.dtype(np.int32): EK_I32, np.dtype(np.int64): EK_I64, np.dtype(np.uint32): EK_U32}[ids.dtype]
+    V = table.shape[0]
+    row_bytes = table.nbytes // max(V, 1) if V > 0 else table.dtype.itemsize * int(np.prod(table.shape[1:]))
+    n = ids.shape[0]
+    if out is None:
+        out = np.zeros((n,) + table.shape[1:], table.dtype)
+    assert out.flags["C_CONTIGUOUS"]
+    lib().orc_gather_rows(_p(table), V, row_bytes, _p(ids), ek, n, oob, _p(out), threads)
+    return out
+
+
+def dequant_i4_bf16(w_packed: np.ndarray, scale_f16_bits: np.ndarray, n: int, k: int, group: int,
+                    threads: int = 1) -> np.ndarray:
+    w = np.ascontiguousarray(w_packed, dtype=np.uint8)
+    s = np.ascontiguousarray(scale_f16_bits, dtype=np.uint16)
+    out = np.empty((n, k), np.uint16)
+    lib().orc_dequant_i4_bf16(_p(w), _p(s), n, k, group, _p(out), threads)
+    return out
+
+
+def w4a16(w_packed, scale_f16_bits, x_bf16_bits, m, n, k, group, threads: int = 1):
+    """(out bf16 bits [m, n], exact f64 [m, n], sum|w*s*x| [m, n])."""
+    w = np.ascontiguousarray(w_packed, dtype=np.uint8)
+    s = np.ascontiguousarray(scale_f16_bits, dtype=np.uint16)
+    x = np.ascontiguousarray(x_bf16_bits, dtype=np.uint16)
+    out = np.empty((m, n), np.uint16)
+    exact = np.empty((m, n), np.float64)
+    abs_sum = np.empty((m, n), np.float64)
+    lib().orc_w4a16(_p(w), _p(s), _p(x), m, n, k, group, _p(out), _p(exact), _p(abs_sum), threads)
+    return out, exact, abs_sum
+
+
+def dequant_gemm_kat(packed, signed, zero, scale, x, R, K, C, group) -> np.ndarray:
+    """The reference's integer dequant-GEMM KAT form (zero points, I32 scales and activations)."""
+    w = np.ascontiguousarray(packed, dtype=np.uint8)
+    z = np.ascontiguousarray(zero, dtype=np.int32)
+    s = np.ascontiguousarray(scale, dtype=np.int32)
+    xx = np.ascontiguousarray(x, dtype=np.int32)
+    out = np.empty(R * C, np.int32)
+    lib().orc_dequant_gemm_kat(_p(w), int(signed), _p(z), _p(s), _p(xx), R, K, C, group, _p(out))
+    return out
+
+
+def f32_to_bf16(x: float) -> int:
+    return int(lib().orc_f32_to_bf16(float(x)))
+
+
+def f64_to_bf16(x: float) -> int:
+    return int(lib().orc_f64_to_bf16(float(x)))
+
+
+def f32_to_f16(x: float) -> int:
+    return int(lib().orc_f32_to_f16(float(x)))
+
+
+def f16_to_f64(b: int) -> float:
+    return float(lib().orc_f16_to_f64(int(b)))
+
+
+def bf16_to_f64(b: int) -> float:
+    return float(lib().orc_bf16_to_f64(int(b)))
+
+
+def i4_value(packed: np.ndarray, idx: int) -> int:
+    p = np.ascontiguousarray(packed, dtype=np.uint8)
+    return int(lib().orc_i4_value(_p(p), idx))

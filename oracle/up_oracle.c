@@ -1,0 +1,350 @@
+/*
+ * up_oracle.c — CPU restatement of the reference oracle for the lifted kernel families.
+ *
+ * TEST INFRASTRUCTURE ONLY. This file is the checker the GPU kernels are compared against (and, timed on
+ * the host cores, the reported CPU baseline). Nothing in the product library links, loads or calls it.
+ *
+ * Each function states the reference code it restates (paths relative to the Unpopped repository).
+ * The reference oracle is Rust and cannot be built in this environment, so parity is pinned by running
+ * these functions on the reference tests' own corpora and comparing with the expectations those tests
+ * compute independently of the oracle (tests/golden/, made by tests/golden/make_golden.py).
+ *
+ * Build: oracle/Makefile (gcc -O2 -ffp-contract=off -fopenmp, the strict-FP flags of the reference's C
+ * test support, crates/unpopped-cpu-c/tests/support/cc.rs:122-175).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define ORC_OP_SUM 0
+#define ORC_OP_MAX 2
+#define ORC_OP_MIN 3
+#define ORC_OOB_SKIP 0
+#define ORC_OOB_CLAMP 1
+#define ORC_OOB_ZERO_FILL 2
+#define ORC_EK_I32 9
+#define ORC_EK_I64 10
+#define ORC_EK_U32 23
+
+static inline uint32_t f32_bits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static inline float bits_f32(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+static inline uint64_t f64_bits(double d) { uint64_t u; memcpy(&u, &d, 8); return u; }
+
+/* ---- codecs: crates/unpopped/src/oracle/float_codec.rs, expr_eval.rs ---------------------------- */
+
+/* bf16_to_f64 (float_codec.rs:200-203): bf16 is the top half of an f32. */
+double orc_bf16_to_f64(uint16_t b) { return (double)bits_f32((uint32_t)b << 16); }
+
+/* f32_to_bf16_bits (float_codec.rs:260-268): RNE; a NaN keeps its top half and is made quiet. */
+uint16_t orc_f32_to_bf16(float x) {
+  uint32_t bits = f32_bits(x);
+  if (x != x) return (uint16_t)((bits >> 16) | 0x0040);
+  uint32_t bias = 0x7fff + ((bits >> 16) & 1);
+  return (uint16_t)((bits + bias) >> 16);
+}
+
+/* f32_to_f16_bits (float_codec.rs:205-258): RNE with subnormals, overflow to inf, quiet NaN. */
+uint16_t orc_f32_to_f16(float x) {
+  uint32_t bits = f32_bits(x);
+  uint16_t sign = (uint16_t)((bits >> 16) & 0x8000);
+  int32_t exp = (int32_t)((bits >> 23) & 0xff);
+  uint32_t mant = bits & 0x007fffff;
+  if (exp == 0xff) return mant ? (uint16_t)(sign | 0x7e00) : (uint16_t)(sign | 0x7c00);
+  int32_t e = exp - 127 + 15;
+  if (e >= 0x1f) return (uint16_t)(sign | 0x7c00);
+  if (e <= 0) {
+    if (e < -10) return sign;
+    uint32_t m = mant | 0x00800000;
+    uint32_t shift = (uint32_t)(14 - e);
+    uint32_t half = 1u << (shift - 1), mask = (1u << shift) - 1;
+    uint32_t rem = m & mask, r = m >> shift;
+    if (rem > half || (rem == half && (r & 1))) r += 1;
+    return (uint16_t)(sign | r);
+  }
+  uint32_t half = 1u << 12, mask = (1u << 13) - 1;
+  uint32_t rem = mant & mask, m10 = mant >> 13;
+  int32_t ee = e;
+  if (rem > half || (rem == half && (m10 & 1))) {
+    m10 += 1;
+    if (m10 == 0x400) {
+      m10 = 0;
+      ee += 1;
+      if (ee >= 0x1f) return (uint16_t)(sign | 0x7c00);
+    }
+  }
+  return (uint16_t)(sign | ((uint32_t)ee << 10) | m10);
+}
+
+/* IEEE binary16 decode (the inverse of the encoder above; exact in f64). */
+double orc_f16_to_f64(uint16_t h) {
+  int s = (h >> 15) & 1, e = (h >> 10) & 0x1f, m = h & 0x3ff;
+  double v;
+  if (e == 0) v = ldexp((double)m, -24);
+  else if (e == 0x1f) v = m ? NAN : INFINITY;
+  else v = ldexp((double)(m | 0x400), e - 25);
+  return s ? -v : v;
+}
+
+/* f64_to_f32_odd (expr_eval.rs:498-512): round to odd, so a later 16-bit rounding is single. */
+float orc_f64_to_f32_odd(double f) {
+  float r = (float)f;
+  if (!isfinite(f) || f == 0.0 || (double)r == f) return r;
+  uint32_t b = f32_bits(r);
+  float t = (fabs((double)r) > fabs(f)) ? bits_f32(b - 1) : r;
+  return bits_f32(f32_bits(t) | 1u);
+}
+
+/* encode_float(f, Bf16) (expr_eval.rs:520-530): odd-rounded f32, then RNE to bf16. */
+uint16_t orc_f64_to_bf16(double f) { return orc_f32_to_bf16(orc_f64_to_f32_odd(f)); }
+
+/* ---- reductions: oracle/plan_eval.rs:501-651, plan_contract.rs:146-245 ---------------------------- */
+
+/* Float Sum over the last axis: f64 accumulator from 0, ascending index (fold_step,
+ * plan_contract.rs:146-156), one rounding to f32 at the store (store_val / encode_float, F32 arm). */
+void orc_row_sum_f32(const float* x, int64_t rows, int64_t cols, int64_t row_stride, float* out,
+                     int threads) {
+#pragma omp parallel for num_threads(threads) schedule(static) if (threads > 1)
+  for (int64_t r = 0; r < rows; ++r) {
+    double acc = 0.0;
+    const float* row = x + r * row_stride;
+    for (int64_t c = 0; c < cols; ++c) acc += (double)row[c];
+    out[r] = (float)acc;
+  }
+}
+
+/* The launched lift's documented order (kernel_lift/block_reduce.rs:13-23; restated in the reference
+ * test crates/unpopped/tests/kernel_parallel_reduction_float_sum_bound.rs:147-170, `documented`):
+ * logical thread t < B folds t, t+B, ... ascending into an f64; then acc[t] += acc[t+s] for
+ * s = B/2 .. 1; one rounding to f32. B is a power of two. */
+void orc_row_sum_f32_documented(const float* x, int64_t rows, int64_t cols, int64_t row_stride,
+                                int64_t block, float* out, int threads) {
+#pragma omp parallel num_threads(threads) if (threads > 1)
+  {
+    double* acc = (double*)malloc(sizeof(double) * (size_t)block);
+#pragma omp for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+      const float* row = x + r * row_stride;
+      for (int64_t t = 0; t < block; ++t) {
+        double a = 0.0;
+        for (int64_t c = t; c < cols; c += block) a += (double)row[c];
+        acc[t] = a;
+      }
+      for (int64_t s = block / 2; s > 0; s /= 2)
+        for (int64_t t = 0; t < s; ++t) acc[t] += acc[t + s];
+      out[r] = (float)acc[0];
+    }
+    free(acc);
+  }
+}
+
+/* Max (extremum_fold, plan_contract.rs:179-210: take = !have || v is NaN || v > acc) and ArgMax
+ * (arg_fold, plan_contract.rs:213-245: take = !have || (!acc.is_nan() && (v.is_nan() || v > acc)))
+ * over a bf16 row, folded in f64. The max is stored as f32 (exact: bf16 is a subset). A NaN max is the
+ * last NaN of the row, widened as the reference's f32->f64->f32 conversions widen it (quiet bit set). */
+void orc_row_max_argmax_bf16(const uint16_t* x, int64_t rows, int64_t cols, int64_t row_stride,
+                             float* max_out, int64_t* argmax_out, int threads) {
+#pragma omp parallel for num_threads(threads) schedule(static) if (threads > 1)
+  for (int64_t r = 0; r < rows; ++r) {
+    const uint16_t* row = x + r * row_stride;
+    double acc_m = 0.0, acc_a = 0.0;
+    uint32_t acc_m_bits = 0;
+    int have_m = 0, have_a = 0;
+    int64_t best = 0;
+    for (int64_t c = 0; c < cols; ++c) {
+      double v = orc_bf16_to_f64(row[c]);
+      int vnan = (v != v);
+      if (!have_m || vnan || v > acc_m) {
+        acc_m = v;
+        acc_m_bits = vnan ? (((uint32_t)row[c] << 16) | 0x00400000u) : f32_bits((float)v);
+      }
+      have_m = 1;
+      int take = !have_a || (!(acc_a != acc_a) && (vnan || v > acc_a));
+      if (take) { acc_a = v; best = c; }
+      have_a = 1;
+    }
+    if (max_out) max_out[r] = cols > 0 ? bits_f32(acc_m_bits) : 0.0f;
+    if (argmax_out) argmax_out[r] = best;
+  }
+}
+
+/* ---- scans: oracle/plan_window.rs:10-238 ---------------------------------------------------------- */
+
+static inline int32_t orc_combine_i32(int op, int32_t a, int32_t b) {
+  if (op == ORC_OP_SUM) return (int32_t)((uint32_t)a + (uint32_t)b); /* wrap_bits(.., 32) */
+  if (op == ORC_OP_MAX) return a > b ? a : b;
+  return a < b ? a : b;
+}
+
+/* scan_identity (plan_window.rs:221-238): Sum 0, Max the type minimum, Min the type maximum. */
+int32_t orc_scan_identity_i32(int op) {
+  if (op == ORC_OP_SUM) return 0;
+  if (op == ORC_OP_MAX) return INT32_MIN;
+  return INT32_MAX;
+}
+
+/* eval_scan for an I32 row-major [rows, k] scan along the last axis: inclusive writes after the combine;
+ * exclusive writes before it, so element 0 gets the identity (Sum: acc starts at 0; Max/Min:
+ * `have ? cur : ident`, plan_window.rs:165-172). Reverse walks j = k-1 .. 0. Integer Sum wraps at 32
+ * bits (plan_window.rs:100-106). `carry` is combined in front of each row (a sharded scan's prefix). */
+void orc_scan_i32(const int32_t* x, int32_t* y, int64_t rows, int64_t k, int op, int exclusive,
+                  int reverse, int32_t carry, int threads) {
+#pragma omp parallel for num_threads(threads) schedule(static) if (threads > 1 && rows > 1)
+  for (int64_t r = 0; r < rows; ++r) {
+    const int32_t* xr = x + r * k;
+    int32_t* yr = y + r * k;
+    int32_t acc = carry;
+    for (int64_t jj = 0; jj < k; ++jj) {
+      int64_t j = reverse ? k - 1 - jj : jj;
+      if (exclusive) {
+        yr[j] = acc;
+        acc = orc_combine_i32(op, acc, xr[j]);
+      } else {
+        acc = orc_combine_i32(op, acc, xr[j]);
+        yr[j] = acc;
+      }
+    }
+  }
+}
+
+/* The same scan over one long row on several threads: chunk totals, an exclusive scan of the totals,
+ * then each chunk scanned from its carry (integer combines are associative, so the bytes equal the
+ * serial walk's). Forward only; the CPU baseline of the reference arm. */
+void orc_scan_i32_chunked(const int32_t* x, int32_t* y, int64_t n, int op, int exclusive, int threads) {
+  if (threads < 1) threads = 1;
+  int32_t* tot = (int32_t*)malloc(sizeof(int32_t) * (size_t)threads);
+  int64_t chunk = (n + threads - 1) / threads;
+#pragma omp parallel num_threads(threads)
+  {
+    int t = 0;
+#ifdef _OPENMP
+    t = omp_get_thread_num();
+#endif
+    int64_t lo = (int64_t)t * chunk, hi = lo + chunk < n ? lo + chunk : n;
+    int32_t a = orc_scan_identity_i32(op);
+    for (int64_t i = lo; i < hi; ++i) a = orc_combine_i32(op, a, x[i]);
+    tot[t] = a;
+#pragma omp barrier
+    int32_t carry = orc_scan_identity_i32(op);
+    for (int u = 0; u < t; ++u) carry = orc_combine_i32(op, carry, tot[u]);
+    int32_t acc = carry;
+    for (int64_t i = lo; i < hi; ++i) {
+      if (exclusive) { y[i] = acc; acc = orc_combine_i32(op, acc, x[i]); }
+      else { acc = orc_combine_i32(op, acc, x[i]); y[i] = acc; }
+    }
+  }
+  free(tot);
+}
+
+/* Fold of a whole array (the per-shard total of a sharded scan). */
+int32_t orc_reduce_i32(const int32_t* x, int64_t n, int op) {
+  int32_t a = orc_scan_identity_i32(op);
+  for (int64_t i = 0; i < n; ++i) a = orc_combine_i32(op, a, x[i]);
+  return a;
+}
+
+/* ---- gather: oracle/plan_eval.rs:284-430 (gather arm 363-385) --------------------------------------- */
+
+/* out[n, :] = table[ids[n], :] for a 1-D index broadcast over the row (OpDef::embedding /
+ * index_select / gather on axis 0, ir.rs:3838-3890). The index is read once (as i64); the load address
+ * is clamped to [0, V-1]; an index outside [0, V) skips the store (Skip: the output keeps its bytes),
+ * writes zeros (ZeroFill: Val::Float(0.0) / Val::Int(0), all-zero bits) or stores the clamped row
+ * (Clamp). The row moves verbatim (store_val's Raw arm, expr_eval.rs:480-484). */
+void orc_gather_rows(const uint8_t* table, int64_t table_rows, int64_t row_bytes, const void* ids,
+                     int index_dtype, int64_t n, int oob, uint8_t* out, int threads) {
+#pragma omp parallel for num_threads(threads) schedule(static) if (threads > 1)
+  for (int64_t i = 0; i < n; ++i) {
+    int64_t raw;
+    if (index_dtype == ORC_EK_I64) raw = ((const int64_t*)ids)[i];
+    else if (index_dtype == ORC_EK_U32) raw = (int64_t)((const uint32_t*)ids)[i];
+    else raw = (int64_t)((const int32_t*)ids)[i];
+    int64_t hi = table_rows - 1 > 0 ? table_rows - 1 : 0;
+    int64_t g = raw < 0 ? 0 : (raw > hi ? hi : raw);
+    uint8_t* dst = out + i * row_bytes;
+    if (raw < 0 || raw >= table_rows) {
+      if (oob == ORC_OOB_SKIP) continue;
+      if (oob == ORC_OOB_ZERO_FILL) { memset(dst, 0, (size_t)row_bytes); continue; }
+    }
+    if (table_rows > 0) memcpy(dst, table + g * row_bytes, (size_t)row_bytes);
+  }
+}
+
+/* ---- int4 dequant and the dequant GEMM ---------------------------------------------------------------- */
+
+/* i4 read (tests/sub_byte_packing.rs:24-40, cfamily.rs:446-470): two per byte, low nibble = even index,
+ * sign-extended. */
+static inline int orc_i4_at(const uint8_t* w, int64_t idx) {
+  uint8_t b = w[idx >> 1];
+  int v = (idx & 1) ? (b >> 4) : (b & 0x0f);
+  return v >= 8 ? v - 16 : v;
+}
+
+int orc_i4_value(const uint8_t* w, int64_t idx) { return orc_i4_at(w, idx); }
+
+/* The reference's dequant GEMM KAT form (crates/unpopped/tests/support/dequant.rs:1-5,163-178):
+ * out[r][c] = sum_k (w[r][k] - zero[r][k/G]) * scale[r][k/G] * x[k][c] with I32 zero points, scales,
+ * activations and result; `w` is I4 (signed) or U4 (unsigned) [R, K]. Shares the nibble reader with
+ * the W4A16 oracle below, so the KAT pins its packing and group indexing. */
+void orc_dequant_gemm_kat(const uint8_t* w, int is_signed, const int32_t* zero, const int32_t* scale,
+                          const int32_t* x, int64_t R, int64_t K, int64_t C, int64_t group, int32_t* out) {
+  int64_t g = K / group;
+  for (int64_t r = 0; r < R; ++r)
+    for (int64_t c = 0; c < C; ++c) {
+      int64_t acc = 0;
+      for (int64_t k = 0; k < K; ++k) {
+        int v = orc_i4_at(w, r * K + k);
+        if (!is_signed && v < 0) v += 16;
+        acc += (int64_t)(v - zero[r * g + k / group]) * scale[r * g + k / group] * x[k * C + c];
+      }
+      out[r * C + c] = (int32_t)acc;
+    }
+}
+
+/* out[n][k] = bf16(w[n][k] * scale[n][k/group]): the product is exact in f64 and rounds once
+ * (encode_float's Bf16 arm). `w` is [N, K] i4 row-major, `scale` f16 [N, K/group]. */
+void orc_dequant_i4_bf16(const uint8_t* w, const uint16_t* scale, int64_t n, int64_t k, int64_t group,
+                         uint16_t* out, int threads) {
+  int64_t g = k / group;
+#pragma omp parallel for num_threads(threads) schedule(static) if (threads > 1)
+  for (int64_t r = 0; r < n; ++r)
+    for (int64_t c = 0; c < k; ++c) {
+      double s = orc_f16_to_f64(scale[r * g + c / group]);
+      out[r * k + c] = orc_f64_to_bf16((double)orc_i4_at(w, r * k + c) * s);
+    }
+}
+
+/* The dequant GEMM (crates/unpopped/tests/support/dequant.rs:1-5,163-178, generalized to a f16 group scale,
+ * bf16 activations and no zero point): out[m][n] = sum_k w[n][k] * scale[n][k/group] * x[m][k], every
+ * product exact in f64, summed in ascending k in f64 (the WideFloat model, docs/accum-policies.md:8-20),
+ * one rounding to bf16. `abs_sum` (optional) receives sum_k |w * scale * x| per output, the scale of the
+ * tolerance a device f32 accumulation is held to. */
+void orc_w4a16(const uint8_t* w, const uint16_t* scale, const uint16_t* x, int64_t m, int64_t n,
+               int64_t k, int64_t group, uint16_t* out, double* exact, double* abs_sum, int threads) {
+  int64_t g = k / group;
+#pragma omp parallel for num_threads(threads) schedule(static) if (threads > 1)
+  for (int64_t r = 0; r < n; ++r) {
+    for (int64_t i = 0; i < m; ++i) {
+      double acc = 0.0, sa = 0.0;
+      for (int64_t c = 0; c < k; ++c) {
+        double p = (double)orc_i4_at(w, r * k + c) * orc_f16_to_f64(scale[r * g + c / group]) *
+                   orc_bf16_to_f64(x[i * k + c]);
+        acc += p;
+        sa += fabs(p);
+      }
+      out[i * n + r] = orc_f64_to_bf16(acc);
+      if (exact) exact[i * n + r] = acc;
+      if (abs_sum) abs_sum[i * n + r] = sa;
+    }
+  }
+}
+
+int orc_max_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}

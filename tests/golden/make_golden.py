@@ -1,0 +1,306 @@
+"""Writes the golden fixtures under tests/golden/ from the reference's own test corpora.
+
+The reference (Unpopped, Rust) cannot be built here, so its tests' corpora and the expectation rules those
+tests compute *independently of the oracle* are restated below in plain Python, one function per
+reference test, each citing the test it follows (paths relative to the Unpopped repository). The C oracle
+restatement (oracle/up_oracle.c) is then pinned against these fixtures by tests/test_oracle_golden.py.
+
+Run: python tests/golden/make_golden.py   (deterministic; rewrites the JSON files beside it)
+"""
+from __future__ import annotations
+
+import json
+import math
+import os
+import struct
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+M64 = (1 << 64) - 1
+I32_MIN, I32_MAX = -(1 << 31), (1 << 31) - 1
+
+
+def f32(x: float) -> float:
+    return struct.unpack("<f", struct.pack("<f", x))[0]
+
+
+def f32_bits(x: float) -> int:
+    return struct.unpack("<I", struct.pack("<f", x))[0]
+
+
+def bf16_bits_exact(x: float) -> int:
+    """bf16 bits of a value that bf16 holds exactly (the corpora below only hold such values)."""
+    b = f32_bits(x)
+    if math.isnan(x):
+        return 0x7FC0
+    assert b & 0xFFFF == 0, f"{x} is not exact in bf16"
+    return b >> 16
+
+
+def wrap32(v: int) -> int:
+    v &= 0xFFFFFFFF
+    return v - (1 << 32) if v >= (1 << 31) else v
+
+
+# --- crates/unpopped/tests/kernel_parallel_reduction_float_sum_bound.rs -------------------------------
+
+def lcg(state: list) -> float:
+    """`lcg` (float_sum_bound.rs:40-46): a u64 LCG, the top 53 bits as a fraction in [0, 1)."""
+    state[0] = (state[0] * 6364136223846793005 + 1442695040888963407) & M64
+    return (state[0] >> 11) / float(1 << 53)
+
+
+def float_sum_corpus() -> list:
+    """`corpus` (float_sum_bound.rs:48-72): five rows of 96 values, interleaved then regrouped row-major."""
+    rows, cols = 5, 96
+    s = [0x9E3779B97F4A7C15]
+    v = []
+    for c in range(cols):
+        v.append(1.0e-3 + 1.0e3 * lcg(s))
+        big = 1.0e8 if c % 2 == 0 else -1.0e8
+        v.append(1.0 + lcg(s) if c % 7 == 0 else big)
+        huge = 1.0e30 if c % 2 == 0 else -1.0e30 * (1.0 + 1e-3 * lcg(s))
+        v.append(huge * 1.0e-20)
+        v.append(0.1)
+        v.append((lcg(s) - 0.5) * 2.0e5)
+    return [[v[c * rows + r] for c in range(cols)] for r in range(rows)]
+
+
+def documented(xs: list, block: int) -> float:
+    """`documented` (float_sum_bound.rs:147-170) at F32, Sum: thread t folds t, t+B, ... into an f64, then
+    acc[t] += acc[t+s] for s = B/2 .. 1, one rounding to f32."""
+    acc = []
+    for t in range(block):
+        a = 0.0
+        for x in xs[t::block]:
+            a = a + x
+        acc.append(a)
+    s = block // 2
+    while s > 0:
+        for t in range(s):
+            acc[t] = acc[t] + acc[t + s]
+        s //= 2
+    return f32(acc[0])
+
+
+def golden_float_sum() -> dict:
+    rows = [[f32(x) for x in r] for r in float_sum_corpus()]  # `values(F32)`: the f32 roundings
+    blocks = [1, 2, 8, 32, 128, 16]  # GEOMETRIES' block sizes (float_sum_bound.rs:37)
+    return {
+        "source": "crates/unpopped/tests/kernel_parallel_reduction_float_sum_bound.rs:37-170",
+        "rows": 5, "cols": 96,
+        "x_f32_bits": [[f32_bits(x) for x in r] for r in rows],
+        "blocks": blocks,
+        "documented_f32_bits": {str(b): [f32_bits(documented(r, b)) for r in rows] for b in blocks},
+        "serial_f32_bits": [f32_bits(documented(r, 1)) for r in rows],
+    }
+
+
+# --- crates/unpopped/tests/reduce_argmax.rs + kernel_collective_tuple.rs --------------------------------
+
+def argmax_corpus() -> list:
+    """`corpus` (reduce_argmax.rs:31-41): ties, a NaN first, a NaN in the middle, all negative, signed
+    zeros, all NaN."""
+    n = float("nan")
+    return [
+        [3.0, 9.0, 9.0, 1.0, 1.0, 2.0],
+        [n, 1.0, 2.0, 3.0, -4.0, 5.0],
+        [1.0, 4.0, n, 7.0, n, 2.0],
+        [-1.0, -2.0, -3.0, -4.0, -5.0, -6.0],
+        [0.0, -0.0, 0.0, -0.0, 0.0, -0.0],
+        [n, n, n, n, n, n],
+    ]
+
+
+def greater(x: float, y: float) -> bool:
+    """`greater` (reduce_argmax.rs:76-78): NaN is the greatest value and equal to NaN."""
+    return (math.isnan(x) and not math.isnan(y)) or (not math.isnan(x) and not math.isnan(y) and x > y)
+
+
+def arg_of(xs: list) -> int:
+    """`arg_of` for ArgMax (reduce_argmax.rs:80-95): only a strictly greater element replaces."""
+    best = 0
+    for i in range(1, len(xs)):
+        if greater(xs[i], xs[best]):
+            best = i
+    return best
+
+
+def max_of(xs: list):
+    """The Max fold's rule (ReduceOp::Max, ir.rs:1700-1748; extremum_fold, plan_contract.rs:179-210): a NaN
+    propagates, and of equal maxima the first is kept (so a row of signed zeros keeps the first zero's
+    sign). Returns f32 bits; a NaN row gives the canonical quiet NaN the corpus holds."""
+    have, acc = False, 0.0
+    for v in xs:
+        if not have or math.isnan(v) or v > acc:
+            acc = v
+        have = True
+    return 0x7FC00000 if math.isnan(acc) else f32_bits(acc)
+
+
+def golden_argmax() -> dict:
+    rows = argmax_corpus()
+    tup = [3.0, 7.0, -1.0, 7.0, 0.0, 9.0, 9.0, 2.0]
+    return {
+        "source": "crates/unpopped/tests/reduce_argmax.rs:31-100; kernel_collective_tuple.rs:6-12",
+        "x_bf16_bits": [[bf16_bits_exact(v) for v in r] for r in rows],
+        "argmax": [arg_of(r) for r in rows],
+        "max_f32_bits": [max_of(r) for r in rows],
+        "tuple_x_bf16_bits": [bf16_bits_exact(v) for v in tup],
+        "tuple_argmax": 5,  # hand-derived in kernel_collective_tuple.rs:8-9: (9, 5)
+        "tuple_max": 9.0,
+    }
+
+
+# --- crates/unpopped/tests/kernel_int_reduce_scan_agrees.rs + kernel_parallel_scan_agrees.rs ---------------
+
+def int_corpus_i32() -> list:
+    """`corpus(I32)` (kernel_int_reduce_scan_agrees.rs:28-45): wrap-around, all negative, ties, big."""
+    hi, lo, big = I32_MAX, I32_MIN, 100_000
+    return [
+        [hi, 1, -1, 2, hi, 3],
+        [-1, -2, -3, -4, -5, -6],
+        [7, 7, 7, -7, lo, 0],
+        [big, big, 3, 1, -1, 2],
+        [4, 9, 2, 8, 6, 5],
+    ]
+
+
+def parallel_scan_ints() -> list:
+    """`int_values` (kernel_parallel_scan_agrees.rs:60-64): ((i*37+11) % 41) - 20 over 4 x 45."""
+    vals = [((i * 37 + 11) % 41) - 20 for i in range(4 * 45)]
+    return [vals[r * 45:(r + 1) * 45] for r in range(4)]
+
+
+def scan_def(row: list, op: str, exclusive: bool, reverse: bool) -> list:
+    """Access::Scan's definition (ir.rs:2153-2195): the running combine along the row (from its end when
+    reversed); exclusive shifts by one with the monoid identity first (Sum 0, Max the type minimum, Min the
+    type maximum); an integer Sum wraps at 32 bits."""
+    ident = {"sum": 0, "max": I32_MIN, "min": I32_MAX}[op]
+    comb = {"sum": lambda a, b: wrap32(a + b), "max": max, "min": min}[op]
+    k = len(row)
+    out = [0] * k
+    acc = ident
+    for jj in range(k):
+        j = k - 1 - jj if reverse else jj
+        if exclusive:
+            out[j] = acc
+            acc = comb(acc, row[j])
+        else:
+            acc = comb(acc, row[j])
+            out[j] = acc
+    return out
+
+
+def golden_scan() -> dict:
+    cases = {}
+    for name, rows in (("int_reduce_scan_5x6", int_corpus_i32()), ("parallel_scan_4x45", parallel_scan_ints())):
+        exp = {}
+        for op in ("sum", "max", "min"):
+            for excl in (False, True):
+                for rev in (False, True):
+                    key = f"{op}_{'excl' if excl else 'incl'}_{'rev' if rev else 'fwd'}"
+                    exp[key] = [scan_def(r, op, excl, rev) for r in rows]
+        cases[name] = {"x": rows, "expected": exp}
+    # Reductions of the wrap corpus along the last axis (fold_step / extremum_fold with wrap at the store).
+    red = {
+        "sum": [wrap32(sum(r)) for r in int_corpus_i32()],
+        "max": [max(r) for r in int_corpus_i32()],
+        "min": [min(r) for r in int_corpus_i32()],
+    }
+    return {
+        "source": "crates/unpopped/tests/kernel_int_reduce_scan_agrees.rs:28-45; "
+                  "kernel_parallel_scan_agrees.rs:60-64",
+        "cases": cases,
+        "row_reductions_5x6": red,
+    }
+
+
+# --- crates/unpopped/tests/kernel_parallel_gather_agrees.rs ---------------------------------------------------
+
+def golden_gather() -> dict:
+    """The 1-D-ids case (kernel_parallel_gather_agrees.rs:22-105): data [5, 6] f32 = i*1.5 - 7, out [9, 6]
+    pre-filled with 0xAB, ids from the OOB pool; the expectation is the gather's definition (clamped load,
+    OOB as a store predicate; plan_eval.rs:363-385)."""
+    data = [[f32((r * 6 + c) * 1.5 - 7.0) for c in range(6)] for r in range(5)]
+    extent = 5
+    pool = [0, extent - 1, 1, extent, extent + 7, 2, -1, I32_MIN, I32_MAX, -3]
+    n = 9
+    ids = [pool[(i * 3 + i // 4) % len(pool)] for i in range(n)]
+    prefill = struct.unpack("<I", bytes([0xAB] * 4))[0]
+    exp = {}
+    for pol in ("skip", "clamp", "zero_fill"):
+        out = []
+        for i in range(n):
+            raw = ids[i]
+            g = min(max(raw, 0), extent - 1)
+            if raw < 0 or raw >= extent:
+                if pol == "skip":
+                    out.append([prefill] * 6)
+                    continue
+                if pol == "zero_fill":
+                    out.append([0] * 6)
+                    continue
+            out.append([f32_bits(v) for v in data[g]])
+        exp[pol] = out
+    return {
+        "source": "crates/unpopped/tests/kernel_parallel_gather_agrees.rs:22-105",
+        "table_f32_bits": [[f32_bits(v) for v in r] for r in data],
+        "ids_i32": ids,
+        "prefill_byte": 0xAB,
+        "expected_f32_bits": exp,
+    }
+
+
+# --- crates/unpopped/tests/support/dequant.rs + sub_byte_packing.rs --------------------------------------------
+
+def golden_dequant() -> dict:
+    """The dequant GEMM KAT (support/dequant.rs:13-20,146-178): R=4, K=8, C=4, GROUP=4; nibble(r,k) =
+    (r*5 + k*3 + 1) % 16 packed low nibble first; zero = (i % 3) - 1, scale = 1 + (i*2 % 3),
+    x = (i*7 % 9) - 4 laid out x[k*C + c]; out[r][c] = sum_k (w - zero) * scale * x."""
+    R, K, C, GROUP = 4, 8, 4, 4
+    G = K // GROUP
+    nib = [[(r * 5 + k * 3 + 1) % 16 for k in range(K)] for r in range(R)]
+    flat = [v for row in nib for v in row]
+    packed = [flat[i] | (flat[i + 1] << 4) for i in range(0, len(flat), 2)]
+    zero = [(i % 3) - 1 for i in range(R * G)]
+    scale = [1 + (i * 2 % 3) for i in range(R * G)]
+    x = [(i * 7 % 9) - 4 for i in range(K * C)]
+
+    def ref(signed: bool):
+        def w(r, k):
+            v = nib[r][k]
+            return v - 16 if signed and v >= 8 else v
+        out = []
+        for r in range(R):
+            for c in range(C):
+                out.append(sum((w(r, k) - zero[r * G + k // GROUP]) * scale[r * G + k // GROUP] * x[k * C + c]
+                               for k in range(K)))
+        return out
+
+    return {
+        "source": "crates/unpopped/tests/support/dequant.rs:13-20,146-178; tests/sub_byte_packing.rs:24-60",
+        "R": R, "K": K, "C": C, "GROUP": GROUP,
+        "packed": packed, "zero": zero, "scale": scale, "x": x,
+        "expected_signed": ref(True), "expected_unsigned": ref(False),
+        # sub_byte_packing.rs: [1, 2] -> 0x21; i4 [-1, -8] and u4 [15, 8] share the byte 0x8F.
+        "packing_kat": {"i4_1_2": 0x21, "i4_m1_m8": 0x8F, "u4_15_8": 0x8F},
+    }
+
+
+def main() -> None:
+    out = {
+        "float_sum_documented.json": golden_float_sum(),
+        "argmax.json": golden_argmax(),
+        "scan_i32.json": golden_scan(),
+        "gather_oob.json": golden_gather(),
+        "dequant_kat.json": golden_dequant(),
+    }
+    for name, obj in out.items():
+        with open(os.path.join(HERE, name), "w") as f:
+            json.dump(obj, f, indent=1, sort_keys=True)
+            f.write("\n")
+        print("wrote", name)
+
+
+if __name__ == "__main__":
+    main()

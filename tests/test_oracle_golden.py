@@ -1,0 +1,152 @@
+"""Pins the CPU oracle restatement (oracle/up_oracle.c) to the reference tests' own corpora and expectations
+(tests/golden/*.json, written by tests/golden/make_golden.py). CPU only."""
+import json
+import os
+import struct
+
+import numpy as np
+import pytest
+
+import oracle as orc
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def load(name):
+    with open(os.path.join(GOLDEN, name)) as f:
+        return json.load(f)
+
+
+def bits_to_f32(bits):
+    return np.array(bits, dtype=np.uint32).view(np.float32)
+
+
+def test_documented_float_sum_order_matches_reference_rule():
+    g = load("float_sum_documented.json")
+    x = bits_to_f32(g["x_f32_bits"]).reshape(g["rows"], g["cols"])
+    for b in g["blocks"]:
+        got = orc.row_sum_f32_documented(x, b).view(np.uint32)
+        assert got.tolist() == g["documented_f32_bits"][str(b)], f"block {b}"
+    # block 1 is the serial order, which is the plan oracle's fold (plan_eval.rs:566-645).
+    assert orc.row_sum_f32(x).view(np.uint32).tolist() == g["serial_f32_bits"]
+
+
+def test_documented_order_threads_do_not_change_bytes():
+    g = load("float_sum_documented.json")
+    x = bits_to_f32(g["x_f32_bits"]).reshape(g["rows"], g["cols"])
+    for b in g["blocks"]:
+        assert np.array_equal(orc.row_sum_f32_documented(x, b, threads=4).view(np.uint32),
+                              orc.row_sum_f32_documented(x, b).view(np.uint32))
+
+
+def test_argmax_corpus_and_tuple_fixture():
+    g = load("argmax.json")
+    x = np.array(g["x_bf16_bits"], dtype=np.uint16)
+    mx, am = orc.row_max_argmax_bf16(x)
+    assert am.tolist() == g["argmax"]
+    assert mx.view(np.uint32).tolist() == g["max_f32_bits"]
+    t = np.array([g["tuple_x_bf16_bits"]], dtype=np.uint16)
+    mx, am = orc.row_max_argmax_bf16(t)
+    assert am.tolist() == [g["tuple_argmax"]] and mx.tolist() == [g["tuple_max"]]
+
+
+@pytest.mark.parametrize("case", ["int_reduce_scan_5x6", "parallel_scan_4x45"])
+def test_scan_corpora(case):
+    g = load("scan_i32.json")["cases"][case]
+    x = np.array(g["x"], dtype=np.int32)
+    ops = {"sum": orc.OP_SUM, "max": orc.OP_MAX, "min": orc.OP_MIN}
+    for key, exp in g["expected"].items():
+        op, mode, direction = key.split("_")
+        got = orc.scan_i32(x, ops[op], mode == "excl", direction == "rev")
+        assert got.tolist() == exp, key
+
+
+def test_int_row_reductions_wrap():
+    g = load("scan_i32.json")
+    x = np.array(g["cases"]["int_reduce_scan_5x6"]["x"], dtype=np.int32)
+    for name, op in (("sum", orc.OP_SUM), ("max", orc.OP_MAX), ("min", orc.OP_MIN)):
+        assert [orc.reduce_i32(r, op) for r in x] == g["row_reductions_5x6"][name]
+
+
+def test_chunked_scan_equals_serial_scan():
+    rng = np.random.default_rng(7)
+    x = rng.integers(-(2**31), 2**31 - 1, size=100_003, dtype=np.int64).astype(np.int32)
+    for op in (orc.OP_SUM, orc.OP_MAX, orc.OP_MIN):
+        for excl in (False, True):
+            assert np.array_equal(orc.scan_i32_chunked(x, op, excl, threads=5), orc.scan_i32(x, op, excl))
+
+
+@pytest.mark.parametrize("policy,code", [("skip", orc.OOB_SKIP), ("clamp", orc.OOB_CLAMP),
+                                         ("zero_fill", orc.OOB_ZERO_FILL)])
+def test_gather_oob_pool(policy, code):
+    g = load("gather_oob.json")
+    table = np.array(g["table_f32_bits"], dtype=np.uint32)
+    ids = np.array(g["ids_i32"], dtype=np.int32)
+    out = np.full((ids.size, table.shape[1]), 0xABABABAB, dtype=np.uint32)
+    orc.gather_rows(table, ids, code, out=out)
+    assert out.tolist() == g["expected_f32_bits"][policy]
+
+
+def test_gather_index_dtypes_agree_on_nonnegative_ids():
+    rng = np.random.default_rng(3)
+    table = rng.integers(0, 2**16, size=(50, 8), dtype=np.uint16)
+    ids = rng.integers(0, 50, size=200)
+    outs = [orc.gather_rows(table, ids.astype(dt), orc.OOB_SKIP) for dt in (np.int32, np.int64, np.uint32)]
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
+    assert np.array_equal(outs[0], table[ids])
+
+
+def test_dequant_gemm_kat_and_packing():
+    g = load("dequant_kat.json")
+    packed = np.array(g["packed"], dtype=np.uint8)
+    for signed, key in ((True, "expected_signed"), (False, "expected_unsigned")):
+        got = orc.dequant_gemm_kat(packed, signed, g["zero"], g["scale"], g["x"], g["R"], g["K"], g["C"], g["GROUP"])
+        assert got.tolist() == g[key]
+    kat = g["packing_kat"]
+    assert orc.i4_value(np.array([kat["i4_1_2"]], np.uint8), 0) == 1
+    assert orc.i4_value(np.array([kat["i4_1_2"]], np.uint8), 1) == 2
+    b = np.array([kat["i4_m1_m8"]], np.uint8)
+    assert (orc.i4_value(b, 0), orc.i4_value(b, 1)) == (-1, -8)
+    for v in range(-8, 8):
+        byte = np.array([(v & 0xF) | ((v & 0xF) << 4)], np.uint8)
+        assert orc.i4_value(byte, 0) == v and orc.i4_value(byte, 1) == v
+
+
+def test_bf16_codec_matches_rne_and_quiet_nan_rule():
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(11)
+    vals = np.concatenate([rng.standard_normal(2000).astype(np.float32),
+                           np.array([0.0, -0.0, 1.0, -1.0, np.inf, -np.inf, 3.0e38, 1e-40], np.float32),
+                           # exact ties at the bf16 rounding point, both parities
+                           np.array([1.0 + 2**-8, 1.0 + 3 * 2**-8], np.float32)])
+    got = np.array([orc.f32_to_bf16(float(v)) for v in vals], np.uint16)
+    want = torch.from_numpy(vals).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(got, want)
+    # float_codec.rs:262-264: a NaN keeps its top half and gets the quiet bit.
+    snan = struct.unpack("<f", struct.pack("<I", 0x7F810000))[0]
+    assert orc.f32_to_bf16(snan) == 0x7FC1
+
+
+def test_f16_codec_round_trips_every_finite_half():
+    for h in range(0, 0x10000, 7):
+        if (h & 0x7C00) == 0x7C00:
+            continue
+        v = orc.f16_to_f64(h)
+        assert orc.f32_to_f16(v) == h, hex(h)
+
+
+def test_w4a16_oracle_matches_direct_f64_sum():
+    rng = np.random.default_rng(5)
+    m, n, k, group = 3, 4, 256, 128
+    w = rng.integers(-8, 8, size=(n, k))
+    packed = ((w[:, 0::2] & 0xF) | ((w[:, 1::2] & 0xF) << 4)).astype(np.uint8)
+    scale = rng.uniform(0.005, 0.02, size=(n, k // group)).astype(np.float16)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    xb = np.array([[orc.f32_to_bf16(float(v)) for v in row] for row in x], np.uint16)
+    out, exact, abs_sum = orc.w4a16(packed, scale.view(np.uint16), xb, m, n, k, group)
+    xf = (xb.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    sf = np.repeat(scale.astype(np.float64), group, axis=1)
+    direct = xf @ (w * sf).T
+    assert np.allclose(exact, direct, rtol=1e-14, atol=1e-14)
+    assert np.allclose(abs_sum, np.abs(xf) @ np.abs(w * sf).T, rtol=1e-14)
+    assert out.tolist() == [[orc.f64_to_bf16(v) for v in row] for row in exact]
