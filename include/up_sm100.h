@@ -33,6 +33,13 @@ extern "C" {
 #endif
 
 #define UP_SM100_ABI_VERSION 1
+
+/* Exported from libunpopped_sm100.so (built with hidden visibility for everything else). */
+#if defined(__GNUC__)
+#define UP_API __attribute__((visibility("default")))
+#else
+#define UP_API
+#endif
 #define UP_MAX_RANK 8
 
 /* Status codes. */
@@ -116,6 +123,7 @@ typedef struct up_plan_desc {
   int32_t keepdim;
   int32_t identity_body; /* 1 when the body is Input(0) and the post is Reduced(0) */
   int32_t accum;         /* up_accum for a float Sum */
+  int32_t block;         /* the launched lift's block size B for UP_ACCUM_AUTO (0 = 256) */
   int32_t scan_axis;     /* Scan: the scanned axis */
   int32_t exclusive;     /* Scan */
   int32_t reverse;       /* Scan */
@@ -148,27 +156,27 @@ typedef struct up_lowered {
 /* ---- Backend seam ------------------------------------------------------------------------------- */
 
 /* UP_SM100_ABI_VERSION of the loaded library. */
-int up_sm100_version(void);
+UP_API int up_sm100_version(void);
 
 /* `Backend::name` / `Backend::provider` (backend.rs:668-690): "cuda_sm100" / "unpopped-cuda-sm100". */
-const char* up_sm100_name(void);
-const char* up_sm100_provider(void);
+UP_API const char* up_sm100_name(void);
+UP_API const char* up_sm100_provider(void);
 
 /* `Backend::supports_dtype(dtype, target)` (backend.rs:779): 0 Supported, 1 Unsupported,
  * 2 NotExpressible (DtypeSupport, backend.rs:645-666). Targets "cuda:sm_100a" and "cuda:sm100a" (and
  * "cuda:sm100") are this backend's; any other target answers Unsupported. */
-int up_sm100_supports_dtype(int dtype, const char* target);
+UP_API int up_sm100_supports_dtype(int dtype, const char* target);
 
 /* `Backend::lower` (backend.rs:708) restricted to what this backend maps: fills `out` with the kernel id,
  * entry symbol and launch scalars, or with the LowerError that refuses the plan. Returns UP_OK when a
  * kernel was chosen, UP_ERR_UNSUPPORTED when the plan is refused, UP_ERR_INVALID on a null argument. */
-int up_sm100_classify(const up_plan_desc* plan, up_lowered* out);
+UP_API int up_sm100_classify(const up_plan_desc* plan, up_lowered* out);
 
 /* ---- Generic launch ------------------------------------------------------------------------------ */
 
 /* Workspace bytes `up_sm100_launch(id, ...)` needs (0 when none). The workspace must be zero-filled
  * once before its first use (`cudaMemset`); the kernels leave it ready for the next launch. */
-int up_sm100_workspace_bytes(int kernel_id, const up_tensor* ins, int n_in, const up_tensor* outs,
+UP_API int up_sm100_workspace_bytes(int kernel_id, const up_tensor* ins, int n_in, const up_tensor* outs,
                              int n_out, const int64_t* scalars, int n_scalars, size_t* bytes);
 
 /* Launch kernel `kernel_id` on tensor descriptors. Operand order and scalars per kernel:
@@ -185,25 +193,25 @@ int up_sm100_workspace_bytes(int kernel_id, const up_tensor* ins, int n_in, cons
  *  W4A16_GEMM:           ins {w i4 [N, K], scale f16 [N, K/group], x bf16 [M, K]},
  *                        outs {out bf16 [M, N]}; scalars {group}
  */
-int up_sm100_launch(int kernel_id, const up_tensor* ins, int n_in, const up_tensor* outs, int n_out,
+UP_API int up_sm100_launch(int kernel_id, const up_tensor* ins, int n_in, const up_tensor* outs, int n_out,
                     const int64_t* scalars, int n_scalars, void* workspace, size_t workspace_bytes,
                     void* stream);
 
 /* Waits for `stream`, then reads and clears the device error word of a workspace: UP_OK, or
  * UP_ERR_DEVICE_TIMEOUT when a bounded wait ran out during an earlier launch on it. */
-int up_sm100_workspace_status(void* workspace, void* stream);
+UP_API int up_sm100_workspace_status(void* workspace, void* stream);
 
 /* ---- Typed entry points (what the generic launch dispatches to) ------------------------------------ */
 
 /* Row sum of a row-major f32 matrix (`ReduceOp::Sum` over the last axis, `Access::Reduction`,
  * ir.rs:2080-2135; oracle fold oracle/plan_eval.rs:501-651). `row_stride` in elements (>= cols). */
-int up_sm100_row_sum_f32(const float* x, int64_t rows, int64_t cols, int64_t row_stride, float* out,
+UP_API int up_sm100_row_sum_f32(const float* x, int64_t rows, int64_t cols, int64_t row_stride, float* out,
                          int accum, int block, void* stream);
 
 /* Row max and argmax of a row-major bf16 matrix: Max is NaN-propagating (oracle/plan_contract.rs:179-210),
  * ArgMax is the first index of the extreme with NaN the greatest value (plan_contract.rs:213-245).
  * Either output may be NULL; `argmax_i64` and `argmax_i32` may both be given. */
-int up_sm100_row_max_argmax_bf16(const uint16_t* x, int64_t rows, int64_t cols, int64_t row_stride,
+UP_API int up_sm100_row_max_argmax_bf16(const uint16_t* x, int64_t rows, int64_t cols, int64_t row_stride,
                                  float* max_out, int32_t* argmax_i32, int64_t* argmax_i64, void* stream);
 
 /* Scan of `rows` independent rows of `k` int32 (`Access::Scan`, ir.rs:2153-2195; oracle
@@ -212,25 +220,25 @@ int up_sm100_row_max_argmax_bf16(const uint16_t* x, int64_t rows, int64_t cols, 
  * `carry_in` (device pointer to one int32, or NULL) is combined in front of every row — the carry of a
  * scan sharded over several GPUs. Single-pass decoupled look-back; `workspace` from
  * up_sm100_scan_workspace_bytes, zero-filled before its first use. */
-int up_sm100_scan_i32(const int32_t* x, int32_t* y, int64_t rows, int64_t k, int op, int exclusive,
+UP_API int up_sm100_scan_i32(const int32_t* x, int32_t* y, int64_t rows, int64_t k, int op, int exclusive,
                       int reverse, const int32_t* carry_in, void* workspace, size_t workspace_bytes,
                       void* stream);
-size_t up_sm100_scan_workspace_bytes(int64_t rows, int64_t k);
+UP_API size_t up_sm100_scan_workspace_bytes(int64_t rows, int64_t k);
 
 /* Fold of a whole int32 array to one value (the first pass of a scan sharded over GPUs): SUM (wrapping),
  * MAX or MIN, written to `total` (device, one int32). Deterministic. */
-int up_sm100_reduce_i32(const int32_t* x, int64_t n, int op, int32_t* total, void* stream);
+UP_API int up_sm100_reduce_i32(const int32_t* x, int64_t n, int op, int32_t* total, void* stream);
 
 /* Row gather `out[n, :] = table[ids[n], :]` (ReadIndex::Indexed on axis 0, ir.rs:2620-2669; oracle
  * oracle/plan_eval.rs:363-385): the row is copied bit for bit; an id outside [0, table_rows) writes
  * nothing (SKIP), zeros (ZERO_FILL) or the clamped row (CLAMP). `row_bytes` is the row size in bytes;
  * `index_dtype` is UP_EK_I32, UP_EK_I64 or UP_EK_U32. */
-int up_sm100_gather_rows(const void* table, int64_t table_rows, int64_t row_bytes, const void* ids,
+UP_API int up_sm100_gather_rows(const void* table, int64_t table_rows, int64_t row_bytes, const void* ids,
                          int index_dtype, int64_t n, int oob, void* out, void* stream);
 
 /* Group-wise int4 dequant: out[n][k] = bf16(w[n][k] * scale[n][k / group]) with one rounding (RNE).
  * `w` is [N, K] i4 packed two per byte along K (low nibble first), `scale` f16 [N, K/group]. */
-int up_sm100_dequant_i4_bf16(const uint8_t* w, const uint16_t* scale, int64_t n, int64_t k,
+UP_API int up_sm100_dequant_i4_bf16(const uint8_t* w, const uint16_t* scale, int64_t n, int64_t k,
                              int64_t group, uint16_t* out, void* stream);
 
 /* W4A16 GEMM: out[m][n] = bf16( sum_k x[m][k] * w[n][k] * scale[n][k / group] ), f32 accumulation on
@@ -238,22 +246,22 @@ int up_sm100_dequant_i4_bf16(const uint8_t* w, const uint16_t* scale, int64_t n,
  * row-major, `out` bf16 [M, N] row-major, M <= 16 per call tile, K % group == 0, group % 128 == 0,
  * N % 128 == 0. `workspace` from up_sm100_w4a16_workspace_bytes (split-K partials and counters),
  * zero-filled before its first use. */
-int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, const uint16_t* x, int64_t m,
+UP_API int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, const uint16_t* x, int64_t m,
                         int64_t n, int64_t k, int64_t group, uint16_t* out, void* workspace,
                         size_t workspace_bytes, void* stream);
-size_t up_sm100_w4a16_workspace_bytes(int64_t m, int64_t n, int64_t k, int64_t group);
+UP_API size_t up_sm100_w4a16_workspace_bytes(int64_t m, int64_t n, int64_t k, int64_t group);
 
 /* ---- Test and tuning hooks ----------------------------------------------------------------------- */
 
 /* Bound, in nanoseconds, of every device-side wait (default 1e9). */
-void up_sm100_set_wait_limit_ns(uint64_t ns);
+UP_API void up_sm100_set_wait_limit_ns(uint64_t ns);
 /* When nonzero, the next scan launches make tile 0 withhold its look-back flag, so every other tile's wait
  * runs out: the host-visible error path of a bounded wait, without hanging or faulting the GPU. */
-void up_sm100_set_test_withhold_flag(int enable);
+UP_API void up_sm100_set_test_withhold_flag(int enable);
 /* Number of kernels this library has launched since load (all entry points). */
-uint64_t up_sm100_launch_count(void);
+UP_API uint64_t up_sm100_launch_count(void);
 /* Last CUDA error text seen by the library (static storage). */
-const char* up_sm100_last_error(void);
+UP_API const char* up_sm100_last_error(void);
 
 #ifdef __cplusplus
 }

@@ -79,14 +79,20 @@ uint16_t orc_f32_to_f16(float x) {
   return (uint16_t)(sign | ((uint32_t)ee << 10) | m10);
 }
 
-/* IEEE binary16 decode (the inverse of the encoder above; exact in f64). */
+/* IEEE binary16 decode (the inverse of the encoder above; exact in f64), by bit assembly. */
 double orc_f16_to_f64(uint16_t h) {
-  int s = (h >> 15) & 1, e = (h >> 10) & 0x1f, m = h & 0x3ff;
-  double v;
-  if (e == 0) v = ldexp((double)m, -24);
-  else if (e == 0x1f) v = m ? NAN : INFINITY;
-  else v = ldexp((double)(m | 0x400), e - 25);
-  return s ? -v : v;
+  uint64_t s = (uint64_t)(h >> 15) << 63;
+  uint32_t e = (h >> 10) & 0x1f, m = h & 0x3ff;
+  uint64_t bits;
+  if (e == 0) {
+    double v = (double)m * (1.0 / 16777216.0); /* m * 2^-24, exact */
+    return s ? -v : v;
+  }
+  if (e == 0x1f) bits = s | 0x7ff0000000000000ull | ((uint64_t)m << 42) | (m ? 0x0008000000000000ull : 0);
+  else bits = s | ((uint64_t)(e - 15 + 1023) << 52) | ((uint64_t)m << 42);
+  double d;
+  memcpy(&d, &bits, 8);
+  return d;
 }
 
 /* f64_to_f32_odd (expr_eval.rs:498-512): round to odd, so a later 16-bit rounding is single. */
@@ -324,21 +330,31 @@ void orc_dequant_i4_bf16(const uint8_t* w, const uint16_t* scale, int64_t n, int
 void orc_w4a16(const uint8_t* w, const uint16_t* scale, const uint16_t* x, int64_t m, int64_t n,
                int64_t k, int64_t group, uint16_t* out, double* exact, double* abs_sum, int threads) {
   int64_t g = k / group;
-#pragma omp parallel for num_threads(threads) schedule(static) if (threads > 1)
-  for (int64_t r = 0; r < n; ++r) {
-    for (int64_t i = 0; i < m; ++i) {
-      double acc = 0.0, sa = 0.0;
-      for (int64_t c = 0; c < k; ++c) {
-        double p = (double)orc_i4_at(w, r * k + c) * orc_f16_to_f64(scale[r * g + c / group]) *
-                   orc_bf16_to_f64(x[i * k + c]);
-        acc += p;
-        sa += fabs(p);
+  double* xf = (double*)malloc(sizeof(double) * (size_t)(m * k));
+  for (int64_t i = 0; i < m * k; ++i) xf[i] = orc_bf16_to_f64(x[i]);
+#pragma omp parallel num_threads(threads) if (threads > 1)
+  {
+    double* ws = (double*)malloc(sizeof(double) * (size_t)k); /* w * scale of one row, exact */
+#pragma omp for schedule(static)
+    for (int64_t r = 0; r < n; ++r) {
+      for (int64_t c = 0; c < k; ++c)
+        ws[c] = (double)orc_i4_at(w, r * k + c) * orc_f16_to_f64(scale[r * g + c / group]);
+      for (int64_t i = 0; i < m; ++i) {
+        const double* xi = xf + i * k;
+        double acc = 0.0, sa = 0.0;
+        for (int64_t c = 0; c < k; ++c) {
+          double p = ws[c] * xi[c];
+          acc += p;
+          sa += fabs(p);
+        }
+        out[i * n + r] = orc_f64_to_bf16(acc);
+        if (exact) exact[i * n + r] = acc;
+        if (abs_sum) abs_sum[i * n + r] = sa;
       }
-      out[i * n + r] = orc_f64_to_bf16(acc);
-      if (exact) exact[i * n + r] = acc;
-      if (abs_sum) abs_sum[i * n + r] = sa;
     }
+    free(ws);
   }
+  free(xf);
 }
 
 int orc_max_threads(void) {

@@ -1,0 +1,130 @@
+"""The C-ABI library loads, exports every symbol include/up_sm100.h declares, and answers the Backend seam
+(name, provider, supports_dtype, lower) on the CPU. No kernel is launched here."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from unpopped_b200 import _lib
+from unpopped_b200.backend import CudaSm100, LowerError, Operand, Plan
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "up_sm100.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^UP_API [^(]*?\b(up_sm100_\w+)\(", text, flags=re.M)))
+
+
+def test_header_declares_the_entry_points():
+    syms = declared_symbols()
+    assert "up_sm100_launch" in syms and "up_sm100_classify" in syms and len(syms) >= 20
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.load()
+    for s in declared_symbols():
+        assert hasattr(L, s), s
+    # and the ctypes binding covers exactly the declared set
+    assert set(_lib.SIGNATURES) == set(declared_symbols())
+
+
+def test_name_provider_version():
+    b = CudaSm100()
+    assert b.name() == "cuda_sm100"
+    assert b.provider() == "unpopped-cuda-sm100"
+    assert _lib.load().up_sm100_version() == 1
+
+
+@pytest.mark.parametrize("target", ["cuda:sm_100a", "cuda:sm100a", "cuda:sm100"])
+def test_supports_dtype_on_our_targets(target):
+    b = CudaSm100()
+    for dt in ("F32", "BF16", "F16", "I32", "I64", "U32", "I4", "U8", "F64"):
+        assert b.supports_dtype(dt, target) == "Supported", dt
+    for dt in ("FP8_E4M3FNUZ", "FP8_E5M2FNUZ", "U4", "B1", "F4_E2M1"):
+        assert b.supports_dtype(dt, target) == "Unsupported", dt
+
+
+def test_supports_dtype_declines_other_targets():
+    b = CudaSm100()
+    for target in ("cuda:sm89", "cuda:sm90a", "vulkan:spirv1.6", "rocm:gfx942"):
+        assert b.supports_dtype("F32", target) == "Unsupported"
+
+
+def _red(op, dtype, out_dtype=None, shape=(64, 96), **kw):
+    return Plan("REDUCTION", [Operand(dtype, shape), Operand(out_dtype or dtype, shape[:1])], dtype=dtype,
+                out_dtype=out_dtype, op=op, **kw)
+
+
+def test_dispatch_table_maps_each_lift():
+    b = CudaSm100()
+    k = b.lower(_red("SUM", "F32"))
+    assert (k.name, k.scalars) == ("up_sm100_row_sum_f32", (1, 256))
+    k = b.lower(_red("SUM", "F32", accum="AUTO", block=128))
+    assert k.scalars == (0, 128)
+    assert b.lower(_red("MAX", "BF16", "F32")).name == "up_sm100_row_max_argmax_bf16"
+    assert b.lower(_red("ARGMAX", "BF16", "I64")).name == "up_sm100_row_max_argmax_bf16"
+    for op in ("SUM", "MAX", "MIN"):
+        for excl in (False, True):
+            for rev in (False, True):
+                k = b.lower(Plan("SCAN", [Operand("I32", (1 << 28,)), Operand("I32", (1 << 28,))], dtype="I32",
+                                 op=op, exclusive=excl, reverse=rev))
+                assert k.name == "up_sm100_scan_i32" and k.scalars == (_lib.OP[op], int(excl), int(rev))
+    g = Plan("STRIDED", [Operand("BF16", (1 << 20, 256)), Operand("I32", (1 << 24, 256), (1, 0)),
+                         Operand("BF16", (1 << 24, 256))], dtype="BF16", read_index=True, oob="ZERO_FILL")
+    k = b.lower(g)
+    assert k.name == "up_sm100_gather_rows" and k.scalars == (_lib.OOB["ZERO_FILL"],)
+    w = Plan("KERNEL_FN", [Operand("I4", (28672, 8192)), Operand("F16", (28672, 64)), Operand("BF16", (16, 8192)),
+                           Operand("BF16", (16, 28672))])
+    k = b.lower(w)
+    assert k.name == "up_sm100_w4a16_gemm" and k.scalars == (128,)
+    d = Plan("KERNEL_FN", [Operand("I4", (256, 512)), Operand("F16", (256, 4)), Operand("BF16", (256, 512))])
+    assert b.lower(d).name == "up_sm100_dequant_i4_bf16"
+
+
+@pytest.mark.parametrize("plan,variant", [
+    (_red("SUM", "F64"), "UnsupportedDtype"),
+    (_red("PROD", "F32"), "UnsupportedOp"),
+    (_red("SUM", "F32", axes_mask=1), "UnsupportedPlanShape"),
+    (_red("ARGMAX", "BF16", "F32"), "InadmissiblePlan"),
+    (_red("SUM", "F32", accum="AUTO", block=3), "UnsupportedPlanShape"),
+    (Plan("SCAN", [Operand("F32", (8,)), Operand("F32", (8,))], dtype="F32"), "UnsupportedDtype"),
+    (Plan("SCAN", [Operand("I32", (4, 8)), Operand("I32", (4, 8))], dtype="I32", scan_axis=0), "UnsupportedPlanShape"),
+    (Plan("STRIDED", [Operand("F32", (8,)), Operand("F32", (8,))]), "UnsupportedSchedule"),
+    (Plan("WINDOW", [Operand("F32", (8,)), Operand("F32", (8,))]), "UnsupportedSchedule"),
+    (Plan("CONTRACTION", [Operand("F32", (8, 8)), Operand("F32", (8, 8))]), "UnsupportedSchedule"),
+    (Plan("KERNEL_FN", [Operand("F32", (8,))]), "UnsupportedKernel"),
+    (_red("SUM", "F32", target="cuda:sm90a"), "UnsupportedSchedule"),
+])
+def test_refuses_rather_than_approximates(plan, variant):
+    with pytest.raises(LowerError) as e:
+        CudaSm100().lower(plan)
+    assert e.value.variant == variant
+
+
+def test_argument_errors_return_before_any_device_work():
+    L = _lib.load()
+    # negative extents, unknown ops and policies are refused on the host
+    assert L.up_sm100_row_sum_f32(None, -1, 4, 4, None, 1, 256, None) == _lib.UP_ERR_INVALID
+    assert L.up_sm100_row_sum_f32(None, 0, 4, 4, None, 1, 256, None) == _lib.UP_OK  # empty: nothing to do
+    assert L.up_sm100_scan_i32(None, None, 1, 8, 7, 0, 0, None, None, 0, None) == _lib.UP_ERR_UNSUPPORTED
+    assert L.up_sm100_scan_i32(None, None, 0, 8, 0, 0, 0, None, None, 0, None) == _lib.UP_OK
+    assert L.up_sm100_gather_rows(None, 4, 16, None, _lib.EK["F32"], 4, 0, None, None) == _lib.UP_ERR_UNSUPPORTED
+    assert L.up_sm100_gather_rows(None, 4, 16, None, _lib.EK["I32"], 4, 9, None, None) == _lib.UP_ERR_UNSUPPORTED
+    assert L.up_sm100_dequant_i4_bf16(None, None, 4, 100, 64, None, None) == _lib.UP_ERR_UNSUPPORTED
+    assert L.up_sm100_w4a16_gemm(None, None, None, 17, 128, 128, 128, None, None, 0, None) == _lib.UP_ERR_UNSUPPORTED
+    assert L.up_sm100_w4a16_gemm(None, None, None, 16, 128, 100, 128, None, None, 0, None) == _lib.UP_ERR_UNSUPPORTED
+    assert L.up_sm100_reduce_i32(None, 4, 4, None, None) == _lib.UP_ERR_INVALID
+
+
+def test_workspace_sizes():
+    L = _lib.load()
+    assert L.up_sm100_scan_workspace_bytes(1, 1 << 28) == 64 + 8 * ((1 << 28) // 4096)
+    assert L.up_sm100_scan_workspace_bytes(3, 10000) == 64 + 8 * 3 * 3
+    assert L.up_sm100_w4a16_workspace_bytes(16, 28672, 8192, 128) > 64
+    n = ctypes.c_size_t(0)
+    ins = (_lib.UpTensor * 1)(Operand("I32", (4, 10000)).to_c())
+    assert L.up_sm100_workspace_bytes(_lib.KERNEL["SCAN_I32"], ins, 1, ins, 1, None, 0, ctypes.byref(n)) == 0
+    assert n.value == 64 + 8 * 4 * 3

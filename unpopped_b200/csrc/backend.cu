@@ -1,0 +1,302 @@
+// backend.cu — host side of libunpopped_sm100: the Backend-seam answers (name, provider, supports_dtype,
+// plan classification) and the generic descriptor-based launch, plus the library's shared host state.
+//
+// Mirrors the reference trait `unpopped::Backend` (crates/unpopped/src/backend.rs:668-835) for the plans
+// this backend lowers, and its refusal rule "refuse rather than approximate" (backend.rs:700-707): every
+// plan outside the table below is declined with a typed LowerError, never run some other way.
+#include "common.cuh"
+
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+namespace up {
+
+static std::atomic<uint64_t> g_launches{0};
+static std::atomic<uint64_t> g_wait_ns{1000000000ull};
+static std::atomic<int> g_withhold{0};
+static thread_local char g_last_error[256] = "";
+static std::mutex g_sm_mu;
+static int g_sm_count[64] = {0};
+
+void note_launch(uint64_t k) { g_launches.fetch_add(k, std::memory_order_relaxed); }
+
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return UP_OK;
+  std::snprintf(g_last_error, sizeof(g_last_error), "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
+  return UP_ERR_CUDA;
+}
+
+int check_launch() { return cuda_status(cudaGetLastError()); }
+
+uint64_t wait_limit_ns() { return g_wait_ns.load(std::memory_order_relaxed); }
+
+int take_withhold_flag() { return g_withhold.exchange(0); }
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lk(g_sm_mu);
+  if (g_sm_count[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    g_sm_count[dev] = n;
+  }
+  return g_sm_count[dev];
+}
+
+static bool is_our_target(const char* t) {
+  if (!t) return false;
+  return !std::strcmp(t, "cuda:sm_100a") || !std::strcmp(t, "cuda:sm100a") || !std::strcmp(t, "cuda:sm100") ||
+         !std::strcmp(t, "cuda:sm_100");
+}
+
+static size_t elem_bits(int ek) {
+  switch (ek) {
+    case UP_EK_F16: case UP_EK_BF16: case UP_EK_I16: case UP_EK_U16: return 16;
+    case UP_EK_F32: case UP_EK_F32_STRICT: case UP_EK_I32: case UP_EK_U32: return 32;
+    case UP_EK_F64: case UP_EK_I64: case UP_EK_U64: case UP_EK_COMPLEX64: return 64;
+    case UP_EK_COMPLEX128: return 128;
+    case UP_EK_I8: case UP_EK_U8: case UP_EK_BOOL: case UP_EK_FP8_E4M3FN: case UP_EK_FP8_E5M2:
+    case UP_EK_F8_E8M0: case UP_EK_F8_E6M2: return 8;
+    case UP_EK_I4: case UP_EK_U4: return 4;
+    default: return 0;
+  }
+}
+
+static const char* k_name(int id) {
+  switch (id) {
+    case UP_K_ROW_SUM_F32: return "up_sm100_row_sum_f32";
+    case UP_K_ROW_MAX_ARGMAX_BF16: return "up_sm100_row_max_argmax_bf16";
+    case UP_K_SCAN_I32: return "up_sm100_scan_i32";
+    case UP_K_GATHER_ROWS: return "up_sm100_gather_rows";
+    case UP_K_DEQUANT_I4: return "up_sm100_dequant_i4_bf16";
+    case UP_K_W4A16_GEMM: return "up_sm100_w4a16_gemm";
+    default: return "";
+  }
+}
+
+static int refuse(up_lowered* out, int err, const char* detail) {
+  out->kernel_id = UP_K_NONE;
+  out->lower_error = err;
+  out->name[0] = '\0';
+  std::snprintf(out->detail, sizeof(out->detail), "%s", detail);
+  out->n_scalars = 0;
+  return UP_ERR_UNSUPPORTED;
+}
+
+static int accept(up_lowered* out, int id, std::initializer_list<int64_t> scalars) {
+  out->kernel_id = id;
+  out->lower_error = UP_LOWER_OK;
+  std::snprintf(out->name, sizeof(out->name), "%s", k_name(id));
+  out->detail[0] = '\0';
+  out->n_scalars = 0;
+  for (int64_t v : scalars) out->scalars[out->n_scalars++] = v;
+  return UP_OK;
+}
+
+// A rank-r operand is row-contiguous on its last axis and its rows stack without overlap.
+static bool last_axis_contiguous(const up_tensor& t) { return t.rank >= 1 && t.stride[t.rank - 1] == 1; }
+
+static bool dense_row_major(const up_tensor& t) {
+  int64_t s = 1;
+  for (int d = t.rank - 1; d >= 0; --d) {
+    if (t.shape[d] != 1 && t.stride[d] != s) return false;
+    s *= t.shape[d];
+  }
+  return true;
+}
+
+}  // namespace up
+
+using namespace up;
+
+extern "C" int up_sm100_version(void) { return UP_SM100_ABI_VERSION; }
+extern "C" const char* up_sm100_name(void) { return "cuda_sm100"; }
+extern "C" const char* up_sm100_provider(void) { return "unpopped-cuda-sm100"; }
+extern "C" uint64_t up_sm100_launch_count(void) { return g_launches.load(); }
+extern "C" const char* up_sm100_last_error(void) { return g_last_error; }
+extern "C" void up_sm100_set_wait_limit_ns(uint64_t ns) { g_wait_ns.store(ns ? ns : 1); }
+extern "C" void up_sm100_set_test_withhold_flag(int enable) { g_withhold.store(enable ? 1 : 0); }
+
+extern "C" int up_sm100_supports_dtype(int dtype, const char* target) {
+  if (!is_our_target(target)) return 1;  // Unsupported: not this backend's target
+  if (dtype < 0 || dtype >= UP_EK_COUNT) return 1;
+  // Reserved tokens (no computation semantics at this schema version, element.rs:1112-1135): decline.
+  if (dtype == UP_EK_FP8_E4M3FNUZ || dtype == UP_EK_FP8_E5M2FNUZ) return 1;
+  // Every dtype a kernel of this backend takes in some role: f32 (sum), bf16 (max/argmax, W4A16, dequant
+  // output), f16 (group scales), i32/i64/u32 (scans, indices, argmax), i4 (packed weights), and every
+  // fixed-width storage type of at least one byte, which the row gather moves bit for bit.
+  if (dtype == UP_EK_I4) return 0;
+  if (dtype == UP_EK_U4 || dtype == UP_EK_B1) return 1;
+  if (dtype == UP_EK_F4_E2M1 || dtype == UP_EK_F6_E2M3 || dtype == UP_EK_F6_E3M2) return 1;
+  return elem_bits(dtype) >= 8 ? 0 : 1;
+}
+
+extern "C" int up_sm100_classify(const up_plan_desc* p, up_lowered* out) {
+  if (!p || !out) return UP_ERR_INVALID;
+  std::memset(out, 0, sizeof(*out));
+  if (!is_our_target(p->target)) return refuse(out, UP_LOWER_UNSUPPORTED_SCHEDULE, "target is not cuda:sm_100a");
+  if (p->n_operands < 0 || p->n_operands > 8) return refuse(out, UP_LOWER_INADMISSIBLE_PLAN, "operand count");
+  const up_tensor* ops = p->operands;
+  switch (p->schedule) {
+    case UP_SCHED_REDUCTION: {
+      if (p->n_operands < 2) return refuse(out, UP_LOWER_INADMISSIBLE_PLAN, "a reduction has an input and an output");
+      const up_tensor& in = ops[0];
+      const bool last_axis = p->axes_mask == 0 || (in.rank >= 1 && p->axes_mask == (1u << (in.rank - 1)));
+      if (!last_axis) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "only the last axis is reduced");
+      if (!p->identity_body) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "body/post must be the identity");
+      if (!last_axis_contiguous(in)) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "reduced axis must be contiguous");
+      if (p->op == UP_OP_SUM) {
+        if (p->dtype != UP_EK_F32) return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "Sum is lowered for f32");
+        if (p->accum != UP_ACCUM_AUTO && p->accum != UP_ACCUM_F32)
+          return refuse(out, UP_LOWER_UNSUPPORTED_OP, "accumulation policy");
+        const int b = p->block ? p->block : 256;
+        if (b < 1 || b > 1024 || (b & (b - 1))) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "block B");
+        return accept(out, UP_K_ROW_SUM_F32, {p->accum, b});
+      }
+      if (p->op == UP_OP_MAX || p->op == UP_OP_ARGMAX) {
+        if (p->dtype != UP_EK_BF16) return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "Max/ArgMax are lowered for bf16");
+        if (p->op == UP_OP_ARGMAX && p->out_dtype != UP_EK_I64 && p->out_dtype != UP_EK_I32)
+          return refuse(out, UP_LOWER_INADMISSIBLE_PLAN, "ArgMax needs an I64 (or I32) output");
+        if (p->op == UP_OP_MAX && p->out_dtype != UP_EK_F32)
+          return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "Max is stored as f32");
+        return accept(out, UP_K_ROW_MAX_ARGMAX_BF16, {});
+      }
+      return refuse(out, UP_LOWER_UNSUPPORTED_OP, "reduction op not lowered by this backend");
+    }
+    case UP_SCHED_SCAN: {
+      if (p->n_operands < 2) return refuse(out, UP_LOWER_INADMISSIBLE_PLAN, "a scan has an input and an output");
+      if (p->dtype != UP_EK_I32) return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "scans are lowered for i32");
+      if (p->op != UP_OP_SUM && p->op != UP_OP_MAX && p->op != UP_OP_MIN)
+        return refuse(out, UP_LOWER_UNSUPPORTED_OP, "scan op");
+      if (p->scan_axis != ops[0].rank - 1) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "only the last axis is scanned");
+      if (!dense_row_major(ops[0]) || !dense_row_major(ops[1]))
+        return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "scan operands must be dense row-major");
+      return accept(out, UP_K_SCAN_I32, {p->op, p->exclusive ? 1 : 0, p->reverse ? 1 : 0});
+    }
+    case UP_SCHED_STRIDED: {
+      if (!p->has_read_index) return refuse(out, UP_LOWER_UNSUPPORTED_SCHEDULE, "only the gather form of Strided");
+      if (p->gather_axis != 0) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "gather along axis 0 only");
+      if (p->index_dtype != UP_EK_I32 && p->index_dtype != UP_EK_I64 && p->index_dtype != UP_EK_U32)
+        return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "index dtype");
+      if (p->n_operands < 3) return refuse(out, UP_LOWER_INADMISSIBLE_PLAN, "table, ids and output");
+      if (!dense_row_major(ops[0]) || !dense_row_major(ops[2]))
+        return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "table and output must be dense row-major");
+      for (int d = 1; d < ops[1].rank; ++d)
+        if (ops[1].stride[d] != 0 && ops[1].shape[d] != 1)
+          return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "ids must be 1-D, broadcast over the row");
+      if (elem_bits(ops[0].dtype) < 8) return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "sub-byte table");
+      return accept(out, UP_K_GATHER_ROWS, {p->oob});
+    }
+    case UP_SCHED_KERNEL_FN: {
+      if (p->n_operands == 3 && ops[0].dtype == UP_EK_I4 && ops[1].dtype == UP_EK_F16 && ops[2].dtype == UP_EK_BF16) {
+        const int64_t group = ops[1].shape[1] > 0 ? ops[0].shape[1] / ops[1].shape[1] : 0;
+        return accept(out, UP_K_DEQUANT_I4, {group});
+      }
+      if (p->n_operands == 4 && ops[0].dtype == UP_EK_I4 && ops[1].dtype == UP_EK_F16 && ops[2].dtype == UP_EK_BF16 &&
+          ops[3].dtype == UP_EK_BF16) {
+        const int64_t group = ops[1].shape[1] > 0 ? ops[0].shape[1] / ops[1].shape[1] : 0;
+        return accept(out, UP_K_W4A16_GEMM, {group});
+      }
+      return refuse(out, UP_LOWER_UNSUPPORTED_KERNEL, "kernel-layer function is not the dequant/W4A16 form");
+    }
+    default:
+      return refuse(out, UP_LOWER_UNSUPPORTED_SCHEDULE, "schedule not lowered by this backend");
+  }
+}
+
+static const char* at(const up_tensor& t) {
+  const size_t bits = elem_bits(t.dtype);
+  return static_cast<const char*>(t.ptr) + (int64_t)((t.base * (int64_t)bits) / 8);
+}
+
+extern "C" int up_sm100_workspace_bytes(int kernel_id, const up_tensor* ins, int n_in, const up_tensor* outs, int n_out,
+                                        const int64_t* scalars, int n_scalars, size_t* bytes) {
+  (void)outs; (void)n_out;
+  if (!bytes) return UP_ERR_INVALID;
+  *bytes = 0;
+  if (kernel_id == UP_K_SCAN_I32) {
+    if (!ins || n_in < 1 || ins[0].rank < 1) return UP_ERR_INVALID;
+    int64_t rows = 1;
+    for (int d = 0; d < ins[0].rank - 1; ++d) rows *= ins[0].shape[d];
+    *bytes = up_sm100_scan_workspace_bytes(rows, ins[0].shape[ins[0].rank - 1]);
+  } else if (kernel_id == UP_K_W4A16_GEMM) {
+    if (!ins || n_in < 3 || !scalars || n_scalars < 1) return UP_ERR_INVALID;
+    *bytes = up_sm100_w4a16_workspace_bytes(ins[2].shape[0], ins[0].shape[0], ins[0].shape[1], scalars[0]);
+  }
+  return UP_OK;
+}
+
+extern "C" int up_sm100_launch(int kernel_id, const up_tensor* ins, int n_in, const up_tensor* outs, int n_out,
+                               const int64_t* scalars, int n_scalars, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  if (!ins || !outs) return UP_ERR_INVALID;
+  auto sc = [&](int i, int64_t dflt) { return (scalars && i < n_scalars) ? scalars[i] : dflt; };
+  switch (kernel_id) {
+    case UP_K_ROW_SUM_F32: {
+      if (n_in < 1 || n_out < 1) return UP_ERR_INVALID;
+      const up_tensor &x = ins[0], &y = outs[0];
+      if (x.dtype != UP_EK_F32 || y.dtype != UP_EK_F32 || x.rank != 2 || x.stride[1] != 1) return UP_ERR_UNSUPPORTED;
+      if (y.shape[0] != x.shape[0] || (y.rank == 1 && y.stride[0] != 1)) return UP_ERR_UNSUPPORTED;
+      return up_sm100_row_sum_f32(reinterpret_cast<const float*>(at(x)), x.shape[0], x.shape[1], x.stride[0],
+                                  (float*)at(y), (int)sc(0, UP_ACCUM_F32), (int)sc(1, 256), stream);
+    }
+    case UP_K_ROW_MAX_ARGMAX_BF16: {
+      if (n_in < 1 || n_out < 2) return UP_ERR_INVALID;
+      const up_tensor &x = ins[0], &mx = outs[0], &am = outs[1];
+      if (x.dtype != UP_EK_BF16 || x.rank != 2 || x.stride[1] != 1) return UP_ERR_UNSUPPORTED;
+      if (mx.ptr && mx.dtype != UP_EK_F32) return UP_ERR_UNSUPPORTED;
+      if (am.ptr && am.dtype != UP_EK_I32 && am.dtype != UP_EK_I64) return UP_ERR_UNSUPPORTED;
+      return up_sm100_row_max_argmax_bf16(reinterpret_cast<const uint16_t*>(at(x)), x.shape[0], x.shape[1], x.stride[0],
+                                          mx.ptr ? (float*)at(mx) : nullptr,
+                                          (am.ptr && am.dtype == UP_EK_I32) ? (int32_t*)at(am) : nullptr,
+                                          (am.ptr && am.dtype == UP_EK_I64) ? (int64_t*)at(am) : nullptr, stream);
+    }
+    case UP_K_SCAN_I32: {
+      if (n_in < 1 || n_out < 1) return UP_ERR_INVALID;
+      const up_tensor &x = ins[0], &y = outs[0];
+      if (x.dtype != UP_EK_I32 || y.dtype != UP_EK_I32 || x.rank < 1) return UP_ERR_UNSUPPORTED;
+      if (!dense_row_major(x) || !dense_row_major(y)) return UP_ERR_UNSUPPORTED;
+      int64_t rows = 1;
+      for (int d = 0; d < x.rank - 1; ++d) rows *= x.shape[d];
+      return up_sm100_scan_i32(reinterpret_cast<const int32_t*>(at(x)), (int32_t*)at(y), rows, x.shape[x.rank - 1],
+                               (int)sc(0, UP_OP_SUM), (int)sc(1, 0), (int)sc(2, 0), nullptr, workspace,
+                               workspace_bytes, stream);
+    }
+    case UP_K_GATHER_ROWS: {
+      if (n_in < 2 || n_out < 1) return UP_ERR_INVALID;
+      const up_tensor &tab = ins[0], &ids = ins[1], &o = outs[0];
+      if (tab.rank < 1 || tab.dtype != o.dtype || !dense_row_major(tab) || !dense_row_major(o)) return UP_ERR_UNSUPPORTED;
+      int64_t row_elems = 1;
+      for (int d = 1; d < tab.rank; ++d) row_elems *= tab.shape[d];
+      const int64_t row_bytes = row_elems * (int64_t)elem_bits(tab.dtype) / 8;
+      const int64_t n = o.shape[0];
+      if (ids.rank < 1 || ids.shape[0] != n || ids.stride[0] != 1) return UP_ERR_UNSUPPORTED;
+      return up_sm100_gather_rows(at(tab), tab.shape[0], row_bytes, at(ids), ids.dtype, n, (int)sc(0, UP_OOB_SKIP),
+                                  (void*)at(o), stream);
+    }
+    case UP_K_DEQUANT_I4: {
+      if (n_in < 2 || n_out < 1) return UP_ERR_INVALID;
+      const up_tensor &w = ins[0], &s = ins[1], &o = outs[0];
+      if (w.dtype != UP_EK_I4 || s.dtype != UP_EK_F16 || o.dtype != UP_EK_BF16) return UP_ERR_UNSUPPORTED;
+      if (!dense_row_major(w) || !dense_row_major(s) || !dense_row_major(o) || w.base % 2) return UP_ERR_UNSUPPORTED;
+      return up_sm100_dequant_i4_bf16(reinterpret_cast<const uint8_t*>(at(w)), reinterpret_cast<const uint16_t*>(at(s)),
+                                      w.shape[0], w.shape[1], sc(0, 128), (uint16_t*)at(o), stream);
+    }
+    case UP_K_W4A16_GEMM: {
+      if (n_in < 3 || n_out < 1) return UP_ERR_INVALID;
+      const up_tensor &w = ins[0], &s = ins[1], &x = ins[2], &o = outs[0];
+      if (w.dtype != UP_EK_I4 || s.dtype != UP_EK_F16 || x.dtype != UP_EK_BF16 || o.dtype != UP_EK_BF16)
+        return UP_ERR_UNSUPPORTED;
+      if (!dense_row_major(w) || !dense_row_major(s) || !dense_row_major(x) || !dense_row_major(o) || w.base % 2)
+        return UP_ERR_UNSUPPORTED;
+      return up_sm100_w4a16_gemm(reinterpret_cast<const uint8_t*>(at(w)), reinterpret_cast<const uint16_t*>(at(s)),
+                                 reinterpret_cast<const uint16_t*>(at(x)), x.shape[0], w.shape[0], w.shape[1], sc(0, 128),
+                                 (uint16_t*)at(o), workspace, workspace_bytes, stream);
+    }
+    default:
+      return UP_ERR_UNSUPPORTED;
+  }
+}

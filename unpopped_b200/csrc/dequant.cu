@@ -1,0 +1,107 @@
+// dequant.cu — group-wise int4 -> bf16 dequant for sm_100a: out[n][k] = bf16(w[n][k] * scale[n][k/group]).
+//
+// Semantics: the i4 reader of the reference (two per byte, low nibble = even index, sign-extended;
+// crates/unpopped/tests/sub_byte_packing.rs:24-40, crates/unpopped/src/cfamily.rs:446-470) and the
+// dequant product of crates/unpopped/tests/support/dequant.rs:163-178 with a f16 group scale and no zero
+// point. w * scale needs at most 4 + 11 significant bits, so the f32 product is exact and the bf16
+// conversion is the single round-to-nearest-even the oracle's f64 path performs (encode_float's Bf16 arm,
+// crates/unpopped/src/oracle/expr_eval.rs:520-530).
+//
+// Each thread turns one 32-bit word of w (8 nibbles) into one 16-byte chunk of output: the int4 bytes are
+// read 4 per lane and the bf16 bytes written 16 per lane, both as contiguous warp accesses.
+#include "common.cuh"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace up {
+
+// 8 signed nibbles of `q` (low first) times `s`, as four packed bf16x2 words.
+__device__ __forceinline__ uint4 dequant8(uint32_t q, float s) {
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    // 2^23 + (nibble ^ 8) as an f32, minus 2^23 + 8: the signed nibble, exactly.
+    const uint32_t a = ((q >> (8 * j)) & 0xfu) ^ 0x8u;
+    const uint32_t b = ((q >> (8 * j + 4)) & 0xfu) ^ 0x8u;
+    const float fa = (__uint_as_float(0x4b000000u | a) - 8388616.0f) * s;
+    const float fb = (__uint_as_float(0x4b000000u | b) - 8388616.0f) * s;
+    uint32_t packed;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(packed) : "f"(fb), "f"(fa));
+    o[j] = packed;
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// k % 8 == 0 and group % 8 == 0: a word of w never straddles a row or a group.
+__global__ void __launch_bounds__(256) dequant_i4_vec_kernel(const uint32_t* __restrict__ w,
+                                                             const __half* __restrict__ scale, int64_t n, int64_t k,
+                                                             int64_t group, uint4* __restrict__ out) {
+  const int64_t words = n * (k >> 3);
+  const int64_t wpr = k >> 3;
+  const int64_t gpr = k / group;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < words; i += 4 * stride) {
+    uint32_t q[4];
+    float s[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t wi = i + u * stride;
+      q[u] = __ldg(w + wi);
+      const int64_t r = wi / wpr, c = (wi - r * wpr) << 3;
+      s[u] = __half2float(scale[r * gpr + c / group]);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) st_cs_v4(out + i + u * stride, dequant8(q[u], s[u]));
+  }
+  for (; i < words; i += stride) {
+    const int64_t r = i / wpr, c = (i - r * wpr) << 3;
+    st_cs_v4(out + i, dequant8(__ldg(w + i), __half2float(scale[r * gpr + c / group])));
+  }
+}
+
+// Any k and group (k % group == 0): one output element per thread.
+__global__ void dequant_i4_any_kernel(const uint8_t* __restrict__ w, const __half* __restrict__ scale, int64_t n,
+                                      int64_t k, int64_t group, uint16_t* __restrict__ out) {
+  const int64_t total = n * k, gpr = k / group;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / k, c = i - r * k;
+    const uint8_t b = w[i >> 1];
+    int v = (i & 1) ? (b >> 4) : (b & 0xf);
+    v = v >= 8 ? v - 16 : v;
+    const float f = (float)v * __half2float(scale[r * gpr + c / group]);
+    out[i] = __bfloat16_as_ushort(__float2bfloat16_rn(f));
+  }
+}
+
+}  // namespace up
+
+using namespace up;
+
+extern "C" int up_sm100_dequant_i4_bf16(const uint8_t* w, const uint16_t* scale, int64_t n, int64_t k, int64_t group,
+                                        uint16_t* out, void* stream) {
+  UP_CHECK_ARG(n >= 0 && k >= 0 && group > 0);
+  if (k % group != 0) return UP_ERR_UNSUPPORTED;
+  if (n == 0 || k == 0) return UP_OK;
+  UP_CHECK_ARG(w != nullptr && scale != nullptr && out != nullptr);
+  if ((n * k) % 2 != 0) return UP_ERR_UNSUPPORTED;  // the last byte would be half a row
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int sms = sm_count();
+  const auto* sc = reinterpret_cast<const __half*>(scale);
+  if (k % 8 == 0 && group % 8 == 0 && aligned(w, 4) && aligned(out, 16)) {
+    const int64_t words = n * (k / 8);
+    int64_t blocks = (words + 255) / 256;
+    const int64_t cap = (int64_t)sms * 8;
+    if (blocks > cap) blocks = cap;
+    dequant_i4_vec_kernel<<<(int)blocks, 256, 0, s>>>(reinterpret_cast<const uint32_t*>(w), sc, n, k, group,
+                                                      reinterpret_cast<uint4*>(out));
+  } else {
+    int64_t blocks = (n * k + 255) / 256;
+    const int64_t cap = (int64_t)sms * 16;
+    if (blocks > cap) blocks = cap;
+    dequant_i4_any_kernel<<<(int)blocks, 256, 0, s>>>(w, sc, n, k, group, out);
+  }
+  note_launch();
+  return check_launch();
+}

@@ -1,0 +1,183 @@
+"""Tensor-level entry points over the C ABI: each lifted kernel family on torch CUDA tensors.
+
+torch supplies device memory and the current stream only; every computation runs in libunpopped_sm100.so.
+Inputs must already be on a CUDA device; nothing here moves data to the host or computes on it.
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import _lib
+from ._lib import ACCUM, EK, OOB, OP, check
+
+_OPS = {"sum": OP["SUM"], "max": OP["MAX"], "min": OP["MIN"]}
+_OOBS = {"skip": OOB["SKIP"], "clamp": OOB["CLAMP"], "zero_fill": OOB["ZERO_FILL"]}
+_IDX = {torch.int32: EK["I32"], torch.int64: EK["I64"], torch.uint32: EK["U32"]}
+
+
+def _stream(t: torch.Tensor):
+    return ctypes_ptr(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def ctypes_ptr(v):
+    return None if v in (0, None) else v
+
+
+def _cuda(t: torch.Tensor, name: str):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{name} must be a CUDA tensor")
+
+
+# ---- workspaces: zero-filled once per (device, stream, kind); the kernels re-arm them after every launch ----
+_ws_lock = threading.Lock()
+_ws_cache: dict = {}
+
+
+def workspace(kind: str, nbytes: int, device: torch.device) -> torch.Tensor:
+    """A zero-filled device workspace for `kind`, reused by later calls on the same stream."""
+    stream = torch.cuda.current_stream(device).cuda_stream
+    key = (kind, device.index, stream)
+    with _ws_lock:
+        ws = _ws_cache.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+            _ws_cache[key] = ws
+        return ws
+
+
+def workspace_status(ws: torch.Tensor) -> int:
+    """Waits for the stream and returns UP_OK or UP_ERR_DEVICE_TIMEOUT (clearing the error word)."""
+    return _lib.load().up_sm100_workspace_status(ws.data_ptr(), _stream(ws))
+
+
+def check_workspace(kind: str, device: torch.device):
+    ws = _ws_cache.get((kind, device.index, torch.cuda.current_stream(device).cuda_stream))
+    if ws is not None:
+        check(workspace_status(ws), f"{kind} device wait")
+
+
+# ---- row sum ----
+def row_sum(x: torch.Tensor, accum: str = "f32", block: int = 256, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Sum of each row of a 2-D f32 tensor (last axis). accum='f32' (fixed-order f32 tree) or 'auto' (f64 in
+    the launched lift's documented order for a block of `block` threads, bit-exact)."""
+    _cuda(x, "x")
+    if x.dtype != torch.float32 or x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("row_sum takes a 2-D float32 tensor with contiguous rows")
+    rows, cols = x.shape
+    if out is None:
+        out = torch.empty(rows, dtype=torch.float32, device=x.device)
+    check(_lib.load().up_sm100_row_sum_f32(x.data_ptr(), rows, cols, x.stride(0), out.data_ptr(),
+                                           ACCUM[accum.upper()], block, _stream(x)), "row_sum")
+    return out
+
+
+# ---- max + argmax ----
+def row_max_argmax(x: torch.Tensor, index_dtype=torch.int32, want_max: bool = True, want_argmax: bool = True):
+    """(max as f32, argmax) of each row of a 2-D bf16 tensor: NaN-propagating max, first index of the maximum
+    with NaN the greatest value."""
+    _cuda(x, "x")
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("row_max_argmax takes a 2-D bfloat16 tensor with contiguous rows")
+    rows, cols = x.shape
+    mx = torch.empty(rows, dtype=torch.float32, device=x.device) if want_max else None
+    am = torch.empty(rows, dtype=index_dtype, device=x.device) if want_argmax else None
+    p32 = am.data_ptr() if (am is not None and index_dtype == torch.int32) else None
+    p64 = am.data_ptr() if (am is not None and index_dtype == torch.int64) else None
+    check(_lib.load().up_sm100_row_max_argmax_bf16(x.data_ptr(), rows, cols, x.stride(0),
+                                                   mx.data_ptr() if mx is not None else None, p32, p64,
+                                                   _stream(x)), "row_max_argmax")
+    return mx, am
+
+
+# ---- scans ----
+def scan(x: torch.Tensor, op: str = "sum", exclusive: bool = False, reverse: bool = False,
+         carry: torch.Tensor | None = None, out: torch.Tensor | None = None,
+         ws: torch.Tensor | None = None) -> torch.Tensor:
+    """Scan of int32 rows along the last axis (decoupled look-back, one pass)."""
+    _cuda(x, "x")
+    if x.dtype != torch.int32 or not x.is_contiguous():
+        raise ValueError("scan takes a contiguous int32 tensor")
+    k = x.shape[-1] if x.dim() > 0 else 1
+    rows = x.numel() // k if k > 0 else 0
+    if out is None:
+        out = torch.empty_like(x)
+    L = _lib.load()
+    nbytes = L.up_sm100_scan_workspace_bytes(rows, k)
+    if ws is None:
+        ws = workspace("scan", nbytes, x.device)
+    check(L.up_sm100_scan_i32(x.data_ptr(), out.data_ptr(), rows, k, _OPS[op], int(exclusive), int(reverse),
+                              carry.data_ptr() if carry is not None else None, ws.data_ptr(), ws.numel(),
+                              _stream(x)), "scan")
+    return out
+
+
+def reduce_i32(x: torch.Tensor, op: str = "sum", out: torch.Tensor | None = None) -> torch.Tensor:
+    """Fold of a whole int32 tensor to one int32 (SUM wraps)."""
+    _cuda(x, "x")
+    if x.dtype != torch.int32 or not x.is_contiguous():
+        raise ValueError("reduce_i32 takes a contiguous int32 tensor")
+    if out is None:
+        out = torch.empty(1, dtype=torch.int32, device=x.device)
+    check(_lib.load().up_sm100_reduce_i32(x.data_ptr(), x.numel(), _OPS[op], out.data_ptr(), _stream(x)),
+          "reduce_i32")
+    return out
+
+
+# ---- gather ----
+def gather_rows(table: torch.Tensor, ids: torch.Tensor, oob: str = "skip",
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[n] = table[ids[n]] (rows copied bit for bit); out-of-range ids per `oob`."""
+    _cuda(table, "table")
+    _cuda(ids, "ids")
+    if not table.is_contiguous() or ids.dim() != 1 or not ids.is_contiguous():
+        raise ValueError("gather_rows takes a contiguous table and 1-D contiguous ids")
+    if ids.dtype not in _IDX:
+        raise ValueError("ids must be int32, int64 or uint32")
+    V = table.shape[0]
+    row_bytes = (table[0].numel() if V > 0 else int(torch.Size(table.shape[1:]).numel())) * table.element_size()
+    n = ids.shape[0]
+    if out is None:
+        out = (torch.zeros if oob == "skip" else torch.empty)((n,) + tuple(table.shape[1:]), dtype=table.dtype,
+                                                              device=table.device)
+    check(_lib.load().up_sm100_gather_rows(table.data_ptr() if V > 0 else None, V, row_bytes, ids.data_ptr(),
+                                           _IDX[ids.dtype], n, _OOBS[oob], out.data_ptr(), _stream(table)),
+          "gather_rows")
+    return out
+
+
+# ---- int4 dequant and W4A16 ----
+def dequant_i4(w_packed: torch.Tensor, scale: torch.Tensor, group: int, out: torch.Tensor | None = None):
+    """bf16 [N, K] from int4 [N, K] packed two per byte ([N, K/2] uint8) and f16 scales [N, K/group]."""
+    _cuda(w_packed, "w")
+    _cuda(scale, "scale")
+    n, kh = w_packed.shape
+    k = 2 * kh
+    if out is None:
+        out = torch.empty((n, k), dtype=torch.bfloat16, device=w_packed.device)
+    check(_lib.load().up_sm100_dequant_i4_bf16(w_packed.data_ptr(), scale.data_ptr(), n, k, group, out.data_ptr(),
+                                               _stream(w_packed)), "dequant_i4")
+    return out
+
+
+def w4a16(w_packed: torch.Tensor, scale: torch.Tensor, x: torch.Tensor, group: int,
+          out: torch.Tensor | None = None, ws: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 [M, N] = x [M, K] (bf16) times the dequantized int4 weights [N, K], f32 accumulation on tcgen05."""
+    for t, nm in ((w_packed, "w"), (scale, "scale"), (x, "x")):
+        _cuda(t, nm)
+    n, kh = w_packed.shape
+    k = 2 * kh
+    m = x.shape[0]
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    L = _lib.load()
+    if ws is None:
+        ws = workspace("w4a16", L.up_sm100_w4a16_workspace_bytes(m, n, k, group), x.device)
+    check(L.up_sm100_w4a16_gemm(w_packed.data_ptr(), scale.data_ptr(), x.data_ptr(), m, n, k, group, out.data_ptr(),
+                                ws.data_ptr(), ws.numel(), _stream(x)), "w4a16")
+    return out
+
+
+def launch_count() -> int:
+    return int(_lib.load().up_sm100_launch_count())
