@@ -133,6 +133,7 @@ class Ctx:
             torch.cuda.set_device(self.local)
         self.dev = torch.device("cuda", self.local)
         self.flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=self.dev)
+        self.sleep_cycles = 1_000_000  # ~0.5 ms at the B200's 1.9 GHz SM clock
 
     def barrier(self):
         if self.world > 1:
@@ -166,6 +167,8 @@ class Ctx:
         l0 = ops.launch_count()
         for i in range(K):
             self.flush_l2()
+            # keep the GPU busy while the host enqueues the step, so the events time device work only
+            torch.cuda._sleep(self.sleep_cycles)
             ev[i][0].record()
             step(kin)
             ev[i][1].record()
@@ -350,6 +353,67 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def profile_cases(which: str):
+    """Small cases of each kernel for ncu (inputs above the 126 MB L2, a few GB on the device at most), each
+    launched 3 times with an L2 flush in between. `which`: a lift name or "all"."""
+    import torch
+
+    from unpopped_b200 import ops, workloads as wl
+
+    dev = torch.device("cuda", 0)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    cases = {}
+
+    def case(name):
+        def deco(f):
+            cases[name] = f
+            return f
+        return deco
+
+    @case("scan")
+    def _():
+        x = wl.scan_input(n=1 << 26, device=dev)
+        y = torch.empty_like(x)
+        return lambda: ops.scan(x, "sum", out=y)
+
+    @case("rowsum")
+    def _():
+        x = wl.rowsum_input(device=dev)
+        o = torch.empty(x.shape[0], device=dev)
+        return lambda: ops.row_sum(x, "f32", out=o)
+
+    @case("argmax")
+    def _():
+        x = wl.argmax_input(rows=8192, device=dev)
+        return lambda: ops.row_max_argmax(x, torch.int32)
+
+    @case("gather")
+    def _():
+        t, i = wl.gather_inputs(n=1 << 22, device=dev)
+        o = torch.empty(i.numel(), t.shape[1], dtype=t.dtype, device=dev)
+        return lambda: ops.gather_rows(t, i, "zero_fill", out=o)
+
+    @case("dequant")
+    def _():
+        d = wl.w4a16_inputs(device=dev)
+        o = torch.empty(d.n, d.k, dtype=torch.bfloat16, device=dev)
+        return lambda: ops.dequant_i4(d.w_packed, d.scale, d.group, out=o)
+
+    @case("w4a16")
+    def _():
+        d = wl.w4a16_inputs(device=dev)
+        o = torch.empty(d.m, d.n, dtype=torch.bfloat16, device=dev)
+        return lambda: ops.w4a16(d.w_packed, d.scale, d.x, d.group, out=o)
+
+    for name in (cases if which == "all" else [which]):
+        run = cases[name]()
+        for _ in range(3):
+            flush.zero_()
+            run()
+        torch.cuda.synchronize()
+        print("profiled case", name, flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -357,7 +421,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--lifts", default="all", choices=["all", "none"])
+    ap.add_argument("--profile", default=None,
+                    help="run only the small ncu case of one lift (scan, rowsum, argmax, gather, dequant, w4a16, all)")
     args = ap.parse_args()
+    if args.profile:
+        profile_cases(args.profile)
+        return
     if args.impl == "reference":
         run_reference(args)
         return

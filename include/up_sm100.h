@@ -175,7 +175,9 @@ UP_API int up_sm100_classify(const up_plan_desc* plan, up_lowered* out);
 /* ---- Generic launch ------------------------------------------------------------------------------ */
 
 /* Workspace bytes `up_sm100_launch(id, ...)` needs (0 when none). The workspace must be zero-filled
- * once before its first use (`cudaMemset`); the kernels leave it ready for the next launch. */
+ * once before its first use (`cudaMemset`); every launch that completes without an error leaves it ready
+ * for the next launch of any shape (the kernels re-arm their counters and clear their partial sums). After
+ * UP_ERR_DEVICE_TIMEOUT, zero-fill it again. Launches that overlap on the GPU need separate workspaces. */
 UP_API int up_sm100_workspace_bytes(int kernel_id, const up_tensor* ins, int n_in, const up_tensor* outs,
                              int n_out, const int64_t* scalars, int n_scalars, size_t* bytes);
 

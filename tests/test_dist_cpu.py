@@ -1,0 +1,194 @@
+"""The multi-GPU exchange logic (unpopped_b200/dist.py) on world_size-2 and -3 gloo ranks on the CPU.
+
+The per-rank kernels are stood in by the CPU oracle (test infrastructure): what is under test is the sharding,
+the all-gather of shard totals, the carry each rank derives from them and the reassembly of outputs. Also a
+rank that leaves before the exchange: the other rank's collective ends with an error within the short
+process-group timeout instead of waiting forever.
+"""
+import datetime
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+OPS = {"sum": 0, "max": 2, "min": 3}
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def cpu_local():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+
+    from unpopped_b200.dist import Local
+
+    def reduce_i32(x, op):
+        return torch.tensor([orc.reduce_i32(x.numpy(), OPS[op])], dtype=torch.int32)
+
+    def scan(x, op, ex, rev, carry):
+        c = int(carry.item()) if carry is not None else None
+        return torch.from_numpy(orc.scan_i32(x.numpy(), OPS[op], ex, rev, carry=c))
+
+    def w4a16(w, s, x, g):
+        n, kh = w.shape
+        out, _, _ = orc.w4a16(w.numpy(), s.view(torch.int16).numpy().view(np.uint16),
+                              x.view(torch.int16).numpy().view(np.uint16), x.shape[0], n, 2 * kh, g)
+        return torch.from_numpy(out.view(np.int16)).view(torch.bfloat16)
+
+    return Local(reduce_i32=reduce_i32, scan=scan, w4a16=w4a16)
+
+
+def _init(rank, world, port, timeout_s=30):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    sys.path.insert(0, ROOT)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def _scan_worker(rank, world, port, n_per, q):
+    try:
+        _init(rank, world, port)
+        from unpopped_b200.dist import sharded_scan
+
+        rng = np.random.default_rng(123)
+        full = rng.integers(-(2 ** 31), 2 ** 31 - 1, size=n_per * world, dtype=np.int64).astype(np.int32)
+        mine = torch.from_numpy(full[rank * n_per:(rank + 1) * n_per].copy())
+        res = {}
+        for op in OPS:
+            for ex in (False, True):
+                for rev in (False, True):
+                    res[(op, ex, rev)] = sharded_scan(mine, op, ex, rev, local=cpu_local()).numpy()
+        q.put((rank, res))
+        dist.destroy_process_group()
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_scan_equals_global_scan(world):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+
+    n_per = 5000
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_scan_worker, args=(r, world, port, n_per, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    rng = np.random.default_rng(123)
+    full = rng.integers(-(2 ** 31), 2 ** 31 - 1, size=n_per * world, dtype=np.int64).astype(np.int32)
+    for r in range(world):
+        assert isinstance(got[r], dict), got[r]
+    for key in got[0]:
+        op, ex, rev = key
+        want = orc.scan_i32(full, OPS[op], ex, rev)
+        cat = np.concatenate([got[r][key] for r in range(world)])
+        assert np.array_equal(cat, want), key
+
+
+def _w4_worker(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        from unpopped_b200.dist import gather_outputs, row_slice, sharded_w4a16
+
+        g = torch.Generator().manual_seed(7)
+        n, k, m, grp = 64 * world, 256, 3, 128
+        w = torch.randint(0, 256, (n, k // 2), generator=g, dtype=torch.int32).to(torch.uint8)
+        s = (torch.rand(n, k // grp, generator=g) * 0.015 + 0.005).to(torch.float16)
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+        sl = row_slice(n, world, rank)
+        y = sharded_w4a16(w[sl].contiguous(), s[sl].contiguous(), x, grp, local=cpu_local())
+        rows = gather_outputs(torch.arange(rank * 4, rank * 4 + 4, dtype=torch.int32).reshape(4, 1))
+        q.put((rank, (y.view(torch.int16).numpy(), rows.numpy())))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, repr(e)))
+
+
+def test_sharded_w4a16_and_output_gather():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_w4_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        assert isinstance(got[r], tuple), got[r]
+    g = torch.Generator().manual_seed(7)
+    n, k, m, grp = 64 * world, 256, 3, 128
+    w = torch.randint(0, 256, (n, k // 2), generator=g, dtype=torch.int32).to(torch.uint8)
+    s = (torch.rand(n, k // grp, generator=g) * 0.015 + 0.005).to(torch.float16)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    want, _, _ = orc.w4a16(w.numpy(), s.view(torch.int16).numpy().view(np.uint16),
+                           x.view(torch.int16).numpy().view(np.uint16), m, n, k, grp)
+    for r in range(world):
+        assert np.array_equal(got[r][0].view(np.uint16), want)
+        assert got[r][1].reshape(-1).tolist() == list(range(4 * world))
+
+
+def test_row_slice_covers_every_row_once():
+    from unpopped_b200.dist import row_slice
+
+    for n in (0, 1, 7, 8192, 8193):
+        for world in (1, 2, 3, 8):
+            covered = []
+            for r in range(world):
+                s = row_slice(n, world, r)
+                covered.extend(range(s.start, s.stop))
+            assert covered == list(range(n))
+
+
+def _leaving_worker(rank, world, port, q):
+    try:
+        _init(rank, world, port, timeout_s=5)
+        if rank == 1:
+            q.put((rank, "left"))
+            q.close()
+            q.join_thread()  # flush the message before the abrupt exit
+            os._exit(0)  # leaves between steps, before the exchange
+        from unpopped_b200.dist import sharded_scan
+
+        try:
+            sharded_scan(torch.arange(10, dtype=torch.int32), "sum", local=cpu_local())
+            q.put((rank, "completed"))
+        except Exception as e:
+            q.put((rank, "error:" + type(e).__name__))
+    except Exception as e:
+        q.put((rank, "setup:" + repr(e)))
+
+
+def test_a_rank_that_leaves_ends_the_exchange_with_an_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert got[1] == "left"
+    assert got[0].startswith("error:"), got[0]

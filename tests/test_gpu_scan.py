@@ -39,7 +39,7 @@ def test_golden_corpora_every_variant(case):
         assert run(x, op, mode == "excl", direction == "rev").tolist() == exp, key
 
 
-SIZES = [1, 2, 31, 512, 4095, 4096, 4097, 8192 + 5, 100_003, (1 << 20) + 12]
+SIZES = [1, 2, 31, 512, 4095, 4096, 4097, 16383, 16384, 16385, 2 * 16384 + 8, 100_003, (1 << 20) + 12]
 
 
 @pytest.mark.parametrize("n", SIZES)
@@ -53,7 +53,7 @@ def test_one_row_bit_exact(n, op):
             assert np.array_equal(got, orc.scan_i32(x, OPS[op], excl, rev)), (excl, rev)
 
 
-@pytest.mark.parametrize("rows,k", [(3, 10_000), (1000, 45), (7, 4096), (2, 12_289)])
+@pytest.mark.parametrize("rows,k", [(3, 10_000), (1000, 45), (7, 4096), (2, 12_289), (3, 40_000), (2, 16_384 * 3 + 2)])
 def test_many_rows(rows, k):
     rng = np.random.default_rng(rows + k)
     x = rng.integers(-50, 50, size=(rows, k)).astype(np.int32)
@@ -105,7 +105,7 @@ def test_bounded_wait_reports_timeout_and_recovers():
     """Tile 0 withholds its flag (a flag nothing sets): every other tile's look-back gives up after the wait
     limit, the status comes back as UP_ERR_DEVICE_TIMEOUT, and the next launch works. No fault, no hang."""
     L = _lib.load()
-    x = torch.ones(1 << 16, dtype=torch.int32, device="cuda")  # 16 tiles
+    x = torch.ones(1 << 18, dtype=torch.int32, device="cuda")  # 16 tiles
     ws = torch.zeros(L.up_sm100_scan_workspace_bytes(1, x.numel()), dtype=torch.uint8, device="cuda")
     L.up_sm100_set_wait_limit_ns(2_000_000)  # 2 ms
     try:

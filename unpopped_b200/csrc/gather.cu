@@ -28,7 +28,7 @@ __global__ void __launch_bounds__(256) gather_rows_vec_kernel(const uint4* __res
   const int lane = threadIdx.x & 31;
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t tw = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  const int64_t hi = V - 1;
+  const int64_t hi = V > 0 ? V - 1 : 0;  // clamp bound of the load address; V itself bounds the range
   for (int64_t r0 = gw * UNROLL; r0 < n; r0 += tw * UNROLL) {
     int64_t my = 0;
     if (lane < UNROLL && r0 + lane < n) my = read_index(ids, kind, r0 + lane);
@@ -45,7 +45,7 @@ __global__ void __launch_bounds__(256) gather_rows_vec_kernel(const uint4* __res
 #pragma unroll
       for (int u = 0; u < UNROLL; ++u) {
         if (r0 + u >= n) continue;
-        const bool bad = raw[u] < 0 || raw[u] > hi;
+        const bool bad = raw[u] < 0 || raw[u] >= V;
         if (bad && oob == UP_OOB_SKIP) continue;
         st_cs_v4(out + (r0 + u) * row_vecs + c, (bad && oob == UP_OOB_ZERO_FILL) ? make_uint4(0u, 0u, 0u, 0u) : val[u]);
       }
@@ -59,12 +59,12 @@ __global__ void gather_rows_any_kernel(const W* __restrict__ table, int64_t V, i
                                        const void* __restrict__ ids, int kind, int64_t n, int oob,
                                        W* __restrict__ out) {
   const int64_t total = n * row_words;
-  const int64_t hi = V - 1;
+  const int64_t hi = V > 0 ? V - 1 : 0;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / row_words, c = i - r * row_words;
     const int64_t raw = read_index(ids, kind, r);
     const int64_t g = raw < 0 ? 0 : (raw > hi ? hi : raw);
-    const bool bad = raw < 0 || raw > hi;
+    const bool bad = raw < 0 || raw >= V;
     if (bad && oob == UP_OOB_SKIP) continue;
     out[i] = (bad && oob == UP_OOB_ZERO_FILL) ? W(0) : table[g * row_words + c];
   }
@@ -84,8 +84,10 @@ extern "C" int up_sm100_gather_rows(const void* table, int64_t table_rows, int64
   // An empty table has no row to clamp to: only ZeroFill and Skip have a defined result.
   if (table_rows == 0 && oob == UP_OOB_CLAMP) return UP_ERR_OOB;
   UP_CHECK_ARG(table != nullptr || table_rows == 0);
-  const void* tab = table_rows == 0 ? out : table;  // never dereferenced when every index is out of range
-  const int64_t V = table_rows == 0 ? 1 : table_rows;
+  // With no table every index is out of range: the (clamped) load reads the output's first row instead and
+  // its value is never stored.
+  const void* tab = table_rows == 0 ? out : table;
+  const int64_t V = table_rows;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int sms = sm_count();
   if (row_bytes % 16 == 0 && aligned(table, 16) && aligned(out, 16)) {

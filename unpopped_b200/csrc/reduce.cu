@@ -182,67 +182,62 @@ __device__ __forceinline__ void write_max_argmax(const uint16_t* row, int64_t r,
   if (am64) am64[r] = arg;
 }
 
-// Fast path: rows of at most 65536 elements, cols % 8 == 0, 16-byte aligned rows. Each thread holds NV
-// uint4 words (8 bf16 each) of a chunk in registers; pass 1 takes their NaN-propagating max with packed
-// bf16x2 instructions, pass 2 finds the first element equal to it.
-template <int NV>
+// Fast path: rows of at most 65536 elements, cols % 8 == 0, 16-byte aligned rows. One streaming pass: for
+// every 16-byte word (8 bf16) a thread takes the NaN-propagating max with packed bf16x2 instructions and
+// keeps the first word whose max has the greatest key; at the end it re-reads that one word to find the
+// first element with that key. The block then combines the packed (key, index) words.
+__device__ __forceinline__ uint32_t word_max_bits(uint4 w) {
+  const __nv_bfloat162 a = __hmax2_nan(*reinterpret_cast<const __nv_bfloat162*>(&w.x),
+                                       *reinterpret_cast<const __nv_bfloat162*>(&w.y));
+  const __nv_bfloat162 b = __hmax2_nan(*reinterpret_cast<const __nv_bfloat162*>(&w.z),
+                                       *reinterpret_cast<const __nv_bfloat162*>(&w.w));
+  const __nv_bfloat162 m = __hmax2_nan(a, b);
+  return __bfloat16_as_ushort(__hmax_nan(__low2bfloat16(m), __high2bfloat16(m)));
+}
+
+template <int UNROLL>
 __global__ void __launch_bounds__(kRowThreads) row_max_argmax_vec_kernel(const uint16_t* __restrict__ x,
                                                                          int64_t rows, int64_t cols,
                                                                          int64_t stride, float* max_out,
                                                                          int32_t* am32, int64_t* am64) {
   __shared__ uint32_t sm32[kRowThreads / 32];
-  const int64_t nvec = cols >> 3;
+  const int nvec = (int)(cols >> 3);
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const uint16_t* row = x + r * stride;
-    uint32_t best = 0;  // (key << 16) | (0xffff - index); 0 = nothing seen
-    for (int64_t c0 = 0; c0 < nvec; c0 += (int64_t)kRowThreads * NV) {
-      uint4 w[NV];
+    const uint4* rv = reinterpret_cast<const uint4*>(row);
+    uint32_t best_key = 0;
+    int best_word = -1;
+    for (int i0 = threadIdx.x; i0 < nvec; i0 += kRowThreads * UNROLL) {
+      uint4 w[UNROLL];
 #pragma unroll
-      for (int u = 0; u < NV; ++u) {
-        const int64_t i = c0 + (int64_t)u * kRowThreads + threadIdx.x;
-        w[u] = i < nvec ? ld_nc_na_v4(row + 8 * i) : make_uint4(0u, 0u, 0u, 0u);
+      for (int u = 0; u < UNROLL; ++u) {
+        const int i = i0 + u * kRowThreads;
+        w[u] = i < nvec ? ld_nc_na_v4(rv + i) : make_uint4(0u, 0u, 0u, 0u);
       }
-      // pass 1: the NaN-propagating max of this thread's valid words
-      __nv_bfloat162 m2 = __halves2bfloat162(__ushort_as_bfloat16(0xff80u), __ushort_as_bfloat16(0xff80u));
-      bool any = false;
 #pragma unroll
-      for (int u = 0; u < NV; ++u) {
-        const int64_t i = c0 + (int64_t)u * kRowThreads + threadIdx.x;
+      for (int u = 0; u < UNROLL; ++u) {
+        const int i = i0 + u * kRowThreads;
         if (i < nvec) {
-          any = true;
-          const uint32_t q[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&q[e]);
-            m2 = __hmax2_nan(m2, h);
+          const uint32_t key = bf16_key(word_max_bits(w[u]));
+          if (best_word < 0 || key > best_key) {
+            best_key = key;
+            best_word = i;
           }
         }
-      }
-      if (any) {
-        const __nv_bfloat16 mlo = __low2bfloat16(m2), mhi = __high2bfloat16(m2);
-        const uint32_t mb = __bfloat16_as_ushort(__hmax_nan(mlo, mhi));
-        const bool mnan = bf16_isnan(mb);
-        const uint32_t mkey = bf16_key(mb);
-        // pass 2: first element of this thread (ascending index) with the max key
-        int64_t idx = -1;
-#pragma unroll
-        for (int u = 0; u < NV; ++u) {
-          const int64_t i = c0 + (int64_t)u * kRowThreads + threadIdx.x;
-          if (idx < 0 && i < nvec) {
-            const uint32_t q[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const uint32_t b = (q[e >> 1] >> ((e & 1) * 16)) & 0xffffu;
-              const bool hit = mnan ? bf16_isnan(b) : (bf16_key(b) == mkey);
-              if (idx < 0 && hit) idx = 8 * i + e;
-            }
-          }
-        }
-        const uint32_t cand = (mkey << 16) | (0xffffu - (uint32_t)idx);
-        best = cand > best ? cand : best;
       }
     }
-    best = block_max_u32(best, sm32);
+    uint32_t packed = 0;
+    if (best_word >= 0) {
+      const uint4 w = rv[best_word];
+      const uint32_t q[4] = {w.x, w.y, w.z, w.w};
+      int e = 0;
+#pragma unroll
+      for (int j = 7; j >= 0; --j)
+        if (bf16_key((q[j >> 1] >> ((j & 1) * 16)) & 0xffffu) == best_key) e = j;
+      const uint32_t idx = (uint32_t)(8 * best_word + e);
+      packed = (best_key << 16) | (0xffffu - idx);
+    }
+    const uint32_t best = block_max_u32(packed, sm32);
     const uint32_t key = best >> 16;
     const int64_t arg = cols > 0 ? (int64_t)(0xffffu - (best & 0xffffu)) : 0;
     uint32_t max_bits = 0;
@@ -391,7 +386,7 @@ extern "C" int up_sm100_row_max_argmax_bf16(const uint16_t* x, int64_t rows, int
   const int grid = (int)(rows < (1 << 30) ? rows : (1 << 30));
   const bool vec = cols > 0 && aligned(x, 16) && (cols % 8 == 0) && (row_stride % 8 == 0) && cols <= 65536;
   if (vec)
-    row_max_argmax_vec_kernel<16><<<grid, kRowThreads, 0, s>>>(x, rows, cols, row_stride, max_out, argmax_i32,
+    row_max_argmax_vec_kernel<4><<<grid, kRowThreads, 0, s>>>(x, rows, cols, row_stride, max_out, argmax_i32,
                                                               argmax_i64);
   else
     row_max_argmax_any_kernel<<<grid, kRowThreads, 0, s>>>(x, rows, cols, row_stride, max_out, argmax_i32,

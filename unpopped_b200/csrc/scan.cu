@@ -7,32 +7,39 @@
 // INT32_MAX); Sum wraps at 32 bits; a reverse scan walks from the row's end. Integer combines are exact
 // and associative, so the tile decomposition below produces the serial walk's bytes.
 //
-// Decomposition: a tile is 4096 consecutive elements of one row (the row's last tile may be short).
-// CTAs take tiles in ticket order (an atomic counter), so every tile's predecessors belong to CTAs that
-// are already running or done — the look-back cannot wait on a CTA that has not started.
-// Within a tile, warp w owns elements [w*512, w*512+512); lane l holds the int4 groups i*32 + l
-// (i = 0..3), which makes every load and store one contiguous 512-byte warp access.
+// Decomposition: a tile is 16384 consecutive elements (64 KiB) of one row (the row's last tile may be
+// short); CTA i scans tile i. One thread moves the tile into shared memory with bulk copies
+// (cp.async.bulk, no multicast) and back out with bulk stores, so the loads in flight cost no registers and
+// three tiles per SM stream concurrently. In shared memory, warp w owns 2048 elements; lane l handles the
+// 16-byte chunks i*32 + l (i = 0..15), which keeps every shared-memory access conflict-free. Pass 1 folds
+// the tile; the tile's aggregate goes out as a look-back flag; pass 2 rescans from shared memory with the
+// prefix found by the look-back and writes the result in place.
 //
-// Look-back flags: one 64-bit word per tile = epoch(30) | status(2) | value(32), written and read with
-// relaxed gpu-scope atomics (the value travels inside the flag word, so no separate fence is needed).
-// Status: 1 = aggregate of this tile, 2 = inclusive prefix through this tile, 3 = aborted. The epoch is
-// bumped by the last CTA of every launch, which also resets the ticket counters, so the workspace needs
-// zero-filling only once. Every wait is bounded by a globaltimer deadline; a wait that runs out sets the
-// workspace error word and publishes "aborted", which its successors propagate at once.
+// Look-back: one 64-bit flag per tile = epoch(30) | status(2) | value(32), written and read with relaxed
+// gpu-scope atomics (the value travels inside the flag word). Status: 1 = aggregate of this tile,
+// 2 = inclusive prefix through this tile, 3 = aborted. Warp 0 examines 32 predecessors per step. CTAs are
+// dispatched in index order, so a tile only ever waits on tiles whose CTAs have started. The epoch is a
+// per-launch number chosen on the host, so flags of earlier launches are never mistaken for this one's and
+// the workspace needs zero-filling only once. Every wait is bounded by a globaltimer deadline; a wait that
+// runs out sets the workspace error word and publishes "aborted", which successors propagate at once.
 #include "common.cuh"
+#include "tc.cuh"
+
+#include <atomic>
+#include <mutex>
 
 namespace up {
 
 constexpr int kScanThreads = 256;
-constexpr int kScanVecs = 4;                                    // int4 per thread
-constexpr int kScanTile = kScanThreads * kScanVecs * 4;         // 4096 elements
-constexpr int kWarpSeg = kScanVecs * 4 * 32;                    // 512 elements per warp
+constexpr int kLaneChunks = 16;                                  // 16-byte chunks per lane
+constexpr int kScanTile = kScanThreads * kLaneChunks * 4;        // 16384 elements
+constexpr int kWarpChunks = 32 * kLaneChunks;                    // 512 chunks = 2048 elements per warp
+constexpr int kTileBytes = kScanTile * 4;                        // 64 KiB
+constexpr size_t kScanSmem = kTileBytes + 64;                    // + the tile's mbarrier
 
 struct ScanHeader {
-  uint32_t ticket;
-  uint32_t done;
-  uint32_t epoch;
-  uint32_t error;
+  uint32_t reserved0, reserved1, reserved2;
+  uint32_t error;  // byte 12: set when a bounded wait ran out
   uint32_t pad[12];
 };
 static_assert(sizeof(ScanHeader) == 64, "header is one 64-byte line");
@@ -75,74 +82,101 @@ __device__ __forceinline__ int32_t warp_incl_scan(int32_t v, int lane) {
   return v;
 }
 
+// The tile in shared memory, read and written by logical chunk (elements 4g .. 4g+3 in scan order).
+// `rev`: the tile is stored back to front (a reverse scan that was bulk-loaded); `cnt`: valid elements.
+template <int OP>
+struct TileView {
+  int32_t* buf;
+  int cnt;
+  bool rev;
+  __device__ __forceinline__ void load(int g, int32_t (&v)[4]) const {
+    const int e0 = 4 * g;
+    if (e0 + 4 <= cnt) {
+      const int4 c = rev ? reinterpret_cast<const int4*>(buf)[(cnt >> 2) - 1 - g] : reinterpret_cast<const int4*>(buf)[g];
+      if (rev) { v[0] = c.w; v[1] = c.z; v[2] = c.y; v[3] = c.x; }
+      else { v[0] = c.x; v[1] = c.y; v[2] = c.z; v[3] = c.w; }
+    } else {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) v[c] = (e0 + c < cnt) ? buf[e0 + c] : ident<OP>();  // only unreversed here
+    }
+  }
+  __device__ __forceinline__ void store(int g, const int32_t (&o)[4]) const {
+    const int e0 = 4 * g;
+    if (e0 + 4 <= cnt) {
+      if (rev) reinterpret_cast<int4*>(buf)[(cnt >> 2) - 1 - g] = make_int4(o[3], o[2], o[1], o[0]);
+      else reinterpret_cast<int4*>(buf)[g] = make_int4(o[0], o[1], o[2], o[3]);
+    } else {
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (e0 + c < cnt) buf[e0 + c] = o[c];
+    }
+  }
+};
+
 template <int OP>
 __global__ void __launch_bounds__(kScanThreads) scan_i32_kernel(const int32_t* __restrict__ x,
                                                                 int32_t* __restrict__ y, int64_t k,
-                                                                int64_t tiles_per_row, int64_t num_tiles,
-                                                                int exclusive, int reverse,
+                                                                int64_t tiles_per_row, int exclusive, int reverse,
                                                                 const int32_t* carry_in, ScanHeader* hdr,
-                                                                uint64_t* flags, uint64_t wait_ns,
-                                                                int withhold, int vec_ok) {
-  __shared__ int64_t s_tile;
-  __shared__ uint32_t s_epoch;
+                                                                uint64_t* flags, uint32_t epoch, uint64_t wait_ns,
+                                                                int withhold, int bulk) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  int32_t* buf = reinterpret_cast<int32_t*>(smem);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kTileBytes);
   __shared__ int32_t s_warp_tot[kScanThreads / 32];
   __shared__ int32_t s_prefix;
   __shared__ int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    s_tile = (int64_t)atomicAdd(&hdr->ticket, 1u);
-    s_epoch = ld_relaxed_u32(&hdr->epoch);
-    s_abort = 0;
-  }
-  __syncthreads();
-  const int64_t t = s_tile;
-  const uint32_t epoch = s_epoch;
+  const int64_t t = blockIdx.x;
   const int64_t row = t / tiles_per_row;
   const int64_t q = t - row * tiles_per_row;
   const int64_t lo = q * kScanTile;
-  const bool full = (lo + kScanTile <= k) && vec_ok;
+  const int cnt = (int)((k - lo) < kScanTile ? (k - lo) : kScanTile);
   const int32_t* xr = x + row * k;
   int32_t* yr = y + row * k;
+  const int64_t pstart = reverse ? (k - lo - cnt) : lo;  // first physical element of the tile
   const int32_t id = ident<OP>();
 
-  // ---- load (logical order; reversed rows are read back to front) ----
-  int32_t v[kScanVecs][4];
-#pragma unroll
-  for (int i = 0; i < kScanVecs; ++i) {
-    const int64_t e0 = lo + warp * kWarpSeg + (i * 32 + lane) * 4;
-    if (full) {
-      if (!reverse) {
-        const uint4 u = ld_nc_na_v4(xr + e0);
-        v[i][0] = (int32_t)u.x; v[i][1] = (int32_t)u.y; v[i][2] = (int32_t)u.z; v[i][3] = (int32_t)u.w;
-      } else {
-        const uint4 u = ld_nc_na_v4(xr + (k - e0 - 4));
-        v[i][0] = (int32_t)u.w; v[i][1] = (int32_t)u.z; v[i][2] = (int32_t)u.y; v[i][3] = (int32_t)u.x;
-      }
-    } else {
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int64_t e = e0 + c;
-        v[i][c] = e < k ? __ldg(xr + (reverse ? k - 1 - e : e)) : id;
+  // ---- bring the tile into shared memory ----
+  if (threadIdx.x == 0) s_abort = 0;
+  if (bulk) {
+    if (threadIdx.x == 0) {
+      tc::mbar_init(bar, 1);
+      tc::mbar_fence_init();
+      const uint32_t bytes = (uint32_t)cnt * 4u;
+      tc::mbar_arrive_expect_tx(bar, bytes);
+      const char* src = reinterpret_cast<const char*>(xr + pstart);
+      for (uint32_t off = 0; off < bytes; off += 16384u)
+        tc::bulk_load(smem + off, src + off, (bytes - off) < 16384u ? (bytes - off) : 16384u, bar);
+    }
+    __syncthreads();
+    const bool ok = tc::mbar_wait(bar, 0, wait_ns, nullptr);
+    if (__syncthreads_or(!ok)) {
+      // the copy did not land in time: report, and let it land before this CTA's shared memory is released
+      if (threadIdx.x == 0) {
+        atomicOr(&hdr->error, 1u);
+        s_abort = 1;
+        tc::mbar_wait(bar, 0, wait_ns, nullptr);
       }
     }
+  } else {
+    // any alignment: element loads, stored in scan order (a reversed row is read back to front)
+    for (int e = threadIdx.x; e < cnt; e += kScanThreads) buf[e] = __ldg(xr + (reverse ? (k - 1 - (lo + e)) : (lo + e)));
   }
+  __syncthreads();
+  const TileView<OP> tile{buf, cnt, bulk && reverse};
 
-  // ---- thread-local scans of each 4-group, warp scans of the group totals ----
-  int32_t gex[kScanVecs];  // exclusive prefix of group (i, lane) within the warp segment
-  int32_t carry = id;      // warp-uniform running total over i
-#pragma unroll
-  for (int i = 0; i < kScanVecs; ++i) {
-    v[i][1] = comb<OP>(v[i][0], v[i][1]);
-    v[i][2] = comb<OP>(v[i][1], v[i][2]);
-    v[i][3] = comb<OP>(v[i][2], v[i][3]);
-    const int32_t inc = warp_incl_scan<OP>(v[i][3], lane);
-    int32_t exc = __shfl_up_sync(0xffffffffu, inc, 1);
-    if (lane == 0) exc = id;
-    gex[i] = comb<OP>(carry, exc);
-    carry = comb<OP>(carry, __shfl_sync(0xffffffffu, inc, 31));
+  // ---- pass 1: fold the tile ----
+  int32_t acc = id;
+#pragma unroll 4
+  for (int i = 0; i < kLaneChunks; ++i) {
+    int32_t v[4];
+    tile.load(warp * kWarpChunks + i * 32 + lane, v);
+    acc = comb<OP>(acc, comb<OP>(comb<OP>(v[0], v[1]), comb<OP>(v[2], v[3])));
   }
-  if (lane == 0) s_warp_tot[warp] = carry;
+  acc = warp_reduce<OP>(acc);
+  if (lane == 0) s_warp_tot[warp] = acc;
   __syncthreads();
   int32_t wpre = id, agg = id;
 #pragma unroll
@@ -155,11 +189,12 @@ __global__ void __launch_bounds__(kScanThreads) scan_i32_kernel(const int32_t* _
   if (warp == 0) {
     const int32_t cin = carry_in ? *carry_in : id;
     int32_t excl = id;
-    bool abort = false;
+    bool abort = s_abort != 0;
     if (q == 0) {
       excl = cin;
-      if (lane == 0 && !(withhold && t == 0)) st_relaxed_u64(flags + t, make_flag(epoch, kFlagIncl, comb<OP>(cin, agg)));
-    } else {
+      if (lane == 0 && !(withhold && t == 0))
+        st_relaxed_u64(flags + t, make_flag(epoch, abort ? kFlagErr : kFlagIncl, comb<OP>(cin, agg)));
+    } else if (!abort) {
       if (lane == 0) st_relaxed_u64(flags + t, make_flag(epoch, kFlagAgg, agg));
       const int64_t row_first = row * tiles_per_row;
       int64_t pred = t - 1;
@@ -180,7 +215,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_i32_kernel(const int32_t* _
             abort = true;
             break;
           }
-          __nanosleep(64);
+          __nanosleep(32);
         }
         if (abort) break;
         if (__any_sync(0xffffffffu, mine && st == kFlagErr)) {
@@ -195,13 +230,11 @@ __global__ void __launch_bounds__(kScanThreads) scan_i32_kernel(const int32_t* _
         pred -= 32;
       }
       if (lane == 0) {
-        if (abort) {
-          atomicOr(&hdr->error, 1u);
-          st_relaxed_u64(flags + t, make_flag(epoch, kFlagErr, 0));
-        } else {
-          st_relaxed_u64(flags + t, make_flag(epoch, kFlagIncl, comb<OP>(excl, agg)));
-        }
+        if (abort) atomicOr(&hdr->error, 1u);
+        st_relaxed_u64(flags + t, abort ? make_flag(epoch, kFlagErr, 0) : make_flag(epoch, kFlagIncl, comb<OP>(excl, agg)));
       }
+    } else if (lane == 0) {
+      st_relaxed_u64(flags + t, make_flag(epoch, kFlagErr, 0));
     }
     if (lane == 0) {
       s_prefix = excl;
@@ -209,49 +242,56 @@ __global__ void __launch_bounds__(kScanThreads) scan_i32_kernel(const int32_t* _
     }
   }
   __syncthreads();
+  if (s_abort) return;  // uniform: nothing written, the error word is set
 
-  // ---- store ----
-  if (!s_abort) {
-    const int32_t base = comb<OP>(s_prefix, wpre);
+  // ---- pass 2: rescan with the tile's prefix, in place ----
+  const int32_t base = comb<OP>(s_prefix, wpre);
+  int32_t carry = id;
+#pragma unroll 2
+  for (int i = 0; i < kLaneChunks; ++i) {
+    const int g = warp * kWarpChunks + i * 32 + lane;
+    int32_t v[4];
+    tile.load(g, v);
+    v[1] = comb<OP>(v[0], v[1]);
+    v[2] = comb<OP>(v[1], v[2]);
+    v[3] = comb<OP>(v[2], v[3]);
+    const int32_t inc = warp_incl_scan<OP>(v[3], lane);
+    int32_t exc = __shfl_up_sync(0xffffffffu, inc, 1);
+    if (lane == 0) exc = id;
+    const int32_t pre = comb<OP>(comb<OP>(base, carry), exc);
+    int32_t o[4];
+    if (exclusive) {
+      o[0] = pre;
+      o[1] = comb<OP>(pre, v[0]);
+      o[2] = comb<OP>(pre, v[1]);
+      o[3] = comb<OP>(pre, v[2]);
+    } else {
 #pragma unroll
-    for (int i = 0; i < kScanVecs; ++i) {
-      const int32_t pre = comb<OP>(base, gex[i]);
-      int32_t o[4];
-      if (exclusive) {
-        o[0] = pre;
-        o[1] = comb<OP>(pre, v[i][0]);
-        o[2] = comb<OP>(pre, v[i][1]);
-        o[3] = comb<OP>(pre, v[i][2]);
-      } else {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) o[c] = comb<OP>(pre, v[i][c]);
-      }
-      const int64_t e0 = lo + warp * kWarpSeg + (i * 32 + lane) * 4;
-      if (full) {
-        if (!reverse) st_cs_v4(yr + e0, make_uint4((uint32_t)o[0], (uint32_t)o[1], (uint32_t)o[2], (uint32_t)o[3]));
-        else st_cs_v4(yr + (k - e0 - 4), make_uint4((uint32_t)o[3], (uint32_t)o[2], (uint32_t)o[1], (uint32_t)o[0]));
-      } else {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int64_t e = e0 + c;
-          if (e < k) yr[reverse ? k - 1 - e : e] = o[c];
-        }
-      }
+      for (int c = 0; c < 4; ++c) o[c] = comb<OP>(pre, v[c]);
     }
+    tile.store(g, o);
+    carry = comb<OP>(carry, __shfl_sync(0xffffffffu, inc, 31));
   }
 
-  // ---- the last CTA of the launch re-arms the workspace for the next one ----
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const uint32_t d = atomicAdd(&hdr->done, 1u);
-    if ((int64_t)d == num_tiles - 1) {
-      atomicExch(&hdr->ticket, 0u);
-      atomicExch(&hdr->done, 0u);
-      __threadfence();
-      atomicAdd(&hdr->epoch, 1u);
+  // ---- write the tile back ----
+  if (bulk) {
+    tc::fence_proxy_async_smem();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const uint32_t bytes = (uint32_t)cnt * 4u;
+      char* dst = reinterpret_cast<char*>(yr + pstart);
+      for (uint32_t off = 0; off < bytes; off += 16384u)
+        tc::bulk_store(dst + off, smem + off, (bytes - off) < 16384u ? (bytes - off) : 16384u);
+      tc::bulk_commit();
+      tc::bulk_wait_read();
     }
+  } else {
+    __syncthreads();
+    for (int e = threadIdx.x; e < cnt; e += kScanThreads) yr[reverse ? (k - 1 - (lo + e)) : (lo + e)] = buf[e];
   }
 }
+
+static std::atomic<uint32_t> g_epoch{0};
 
 }  // namespace up
 
@@ -261,6 +301,28 @@ extern "C" size_t up_sm100_scan_workspace_bytes(int64_t rows, int64_t k) {
   if (rows <= 0 || k <= 0) return sizeof(ScanHeader);
   const int64_t tiles = rows * ((k + kScanTile - 1) / kScanTile);
   return sizeof(ScanHeader) + (size_t)tiles * sizeof(uint64_t);
+}
+
+template <int OP>
+static cudaError_t launch_scan(unsigned grid, cudaStream_t s, const int32_t* x, int32_t* y, int64_t k, int64_t tpr,
+                               int exclusive, int reverse, const int32_t* carry_in, ScanHeader* hdr, uint64_t* flags,
+                               uint32_t epoch, uint64_t wns, int withhold, int bulk) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static std::mutex mu;
+  static bool attr_set[64] = {false};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+      e = cudaFuncSetAttribute(scan_i32_kernel<OP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kScanSmem);
+      if (e != cudaSuccess) return e;
+      if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+  }
+  scan_i32_kernel<OP><<<grid, kScanThreads, kScanSmem, s>>>(x, y, k, tpr, exclusive, reverse, carry_in, hdr, flags,
+                                                            epoch, wns, withhold, bulk);
+  return cudaGetLastError();
 }
 
 extern "C" int up_sm100_scan_i32(const int32_t* x, int32_t* y, int64_t rows, int64_t k, int op, int exclusive,
@@ -277,21 +339,24 @@ extern "C" int up_sm100_scan_i32(const int32_t* x, int32_t* y, int64_t rows, int
   if (workspace_bytes < up_sm100_scan_workspace_bytes(rows, k)) return UP_ERR_INVALID;
   auto* hdr = static_cast<ScanHeader*>(workspace);
   auto* flags = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + sizeof(ScanHeader));
-  const int vec_ok = aligned(x, 16) && aligned(y, 16) && (k % 4 == 0);
+  // bulk copies need 16-byte aligned rows of whole 16-byte chunks
+  const int bulk = aligned(x, 16) && aligned(y, 16) && (k % 4 == 0);
   const int withhold = take_withhold_flag();
+  const uint32_t epoch = ++g_epoch;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const uint64_t wns = wait_limit_ns();
+  cudaError_t e;
   if (op == UP_OP_SUM)
-    scan_i32_kernel<UP_OP_SUM><<<(unsigned)tiles, kScanThreads, 0, s>>>(x, y, k, tpr, tiles, exclusive, reverse,
-                                                                       carry_in, hdr, flags, wns, withhold, vec_ok);
+    e = launch_scan<UP_OP_SUM>((unsigned)tiles, s, x, y, k, tpr, exclusive, reverse, carry_in, hdr, flags, epoch, wns,
+                               withhold, bulk);
   else if (op == UP_OP_MAX)
-    scan_i32_kernel<UP_OP_MAX><<<(unsigned)tiles, kScanThreads, 0, s>>>(x, y, k, tpr, tiles, exclusive, reverse,
-                                                                       carry_in, hdr, flags, wns, withhold, vec_ok);
+    e = launch_scan<UP_OP_MAX>((unsigned)tiles, s, x, y, k, tpr, exclusive, reverse, carry_in, hdr, flags, epoch, wns,
+                               withhold, bulk);
   else
-    scan_i32_kernel<UP_OP_MIN><<<(unsigned)tiles, kScanThreads, 0, s>>>(x, y, k, tpr, tiles, exclusive, reverse,
-                                                                       carry_in, hdr, flags, wns, withhold, vec_ok);
+    e = launch_scan<UP_OP_MIN>((unsigned)tiles, s, x, y, k, tpr, exclusive, reverse, carry_in, hdr, flags, epoch, wns,
+                               withhold, bulk);
   note_launch();
-  return check_launch();
+  return cuda_status(e);
 }
 
 extern "C" int up_sm100_workspace_status(void* workspace, void* stream) {

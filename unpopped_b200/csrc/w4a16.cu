@@ -298,7 +298,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int m = 0; m < kMmaN; ++m) {
                   float v = 0.f;
                   for (int64_t sg = 0; sg < nseg; ++sg) {
-                    const float pv = __ldcg(partials + ((t * S_max + sg) * kMmaN + m) * kTileN + row);
+                    float* pp = partials + ((t * S_max + sg) * kMmaN + m) * kTileN + row;
+                    const float pv = __ldcg(pp);
+                    __stcg(pp, 0.f);  // leave the workspace all-zero: any later shape may reuse these bytes
                     v = (sg == 0) ? pv : v + pv;
                   }
                   if (m < M && nn < N) out[(int64_t)m * N + nn] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
@@ -362,6 +364,60 @@ static Plan make_plan(int64_t n, int64_t k) {
   return p;
 }
 
+
+// The two tensor maps of a call. Encoding is a host-side driver call of a few microseconds; the last few
+// (pointer, shape) combinations are cached so a steady stream of calls on the same buffers skips it.
+static int tensor_maps(const uint8_t* w, const uint16_t* x, int64_t m, int64_t n, int64_t k, CUtensorMap* tmW,
+                       CUtensorMap* tmX) {
+  struct Entry {
+    const void* w;
+    const void* x;
+    int64_t m, n, k;
+    CUtensorMap tw, tx;
+  };
+  static std::mutex mu;
+  static Entry cache[8];
+  static int next = 0, used = 0;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    for (int i = 0; i < used; ++i) {
+      const Entry& e = cache[i];
+      if (e.w == w && e.x == x && e.m == m && e.n == n && e.k == k) {
+        *tmW = e.tw;
+        *tmX = e.tx;
+        return UP_OK;
+      }
+    }
+  }
+  auto enc = encode_fn();
+  if (!enc) return UP_ERR_CUDA;
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)(k / 2), (cuuint64_t)n};
+    const cuuint64_t strides[1] = {(cuuint64_t)(k / 2)};
+    const cuuint32_t box[2] = {kKB / 2, kTileN};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return UP_ERR_CUDA;
+  }
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
+    const cuuint64_t strides[1] = {(cuuint64_t)(k * 2)};
+    const cuuint32_t box[2] = {64, kMmaN};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(tmX, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(x), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return UP_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  cache[next] = Entry{w, x, m, n, k, *tmW, *tmX};
+  next = (next + 1) % 8;
+  if (used < 8) ++used;
+  return UP_OK;
+}
+
 }  // namespace w4
 }  // namespace up
 
@@ -387,34 +443,24 @@ extern "C" int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, cons
   if (!aligned(w, 16) || !aligned(x, 16) || !aligned(workspace, 256)) return UP_ERR_INVALID;
   const Plan p = make_plan(n, k);
   if (workspace_bytes < p.bytes) return UP_ERR_INVALID;
-  auto enc = encode_fn();
-  if (!enc) return UP_ERR_CUDA;
-
   CUtensorMap tmW, tmX;
   {
-    const cuuint64_t dims[2] = {(cuuint64_t)(k / 2), (cuuint64_t)n};
-    const cuuint64_t strides[1] = {(cuuint64_t)(k / 2)};
-    const cuuint32_t box[2] = {kKB / 2, kTileN};
-    const cuuint32_t estr[2] = {1, 1};
-    if (enc(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return UP_ERR_CUDA;
+    const int st = tensor_maps(w, x, m, n, k, &tmW, &tmX);
+    if (st != UP_OK) return st;
   }
   {
-    const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
-    const cuuint64_t strides[1] = {(cuuint64_t)(k * 2)};
-    const cuuint32_t box[2] = {64, kMmaN};
-    const cuuint32_t estr[2] = {1, 1};
-    if (enc(&tmX, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(x), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return UP_ERR_CUDA;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_status(e);
+    static std::mutex mu;
+    static bool attr_set[64] = {false};
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+      e = cudaFuncSetAttribute(w4a16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+      if (e != cudaSuccess) return cuda_status(e);
+      if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
   }
-  // Per call: the attribute belongs to the current device's context.
-  const cudaError_t attr_err =
-      cudaFuncSetAttribute(w4a16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
-  if (attr_err != cudaSuccess) return cuda_status(attr_err);
   auto* base = static_cast<char*>(workspace);
   auto* hdr = reinterpret_cast<WsHeader*>(base);
   auto* counters = reinterpret_cast<uint32_t*>(base + p.counters_off);
