@@ -132,15 +132,11 @@ class Ctx:
         else:
             torch.cuda.set_device(self.local)
         self.dev = torch.device("cuda", self.local)
-        self.flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=self.dev)
         self.sleep_cycles = 1_000_000  # ~0.5 ms at the B200's 1.9 GHz SM clock
 
     def barrier(self):
         if self.world > 1:
             self.dist.barrier(device_ids=[self.local])
-
-    def flush_l2(self):
-        self.flush_buf.zero_()  # 256 MiB written: more than the 126 MB L2
 
     def max_over_ranks(self, v: float) -> float:
         if self.world == 1:
@@ -149,39 +145,43 @@ class Ctx:
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
-    def timed(self, step, K, W, inner=None):
-        """W warm-up steps, then K steps each between its own events (L2 flushed before each, outside the
-        events). `inner` (optional) is a list the step appends (start, end) event pairs of its dominant kernel
-        to. Returns (mean ms per step over ranks' max, mean inner-kernel ms, our kernel launches in the region)."""
+    def timed(self, step, K, W, inner=False):
+        """W warm-up steps, then EXACTLY K steps between one pair of events on the launching stream, with a
+        barrier + synchronize on both sides. `step(i, kin)` runs step i; callers rotate through enough input
+        copies that every step's inputs are colder than the 126 MB L2 (no flush inside the timed region). A GPU
+        sleep before the start event lets the host enqueue all K steps ahead of the device, so the events time
+        device work only. With `inner`, the step appends (start, end) events of its dominant kernel to `kin`.
+        Returns (ms per step, max over ranks; mean inner-kernel ms; our kernel launches in the timed region)."""
         from unpopped_b200 import ops
 
         torch = self.torch
-        for _ in range(W):
-            self.flush_l2()
-            step(None)
+        for i in range(W):
+            step(i, None)
         torch.cuda.synchronize()
         self.barrier()
         torch.cuda.synchronize()
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
         kin = [] if inner else None
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         l0 = ops.launch_count()
+        torch.cuda._sleep(self.sleep_cycles + K * 200_000)  # ~0.1 ms per step of head start for the host
+        a.record()
         for i in range(K):
-            self.flush_l2()
-            # keep the GPU busy while the host enqueues the step, so the events time device work only
-            torch.cuda._sleep(self.sleep_cycles)
-            ev[i][0].record()
-            step(kin)
-            ev[i][1].record()
+            step(i, kin)
+        b.record()
         torch.cuda.synchronize()
         launches = ops.launch_count() - l0
         self.barrier()
         torch.cuda.synchronize()
-        tot = sum(a.elapsed_time(b) for a, b in ev)
-        ms = self.max_over_ranks(tot) / K
+        ms = self.max_over_ranks(a.elapsed_time(b)) / K
         kms = None
         if kin:
-            kms = self.max_over_ranks(sum(a.elapsed_time(b) for a, b in kin)) / len(kin)
+            kms = self.max_over_ranks(sum(x.elapsed_time(y) for x, y in kin)) / len(kin)
         return ms, kms, launches
+
+
+def copies_for(nbytes: int, l2_bytes: int = 126 << 20) -> int:
+    """Input copies to rotate through so that each step's inputs were last touched >= 2 x L2 bytes ago."""
+    return max(1, -(-(2 * l2_bytes) // max(1, nbytes)) + 1) if nbytes < 4 * l2_bytes else 1
 
 
 def make_scan_step(ctx, x, y, ws_kind="scan"):
@@ -190,22 +190,15 @@ def make_scan_step(ctx, x, y, ws_kind="scan"):
 
     torch = ctx.torch
     if ctx.world == 1:
-        def step(kin):
-            if kin is not None:
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record()
-                ops.scan(x, "sum", out=y)
-                b.record()
-                kin.append((a, b))
-            else:
-                ops.scan(x, "sum", out=y)
+        def step(i, kin):  # one kernel: the step time is the kernel time
+            ops.scan(x, "sum", out=y)
         return step
 
     total = torch.empty(1, dtype=torch.int32, device=ctx.dev)
     totals = torch.empty(ctx.world, dtype=torch.int32, device=ctx.dev)
     carry = torch.empty(1, dtype=torch.int32, device=ctx.dev)
 
-    def step(kin):
+    def step(i, kin):
         ops.reduce_i32(x, "sum", out=total)
         ctx.dist.all_gather_into_tensor(totals, total)
         # the carry is the wrapped sum of the lower ranks' totals
@@ -226,34 +219,35 @@ def make_scan_step(ctx, x, y, ws_kind="scan"):
 
 def bench_lifts(ctx, K, W, hbm, bf16):
     """Every other configuration, each in its own timed region (same rules as the headline)."""
-    from unpopped_b200 import ops, workloads as wl
+    from unpopped_b200 import _lib, ops, workloads as wl
 
     torch = ctx.torch
     res = {}
 
-    def record(name, nbytes, ms, kernel, extra=None):
+    def record(name, nbytes, ms, kernel, copies, extra=None):
         gbs = ctx.world * nbytes / (ms * 1e-3) / 1e9
         r = {"value": round(gbs, 1), "unit": "GB/s", "ms_per_step": round(ms, 4), "bytes_per_gpu": nbytes,
-             "frac_of_hbm": round(gbs / (ctx.world * hbm), 4), "kernel": kernel}
+             "frac_of_hbm": round(gbs / (ctx.world * hbm), 4), "kernel": kernel, "input_copies_rotated": copies}
         if extra:
             r.update(extra)
         res[name] = r
 
     # config 1: row sum f32 8192 x 8192 (f32 accumulation, and the documented f64 order)
-    x = wl.rowsum_input(device=ctx.dev)
-    out = torch.empty(x.shape[0], dtype=torch.float32, device=ctx.dev)
-    ms, _, _ = ctx.timed(lambda kin: ops.row_sum(x, "f32", out=out), K, W)
-    record("rowsum_f32_8192x8192", wl.rowsum_bytes(), ms, "row_sum_f32_kernel")
-    ms, _, _ = ctx.timed(lambda kin: ops.row_sum(x, "auto", 1024, out=out), K, W)
-    record("rowsum_f32_auto_f64order_B1024", wl.rowsum_bytes(), ms, "row_sum_auto_kernel")
-    del x, out
+    R = copies_for(wl.rowsum_bytes())
+    xs = [wl.rowsum_input(device=ctx.dev, seed=wl.SEED + 10 * c) for c in range(R)]
+    out = torch.empty(xs[0].shape[0], dtype=torch.float32, device=ctx.dev)
+    ms, _, _ = ctx.timed(lambda i, kin: ops.row_sum(xs[i % R], "f32", out=out), K, W)
+    record("rowsum_f32_8192x8192", wl.rowsum_bytes(), ms, "row_sum_f32_kernel", R)
+    ms, _, _ = ctx.timed(lambda i, kin: ops.row_sum(xs[i % R], "auto", 1024, out=out), K, W)
+    record("rowsum_f32_auto_f64order_B1024", wl.rowsum_bytes(), ms, "row_sum_auto_kernel", R)
+    del xs, out
 
     # config 2 variants: exclusive add and inclusive max (the headline is the inclusive add)
     x = wl.scan_input(device=ctx.dev)
     y = torch.empty_like(x)
     for name, op, ex in (("scan_excl_add_i32_2p28", "sum", True), ("scan_incl_max_i32_2p28", "max", False)):
-        ms, _, _ = ctx.timed(lambda kin, op=op, ex=ex: ops.scan(x, op, ex, out=y), K, W)
-        record(name, wl.scan_bytes(), ms, "scan_i32_kernel")
+        ms, _, _ = ctx.timed(lambda i, kin, op=op, ex=ex: ops.scan(x, op, ex, out=y), K, W)
+        record(name, wl.scan_bytes(), ms, "scan_i32_kernel", 1)
     ops.check_workspace("scan", ctx.dev)
     del x, y
 
@@ -261,40 +255,43 @@ def bench_lifts(ctx, K, W, hbm, bf16):
     x = wl.argmax_input(device=ctx.dev)
     mx = torch.empty(x.shape[0], dtype=torch.float32, device=ctx.dev)
     am = torch.empty(x.shape[0], dtype=torch.int32, device=ctx.dev)
-    from unpopped_b200 import _lib
     L = _lib.load()
 
-    def am_step(kin):
+    def am_step(i, kin):
         _lib.check(L.up_sm100_row_max_argmax_bf16(x.data_ptr(), x.shape[0], x.shape[1], x.shape[1], mx.data_ptr(),
                                                   am.data_ptr(), None, torch.cuda.current_stream().cuda_stream),
                    "argmax")
     ms, _, _ = ctx.timed(am_step, K, W)
-    record("max_argmax_bf16_32768x32000", wl.argmax_bytes(), ms, "row_max_argmax_vec_kernel")
+    record("max_argmax_bf16_32768x32000", wl.argmax_bytes(), ms, "row_max_argmax_vec_kernel", 1)
     del x, mx, am
 
     # config 3: Zipf gather, table 2^20 x 256 bf16, 2^24 ids
     table, ids = wl.gather_inputs(device=ctx.dev)
     comp, logical, uniq = wl.gather_bytes(ids)
     g_out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=ctx.dev)
-    ms, _, _ = ctx.timed(lambda kin: ops.gather_rows(table, ids, "zero_fill", out=g_out), K, W)
-    record("gather_rows_bf16_zipf1.1", comp, ms, "gather_rows_vec_kernel",
+    ms, _, _ = ctx.timed(lambda i, kin: ops.gather_rows(table, ids, "zero_fill", out=g_out), K, W)
+    record("gather_rows_bf16_zipf1.1", comp, ms, "gather_rows_vec_kernel", 1,
            {"bytes_basis": "compulsory (ids + output + each distinct row once)", "unique_rows": uniq,
             "logical_GBps": round(ctx.world * logical / (ms * 1e-3) / 1e9, 1)})
     del table, ids, g_out
 
     # config 5: int4 group-128 dequant (standalone) and the W4A16 GEMM 16 x 28672 x 8192
-    d = wl.w4a16_inputs(device=ctx.dev)
-    dq = torch.empty(d.n, d.k, dtype=torch.bfloat16, device=ctx.dev)
-    ms, _, _ = ctx.timed(lambda kin: ops.dequant_i4(d.w_packed, d.scale, d.group, out=dq), K, W)
-    record("dequant_i4_g128_bf16_28672x8192", wl.dequant_bytes(), ms, "dequant_i4_vec_kernel")
+    R = copies_for(wl.w4a16_bytes())
+    ds = [wl.w4a16_inputs(device=ctx.dev, seed=wl.SEED + 5 + 10 * c) for c in range(R)]
+    Rd = min(R, 2)
+    dq = torch.empty(ds[0].n, ds[0].k, dtype=torch.bfloat16, device=ctx.dev)
+    ms, _, _ = ctx.timed(lambda i, kin: ops.dequant_i4(ds[i % Rd].w_packed, ds[i % Rd].scale, ds[0].group, out=dq),
+                         K, W)
+    record("dequant_i4_g128_bf16_28672x8192", wl.dequant_bytes(), ms, "dequant_i4_rows_kernel", Rd)
     del dq
-    o = torch.empty(d.m, d.n, dtype=torch.bfloat16, device=ctx.dev)
-    ms, _, _ = ctx.timed(lambda kin: ops.w4a16(d.w_packed, d.scale, d.x, d.group, out=o), K, W)
+    o = torch.empty(ds[0].m, ds[0].n, dtype=torch.bfloat16, device=ctx.dev)
+    ms, _, _ = ctx.timed(lambda i, kin: ops.w4a16(ds[i % R].w_packed, ds[i % R].scale, ds[i % R].x, ds[0].group,
+                                                  out=o), K, W)
     ops.check_workspace("w4a16", ctx.dev)
     tflops = ctx.world * wl.w4a16_flops() / (ms * 1e-3) / 1e12
-    record("w4a16_gemm_16x28672x8192_g128", wl.w4a16_bytes(), ms, "w4a16_kernel (tcgen05, TMEM A operand)",
+    record("w4a16_gemm_16x28672x8192_g128", wl.w4a16_bytes(), ms, "w4a16_kernel (tcgen05, TMEM A operand)", R,
            {"tflops": round(tflops, 1), "frac_of_bf16_peak": round(tflops / (ctx.world * bf16), 4)})
-    del d, o
+    del ds, o
     torch.cuda.empty_cache()
     return res
 
@@ -444,7 +441,9 @@ def main():
     x = wl.scan_input(device=ctx.dev, seed=wl.SEED + 2 + ctx.rank)
     y = torch.empty_like(x)
     step = make_scan_step(ctx, x, y)
-    ms, kms, launches = ctx.timed(step, K, W, inner=True)
+    ms, kms, launches = ctx.timed(step, K, W, inner=ctx.world > 1)
+    if kms is None:
+        kms = ms
     ops.check_workspace("scan", ctx.dev)
     nbytes = wl.scan_bytes()
     value = ctx.world * nbytes / (ms * 1e-3) / 1e9
@@ -454,9 +453,9 @@ def main():
     xh = x.cpu().pin_memory()
     yh = torch.empty_like(xh).pin_memory()
 
-    def e2e_step(kin):
+    def e2e_step(i, kin):
         x.copy_(xh, non_blocking=True)
-        step(None)
+        step(i, None)
         yh.copy_(y, non_blocking=True)
     e_ms, _, _ = ctx.timed(e2e_step, max(3, K // 4), 1)
     e2e = {"value": round(ctx.world * nbytes / (e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
@@ -476,7 +475,7 @@ def main():
         "config": {"workload": "configs[1]: inclusive add-scan over 2^28 int32 per GPU (1 GiB in, 1 GiB out), "
                                "single-pass decoupled look-back" + (
                                    "; shards combined by an NCCL all-gather of per-GPU totals" if ctx.world > 1 else ""),
-                   "lift": "scan_incl_add_i32", "elements_per_gpu": SCAN_N, "l2": "flushed between steps (256 MiB write)",
+                   "lift": "scan_incl_add_i32", "elements_per_gpu": SCAN_N, "l2": "input (1 GiB per GPU) larger than the 126 MB L2; no flush",
                    "parallelism": f"sharded x{ctx.world}"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": traffic, "peak_source": peak_src,

@@ -33,31 +33,32 @@ __device__ __forceinline__ uint4 dequant8(uint32_t q, float s) {
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// k % 8 == 0 and group % 8 == 0: a word of w never straddles a row or a group.
-__global__ void __launch_bounds__(256) dequant_i4_vec_kernel(const uint32_t* __restrict__ w,
-                                                             const __half* __restrict__ scale, int64_t n, int64_t k,
-                                                             int64_t group, uint4* __restrict__ out) {
-  const int64_t words = n * (k >> 3);
-  const int64_t wpr = k >> 3;
-  const int64_t gpr = k / group;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  for (; i + 3 * stride < words; i += 4 * stride) {
-    uint32_t q[4];
-    float s[4];
+// k % 8 == 0 and group % 8 == 0: a word of w never straddles a row or a group. CTAs take whole rows; a row's
+// words are split over the threads with 32-bit index arithmetic only.
+__global__ void __launch_bounds__(256) dequant_i4_rows_kernel(const uint32_t* __restrict__ w,
+                                                              const __half* __restrict__ scale, int64_t n, int wpr,
+                                                              int gpr, int wpg, uint4* __restrict__ out) {
+  for (int64_t r = blockIdx.x; r < n; r += gridDim.x) {
+    const uint32_t* wr = w + r * wpr;
+    const __half* sr = scale + r * gpr;
+    uint4* orow = out + r * wpr;
+    for (int i0 = threadIdx.x; i0 < wpr; i0 += 256 * 4) {
+      uint32_t q[4];
+      float sc[4];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int64_t wi = i + u * stride;
-      q[u] = __ldg(w + wi);
-      const int64_t r = wi / wpr, c = (wi - r * wpr) << 3;
-      s[u] = __half2float(scale[r * gpr + c / group]);
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * 256;
+        if (i < wpr) {
+          q[u] = __ldg(wr + i);
+          sc[u] = __half2float(sr[(unsigned)i / (unsigned)wpg]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * 256;
+        if (i < wpr) st_cs_v4(orow + i, dequant8(q[u], sc[u]));
+      }
     }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) st_cs_v4(out + i + u * stride, dequant8(q[u], s[u]));
-  }
-  for (; i < words; i += stride) {
-    const int64_t r = i / wpr, c = (i - r * wpr) << 3;
-    st_cs_v4(out + i, dequant8(__ldg(w + i), __half2float(scale[r * gpr + c / group])));
   }
 }
 
@@ -89,13 +90,12 @@ extern "C" int up_sm100_dequant_i4_bf16(const uint8_t* w, const uint16_t* scale,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int sms = sm_count();
   const auto* sc = reinterpret_cast<const __half*>(scale);
-  if (k % 8 == 0 && group % 8 == 0 && aligned(w, 4) && aligned(out, 16)) {
-    const int64_t words = n * (k / 8);
-    int64_t blocks = (words + 255) / 256;
+  if (k % 8 == 0 && group % 8 == 0 && aligned(w, 4) && aligned(out, 16) && k / 8 <= 0x7fffffff) {
+    int64_t blocks = n;
     const int64_t cap = (int64_t)sms * 8;
     if (blocks > cap) blocks = cap;
-    dequant_i4_vec_kernel<<<(int)blocks, 256, 0, s>>>(reinterpret_cast<const uint32_t*>(w), sc, n, k, group,
-                                                      reinterpret_cast<uint4*>(out));
+    dequant_i4_rows_kernel<<<(int)blocks, 256, 0, s>>>(reinterpret_cast<const uint32_t*>(w), sc, n, (int)(k / 8),
+                                                       (int)(k / group), (int)(group / 8), reinterpret_cast<uint4*>(out));
   } else {
     int64_t blocks = (n * k + 255) / 256;
     const int64_t cap = (int64_t)sms * 16;

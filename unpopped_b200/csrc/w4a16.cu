@@ -42,7 +42,8 @@ constexpr int kKB = 128;                       // k per unit
 constexpr int kStages = 10;                    // smem ring depth
 constexpr int kWBytes = kTileN * kKB / 2;      // 8 KiB of int4
 constexpr int kXBytes = kMmaN * kKB * 2;       // 4 KiB of bf16
-constexpr int kStageBytes = kWBytes + kXBytes; // 12 KiB
+constexpr int kSBytes = kTileN * 8 * 2;        // 2 KiB: an 8-wide column block of f16 scales per row
+constexpr int kStageBytes = kWBytes + kXBytes + kSBytes;  // 14 KiB (1024-aligned parts)
 constexpr int kAStages = 4;                    // TMEM A stages, 64 columns each
 constexpr int kDSlots = 4;                     // TMEM accumulator slots, 16 columns each
 constexpr int kTmemCols = 512;
@@ -83,9 +84,12 @@ __device__ __forceinline__ uint32_t nib2_to_bf16x2(uint32_t q, uint32_t q4, int 
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
+// kScaleTma: the unit's group scales arrive in the stage by TMA (needs K/group % 8 == 0, so a row of scales
+// is a whole number of 16-byte chunks); otherwise each thread reads its scale from global memory.
+template <bool kScaleTma>
 __global__ void __launch_bounds__(kThreads, 1)
     w4a16_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
-                 const __half* __restrict__ scale, uint16_t* __restrict__ out, int M, int64_t N, int64_t K,
+                 const __grid_constant__ CUtensorMap tmS, const __half* __restrict__ scale, uint16_t* __restrict__ out, int M, int64_t N, int64_t K,
                  int64_t group, int64_t U, int64_t G, int64_t S_max, WsHeader* hdr, uint32_t* counters,
                  float* partials, uint64_t wait_ns) {
   extern __shared__ uint8_t smem_raw[];
@@ -139,6 +143,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       tc::tma_prefetch_desc(&tmW);
       tc::tma_prefetch_desc(&tmX);
+      if (kScaleTma) tc::tma_prefetch_desc(&tmS);
       int64_t issued = 0;
       for (int64_t i = 0; i < n_units; ++i) {
         const int s = (int)(i % kStages);
@@ -150,10 +155,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t u = lo + i;
         const int32_t t = (int32_t)(u / G), kb = (int32_t)(u % G);
         uint8_t* st = smem + (size_t)s * kStageBytes;
-        tc::mbar_arrive_expect_tx(&full[s], kStageBytes);
+        tc::mbar_arrive_expect_tx(&full[s], kScaleTma ? kStageBytes : kWBytes + kXBytes);
         tc::tma_load_2d(st, &tmW, &full[s], kb * (kKB / 2), t * kTileN);
         tc::tma_load_2d(st + kWBytes, &tmX, &full[s], kb * kKB, 0);
         tc::tma_load_2d(st + kWBytes + 2048, &tmX, &full[s], kb * kKB + 64, 0);
+        if (kScaleTma)
+          tc::tma_load_2d(st + kWBytes + kXBytes, &tmS, &full[s], (int32_t)(((int64_t)kb * kKB / group) & ~int64_t(7)),
+                          t * kTileN);
         issued = i + 1;
       }
       // Unwinding after an abort: let the copies already issued land before smem is released.
@@ -217,12 +225,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t u = lo + i;
         const int64_t t = u / G, kb = u % G;
         const int64_t n = t * kTileN + r;
-        p0 = n < N ? __half2float(scale[n * gpr + (kb * kKB) / group]) : 0.f;
+        if (!kScaleTma) p0 = n < N ? __half2float(scale[n * gpr + (kb * kKB) / group]) : 0.f;
         bool ok = tc::mbar_wait(&full[s], ph, wait_ns, abort_flag) &&
                   tc::mbar_wait(&a_empty[a], aph ^ 1u, wait_ns, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) {  // warp-uniform: the tcgen05 ops below are .sync.aligned
           give_up();
           break;
+        }
+        if (kScaleTma) {  // rows past N arrive as zeros
+          const __half* sst = reinterpret_cast<const __half*>(smem + (size_t)s * kStageBytes + kWBytes + kXBytes);
+          p0 = __half2float(sst[r * 8 + (int)(((kb * kKB) / group) & 7)]);
         }
         const uint8_t* wrow = smem + (size_t)s * kStageBytes + r * 64;
         uint32_t regs[32];
@@ -367,13 +379,14 @@ static Plan make_plan(int64_t n, int64_t k) {
 
 // The two tensor maps of a call. Encoding is a host-side driver call of a few microseconds; the last few
 // (pointer, shape) combinations are cached so a steady stream of calls on the same buffers skips it.
-static int tensor_maps(const uint8_t* w, const uint16_t* x, int64_t m, int64_t n, int64_t k, CUtensorMap* tmW,
-                       CUtensorMap* tmX) {
+static int tensor_maps(const uint8_t* w, const uint16_t* x, const uint16_t* scale, int64_t m, int64_t n, int64_t k,
+                       int64_t group, CUtensorMap* tmW, CUtensorMap* tmX, CUtensorMap* tmS) {
   struct Entry {
     const void* w;
     const void* x;
-    int64_t m, n, k;
-    CUtensorMap tw, tx;
+    const void* sc;
+    int64_t m, n, k, g;
+    CUtensorMap tw, tx, ts;
   };
   static std::mutex mu;
   static Entry cache[8];
@@ -382,9 +395,10 @@ static int tensor_maps(const uint8_t* w, const uint16_t* x, int64_t m, int64_t n
     std::lock_guard<std::mutex> lk(mu);
     for (int i = 0; i < used; ++i) {
       const Entry& e = cache[i];
-      if (e.w == w && e.x == x && e.m == m && e.n == n && e.k == k) {
+      if (e.w == w && e.x == x && e.sc == scale && e.m == m && e.n == n && e.k == k && e.g == group) {
         *tmW = e.tw;
         *tmX = e.tx;
+        *tmS = e.ts;
         return UP_OK;
       }
     }
@@ -411,8 +425,19 @@ static int tensor_maps(const uint8_t* w, const uint16_t* x, int64_t m, int64_t n
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return UP_ERR_CUDA;
   }
+  *tmS = *tmX;  // unused unless the scales qualify for TMA
+  if ((k / group) % 8 == 0 && reinterpret_cast<uintptr_t>(scale) % 16 == 0) {
+    const cuuint64_t dims[2] = {(cuuint64_t)(k / group), (cuuint64_t)n};
+    const cuuint64_t strides[1] = {(cuuint64_t)(k / group * 2)};
+    const cuuint32_t box[2] = {8, kTileN};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(scale), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return UP_ERR_CUDA;
+  }
   std::lock_guard<std::mutex> lk(mu);
-  cache[next] = Entry{w, x, m, n, k, *tmW, *tmX};
+  cache[next] = Entry{w, x, scale, m, n, k, group, *tmW, *tmX, *tmS};
   next = (next + 1) % 8;
   if (used < 8) ++used;
   return UP_OK;
@@ -443,11 +468,12 @@ extern "C" int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, cons
   if (!aligned(w, 16) || !aligned(x, 16) || !aligned(workspace, 256)) return UP_ERR_INVALID;
   const Plan p = make_plan(n, k);
   if (workspace_bytes < p.bytes) return UP_ERR_INVALID;
-  CUtensorMap tmW, tmX;
+  CUtensorMap tmW, tmX, tmS;
   {
-    const int st = tensor_maps(w, x, m, n, k, &tmW, &tmX);
+    const int st = tensor_maps(w, x, scale, m, n, k, group, &tmW, &tmX, &tmS);
     if (st != UP_OK) return st;
   }
+  const bool scale_tma = (k / group) % 8 == 0 && aligned(scale, 16);
   {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -456,7 +482,9 @@ extern "C" int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, cons
     static bool attr_set[64] = {false};
     std::lock_guard<std::mutex> lk(mu);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-      e = cudaFuncSetAttribute(w4a16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+      e = cudaFuncSetAttribute(w4a16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(w4a16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
       if (e != cudaSuccess) return cuda_status(e);
       if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
@@ -466,9 +494,10 @@ extern "C" int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, cons
   auto* counters = reinterpret_cast<uint32_t*>(base + p.counters_off);
   auto* partials = reinterpret_cast<float*>(base + p.partials_off);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  w4a16_kernel<<<(unsigned)p.P, kThreads, kSmemBytes, s>>>(tmW, tmX, reinterpret_cast<const __half*>(scale), out,
-                                                          (int)m, n, k, group, p.U, p.G, p.S_max, hdr, counters,
-                                                          partials, wait_limit_ns());
+  auto kern = scale_tma ? w4a16_kernel<true> : w4a16_kernel<false>;
+  kern<<<(unsigned)p.P, kThreads, kSmemBytes, s>>>(tmW, tmX, tmS, reinterpret_cast<const __half*>(scale), out,
+                                                  (int)m, n, k, group, p.U, p.G, p.S_max, hdr, counters, partials,
+                                                  wait_limit_ns());
   note_launch();
   return check_launch();
 }
