@@ -7,29 +7,32 @@
 // tests/sub_byte_packing.rs:24-40), with f32 accumulation. The oracle sums exactly and rounds once
 // (docs/accum-policies.md:8-20); this kernel is held to |got - exact_bf16| <= 1/2 ulp_bf16 + gamma * sum|x w s|.
 //
-// Design (swap-AB: the weight rows are the MMA's M, the <= 16 activation rows its N):
+// Design (swap-AB: the weight rows are the MMA's M = 128, the <= 16 activation rows its N = 16):
 //  * A unit of work is one k-block (128 k) of one 128-row tile of W. The N/128 x K/128 units are split
 //    evenly over one persistent CTA per SM (stream-K), so every SM streams the same share of W.
-//  * warp 0 (one lane): TMA producer. Per unit it loads the int4 tile (128 rows x 64 bytes, 64-byte
-//    swizzle) and the bf16 activation k-block (16 rows x 128 k, 128-byte swizzle) into a ring of smem
-//    stages. No multicast.
-//  * warps 2..9: dequant. Each thread owns one W row (its TMEM lane) and half of the k-block; it turns
-//    the nibbles into exact bf16 with one prmt + one lop3 + one bf16x2 subtract per pair and stores them
-//    straight into tensor memory (tcgen05.st), where they are the MMA's A operand. Dequantized weights
-//    never touch shared memory, which keeps smem bandwidth for the TMA stream.
-//  * warp 1 (one lane): issues 8 tcgen05.mma (M=128, N=16, K=16, A from TMEM, B from smem) per unit into
-//    one of four TMEM accumulator slots, and commits to mbarriers.
-//  * the same dequant warps, two units behind, read the unit's f32 accumulator (tcgen05.ld), scale it by
-//    scale[n][k-block] in f32 and add it to registers. A tile finished inside one CTA is written as bf16;
-//    a tile split between CTAs writes f32 partials, and whichever CTA finishes it last (an atomic count)
-//    sums the partials in CTA order and writes bf16 — no CTA ever waits on another.
+//  * Data movement: every dequant thread keeps its own copy pipeline, kPrefetch units deep, of plain
+//    asynchronous 16-byte copies (cp.async): the 32 bytes of its W row for the unit, one 16-byte piece of
+//    the unit's activation tile (written straight into the 128-byte-swizzled layout the MMA reads), and the
+//    16-byte chunk holding its row's group scale. The tensor-memory-access (TMA) unit is not used: its
+//    fixed cost of a few hundred cycles per copy would cap this kernel far below the HBM bound for tiles
+//    this narrow.
+//  * warps 4..11 (dequant): each thread owns one W row (its TMEM lane) and half of the k-block. It turns
+//    the nibbles into exact bf16 (one prmt, one lop3 and one bf16x2 subtract per pair) and stores them into
+//    tensor memory (tcgen05.st), where they are the MMA's A operand; dequantized weights never touch shared
+//    memory.
+//  * warps 0..3 (MMA issuers): a single thread issues only about one tcgen05.mma per ~100 cycles, much
+//    slower than an M=128, N=16, K=16 MMA executes, so four warps issue in parallel: warp g runs k-steps
+//    2g and 2g+1 of every unit into its own TMEM accumulator.
+//  * the dequant warps, two units behind, read the unit's four accumulators (tcgen05.ld), add them, scale
+//    by scale[n][k-block] in f32 and accumulate in registers. A tile finished inside one CTA is written as
+//    bf16; a tile split between CTAs writes f32 partials, and whichever CTA finishes it last (an atomic
+//    count) sums them in CTA order, writes bf16 and clears the partials — no CTA ever waits on another.
 // Every mbarrier wait is bounded; a wait that runs out sets the workspace error word and the CTA unwinds.
 #include "common.cuh"
 #include "tc.cuh"
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
-#include <cudaTypedefs.h>
 
 #include <mutex>
 
@@ -39,21 +42,25 @@ namespace w4 {
 constexpr int kTileN = 128;                    // W rows per tile = MMA M
 constexpr int kMmaN = 16;                      // activation rows = MMA N
 constexpr int kKB = 128;                       // k per unit
-constexpr int kStages = 10;                    // smem ring depth
-constexpr int kWBytes = kTileN * kKB / 2;      // 8 KiB of int4
-constexpr int kXBytes = kMmaN * kKB * 2;       // 4 KiB of bf16
-constexpr int kSBytes = kTileN * 8 * 2;        // 2 KiB: an 8-wide column block of f16 scales per row
-constexpr int kStageBytes = kWBytes + kXBytes + kSBytes;  // 14 KiB (1024-aligned parts)
-constexpr int kAStages = 4;                    // TMEM A stages, 64 columns each
-constexpr int kDSlots = 4;                     // TMEM accumulator slots, 16 columns each
+constexpr int kDqThreads = 256;                // 8 dequant warps: 128 rows x 2 k-halves
+constexpr int kWBytes = kTileN * kKB / 2;      // 8 KiB of int4 per unit: [2 chunks][256 threads][16 B]
+constexpr int kXBytes = kMmaN * kKB * 2;       // 4 KiB of bf16 per unit, 128-byte swizzled (2 atoms per 64 k)
+constexpr int kSBytes = kDqThreads * 16;       // 4 KiB: each thread's 16-byte chunk of scales
+constexpr int kStageBytes = kXBytes + kWBytes + kSBytes;  // 16 KiB; x first (1024-aligned)
+constexpr int kPrefetch = 4;                   // units a thread's copies run ahead
+constexpr int kStages = kPrefetch + 3;         // a stage is refilled 3 units after its MMAs were issued
+constexpr int kRing = 4;                       // units in flight between dequant, MMA and epilogue
+constexpr int kIssuers = 4;                    // MMA-issuing warps
 constexpr int kTmemCols = 512;
-constexpr int kACol0 = 0;
-constexpr int kDCol0 = kAStages * 64;          // 256
+constexpr int kACol0 = 0;                      // A (dequantized W) stages: kRing x 64 columns
+constexpr int kDCol0 = kRing * 64;             // accumulators: kRing units x kIssuers x 16 columns
 constexpr int kLag = 2;                        // epilogue trails the dequant by this many units
-constexpr int kThreads = 320;                  // warp 0 TMA, warp 1 MMA, warps 2..9 dequant/epilogue
-constexpr int kDqThreads = 256;
-constexpr int kBarBytes = 1024;
+constexpr int kDq0 = kIssuers;                 // first dequant warp
+constexpr int kThreads = 32 * kIssuers + kDqThreads;  // 384
+constexpr int kBarBytes = 512;
 constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + (size_t)kStages * kStageBytes + kBarBytes;
+static_assert(kStages * kStageBytes + kBarBytes + 1024 <= 227 * 1024, "shared memory");
+static_assert(kStages - kPrefetch >= 3 && kRing >= kLag + 2, "pipeline distances");
 
 struct WsHeader {
   uint32_t ticket, done, epoch, error;  // same layout as the scan workspace: `error` at byte 12
@@ -84,23 +91,54 @@ __device__ __forceinline__ uint32_t nib2_to_bf16x2(uint32_t q, uint32_t q4, int 
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-// kScaleTma: the unit's group scales arrive in the stage by TMA (needs K/group % 8 == 0, so a row of scales
-// is a whole number of 16-byte chunks); otherwise each thread reads its scale from global memory.
-template <bool kScaleTma>
+// Position of a unit (tile t, k-block kb, scale-group index gi = kb*128/group) advanced one unit at a time
+// with additions only: 64-bit division and modulo are emulated in software and would dominate the loop.
+struct UnitCursor {
+  int t, kb, sub, gi;  // sub = kb % (group / 128)
+  __device__ __forceinline__ void init(int64_t u, int64_t G, int kpg) {
+    t = (int)(u / G);
+    kb = (int)(u - (int64_t)t * G);
+    gi = kb / kpg;
+    sub = kb - gi * kpg;
+  }
+  __device__ __forceinline__ void next(int G, int kpg) {
+    if (++kb == G) {
+      kb = 0;
+      sub = 0;
+      gi = 0;
+      ++t;
+    } else if (++sub == kpg) {
+      sub = 0;
+      ++gi;
+    }
+  }
+};
+
+// 16-byte asynchronous copy global -> shared; `valid` == false fills zeros without reading the source.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(tc::smem_u32(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// kScaleChunk: K/group % 8 == 0 and the scales are 16-byte aligned, so each row's scales are whole 16-byte
+// chunks and every thread copies the chunk holding its scale; otherwise each thread reads its scale with a
+// plain load.
+template <bool kScaleChunk>
 __global__ void __launch_bounds__(kThreads, 1)
-    w4a16_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
-                 const __grid_constant__ CUtensorMap tmS, const __half* __restrict__ scale, uint16_t* __restrict__ out, int M, int64_t N, int64_t K,
-                 int64_t group, int64_t U, int64_t G, int64_t S_max, WsHeader* hdr, uint32_t* counters,
-                 float* partials, uint64_t wait_ns) {
+    w4a16_kernel(const uint8_t* __restrict__ w, const __half* __restrict__ scale, const uint16_t* __restrict__ x,
+                 uint16_t* __restrict__ out, int M, int64_t N, int64_t K, int64_t group, int64_t U, int64_t G,
+                 int64_t S_max, WsHeader* hdr, uint32_t* counters, float* partials, uint64_t wait_ns) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)kStages * kStageBytes);
-  uint64_t* empty = full + kStages;
-  uint64_t* a_full = empty + kStages;
-  uint64_t* a_empty = a_full + kAStages;
-  uint64_t* d_full = a_empty + kAStages;
-  uint64_t* d_empty = d_full + kDSlots;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + kDSlots);
+  uint64_t* x_ready = reinterpret_cast<uint64_t*>(smem + (size_t)kStages * kStageBytes);  // [kStages]: 256
+  uint64_t* a_full = x_ready + kStages;        // [kRing][2]: the A half h of a unit is in TMEM (128 threads)
+  uint64_t* mma_done = a_full + 2 * kRing;     // [kRing]: every issuer's MMAs of the unit completed
+  uint64_t* d_empty = mma_done + kRing;        // [kRing]: the epilogue has read the unit's accumulators
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + kRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -109,17 +147,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t n_units = hi - lo;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      tc::mbar_init(&full[s], 1);
-      tc::mbar_init(&empty[s], kDqThreads + 1);
-    }
-    for (int a = 0; a < kAStages; ++a) {
-      tc::mbar_init(&a_full[a], kDqThreads);
-      tc::mbar_init(&a_empty[a], 1);
-    }
-    for (int d = 0; d < kDSlots; ++d) {
-      tc::mbar_init(&d_full[d], 1);
-      tc::mbar_init(&d_empty[d], kDqThreads);
+    for (int s = 0; s < kStages; ++s) tc::mbar_init(&x_ready[s], kDqThreads);
+    for (int a = 0; a < kRing; ++a) {
+      tc::mbar_init(&a_full[2 * a], kDqThreads / 2);
+      tc::mbar_init(&a_full[2 * a + 1], kDqThreads / 2);
+      tc::mbar_init(&mma_done[a], kIssuers);
+      tc::mbar_init(&d_empty[a], kDqThreads);
     }
     *abort_flag = 0;
     tc::mbar_fence_init();
@@ -138,79 +171,79 @@ __global__ void __launch_bounds__(kThreads, 1)
     atomicOr(&hdr->error, 1u);
   };
 
-  if (warp == 0) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      tc::tma_prefetch_desc(&tmW);
-      tc::tma_prefetch_desc(&tmX);
-      if (kScaleTma) tc::tma_prefetch_desc(&tmS);
-      int64_t issued = 0;
-      for (int64_t i = 0; i < n_units; ++i) {
-        const int s = (int)(i % kStages);
-        const uint32_t ph = (uint32_t)((i / kStages) & 1);
-        if (!tc::mbar_wait(&empty[s], ph ^ 1u, wait_ns, abort_flag)) {
-          give_up();
-          break;
-        }
-        const int64_t u = lo + i;
-        const int32_t t = (int32_t)(u / G), kb = (int32_t)(u % G);
-        uint8_t* st = smem + (size_t)s * kStageBytes;
-        tc::mbar_arrive_expect_tx(&full[s], kScaleTma ? kStageBytes : kWBytes + kXBytes);
-        tc::tma_load_2d(st, &tmW, &full[s], kb * (kKB / 2), t * kTileN);
-        tc::tma_load_2d(st + kWBytes, &tmX, &full[s], kb * kKB, 0);
-        tc::tma_load_2d(st + kWBytes + 2048, &tmX, &full[s], kb * kKB + 64, 0);
-        if (kScaleTma)
-          tc::tma_load_2d(st + kWBytes + kXBytes, &tmS, &full[s], (int32_t)(((int64_t)kb * kKB / group) & ~int64_t(7)),
-                          t * kTileN);
-        issued = i + 1;
-      }
-      // Unwinding after an abort: let the copies already issued land before smem is released.
-      if (*abort_flag) {
-        for (int64_t i = (issued > kStages ? issued - kStages : 0); i < issued; ++i)
-          tc::mbar_wait(&full[i % kStages], (uint32_t)((i / kStages) & 1), wait_ns, nullptr);
-      }
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+  if (warp < kIssuers) {
+    // ---------------- MMA issuers: warp g issues k-steps 2g, 2g+1 of every unit ----------------
+    const int g = warp;
     if (lane == 0) {
       constexpr uint32_t idesc = tc::idesc_bf16_f32(kTileN, kMmaN);
       int64_t issued = 0;
       for (int64_t i = 0; i < n_units; ++i) {
-        const int s = (int)(i % kStages), a = (int)(i % kAStages), d = (int)(i % kDSlots);
-        const uint32_t ph = (uint32_t)((i / kStages) & 1), aph = (uint32_t)((i / kAStages) & 1),
-                       dph = (uint32_t)((i / kDSlots) & 1);
-        if (!tc::mbar_wait(&full[s], ph, wait_ns, abort_flag) || !tc::mbar_wait(&a_full[a], aph, wait_ns, abort_flag) ||
-            !tc::mbar_wait(&d_empty[d], dph ^ 1u, wait_ns, abort_flag)) {
+        const int s = (int)(i % kStages), a = (int)(i % kRing);
+        const uint32_t ph = (uint32_t)((i / kStages) & 1), rph = (uint32_t)((i / kRing) & 1);
+        if (!tc::mbar_wait(&x_ready[s], ph, wait_ns, abort_flag) ||
+            !tc::mbar_wait(&a_full[2 * a + (g >> 1)], rph, wait_ns, abort_flag) ||
+            !tc::mbar_wait(&d_empty[a], rph ^ 1u, wait_ns, abort_flag)) {
           give_up();
           break;
         }
         tc::fence_after_sync();
-        const uint32_t xaddr = tc::smem_u32(smem + (size_t)s * kStageBytes + kWBytes);
+        const uint32_t xaddr = tc::smem_u32(smem + (size_t)s * kStageBytes);
 #pragma unroll
-        for (int j = 0; j < kKB / 16; ++j) {
+        for (int jj = 0; jj < 2; ++jj) {
+          const int j = 2 * g + jj;
           const uint64_t bdesc = tc::sdesc_kmajor_sw128(xaddr + (uint32_t)((j >> 2) * 2048 + (j & 3) * 32));
-          tc::mma_ts_bf16(tmem + kDCol0 + d * 16, tmem + kACol0 + a * 64 + j * 8, bdesc, idesc, j > 0 ? 1u : 0u);
+          tc::mma_ts_bf16(tmem + kDCol0 + a * (16 * kIssuers) + g * 16, tmem + kACol0 + a * 64 + j * 8, bdesc, idesc,
+                          jj > 0 ? 1u : 0u);
         }
-        tc::commit(&d_full[d]);
-        tc::commit(&a_empty[a]);
-        tc::commit(&empty[s]);
+        tc::commit(&mma_done[a]);
         issued = i + 1;
       }
       // Unwinding after an abort: the MMAs already issued must finish before TMEM is released.
       if (*abort_flag && issued > 0) {
         const int64_t i = issued - 1;
-        tc::mbar_wait(&d_full[i % kDSlots], (uint32_t)((i / kDSlots) & 1), wait_ns, nullptr);
+        tc::mbar_wait(&mma_done[i % kRing], (uint32_t)((i / kRing) & 1), wait_ns, nullptr);
       }
     }
   } else {
     // ---------------- dequant + epilogue ----------------
-    const int dw = warp - 2;
+    const int dw = warp - kDq0;
     const int q = warp & 3;         // TMEM lane quarter this warp may access
     const int h = dw >> 2;          // k half (dequant) and m half (epilogue)
     const int r = q * 32 + lane;    // row of the tile = TMEM lane
+    const int slot = dw * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-    const int sw = (r >> 1) & 3;    // 64-byte swizzle of this row
     const int64_t gpr = K / group;  // scales per row
+    // this thread's piece of every activation tile: row xm, 16-byte chunk xc of the 256-byte row
+    const int xm = slot >> 4, xc = slot & 15, xkh = xc >> 3, xcc = xc & 7;
+    const uint32_t x_dst = (uint32_t)(xkh * 2048 + xm * 128 + ((xcc ^ (xm & 7)) << 4));
+
+    const int Gi = (int)G, kpg = (int)(group / kKB);
+    const int64_t wrow = K / 2;
+    // issue the copies of unit j (at cursor c) into its stage
+    auto issue = [&](int64_t j, const UnitCursor& c) {
+      uint8_t* st = smem + (size_t)(j % kStages) * kStageBytes;
+      const int64_t n = (int64_t)c.t * kTileN + r;
+      const bool nv = n < N;
+      const uint8_t* wsrc = w + (nv ? n : 0) * wrow + c.kb * (kKB / 2) + h * 32;
+      cp_async16(st + kXBytes + slot * 16, wsrc, nv);
+      cp_async16(st + kXBytes + 4096 + slot * 16, wsrc + 16, nv);
+      const bool mv = xm < M;
+      cp_async16(st + x_dst, x + (mv ? xm : 0) * K + c.kb * kKB + xkh * 64 + xcc * 8, mv);
+      if (kScaleChunk) cp_async16(st + kXBytes + kWBytes + slot * 16, scale + (nv ? n : 0) * gpr + (c.gi & ~7), nv);
+    };
+
+    UnitCursor cn, cu, ce;  // the unit being prefetched, dequantized, and finished by the epilogue
+    cn.init(lo, G, kpg);
+    cu = cn;
+    ce = cn;
+    for (int64_t j = 0; j < kPrefetch; ++j) {
+      if (j < n_units) {
+        issue(j, cn);
+        cn.next(Gi, kpg);
+      }
+      cp_async_commit();
+    }
+
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.f;
@@ -220,66 +253,85 @@ __global__ void __launch_bounds__(kThreads, 1)
       p2 = p1;
       p1 = p0;
       if (i < n_units) {
-        const int s = (int)(i % kStages), a = (int)(i % kAStages);
-        const uint32_t ph = (uint32_t)((i / kStages) & 1), aph = (uint32_t)((i / kAStages) & 1);
-        const int64_t u = lo + i;
-        const int64_t t = u / G, kb = u % G;
-        const int64_t n = t * kTileN + r;
-        if (!kScaleTma) p0 = n < N ? __half2float(scale[n * gpr + (kb * kKB) / group]) : 0.f;
-        bool ok = tc::mbar_wait(&full[s], ph, wait_ns, abort_flag) &&
-                  tc::mbar_wait(&a_empty[a], aph ^ 1u, wait_ns, abort_flag);
+        const int s = (int)(i % kStages), a = (int)(i % kRing);
+        const uint32_t aph = (uint32_t)((i / kRing) & 1);
+        // refill the stage of unit i + kPrefetch once the MMAs that read its previous contents are done
+        const int64_t jn = i + kPrefetch;
+        bool ok = true;
+        if (jn < n_units && jn >= kStages) {
+          const int64_t old = jn - kStages;  // <= i - 3
+          ok = tc::mbar_wait(&mma_done[old % kRing], (uint32_t)((old / kRing) & 1), wait_ns, abort_flag);
+        }
+        // the A stage is free once the unit kRing earlier has been multiplied
+        ok = ok && tc::mbar_wait(&mma_done[a], aph ^ 1u, wait_ns, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) {  // warp-uniform: the tcgen05 ops below are .sync.aligned
           give_up();
           break;
         }
-        if (kScaleTma) {  // rows past N arrive as zeros
-          const __half* sst = reinterpret_cast<const __half*>(smem + (size_t)s * kStageBytes + kWBytes + kXBytes);
-          p0 = __half2float(sst[r * 8 + (int)(((kb * kKB) / group) & 7)]);
+        if (jn < n_units) {
+          issue(jn, cn);
+          cn.next(Gi, kpg);
         }
-        const uint8_t* wrow = smem + (size_t)s * kStageBytes + r * 64;
+        cp_async_commit();
+        cp_async_wait<kPrefetch>();  // this thread's copies of unit i have landed
+        tc::fence_proxy_async_smem();  // ... and are visible to the tensor core's reads of the activations
+        tc::mbar_arrive(&x_ready[s]);
+        const uint8_t* st = smem + (size_t)s * kStageBytes;
+        if (kScaleChunk) {
+          p0 = __half2float(reinterpret_cast<const __half*>(st + kXBytes + kWBytes + slot * 16)[cu.gi & 7]);
+        } else {
+          const int64_t n = (int64_t)cu.t * kTileN + r;
+          p0 = n < N ? __half2float(scale[n * gpr + cu.gi]) : 0.f;
+        }
+        cu.next(Gi, kpg);
         uint32_t regs[32];
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
-          const int c = 2 * h + cc;
-          const uint4 v = *reinterpret_cast<const uint4*>(wrow + ((c ^ sw) << 4));
+          const uint4 v = *reinterpret_cast<const uint4*>(st + kXBytes + cc * 4096 + slot * 16);
           const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const uint32_t q4 = wd[w] >> 4;
+          for (int wi = 0; wi < 4; ++wi) {
+            const uint32_t q4 = wd[wi] >> 4;
 #pragma unroll
-            for (int pp = 0; pp < 4; ++pp) regs[cc * 16 + w * 4 + pp] = nib2_to_bf16x2(wd[w], q4, pp);
+            for (int pp = 0; pp < 4; ++pp) regs[cc * 16 + wi * 4 + pp] = nib2_to_bf16x2(wd[wi], q4, pp);
           }
         }
-        tc::mbar_arrive(&empty[s]);
         tc::st_32x32b_x32(tmem + lane_addr + kACol0 + a * 64 + 32 * h, regs);
         tc::wait_st();
         tc::fence_before_sync();
-        tc::mbar_arrive(&a_full[a]);
+        tc::mbar_arrive(&a_full[2 * a + h]);
       }
       if (i >= kLag) {
         const int64_t e = i - kLag;
-        const int d = (int)(e % kDSlots);
-        const uint32_t dph = (uint32_t)((e / kDSlots) & 1);
-        const bool ok = tc::mbar_wait(&d_full[d], dph, wait_ns, abort_flag);
+        const int d = (int)(e % kRing);
+        const uint32_t dph = (uint32_t)((e / kRing) & 1);
+        const bool ok = tc::mbar_wait(&mma_done[d], dph, wait_ns, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) {
           give_up();
           break;
         }
         tc::fence_after_sync();
-        uint32_t dv[8];
-        tc::ld_32x32b_x8(tmem + lane_addr + kDCol0 + d * 16 + 8 * h, dv);
+        uint32_t dv[kIssuers][8];
+#pragma unroll
+        for (int gg = 0; gg < kIssuers; ++gg)
+          tc::ld_32x32b_x8(tmem + lane_addr + kDCol0 + d * (16 * kIssuers) + gg * 16 + 8 * h, dv[gg]);
         tc::wait_ld();
         tc::fence_before_sync();
         tc::mbar_arrive(&d_empty[d]);
         const int64_t u = lo + e;
-        const int64_t t = u / G, kb = u % G;
+        const int64_t t = ce.t, kb = ce.kb;
+        ce.next(Gi, kpg);
         if (e == 0 || kb == 0) {
           seg_kb0 = kb;
 #pragma unroll
           for (int j = 0; j < 8; ++j) acc[j] = 0.f;
         }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = fmaf(p2, __uint_as_float(dv[j]), acc[j]);
+        for (int j = 0; j < 8; ++j) {
+          const float sum = (__uint_as_float(dv[0][j]) + __uint_as_float(dv[1][j])) +
+                            (__uint_as_float(dv[2][j]) + __uint_as_float(dv[3][j]));
+          acc[j] = fmaf(p2, sum, acc[j]);
+        }
         if (u + 1 == hi || kb == G - 1) {
           // ---- the segment [seg_kb0, kb] of tile t ends here ----
           const int64_t n = t * kTileN + r;
@@ -294,9 +346,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             // completes the tile's count (8 warps per contributing CTA) sums the partials in CTA order.
             const int64_t c0 = cta_of_unit(t * G, U, P), c1 = cta_of_unit(t * G + G - 1, U, P);
             const int64_t nseg = c1 - c0 + 1, sidx = (int64_t)blockIdx.x - c0;
-            float* slot = partials + ((t * S_max + sidx) * kMmaN) * kTileN;
+            float* pslot = partials + ((t * S_max + sidx) * kMmaN) * kTileN;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) __stcg(slot + (8 * h + j) * kTileN + r, acc[j]);
+            for (int j = 0; j < 8; ++j) __stcg(pslot + (8 * h + j) * kTileN + r, acc[j]);
             __threadfence();
             __syncwarp();
             uint32_t last = 0;
@@ -324,6 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    cp_async_wait<0>();  // no copy may still target this CTA's shared memory when it exits
   }
 
   tc::fence_before_sync();
@@ -333,19 +386,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---- host side ----
-static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, []() {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
 static int64_t host_cta_of_unit(int64_t u, int64_t U, int64_t P) {
   int64_t c = (u * P) / U;
   while (c + 1 < P && ((c + 1) * U) / P <= u) ++c;
@@ -376,73 +416,6 @@ static Plan make_plan(int64_t n, int64_t k) {
   return p;
 }
 
-
-// The two tensor maps of a call. Encoding is a host-side driver call of a few microseconds; the last few
-// (pointer, shape) combinations are cached so a steady stream of calls on the same buffers skips it.
-static int tensor_maps(const uint8_t* w, const uint16_t* x, const uint16_t* scale, int64_t m, int64_t n, int64_t k,
-                       int64_t group, CUtensorMap* tmW, CUtensorMap* tmX, CUtensorMap* tmS) {
-  struct Entry {
-    const void* w;
-    const void* x;
-    const void* sc;
-    int64_t m, n, k, g;
-    CUtensorMap tw, tx, ts;
-  };
-  static std::mutex mu;
-  static Entry cache[8];
-  static int next = 0, used = 0;
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    for (int i = 0; i < used; ++i) {
-      const Entry& e = cache[i];
-      if (e.w == w && e.x == x && e.sc == scale && e.m == m && e.n == n && e.k == k && e.g == group) {
-        *tmW = e.tw;
-        *tmX = e.tx;
-        *tmS = e.ts;
-        return UP_OK;
-      }
-    }
-  }
-  auto enc = encode_fn();
-  if (!enc) return UP_ERR_CUDA;
-  {
-    const cuuint64_t dims[2] = {(cuuint64_t)(k / 2), (cuuint64_t)n};
-    const cuuint64_t strides[1] = {(cuuint64_t)(k / 2)};
-    const cuuint32_t box[2] = {kKB / 2, kTileN};
-    const cuuint32_t estr[2] = {1, 1};
-    if (enc(tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return UP_ERR_CUDA;
-  }
-  {
-    const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
-    const cuuint64_t strides[1] = {(cuuint64_t)(k * 2)};
-    const cuuint32_t box[2] = {64, kMmaN};
-    const cuuint32_t estr[2] = {1, 1};
-    if (enc(tmX, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(x), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return UP_ERR_CUDA;
-  }
-  *tmS = *tmX;  // unused unless the scales qualify for TMA
-  if ((k / group) % 8 == 0 && reinterpret_cast<uintptr_t>(scale) % 16 == 0) {
-    const cuuint64_t dims[2] = {(cuuint64_t)(k / group), (cuuint64_t)n};
-    const cuuint64_t strides[1] = {(cuuint64_t)(k / group * 2)};
-    const cuuint32_t box[2] = {8, kTileN};
-    const cuuint32_t estr[2] = {1, 1};
-    if (enc(tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(scale), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return UP_ERR_CUDA;
-  }
-  std::lock_guard<std::mutex> lk(mu);
-  cache[next] = Entry{w, x, scale, m, n, k, group, *tmW, *tmX, *tmS};
-  next = (next + 1) % 8;
-  if (used < 8) ++used;
-  return UP_OK;
-}
-
 }  // namespace w4
 }  // namespace up
 
@@ -465,15 +438,11 @@ extern "C" int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, cons
   if (k == 0 || k % kKB != 0 || group % kKB != 0 || k % group != 0) return UP_ERR_UNSUPPORTED;
   if (k / 2 > 0x7fffffff || n > 0x7fffffff) return UP_ERR_UNSUPPORTED;
   UP_CHECK_ARG(w && scale && x && out && workspace);
+  // 16-byte copies: W rows (K/2 bytes, a multiple of 64) and activation rows (2K bytes) start 16-byte aligned
   if (!aligned(w, 16) || !aligned(x, 16) || !aligned(workspace, 256)) return UP_ERR_INVALID;
   const Plan p = make_plan(n, k);
   if (workspace_bytes < p.bytes) return UP_ERR_INVALID;
-  CUtensorMap tmW, tmX, tmS;
-  {
-    const int st = tensor_maps(w, x, scale, m, n, k, group, &tmW, &tmX, &tmS);
-    if (st != UP_OK) return st;
-  }
-  const bool scale_tma = (k / group) % 8 == 0 && aligned(scale, 16);
+  const bool scale_chunk = (k / group) % 8 == 0 && aligned(scale, 16);
   {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -494,10 +463,9 @@ extern "C" int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, cons
   auto* counters = reinterpret_cast<uint32_t*>(base + p.counters_off);
   auto* partials = reinterpret_cast<float*>(base + p.partials_off);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  auto kern = scale_tma ? w4a16_kernel<true> : w4a16_kernel<false>;
-  kern<<<(unsigned)p.P, kThreads, kSmemBytes, s>>>(tmW, tmX, tmS, reinterpret_cast<const __half*>(scale), out,
-                                                  (int)m, n, k, group, p.U, p.G, p.S_max, hdr, counters, partials,
-                                                  wait_limit_ns());
+  auto kern = scale_chunk ? w4a16_kernel<true> : w4a16_kernel<false>;
+  kern<<<(unsigned)p.P, kThreads, kSmemBytes, s>>>(w, reinterpret_cast<const __half*>(scale), x, out, (int)m, n, k,
+                                                  group, p.U, p.G, p.S_max, hdr, counters, partials, wait_limit_ns());
   note_launch();
   return check_launch();
 }
