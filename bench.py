@@ -467,7 +467,7 @@ def main():
     clocks = clk.stop()
 
     cpu = cpu_scan_baseline() if (ctx.rank == 0 and ctx.world == 1) else None
-    traffic = ncu_traffic("scan_i32_incl_add_2p28.md")
+    traffic = ncu_traffic("scan_i32_kernel_incl_add.md")
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": ctx.world, "steps": K, "warmup": W,
         "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
