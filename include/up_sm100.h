@@ -227,6 +227,21 @@ UP_API int up_sm100_scan_i32(const int32_t* x, int32_t* y, int64_t rows, int64_t
                       void* stream);
 UP_API size_t up_sm100_scan_workspace_bytes(int64_t rows, int64_t k);
 
+/* No counterpart in the reference: up_sm100_scan_i32 for callers that cannot allocate device memory,
+ * for example a host runtime whose allocator must not run on this path. The scratch is a built-in
+ * device array (128 KiB per device), so nothing is allocated or freed. It holds at most 16384 tiles:
+ * rows * ceil(k / 16384) <= 16384, one row of up to 2^28 elements. Larger shapes return
+ * UP_ERR_UNSUPPORTED with the reason in up_sm100_last_error. The first call on each device does set-up
+ * (looks up the array's address, sets the kernel's shared-memory size); make it before any stream
+ * capture. Every call on a device shares the array, so calls that overlap in time (other streams, other
+ * host threads) race; serialize them. `sync` != 0 waits for the scan and returns UP_ERR_DEVICE_TIMEOUT
+ * if its look-back ran out of time. The timeout flag is sticky: the report also covers any earlier
+ * unreported call on this device, and reporting clears it. `sync` == 0 returns once the scan is
+ * enqueued. */
+UP_API int up_sm100_scan_i32_noalloc(const int32_t* x, int32_t* y, int64_t rows, int64_t k, int op,
+                                     int exclusive, int reverse, const int32_t* carry_in, int sync,
+                                     void* stream);
+
 /* Fold of a whole int32 array to one value (the first pass of a scan sharded over GPUs): SUM (wrapping),
  * MAX or MIN, written to `total` (device, one int32). Deterministic. */
 UP_API int up_sm100_reduce_i32(const int32_t* x, int64_t n, int op, int32_t* total, void* stream);

@@ -30,6 +30,11 @@ int cuda_status(cudaError_t e) {
 
 int check_launch() { return cuda_status(cudaGetLastError()); }
 
+int fail_with(int status, const char* text) {
+  std::snprintf(g_last_error, sizeof(g_last_error), "%s", text);
+  return status;
+}
+
 uint64_t wait_limit_ns() { return g_wait_ns.load(std::memory_order_relaxed); }
 
 int take_withhold_flag() { return g_withhold.exchange(0); }

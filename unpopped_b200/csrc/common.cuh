@@ -19,6 +19,7 @@ int check_launch();               // cudaGetLastError after a launch
 uint64_t wait_limit_ns();
 int take_withhold_flag();         // returns and clears the scan test hook
 int sm_count();                   // SMs of the current device (cached per device)
+int fail_with(int status, const char* text);  // records `text` as the last error, returns `status`
 
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 

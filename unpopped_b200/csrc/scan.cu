@@ -376,3 +376,54 @@ extern "C" int up_sm100_workspace_status(void* workspace, void* stream) {
   }
   return UP_OK;
 }
+
+// ---- scan with built-in scratch, for callers that cannot allocate ----
+//
+// The look-back flags and the error word live in one file-scope device array instead of a caller's
+// workspace. Each device holds its own copy of the array, zero from module load. What must be zero is
+// the error word, and it is cleared again whenever a timeout is reported. The flags are epoch-tagged,
+// so they never need clearing. Every call on a device uses the same array: calls that overlap in time
+// race, through concurrent streams or host threads, and must be serialized by the caller.
+namespace up {
+constexpr int64_t kNoAllocMaxTiles = 16384;  // rows x ceil(k / 16384) tiles, e.g. one row of 2^28 elements
+static __device__ __align__(256) uint64_t g_noalloc_scratch[sizeof(ScanHeader) / 8 + kNoAllocMaxTiles];
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[64] = {};
+
+// The device address of this device's copy of the scratch, looked up once per device (with it current).
+static cudaError_t noalloc_scratch(int dev, void** out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return cudaSuccess;
+}
+}  // namespace up
+
+extern "C" int up_sm100_scan_i32_noalloc(const int32_t* x, int32_t* y, int64_t rows, int64_t k, int op,
+                                         int exclusive, int reverse, const int32_t* carry_in, int sync,
+                                         void* stream) {
+  UP_CHECK_ARG(rows >= 0 && k >= 0);
+  if (op != UP_OP_SUM && op != UP_OP_MAX && op != UP_OP_MIN) return UP_ERR_UNSUPPORTED;
+  if (rows == 0 || k == 0) return UP_OK;
+  const int64_t tpr = (k + kScanTile - 1) / kScanTile;
+  if (rows > kNoAllocMaxTiles || rows * tpr > kNoAllocMaxTiles)
+    return fail_with(UP_ERR_UNSUPPORTED,
+                     "up_sm100_scan_i32_noalloc: rows * ceil(k / 16384) exceeds the built-in scratch's 16384 "
+                     "tiles; use up_sm100_scan_i32 with a workspace");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (dev < 0 || dev >= 64) return fail_with(UP_ERR_UNSUPPORTED, "up_sm100_scan_i32_noalloc: device index >= 64");
+  void* scratch = nullptr;
+  e = noalloc_scratch(dev, &scratch);
+  if (e != cudaSuccess) return cuda_status(e);
+  const int st = up_sm100_scan_i32(x, y, rows, k, op, exclusive, reverse, carry_in, scratch,
+                                   sizeof(g_noalloc_scratch), stream);
+  if (st != UP_OK || !sync) return st;
+  return up_sm100_workspace_status(scratch, stream);
+}
