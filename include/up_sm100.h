@@ -229,8 +229,8 @@ UP_API size_t up_sm100_scan_workspace_bytes(int64_t rows, int64_t k);
 
 /* No counterpart in the reference: up_sm100_scan_i32 for callers that cannot allocate device memory,
  * for example a host runtime whose allocator must not run on this path. The scratch is a built-in
- * device array (128 KiB per device), so nothing is allocated or freed. It holds at most 16384 tiles:
- * rows * ceil(k / 16384) <= 16384, one row of up to 2^28 elements. Larger shapes return
+ * device array (256 KiB per device), so nothing is allocated or freed. It holds at most 32768 tiles:
+ * rows * ceil(k / 8192) <= 32768, one row of up to 2^28 elements. Larger shapes return
  * UP_ERR_UNSUPPORTED with the reason in up_sm100_last_error. The first call on each device does set-up
  * (looks up the array's address, sets the kernel's shared-memory size); make it before any stream
  * capture. Every call on a device shares the array, so calls that overlap in time (other streams, other

@@ -121,10 +121,10 @@ def test_argument_errors_return_before_any_device_work():
 
 def test_workspace_sizes():
     L = _lib.load()
-    assert L.up_sm100_scan_workspace_bytes(1, 1 << 28) == 64 + 8 * ((1 << 28) // 16384)
-    assert L.up_sm100_scan_workspace_bytes(3, 40000) == 64 + 8 * 3 * 3
+    assert L.up_sm100_scan_workspace_bytes(1, 1 << 28) == 64 + 8 * ((1 << 28) // 8192)  # one flag per 8192-tile
+    assert L.up_sm100_scan_workspace_bytes(3, 40000) == 64 + 8 * 3 * 5
     assert L.up_sm100_w4a16_workspace_bytes(16, 28672, 8192, 128) > 64
     n = ctypes.c_size_t(0)
     ins = (_lib.UpTensor * 1)(Operand("I32", (4, 40000)).to_c())
     assert L.up_sm100_workspace_bytes(_lib.KERNEL["SCAN_I32"], ins, 1, ins, 1, None, 0, ctypes.byref(n)) == 0
-    assert n.value == 64 + 8 * 4 * 3
+    assert n.value == 64 + 8 * 4 * 5

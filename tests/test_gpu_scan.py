@@ -39,7 +39,8 @@ def test_golden_corpora_every_variant(case):
         assert run(x, op, mode == "excl", direction == "rev").tolist() == exp, key
 
 
-SIZES = [1, 2, 31, 512, 4095, 4096, 4097, 16383, 16384, 16385, 2 * 16384 + 8, 100_003, (1 << 20) + 12]
+SIZES = [1, 2, 31, 512, 4095, 4096, 4097, 8191, 8192, 8196, 16383, 16384, 16385, 2 * 16384 + 8, 100_003,
+         (1 << 20) + 12, 160 * 8192 + 4]
 
 
 @pytest.mark.parametrize("n", SIZES)
@@ -105,7 +106,7 @@ def test_bounded_wait_reports_timeout_and_recovers():
     """Tile 0 withholds its flag (a flag nothing sets): every other tile's look-back gives up after the wait
     limit, the status comes back as UP_ERR_DEVICE_TIMEOUT, and the next launch works. No fault, no hang."""
     L = _lib.load()
-    x = torch.ones(1 << 18, dtype=torch.int32, device="cuda")  # 16 tiles
+    x = torch.ones(1 << 18, dtype=torch.int32, device="cuda")  # 32 tiles
     ws = torch.zeros(L.up_sm100_scan_workspace_bytes(1, x.numel()), dtype=torch.uint8, device="cuda")
     L.up_sm100_set_wait_limit_ns(2_000_000)  # 2 ms
     try:

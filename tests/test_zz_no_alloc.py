@@ -16,8 +16,8 @@ from unpopped_b200 import _lib
 
 pytestmark = pytest.mark.gpu
 OPS = {"sum": orc.OP_SUM, "max": orc.OP_MAX, "min": orc.OP_MIN}
-MAX_TILES = 16384
-TILE = 16384
+MAX_TILES = 32768
+TILE = 8192
 
 
 @pytest.fixture(scope="module")
@@ -87,7 +87,7 @@ def test_larger_shapes_are_refused_before_any_device_work(L):
     before = L.up_sm100_launch_count()
     st, _ = noalloc(L, x.view(MAX_TILES + 1, 1), "sum", False, False)
     assert st == _lib.UP_ERR_UNSUPPORTED
-    assert b"16384" in L.up_sm100_last_error()
+    assert b"32768" in L.up_sm100_last_error()
     st, _ = noalloc(L, torch.zeros(2, TILE * (MAX_TILES // 2) + 1, dtype=torch.int32, device="cuda"), "max",
                     False, False)
     assert st == _lib.UP_ERR_UNSUPPORTED
@@ -102,7 +102,7 @@ def test_larger_shapes_are_refused_before_any_device_work(L):
 def test_a_timeout_is_reported_once_and_the_next_call_works(L):
     """The bounded-wait test hook: tile 0 withholds its flag, so every later tile's look-back gives up after
     the (shortened) limit. The sync report returns UP_ERR_DEVICE_TIMEOUT and clears the flag."""
-    x = torch.ones(1 << 18, dtype=torch.int32, device="cuda")  # 16 tiles
+    x = torch.ones(1 << 18, dtype=torch.int32, device="cuda")  # 32 tiles
     L.up_sm100_set_wait_limit_ns(2_000_000)
     try:
         L.up_sm100_set_test_withhold_flag(1)

@@ -7,21 +7,19 @@
 // INT32_MAX); Sum wraps at 32 bits; a reverse scan walks from the row's end. Integer combines are exact
 // and associative, so the tile decomposition below produces the serial walk's bytes.
 //
-// Decomposition: a tile is 16384 consecutive elements (64 KiB) of one row (the row's last tile may be
-// short); CTA i scans tile i. One thread moves the tile into shared memory with bulk copies
-// (cp.async.bulk, no multicast) and back out with bulk stores, so the loads in flight cost no registers and
-// three tiles per SM stream concurrently. In shared memory, warp w owns 2048 elements; lane l handles the
-// 16-byte chunks i*32 + l (i = 0..15), which keeps every shared-memory access conflict-free. Pass 1 folds
-// the tile; the tile's aggregate goes out as a look-back flag; pass 2 rescans from shared memory with the
-// prefix found by the look-back and writes the result in place.
+// Two forms share one flag protocol:
+//  * the persistent form (scan_i32_persist_kernel, below), for rows that are 16-byte aligned and whole
+//    16-byte chunks long: one CTA per SM streams 8192-element tiles through a ring of shared-memory stages
+//    by bulk copies, and resolves each tile's prefix from the other tiles' aggregates off the critical path;
+//  * the general form (scan_i32_kernel), for any alignment: one CTA per 16384-element tile, element loads,
+//    decoupled look-back with aggregate and inclusive flags.
 //
-// Look-back: one 64-bit flag per tile = epoch(30) | status(2) | value(32), written and read with relaxed
-// gpu-scope atomics (the value travels inside the flag word). Status: 1 = aggregate of this tile,
-// 2 = inclusive prefix through this tile, 3 = aborted. Warp 0 examines 32 predecessors per step. CTAs are
-// dispatched in index order, so a tile only ever waits on tiles whose CTAs have started. The epoch is a
-// per-launch number chosen on the host, so flags of earlier launches are never mistaken for this one's and
-// the workspace needs zero-filling only once. Every wait is bounded by a globaltimer deadline; a wait that
-// runs out sets the workspace error word and publishes "aborted", which successors propagate at once.
+// Look-back flags: one 64-bit word per tile = epoch(30) | status(2) | value(32), written and read with
+// relaxed gpu-scope atomics (the value travels inside the flag word). Status: 1 = aggregate of this tile,
+// 2 = inclusive prefix through this tile, 3 = aborted. The epoch is a per-launch number chosen on the host,
+// so flags of earlier launches are never mistaken for this one's and the workspace needs zero-filling only
+// once. Every wait is bounded by a globaltimer deadline; a wait that runs out sets the workspace error word
+// and publishes "aborted", which the tiles that wait on it propagate at once.
 #include "common.cuh"
 #include "tc.cuh"
 
@@ -35,7 +33,7 @@ constexpr int kLaneChunks = 16;                                  // 16-byte chun
 constexpr int kScanTile = kScanThreads * kLaneChunks * 4;        // 16384 elements
 constexpr int kWarpChunks = 32 * kLaneChunks;                    // 512 chunks = 2048 elements per warp
 constexpr int kTileBytes = kScanTile * 4;                        // 64 KiB
-constexpr size_t kScanSmem = kTileBytes + 64;                    // + the tile's mbarrier
+constexpr size_t kScanSmem = kTileBytes;
 
 struct ScanHeader {
   uint32_t reserved0, reserved1, reserved2;
@@ -82,29 +80,26 @@ __device__ __forceinline__ int32_t warp_incl_scan(int32_t v, int lane) {
   return v;
 }
 
-// The tile in shared memory, read and written by logical chunk (elements 4g .. 4g+3 in scan order).
-// `rev`: the tile is stored back to front (a reverse scan that was bulk-loaded); `cnt`: valid elements.
+// The tile in shared memory, in scan order, read and written by chunk (elements 4g .. 4g+3); `cnt` valid
+// elements, the rest read as the identity.
 template <int OP>
 struct TileView {
   int32_t* buf;
   int cnt;
-  bool rev;
   __device__ __forceinline__ void load(int g, int32_t (&v)[4]) const {
     const int e0 = 4 * g;
     if (e0 + 4 <= cnt) {
-      const int4 c = rev ? reinterpret_cast<const int4*>(buf)[(cnt >> 2) - 1 - g] : reinterpret_cast<const int4*>(buf)[g];
-      if (rev) { v[0] = c.w; v[1] = c.z; v[2] = c.y; v[3] = c.x; }
-      else { v[0] = c.x; v[1] = c.y; v[2] = c.z; v[3] = c.w; }
+      const int4 c = reinterpret_cast<const int4*>(buf)[g];
+      v[0] = c.x; v[1] = c.y; v[2] = c.z; v[3] = c.w;
     } else {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) v[c] = (e0 + c < cnt) ? buf[e0 + c] : ident<OP>();  // only unreversed here
+      for (int c = 0; c < 4; ++c) v[c] = (e0 + c < cnt) ? buf[e0 + c] : ident<OP>();
     }
   }
   __device__ __forceinline__ void store(int g, const int32_t (&o)[4]) const {
     const int e0 = 4 * g;
     if (e0 + 4 <= cnt) {
-      if (rev) reinterpret_cast<int4*>(buf)[(cnt >> 2) - 1 - g] = make_int4(o[3], o[2], o[1], o[0]);
-      else reinterpret_cast<int4*>(buf)[g] = make_int4(o[0], o[1], o[2], o[3]);
+      reinterpret_cast<int4*>(buf)[g] = make_int4(o[0], o[1], o[2], o[3]);
     } else {
 #pragma unroll
       for (int c = 0; c < 4; ++c)
@@ -113,16 +108,21 @@ struct TileView {
   }
 };
 
+// General form: CTA i scans tile i (16384 elements of one row; the row's last tile may be short). The tile
+// is read with element loads into shared memory in scan order; in shared memory, warp w owns 2048 elements
+// and lane l handles the 16-byte chunks i*32 + l (i = 0..15), which keeps every access conflict-free.
+// Pass 1 folds the tile; the aggregate goes out as a look-back flag; warp 0 walks back 32 predecessors
+// per step until an inclusive prefix; pass 2 rescans with the prefix and writes the result. CTAs are
+// dispatched in index order, so a tile only ever waits on tiles whose CTAs have started.
 template <int OP>
 __global__ void __launch_bounds__(kScanThreads) scan_i32_kernel(const int32_t* __restrict__ x,
                                                                 int32_t* __restrict__ y, int64_t k,
                                                                 int64_t tiles_per_row, int exclusive, int reverse,
                                                                 const int32_t* carry_in, ScanHeader* hdr,
                                                                 uint64_t* flags, uint32_t epoch, uint64_t wait_ns,
-                                                                int withhold, int bulk) {
+                                                                int withhold) {
   extern __shared__ __align__(128) uint8_t smem[];
   int32_t* buf = reinterpret_cast<int32_t*>(smem);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kTileBytes);
   __shared__ int32_t s_warp_tot[kScanThreads / 32];
   __shared__ int32_t s_prefix;
   __shared__ int s_abort;
@@ -135,37 +135,13 @@ __global__ void __launch_bounds__(kScanThreads) scan_i32_kernel(const int32_t* _
   const int cnt = (int)((k - lo) < kScanTile ? (k - lo) : kScanTile);
   const int32_t* xr = x + row * k;
   int32_t* yr = y + row * k;
-  const int64_t pstart = reverse ? (k - lo - cnt) : lo;  // first physical element of the tile
   const int32_t id = ident<OP>();
 
-  // ---- bring the tile into shared memory ----
+  // ---- bring the tile into shared memory, in scan order (a reversed row is read back to front) ----
   if (threadIdx.x == 0) s_abort = 0;
-  if (bulk) {
-    if (threadIdx.x == 0) {
-      tc::mbar_init(bar, 1);
-      tc::mbar_fence_init();
-      const uint32_t bytes = (uint32_t)cnt * 4u;
-      tc::mbar_arrive_expect_tx(bar, bytes);
-      const char* src = reinterpret_cast<const char*>(xr + pstart);
-      for (uint32_t off = 0; off < bytes; off += 16384u)
-        tc::bulk_load(smem + off, src + off, (bytes - off) < 16384u ? (bytes - off) : 16384u, bar);
-    }
-    __syncthreads();
-    const bool ok = tc::mbar_wait(bar, 0, wait_ns, nullptr);
-    if (__syncthreads_or(!ok)) {
-      // the copy did not land in time: report, and let it land before this CTA's shared memory is released
-      if (threadIdx.x == 0) {
-        atomicOr(&hdr->error, 1u);
-        s_abort = 1;
-        tc::mbar_wait(bar, 0, wait_ns, nullptr);
-      }
-    }
-  } else {
-    // any alignment: element loads, stored in scan order (a reversed row is read back to front)
-    for (int e = threadIdx.x; e < cnt; e += kScanThreads) buf[e] = __ldg(xr + (reverse ? (k - 1 - (lo + e)) : (lo + e)));
-  }
+  for (int e = threadIdx.x; e < cnt; e += kScanThreads) buf[e] = __ldg(xr + (reverse ? (k - 1 - (lo + e)) : (lo + e)));
   __syncthreads();
-  const TileView<OP> tile{buf, cnt, bulk && reverse};
+  const TileView<OP> tile{buf, cnt};
 
   // ---- pass 1: fold the tile ----
   int32_t acc = id;
@@ -274,21 +250,435 @@ __global__ void __launch_bounds__(kScanThreads) scan_i32_kernel(const int32_t* _
   }
 
   // ---- write the tile back ----
-  if (bulk) {
-    tc::fence_proxy_async_smem();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      const uint32_t bytes = (uint32_t)cnt * 4u;
-      char* dst = reinterpret_cast<char*>(yr + pstart);
-      for (uint32_t off = 0; off < bytes; off += 16384u)
-        tc::bulk_store(dst + off, smem + off, (bytes - off) < 16384u ? (bytes - off) : 16384u);
-      tc::bulk_commit();
-      tc::bulk_wait_read();
-    }
-  } else {
-    __syncthreads();
-    for (int e = threadIdx.x; e < cnt; e += kScanThreads) yr[reverse ? (k - 1 - (lo + e)) : (lo + e)] = buf[e];
+  __syncthreads();
+  for (int e = threadIdx.x; e < cnt; e += kScanThreads) yr[reverse ? (k - 1 - (lo + e)) : (lo + e)] = buf[e];
+}
+
+// ===================================================================================================
+// Persistent form, for rows that are 16-byte aligned and whole 16-byte chunks long (the common case).
+//
+// One CTA per SM; CTA b scans the 8192-element tiles b, b + P, b + 2P, ... (P = grid size) in that order.
+//  * Copy warp: one thread keeps a ring of kQStages tiles loading into shared memory by bulk copies and sends
+//    each scanned tile back out with bulk stores, so HBM reads stay in flight while tiles are scanned.
+//  * Compute warps (512 threads): thread r owns the 4 consecutive 16-byte chunks 4r .. 4r+3 of a tile. It
+//    folds a tile as soon as it lands (pass 1: chunk sums, their prefixes in scan order, a warp scan, the
+//    tile aggregate, which is published at once as the tile's look-back flag) and rescans it (pass 2) once its
+//    prefix is known. Folding runs kQFold tiles ahead of rescanning. A thread visits its chunks in a rotated
+//    order, (i + (lane / 2)) mod 4, which spreads each 8-lane phase of a warp over all eight 16-byte bank
+//    groups, so every shared-memory access is conflict-free; chunk prefixes are rotated into scan order and
+//    back by a two-step barrel shift.
+//  * Look-back warp: computes the exclusive prefix of each of the CTA's tiles from the published aggregates
+//    alone. For tile t whose previous tile t - P (this CTA's) is in the same row,
+//        prefix(t) = prefix(t - P) + aggregate(t - P) + ... + aggregate(t - 1),
+//    P flags read in one batch (up to 5 per lane); otherwise it sums the row from its first tile. Every flag
+//    it reads is an aggregate, which depends only on its own tile's data: there is no chain of prefixes across
+//    CTAs, and this warp runs ahead of the rescans as far as the aggregates allow, so the round trips to L2
+//    overlap the scanning instead of stalling it.
+// Forward progress: every CTA is resident (one per SM, grid <= SMs); a tile's aggregate needs only its data,
+// and a stage is refilled only after its tile's rescan, whose prefix needs aggregates of smaller tiles only.
+// Aborts: a wait that runs out (or an aborted tile in a window) makes the CTA publish "aborted" for its
+// remaining tiles, stop loading, let the loads in flight land, and exit; the error word is set.
+constexpr int kQTile = 8192;                        // elements per tile
+constexpr int kQTileBytes = kQTile * 4;             // 32 KiB
+constexpr int kQStages = 6;
+constexpr int kQRowChunks = 4;                      // 16-byte chunks per compute thread
+constexpr int kQCompute = kQTile / (4 * kQRowChunks);  // 512 compute threads
+constexpr int kQCWarps = kQCompute / 32;            // 16
+constexpr int kQCopyWarp = kQCWarps, kQLookWarp = kQCWarps + 1;
+constexpr int kQThreads = kQCompute + 64;           // + copy warp + look-back warp
+constexpr int kQFold = 2;                           // tiles folded ahead of the rescan
+constexpr int kQRing = 4;                           // prefix and warp-total ring (>= kQFold + 2)
+constexpr int kQMaxWin = 5;                         // look-back flags per lane: grids of up to 160 CTAs
+constexpr int kQMaxGrid = 32 * kQMaxWin;
+constexpr size_t kQSmem = (size_t)kQStages * kQTileBytes + 256;
+static_assert(kQRing >= kQFold + 2, "warp-total ring");
+static_assert(kQStages >= kQFold + 2, "stages");
+
+// Barrier `id` over `n` threads that also returns whether any of them passed `v`.
+__device__ __forceinline__ bool named_bar_or(int id, int n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.or.pred p, %2, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
+// a[j] <- a[(j - k) mod 4] (rotate toward higher index by k), k in [0, 4), as two conditional steps.
+__device__ __forceinline__ void rot_up4(int32_t (&a)[4], int k) {
+#pragma unroll
+  for (int step = 1; step < 4; step <<= 1) {
+    const bool on = (k & step) != 0;
+    int32_t t[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) t[j] = on ? a[(j - step) & 3] : a[j];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) a[j] = t[j];
   }
+}
+// a[j] <- a[(j + k) mod 4], the inverse of rot_up4.
+__device__ __forceinline__ void rot_down4(int32_t (&a)[4], int k) {
+#pragma unroll
+  for (int step = 1; step < 4; step <<= 1) {
+    const bool on = (k & step) != 0;
+    int32_t t[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) t[j] = on ? a[(j + step) & 3] : a[j];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) a[j] = t[j];
+  }
+}
+
+// This CTA's j-th tile t = b + j*P as (row, tile within the row), advanced by additions.
+struct QCursor {
+  int64_t t, row, q;
+  __device__ __forceinline__ void init(int64_t t0, int64_t tpr) {
+    t = t0;
+    row = t0 / tpr;
+    q = t0 - row * tpr;
+  }
+  __device__ __forceinline__ void next(int64_t P, int64_t tpr) {
+    t += P;
+    q += P;
+    if (q >= tpr) {  // crossed into a later row (only when rows are shorter than P tiles, or at a row's end)
+      const int64_t dr = q / tpr;
+      row += dr;
+      q -= dr * tpr;
+    }
+  }
+};
+
+// What pass 1 leaves for pass 2 of one tile, per thread.
+struct QFold {
+  int32_t cp[kQRowChunks];  // slot i: exclusive prefix, within this thread's row, of chunk (i + R) mod 4
+  int32_t texcl;            // exclusive prefix of this thread's row within its warp
+};
+
+template <int OP, bool REV>
+__global__ void __launch_bounds__(kQThreads, 1)
+    scan_i32_persist_kernel(const int32_t* __restrict__ x, int32_t* __restrict__ y, int64_t k, int64_t tiles_per_row,
+                            int64_t n_tiles, int exclusive, const int32_t* carry_in, ScanHeader* hdr, uint64_t* flags,
+                            uint32_t epoch, uint64_t wait_ns, int withhold) {
+  constexpr bool reverse = REV;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)kQStages * kQTileBytes);  // [stages] data landed
+  uint64_t* done = full + kQStages;      // [stages] rescanned (one arrival per compute warp)
+  uint64_t* pfull = done + kQStages;     // [ring] prefix delivered (look-back lane 0)
+  uint64_t* pempty = pfull + kQRing;     // [ring] prefix consumed (one arrival per compute warp)
+  __shared__ int32_t s_wt[kQRing][kQCWarps];
+  __shared__ int32_t s_prefix[kQRing];
+  __shared__ int s_abort_mem;
+  volatile int* s_abort = &s_abort_mem;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t P = gridDim.x, b = blockIdx.x;
+  const int64_t n_mine = (n_tiles - b + P - 1) / P;  // >= 1: the grid is at most n_tiles
+  const int32_t id = ident<OP>();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kQStages; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&done[s], kQCWarps);
+    }
+    for (int s = 0; s < kQRing; ++s) {
+      tc::mbar_init(&pfull[s], 1);
+      tc::mbar_init(&pempty[s], kQCWarps);
+    }
+    *s_abort = 0;
+    tc::mbar_fence_init();
+  }
+  __syncthreads();
+
+  auto count_of = [&](const QCursor& c) {  // elements in the tile (the row's last tile may be short)
+    const int64_t lo = c.q * kQTile;
+    return (int)((k - lo) < kQTile ? (k - lo) : kQTile);
+  };
+  auto start_of = [&](const QCursor& c, int cnt) {  // first physical element of the tile
+    const int64_t lo = c.q * kQTile;
+    return c.row * k + (reverse ? (k - lo - cnt) : lo);
+  };
+  auto stage = [&](int64_t j) { return smem + (size_t)(j % kQStages) * kQTileBytes; };
+  auto sphase = [&](int64_t j) { return (uint32_t)((j / kQStages) & 1); };
+  auto rphase = [&](int64_t j) { return (uint32_t)((j / kQRing) & 1); };
+  // Marks this CTA's tiles from `from` on as aborted, so that no other CTA waits for them.
+  auto abort_from = [&](int64_t from) {
+    if (!*s_abort) atomicOr(&hdr->error, 1u);
+    *s_abort = 1;
+    for (int64_t jj = from; jj < n_mine; ++jj) st_relaxed_u64(flags + b + jj * P, make_flag(epoch, kFlagErr, 0));
+  };
+
+  if (warp == kQCopyWarp) {
+    // ---------------- copy warp ----------------
+    if (lane == 0) {
+      QCursor lc, sc;  // the next tile to load, the next tile to store
+      lc.init(b, tiles_per_row);
+      sc = lc;
+      auto store = [&](int64_t j) {
+        const int cnt = count_of(sc);
+        const uint32_t bytes = (uint32_t)cnt * 4u;
+        char* dst = reinterpret_cast<char*>(y + start_of(sc, cnt));
+        for (uint32_t off = 0; off < bytes; off += 16384u)
+          tc::bulk_store(dst + off, stage(j) + off, (bytes - off) < 16384u ? (bytes - off) : 16384u);
+        tc::bulk_commit();
+        sc.next(P, tiles_per_row);
+      };
+      int64_t issued = 0, stored = 0;
+      bool ok = true;
+      while (issued < n_mine && !*s_abort) {
+        const int64_t j = issued;
+        if (j >= kQStages) {  // the stage's previous tile must be rescanned and sent out first
+          const int64_t jo = j - kQStages;
+          if (!tc::mbar_wait(&done[jo % kQStages], sphase(jo), wait_ns, s_abort)) {
+            ok = false;
+            break;
+          }
+          store(jo);
+          stored = jo + 1;
+          tc::bulk_wait_read();  // the stage has been read out: it may be refilled
+        }
+        const int cnt = count_of(lc);
+        const uint32_t bytes = (uint32_t)cnt * 4u;
+        uint64_t* bar = &full[j % kQStages];
+        tc::mbar_arrive_expect_tx(bar, bytes);
+        const char* src = reinterpret_cast<const char*>(x + start_of(lc, cnt));
+        for (uint32_t off = 0; off < bytes; off += 16384u)
+          tc::bulk_load(stage(j) + off, src + off, (bytes - off) < 16384u ? (bytes - off) : 16384u, bar);
+        lc.next(P, tiles_per_row);
+        issued = j + 1;
+      }
+      for (int64_t jo = stored; ok && jo < issued && !*s_abort; ++jo) {
+        if (!tc::mbar_wait(&done[jo % kQStages], sphase(jo), wait_ns, s_abort)) {
+          ok = false;
+          break;
+        }
+        store(jo);
+      }
+      if (!ok && !*s_abort) abort_from(stored);
+      if (*s_abort) {
+        // loads still in flight must land before this CTA's shared memory is released
+        for (int64_t j = (issued > kQStages ? issued - kQStages : 0); j < issued; ++j)
+          tc::mbar_wait(&full[j % kQStages], sphase(j), wait_ns, nullptr);
+      }
+      asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    }
+    return;
+  }
+
+  if (warp == kQLookWarp) {
+    // ---------------- look-back warp ----------------
+    const int32_t cin = carry_in ? *carry_in : id;
+    int32_t pre_prev = id;
+    QCursor c;
+    c.init(b, tiles_per_row);
+    for (int64_t j = 0; j < n_mine; ++j, c.next(P, tiles_per_row)) {
+      int32_t pre = cin;
+      if (c.q != 0) {
+        const bool chain = j > 0 && c.q >= P;  // this CTA's previous tile is in the same row
+        const int m = (int)(chain ? P : c.q);  // aggregates to add: tiles t - m .. t - 1
+        const int32_t base = chain ? pre_prev : cin;
+        const uint64_t t0 = globaltimer_ns();
+        bool bad = false;
+        while (true) {
+          uint64_t f[kQMaxWin];
+#pragma unroll
+          for (int i = 0; i < kQMaxWin; ++i) {  // all loads first: one round trip
+            const int d = lane + 32 * i + 1;
+            f[i] = d <= m ? ld_relaxed_u64(flags + (c.t - d)) : 0;
+          }
+          bool ready = true, err = false;
+#pragma unroll
+          for (int i = 0; i < kQMaxWin; ++i) {
+            const int d = lane + 32 * i + 1;
+            if (d <= m) {
+              const uint32_t st = flag_status(f[i], epoch);
+              ready = ready && st == kFlagAgg;
+              err = err || st == kFlagErr;
+            }
+          }
+          if (__any_sync(0xffffffffu, err) || __shfl_sync(0xffffffffu, *s_abort, 0)) {
+            bad = true;
+            break;
+          }
+          if (__all_sync(0xffffffffu, ready)) {
+            int32_t s = id;
+#pragma unroll
+            for (int i = 0; i < kQMaxWin; ++i) {
+              const int d = lane + 32 * i + 1;
+              if (d <= m) s = comb<OP>(s, (int32_t)(uint32_t)f[i]);
+            }
+            pre = comb<OP>(base, warp_reduce<OP>(s));
+            break;
+          }
+          if (__shfl_sync(0xffffffffu, globaltimer_ns() - t0 > wait_ns, 0)) {
+            bad = true;
+            break;
+          }
+          __nanosleep(32);
+        }
+        if (bad) {
+          if (lane == 0) abort_from(j);
+          return;
+        }
+      }
+      pre_prev = pre;
+      if (lane == 0) {
+        if (j >= kQRing && !tc::mbar_wait(&pempty[j % kQRing], rphase(j - kQRing), wait_ns, s_abort)) {
+          abort_from(j);
+          return;
+        }
+        s_prefix[j % kQRing] = pre;
+        tc::mbar_arrive(&pfull[j % kQRing]);
+      }
+      __syncwarp();
+    }
+    return;
+  }
+
+  // ---------------- compute warps ----------------
+  const int r = threadIdx.x;      // owns logical chunks 4r .. 4r+3 of every tile
+  const int R = (lane >> 1) & 3;  // rotation of this thread's visiting order: lanes 2l and 2l+1 sit 64 bytes
+                                  // apart, so this spreads each 8-lane phase over all 8 bank groups
+  QCursor fc, rc;                 // the next tile to fold, the next tile to rescan
+  fc.init(b, tiles_per_row);
+  rc = fc;
+
+  // Loads this thread's chunks of tile j (visiting order); chunks past the tile's end read as the identity.
+  auto load_row = [&](int64_t j, int cnt, int32_t (&v)[kQRowChunks][4]) {
+    const int4* buf = reinterpret_cast<const int4*>(stage(j));
+    const int nch = cnt >> 2;  // whole 16-byte chunks (cnt % 4 == 0 here)
+#pragma unroll
+    for (int i = 0; i < kQRowChunks; ++i) {
+      const int g = kQRowChunks * r + ((i + R) & 3);
+      if (g < nch) {
+        const int4 c = buf[REV ? nch - 1 - g : g];
+        if (REV) { v[i][0] = c.w; v[i][1] = c.z; v[i][2] = c.y; v[i][3] = c.x; }
+        else { v[i][0] = c.x; v[i][1] = c.y; v[i][2] = c.z; v[i][3] = c.w; }
+      } else {
+        v[i][0] = v[i][1] = v[i][2] = v[i][3] = id;
+      }
+    }
+  };
+  // Pass 1 on loaded chunks: chunk prefixes within the row, the row's warp-exclusive prefix, the warp total.
+  auto fold_math = [&](int64_t j, const int32_t (&v)[kQRowChunks][4], QFold& st) {
+#pragma unroll
+    for (int i = 0; i < kQRowChunks; ++i) st.cp[i] = comb<OP>(comb<OP>(v[i][0], v[i][1]), comb<OP>(v[i][2], v[i][3]));
+    rot_up4(st.cp, R);  // cp[c] = sum of chunk c of the row
+    int32_t run = id;
+#pragma unroll
+    for (int c = 0; c < kQRowChunks; ++c) {
+      const int32_t s = st.cp[c];
+      st.cp[c] = run;
+      run = comb<OP>(run, s);
+    }
+    rot_down4(st.cp, R);  // back to visiting order
+    const int32_t inc = warp_incl_scan<OP>(run, lane);
+    st.texcl = __shfl_up_sync(0xffffffffu, inc, 1);
+    if (lane == 0) st.texcl = id;
+    if (lane == 31) s_wt[j % kQRing][warp] = inc;
+  };
+  // After the barrier that follows fold_math: the tile's aggregate goes out as its look-back flag.
+  auto publish = [&](int64_t j, int64_t t) {
+    if (threadIdx.x == 0) {
+      int32_t agg = id;
+#pragma unroll
+      for (int w = 0; w < kQCWarps; ++w) agg = comb<OP>(agg, s_wt[j % kQRing][w]);
+      if (!(withhold && t == 0)) st_relaxed_u64(flags + t, make_flag(epoch, kFlagAgg, agg));
+    }
+  };
+
+  QFold A, B, C;
+  int64_t j = 0;
+  bool ok = true;
+  // prologue: fold the first kQFold tiles
+  for (int64_t jf = 0; jf < kQFold && jf < n_mine; ++jf) {
+    const int cnt = count_of(fc);
+    const int64_t t = fc.t;
+    fc.next(P, tiles_per_row);
+    const bool landed = tc::mbar_wait(&full[jf % kQStages], sphase(jf), wait_ns, s_abort);
+    int32_t v[kQRowChunks][4];
+    load_row(jf, cnt, v);
+    fold_math(jf, v, jf == 0 ? A : B);
+    if (named_bar_or(1, kQCompute, !landed || *s_abort)) {
+      ok = false;
+      break;
+    }
+    publish(jf, t);
+  }
+  // Steady state: iteration j folds tile j + kQFold (publishing its aggregate as early as possible), then
+  // rescans tile j. One barrier per iteration; it also settles whether any warp's wait for the previous
+  // prefix ran out (such a warp releases nothing and has flagged the abort).
+  bool good_prev = true;
+  for (; ok && j < n_mine; ++j) {
+    const bool fold_next = j + kQFold < n_mine;
+    const int64_t jf = j + kQFold;
+    bool good_f = true;
+    int64_t ft = 0;
+    if (fold_next) {
+      const int fcnt = count_of(fc);
+      ft = fc.t;
+      fc.next(P, tiles_per_row);
+      good_f = tc::mbar_wait(&full[jf % kQStages], sphase(jf), wait_ns, s_abort);
+      int32_t fv[kQRowChunks][4];
+      load_row(jf, fcnt, fv);
+      fold_math(jf, fv, C);
+    }
+    if (named_bar_or(1, kQCompute, !good_f || !good_prev || *s_abort)) {
+      ok = false;
+      break;
+    }
+    if (fold_next) publish(jf, ft);
+
+    // pass 2 of tile j
+    const int rcnt = count_of(rc);
+    rc.next(P, tiles_per_row);
+    const bool gr = tc::mbar_wait(&pfull[j % kQRing], rphase(j), wait_ns, s_abort);
+    int32_t rv[kQRowChunks][4];
+    load_row(j, rcnt, rv);
+    const int32_t pre = s_prefix[j % kQRing];
+    int32_t wpre = id;
+#pragma unroll
+    for (int w = 0; w < kQCWarps; ++w)
+      if (w < warp) wpre = comb<OP>(wpre, s_wt[j % kQRing][w]);
+    const int32_t base = comb<OP>(comb<OP>(pre, wpre), A.texcl);
+    int4* wbuf = reinterpret_cast<int4*>(stage(j));
+    const int nch = rcnt >> 2;
+#pragma unroll
+    for (int i = 0; i < kQRowChunks; ++i) {
+      const int g = kQRowChunks * r + ((i + R) & 3);
+      const int32_t p = comb<OP>(base, A.cp[i]);
+      int32_t o[4];
+      if (exclusive) {
+        o[0] = p;
+        o[1] = comb<OP>(p, rv[i][0]);
+        o[2] = comb<OP>(o[1], rv[i][1]);
+        o[3] = comb<OP>(o[2], rv[i][2]);
+      } else {
+        o[0] = comb<OP>(p, rv[i][0]);
+        o[1] = comb<OP>(o[0], rv[i][1]);
+        o[2] = comb<OP>(o[1], rv[i][2]);
+        o[3] = comb<OP>(o[2], rv[i][3]);
+      }
+      if (g < nch) wbuf[REV ? nch - 1 - g : g] = REV ? make_int4(o[3], o[2], o[1], o[0]) : make_int4(o[0], o[1], o[2], o[3]);
+    }
+    tc::fence_proxy_async_smem();  // this thread's writes are visible to the bulk store
+    const bool wgood = __all_sync(0xffffffffu, gr);
+    if (lane == 0) {
+      if (wgood) {  // one arrival per warp
+        tc::mbar_arrive(&done[j % kQStages]);
+        tc::mbar_arrive(&pempty[j % kQRing]);
+      } else {
+        abort_from(j);  // stops the copy and look-back warps; the next barrier stops the compute warps
+      }
+    }
+    good_prev = wgood;
+    A = B;
+    B = C;
+  }
+  if (!ok && threadIdx.x == 0) abort_from(j);
 }
 
 static std::atomic<uint32_t> g_epoch{0};
@@ -299,14 +689,15 @@ using namespace up;
 
 extern "C" size_t up_sm100_scan_workspace_bytes(int64_t rows, int64_t k) {
   if (rows <= 0 || k <= 0) return sizeof(ScanHeader);
-  const int64_t tiles = rows * ((k + kScanTile - 1) / kScanTile);
+  // one flag per tile of the persistent form (8192 elements); the one-tile-per-CTA form needs fewer
+  const int64_t tiles = rows * ((k + kQTile - 1) / kQTile);
   return sizeof(ScanHeader) + (size_t)tiles * sizeof(uint64_t);
 }
 
 template <int OP>
 static cudaError_t launch_scan(unsigned grid, cudaStream_t s, const int32_t* x, int32_t* y, int64_t k, int64_t tpr,
                                int exclusive, int reverse, const int32_t* carry_in, ScanHeader* hdr, uint64_t* flags,
-                               uint32_t epoch, uint64_t wns, int withhold, int bulk) {
+                               uint32_t epoch, uint64_t wns, int withhold) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -321,8 +712,43 @@ static cudaError_t launch_scan(unsigned grid, cudaStream_t s, const int32_t* x, 
     }
   }
   scan_i32_kernel<OP><<<grid, kScanThreads, kScanSmem, s>>>(x, y, k, tpr, exclusive, reverse, carry_in, hdr, flags,
-                                                            epoch, wns, withhold, bulk);
+                                                            epoch, wns, withhold);
   return cudaGetLastError();
+}
+
+template <int OP, bool REV>
+static cudaError_t launch_scan_persist_dir(unsigned grid, cudaStream_t s, const int32_t* x, int32_t* y, int64_t k,
+                                           int64_t tpr, int64_t tiles, int exclusive, const int32_t* carry_in,
+                                           ScanHeader* hdr, uint64_t* flags, uint32_t epoch, uint64_t wns,
+                                           int withhold) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static std::mutex mu;
+  static bool attr_set[64] = {false};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+      e = cudaFuncSetAttribute(scan_i32_persist_kernel<OP, REV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)kQSmem);
+      if (e != cudaSuccess) return e;
+      if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+  }
+  scan_i32_persist_kernel<OP, REV><<<grid, kQThreads, kQSmem, s>>>(x, y, k, tpr, tiles, exclusive, carry_in, hdr,
+                                                                   flags, epoch, wns, withhold);
+  return cudaGetLastError();
+}
+
+template <int OP>
+static cudaError_t launch_scan_persist(unsigned grid, cudaStream_t s, const int32_t* x, int32_t* y, int64_t k,
+                                       int64_t tpr, int64_t tiles, int exclusive, int reverse,
+                                       const int32_t* carry_in, ScanHeader* hdr, uint64_t* flags, uint32_t epoch,
+                                       uint64_t wns, int withhold) {
+  return reverse ? launch_scan_persist_dir<OP, true>(grid, s, x, y, k, tpr, tiles, exclusive, carry_in, hdr, flags,
+                                                     epoch, wns, withhold)
+                 : launch_scan_persist_dir<OP, false>(grid, s, x, y, k, tpr, tiles, exclusive, carry_in, hdr, flags,
+                                                      epoch, wns, withhold);
 }
 
 extern "C" int up_sm100_scan_i32(const int32_t* x, int32_t* y, int64_t rows, int64_t k, int op, int exclusive,
@@ -335,7 +761,7 @@ extern "C" int up_sm100_scan_i32(const int32_t* x, int32_t* y, int64_t rows, int
   UP_CHECK_ARG(aligned(workspace, 64));
   const int64_t tpr = (k + kScanTile - 1) / kScanTile;
   const int64_t tiles = rows * tpr;
-  if (tiles >= (int64_t)0x7fffffff) return UP_ERR_UNSUPPORTED;
+  if (rows * ((k + kQTile - 1) / kQTile) >= (int64_t)0x7fffffff) return UP_ERR_UNSUPPORTED;
   if (workspace_bytes < up_sm100_scan_workspace_bytes(rows, k)) return UP_ERR_INVALID;
   auto* hdr = static_cast<ScanHeader*>(workspace);
   auto* flags = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + sizeof(ScanHeader));
@@ -346,15 +772,33 @@ extern "C" int up_sm100_scan_i32(const int32_t* x, int32_t* y, int64_t rows, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const uint64_t wns = wait_limit_ns();
   cudaError_t e;
+  if (bulk) {
+    const int64_t qtpr = (k + kQTile - 1) / kQTile, qtiles = rows * qtpr;
+    int64_t grid = sm_count();
+    if (grid > kQMaxGrid) grid = kQMaxGrid;
+    if (grid > qtiles) grid = qtiles;
+    const unsigned g = (unsigned)grid;
+    if (op == UP_OP_SUM)
+      e = launch_scan_persist<UP_OP_SUM>(g, s, x, y, k, qtpr, qtiles, exclusive, reverse, carry_in, hdr, flags, epoch,
+                                         wns, withhold);
+    else if (op == UP_OP_MAX)
+      e = launch_scan_persist<UP_OP_MAX>(g, s, x, y, k, qtpr, qtiles, exclusive, reverse, carry_in, hdr, flags, epoch,
+                                         wns, withhold);
+    else
+      e = launch_scan_persist<UP_OP_MIN>(g, s, x, y, k, qtpr, qtiles, exclusive, reverse, carry_in, hdr, flags, epoch,
+                                         wns, withhold);
+    note_launch();
+    return cuda_status(e);
+  }
   if (op == UP_OP_SUM)
     e = launch_scan<UP_OP_SUM>((unsigned)tiles, s, x, y, k, tpr, exclusive, reverse, carry_in, hdr, flags, epoch, wns,
-                               withhold, bulk);
+                               withhold);
   else if (op == UP_OP_MAX)
     e = launch_scan<UP_OP_MAX>((unsigned)tiles, s, x, y, k, tpr, exclusive, reverse, carry_in, hdr, flags, epoch, wns,
-                               withhold, bulk);
+                               withhold);
   else
     e = launch_scan<UP_OP_MIN>((unsigned)tiles, s, x, y, k, tpr, exclusive, reverse, carry_in, hdr, flags, epoch, wns,
-                               withhold, bulk);
+                               withhold);
   note_launch();
   return cuda_status(e);
 }
@@ -385,7 +829,7 @@ extern "C" int up_sm100_workspace_status(void* workspace, void* stream) {
 // so they never need clearing. Every call on a device uses the same array: calls that overlap in time
 // race, through concurrent streams or host threads, and must be serialized by the caller.
 namespace up {
-constexpr int64_t kNoAllocMaxTiles = 16384;  // rows x ceil(k / 16384) tiles, e.g. one row of 2^28 elements
+constexpr int64_t kNoAllocMaxTiles = 32768;  // rows x ceil(k / 8192) tiles, e.g. one row of 2^28 elements
 static __device__ __align__(256) uint64_t g_noalloc_scratch[sizeof(ScanHeader) / 8 + kNoAllocMaxTiles];
 static std::mutex g_noalloc_mu;
 static void* g_noalloc_ptr[64] = {};
@@ -410,10 +854,10 @@ extern "C" int up_sm100_scan_i32_noalloc(const int32_t* x, int32_t* y, int64_t r
   UP_CHECK_ARG(rows >= 0 && k >= 0);
   if (op != UP_OP_SUM && op != UP_OP_MAX && op != UP_OP_MIN) return UP_ERR_UNSUPPORTED;
   if (rows == 0 || k == 0) return UP_OK;
-  const int64_t tpr = (k + kScanTile - 1) / kScanTile;
+  const int64_t tpr = (k + kQTile - 1) / kQTile;
   if (rows > kNoAllocMaxTiles || rows * tpr > kNoAllocMaxTiles)
     return fail_with(UP_ERR_UNSUPPORTED,
-                     "up_sm100_scan_i32_noalloc: rows * ceil(k / 16384) exceeds the built-in scratch's 16384 "
+                     "up_sm100_scan_i32_noalloc: rows * ceil(k / 8192) exceeds the built-in scratch's 32768 "
                      "tiles; use up_sm100_scan_i32 with a workspace");
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
