@@ -247,7 +247,7 @@ def bench_lifts(ctx, K, W, hbm, bf16):
     y = torch.empty_like(x)
     for name, op, ex in (("scan_excl_add_i32_2p28", "sum", True), ("scan_incl_max_i32_2p28", "max", False)):
         ms, _, _ = ctx.timed(lambda i, kin, op=op, ex=ex: ops.scan(x, op, ex, out=y), K, W)
-        record(name, wl.scan_bytes(), ms, "scan_i32_kernel", 1)
+        record(name, wl.scan_bytes(), ms, "scan_i32_persist_kernel", 1)
     ops.check_workspace("scan", ctx.dev)
     del x, y
 
@@ -314,6 +314,14 @@ def cpu_scan_baseline():
             "sample": f"full config: 2^28 int32 inclusive add-scan, serial C restatement of eval_scan, {reps} passes"}
 
 
+def scan_config(world):
+    """The headline workload's `config`, shared by both arms of the bench."""
+    return {"workload": "configs[1]: inclusive add-scan over 2^28 int32 per GPU (1 GiB in, 1 GiB out)"
+                        + ("; shards combined by an all-gather of per-GPU totals" if world > 1 else ""),
+            "lift": "scan_incl_add_i32", "elements_per_gpu": SCAN_N,
+            "l2": "input (1 GiB per GPU) larger than the 126 MB L2; no flush", "parallelism": f"sharded x{world}"}
+
+
 def run_reference(args):
     """The reference's CPU implementation of the path on all host cores (OpenMP chunked scan)."""
     import numpy as np
@@ -340,8 +348,7 @@ def run_reference(args):
     line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int32", "data": "synthetic (seeded, uniform [0,16))",
-            "config": {"workload": "configs[1]: inclusive add-scan over 2^28 int32 (1 GiB in, 1 GiB out)",
-                       "lift": "scan_incl_add_i32", "elements": SCAN_N},
+            "config": scan_config(world),
             "cpu_baseline": {"value": round(gbs, 2), "unit": "GB/s", "cores": threads, "kind": "port",
                              "sample": "full config per step: OpenMP chunked scan (chunk totals, carry, rescan) "
                                        "restating eval_scan (oracle/plan_window.rs:10-238); the reference is Rust "
@@ -467,19 +474,15 @@ def main():
     clocks = clk.stop()
 
     cpu = cpu_scan_baseline() if (ctx.rank == 0 and ctx.world == 1) else None
-    traffic = ncu_traffic("scan_i32_kernel_incl_add.md")
+    traffic = ncu_traffic("scan_i32_persist_kernel_incl_add.md")
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": ctx.world, "steps": K, "warmup": W,
         "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int32", "data": "synthetic (seeded torch generator, uniform [0,16))",
-        "config": {"workload": "configs[1]: inclusive add-scan over 2^28 int32 per GPU (1 GiB in, 1 GiB out), "
-                               "single-pass decoupled look-back" + (
-                                   "; shards combined by an NCCL all-gather of per-GPU totals" if ctx.world > 1 else ""),
-                   "lift": "scan_incl_add_i32", "elements_per_gpu": SCAN_N, "l2": "input (1 GiB per GPU) larger than the 126 MB L2; no flush",
-                   "parallelism": f"sharded x{ctx.world}"},
+        "config": scan_config(ctx.world),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": traffic, "peak_source": peak_src,
-                     "kernel": "scan_i32_kernel<SUM>", "algorithmic_bytes_per_launch": nbytes,
+                     "kernel": "scan_i32_persist_kernel<SUM>", "algorithmic_bytes_per_launch": nbytes,
                      "kernel_ms": round(kms, 4)},
         "e2e": e2e,
         "gpu_launches": launches,

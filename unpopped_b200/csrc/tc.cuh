@@ -48,13 +48,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity, ui
 
 // Waits for the phase with the given parity to complete, at most `limit_ns`; false when it ran out
 // or when `*abort` became nonzero (another role of the CTA gave up).
+// The clock and the abort word are looked at once every 16 attempts: a waiting thread then spends its issue
+// slots on the barrier test alone, not on reading %globaltimer, which shares a pipe with other work.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns, volatile int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  while (true) {
+  for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (abort && *abort) return false;
-    if (globaltimer_ns() - t0 > limit_ns) return false;
+    if ((it & 15u) == 0) {
+      if (abort && *abort) return false;
+      if (globaltimer_ns() - t0 > limit_ns) return false;
+    }
   }
 }
 
