@@ -10,27 +10,26 @@
 // Design (swap-AB: the weight rows are the MMA's M = 128, the <= 16 activation rows its N = 16):
 //  * A unit of work is one k-block (128 k) of one 128-row tile of W. The N/128 x K/128 units are split
 //    evenly over one persistent CTA per SM (stream-K), so every SM streams the same share of W.
-//  * Data movement: every dequant thread keeps its own copy pipeline, kPrefetch units deep, of plain
-//    asynchronous 16-byte copies (cp.async): the 32 bytes of its W row for the unit, one 16-byte piece of
-//    the unit's activation tile (written straight into the 128-byte-swizzled layout the MMA reads), and the
-//    16-byte chunk holding its row's group scale. The tensor-memory-access (TMA) unit is not used: its
-//    fixed cost of a few hundred cycles per copy would cap this kernel far below the HBM bound for tiles
-//    this narrow.
-//  * warps 4..11 (dequant): each thread owns one W row (its TMEM lane) and half of the k-block. It turns
-//    the nibbles into exact bf16 (one prmt, one lop3 and one bf16x2 subtract per pair) and stores them into
-//    tensor memory (tcgen05.st), where they are the MMA's A operand; dequantized weights never touch shared
-//    memory.
-//  * warps 0..3 (MMA issuers): a single thread issues only about one tcgen05.mma per ~100 cycles, much
-//    slower than an M=128, N=16, K=16 MMA executes, so four warps issue in parallel: warp g runs k-steps
-//    2g and 2g+1 of every unit into its own TMEM accumulator.
-//  * the dequant warps, two units behind, read the unit's four accumulators (tcgen05.ld), add them, scale
-//    by scale[n][k-block] in f32 and accumulate in registers. A tile finished inside one CTA is written as
-//    bf16; a tile split between CTAs writes f32 partials, and whichever CTA finishes it last (an atomic
-//    count) sums them in CTA order, writes bf16 and clears the partials — no CTA ever waits on another.
+//  * warps 0..15 (dequant): warp w owns TMEM lane quarter w % 4 and k-quarter w / 4, so thread (w, lane)
+//    owns row 32 (w % 4) + lane of the tile and 32 k of every unit: 16 bytes of W, which it loads straight
+//    into registers kPrefetch units ahead of use (no shared-memory round trip). It turns the nibbles into
+//    exact bf16 (one prmt, one lop3 and one bf16x2 subtract per pair) and stores them into tensor memory
+//    (tcgen05.st), where they are the MMA's A operand.
+//  * warps 16..19 (MMA issuers): a single thread issues only about one tcgen05.mma per ~100 cycles, so four
+//    warps issue in parallel: issuer g runs the two k-steps of k-quarter g of every unit into its own TMEM
+//    accumulator, and waits only for the four dequant warps of that quarter.
+//  * warp 24 (activation loader): one thread brings each unit's [16 x 128] activation tile into a ring of
+//    shared-memory stages with two TMA boxes, 128-byte swizzled as the MMA reads it; rows past M read as 0.
+//  * warps 20..23 (epilogue): read the unit's four accumulators (tcgen05.ld), add them, scale by
+//    scale[n][k-block] in f32 and accumulate in registers. A tile finished inside one CTA is written as bf16;
+//    a tile split between CTAs writes f32 partials, and whichever CTA finishes it last (an atomic count)
+//    sums them in CTA order, writes bf16 and clears the partials — no CTA ever waits on another.
 // Every mbarrier wait is bounded; a wait that runs out sets the workspace error word and the CTA unwinds.
 #include "common.cuh"
 #include "tc.cuh"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -39,28 +38,26 @@
 namespace up {
 namespace w4 {
 
-constexpr int kTileN = 128;                    // W rows per tile = MMA M
-constexpr int kMmaN = 16;                      // activation rows = MMA N
-constexpr int kKB = 128;                       // k per unit
-constexpr int kDqThreads = 256;                // 8 dequant warps: 128 rows x 2 k-halves
-constexpr int kWBytes = kTileN * kKB / 2;      // 8 KiB of int4 per unit: [2 chunks][256 threads][16 B]
-constexpr int kXBytes = kMmaN * kKB * 2;       // 4 KiB of bf16 per unit, 128-byte swizzled (2 atoms per 64 k)
-constexpr int kSBytes = kDqThreads * 16;       // 4 KiB: each thread's 16-byte chunk of scales
-constexpr int kStageBytes = kXBytes + kWBytes + kSBytes;  // 16 KiB; x first (1024-aligned)
-constexpr int kPrefetch = 4;                   // units a thread's copies run ahead
-constexpr int kStages = kPrefetch + 3;         // a stage is refilled 3 units after its MMAs were issued
-constexpr int kRing = 4;                       // units in flight between dequant, MMA and epilogue
-constexpr int kIssuers = 4;                    // MMA-issuing warps
+constexpr int kTileN = 128;                      // W rows per tile = MMA M
+constexpr int kMmaN = 16;                        // activation rows = MMA N
+constexpr int kKB = 128;                         // k per unit
+constexpr int kDqWarps = 16;                     // warps 0..15
+constexpr int kIssuers = 4;                      // warps 16..19
+constexpr int kEpiWarps = 4;                     // warps 20..23
+constexpr int kIss0 = kDqWarps, kEpi0 = kIss0 + kIssuers, kXWarp = kEpi0 + kEpiWarps;
+constexpr int kThreads = 32 * (kXWarp + 1);      // 800
+constexpr int kPrefetch = 4;                     // units of W a dequant thread has in flight
+constexpr int kScaleAhead = 4;                   // units an epilogue thread's scale loads run ahead
+constexpr int kXBytes = kMmaN * kKB * 2;         // 4 KiB of bf16 per unit: two 128-byte-swizzled boxes of 64 k
+constexpr int kXStages = 8;
+constexpr int kRing = 4;                         // units in flight between dequant, MMA and epilogue
 constexpr int kTmemCols = 512;
-constexpr int kACol0 = 0;                      // A (dequantized W) stages: kRing x 64 columns
-constexpr int kDCol0 = kRing * 64;             // accumulators: kRing units x kIssuers x 16 columns
-constexpr int kLag = 2;                        // epilogue trails the dequant by this many units
-constexpr int kDq0 = kIssuers;                 // first dequant warp
-constexpr int kThreads = 32 * kIssuers + kDqThreads;  // 384
+constexpr int kACol0 = 0;                        // A (dequantized W): kRing x 64 columns
+constexpr int kDCol0 = kRing * 64;               // accumulators: kRing units x kIssuers x 16 columns
 constexpr int kBarBytes = 512;
-constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + (size_t)kStages * kStageBytes + kBarBytes;
-static_assert(kStages * kStageBytes + kBarBytes + 1024 <= 227 * 1024, "shared memory");
-static_assert(kStages - kPrefetch >= 3 && kRing >= kLag + 2, "pipeline distances");
+constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + (size_t)kXStages * kXBytes + kBarBytes;
+static_assert(kEpi0 % 4 == 0, "epilogue warp e reads TMEM lane quarter e % 4");
+static_assert(kDCol0 + kRing * kIssuers * kMmaN <= kTmemCols, "tensor memory");
 
 struct WsHeader {
   uint32_t ticket, done, epoch, error;  // same layout as the scan workspace: `error` at byte 12
@@ -92,7 +89,7 @@ __device__ __forceinline__ uint32_t nib2_to_bf16x2(uint32_t q, uint32_t q4, int 
 }
 
 // Position of a unit (tile t, k-block kb, scale-group index gi = kb*128/group) advanced one unit at a time
-// with additions only: 64-bit division and modulo are emulated in software and would dominate the loop.
+// with additions only: 64-bit division and modulo are emulated in software and would dominate the loops.
 struct UnitCursor {
   int t, kb, sub, gi;  // sub = kb % (group / 128)
   __device__ __forceinline__ void init(int64_t u, int64_t G, int kpg) {
@@ -114,30 +111,18 @@ struct UnitCursor {
   }
 };
 
-// 16-byte asynchronous copy global -> shared; `valid` == false fills zeros without reading the source.
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(tc::smem_u32(dst)), "l"(src),
-               "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-// kScaleChunk: K/group % 8 == 0 and the scales are 16-byte aligned, so each row's scales are whole 16-byte
-// chunks and every thread copies the chunk holding its scale; otherwise each thread reads its scale with a
-// plain load.
-template <bool kScaleChunk>
 __global__ void __launch_bounds__(kThreads, 1)
-    w4a16_kernel(const uint8_t* __restrict__ w, const __half* __restrict__ scale, const uint16_t* __restrict__ x,
-                 uint16_t* __restrict__ out, int M, int64_t N, int64_t K, int64_t group, int64_t U, int64_t G,
-                 int64_t S_max, WsHeader* hdr, uint32_t* counters, float* partials, uint64_t wait_ns) {
+    w4a16_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ w,
+                 const __half* __restrict__ scale, uint16_t* __restrict__ out, int M, int64_t N, int64_t K,
+                 int64_t group, int64_t U, int64_t G, int64_t S_max, WsHeader* hdr, uint32_t* counters,
+                 float* partials, uint64_t wait_ns) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* x_ready = reinterpret_cast<uint64_t*>(smem + (size_t)kStages * kStageBytes);  // [kStages]: 256
-  uint64_t* a_full = x_ready + kStages;        // [kRing][2]: the A half h of a unit is in TMEM (128 threads)
-  uint64_t* mma_done = a_full + 2 * kRing;     // [kRing]: every issuer's MMAs of the unit completed
-  uint64_t* d_empty = mma_done + kRing;        // [kRing]: the epilogue has read the unit's accumulators
+  uint8_t* xs = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* x_full = reinterpret_cast<uint64_t*>(xs + (size_t)kXStages * kXBytes);  // [kXStages]: TMA landed
+  uint64_t* x_empty = x_full + kXStages;        // [kXStages]: the stage's MMAs completed (4 issuer commits)
+  uint64_t* a_full = x_empty + kXStages;        // [kRing][4]: k-quarter q of the unit's A is in TMEM (4 warps)
+  uint64_t* mma_done = a_full + 4 * kRing;      // [kRing]: every issuer's MMAs of the unit completed
+  uint64_t* d_empty = mma_done + kRing;         // [kRing]: the epilogue has read the unit's accumulators
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + kRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -145,14 +130,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t P = gridDim.x;
   const int64_t lo = ((int64_t)blockIdx.x * U) / P, hi = (((int64_t)blockIdx.x + 1) * U) / P;
   const int64_t n_units = hi - lo;
+  const int Gi = (int)G, kpg = (int)(group / kKB);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) tc::mbar_init(&x_ready[s], kDqThreads);
+    for (int s = 0; s < kXStages; ++s) {
+      tc::mbar_init(&x_full[s], 1);
+      tc::mbar_init(&x_empty[s], kIssuers);
+    }
     for (int a = 0; a < kRing; ++a) {
-      tc::mbar_init(&a_full[2 * a], kDqThreads / 2);
-      tc::mbar_init(&a_full[2 * a + 1], kDqThreads / 2);
+      for (int q = 0; q < 4; ++q) tc::mbar_init(&a_full[4 * a + q], 4);
       tc::mbar_init(&mma_done[a], kIssuers);
-      tc::mbar_init(&d_empty[a], kDqThreads);
+      tc::mbar_init(&d_empty[a], kEpiWarps);
     }
     *abort_flag = 0;
     tc::mbar_fence_init();
@@ -171,31 +159,81 @@ __global__ void __launch_bounds__(kThreads, 1)
     atomicOr(&hdr->error, 1u);
   };
 
-  if (warp < kIssuers) {
-    // ---------------- MMA issuers: warp g issues k-steps 2g, 2g+1 of every unit ----------------
-    const int g = warp;
+  if (warp < kDqWarps) {
+    // ---------------- dequant: row 32 (warp % 4) + lane, k-quarter warp / 4 ----------------
+    const int lq = warp & 3, kq = warp >> 2;
+    const int r = lq * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(lq * 32) << 16;
+    const int64_t wrow = K / 2;
+    UnitCursor cl;
+    cl.init(lo, G, kpg);
+    auto load_w = [&]() {  // this thread's 16 bytes of the unit at cl, then advance cl
+      const int64_t n = (int64_t)cl.t * kTileN + r;
+      const uint4 v = n < N ? ld_nc_na_v4(w + n * wrow + (int64_t)cl.kb * (kKB / 2) + kq * 16) : make_uint4(0, 0, 0, 0);
+      cl.next(Gi, kpg);
+      return v;
+    };
+    uint4 wq[kPrefetch];
+#pragma unroll
+    for (int u = 0; u < kPrefetch; ++u) wq[u] = u < n_units ? load_w() : make_uint4(0, 0, 0, 0);
+    bool ok = true;
+    for (int64_t i0 = 0; ok && i0 < n_units; i0 += kPrefetch) {
+#pragma unroll
+      for (int u = 0; u < kPrefetch; ++u) {
+        const int64_t i = i0 + u;
+        if (i >= n_units) break;
+        const uint4 cur = wq[u];
+        if (i + kPrefetch < n_units) wq[u] = load_w();
+        const int a = (int)(i % kRing);
+        const uint32_t aph = (uint32_t)((i / kRing) & 1);
+        // the A stage is free once the unit kRing earlier has been multiplied
+        const bool good = tc::mbar_wait(&mma_done[a], aph ^ 1u, wait_ns, abort_flag);
+        if (!__all_sync(0xffffffffu, good)) {  // warp-uniform: the tcgen05 ops below are .sync.aligned
+          give_up();
+          ok = false;
+          break;
+        }
+        uint32_t regs[16];
+        const uint32_t wd[4] = {cur.x, cur.y, cur.z, cur.w};
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+          const uint32_t q4 = wd[wi] >> 4;
+#pragma unroll
+          for (int p = 0; p < 4; ++p) regs[4 * wi + p] = nib2_to_bf16x2(wd[wi], q4, p);
+        }
+        tc::st_32x32b_x16(tmem + lane_addr + kACol0 + a * 64 + 16 * kq, regs);
+        tc::wait_st();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&a_full[4 * a + kq]);
+      }
+    }
+  } else if (warp < kEpi0) {
+    // ---------------- MMA issuers: issuer g runs k-steps 2g, 2g+1 (k-quarter g) of every unit ----------------
+    const int g = warp - kIss0;
     if (lane == 0) {
       constexpr uint32_t idesc = tc::idesc_bf16_f32(kTileN, kMmaN);
       int64_t issued = 0;
       for (int64_t i = 0; i < n_units; ++i) {
-        const int s = (int)(i % kStages), a = (int)(i % kRing);
-        const uint32_t ph = (uint32_t)((i / kStages) & 1), rph = (uint32_t)((i / kRing) & 1);
-        if (!tc::mbar_wait(&x_ready[s], ph, wait_ns, abort_flag) ||
-            !tc::mbar_wait(&a_full[2 * a + (g >> 1)], rph, wait_ns, abort_flag) ||
+        const int a = (int)(i % kRing), s = (int)(i % kXStages);
+        const uint32_t rph = (uint32_t)((i / kRing) & 1), xph = (uint32_t)((i / kXStages) & 1);
+        if (!tc::mbar_wait(&a_full[4 * a + g], rph, wait_ns, abort_flag) ||
+            !tc::mbar_wait(&x_full[s], xph, wait_ns, abort_flag) ||
             !tc::mbar_wait(&d_empty[a], rph ^ 1u, wait_ns, abort_flag)) {
           give_up();
           break;
         }
         tc::fence_after_sync();
-        const uint32_t xaddr = tc::smem_u32(smem + (size_t)s * kStageBytes);
+        const uint32_t xaddr = tc::smem_u32(xs + (size_t)s * kXBytes);
 #pragma unroll
         for (int jj = 0; jj < 2; ++jj) {
-          const int j = 2 * g + jj;
+          const int j = 2 * g + jj;  // k-step: 16 k = 32 bytes of a 128-byte swizzle atom row
           const uint64_t bdesc = tc::sdesc_kmajor_sw128(xaddr + (uint32_t)((j >> 2) * 2048 + (j & 3) * 32));
           tc::mma_ts_bf16(tmem + kDCol0 + a * (16 * kIssuers) + g * 16, tmem + kACol0 + a * 64 + j * 8, bdesc, idesc,
                           jj > 0 ? 1u : 0u);
         }
         tc::commit(&mma_done[a]);
+        tc::commit(&x_empty[s]);
         issued = i + 1;
       }
       // Unwinding after an abort: the MMAs already issued must finish before TMEM is released.
@@ -204,179 +242,137 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::mbar_wait(&mma_done[i % kRing], (uint32_t)((i / kRing) & 1), wait_ns, nullptr);
       }
     }
-  } else {
-    // ---------------- dequant + epilogue ----------------
-    const int dw = warp - kDq0;
-    const int q = warp & 3;         // TMEM lane quarter this warp may access
-    const int h = dw >> 2;          // k half (dequant) and m half (epilogue)
-    const int r = q * 32 + lane;    // row of the tile = TMEM lane
-    const int slot = dw * 32 + lane;
-    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+  } else if (warp < kXWarp) {
+    // ---------------- epilogue: row 32 (warp % 4) + lane, all 16 activation rows ----------------
+    const int lq = warp & 3;
+    const int r = lq * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(lq * 32) << 16;
     const int64_t gpr = K / group;  // scales per row
-    // this thread's piece of every activation tile: row xm, 16-byte chunk xc of the 256-byte row
-    const int xm = slot >> 4, xc = slot & 15, xkh = xc >> 3, xcc = xc & 7;
-    const uint32_t x_dst = (uint32_t)(xkh * 2048 + xm * 128 + ((xcc ^ (xm & 7)) << 4));
-
-    const int Gi = (int)G, kpg = (int)(group / kKB);
-    const int64_t wrow = K / 2;
-    // issue the copies of unit j (at cursor c) into its stage
-    auto issue = [&](int64_t j, const UnitCursor& c) {
-      uint8_t* st = smem + (size_t)(j % kStages) * kStageBytes;
-      const int64_t n = (int64_t)c.t * kTileN + r;
-      const bool nv = n < N;
-      const uint8_t* wsrc = w + (nv ? n : 0) * wrow + c.kb * (kKB / 2) + h * 32;
-      cp_async16(st + kXBytes + slot * 16, wsrc, nv);
-      cp_async16(st + kXBytes + 4096 + slot * 16, wsrc + 16, nv);
-      const bool mv = xm < M;
-      cp_async16(st + x_dst, x + (mv ? xm : 0) * K + c.kb * kKB + xkh * 64 + xcc * 8, mv);
-      if (kScaleChunk) cp_async16(st + kXBytes + kWBytes + slot * 16, scale + (nv ? n : 0) * gpr + (c.gi & ~7), nv);
+    UnitCursor ce, cs;  // the unit being finished, the unit whose scale is loaded next
+    ce.init(lo, G, kpg);
+    cs = ce;
+    auto load_scale = [&]() {  // raw f16 bits of this row's scale for the unit at cs, then advance cs
+      const int64_t n = (int64_t)cs.t * kTileN + r;
+      const unsigned short v = n < N ? __ldg(reinterpret_cast<const unsigned short*>(scale) + n * gpr + cs.gi) : 0;
+      cs.next(Gi, kpg);
+      return v;
     };
-
-    UnitCursor cn, cu, ce;  // the unit being prefetched, dequantized, and finished by the epilogue
-    cn.init(lo, G, kpg);
-    cu = cn;
-    ce = cn;
-    for (int64_t j = 0; j < kPrefetch; ++j) {
-      if (j < n_units) {
-        issue(j, cn);
-        cn.next(Gi, kpg);
-      }
-      cp_async_commit();
-    }
-
-    float acc[8];
+    // scales are loaded kScaleAhead units before use, so their latency hides behind the units in between
+    unsigned short sq[kScaleAhead];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-    float p0 = 0.f, p1 = 0.f, p2 = 0.f;  // scale pipeline: units i, i-1, i-2
+    for (int u = 0; u < kScaleAhead; ++u) sq[u] = u < n_units ? load_scale() : 0;
+    float acc[kMmaN];
+#pragma unroll
+    for (int j = 0; j < kMmaN; ++j) acc[j] = 0.f;
     int64_t seg_kb0 = 0;
-    for (int64_t i = 0; i < n_units + kLag; ++i) {
-      p2 = p1;
-      p1 = p0;
-      if (i < n_units) {
-        const int s = (int)(i % kStages), a = (int)(i % kRing);
-        const uint32_t aph = (uint32_t)((i / kRing) & 1);
-        // refill the stage of unit i + kPrefetch once the MMAs that read its previous contents are done
-        const int64_t jn = i + kPrefetch;
-        bool ok = true;
-        if (jn < n_units && jn >= kStages) {
-          const int64_t old = jn - kStages;  // <= i - 3
-          ok = tc::mbar_wait(&mma_done[old % kRing], (uint32_t)((old / kRing) & 1), wait_ns, abort_flag);
-        }
-        // the A stage is free once the unit kRing earlier has been multiplied
-        ok = ok && tc::mbar_wait(&mma_done[a], aph ^ 1u, wait_ns, abort_flag);
-        if (!__all_sync(0xffffffffu, ok)) {  // warp-uniform: the tcgen05 ops below are .sync.aligned
-          give_up();
-          break;
-        }
-        if (jn < n_units) {
-          issue(jn, cn);
-          cn.next(Gi, kpg);
-        }
-        cp_async_commit();
-        cp_async_wait<kPrefetch>();  // this thread's copies of unit i have landed
-        tc::fence_proxy_async_smem();  // ... and are visible to the tensor core's reads of the activations
-        tc::mbar_arrive(&x_ready[s]);
-        const uint8_t* st = smem + (size_t)s * kStageBytes;
-        if (kScaleChunk) {
-          p0 = __half2float(reinterpret_cast<const __half*>(st + kXBytes + kWBytes + slot * 16)[cu.gi & 7]);
-        } else {
-          const int64_t n = (int64_t)cu.t * kTileN + r;
-          p0 = n < N ? __half2float(scale[n * gpr + cu.gi]) : 0.f;
-        }
-        cu.next(Gi, kpg);
-        uint32_t regs[32];
+    for (int64_t e = 0; e < n_units; ++e) {
+      const int d = (int)(e % kRing);
+      const uint32_t dph = (uint32_t)((e / kRing) & 1);
+      const float sc = __half2float(__ushort_as_half(sq[0]));
 #pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          const uint4 v = *reinterpret_cast<const uint4*>(st + kXBytes + cc * 4096 + slot * 16);
-          const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+      for (int u = 0; u + 1 < kScaleAhead; ++u) sq[u] = sq[u + 1];
+      sq[kScaleAhead - 1] = e + kScaleAhead < n_units ? load_scale() : 0;
+      const bool good = tc::mbar_wait(&mma_done[d], dph, wait_ns, abort_flag);
+      if (!__all_sync(0xffffffffu, good)) {
+        give_up();
+        break;
+      }
+      tc::fence_after_sync();
+      const int64_t t = ce.t, kb = ce.kb;
+      if (e == 0 || kb == 0) {
+        seg_kb0 = kb;
 #pragma unroll
-          for (int wi = 0; wi < 4; ++wi) {
-            const uint32_t q4 = wd[wi] >> 4;
+        for (int j = 0; j < kMmaN; ++j) acc[j] = 0.f;
+      }
 #pragma unroll
-            for (int pp = 0; pp < 4; ++pp) regs[cc * 16 + wi * 4 + pp] = nib2_to_bf16x2(wd[wi], q4, pp);
+      for (int h = 0; h < 2; ++h) {  // columns 8h .. 8h+7, two accumulators at a time (register budget)
+        float sum[8];
+#pragma unroll
+        for (int pr = 0; pr < 2; ++pr) {
+          uint32_t dv[2][8];
+#pragma unroll
+          for (int gg = 0; gg < 2; ++gg)
+            tc::ld_32x32b_x8(tmem + lane_addr + kDCol0 + d * (16 * kIssuers) + (2 * pr + gg) * 16 + 8 * h, dv[gg]);
+          tc::wait_ld();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float s2 = __uint_as_float(dv[0][j]) + __uint_as_float(dv[1][j]);
+            sum[j] = pr == 0 ? s2 : sum[j] + s2;
           }
         }
-        tc::st_32x32b_x32(tmem + lane_addr + kACol0 + a * 64 + 32 * h, regs);
-        tc::wait_st();
-        tc::fence_before_sync();
-        tc::mbar_arrive(&a_full[2 * a + h]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[8 * h + j] = fmaf(sc, sum[j], acc[8 * h + j]);
       }
-      if (i >= kLag) {
-        const int64_t e = i - kLag;
-        const int d = (int)(e % kRing);
-        const uint32_t dph = (uint32_t)((e / kRing) & 1);
-        const bool ok = tc::mbar_wait(&mma_done[d], dph, wait_ns, abort_flag);
-        if (!__all_sync(0xffffffffu, ok)) {
-          give_up();
-          break;
-        }
-        tc::fence_after_sync();
-        uint32_t dv[kIssuers][8];
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&d_empty[d]);
+      ce.next(Gi, kpg);
+      const int64_t u = lo + e;
+      if (u + 1 == hi || kb == G - 1) {
+        // ---- the segment [seg_kb0, kb] of tile t ends here ----
+        const int64_t n = t * kTileN + r;
+        if (seg_kb0 == 0 && kb == G - 1) {
 #pragma unroll
-        for (int gg = 0; gg < kIssuers; ++gg)
-          tc::ld_32x32b_x8(tmem + lane_addr + kDCol0 + d * (16 * kIssuers) + gg * 16 + 8 * h, dv[gg]);
-        tc::wait_ld();
-        tc::fence_before_sync();
-        tc::mbar_arrive(&d_empty[d]);
-        const int64_t u = lo + e;
-        const int64_t t = ce.t, kb = ce.kb;
-        ce.next(Gi, kpg);
-        if (e == 0 || kb == 0) {
-          seg_kb0 = kb;
+          for (int m = 0; m < kMmaN; ++m)
+            if (m < M && n < N) out[(int64_t)m * N + n] = __bfloat16_as_ushort(__float2bfloat16_rn(acc[m]));
+        } else {
+          // Split tile: this warp publishes its 32 rows x 16 columns of f32 partials; the warp that completes
+          // the tile's count (4 warps per contributing CTA) sums the partials in CTA order.
+          const int64_t c0 = cta_of_unit(t * G, U, P), c1 = cta_of_unit(t * G + G - 1, U, P);
+          const int64_t nseg = c1 - c0 + 1, sidx = (int64_t)blockIdx.x - c0;
+          float* pslot = partials + ((t * S_max + sidx) * kMmaN) * kTileN;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float sum = (__uint_as_float(dv[0][j]) + __uint_as_float(dv[1][j])) +
-                            (__uint_as_float(dv[2][j]) + __uint_as_float(dv[3][j]));
-          acc[j] = fmaf(p2, sum, acc[j]);
-        }
-        if (u + 1 == hi || kb == G - 1) {
-          // ---- the segment [seg_kb0, kb] of tile t ends here ----
-          const int64_t n = t * kTileN + r;
-          if (seg_kb0 == 0 && kb == G - 1) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int m = 8 * h + j;
-              if (m < M && n < N) out[(int64_t)m * N + n] = __bfloat16_as_ushort(__float2bfloat16_rn(acc[j]));
-            }
-          } else {
-            // Split tile: this warp publishes its 32 rows x 8 columns of f32 partials; the warp that
-            // completes the tile's count (8 warps per contributing CTA) sums the partials in CTA order.
-            const int64_t c0 = cta_of_unit(t * G, U, P), c1 = cta_of_unit(t * G + G - 1, U, P);
-            const int64_t nseg = c1 - c0 + 1, sidx = (int64_t)blockIdx.x - c0;
-            float* pslot = partials + ((t * S_max + sidx) * kMmaN) * kTileN;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) __stcg(pslot + (8 * h + j) * kTileN + r, acc[j]);
+          for (int m = 0; m < kMmaN; ++m) __stcg(pslot + m * kTileN + r, acc[m]);
+          __threadfence();
+          __syncwarp();
+          uint32_t last = 0;
+          if (lane == 0) last = (atomicAdd(&counters[t], 1u) == (uint32_t)(nseg * kEpiWarps - 1)) ? 1u : 0u;
+          last = __shfl_sync(0xffffffffu, last, 0);
+          if (last) {
             __threadfence();
-            __syncwarp();
-            uint32_t last = 0;
-            if (lane == 0) last = (atomicAdd(&counters[t], 1u) == (uint32_t)(nseg * 8 - 1)) ? 1u : 0u;
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (last) {
-              __threadfence();
-              for (int rr = 0; rr < kTileN / 32; ++rr) {
-                const int row = rr * 32 + lane;
-                const int64_t nn = t * kTileN + row;
-                for (int m = 0; m < kMmaN; ++m) {
-                  float v = 0.f;
-                  for (int64_t sg = 0; sg < nseg; ++sg) {
-                    float* pp = partials + ((t * S_max + sg) * kMmaN + m) * kTileN + row;
-                    const float pv = __ldcg(pp);
-                    __stcg(pp, 0.f);  // leave the workspace all-zero: any later shape may reuse these bytes
-                    v = (sg == 0) ? pv : v + pv;
-                  }
-                  if (m < M && nn < N) out[(int64_t)m * N + nn] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+            for (int rr = 0; rr < kTileN / 32; ++rr) {
+              const int row = rr * 32 + lane;
+              const int64_t nn = t * kTileN + row;
+              for (int m = 0; m < kMmaN; ++m) {
+                float v = 0.f;
+                for (int64_t sg = 0; sg < nseg; ++sg) {
+                  float* pp = partials + ((t * S_max + sg) * kMmaN + m) * kTileN + row;
+                  const float pv = __ldcg(pp);
+                  __stcg(pp, 0.f);  // leave the workspace all-zero: any later shape may reuse these bytes
+                  v = (sg == 0) ? pv : v + pv;
                 }
+                if (m < M && nn < N) out[(int64_t)m * N + nn] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
               }
-              if (lane == 0) counters[t] = 0u;  // re-armed for the next launch
             }
+            if (lane == 0) counters[t] = 0u;  // re-armed for the next launch
           }
         }
       }
     }
-    cp_async_wait<0>();  // no copy may still target this CTA's shared memory when it exits
+  } else {
+    // ---------------- activation loader: two TMA boxes per unit ----------------
+    if (lane == 0) {
+      tc::tma_prefetch_desc(&xmap);
+      UnitCursor cx;
+      cx.init(lo, G, kpg);
+      int64_t issued = 0;
+      for (int64_t i = 0; i < n_units; ++i) {
+        const int s = (int)(i % kXStages);
+        if (!tc::mbar_wait(&x_empty[s], (uint32_t)(((i / kXStages) & 1) ^ 1), wait_ns, abort_flag)) {
+          give_up();
+          break;
+        }
+        uint8_t* dst = xs + (size_t)s * kXBytes;
+        tc::mbar_arrive_expect_tx(&x_full[s], kXBytes);
+        tc::tma_load_2d(dst, &xmap, &x_full[s], cx.kb * kKB, 0);
+        tc::tma_load_2d(dst + kXBytes / 2, &xmap, &x_full[s], cx.kb * kKB + kKB / 2, 0);
+        cx.next(Gi, kpg);
+        issued = i + 1;
+      }
+      // every issued load must land before this CTA's shared memory is released
+      for (int64_t j = issued > kXStages ? issued - kXStages : 0; j < issued; ++j)
+        tc::mbar_wait(&x_full[j % kXStages], (uint32_t)((j / kXStages) & 1), wait_ns, nullptr);
+    }
   }
 
   tc::fence_before_sync();
@@ -416,6 +412,19 @@ static Plan make_plan(int64_t n, int64_t k) {
   return p;
 }
 
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
 }  // namespace w4
 }  // namespace up
 
@@ -438,11 +447,22 @@ extern "C" int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, cons
   if (k == 0 || k % kKB != 0 || group % kKB != 0 || k % group != 0) return UP_ERR_UNSUPPORTED;
   if (k / 2 > 0x7fffffff || n > 0x7fffffff) return UP_ERR_UNSUPPORTED;
   UP_CHECK_ARG(w && scale && x && out && workspace);
-  // 16-byte copies: W rows (K/2 bytes, a multiple of 64) and activation rows (2K bytes) start 16-byte aligned
+  // 16-byte loads of W rows (K/2 bytes, a multiple of 64) and TMA boxes of activation rows (2K bytes)
   if (!aligned(w, 16) || !aligned(x, 16) || !aligned(workspace, 256)) return UP_ERR_INVALID;
   const Plan p = make_plan(n, k);
   if (workspace_bytes < p.bytes) return UP_ERR_INVALID;
-  const bool scale_chunk = (k / group) % 8 == 0 && aligned(scale, 16);
+  auto enc = encode_fn();
+  if (enc == nullptr) return fail_with(UP_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  // activations as a [M, K] bf16 tensor; boxes of 16 rows x 64 k, 128-byte swizzled; rows >= M read as zero
+  CUtensorMap xmap;
+  const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
+  const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)(kKB / 2), (cuuint32_t)kMmaN};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult cr = enc(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(x), dims, strides, box,
+                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail_with(UP_ERR_CUDA, "cuTensorMapEncodeTiled refused the activation tensor map");
   {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -451,9 +471,7 @@ extern "C" int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, cons
     static bool attr_set[64] = {false};
     std::lock_guard<std::mutex> lk(mu);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-      e = cudaFuncSetAttribute(w4a16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
-      if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(w4a16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+      e = cudaFuncSetAttribute(w4a16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
       if (e != cudaSuccess) return cuda_status(e);
       if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
@@ -463,9 +481,9 @@ extern "C" int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, cons
   auto* counters = reinterpret_cast<uint32_t*>(base + p.counters_off);
   auto* partials = reinterpret_cast<float*>(base + p.partials_off);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  auto kern = scale_chunk ? w4a16_kernel<true> : w4a16_kernel<false>;
-  kern<<<(unsigned)p.P, kThreads, kSmemBytes, s>>>(w, reinterpret_cast<const __half*>(scale), x, out, (int)m, n, k,
-                                                  group, p.U, p.G, p.S_max, hdr, counters, partials, wait_limit_ns());
+  w4a16_kernel<<<(unsigned)p.P, kThreads, kSmemBytes, s>>>(xmap, w, reinterpret_cast<const __half*>(scale), out,
+                                                          (int)m, n, k, group, p.U, p.G, p.S_max, hdr, counters,
+                                                          partials, wait_limit_ns());
   note_launch();
   return check_launch();
 }
