@@ -16,12 +16,15 @@
 //    exact bf16 (one prmt, one lop3 and one bf16x2 subtract per pair) and stores them into tensor memory
 //    (tcgen05.st), where they are the MMA's A operand.
 //  * warps 16..19 (MMA issuers): a single thread issues only about one tcgen05.mma per ~100 cycles, so four
-//    warps issue in parallel: issuer g runs the two k-steps of k-quarter g of every unit into its own TMEM
-//    accumulator, and waits only for the four dequant warps of that quarter.
+//    threads share the eight k-steps of a unit as a pipeline: issuer g runs the two k-steps of k-quarter g
+//    into the unit's accumulator after issuer g - 1 has issued its own (an mbarrier hand-off between
+//    tcgen05.fence::before_thread_sync and ::after_thread_sync orders them), so each unit ends in one
+//    accumulator while several units are in issue at once. (Four separate accumulators per unit were measured
+//    slower: the epilogue's reads of four times the tensor-memory data cost more than the hand-offs.)
 //  * warp 24 (activation loader): one thread brings each unit's [16 x 128] activation tile into a ring of
 //    shared-memory stages with two TMA boxes, 128-byte swizzled as the MMA reads it; rows past M read as 0.
-//  * warps 20..23 (epilogue): read the unit's four accumulators (tcgen05.ld), add them, scale by
-//    scale[n][k-block] in f32 and accumulate in registers. A tile finished inside one CTA is written as bf16;
+//  * warps 20..23 (epilogue): read the unit's accumulator (tcgen05.ld), scale it by scale[n][k-block] in f32
+//    and accumulate in registers. A tile finished inside one CTA is written as bf16;
 //    a tile split between CTAs writes f32 partials, and whichever CTA finishes it last (an atomic count)
 //    sums them in CTA order, writes bf16 and clears the partials — no CTA ever waits on another.
 // Every mbarrier wait is bounded; a wait that runs out sets the workspace error word and the CTA unwinds.
@@ -48,16 +51,22 @@ constexpr int kIss0 = kDqWarps, kEpi0 = kIss0 + kIssuers, kXWarp = kEpi0 + kEpiW
 constexpr int kThreads = 32 * (kXWarp + 1);      // 800
 constexpr int kPrefetch = 4;                     // units of W a dequant thread has in flight
 constexpr int kScaleAhead = 4;                   // units an epilogue thread's scale loads run ahead
+constexpr uint32_t kSleepNs = 64;                // pause between polls of a waiting dequant/epilogue/loader warp
 constexpr int kXBytes = kMmaN * kKB * 2;         // 4 KiB of bf16 per unit: two 128-byte-swizzled boxes of 64 k
 constexpr int kXStages = 8;
-constexpr int kRing = 4;                         // units in flight between dequant, MMA and epilogue
+constexpr int kRing = 6;                         // units in flight between dequant, MMA and epilogue
 constexpr int kTmemCols = 512;
 constexpr int kACol0 = 0;                        // A (dequantized W): kRing x 64 columns
-constexpr int kDCol0 = kRing * 64;               // accumulators: kRing units x kIssuers x 16 columns
-constexpr int kBarBytes = 512;
+constexpr int kDCol0 = kRing * 64;               // accumulators: kRing units x 16 columns
+// mbarriers: x_full, x_empty [kXStages]; a_full [kRing][4]; mma_done, d_empty [kRing]; hand [kIssuers-1][kRing];
+// seg_in, seg_out;
+// then the TMEM address word, the abort word and the fix-up verdict
+constexpr int kNumBars = 2 * kXStages + 4 * kRing + 2 * kRing + (kIssuers - 1) * kRing + 2;
+constexpr int kBarBytes = 1024;
+static_assert(kNumBars * 8 + 12 <= kBarBytes, "barrier region");
 constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + (size_t)kXStages * kXBytes + kBarBytes;
 static_assert(kEpi0 % 4 == 0, "epilogue warp e reads TMEM lane quarter e % 4");
-static_assert(kDCol0 + kRing * kIssuers * kMmaN <= kTmemCols, "tensor memory");
+static_assert(kDCol0 + kRing * kMmaN <= kTmemCols, "tensor memory");
 
 struct WsHeader {
   uint32_t ticket, done, epoch, error;  // same layout as the scan workspace: `error` at byte 12
@@ -111,6 +120,66 @@ struct UnitCursor {
   }
 };
 
+// The end of a tile segment [seg_kb0, kb] in the epilogue (all kEpiWarps epilogue warps reach it together):
+// a whole tile is written as bf16. For a tile split between CTAs, each epilogue thread publishes its row's
+// 16 f32 partials; the epilogue warps meet on an mbarrier (seg_in, one arrival per warp), one thread counts
+// this CTA in and announces whether it completed the count (seg_out); in the CTA that did, every epilogue
+// thread sums its own row over the contributing CTAs in CTA order (a segment's loads issued together),
+// writes bf16 and clears the partials. `nfix` counts this warp's split-tile ends (the barriers' phase).
+// Both waits are bounded; false means the CTA is giving up.
+__device__ __forceinline__ bool finish_segment(const float (&acc)[kMmaN], int64_t t, int64_t seg_kb0, int64_t kb,
+                                               int r, int lane, int M, int64_t N, int64_t U, int64_t G, int64_t P,
+                                               int64_t S_max, uint16_t* out, uint32_t* counters, float* partials,
+                                               uint64_t* seg_in, uint64_t* seg_out, volatile uint32_t* s_last,
+                                               uint32_t& nfix, uint64_t wait_ns, volatile int* abort_flag) {
+  const int64_t n = t * kTileN + r;
+  if (seg_kb0 == 0 && kb == G - 1) {
+#pragma unroll
+    for (int m = 0; m < kMmaN; ++m)
+      if (m < M && n < N) out[(int64_t)m * N + n] = __bfloat16_as_ushort(__float2bfloat16_rn(acc[m]));
+    return true;
+  }
+  const int64_t c0 = cta_of_unit(t * G, U, P), c1 = cta_of_unit(t * G + G - 1, U, P);
+  const int64_t nseg = c1 - c0 + 1, sidx = (int64_t)blockIdx.x - c0;
+  float* tile_parts = partials + t * S_max * kMmaN * kTileN;
+#pragma unroll
+  for (int m = 0; m < kMmaN; ++m) __stcg(tile_parts + (sidx * kMmaN + m) * kTileN + r, acc[m]);
+  __threadfence();
+  __syncwarp();
+  const uint32_t ph = nfix & 1u;
+  ++nfix;
+  if (lane == 0) tc::mbar_arrive(seg_in);
+  if (!__all_sync(0xffffffffu, tc::mbar_wait(seg_in, ph, wait_ns, abort_flag))) return false;
+  if (r == 0) {
+    *s_last = (atomicAdd(&counters[t], 1u) == (uint32_t)(nseg - 1)) ? 1u : 0u;
+    tc::mbar_arrive(seg_out);
+  }
+  if (!__all_sync(0xffffffffu, tc::mbar_wait(seg_out, ph, wait_ns, abort_flag))) return false;
+  if (!*s_last) return true;
+  __threadfence();
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {  // 8 activation rows at a time (register budget)
+    float v[8];
+    for (int64_t sg = 0; sg < nseg; ++sg) {
+      float pv[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) pv[j] = __ldcg(tile_parts + (sg * kMmaN + 8 * half + j) * kTileN + r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[j] = (sg == 0) ? pv[j] : v[j] + pv[j];
+        __stcg(tile_parts + (sg * kMmaN + 8 * half + j) * kTileN + r, 0.f);  // all-zero again for any later shape
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int m = 8 * half + j;
+      if (m < M && n < N) out[(int64_t)m * N + n] = __bfloat16_as_ushort(__float2bfloat16_rn(v[j]));
+    }
+  }
+  if (r == 0) counters[t] = 0u;  // re-armed for the next launch
+  return true;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     w4a16_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ w,
                  const __half* __restrict__ scale, uint16_t* __restrict__ out, int M, int64_t N, int64_t K,
@@ -119,12 +188,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* xs = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* x_full = reinterpret_cast<uint64_t*>(xs + (size_t)kXStages * kXBytes);  // [kXStages]: TMA landed
-  uint64_t* x_empty = x_full + kXStages;        // [kXStages]: the stage's MMAs completed (4 issuer commits)
+  uint64_t* x_empty = x_full + kXStages;        // [kXStages]: the stage's MMAs completed (last issuer's commit)
   uint64_t* a_full = x_empty + kXStages;        // [kRing][4]: k-quarter q of the unit's A is in TMEM (4 warps)
-  uint64_t* mma_done = a_full + 4 * kRing;      // [kRing]: every issuer's MMAs of the unit completed
-  uint64_t* d_empty = mma_done + kRing;         // [kRing]: the epilogue has read the unit's accumulators
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + kRing);
+  uint64_t* mma_done = a_full + 4 * kRing;      // [kRing]: all of the unit's MMAs completed
+  uint64_t* d_empty = mma_done + kRing;         // [kRing]: the epilogue has read the unit's accumulator
+  uint64_t* hand = d_empty + kRing;             // [kIssuers - 1][kRing]: issuer g has issued the unit's k-quarter g
+  uint64_t* seg_in = hand + (kIssuers - 1) * kRing;  // split-tile end: every epilogue warp has published
+  uint64_t* seg_out = seg_in + 1;                     // split-tile end: the count verdict is in s_last
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(seg_out + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile uint32_t* s_last = reinterpret_cast<volatile uint32_t*>(tmem_slot + 2);  // split-tile fix-up verdict
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t P = gridDim.x;
@@ -135,13 +208,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kXStages; ++s) {
       tc::mbar_init(&x_full[s], 1);
-      tc::mbar_init(&x_empty[s], kIssuers);
+      tc::mbar_init(&x_empty[s], 1);
     }
     for (int a = 0; a < kRing; ++a) {
       for (int q = 0; q < 4; ++q) tc::mbar_init(&a_full[4 * a + q], 4);
-      tc::mbar_init(&mma_done[a], kIssuers);
+      tc::mbar_init(&mma_done[a], 1);
       tc::mbar_init(&d_empty[a], kEpiWarps);
+      for (int g = 0; g + 1 < kIssuers; ++g) tc::mbar_init(&hand[g * kRing + a], 1);
     }
+    tc::mbar_init(seg_in, kEpiWarps);
+    tc::mbar_init(seg_out, 1);
     *abort_flag = 0;
     tc::mbar_fence_init();
   }
@@ -187,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int a = (int)(i % kRing);
         const uint32_t aph = (uint32_t)((i / kRing) & 1);
         // the A stage is free once the unit kRing earlier has been multiplied
-        const bool good = tc::mbar_wait(&mma_done[a], aph ^ 1u, wait_ns, abort_flag);
+        const bool good = tc::mbar_wait_sleepy(&mma_done[a], aph ^ 1u, wait_ns, abort_flag, kSleepNs);
         if (!__all_sync(0xffffffffu, good)) {  // warp-uniform: the tcgen05 ops below are .sync.aligned
           give_up();
           ok = false;
@@ -217,9 +293,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int64_t i = 0; i < n_units; ++i) {
         const int a = (int)(i % kRing), s = (int)(i % kXStages);
         const uint32_t rph = (uint32_t)((i / kRing) & 1), xph = (uint32_t)((i / kXStages) & 1);
-        if (!tc::mbar_wait(&a_full[4 * a + g], rph, wait_ns, abort_flag) ||
-            !tc::mbar_wait(&x_full[s], xph, wait_ns, abort_flag) ||
-            !tc::mbar_wait(&d_empty[a], rph ^ 1u, wait_ns, abort_flag)) {
+        // issuer 0 starts the accumulator once the epilogue has read its previous unit; issuer g > 0 adds to it
+        // after issuer g - 1
+        const bool ready = tc::mbar_wait(&a_full[4 * a + g], rph, wait_ns, abort_flag) &&
+                           tc::mbar_wait(&x_full[s], xph, wait_ns, abort_flag) &&
+                           (g == 0 ? tc::mbar_wait(&d_empty[a], rph ^ 1u, wait_ns, abort_flag)
+                                   : tc::mbar_wait(&hand[(g - 1) * kRing + a], rph, wait_ns, abort_flag));
+        if (!ready) {
           give_up();
           break;
         }
@@ -229,11 +309,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int jj = 0; jj < 2; ++jj) {
           const int j = 2 * g + jj;  // k-step: 16 k = 32 bytes of a 128-byte swizzle atom row
           const uint64_t bdesc = tc::sdesc_kmajor_sw128(xaddr + (uint32_t)((j >> 2) * 2048 + (j & 3) * 32));
-          tc::mma_ts_bf16(tmem + kDCol0 + a * (16 * kIssuers) + g * 16, tmem + kACol0 + a * 64 + j * 8, bdesc, idesc,
-                          jj > 0 ? 1u : 0u);
+          tc::mma_ts_bf16(tmem + kDCol0 + a * kMmaN, tmem + kACol0 + a * 64 + j * 8, bdesc, idesc,
+                          (g > 0 || jj > 0) ? 1u : 0u);
         }
-        tc::commit(&mma_done[a]);
-        tc::commit(&x_empty[s]);
+        if (g + 1 < kIssuers) {
+          tc::fence_before_sync();
+          tc::mbar_arrive(&hand[g * kRing + a]);
+        } else {
+          // the unit's MMAs run in issue order, so the last issuer's completing covers all of them
+          tc::commit(&mma_done[a]);
+          tc::commit(&x_empty[s]);
+        }
         issued = i + 1;
       }
       // Unwinding after an abort: the MMAs already issued must finish before TMEM is released.
@@ -265,6 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int j = 0; j < kMmaN; ++j) acc[j] = 0.f;
     int64_t seg_kb0 = 0;
+    uint32_t nfix = 0;
     for (int64_t e = 0; e < n_units; ++e) {
       const int d = (int)(e % kRing);
       const uint32_t dph = (uint32_t)((e / kRing) & 1);
@@ -272,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int u = 0; u + 1 < kScaleAhead; ++u) sq[u] = sq[u + 1];
       sq[kScaleAhead - 1] = e + kScaleAhead < n_units ? load_scale() : 0;
-      const bool good = tc::mbar_wait(&mma_done[d], dph, wait_ns, abort_flag);
+      const bool good = tc::mbar_wait_sleepy(&mma_done[d], dph, wait_ns, abort_flag, kSleepNs);
       if (!__all_sync(0xffffffffu, good)) {
         give_up();
         break;
@@ -284,70 +371,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < kMmaN; ++j) acc[j] = 0.f;
       }
+      {
+        uint32_t dv[kMmaN];
+        tc::ld_32x32b_x16(tmem + lane_addr + kDCol0 + d * kMmaN, dv);
+        tc::wait_ld();
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {  // columns 8h .. 8h+7, two accumulators at a time (register budget)
-        float sum[8];
-#pragma unroll
-        for (int pr = 0; pr < 2; ++pr) {
-          uint32_t dv[2][8];
-#pragma unroll
-          for (int gg = 0; gg < 2; ++gg)
-            tc::ld_32x32b_x8(tmem + lane_addr + kDCol0 + d * (16 * kIssuers) + (2 * pr + gg) * 16 + 8 * h, dv[gg]);
-          tc::wait_ld();
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float s2 = __uint_as_float(dv[0][j]) + __uint_as_float(dv[1][j]);
-            sum[j] = pr == 0 ? s2 : sum[j] + s2;
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[8 * h + j] = fmaf(sc, sum[j], acc[8 * h + j]);
+        for (int j = 0; j < kMmaN; ++j) acc[j] = fmaf(sc, __uint_as_float(dv[j]), acc[j]);
       }
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&d_empty[d]);
       ce.next(Gi, kpg);
       const int64_t u = lo + e;
-      if (u + 1 == hi || kb == G - 1) {
-        // ---- the segment [seg_kb0, kb] of tile t ends here ----
-        const int64_t n = t * kTileN + r;
-        if (seg_kb0 == 0 && kb == G - 1) {
-#pragma unroll
-          for (int m = 0; m < kMmaN; ++m)
-            if (m < M && n < N) out[(int64_t)m * N + n] = __bfloat16_as_ushort(__float2bfloat16_rn(acc[m]));
-        } else {
-          // Split tile: this warp publishes its 32 rows x 16 columns of f32 partials; the warp that completes
-          // the tile's count (4 warps per contributing CTA) sums the partials in CTA order.
-          const int64_t c0 = cta_of_unit(t * G, U, P), c1 = cta_of_unit(t * G + G - 1, U, P);
-          const int64_t nseg = c1 - c0 + 1, sidx = (int64_t)blockIdx.x - c0;
-          float* pslot = partials + ((t * S_max + sidx) * kMmaN) * kTileN;
-#pragma unroll
-          for (int m = 0; m < kMmaN; ++m) __stcg(pslot + m * kTileN + r, acc[m]);
-          __threadfence();
-          __syncwarp();
-          uint32_t last = 0;
-          if (lane == 0) last = (atomicAdd(&counters[t], 1u) == (uint32_t)(nseg * kEpiWarps - 1)) ? 1u : 0u;
-          last = __shfl_sync(0xffffffffu, last, 0);
-          if (last) {
-            __threadfence();
-            for (int rr = 0; rr < kTileN / 32; ++rr) {
-              const int row = rr * 32 + lane;
-              const int64_t nn = t * kTileN + row;
-              for (int m = 0; m < kMmaN; ++m) {
-                float v = 0.f;
-                for (int64_t sg = 0; sg < nseg; ++sg) {
-                  float* pp = partials + ((t * S_max + sg) * kMmaN + m) * kTileN + row;
-                  const float pv = __ldcg(pp);
-                  __stcg(pp, 0.f);  // leave the workspace all-zero: any later shape may reuse these bytes
-                  v = (sg == 0) ? pv : v + pv;
-                }
-                if (m < M && nn < N) out[(int64_t)m * N + nn] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
-              }
-            }
-            if (lane == 0) counters[t] = 0u;  // re-armed for the next launch
-          }
+      if (u + 1 == hi || kb == G - 1)  // the segment [seg_kb0, kb] of tile t ends here
+        if (!finish_segment(acc, t, seg_kb0, kb, r, lane, M, N, U, G, P, S_max, out, counters, partials, seg_in,
+                            seg_out, s_last, nfix, wait_ns, abort_flag)) {
+          give_up();
+          break;
         }
-      }
     }
   } else {
     // ---------------- activation loader: two TMA boxes per unit ----------------
@@ -358,7 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int64_t issued = 0;
       for (int64_t i = 0; i < n_units; ++i) {
         const int s = (int)(i % kXStages);
-        if (!tc::mbar_wait(&x_empty[s], (uint32_t)(((i / kXStages) & 1) ^ 1), wait_ns, abort_flag)) {
+        if (!tc::mbar_wait_sleepy(&x_empty[s], (uint32_t)(((i / kXStages) & 1) ^ 1), wait_ns, abort_flag, kSleepNs)) {
           give_up();
           break;
         }
