@@ -75,7 +75,12 @@ def _p(a: np.ndarray):
 
 
 def max_threads() -> int:
-    return int(lib().orc_max_threads())
+    """Host threads this process may run on. Taken from the CPU affinity rather than OpenMP's default, which
+    launchers such as torchrun pin to 1 through OMP_NUM_THREADS; every parallel region names its count."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return max(1, os.cpu_count() or int(lib().orc_max_threads()))
 
 
 def row_sum_f32(x: np.ndarray, threads: int = 1) -> np.ndarray:
