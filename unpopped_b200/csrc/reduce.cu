@@ -207,6 +207,7 @@ __global__ void __launch_bounds__(kRowThreads) row_max_argmax_vec_kernel(const u
     const uint4* rv = reinterpret_cast<const uint4*>(row);
     uint32_t best_key = 0;
     int best_word = -1;
+    uint4 best_w = make_uint4(0u, 0u, 0u, 0u);  // the best word's bits, kept so the row is never re-read
     for (int i0 = threadIdx.x; i0 < nvec; i0 += kRowThreads * UNROLL) {
       uint4 w[UNROLL];
 #pragma unroll
@@ -222,36 +223,37 @@ __global__ void __launch_bounds__(kRowThreads) row_max_argmax_vec_kernel(const u
           if (best_word < 0 || key > best_key) {
             best_key = key;
             best_word = i;
+            best_w = w[u];
           }
         }
       }
     }
-    uint32_t packed = 0;
+    uint32_t packed = 0, my_bits = 0;
     if (best_word >= 0) {
-      const uint4 w = rv[best_word];
-      const uint32_t q[4] = {w.x, w.y, w.z, w.w};
+      const uint32_t q[4] = {best_w.x, best_w.y, best_w.z, best_w.w};
       int e = 0;
 #pragma unroll
       for (int j = 7; j >= 0; --j)
         if (bf16_key((q[j >> 1] >> ((j & 1) * 16)) & 0xffffu) == best_key) e = j;
       const uint32_t idx = (uint32_t)(8 * best_word + e);
       packed = (best_key << 16) | (0xffffu - idx);
+      my_bits = (q[e >> 1] >> ((e & 1) * 16)) & 0xffffu;
     }
     const uint32_t best = block_max_u32(packed, sm32);
     const uint32_t key = best >> 16;
     const int64_t arg = cols > 0 ? (int64_t)(0xffffu - (best & 0xffffu)) : 0;
-    uint32_t max_bits = 0;
     if (key == 0xffffu) {
       // NaN row: the max is the last NaN (rare; re-read the row).
       uint32_t last = 0;
       for (int64_t i = threadIdx.x; i < cols; i += kRowThreads)
         if (bf16_isnan(row[i])) last = (uint32_t)i + 1;
       last = block_max_u32(last, sm32);
-      max_bits = ((uint32_t)row[last - 1] << 16) | 0x00400000u;
-    } else if (cols > 0) {
-      max_bits = (uint32_t)row[arg] << 16;
+      if (threadIdx.x == 0)
+        write_max_argmax(row, r, arg, ((uint32_t)row[last - 1] << 16) | 0x00400000u, max_out, am32, am64);
+    } else if (best_word >= 0 && packed == best) {
+      // exactly one thread holds the winning (key, index): it writes from its own registers
+      write_max_argmax(row, r, arg, my_bits << 16, max_out, am32, am64);
     }
-    if (threadIdx.x == 0) write_max_argmax(row, r, arg, max_bits, max_out, am32, am64);
   }
 }
 
