@@ -286,8 +286,8 @@ constexpr int kQCompute = kQTile / (4 * kQRowChunks);  // 512 compute threads
 constexpr int kQCWarps = kQCompute / 32;            // 16
 constexpr int kQCopyWarp = kQCWarps, kQLookWarp = kQCWarps + 1;
 constexpr int kQThreads = kQCompute + 64;           // + copy warp + look-back warp
-constexpr int kQFold = 2;                           // tiles folded ahead of the rescan
-constexpr int kQRing = 4;                           // prefix and warp-total ring (>= kQFold + 2)
+constexpr int kQFold = 3;                           // tiles folded ahead of the rescan
+constexpr int kQRing = 5;                           // prefix and warp-total ring (>= kQFold + 2)
 constexpr int kQMaxWin = 5;                         // look-back flags per lane: grids of up to 160 CTAs
 constexpr int kQMaxGrid = 32 * kQMaxWin;
 constexpr size_t kQSmem = (size_t)kQStages * kQTileBytes + 256;
@@ -580,33 +580,38 @@ __global__ void __launch_bounds__(kQThreads, 1)
     if (lane == 0) st.texcl = id;
     if (lane == 31) s_wt[j % kQRing][warp] = inc;
   };
-  // After the barrier that follows fold_math: the tile's aggregate goes out as its look-back flag.
+  // After the barrier that follows fold_math: the tile's aggregate goes out as its look-back flag, and the
+  // warp totals are replaced by their exclusive prefixes, which the tile's rescan reads one per warp.
   auto publish = [&](int64_t j, int64_t t) {
     if (threadIdx.x == 0) {
-      int32_t agg = id;
+      int32_t run = id;
 #pragma unroll
-      for (int w = 0; w < kQCWarps; ++w) agg = comb<OP>(agg, s_wt[j % kQRing][w]);
-      if (!(withhold && t == 0)) st_relaxed_u64(flags + t, make_flag(epoch, kFlagAgg, agg));
+      for (int w = 0; w < kQCWarps; ++w) {
+        const int32_t v = s_wt[j % kQRing][w];
+        s_wt[j % kQRing][w] = run;
+        run = comb<OP>(run, v);
+      }
+      if (!(withhold && t == 0)) st_relaxed_u64(flags + t, make_flag(epoch, kFlagAgg, run));
     }
   };
 
-  QFold A, B, C;
+  QFold st[kQFold + 1];  // st[0]: the tile to rescan next; st[i]: the tile folded i tiles after it
   int64_t j = 0;
   bool ok = true;
-  // prologue: fold the first kQFold tiles
-  for (int64_t jf = 0; jf < kQFold && jf < n_mine; ++jf) {
-    const int cnt = count_of(fc);
-    const int64_t t = fc.t;
-    fc.next(P, tiles_per_row);
-    const bool landed = tc::mbar_wait(&full[jf % kQStages], sphase(jf), wait_ns, s_abort);
-    int32_t v[kQRowChunks][4];
-    load_row(jf, cnt, v);
-    fold_math(jf, v, jf == 0 ? A : B);
-    if (named_bar_or(1, kQCompute, !landed || *s_abort)) {
-      ok = false;
-      break;
+  // prologue: fold the first kQFold tiles (unrolled, so the states stay in registers)
+#pragma unroll
+  for (int jf = 0; jf < kQFold; ++jf) {
+    if (ok && jf < n_mine) {
+      const int cnt = count_of(fc);
+      const int64_t t = fc.t;
+      fc.next(P, tiles_per_row);
+      const bool landed = tc::mbar_wait(&full[jf % kQStages], sphase(jf), wait_ns, s_abort);
+      int32_t v[kQRowChunks][4];
+      load_row(jf, cnt, v);
+      fold_math(jf, v, st[jf]);
+      if (named_bar_or(1, kQCompute, !landed || *s_abort)) ok = false;
+      else publish(jf, t);
     }
-    publish(jf, t);
   }
   // Steady state: iteration j folds tile j + kQFold (publishing its aggregate as early as possible), then
   // rescans tile j. One barrier per iteration; it also settles whether any warp's wait for the previous
@@ -624,7 +629,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
       good_f = tc::mbar_wait(&full[jf % kQStages], sphase(jf), wait_ns, s_abort);
       int32_t fv[kQRowChunks][4];
       load_row(jf, fcnt, fv);
-      fold_math(jf, fv, C);
+      fold_math(jf, fv, st[kQFold]);
     }
     if (named_bar_or(1, kQCompute, !good_f || !good_prev || *s_abort)) {
       ok = false;
@@ -639,17 +644,14 @@ __global__ void __launch_bounds__(kQThreads, 1)
     int32_t rv[kQRowChunks][4];
     load_row(j, rcnt, rv);
     const int32_t pre = s_prefix[j % kQRing];
-    int32_t wpre = id;
-#pragma unroll
-    for (int w = 0; w < kQCWarps; ++w)
-      if (w < warp) wpre = comb<OP>(wpre, s_wt[j % kQRing][w]);
-    const int32_t base = comb<OP>(comb<OP>(pre, wpre), A.texcl);
+    const int32_t wpre = s_wt[j % kQRing][warp];  // exclusive prefix of this warp's rows (see publish)
+    const int32_t base = comb<OP>(comb<OP>(pre, wpre), st[0].texcl);
     int4* wbuf = reinterpret_cast<int4*>(stage(j));
     const int nch = rcnt >> 2;
 #pragma unroll
     for (int i = 0; i < kQRowChunks; ++i) {
       const int g = kQRowChunks * r + ((i + R) & 3);
-      const int32_t p = comb<OP>(base, A.cp[i]);
+      const int32_t p = comb<OP>(base, st[0].cp[i]);
       int32_t o[4];
       if (exclusive) {
         o[0] = p;
@@ -675,8 +677,8 @@ __global__ void __launch_bounds__(kQThreads, 1)
       }
     }
     good_prev = wgood;
-    A = B;
-    B = C;
+#pragma unroll
+    for (int q = 0; q < kQFold; ++q) st[q] = st[q + 1];
   }
   if (!ok && threadIdx.x == 0) abort_from(j);
 }
