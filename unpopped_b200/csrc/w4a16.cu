@@ -8,23 +8,25 @@
 // (docs/accum-policies.md:8-20); this kernel is held to |got - exact_bf16| <= 1/2 ulp_bf16 + gamma * sum|x w s|.
 //
 // Design (swap-AB: the weight rows are the MMA's M = 128, the <= 16 activation rows its N = 16):
-//  * A unit of work is one k-block (128 k) of one 128-row tile of W. The N/128 x K/128 units are split
-//    evenly over one persistent CTA per SM (stream-K), so every SM streams the same share of W.
+//  * A unit of work is UK k-blocks (UK x 128 k; UK = 2 when K allows, else 1) of one 128-row tile of W. The
+//    units are split evenly over one persistent CTA per SM (stream-K), so every SM streams the same share of
+//    W. Each k-block keeps its own accumulator (its own group scale), but a unit's hand-offs between the roles
+//    are paid once for UK k-blocks: measured, these hand-offs, not the data or the math, set the unit's time.
 //  * warps 0..15 (dequant): warp w owns TMEM lane quarter w % 4 and k-quarter w / 4, so thread (w, lane)
-//    owns row 32 (w % 4) + lane of the tile and 32 k of every unit: 16 bytes of W, which it loads straight
-//    into registers kPrefetch units ahead of use (no shared-memory round trip). It turns the nibbles into
+//    owns row 32 (w % 4) + lane of the tile and 32 UK k of every unit: 16 UK bytes of W, which it loads
+//    straight into registers several units ahead of use (no shared-memory round trip). It turns the nibbles into
 //    exact bf16 (one prmt, one lop3 and one bf16x2 subtract per pair) and stores them into tensor memory
 //    (tcgen05.st), where they are the MMA's A operand.
 //  * warps 16..19 (MMA issuers): a single thread issues only about one tcgen05.mma per ~100 cycles, so four
-//    threads share the eight k-steps of a unit as a pipeline: issuer g runs the two k-steps of k-quarter g
-//    into the unit's accumulator after issuer g - 1 has issued its own (an mbarrier hand-off between
-//    tcgen05.fence::before_thread_sync and ::after_thread_sync orders them), so each unit ends in one
-//    accumulator while several units are in issue at once. (Four separate accumulators per unit were measured
+//    threads share a unit's 8 UK k-steps as pipelines: issuer g runs the 2 UK k-steps of k-quarter g into
+//    its k-block's accumulator after the issuer before it in that k-block has issued its own (an mbarrier
+//    hand-off between tcgen05.fence::before_thread_sync and ::after_thread_sync orders them), so each
+//    k-block ends in one accumulator while several units are in issue at once. (Four separate accumulators per unit were measured
 //    slower: the epilogue's reads of four times the tensor-memory data cost more than the hand-offs.)
-//  * warp 24 (activation loader): one thread brings each unit's [16 x 128] activation tile into a ring of
-//    shared-memory stages with two TMA boxes, 128-byte swizzled as the MMA reads it; rows past M read as 0.
-//  * warps 20..23 (epilogue): read the unit's accumulator (tcgen05.ld), scale it by scale[n][k-block] in f32
-//    and accumulate in registers. A tile finished inside one CTA is written as bf16;
+//  * warp 24 (activation loader): one thread brings each unit's [16 x 128 UK] activation tile into a ring of
+//    shared-memory stages with 2 UK TMA boxes, 128-byte swizzled as the MMA reads it; rows past M read as 0.
+//  * warps 20..23 (epilogue): read the unit's accumulators (tcgen05.ld), scale each by scale[n][k-block] in
+//    f32 and accumulate in registers, k-block by k-block. A tile finished inside one CTA is written as bf16;
 //    a tile split between CTAs writes f32 partials, and whichever CTA finishes it last (an atomic count)
 //    sums them in CTA order, writes bf16 and clears the partials — no CTA ever waits on another.
 // Every mbarrier wait is bounded; a wait that runs out sets the workspace error word and the CTA unwinds.
@@ -49,24 +51,32 @@ constexpr int kIssuers = 4;                      // warps 16..19
 constexpr int kEpiWarps = 4;                     // warps 20..23
 constexpr int kIss0 = kDqWarps, kEpi0 = kIss0 + kIssuers, kXWarp = kEpi0 + kEpiWarps;
 constexpr int kThreads = 32 * (kXWarp + 1);      // 800
-constexpr int kPrefetch = 4;                     // units of W a dequant thread has in flight
 constexpr int kScaleAhead = 4;                   // units an epilogue thread's scale loads run ahead
 constexpr uint32_t kSleepNs = 64;                // pause between polls of a waiting dequant/epilogue/loader warp
-constexpr int kXBytes = kMmaN * kKB * 2;         // 4 KiB of bf16 per unit: two 128-byte-swizzled boxes of 64 k
-constexpr int kXStages = 8;
-constexpr int kRing = 6;                         // units in flight between dequant, MMA and epilogue
+constexpr int kXBytes = kMmaN * kKB * 2;         // 4 KiB of bf16 per k-block: two 128-byte-swizzled boxes of 64 k
 constexpr int kTmemCols = 512;
-constexpr int kACol0 = 0;                        // A (dequantized W): kRing x 64 columns
-constexpr int kDCol0 = kRing * 64;               // accumulators: kRing units x 16 columns
-// mbarriers: x_full, x_empty [kXStages]; a_full [kRing][4]; mma_done, d_empty [kRing]; hand [kIssuers-1][kRing];
-// seg_in, seg_out;
-// then the TMEM address word, the abort word and the fix-up verdict
-constexpr int kNumBars = 2 * kXStages + 4 * kRing + 2 * kRing + (kIssuers - 1) * kRing + 2;
+
+// The layout for units of UK k-blocks.
+template <int UK>
+struct Cfg {
+  static constexpr int kACols = 64 * UK;               // A (dequantized W) columns per unit
+  static constexpr int kDCols = kMmaN * UK;            // accumulator columns per unit: one 16-column block per k-block
+  static constexpr int kRing = UK == 1 ? 6 : 3;        // units in flight between dequant, MMA and epilogue
+  static constexpr int kACol0 = 0;
+  static constexpr int kDCol0 = kRing * kACols;
+  static constexpr int kXUnit = kXBytes * UK;          // activation bytes per unit
+  static constexpr int kXStages = 8 / UK;              // 32 KiB of activation stages either way
+  static constexpr int kChain = kIssuers / UK;         // issuers chained into one k-block's accumulator
+  static constexpr int kPrefetch = 4 / UK;             // units of W a dequant thread has in flight (64 bytes)
+  // mbarriers: x_full, x_empty [kXStages]; a_full [kRing][4]; mma_done, d_empty [kRing]; hand [kIssuers][kRing];
+  // seg_in, seg_out; then the TMEM address word, the abort word and the fix-up verdict
+  static constexpr int kNumBars = 2 * kXStages + 4 * kRing + 2 * kRing + kIssuers * kRing + 2;
+  static_assert(kDCol0 + kRing * kDCols <= kTmemCols, "tensor memory");
+};
 constexpr int kBarBytes = 1024;
-static_assert(kNumBars * 8 + 12 <= kBarBytes, "barrier region");
-constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + (size_t)kXStages * kXBytes + kBarBytes;
+static_assert(Cfg<1>::kNumBars * 8 + 12 <= kBarBytes && Cfg<2>::kNumBars * 8 + 12 <= kBarBytes, "barrier region");
+constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + (size_t)8 * kXBytes + kBarBytes;
 static_assert(kEpi0 % 4 == 0, "epilogue warp e reads TMEM lane quarter e % 4");
-static_assert(kDCol0 + kRing * kMmaN <= kTmemCols, "tensor memory");
 
 struct WsHeader {
   uint32_t ticket, done, epoch, error;  // same layout as the scan workspace: `error` at byte 12
@@ -97,49 +107,59 @@ __device__ __forceinline__ uint32_t nib2_to_bf16x2(uint32_t q, uint32_t q4, int 
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-// Position of a unit (tile t, k-block kb, scale-group index gi = kb*128/group) advanced one unit at a time
-// with additions only: 64-bit division and modulo are emulated in software and would dominate the loops.
+// Position of a unit of UK k-blocks (tile t, first k-block kb, scale-group index gi = kb*128/group) advanced
+// one unit at a time with additions only: 64-bit division and modulo are emulated in software and would
+// dominate the loops. G (k-blocks per tile) is a multiple of UK.
+template <int UK>
 struct UnitCursor {
   int t, kb, sub, gi;  // sub = kb % (group / 128)
   __device__ __forceinline__ void init(int64_t u, int64_t G, int kpg) {
-    t = (int)(u / G);
-    kb = (int)(u - (int64_t)t * G);
+    const int64_t GU = G / UK;
+    t = (int)(u / GU);
+    kb = (int)(u - (int64_t)t * GU) * UK;
     gi = kb / kpg;
     sub = kb - gi * kpg;
   }
   __device__ __forceinline__ void next(int G, int kpg) {
-    if (++kb == G) {
+    kb += UK;
+    if (kb == G) {
       kb = 0;
       sub = 0;
       gi = 0;
       ++t;
-    } else if (++sub == kpg) {
-      sub = 0;
-      ++gi;
+      return;
     }
+#pragma unroll
+    for (int h = 0; h < UK; ++h)
+      if (++sub == kpg) {
+        sub = 0;
+        ++gi;
+      }
   }
+  // scale-group index of k-block kb + h of the unit
+  __device__ __forceinline__ int gi_at(int h, int kpg) const { return gi + (sub + h) / kpg; }
 };
 
-// The end of a tile segment [seg_kb0, kb] in the epilogue (all kEpiWarps epilogue warps reach it together):
+// The end of a tile segment in the epilogue (all kEpiWarps epilogue warps reach it together):
 // a whole tile is written as bf16. For a tile split between CTAs, each epilogue thread publishes its row's
 // 16 f32 partials; the epilogue warps meet on an mbarrier (seg_in, one arrival per warp), one thread counts
 // this CTA in and announces whether it completed the count (seg_out); in the CTA that did, every epilogue
 // thread sums its own row over the contributing CTAs in CTA order (a segment's loads issued together),
 // writes bf16 and clears the partials. `nfix` counts this warp's split-tile ends (the barriers' phase).
 // Both waits are bounded; false means the CTA is giving up.
-__device__ __forceinline__ bool finish_segment(const float (&acc)[kMmaN], int64_t t, int64_t seg_kb0, int64_t kb,
-                                               int r, int lane, int M, int64_t N, int64_t U, int64_t G, int64_t P,
-                                               int64_t S_max, uint16_t* out, uint32_t* counters, float* partials,
-                                               uint64_t* seg_in, uint64_t* seg_out, volatile uint32_t* s_last,
-                                               uint32_t& nfix, uint64_t wait_ns, volatile int* abort_flag) {
+__device__ __forceinline__ bool finish_segment(const float (&acc)[kMmaN], int64_t t, bool whole, int r, int lane,
+                                               int M, int64_t N, int64_t U, int64_t GU, int64_t P, int64_t S_max,
+                                               uint16_t* out, uint32_t* counters, float* partials, uint64_t* seg_in,
+                                               uint64_t* seg_out, volatile uint32_t* s_last, uint32_t& nfix,
+                                               uint64_t wait_ns, volatile int* abort_flag) {
   const int64_t n = t * kTileN + r;
-  if (seg_kb0 == 0 && kb == G - 1) {
+  if (whole) {
 #pragma unroll
     for (int m = 0; m < kMmaN; ++m)
       if (m < M && n < N) out[(int64_t)m * N + n] = __bfloat16_as_ushort(__float2bfloat16_rn(acc[m]));
     return true;
   }
-  const int64_t c0 = cta_of_unit(t * G, U, P), c1 = cta_of_unit(t * G + G - 1, U, P);
+  const int64_t c0 = cta_of_unit(t * GU, U, P), c1 = cta_of_unit(t * GU + GU - 1, U, P);
   const int64_t nseg = c1 - c0 + 1, sidx = (int64_t)blockIdx.x - c0;
   float* tile_parts = partials + t * S_max * kMmaN * kTileN;
 #pragma unroll
@@ -180,21 +200,24 @@ __device__ __forceinline__ bool finish_segment(const float (&acc)[kMmaN], int64_
   return true;
 }
 
+template <int UK>
 __global__ void __launch_bounds__(kThreads, 1)
     w4a16_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ w,
                  const __half* __restrict__ scale, uint16_t* __restrict__ out, int M, int64_t N, int64_t K,
                  int64_t group, int64_t U, int64_t G, int64_t S_max, WsHeader* hdr, uint32_t* counters,
                  float* partials, uint64_t wait_ns) {
+  using C = Cfg<UK>;
+  constexpr int kRing = C::kRing, kXStages = C::kXStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* xs = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* x_full = reinterpret_cast<uint64_t*>(xs + (size_t)kXStages * kXBytes);  // [kXStages]: TMA landed
-  uint64_t* x_empty = x_full + kXStages;        // [kXStages]: the stage's MMAs completed (last issuer's commit)
+  uint64_t* x_full = reinterpret_cast<uint64_t*>(xs + (size_t)kXStages * C::kXUnit);  // [kXStages]: TMA landed
+  uint64_t* x_empty = x_full + kXStages;        // [kXStages]: the stage's MMAs completed (chain ends' commits)
   uint64_t* a_full = x_empty + kXStages;        // [kRing][4]: k-quarter q of the unit's A is in TMEM (4 warps)
   uint64_t* mma_done = a_full + 4 * kRing;      // [kRing]: all of the unit's MMAs completed
-  uint64_t* d_empty = mma_done + kRing;         // [kRing]: the epilogue has read the unit's accumulator
-  uint64_t* hand = d_empty + kRing;             // [kIssuers - 1][kRing]: issuer g has issued the unit's k-quarter g
-  uint64_t* seg_in = hand + (kIssuers - 1) * kRing;  // split-tile end: every epilogue warp has published
-  uint64_t* seg_out = seg_in + 1;                     // split-tile end: the count verdict is in s_last
+  uint64_t* d_empty = mma_done + kRing;         // [kRing]: the epilogue has read the unit's accumulators
+  uint64_t* hand = d_empty + kRing;             // [kIssuers][kRing]: issuer g has issued the unit's k-quarter g
+  uint64_t* seg_in = hand + kIssuers * kRing;   // split-tile end: every epilogue warp has published
+  uint64_t* seg_out = seg_in + 1;               // split-tile end: the count verdict is in s_last
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(seg_out + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile uint32_t* s_last = reinterpret_cast<volatile uint32_t*>(tmem_slot + 2);  // split-tile fix-up verdict
@@ -208,13 +231,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kXStages; ++s) {
       tc::mbar_init(&x_full[s], 1);
-      tc::mbar_init(&x_empty[s], 1);
+      tc::mbar_init(&x_empty[s], UK);
     }
     for (int a = 0; a < kRing; ++a) {
       for (int q = 0; q < 4; ++q) tc::mbar_init(&a_full[4 * a + q], 4);
-      tc::mbar_init(&mma_done[a], 1);
+      tc::mbar_init(&mma_done[a], UK);
       tc::mbar_init(&d_empty[a], kEpiWarps);
-      for (int g = 0; g + 1 < kIssuers; ++g) tc::mbar_init(&hand[g * kRing + a], 1);
+      for (int g = 0; g < kIssuers; ++g) tc::mbar_init(&hand[g * kRing + a], 1);
     }
     tc::mbar_init(seg_in, kEpiWarps);
     tc::mbar_init(seg_out, 1);
@@ -241,25 +264,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = lq * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(lq * 32) << 16;
     const int64_t wrow = K / 2;
-    UnitCursor cl;
+    UnitCursor<UK> cl;
     cl.init(lo, G, kpg);
-    auto load_w = [&]() {  // this thread's 16 bytes of the unit at cl, then advance cl
+    // this thread's 16 UK bytes of the unit at cl (k-quarter kq of its 128 UK k), then advance cl
+    auto load_w = [&](uint4 (&v)[UK]) {
       const int64_t n = (int64_t)cl.t * kTileN + r;
-      const uint4 v = n < N ? ld_nc_na_v4(w + n * wrow + (int64_t)cl.kb * (kKB / 2) + kq * 16) : make_uint4(0, 0, 0, 0);
+      const uint8_t* src = w + n * wrow + (int64_t)cl.kb * (kKB / 2) + kq * 16 * UK;
+#pragma unroll
+      for (int h = 0; h < UK; ++h) v[h] = n < N ? ld_nc_na_v4(src + 16 * h) : make_uint4(0, 0, 0, 0);
       cl.next(Gi, kpg);
-      return v;
     };
-    uint4 wq[kPrefetch];
+    uint4 wq[C::kPrefetch][UK];
 #pragma unroll
-    for (int u = 0; u < kPrefetch; ++u) wq[u] = u < n_units ? load_w() : make_uint4(0, 0, 0, 0);
+    for (int u = 0; u < C::kPrefetch; ++u) {
+      if (u < n_units) load_w(wq[u]);
+      else
+#pragma unroll
+        for (int h = 0; h < UK; ++h) wq[u][h] = make_uint4(0, 0, 0, 0);
+    }
     bool ok = true;
-    for (int64_t i0 = 0; ok && i0 < n_units; i0 += kPrefetch) {
+    for (int64_t i0 = 0; ok && i0 < n_units; i0 += C::kPrefetch) {
 #pragma unroll
-      for (int u = 0; u < kPrefetch; ++u) {
+      for (int u = 0; u < C::kPrefetch; ++u) {
         const int64_t i = i0 + u;
         if (i >= n_units) break;
-        const uint4 cur = wq[u];
-        if (i + kPrefetch < n_units) wq[u] = load_w();
+        uint4 cur[UK];
+#pragma unroll
+        for (int h = 0; h < UK; ++h) cur[h] = wq[u][h];
+        if (i + C::kPrefetch < n_units) load_w(wq[u]);
         const int a = (int)(i % kRing);
         const uint32_t aph = (uint32_t)((i / kRing) & 1);
         // the A stage is free once the unit kRing earlier has been multiplied
@@ -269,15 +301,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        uint32_t regs[16];
-        const uint32_t wd[4] = {cur.x, cur.y, cur.z, cur.w};
 #pragma unroll
-        for (int wi = 0; wi < 4; ++wi) {
-          const uint32_t q4 = wd[wi] >> 4;
+        for (int h = 0; h < UK; ++h) {
+          uint32_t regs[16];
+          const uint32_t wd[4] = {cur[h].x, cur[h].y, cur[h].z, cur[h].w};
 #pragma unroll
-          for (int p = 0; p < 4; ++p) regs[4 * wi + p] = nib2_to_bf16x2(wd[wi], q4, p);
+          for (int wi = 0; wi < 4; ++wi) {
+            const uint32_t q4 = wd[wi] >> 4;
+#pragma unroll
+            for (int p = 0; p < 4; ++p) regs[4 * wi + p] = nib2_to_bf16x2(wd[wi], q4, p);
+          }
+          tc::st_32x32b_x16(tmem + lane_addr + C::kACol0 + a * C::kACols + 16 * (UK * kq + h), regs);
         }
-        tc::st_32x32b_x16(tmem + lane_addr + kACol0 + a * 64 + 16 * kq, regs);
         tc::wait_st();
         tc::fence_before_sync();
         __syncwarp();
@@ -285,38 +320,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp < kEpi0) {
-    // ---------------- MMA issuers: issuer g runs k-steps 2g, 2g+1 (k-quarter g) of every unit ----------------
+    // ------- MMA issuers: issuer g runs the 2 UK k-steps of k-quarter g, in its k-block's chain -------
     const int g = warp - kIss0;
+    const int hk = (UK * g) / 4;          // the k-block (accumulator) of this issuer's k-steps
+    const int pos = g % C::kChain;        // place in that k-block's chain
     if (lane == 0) {
       constexpr uint32_t idesc = tc::idesc_bf16_f32(kTileN, kMmaN);
       int64_t issued = 0;
       for (int64_t i = 0; i < n_units; ++i) {
         const int a = (int)(i % kRing), s = (int)(i % kXStages);
         const uint32_t rph = (uint32_t)((i / kRing) & 1), xph = (uint32_t)((i / kXStages) & 1);
-        // issuer 0 starts the accumulator once the epilogue has read its previous unit; issuer g > 0 adds to it
-        // after issuer g - 1
+        // the first issuer of a chain starts the accumulator once the epilogue has read the slot's previous
+        // unit; the others add to it after the issuer before them
         const bool ready = tc::mbar_wait(&a_full[4 * a + g], rph, wait_ns, abort_flag) &&
                            tc::mbar_wait(&x_full[s], xph, wait_ns, abort_flag) &&
-                           (g == 0 ? tc::mbar_wait(&d_empty[a], rph ^ 1u, wait_ns, abort_flag)
-                                   : tc::mbar_wait(&hand[(g - 1) * kRing + a], rph, wait_ns, abort_flag));
+                           (pos == 0 ? tc::mbar_wait(&d_empty[a], rph ^ 1u, wait_ns, abort_flag)
+                                     : tc::mbar_wait(&hand[(g - 1) * kRing + a], rph, wait_ns, abort_flag));
         if (!ready) {
           give_up();
           break;
         }
         tc::fence_after_sync();
-        const uint32_t xaddr = tc::smem_u32(xs + (size_t)s * kXBytes);
+        const uint32_t xaddr = tc::smem_u32(xs + (size_t)s * C::kXUnit);
 #pragma unroll
-        for (int jj = 0; jj < 2; ++jj) {
-          const int j = 2 * g + jj;  // k-step: 16 k = 32 bytes of a 128-byte swizzle atom row
+        for (int jj = 0; jj < 2 * UK; ++jj) {
+          const int j = 2 * UK * g + jj;  // k-step: 16 k = 32 bytes of a 128-byte swizzle atom row
           const uint64_t bdesc = tc::sdesc_kmajor_sw128(xaddr + (uint32_t)((j >> 2) * 2048 + (j & 3) * 32));
-          tc::mma_ts_bf16(tmem + kDCol0 + a * kMmaN, tmem + kACol0 + a * 64 + j * 8, bdesc, idesc,
-                          (g > 0 || jj > 0) ? 1u : 0u);
+          tc::mma_ts_bf16(tmem + C::kDCol0 + a * C::kDCols + hk * kMmaN, tmem + C::kACol0 + a * C::kACols + j * 8,
+                          bdesc, idesc, (pos > 0 || jj > 0) ? 1u : 0u);
         }
-        if (g + 1 < kIssuers) {
+        if (pos + 1 < C::kChain) {
           tc::fence_before_sync();
           tc::mbar_arrive(&hand[g * kRing + a]);
         } else {
-          // the unit's MMAs run in issue order, so the last issuer's completing covers all of them
+          // a chain's MMAs run in issue order, so its last issuer's completing covers all of them
           tc::commit(&mma_done[a]);
           tc::commit(&x_empty[s]);
         }
@@ -334,19 +371,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = lq * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(lq * 32) << 16;
     const int64_t gpr = K / group;  // scales per row
-    UnitCursor ce, cs;  // the unit being finished, the unit whose scale is loaded next
+    const int64_t GU = G / UK;      // units per tile
+    UnitCursor<UK> ce, cs;          // the unit being finished, the unit whose scales are loaded next
     ce.init(lo, G, kpg);
     cs = ce;
-    auto load_scale = [&]() {  // raw f16 bits of this row's scale for the unit at cs, then advance cs
+    // raw f16 bits of this row's scales for the unit at cs, k-block h in bits 16h .. 16h+15; then advance cs
+    auto load_scales = [&]() {
       const int64_t n = (int64_t)cs.t * kTileN + r;
-      const unsigned short v = n < N ? __ldg(reinterpret_cast<const unsigned short*>(scale) + n * gpr + cs.gi) : 0;
+      uint32_t v = 0;
+#pragma unroll
+      for (int h = 0; h < UK; ++h)
+        if (n < N) v |= (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(scale) + n * gpr + cs.gi_at(h, kpg))
+                        << (16 * h);
       cs.next(Gi, kpg);
       return v;
     };
     // scales are loaded kScaleAhead units before use, so their latency hides behind the units in between
-    unsigned short sq[kScaleAhead];
+    uint32_t sq[kScaleAhead];
 #pragma unroll
-    for (int u = 0; u < kScaleAhead; ++u) sq[u] = u < n_units ? load_scale() : 0;
+    for (int u = 0; u < kScaleAhead; ++u) sq[u] = u < n_units ? load_scales() : 0u;
     float acc[kMmaN];
 #pragma unroll
     for (int j = 0; j < kMmaN; ++j) acc[j] = 0.f;
@@ -355,10 +398,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int64_t e = 0; e < n_units; ++e) {
       const int d = (int)(e % kRing);
       const uint32_t dph = (uint32_t)((e / kRing) & 1);
-      const float sc = __half2float(__ushort_as_half(sq[0]));
+      float sc[UK];
+#pragma unroll
+      for (int h = 0; h < UK; ++h) sc[h] = __half2float(__ushort_as_half((unsigned short)(sq[0] >> (16 * h))));
 #pragma unroll
       for (int u = 0; u + 1 < kScaleAhead; ++u) sq[u] = sq[u + 1];
-      sq[kScaleAhead - 1] = e + kScaleAhead < n_units ? load_scale() : 0;
+      sq[kScaleAhead - 1] = e + kScaleAhead < n_units ? load_scales() : 0u;
       const bool good = tc::mbar_wait_sleepy(&mma_done[d], dph, wait_ns, abort_flag, kSleepNs);
       if (!__all_sync(0xffffffffu, good)) {
         give_up();
@@ -371,30 +416,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < kMmaN; ++j) acc[j] = 0.f;
       }
-      {
+#pragma unroll
+      for (int h = 0; h < UK; ++h) {  // k-block by k-block, in k order
         uint32_t dv[kMmaN];
-        tc::ld_32x32b_x16(tmem + lane_addr + kDCol0 + d * kMmaN, dv);
+        tc::ld_32x32b_x16(tmem + lane_addr + C::kDCol0 + d * C::kDCols + h * kMmaN, dv);
         tc::wait_ld();
 #pragma unroll
-        for (int j = 0; j < kMmaN; ++j) acc[j] = fmaf(sc, __uint_as_float(dv[j]), acc[j]);
+        for (int j = 0; j < kMmaN; ++j) acc[j] = fmaf(sc[h], __uint_as_float(dv[j]), acc[j]);
       }
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&d_empty[d]);
       ce.next(Gi, kpg);
       const int64_t u = lo + e;
-      if (u + 1 == hi || kb == G - 1)  // the segment [seg_kb0, kb] of tile t ends here
-        if (!finish_segment(acc, t, seg_kb0, kb, r, lane, M, N, U, G, P, S_max, out, counters, partials, seg_in,
-                            seg_out, s_last, nfix, wait_ns, abort_flag)) {
+      if (u + 1 == hi || kb + UK == G)  // the segment [seg_kb0, kb + UK) of tile t ends here
+        if (!finish_segment(acc, t, seg_kb0 == 0 && kb + UK == G, r, lane, M, N, U, GU, P, S_max, out, counters,
+                            partials, seg_in, seg_out, s_last, nfix, wait_ns, abort_flag)) {
           give_up();
           break;
         }
     }
   } else {
-    // ---------------- activation loader: two TMA boxes per unit ----------------
+    // ---------------- activation loader: 2 UK TMA boxes per unit ----------------
     if (lane == 0) {
       tc::tma_prefetch_desc(&xmap);
-      UnitCursor cx;
+      UnitCursor<UK> cx;
       cx.init(lo, G, kpg);
       int64_t issued = 0;
       for (int64_t i = 0; i < n_units; ++i) {
@@ -403,10 +449,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           give_up();
           break;
         }
-        uint8_t* dst = xs + (size_t)s * kXBytes;
-        tc::mbar_arrive_expect_tx(&x_full[s], kXBytes);
-        tc::tma_load_2d(dst, &xmap, &x_full[s], cx.kb * kKB, 0);
-        tc::tma_load_2d(dst + kXBytes / 2, &xmap, &x_full[s], cx.kb * kKB + kKB / 2, 0);
+        uint8_t* dst = xs + (size_t)s * C::kXUnit;
+        tc::mbar_arrive_expect_tx(&x_full[s], C::kXUnit);
+#pragma unroll
+        for (int bx = 0; bx < 2 * UK; ++bx)
+          tc::tma_load_2d(dst + bx * (kXBytes / 2), &xmap, &x_full[s], cx.kb * kKB + bx * (kKB / 2), 0);
         cx.next(Gi, kpg);
         issued = i + 1;
       }
@@ -431,7 +478,7 @@ static int64_t host_cta_of_unit(int64_t u, int64_t U, int64_t P) {
 }
 
 struct Plan {
-  int64_t tiles, G, U, P, S_max;
+  int64_t tiles, G, UK, GU, U, P, S_max;  // G k-blocks per tile, UK k-blocks per unit, GU units per tile
   size_t counters_off, partials_off, bytes;
 };
 
@@ -439,12 +486,15 @@ static Plan make_plan(int64_t n, int64_t k) {
   Plan p{};
   p.tiles = (n + kTileN - 1) / kTileN;
   p.G = k / kKB;
-  p.U = p.tiles * p.G;
+  p.UK = (p.G % 2 == 0) ? 2 : 1;
+  p.GU = p.G / p.UK;
+  p.U = p.tiles * p.GU;
   p.P = p.U < sm_count() ? p.U : sm_count();
   if (p.P < 1) p.P = 1;
   p.S_max = 1;
   for (int64_t t = 0; t < p.tiles && p.U > 0; ++t) {
-    const int64_t ns = host_cta_of_unit(t * p.G + p.G - 1, p.U, p.P) - host_cta_of_unit(t * p.G, p.U, p.P) + 1;
+    const int64_t ns =
+        host_cta_of_unit(t * p.GU + p.GU - 1, p.U, p.P) - host_cta_of_unit(t * p.GU, p.U, p.P) + 1;
     if (ns > p.S_max) p.S_max = ns;
   }
   p.counters_off = sizeof(WsHeader);
@@ -512,7 +562,9 @@ extern "C" int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, cons
     static bool attr_set[64] = {false};
     std::lock_guard<std::mutex> lk(mu);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-      e = cudaFuncSetAttribute(w4a16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+      e = cudaFuncSetAttribute(w4a16_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(w4a16_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
       if (e != cudaSuccess) return cuda_status(e);
       if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
@@ -522,9 +574,10 @@ extern "C" int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, cons
   auto* counters = reinterpret_cast<uint32_t*>(base + p.counters_off);
   auto* partials = reinterpret_cast<float*>(base + p.partials_off);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  w4a16_kernel<<<(unsigned)p.P, kThreads, kSmemBytes, s>>>(xmap, w, reinterpret_cast<const __half*>(scale), out,
-                                                          (int)m, n, k, group, p.U, p.G, p.S_max, hdr, counters,
-                                                          partials, wait_limit_ns());
+  auto kern = p.UK == 2 ? w4a16_kernel<2> : w4a16_kernel<1>;
+  kern<<<(unsigned)p.P, kThreads, kSmemBytes, s>>>(xmap, w, reinterpret_cast<const __half*>(scale), out, (int)m, n, k,
+                                                   group, p.U, p.G, p.S_max, hdr, counters, partials,
+                                                   wait_limit_ns());
   note_launch();
   return check_launch();
 }
