@@ -6,8 +6,9 @@ Headline (`value`): the inclusive add-scan over 2^28 int32 (the benchmark's conf
 look-back pass per step, inputs resident in HBM, L2 flushed between steps, CUDA events on the launching
 stream, max over ranks. With N GPUs every rank scans its own 2^28 shard of an N x 2^28 array (weak scaling):
 local fold, an NCCL all-gather of the N shard totals, then the single-pass scan seeded with the carry.
-`e2e`: the same scan through the C ABI with the input copied in from pinned host memory and the result copied
-back inside the timed region. `lifts`: every other configuration (row sum, max+argmax, Zipf gather, int4
+`e2e`: the same scan through the C ABI from pinned host memory, copies inside the timed region: at N=1 the
+host-buffer entry (up_sm100_scan_i32_host, copy-in, scan and copy-out overlapped chunk by chunk); at N>1 the
+shard is copied in whole (the carry needs every shard's total), scanned, and copied back. `lifts`: every other configuration (row sum, max+argmax, Zipf gather, int4
 dequant, W4A16) measured the same way in the same run. `roofline`: the scan kernel's algorithmic bytes over
 its event-timed duration against the measured copy bandwidth. `cpu_baseline`: the oracle restatement timed
 on the host cores (rank 0, N=1 only).
@@ -145,12 +146,14 @@ class Ctx:
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
-    def timed(self, step, K, W, inner=False):
+    def timed(self, step, K, W, inner=False, head_start=True):
         """W warm-up steps, then EXACTLY K steps between one pair of events on the launching stream, with a
         barrier + synchronize on both sides. `step(i, kin)` runs step i; callers rotate through enough input
         copies that every step's inputs are colder than the 126 MB L2 (no flush inside the timed region). A GPU
         sleep before the start event lets the host enqueue all K steps ahead of the device, so the events time
-        device work only. With `inner`, the step appends (start, end) events of its dominant kernel to `kin`.
+        device work only; a step that blocks the host (a host-buffer call) takes head_start=False, so the events
+        bracket its whole duration. With `inner`, the step appends (start, end) events of its dominant kernel to
+        `kin`.
         Returns (ms per step, max over ranks; mean inner-kernel ms; our kernel launches in the timed region)."""
         from unpopped_b200 import ops
 
@@ -163,7 +166,8 @@ class Ctx:
         kin = [] if inner else None
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         l0 = ops.launch_count()
-        torch.cuda._sleep(self.sleep_cycles + K * 200_000)  # ~0.1 ms per step of head start for the host
+        if head_start:
+            torch.cuda._sleep(self.sleep_cycles + K * 200_000)  # ~0.1 ms per step of head start for the host
         a.record()
         for i in range(K):
             step(i, kin)
@@ -386,6 +390,12 @@ def profile_cases(which: str):
         o = torch.empty(x.shape[0], device=dev)
         return lambda: ops.row_sum(x, "f32", out=o)
 
+    @case("rowsum_auto")
+    def _():
+        x = wl.rowsum_input(device=dev)
+        o = torch.empty(x.shape[0], device=dev)
+        return lambda: ops.row_sum(x, "auto", block=1024, out=o)
+
     @case("argmax")
     def _():
         x = wl.argmax_input(rows=8192, device=dev)
@@ -426,7 +436,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--lifts", default="all", choices=["all", "none"])
     ap.add_argument("--profile", default=None,
-                    help="run only the small ncu case of one lift (scan, rowsum, argmax, gather, dequant, w4a16, all)")
+                    help="run only the small ncu case of one lift (scan, rowsum, rowsum_auto, argmax, gather, dequant, w4a16, all)")
     args = ap.parse_args()
     if args.profile:
         profile_cases(args.profile)
@@ -459,14 +469,21 @@ def main():
     # ---- e2e through the C ABI from pinned host memory (copies inside the timed region) ----
     xh = x.cpu().pin_memory()
     yh = torch.empty_like(xh).pin_memory()
-
-    def e2e_step(i, kin):
-        x.copy_(xh, non_blocking=True)
-        step(i, None)
-        yh.copy_(y, non_blocking=True)
-    e_ms, _, _ = ctx.timed(e2e_step, max(3, K // 4), 1)
+    if ctx.world == 1:
+        # the host-buffer entry: chunks stream through the device with copy-in, scan and copy-out overlapped
+        def e2e_step(i, kin):
+            ops.scan_host(xh, "sum", out=yh)
+        api = "up_sm100_scan_i32_host (pinned host buffers, copies overlapped with the scan)"
+    else:
+        # sharded: the carry needs every shard's total first, so the shard is copied in whole
+        def e2e_step(i, kin):
+            x.copy_(xh, non_blocking=True)
+            step(i, None)
+            yh.copy_(y, non_blocking=True)
+        api = "copy in, sharded up_sm100_scan_i32 (reduce, all-gather of totals, scan), copy out"
+    e_ms, _, _ = ctx.timed(e2e_step, max(3, K // 4), 3, head_start=ctx.world > 1)
     e2e = {"value": round(ctx.world * nbytes / (e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-           "h2d_bytes_per_step": xh.numel() * 4, "d2h_bytes_per_step": yh.numel() * 4}
+           "h2d_bytes_per_step": xh.numel() * 4, "d2h_bytes_per_step": yh.numel() * 4, "api": api}
     del xh, yh, x, y
     torch.cuda.empty_cache()
 

@@ -242,6 +242,17 @@ UP_API int up_sm100_scan_i32_noalloc(const int32_t* x, int32_t* y, int64_t rows,
                                      int exclusive, int reverse, const int32_t* carry_in, int sync,
                                      void* stream);
 
+/* No counterpart in the reference as a device entry: up_sm100_scan_i32 over HOST buffers, the buffers the
+ * reference's own scan evaluation reads and writes (crates/unpopped/src/oracle/plan_window.rs:10-238). The
+ * array streams through a ring of device slots on three streams (copy in, scan, copy out), so both
+ * directions of the host link and the scan overlap; pinned host memory gives the full copy rate. Rows longer
+ * than a slot are cut along the row with the carry derived on the device. `carry_in`: HOST pointer to one
+ * int32, or NULL. Blocks until `y` is written. The first call on each device allocates the slots (256 MiB)
+ * and its streams, and keeps them; calls are serialized. Returns UP_ERR_DEVICE_TIMEOUT when a bounded
+ * device wait ran out. */
+UP_API int up_sm100_scan_i32_host(const int32_t* x, int32_t* y, int64_t rows, int64_t k, int op, int exclusive,
+                                  int reverse, const int32_t* carry_in);
+
 /* Fold of a whole int32 array to one value (the first pass of a scan sharded over GPUs): SUM (wrapping),
  * MAX or MIN, written to `total` (device, one int32). Deterministic. */
 UP_API int up_sm100_reduce_i32(const int32_t* x, int64_t n, int op, int32_t* total, void* stream);

@@ -60,6 +60,56 @@ def test_auto_sum_bit_exact_vs_oracle(rows, cols, block):
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
+@pytest.mark.parametrize("rows,cols,stride", [(7, 9000, 9000), (5, 1000, 1004), (1, 4096, 4096),
+                                              (3000, 520, 520), (611, 20000, 20480)])
+@pytest.mark.parametrize("block", [128, 256, 512, 1024])
+def test_auto_sum_row_sets_bit_exact(rows, cols, stride, block):
+    """Float4 rows at every block of 128 and up: rows shorter and longer than 8 * block (a thread's group
+    of eight loads partial or repeated), row counts that leave a CTA's row set partial, row strides wider
+    than the row."""
+    rng = np.random.default_rng(rows + cols + block)
+    full = (rng.standard_normal((rows, stride)) * 10.0 ** rng.integers(-3, 4, (rows, 1))).astype(np.float32)
+    x = full[:, :cols]
+    want = orc.row_sum_f32_documented(np.ascontiguousarray(x), block)
+    got = ops.row_sum(torch.from_numpy(full).cuda()[:, :cols], accum="auto", block=block).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("block", [1, 4, 128, 256, 512, 1024])
+def test_auto_sum_extreme_magnitudes_and_specials(block):
+    """Denormals, cancelling tiny values, magnitudes near the f32 limit, signed zeros, every finite bit
+    pattern, and rows holding Inf or NaN all match the documented order bit for bit (NaN results match as
+    NaN)."""
+    rng = np.random.default_rng(block + 7)
+    rows, cols = 12, 2048
+    x = np.zeros((rows, cols), dtype=np.float32)
+    x[0] = (rng.standard_normal(cols) * 2.0 ** -140).astype(np.float32)            # denormals
+    tiny = (rng.standard_normal(cols // 2) * 2.0 ** rng.integers(-149, -110, cols // 2)).astype(np.float32)
+    x[1] = np.concatenate([tiny, -tiny[::-1]])                                       # cancels to ~0
+    x[2] = (rng.uniform(-1.9, 1.9, cols) * 2.0 ** rng.integers(-149, 128, cols)).astype(np.float32)
+    x[3] = (rng.standard_normal(cols) * 2.0 ** 126).astype(np.float32)              # f32 result overflows
+    x[4] = -0.0                                                                      # all negative zeros
+    x[5] = rng.integers(0, 2**32, cols, dtype=np.uint64).astype(np.uint32).view(np.float32)
+    x[5][~np.isfinite(x[5])] = 1.0                                                   # every finite bit pattern
+    x[6] = rng.standard_normal(cols)
+    x[6, 1500] = np.inf
+    x[7] = rng.standard_normal(cols)
+    x[7, 3] = np.inf
+    x[7, 2000] = -np.inf
+    x[8] = rng.standard_normal(cols)
+    x[8, 77] = np.nan
+    x[9] = rng.standard_normal(cols)                                                 # shares a CTA with row 8
+    x[10] = (rng.uniform(-1.9, 1.9, cols) * 2.0 ** 127).astype(np.float32)
+    x[10, 5] = -np.inf
+    x[11] = rng.standard_normal(cols).astype(np.float32)
+    x[11, -1] = np.float32(3.4e38)
+    want = orc.row_sum_f32_documented(x, block)
+    got = ops.row_sum(torch.from_numpy(x).cuda(), accum="auto", block=block).cpu().numpy()
+    both_nan = np.isnan(got) & np.isnan(want)
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    assert np.array_equal(got.view(np.uint32)[~both_nan], want.view(np.uint32)[~both_nan])
+
+
 def test_auto_sum_full_config_and_strided_rows():
     x = workloads.rowsum_input(device="cuda")
     for b in (256, 1024):

@@ -80,6 +80,7 @@ SIGNATURES = {
     "up_sm100_scan_i32": ([_P, _P, _I64, _I64, _I, _I, _I, _P, _P, _SZ, _P], _I),
     "up_sm100_scan_workspace_bytes": ([_I64, _I64], _SZ),
     "up_sm100_scan_i32_noalloc": ([_P, _P, _I64, _I64, _I, _I, _I, _P, _I, _P], _I),
+    "up_sm100_scan_i32_host": ([_P, _P, _I64, _I64, _I, _I, _I, _P], _I),
     "up_sm100_reduce_i32": ([_P, _I64, _I, _P, _P], _I),
     "up_sm100_gather_rows": ([_P, _I64, _I64, _P, _I, _I64, _I, _P, _P], _I),
     "up_sm100_dequant_i4_bf16": ([_P, _P, _I64, _I64, _I64, _P, _P], _I),

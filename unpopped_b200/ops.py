@@ -1,12 +1,15 @@
 """Tensor-level entry points over the C ABI: each lifted kernel family on torch CUDA tensors.
 
 torch supplies device memory and the current stream only; every computation runs in libunpopped_sm100.so.
-Inputs must already be on a CUDA device; nothing here moves data to the host or computes on it.
+Inputs must already be on a CUDA device; nothing here moves data to the host or computes on it. The one
+exception is `scan_host`, whose buffers are in host memory: the library itself streams them through the device.
 """
 from __future__ import annotations
 
+import ctypes
 import threading
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -110,6 +113,32 @@ def scan(x: torch.Tensor, op: str = "sum", exclusive: bool = False, reverse: boo
     check(L.up_sm100_scan_i32(x.data_ptr(), out.data_ptr(), rows, k, _OPS[op], int(exclusive), int(reverse),
                               carry.data_ptr() if carry is not None else None, ws.data_ptr(), ws.numel(),
                               _stream(x)), "scan")
+    return out
+
+
+def scan_host(x, op: str = "sum", exclusive: bool = False, reverse: bool = False, carry: int | None = None,
+              out=None):
+    """Scan of int32 rows held in HOST memory (a numpy array or a CPU tensor, pinned for the full copy rate),
+    streamed through the device with the copies overlapped; returns the output in host memory."""
+    is_t = isinstance(x, torch.Tensor)
+    if is_t:
+        if x.device.type != "cpu" or x.dtype != torch.int32 or not x.is_contiguous():
+            raise ValueError("scan_host takes a contiguous int32 tensor in host memory")
+        if out is None:
+            out = torch.empty_like(x, pin_memory=x.is_pinned())
+        xp, yp = x.data_ptr(), out.data_ptr()
+    else:
+        x = np.ascontiguousarray(x)
+        if x.dtype != np.int32:
+            raise ValueError("scan_host takes an int32 array")
+        if out is None:
+            out = np.empty_like(x)
+        xp, yp = x.ctypes.data, out.ctypes.data
+    k = x.shape[-1] if x.ndim > 0 else 1
+    rows = (x.size if not is_t else x.numel()) // k if k > 0 else 0
+    c = ctypes.c_int32(carry) if carry is not None else None
+    check(_lib.load().up_sm100_scan_i32_host(xp, yp, rows, k, _OPS[op], int(exclusive), int(reverse),
+                                             ctypes.byref(c) if c is not None else None), "scan_host")
     return out
 
 
