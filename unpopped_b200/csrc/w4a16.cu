@@ -12,11 +12,14 @@
 //    units are split evenly over one persistent CTA per SM (stream-K), so every SM streams the same share of
 //    W. Each k-block keeps its own accumulator (its own group scale), but a unit's hand-offs between the roles
 //    are paid once for UK k-blocks: measured, these hand-offs, not the data or the math, set the unit's time.
-//  * warps 0..15 (dequant): warp w owns TMEM lane quarter w % 4 and k-quarter w / 4, so thread (w, lane)
-//    owns row 32 (w % 4) + lane of the tile and 32 UK k of every unit: 16 UK bytes of W, which it loads
-//    straight into registers several units ahead of use (no shared-memory round trip). It turns the nibbles into
-//    exact bf16 (one prmt, one lop3 and one bf16x2 subtract per pair) and stores them into tensor memory
-//    (tcgen05.st), where they are the MMA's A operand.
+//  * warp 26 (W loader): one thread brings each unit's W, 128 rows x 64 UK bytes, into a ring of shared-memory
+//    stages with one TMA box (128-byte swizzled when a box row is 128 bytes; rows past N read as 0). The ring holds
+//    128 KiB, far ahead of use, and the load path of the SM stays free for everything else: the plain 16-byte loads
+//    this replaced put 32 rows' worth of sector requests behind every warp instruction.
+//  * warps 0..15 (dequant): warp w owns TMEM lane quarter w % 4 and k-quarter w / 4, so thread (w, lane) owns row
+//    32 (w % 4) + lane of the tile and 32 UK k of every unit: 16 UK bytes of W, read from the W stage (conflict
+//    free under the swizzle). It turns the nibbles into exact bf16 (one prmt, one lop3 and one bf16x2 subtract per
+//    pair) and stores them into tensor memory (tcgen05.st), where they are the MMA's A operand.
 //  * warps 16..19 (MMA issuers): a single thread issues only about one tcgen05.mma per ~100 cycles, so four
 //    threads share a unit's 8 UK k-steps as pipelines: issuer g runs the 2 UK k-steps of k-quarter g into
 //    its k-block's accumulator after the issuer before it in that k-block has issued its own (an mbarrier
@@ -25,6 +28,10 @@
 //    slower: the epilogue's reads of four times the tensor-memory data cost more than the hand-offs.)
 //  * warp 24 (activation loader): one thread brings each unit's [16 x 128 UK] activation tile into a ring of
 //    shared-memory stages with 2 UK TMA boxes, 128-byte swizzled as the MMA reads it; rows past M read as 0.
+//  * warp 25 (scale loader): one thread brings each unit's scales, f16 groups [g0, g0 + 16) of its 128 rows with
+//    g0 = the unit's first group rounded down to a multiple of 8, into a ring of shared-memory slots with one TMA
+//    box. (A scale row stride that is not a multiple of 16 bytes cannot be a TMA tensor; then the warp's lanes load
+//    and store the same slot layout.) Loading them in the epilogue put a global-load latency on every unit.
 //  * warps 20..23 (epilogue): read the unit's accumulators (tcgen05.ld), scale each by scale[n][k-block] in
 //    f32 and accumulate in registers, k-block by k-block. A tile finished inside one CTA is written as bf16;
 //    a tile split between CTAs writes f32 partials, and whichever CTA finishes it last (an atomic count)
@@ -38,6 +45,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <cstring>
 #include <mutex>
 
 namespace up {
@@ -49,9 +57,11 @@ constexpr int kKB = 128;                         // k per unit
 constexpr int kDqWarps = 16;                     // warps 0..15
 constexpr int kIssuers = 4;                      // warps 16..19
 constexpr int kEpiWarps = 4;                     // warps 20..23
-constexpr int kIss0 = kDqWarps, kEpi0 = kIss0 + kIssuers, kXWarp = kEpi0 + kEpiWarps;
-constexpr int kThreads = 32 * (kXWarp + 1);      // 800
-constexpr int kScaleAhead = 4;                   // units an epilogue thread's scale loads run ahead
+constexpr int kIss0 = kDqWarps, kEpi0 = kIss0 + kIssuers, kXWarp = kEpi0 + kEpiWarps, kScWarp = kXWarp + 1;
+constexpr int kWWarp = kScWarp + 1;
+constexpr int kThreads = 32 * (kWWarp + 1);      // 864
+constexpr int kScRing = 8;                       // units of scales staged in shared memory
+constexpr int kScCols = 16;                      // f16 scales per row in a slot: groups [g0, g0 + 16), g0 % 8 == 0
 constexpr uint32_t kSleepNs = 64;                // pause between polls of a waiting dequant/epilogue/loader warp
 constexpr int kXBytes = kMmaN * kKB * 2;         // 4 KiB of bf16 per k-block: two 128-byte-swizzled boxes of 64 k
 constexpr int kTmemCols = 512;
@@ -67,15 +77,21 @@ struct Cfg {
   static constexpr int kXUnit = kXBytes * UK;          // activation bytes per unit
   static constexpr int kXStages = 8 / UK;              // 32 KiB of activation stages either way
   static constexpr int kChain = kIssuers / UK;         // issuers chained into one k-block's accumulator
-  static constexpr int kPrefetch = 4 / UK;             // units of W a dequant thread has in flight (64 bytes)
+  static constexpr int kWRow = 64 * UK;                // bytes of one W row in a unit
+  static constexpr int kWUnit = kTileN * kWRow;        // W bytes per unit (one TMA box of 128 rows)
+  static constexpr int kWStages = 16 / UK;             // 128 KiB of W in flight either way
   // mbarriers: x_full, x_empty [kXStages]; a_full [kRing][4]; mma_done, d_empty [kRing]; hand [kIssuers][kRing];
   // seg_in, seg_out; then the TMEM address word, the abort word and the fix-up verdict
-  static constexpr int kNumBars = 2 * kXStages + 4 * kRing + 2 * kRing + kIssuers * kRing + 2;
+  static constexpr int kNumBars =
+      2 * kXStages + 4 * kRing + 2 * kRing + kIssuers * kRing + 2 * kScRing + 2 * kWStages + 2;
   static_assert(kDCol0 + kRing * kDCols <= kTmemCols, "tensor memory");
 };
-constexpr int kBarBytes = 1024;
+constexpr int kBarBytes = 2048;
+constexpr size_t kWBytes = (size_t)16 * kTileN * 64;  // the W ring: Cfg<UK>::kWStages * kWUnit for either UK
 static_assert(Cfg<1>::kNumBars * 8 + 12 <= kBarBytes && Cfg<2>::kNumBars * 8 + 12 <= kBarBytes, "barrier region");
-constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + (size_t)8 * kXBytes + kBarBytes;
+constexpr size_t kScSlot = (size_t)kTileN * kScCols * 2;  // one TMA box of 128 rows x 16 f16
+constexpr size_t kScBytes = kScRing * kScSlot;
+constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + (size_t)8 * kXBytes + kWBytes + kScBytes + kBarBytes;
 static_assert(kEpi0 % 4 == 0, "epilogue warp e reads TMEM lane quarter e % 4");
 
 struct WsHeader {
@@ -202,7 +218,8 @@ __device__ __forceinline__ bool finish_segment(const float (&acc)[kMmaN], int64_
 
 template <int UK>
 __global__ void __launch_bounds__(kThreads, 1)
-    w4a16_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ w,
+    w4a16_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                 const __grid_constant__ CUtensorMap smap, int scale_tma,
                  const __half* __restrict__ scale, uint16_t* __restrict__ out, int M, int64_t N, int64_t K,
                  int64_t group, int64_t U, int64_t G, int64_t S_max, WsHeader* hdr, uint32_t* counters,
                  float* partials, uint64_t wait_ns) {
@@ -210,13 +227,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kRing = C::kRing, kXStages = C::kXStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* xs = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* x_full = reinterpret_cast<uint64_t*>(xs + (size_t)kXStages * C::kXUnit);  // [kXStages]: TMA landed
+  uint8_t* wst = xs + (size_t)kXStages * C::kXUnit;  // [kWStages] W boxes (1024-byte aligned: 32 KiB after xs)
+  __half* scs = reinterpret_cast<__half*>(wst + kWBytes);  // [kScRing][128][kScCols] f16 scales
+  uint64_t* x_full = reinterpret_cast<uint64_t*>(wst + kWBytes + kScBytes);  // [kXStages]: TMA landed
   uint64_t* x_empty = x_full + kXStages;        // [kXStages]: the stage's MMAs completed (chain ends' commits)
   uint64_t* a_full = x_empty + kXStages;        // [kRing][4]: k-quarter q of the unit's A is in TMEM (4 warps)
   uint64_t* mma_done = a_full + 4 * kRing;      // [kRing]: all of the unit's MMAs completed
   uint64_t* d_empty = mma_done + kRing;         // [kRing]: the epilogue has read the unit's accumulators
   uint64_t* hand = d_empty + kRing;             // [kIssuers][kRing]: issuer g has issued the unit's k-quarter g
-  uint64_t* seg_in = hand + kIssuers * kRing;   // split-tile end: every epilogue warp has published
+  uint64_t* sc_full = hand + kIssuers * kRing;  // [kScRing]: the scale warp has written the unit's scales
+  uint64_t* sc_empty = sc_full + kScRing;       // [kScRing]: every epilogue warp has read them
+  uint64_t* w_full = sc_empty + kScRing;        // [kWStages]: the unit's W box has landed
+  uint64_t* w_empty = w_full + C::kWStages;     // [kWStages]: every dequant warp has read it
+  uint64_t* seg_in = w_empty + C::kWStages;     // split-tile end: every epilogue warp has published
   uint64_t* seg_out = seg_in + 1;               // split-tile end: the count verdict is in s_last
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(seg_out + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -238,6 +261,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::mbar_init(&mma_done[a], UK);
       tc::mbar_init(&d_empty[a], kEpiWarps);
       for (int g = 0; g < kIssuers; ++g) tc::mbar_init(&hand[g * kRing + a], 1);
+    }
+    for (int q = 0; q < kScRing; ++q) {
+      tc::mbar_init(&sc_full[q], 1);
+      tc::mbar_init(&sc_empty[q], kEpiWarps);
+    }
+    for (int q = 0; q < C::kWStages; ++q) {
+      tc::mbar_init(&w_full[q], 1);
+      tc::mbar_init(&w_empty[q], kDqWarps);
     }
     tc::mbar_init(seg_in, kEpiWarps);
     tc::mbar_init(seg_out, 1);
@@ -263,35 +294,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lq = warp & 3, kq = warp >> 2;
     const int r = lq * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(lq * 32) << 16;
-    const int64_t wrow = K / 2;
-    UnitCursor<UK> cl;
-    cl.init(lo, G, kpg);
-    // this thread's 16 UK bytes of the unit at cl (k-quarter kq of its 128 UK k), then advance cl
-    auto load_w = [&](uint4 (&v)[UK]) {
-      const int64_t n = (int64_t)cl.t * kTileN + r;
-      const uint8_t* src = w + n * wrow + (int64_t)cl.kb * (kKB / 2) + kq * 16 * UK;
-#pragma unroll
-      for (int h = 0; h < UK; ++h) v[h] = n < N ? ld_nc_na_v4(src + 16 * h) : make_uint4(0, 0, 0, 0);
-      cl.next(Gi, kpg);
-    };
-    uint4 wq[C::kPrefetch][UK];
-#pragma unroll
-    for (int u = 0; u < C::kPrefetch; ++u) {
-      if (u < n_units) load_w(wq[u]);
-      else
-#pragma unroll
-        for (int h = 0; h < UK; ++h) wq[u][h] = make_uint4(0, 0, 0, 0);
-    }
+    // this thread's 16-byte chunks of its row in a W stage: chunk UK kq + h, 128-byte swizzled when UK = 2
+    const uint8_t* wrow = wst + (size_t)r * C::kWRow;
     bool ok = true;
-    for (int64_t i0 = 0; ok && i0 < n_units; i0 += C::kPrefetch) {
+    for (int64_t i = 0; ok && i < n_units; ++i) {
+      {
+        const int sw = (int)(i % C::kWStages);
+        if (!__all_sync(0xffffffffu, tc::mbar_wait(&w_full[sw], (uint32_t)((i / C::kWStages) & 1), wait_ns,
+                                                   abort_flag))) {
+          give_up();
+          break;
+        }
+      }
+      uint4 cur[UK];
 #pragma unroll
-      for (int u = 0; u < C::kPrefetch; ++u) {
-        const int64_t i = i0 + u;
-        if (i >= n_units) break;
-        uint4 cur[UK];
-#pragma unroll
-        for (int h = 0; h < UK; ++h) cur[h] = wq[u][h];
-        if (i + C::kPrefetch < n_units) load_w(wq[u]);
+      for (int h = 0; h < UK; ++h) {
+        const int c = UK * kq + h;
+        const int cs = UK == 2 ? (c ^ (r & 7)) : c;
+        cur[h] = *reinterpret_cast<const uint4*>(wrow + (size_t)(i % C::kWStages) * C::kWUnit + (cs << 4));
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&w_empty[i % C::kWStages]);
+      {
         const int a = (int)(i % kRing);
         const uint32_t aph = (uint32_t)((i / kRing) & 1);
         // the A stage is free once the unit kRing earlier has been multiplied
@@ -370,26 +394,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lq = warp & 3;
     const int r = lq * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(lq * 32) << 16;
-    const int64_t gpr = K / group;  // scales per row
     const int64_t GU = G / UK;      // units per tile
-    UnitCursor<UK> ce, cs;          // the unit being finished, the unit whose scales are loaded next
+    UnitCursor<UK> ce;              // the unit being finished
     ce.init(lo, G, kpg);
-    cs = ce;
-    // raw f16 bits of this row's scales for the unit at cs, k-block h in bits 16h .. 16h+15; then advance cs
-    auto load_scales = [&]() {
-      const int64_t n = (int64_t)cs.t * kTileN + r;
-      uint32_t v = 0;
-#pragma unroll
-      for (int h = 0; h < UK; ++h)
-        if (n < N) v |= (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(scale) + n * gpr + cs.gi_at(h, kpg))
-                        << (16 * h);
-      cs.next(Gi, kpg);
-      return v;
-    };
-    // scales are loaded kScaleAhead units before use, so their latency hides behind the units in between
-    uint32_t sq[kScaleAhead];
-#pragma unroll
-    for (int u = 0; u < kScaleAhead; ++u) sq[u] = u < n_units ? load_scales() : 0u;
     float acc[kMmaN];
 #pragma unroll
     for (int j = 0; j < kMmaN; ++j) acc[j] = 0.f;
@@ -398,12 +405,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int64_t e = 0; e < n_units; ++e) {
       const int d = (int)(e % kRing);
       const uint32_t dph = (uint32_t)((e / kRing) & 1);
+      // this row's scales of the unit, staged by the scale warp; the slot is released once they are read
+      const int q = (int)(e % kScRing);
+      if (!__all_sync(0xffffffffu, tc::mbar_wait(&sc_full[q], (uint32_t)((e / kScRing) & 1), wait_ns, abort_flag))) {
+        give_up();
+        break;
+      }
       float sc[UK];
 #pragma unroll
-      for (int h = 0; h < UK; ++h) sc[h] = __half2float(__ushort_as_half((unsigned short)(sq[0] >> (16 * h))));
-#pragma unroll
-      for (int u = 0; u + 1 < kScaleAhead; ++u) sq[u] = sq[u + 1];
-      sq[kScaleAhead - 1] = e + kScaleAhead < n_units ? load_scales() : 0u;
+      for (int h = 0; h < UK; ++h)
+        sc[h] = __half2float(scs[((size_t)q * kTileN + r) * kScCols + (ce.gi_at(h, kpg) - (ce.gi & ~7))]);
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&sc_empty[q]);
       const bool good = tc::mbar_wait_sleepy(&mma_done[d], dph, wait_ns, abort_flag, kSleepNs);
       if (!__all_sync(0xffffffffu, good)) {
         give_up();
@@ -435,6 +448,80 @@ __global__ void __launch_bounds__(kThreads, 1)
           give_up();
           break;
         }
+    }
+  } else if (warp == kScWarp) {
+    // ------- scale warp: stages each unit's scales, f16 groups [g0, g0 + 16) of its 128 rows, g0 = gi & ~7 -------
+    // With a scale row stride of a multiple of 16 bytes one thread brings them in with one TMA box per unit;
+    // otherwise the lanes load and store them (rows l, l + 32, l + 64, l + 96).
+    UnitCursor<UK> cs;
+    cs.init(lo, G, kpg);
+    if (scale_tma) {
+      if (lane == 0) {
+        tc::tma_prefetch_desc(&smap);
+        int64_t issued = 0;
+        for (int64_t i = 0; i < n_units; ++i) {
+          const int q = (int)(i % kScRing);
+          if (!tc::mbar_wait_sleepy(&sc_empty[q], (uint32_t)(((i / kScRing) & 1) ^ 1), wait_ns, abort_flag,
+                                    kSleepNs)) {
+            give_up();
+            break;
+          }
+          tc::mbar_arrive_expect_tx(&sc_full[q], (uint32_t)kScSlot);
+          tc::tma_load_2d(scs + (size_t)q * kTileN * kScCols, &smap, &sc_full[q], cs.gi & ~7,
+                          cs.t * kTileN);
+          cs.next(Gi, kpg);
+          issued = i + 1;
+        }
+        for (int64_t j = issued > kScRing ? issued - kScRing : 0; j < issued; ++j)
+          tc::mbar_wait(&sc_full[j % kScRing], (uint32_t)((j / kScRing) & 1), wait_ns, nullptr);
+      }
+    } else {
+      const int64_t gpr = K / group;  // scales per row
+      for (int64_t i = 0; i < n_units; ++i) {
+        const int q = (int)(i % kScRing);
+        if (!__all_sync(0xffffffffu, tc::mbar_wait_sleepy(&sc_empty[q], (uint32_t)(((i / kScRing) & 1) ^ 1), wait_ns,
+                                                          abort_flag, kSleepNs))) {
+          give_up();
+          break;
+        }
+        __half* slot = scs + (size_t)q * kTileN * kScCols;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int row = lane + 32 * j;
+          const int64_t n = (int64_t)cs.t * kTileN + row;
+#pragma unroll
+          for (int h = 0; h < UK; ++h) {
+            const int gi = cs.gi_at(h, kpg);
+            slot[row * kScCols + (gi - (cs.gi & ~7))] = n < N ? scale[n * gpr + gi] : __ushort_as_half(0);
+          }
+        }
+        cs.next(Gi, kpg);
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&sc_full[q]);
+      }
+    }
+  } else if (warp == kWWarp) {
+    // ---------------- W loader: one TMA box of 128 rows x 64 UK bytes per unit ----------------
+    if (lane == 0) {
+      tc::tma_prefetch_desc(&wmap);
+      UnitCursor<UK> cw;
+      cw.init(lo, G, kpg);
+      int64_t issued = 0;
+      for (int64_t i = 0; i < n_units; ++i) {
+        const int sw = (int)(i % C::kWStages);
+        if (!tc::mbar_wait_sleepy(&w_empty[sw], (uint32_t)(((i / C::kWStages) & 1) ^ 1), wait_ns, abort_flag,
+                                  kSleepNs)) {
+          give_up();
+          break;
+        }
+        tc::mbar_arrive_expect_tx(&w_full[sw], C::kWUnit);
+        tc::tma_load_2d(wst + (size_t)sw * C::kWUnit, &wmap, &w_full[sw], cw.kb * (kKB / 2), cw.t * kTileN);
+        cw.next(Gi, kpg);
+        issued = i + 1;
+      }
+      // every issued load must land before this CTA's shared memory is released
+      for (int64_t j = issued > C::kWStages ? issued - C::kWStages : 0; j < issued; ++j)
+        tc::mbar_wait(&w_full[j % C::kWStages], (uint32_t)((j / C::kWStages) & 1), wait_ns, nullptr);
     }
   } else {
     // ---------------- activation loader: 2 UK TMA boxes per unit ----------------
@@ -538,7 +625,7 @@ extern "C" int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, cons
   if (k == 0 || k % kKB != 0 || group % kKB != 0 || k % group != 0) return UP_ERR_UNSUPPORTED;
   if (k / 2 > 0x7fffffff || n > 0x7fffffff) return UP_ERR_UNSUPPORTED;
   UP_CHECK_ARG(w && scale && x && out && workspace);
-  // 16-byte loads of W rows (K/2 bytes, a multiple of 64) and TMA boxes of activation rows (2K bytes)
+  // TMA boxes of W rows (K/2 bytes, a multiple of 64) and of activation rows (2K bytes)
   if (!aligned(w, 16) || !aligned(x, 16) || !aligned(workspace, 256)) return UP_ERR_INVALID;
   const Plan p = make_plan(n, k);
   if (workspace_bytes < p.bytes) return UP_ERR_INVALID;
@@ -554,6 +641,34 @@ extern "C" int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, cons
                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return fail_with(UP_ERR_CUDA, "cuTensorMapEncodeTiled refused the activation tensor map");
+  // W as a [N, K/2] byte tensor; boxes of 128 rows x 64 UK bytes (one unit), 128-byte swizzled when a box row is
+  // 128 bytes; rows >= N read as zero
+  CUtensorMap wmap;
+  {
+    const cuuint64_t wdims[2] = {(cuuint64_t)(k / 2), (cuuint64_t)n};
+    const cuuint64_t wstrides[1] = {(cuuint64_t)(k / 2)};
+    const cuuint32_t wbox[2] = {(cuuint32_t)(64 * p.UK), (cuuint32_t)kTileN};
+    const CUresult wr = enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w), wdims, wstrides, wbox,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            p.UK == 2 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (wr != CUDA_SUCCESS) return fail_with(UP_ERR_CUDA, "cuTensorMapEncodeTiled refused the weight tensor map");
+  }
+  // scales as a [N, K / group] f16 tensor; boxes of 128 rows x 16 groups. A TMA row stride must be a multiple of
+  // 16 bytes; other shapes stage the scales with plain loads.
+  CUtensorMap smap;
+  std::memset(&smap, 0, sizeof(smap));
+  const int64_t gpr = k / group;
+  const int scale_tma = (gpr % 8 == 0 && aligned(scale, 16)) ? 1 : 0;
+  if (scale_tma) {
+    const cuuint64_t sdims[2] = {(cuuint64_t)gpr, (cuuint64_t)n};
+    const cuuint64_t sstrides[1] = {(cuuint64_t)gpr * 2};
+    const cuuint32_t sbox[2] = {(cuuint32_t)kScCols, (cuuint32_t)kTileN};
+    const CUresult sr = enc(&smap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(scale), sdims, sstrides,
+                            sbox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (sr != CUDA_SUCCESS) return fail_with(UP_ERR_CUDA, "cuTensorMapEncodeTiled refused the scale tensor map");
+  }
   {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -575,7 +690,8 @@ extern "C" int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, cons
   auto* partials = reinterpret_cast<float*>(base + p.partials_off);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto kern = p.UK == 2 ? w4a16_kernel<2> : w4a16_kernel<1>;
-  kern<<<(unsigned)p.P, kThreads, kSmemBytes, s>>>(xmap, w, reinterpret_cast<const __half*>(scale), out, (int)m, n, k,
+  kern<<<(unsigned)p.P, kThreads, kSmemBytes, s>>>(xmap, wmap, smap, scale_tma, reinterpret_cast<const __half*>(scale),
+                                                   out, (int)m, n, k,
                                                    group, p.U, p.G, p.S_max, hdr, counters, partials,
                                                    wait_limit_ns());
   note_launch();
