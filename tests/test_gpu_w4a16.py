@@ -37,7 +37,8 @@ def _np(t, dt):
     return t.cpu().contiguous().view({np.uint16: torch.int16, np.uint8: torch.uint8}[dt]).numpy().view(dt)
 
 
-@pytest.mark.parametrize("n,k,group", [(128, 256, 128), (300, 512, 64), (64, 40, 8), (33, 24, 24), (1, 8, 8), (3, 6, 2), (5, 12, 4)])
+@pytest.mark.parametrize("n,k,group", [(128, 256, 128), (300, 512, 64), (64, 40, 8), (33, 24, 24), (1, 8, 8), (3, 6, 2),
+                                       (5, 12, 4), (7, 16448, 64), (9000, 64, 64)])  # rows past 8192 k; many rows per CTA
 def test_dequant_bit_exact(n, k, group):
     d = workloads.w4a16_inputs(n=n, k=k, m=1, group=group, seed=n + k)
     got = ops.dequant_i4(d.w_packed, d.scale, group)
