@@ -99,7 +99,9 @@ typedef enum up_kernel_id {
   UP_K_SCAN_I32 = 3,
   UP_K_GATHER_ROWS = 4,
   UP_K_DEQUANT_I4 = 5,
-  UP_K_W4A16_GEMM = 6
+  UP_K_W4A16_GEMM = 6,
+  UP_K_REDUCE2D_F32 = 7,  /* f32 Sum/Mean/Max/Min over the last or the outer axis of a rank-2 input */
+  UP_K_REDUCE2D_I32 = 8   /* i32 Sum/Prod/Max/Min/And/Or/Xor, same axes */
 } up_kernel_id;
 
 /* A buffer argument: the reference's TypedBuffer / OperandDesc. `base` and `stride` count elements
@@ -209,6 +211,21 @@ UP_API int up_sm100_workspace_status(void* workspace, void* stream);
  * ir.rs:2080-2135; oracle fold oracle/plan_eval.rs:501-651). `row_stride` in elements (>= cols). */
 UP_API int up_sm100_row_sum_f32(const float* x, int64_t rows, int64_t cols, int64_t row_stride, float* out,
                          int accum, int block, void* stream);
+
+/* The reduction lift's other ops on a row-major rank-2 [rows, cols] input reduced over one axis: axis 1 (the
+ * last; `out` has `rows` entries) or axis 0 (the outer; `out` has `cols`). `ReduceOp` (ir.rs:1700-1748) and
+ * `Access::Reduction` with an axes mask (ir.rs:2080-2135), evaluated as the oracle does (oracle/plan_eval.rs:
+ * 501-651, plan_contract.rs:146-245).
+ * f32: op SUM, MEAN, MAX or MIN. Over the last axis Sum/Mean follow `accum` (Mean: Auto only) and the launched
+ * lift's documented order for logical block `block` (kernel_lift/block_reduce.rs:13-23); over the outer axis
+ * Sum/Mean fold each column in the serial order (Auto only). Max/Min are NaN-propagating and bit-exact to the
+ * serial fold: the last NaN (quiet bit set) if any, else the first element of the extreme value.
+ * i32: op SUM or PROD (both wrapping), MAX, MIN, AND, OR or XOR; bit-exact. An empty fold stores 0 (1 for Prod;
+ * an f32 Mean: 0/0). */
+UP_API int up_sm100_reduce2d_f32(const float* x, int64_t rows, int64_t cols, int64_t row_stride, int axis, int op,
+                                 int accum, int block, float* out, void* stream);
+UP_API int up_sm100_reduce2d_i32(const int32_t* x, int64_t rows, int64_t cols, int64_t row_stride, int axis,
+                                 int op, int32_t* out, void* stream);
 
 /* Row max and argmax of a row-major bf16 matrix: Max is NaN-propagating (oracle/plan_contract.rs:179-210),
  * ArgMax is the first index of the extreme with NaN the greatest value (plan_contract.rs:213-245).

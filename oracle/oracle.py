@@ -40,6 +40,9 @@ def lib():
         L.orc_row_sum_f32.argtypes = [P, I64, I64, I64, P, I]
         L.orc_row_sum_f32_documented.argtypes = [P, I64, I64, I64, I64, P, I]
         L.orc_row_max_argmax_bf16.argtypes = [P, I64, I64, I64, P, P, I]
+        L.orc_reduce2d_f32.argtypes = [P, I64, I64, I64, I, I, P, I]
+        L.orc_row_mean_f32_documented.argtypes = [P, I64, I64, I64, I64, P, I]
+        L.orc_reduce2d_i32.argtypes = [P, I64, I64, I64, I, I, P, I]
         L.orc_scan_i32.argtypes = [P, P, I64, I64, I, I, I, ctypes.c_int32, I]
         L.orc_scan_i32_chunked.argtypes = [P, P, I64, I, I, I]
         L.orc_reduce_i32.argtypes = [P, I64, I]
@@ -98,6 +101,36 @@ def row_sum_f32_documented(x: np.ndarray, block: int, threads: int = 1) -> np.nd
     rows, cols = x.shape
     out = np.empty(rows, np.float32)
     lib().orc_row_sum_f32_documented(_p(x), rows, cols, cols, block, _p(out), threads)
+    return out
+
+
+REDUCE_OPS = {"sum": 0, "mean": 1, "max": 2, "min": 3, "prod": 4, "and": 5, "or": 6, "xor": 7}
+
+
+def reduce2d_f32(x: np.ndarray, op: str, axis: int, threads: int = 1) -> np.ndarray:
+    """Serial-order f64 fold of a [rows, cols] f32 array over one axis (oracle/plan_eval.rs:501-651)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, cols = x.shape
+    out = np.empty(rows if axis == 1 else cols, np.float32)
+    lib().orc_reduce2d_f32(_p(x), rows, cols, cols, axis, REDUCE_OPS[op], _p(out), threads)
+    return out
+
+
+def row_mean_f32_documented(x: np.ndarray, block: int, threads: int = 1) -> np.ndarray:
+    """Mean over the last axis in the launched lift's documented order (kernel_lift/block_reduce.rs:13-23)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, cols = x.shape
+    out = np.empty(rows, np.float32)
+    lib().orc_row_mean_f32_documented(_p(x), rows, cols, cols, block, _p(out), threads)
+    return out
+
+
+def reduce2d_i32(x: np.ndarray, op: str, axis: int, threads: int = 1) -> np.ndarray:
+    """Fold of a [rows, cols] i32 array over one axis (oracle/plan_eval.rs:501-651, bit_fold)."""
+    x = np.ascontiguousarray(x, dtype=np.int32)
+    rows, cols = x.shape
+    out = np.empty(rows if axis == 1 else cols, np.int32)
+    lib().orc_reduce2d_i32(_p(x), rows, cols, cols, axis, REDUCE_OPS[op], _p(out), threads)
     return out
 
 

@@ -177,6 +177,91 @@ void orc_row_max_argmax_bf16(const uint16_t* x, int64_t rows, int64_t cols, int6
   }
 }
 
+/* eval_reduction (oracle/plan_eval.rs:501-651) for a rank-2 f32 [rows, cols] input reduced over one axis (axis 1:
+ * out[rows]; axis 0: out[cols]) in the serial order: fold_step / extremum_fold (plan_contract.rs:146-210) with an
+ * f64 accumulator from 0, Mean divided by the reduced extent (an empty Mean is 0/0), one rounding to f32 at the
+ * store. op: 0 Sum, 1 Mean, 2 Max, 3 Min. Max/Min: take = !have || v is NaN || v better than acc; a NaN result is
+ * the fold's last NaN, widened as the f32->f64->f32 conversions widen it (quiet bit set). */
+void orc_reduce2d_f32(const float* x, int64_t rows, int64_t cols, int64_t row_stride, int axis, int op, float* out,
+                      int threads) {
+  const int64_t nk = axis == 1 ? rows : cols, nr = axis == 1 ? cols : rows;
+#pragma omp parallel for num_threads(threads) schedule(static) if (threads > 1)
+  for (int64_t k = 0; k < nk; ++k) {
+    double acc = 0.0;
+    uint32_t acc_bits = 0;
+    int have = 0;
+    for (int64_t i = 0; i < nr; ++i) {
+      const float f = axis == 1 ? x[k * row_stride + i] : x[i * row_stride + k];
+      const double v = (double)f;
+      if (op == 0 || op == 1) {
+        acc += v;
+      } else {
+        const int vnan = v != v;
+        const int better = op == 2 ? v > acc : v < acc;
+        if (!have || vnan || better) {
+          acc = v;
+          acc_bits = vnan ? (f32_bits(f) | 0x00400000u) : f32_bits(f);
+        }
+        have = 1;
+      }
+    }
+    if (op == 0) out[k] = (float)acc;
+    else if (op == 1) out[k] = (float)(acc / (double)nr);
+    else out[k] = have ? bits_f32(acc_bits) : 0.0f;
+  }
+}
+
+/* Mean over the last axis in the launched lift's documented order (kernel_lift/block_reduce.rs:13-23): the
+ * documented f64 sum of orc_row_sum_f32_documented, divided by the extent, one rounding. */
+void orc_row_mean_f32_documented(const float* x, int64_t rows, int64_t cols, int64_t row_stride, int64_t block,
+                                 float* out, int threads) {
+#pragma omp parallel num_threads(threads) if (threads > 1)
+  {
+    double* acc = (double*)malloc(sizeof(double) * (size_t)block);
+#pragma omp for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+      const float* row = x + r * row_stride;
+      for (int64_t t = 0; t < block; ++t) {
+        double a = 0.0;
+        for (int64_t c = t; c < cols; c += block) a += (double)row[c];
+        acc[t] = a;
+      }
+      for (int64_t s = block / 2; s > 0; s /= 2)
+        for (int64_t t = 0; t < s; ++t) acc[t] += acc[t + s];
+      out[r] = (float)(acc[0] / (double)cols);
+    }
+    free(acc);
+  }
+}
+
+/* eval_reduction for a rank-2 i32 input over one axis: the oracle folds in an i128 wrapped at 64 bits and the store
+ * truncates to 32 (plan_eval.rs:530-545), which for Sum and Prod is wrapping 32-bit arithmetic; Max/Min take the
+ * first element and then a strictly better one; And/Or/Xor are seeded by the first element (bit_fold); an empty fold
+ * stores 0, or 1 for Prod. op: 0 Sum, 2 Max, 3 Min, 4 Prod, 5 And, 6 Or, 7 Xor. */
+void orc_reduce2d_i32(const int32_t* x, int64_t rows, int64_t cols, int64_t row_stride, int axis, int op,
+                      int32_t* out, int threads) {
+  const int64_t nk = axis == 1 ? rows : cols, nr = axis == 1 ? cols : rows;
+#pragma omp parallel for num_threads(threads) schedule(static) if (threads > 1)
+  for (int64_t k = 0; k < nk; ++k) {
+    uint32_t acc = op == 4 ? 1u : 0u;
+    int have = 0;
+    for (int64_t i = 0; i < nr; ++i) {
+      const int32_t v = axis == 1 ? x[k * row_stride + i] : x[i * row_stride + k];
+      switch (op) {
+        case 0: acc += (uint32_t)v; break;
+        case 4: acc *= (uint32_t)v; break;
+        case 2: if (!have || v > (int32_t)acc) acc = (uint32_t)v; break;
+        case 3: if (!have || v < (int32_t)acc) acc = (uint32_t)v; break;
+        case 5: acc = have ? (acc & (uint32_t)v) : (uint32_t)v; break;
+        case 6: acc = have ? (acc | (uint32_t)v) : (uint32_t)v; break;
+        case 7: acc = have ? (acc ^ (uint32_t)v) : (uint32_t)v; break;
+      }
+      have = 1;
+    }
+    out[k] = (int32_t)acc;
+  }
+}
+
 /* ---- scans: oracle/plan_window.rs:10-238 ---------------------------------------------------------- */
 
 static inline int32_t orc_combine_i32(int op, int32_t a, int32_t b) {

@@ -9,6 +9,7 @@ Run: python tests/golden/make_golden.py   (deterministic; rewrites the JSON file
 """
 from __future__ import annotations
 
+import functools
 import json
 import math
 import os
@@ -65,9 +66,10 @@ def float_sum_corpus() -> list:
     return [[v[c * rows + r] for c in range(cols)] for r in range(rows)]
 
 
-def documented(xs: list, block: int) -> float:
+def documented(xs: list, block: int, mean: bool = False) -> float:
     """`documented` (float_sum_bound.rs:147-170) at F32, Sum: thread t folds t, t+B, ... into an f64, then
-    acc[t] += acc[t+s] for s = B/2 .. 1, one rounding to f32."""
+    acc[t] += acc[t+s] for s = B/2 .. 1, one rounding to f32. Mean divides the f64 total by the extent before
+    that rounding (kernel_lift/block_reduce.rs:13-23)."""
     acc = []
     for t in range(block):
         a = 0.0
@@ -79,7 +81,17 @@ def documented(xs: list, block: int) -> float:
         for t in range(s):
             acc[t] = acc[t] + acc[t + s]
         s //= 2
-    return f32(acc[0])
+    return f32(acc[0] / len(xs) if mean else acc[0])
+
+
+def serial_extremum(xs: list, is_max: bool) -> float:
+    """extremum_fold (oracle/plan_contract.rs:179-210) on finite values: the first element, replaced by a strictly
+    better one."""
+    acc = xs[0]
+    for x in xs[1:]:
+        if (x > acc) if is_max else (x < acc):
+            acc = x
+    return acc
 
 
 def golden_float_sum() -> dict:
@@ -92,6 +104,11 @@ def golden_float_sum() -> dict:
         "blocks": blocks,
         "documented_f32_bits": {str(b): [f32_bits(documented(r, b)) for r in rows] for b in blocks},
         "serial_f32_bits": [f32_bits(documented(r, 1)) for r in rows],
+        "documented_mean_f32_bits": {str(b): [f32_bits(documented(r, b, True)) for r in rows] for b in blocks},
+        "max_f32_bits": [f32_bits(serial_extremum(r, True)) for r in rows],
+        "min_f32_bits": [f32_bits(serial_extremum(r, False)) for r in rows],
+        "col_sum_f32_bits": [f32_bits(documented([r[c] for r in rows], 1)) for c in range(96)],
+        "col_max_f32_bits": [f32_bits(serial_extremum([r[c] for r in rows], True)) for c in range(96)],
     }
 
 
@@ -207,11 +224,26 @@ def golden_scan() -> dict:
         "max": [max(r) for r in int_corpus_i32()],
         "min": [min(r) for r in int_corpus_i32()],
     }
+    # Every integer ReduceOp (ir.rs:1700-1748) over both axes of the corpus, as reduce_both runs them
+    # (kernel_int_reduce_scan_agrees.rs:80-110): Sum and Prod wrap at the dtype's width, Max/Min exact, the bit
+    # folds seeded by the first element.
+    folds = {
+        "sum": lambda v: wrap32(sum(v)),
+        "prod": lambda v: wrap32(functools.reduce(lambda a, b: a * b, v, 1)),
+        "max": max, "min": min,
+        "and": lambda v: functools.reduce(lambda a, b: a & b, v),
+        "or": lambda v: functools.reduce(lambda a, b: a | b, v),
+        "xor": lambda v: functools.reduce(lambda a, b: a ^ b, v),
+    }
+    ic = int_corpus_i32()
+    axes = {op: {"axis1": [f(r) for r in ic], "axis0": [f([r[c] for r in ic]) for c in range(len(ic[0]))]}
+            for op, f in folds.items()}
     return {
         "source": "crates/unpopped/tests/kernel_int_reduce_scan_agrees.rs:28-45; "
                   "kernel_parallel_scan_agrees.rs:60-64",
         "cases": cases,
         "row_reductions_5x6": red,
+        "reductions_5x6_both_axes": axes,
     }
 
 

@@ -7,6 +7,7 @@ import re
 import pytest
 
 from unpopped_b200 import _lib
+from unpopped_b200._lib import OP
 from unpopped_b200.backend import CudaSm100, LowerError, Operand, Plan
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -58,6 +59,23 @@ def _red(op, dtype, out_dtype=None, shape=(64, 96), **kw):
                 out_dtype=out_dtype, op=op, **kw)
 
 
+def test_dispatch_table_maps_the_reduction_breadth():
+    b = CudaSm100()
+    k = b.lower(_red("MEAN", "F32", accum="AUTO", block=64))
+    assert (k.name, k.scalars) == ("up_sm100_reduce2d_f32", (OP["MEAN"], 1, 0, 64))
+    for op in ("MAX", "MIN"):
+        k = b.lower(_red(op, "F32"))
+        assert (k.name, k.scalars[:2]) == ("up_sm100_reduce2d_f32", (OP[op], 1))
+        k = b.lower(_red(op, "F32", axes_mask=1))
+        assert (k.name, k.scalars[:2]) == ("up_sm100_reduce2d_f32", (OP[op], 0))
+    k = b.lower(_red("SUM", "F32", axes_mask=1, accum="AUTO"))
+    assert (k.name, k.scalars) == ("up_sm100_reduce2d_f32", (OP["SUM"], 0, 0, 1))
+    for op in ("SUM", "PROD", "MAX", "MIN", "AND", "OR", "XOR"):
+        for mask, axis in ((0, 1), (2, 1), (1, 0)):
+            k = b.lower(_red(op, "I32", axes_mask=mask))
+            assert (k.name, k.scalars) == ("up_sm100_reduce2d_i32", (OP[op], axis)), (op, mask)
+
+
 def test_dispatch_table_maps_each_lift():
     b = CudaSm100()
     k = b.lower(_red("SUM", "F32"))
@@ -87,7 +105,12 @@ def test_dispatch_table_maps_each_lift():
 @pytest.mark.parametrize("plan,variant", [
     (_red("SUM", "F64"), "UnsupportedDtype"),
     (_red("PROD", "F32"), "UnsupportedOp"),
-    (_red("SUM", "F32", axes_mask=1), "UnsupportedPlanShape"),
+    (_red("SUM", "F32", shape=(4, 8, 16), axes_mask=2), "UnsupportedPlanShape"),  # a middle axis
+    (_red("SUM", "F32", axes_mask=1), "UnsupportedOp"),  # outer axis under the F32 policy: Auto only
+    (_red("SUM", "F32", axes_mask=1, accum="AUTO", block=4), "UnsupportedPlanShape"),  # outer Sum: serial order
+    (_red("MEAN", "I32"), "UnsupportedOp"),  # the oracle has no integer Mean
+    (_red("AND", "F32"), "UnsupportedOp"),  # bit folds are integer-only
+    (_red("ARGMAX", "F32", "I64"), "UnsupportedDtype"),
     (_red("ARGMAX", "BF16", "F32"), "InadmissiblePlan"),
     (_red("SUM", "F32", accum="AUTO", block=3), "UnsupportedPlanShape"),
     (Plan("SCAN", [Operand("F32", (8,)), Operand("F32", (8,))], dtype="F32"), "UnsupportedDtype"),

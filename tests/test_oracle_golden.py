@@ -68,6 +68,43 @@ def test_int_row_reductions_wrap():
         assert [orc.reduce_i32(r, op) for r in x] == g["row_reductions_5x6"][name]
 
 
+def test_int_reductions_every_op_both_axes():
+    """reduce2d_i32 against the reference corpus's Sum/Prod/Max/Min/And/Or/Xor over both axes."""
+    g = load("scan_i32.json")
+    x = np.array(g["cases"]["int_reduce_scan_5x6"]["x"], dtype=np.int32)
+    for op, exp in g["reductions_5x6_both_axes"].items():
+        assert orc.reduce2d_i32(x, op, 1).tolist() == exp["axis1"], op
+        assert orc.reduce2d_i32(x, op, 0).tolist() == exp["axis0"], op
+
+
+def test_float_mean_max_min_and_columns():
+    """Documented-order Mean for every block, serial Max/Min, and the serial column Sum/Max of the float corpus."""
+    g = load("float_sum_documented.json")
+    x = np.array(g["x_f32_bits"], dtype=np.uint32).view(np.float32).reshape(g["rows"], g["cols"])
+    bits = lambda a: np.asarray(a, dtype=np.float32).view(np.uint32).tolist()
+    for b in g["blocks"]:
+        assert bits(orc.row_mean_f32_documented(x, b)) == g["documented_mean_f32_bits"][str(b)], b
+    assert bits(orc.reduce2d_f32(x, "mean", 1)) == g["documented_mean_f32_bits"]["1"]
+    assert bits(orc.reduce2d_f32(x, "max", 1)) == g["max_f32_bits"]
+    assert bits(orc.reduce2d_f32(x, "min", 1)) == g["min_f32_bits"]
+    assert bits(orc.reduce2d_f32(x, "sum", 0)) == g["col_sum_f32_bits"]
+    assert bits(orc.reduce2d_f32(x, "max", 0)) == g["col_max_f32_bits"]
+
+
+def test_float_extremum_nan_and_zero_rules():
+    """extremum_fold's rules on the oracle: the last NaN (quiet bit set) wins, and of +0/-0 the first is kept."""
+    nan_a = np.array([0x7f800001], np.uint32).view(np.float32)[0]  # signalling payload 1
+    nan_b = np.array([0xffc00002], np.uint32).view(np.float32)[0]
+    x = np.array([[1.0, nan_a, 5.0, nan_b, 2.0], [-0.0, 0.0, -1.0, -0.0, -1.0], [0.0, -0.0, 3.0, 3.0, 0.0]],
+                 np.float32)
+    mx = orc.reduce2d_f32(x, "max", 1).view(np.uint32).tolist()
+    mn = orc.reduce2d_f32(x, "min", 1).view(np.uint32).tolist()
+    assert mx[0] == 0xffc00002 and mn[0] == 0xffc00002
+    assert mx[1] == 0x80000000  # -0 first, +0 not strictly greater
+    assert mn[2] == 0x00000000  # +0 first
+    assert np.isnan(orc.reduce2d_f32(np.zeros((3, 0), np.float32), "mean", 1)).all()
+
+
 def test_chunked_scan_equals_serial_scan():
     rng = np.random.default_rng(7)
     x = rng.integers(-(2**31), 2**31 - 1, size=100_003, dtype=np.int64).astype(np.int32)

@@ -78,6 +78,8 @@ static const char* k_name(int id) {
     case UP_K_GATHER_ROWS: return "up_sm100_gather_rows";
     case UP_K_DEQUANT_I4: return "up_sm100_dequant_i4_bf16";
     case UP_K_W4A16_GEMM: return "up_sm100_w4a16_gemm";
+    case UP_K_REDUCE2D_F32: return "up_sm100_reduce2d_f32";
+    case UP_K_REDUCE2D_I32: return "up_sm100_reduce2d_i32";
     default: return "";
   }
 }
@@ -150,26 +152,43 @@ extern "C" int up_sm100_classify(const up_plan_desc* p, up_lowered* out) {
       if (p->n_operands < 2) return refuse(out, UP_LOWER_INADMISSIBLE_PLAN, "a reduction has an input and an output");
       const up_tensor& in = ops[0];
       const bool last_axis = p->axes_mask == 0 || (in.rank >= 1 && p->axes_mask == (1u << (in.rank - 1)));
-      if (!last_axis) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "only the last axis is reduced");
+      const bool outer_axis = in.rank == 2 && p->axes_mask == 1u;  // axis 0 of a rank-2 input
+      if (!last_axis && !outer_axis)
+        return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "the last axis, or axis 0 of a rank-2 input, is reduced");
       if (!p->identity_body) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "body/post must be the identity");
-      if (!last_axis_contiguous(in)) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "reduced axis must be contiguous");
-      if (p->op == UP_OP_SUM) {
-        if (p->dtype != UP_EK_F32) return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "Sum is lowered for f32");
-        if (p->accum != UP_ACCUM_AUTO && p->accum != UP_ACCUM_F32)
-          return refuse(out, UP_LOWER_UNSUPPORTED_OP, "accumulation policy");
-        const int b = p->block ? p->block : 256;
-        if (b < 1 || b > 1024 || (b & (b - 1))) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "block B");
-        return accept(out, UP_K_ROW_SUM_F32, {p->accum, b});
-      }
+      if (!last_axis_contiguous(in)) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "rows must be contiguous");
+      const int axis = last_axis ? 1 : 0;
       if (p->op == UP_OP_MAX || p->op == UP_OP_ARGMAX) {
-        if (p->dtype != UP_EK_BF16) return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "Max/ArgMax are lowered for bf16");
-        if (p->op == UP_OP_ARGMAX && p->out_dtype != UP_EK_I64 && p->out_dtype != UP_EK_I32)
-          return refuse(out, UP_LOWER_INADMISSIBLE_PLAN, "ArgMax needs an I64 (or I32) output");
-        if (p->op == UP_OP_MAX && p->out_dtype != UP_EK_F32)
-          return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "Max is stored as f32");
-        return accept(out, UP_K_ROW_MAX_ARGMAX_BF16, {});
+        if (p->dtype == UP_EK_BF16 && axis == 1) {
+          if (p->op == UP_OP_ARGMAX && p->out_dtype != UP_EK_I64 && p->out_dtype != UP_EK_I32)
+            return refuse(out, UP_LOWER_INADMISSIBLE_PLAN, "ArgMax needs an I64 (or I32) output");
+          if (p->op == UP_OP_MAX && p->out_dtype != UP_EK_F32)
+            return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "Max is stored as f32");
+          return accept(out, UP_K_ROW_MAX_ARGMAX_BF16, {});
+        }
+        if (p->op == UP_OP_ARGMAX)
+          return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "ArgMax is lowered for bf16 over the last axis");
       }
-      return refuse(out, UP_LOWER_UNSUPPORTED_OP, "reduction op not lowered by this backend");
+      if (p->dtype == UP_EK_F32) {
+        if (p->op != UP_OP_SUM && p->op != UP_OP_MEAN && p->op != UP_OP_MAX && p->op != UP_OP_MIN)
+          return refuse(out, UP_LOWER_UNSUPPORTED_OP, "f32 reductions lowered: Sum, Mean, Max, Min");
+        const bool summing = p->op == UP_OP_SUM || p->op == UP_OP_MEAN;
+        if (summing && p->accum != UP_ACCUM_AUTO && !(p->accum == UP_ACCUM_F32 && p->op == UP_OP_SUM && axis == 1))
+          return refuse(out, UP_LOWER_UNSUPPORTED_OP, "accumulation policy");
+        const int b = p->block ? p->block : (axis == 1 ? 256 : 1);
+        if (b < 1 || b > 1024 || (b & (b - 1))) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "block B");
+        if (summing && axis == 0 && b != 1)
+          return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "an outer-axis Sum/Mean folds in the serial order");
+        if (p->op == UP_OP_SUM && axis == 1) return accept(out, UP_K_ROW_SUM_F32, {p->accum, b});
+        return accept(out, UP_K_REDUCE2D_F32, {p->op, axis, p->accum, b});
+      }
+      if (p->dtype == UP_EK_I32) {
+        if (p->op != UP_OP_SUM && p->op != UP_OP_PROD && p->op != UP_OP_MAX && p->op != UP_OP_MIN &&
+            p->op != UP_OP_AND && p->op != UP_OP_OR && p->op != UP_OP_XOR)
+          return refuse(out, UP_LOWER_UNSUPPORTED_OP, "i32 reductions lowered: Sum, Prod, Max, Min, And, Or, Xor");
+        return accept(out, UP_K_REDUCE2D_I32, {p->op, axis});
+      }
+      return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "reductions are lowered for f32, i32 and (Max/ArgMax) bf16");
     }
     case UP_SCHED_SCAN: {
       if (p->n_operands < 2) return refuse(out, UP_LOWER_INADMISSIBLE_PLAN, "a scan has an input and an output");
@@ -247,6 +266,25 @@ extern "C" int up_sm100_launch(int kernel_id, const up_tensor* ins, int n_in, co
       if (y.shape[0] != x.shape[0] || (y.rank == 1 && y.stride[0] != 1)) return UP_ERR_UNSUPPORTED;
       return up_sm100_row_sum_f32(reinterpret_cast<const float*>(at(x)), x.shape[0], x.shape[1], x.stride[0],
                                   (float*)at(y), (int)sc(0, UP_ACCUM_F32), (int)sc(1, 256), stream);
+    }
+    case UP_K_REDUCE2D_F32:
+    case UP_K_REDUCE2D_I32: {
+      if (n_in < 1 || n_out < 1) return UP_ERR_INVALID;
+      const up_tensor &x = ins[0], &y = outs[0];
+      const int axis = (int)sc(1, 1);
+      const bool f32 = kernel_id == UP_K_REDUCE2D_F32;
+      if (x.dtype != (f32 ? UP_EK_F32 : UP_EK_I32) || y.dtype != x.dtype || x.rank != 2 || x.stride[1] != 1)
+        return UP_ERR_UNSUPPORTED;
+      if (axis != 0 && axis != 1) return UP_ERR_INVALID;
+      const int64_t n_out_elems = axis == 1 ? x.shape[0] : x.shape[1];
+      const int64_t y_count = y.rank == 2 ? y.shape[0] * y.shape[1] : (y.rank == 1 ? y.shape[0] : 1);
+      if (y_count != n_out_elems || (y.rank >= 1 && y.stride[y.rank - 1] != 1)) return UP_ERR_UNSUPPORTED;
+      if (f32)
+        return up_sm100_reduce2d_f32(reinterpret_cast<const float*>(at(x)), x.shape[0], x.shape[1], x.stride[0], axis,
+                                     (int)sc(0, UP_OP_SUM), (int)sc(2, UP_ACCUM_AUTO), (int)sc(3, 256), (float*)at(y),
+                                     stream);
+      return up_sm100_reduce2d_i32(reinterpret_cast<const int32_t*>(at(x)), x.shape[0], x.shape[1], x.stride[0], axis,
+                                   (int)sc(0, UP_OP_SUM), (int32_t*)at(y), stream);
     }
     case UP_K_ROW_MAX_ARGMAX_BF16: {
       if (n_in < 1 || n_out < 2) return UP_ERR_INVALID;

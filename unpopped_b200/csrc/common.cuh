@@ -20,6 +20,8 @@ uint64_t wait_limit_ns();
 int take_withhold_flag();         // returns and clears the scan test hook
 int sm_count();                   // SMs of the current device (cached per device)
 int fail_with(int status, const char* text);  // records `text` as the last error, returns `status`
+int row_mean_f32_auto(const float* x, int64_t rows, int64_t cols, int64_t row_stride, int block, float* out,
+                      void* stream);  // reduce.cu: the Auto row sum divided by cols
 
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 

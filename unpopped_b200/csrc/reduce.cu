@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(kRowThreads) row_sum_f32_kernel(const float* _
 // ===================================================================================================
 template <int V>
 __global__ void row_sum_auto_kernel(const float* __restrict__ x, int64_t rows, int64_t cols, int64_t stride,
-                                    int B, float* __restrict__ out) {
+                                    int B, bool mean, float* __restrict__ out) {
   extern __shared__ double sacc[];  // [rows per CTA][B]
   const int P = B / V;
   const int rpc = blockDim.x / P;
@@ -123,7 +123,8 @@ __global__ void row_sum_auto_kernel(const float* __restrict__ x, int64_t rows, i
         for (int t = p; t < st; t += P) s[t] += s[t + st];
       __syncthreads();
     }
-    if (lr < rpc && p == 0 && r < rows) out[r] = __double2float_rn(s[0]);
+    // Mean divides the f64 total by the extent before the one rounding (block_reduce.rs:13-23)
+    if (lr < rpc && p == 0 && r < rows) out[r] = __double2float_rn(mean ? s[0] / (double)cols : s[0]);
     __syncthreads();
   }
 }
@@ -342,6 +343,39 @@ __global__ void __launch_bounds__(256) reduce_i32_kernel(const int32_t* __restri
 
 using namespace up;
 
+// The Auto row sum (documented f64 order of a logical block of B threads); with `mean` it divides by cols before
+// the one rounding.
+static int launch_row_sum_auto(const float* x, int64_t rows, int64_t cols, int64_t row_stride, int block, bool mean,
+                               float* out, cudaStream_t s) {
+  if (block < 1 || block > 1024 || (block & (block - 1)) != 0) return UP_ERR_UNSUPPORTED;
+  const bool vec = aligned(x, 16) && (cols % 4 == 0) && (row_stride % 4 == 0);
+  if (vec && block >= 4) {
+    const int P = block / 4, threads = 256, rpc = threads / P;
+    const int64_t g = (rows + rpc - 1) / rpc;
+    const size_t smem = (size_t)rpc * block * sizeof(double);
+    row_sum_auto_kernel<4><<<(int)(g < (1 << 30) ? g : (1 << 30)), threads, smem, s>>>(x, rows, cols, row_stride,
+                                                                                       block, mean, out);
+  } else {
+    const int threads = block > 256 ? block : 256, rpc = threads / block;
+    const int64_t g = (rows + rpc - 1) / rpc;
+    const size_t smem = (size_t)rpc * block * sizeof(double);
+    row_sum_auto_kernel<1><<<(int)(g < (1 << 30) ? g : (1 << 30)), threads, smem, s>>>(x, rows, cols, row_stride,
+                                                                                       block, mean, out);
+  }
+  return UP_OK;
+}
+
+namespace up {
+int row_mean_f32_auto(const float* x, int64_t rows, int64_t cols, int64_t row_stride, int block, float* out,
+                      void* stream) {
+  if (rows == 0) return UP_OK;
+  const int st = launch_row_sum_auto(x, rows, cols, row_stride, block, true, out, static_cast<cudaStream_t>(stream));
+  if (st != UP_OK) return st;
+  note_launch();
+  return check_launch();
+}
+}  // namespace up
+
 extern "C" int up_sm100_row_sum_f32(const float* x, int64_t rows, int64_t cols, int64_t row_stride, float* out,
                                     int accum, int block, void* stream) {
   UP_CHECK_ARG(rows >= 0 && cols >= 0 && row_stride >= cols);
@@ -355,20 +389,8 @@ extern "C" int up_sm100_row_sum_f32(const float* x, int64_t rows, int64_t cols, 
     if (vec) row_sum_f32_kernel<true><<<grid, kRowThreads, 0, s>>>(x, rows, cols, row_stride, out);
     else row_sum_f32_kernel<false><<<grid, kRowThreads, 0, s>>>(x, rows, cols, row_stride, out);
   } else if (accum == UP_ACCUM_AUTO) {
-    if (block < 1 || block > 1024 || (block & (block - 1)) != 0) return UP_ERR_UNSUPPORTED;
-    if (vec && block >= 4) {
-      const int P = block / 4, threads = 256, rpc = threads / P;
-      const int64_t g = (rows + rpc - 1) / rpc;
-      const size_t smem = (size_t)rpc * block * sizeof(double);
-      row_sum_auto_kernel<4><<<(int)(g < (1 << 30) ? g : (1 << 30)), threads, smem, s>>>(x, rows, cols,
-                                                                                         row_stride, block, out);
-    } else {
-      const int threads = block > 256 ? block : 256, rpc = threads / block;
-      const int64_t g = (rows + rpc - 1) / rpc;
-      const size_t smem = (size_t)rpc * block * sizeof(double);
-      row_sum_auto_kernel<1><<<(int)(g < (1 << 30) ? g : (1 << 30)), threads, smem, s>>>(x, rows, cols,
-                                                                                         row_stride, block, out);
-    }
+    const int st = launch_row_sum_auto(x, rows, cols, row_stride, block, false, out, s);
+    if (st != UP_OK) return st;
   } else {
     return UP_ERR_UNSUPPORTED;
   }

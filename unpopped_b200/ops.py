@@ -77,6 +77,30 @@ def row_sum(x: torch.Tensor, accum: str = "f32", block: int = 256, out: torch.Te
 
 
 # ---- max + argmax ----
+def reduce2d(x: torch.Tensor, op: str, axis: int = 1, accum: str = "auto", block: int | None = None,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """Reduction of a [rows, cols] f32 or i32 tensor with contiguous rows over axis 1 (the last; one value per
+    row) or axis 0 (the outer; one per column). f32: sum, mean, max, min; i32: sum, prod, max, min, and, or, xor."""
+    _cuda(x, "x")
+    if x.dim() != 2 or x.stride(1) != 1 or x.dtype not in (torch.float32, torch.int32):
+        raise ValueError("reduce2d takes a 2-D float32 or int32 tensor with contiguous rows")
+    if axis not in (0, 1):
+        raise ValueError("axis is 0 or 1")
+    rows, cols = x.shape
+    n = rows if axis == 1 else cols
+    if out is None:
+        out = torch.empty(n, dtype=x.dtype, device=x.device)
+    L = _lib.load()
+    if x.dtype == torch.float32:
+        b = block if block is not None else (256 if axis == 1 else 1)
+        check(L.up_sm100_reduce2d_f32(x.data_ptr(), rows, cols, x.stride(0), axis, OP[op.upper()],
+                                      ACCUM[accum.upper()], b, out.data_ptr(), _stream(x)), "reduce2d_f32")
+    else:
+        check(L.up_sm100_reduce2d_i32(x.data_ptr(), rows, cols, x.stride(0), axis, OP[op.upper()], out.data_ptr(),
+                                      _stream(x)), "reduce2d_i32")
+    return out
+
+
 def row_max_argmax(x: torch.Tensor, index_dtype=torch.int32, want_max: bool = True, want_argmax: bool = True):
     """(max as f32, argmax) of each row of a 2-D bf16 tensor: NaN-propagating max, first index of the maximum
     with NaN the greatest value."""
