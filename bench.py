@@ -244,6 +244,20 @@ def bench_lifts(ctx, K, W, hbm, bf16):
     record("rowsum_f32_8192x8192", wl.rowsum_bytes(), ms, "row_sum_f32_kernel", R)
     ms, _, _ = ctx.timed(lambda i, kin: ops.row_sum(xs[i % R], "auto", 1024, out=out), K, W)
     record("rowsum_f32_auto_f64order_B1024", wl.rowsum_bytes(), ms, "row_sum_auto_kernel", R)
+    # the reduction breadth on the same input: f32 Max over the last axis, and Max over the outer axis
+    ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xs[i % R], "max", 1, out=out), K, W)
+    record("rowmax_f32_8192x8192", wl.rowsum_bytes(), ms, "row_extremum_f32_kernel", R)
+    ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xs[i % R], "max", 0, out=out), K, W)
+    record("colmax_f32_8192x8192", wl.rowsum_bytes(), ms, "col_extremum_f32_kernel", R)
+    ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xs[i % R], "sum", 0, block=256, out=out), K, W)
+    record("colsum_f32_documented_B256", wl.rowsum_bytes(), ms, "col_sum_f32_doc_kernel", R)
+    xi = [x.view(torch.int32) for x in xs]  # the same bytes read as i32
+    oi = out.view(torch.int32)
+    ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xi[i % R], "xor", 1, out=oi), K, W)
+    record("rowxor_i32_8192x8192", wl.rowsum_bytes(), ms, "row_fold_i32_kernel", R)
+    ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xi[i % R], "sum", 0, out=oi), K, W)
+    record("colsum_i32_8192x8192", wl.rowsum_bytes() + 8192 * 4, ms, "col_fold_i32_kernel", R)
+    del xi, oi
     del xs, out
 
     # config 2 variants: exclusive add and inclusive max (the headline is the inclusive add)

@@ -218,7 +218,8 @@ UP_API int up_sm100_row_sum_f32(const float* x, int64_t rows, int64_t cols, int6
  * 501-651, plan_contract.rs:146-245).
  * f32: op SUM, MEAN, MAX or MIN. Over the last axis Sum/Mean follow `accum` (Mean: Auto only) and the launched
  * lift's documented order for logical block `block` (kernel_lift/block_reduce.rs:13-23); over the outer axis
- * Sum/Mean fold each column in the serial order (Auto only). Max/Min are NaN-propagating and bit-exact to the
+ * Sum/Mean follow the same documented order down each column for a block of up to 256 (block 1: the serial
+ * order; Auto only). Max/Min are NaN-propagating and bit-exact to the
  * serial fold: the last NaN (quiet bit set) if any, else the first element of the extreme value.
  * i32: op SUM or PROD (both wrapping), MAX, MIN, AND, OR or XOR; bit-exact. An empty fold stores 0 (1 for Prod;
  * an f32 Mean: 0/0). */

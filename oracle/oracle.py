@@ -43,6 +43,7 @@ def lib():
         L.orc_reduce2d_f32.argtypes = [P, I64, I64, I64, I, I, P, I]
         L.orc_row_mean_f32_documented.argtypes = [P, I64, I64, I64, I64, P, I]
         L.orc_reduce2d_i32.argtypes = [P, I64, I64, I64, I, I, P, I]
+        L.orc_col_sum_f32_documented.argtypes = [P, I64, I64, I64, I64, I, P, I]
         L.orc_scan_i32.argtypes = [P, P, I64, I64, I, I, I, ctypes.c_int32, I]
         L.orc_scan_i32_chunked.argtypes = [P, P, I64, I, I, I]
         L.orc_reduce_i32.argtypes = [P, I64, I]
@@ -122,6 +123,15 @@ def row_mean_f32_documented(x: np.ndarray, block: int, threads: int = 1) -> np.n
     rows, cols = x.shape
     out = np.empty(rows, np.float32)
     lib().orc_row_mean_f32_documented(_p(x), rows, cols, cols, block, _p(out), threads)
+    return out
+
+
+def col_sum_f32_documented(x: np.ndarray, block: int, mean: bool = False, threads: int = 1) -> np.ndarray:
+    """Sum/Mean over the outer axis in the launched lift's documented order (kernel_lift/block_reduce.rs:13-30)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, cols = x.shape
+    out = np.empty(cols, np.float32)
+    lib().orc_col_sum_f32_documented(_p(x), rows, cols, cols, block, int(mean), _p(out), threads)
     return out
 
 

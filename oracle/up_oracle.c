@@ -234,6 +234,29 @@ void orc_row_mean_f32_documented(const float* x, int64_t rows, int64_t cols, int
   }
 }
 
+/* Sum (or Mean) over the outer axis of a rank-2 f32 input in the launched lift's documented order
+ * (kernel_lift/block_reduce.rs:13-30: with the outer axis reduced, logical thread t folds rows t, t+B, ... of each
+ * column into an f64; then acc[t] += acc[t+s] for s = B/2 .. 1; Mean divides by the row count; one rounding). */
+void orc_col_sum_f32_documented(const float* x, int64_t rows, int64_t cols, int64_t row_stride, int64_t block,
+                                int mean, float* out, int threads) {
+#pragma omp parallel num_threads(threads) if (threads > 1)
+  {
+    double* acc = (double*)malloc(sizeof(double) * (size_t)block);
+#pragma omp for schedule(static)
+    for (int64_t c = 0; c < cols; ++c) {
+      for (int64_t t = 0; t < block; ++t) {
+        double a = 0.0;
+        for (int64_t r = t; r < rows; r += block) a += (double)x[r * row_stride + c];
+        acc[t] = a;
+      }
+      for (int64_t s = block / 2; s > 0; s /= 2)
+        for (int64_t t = 0; t < s; ++t) acc[t] += acc[t + s];
+      out[c] = mean ? (float)(acc[0] / (double)rows) : (float)acc[0];
+    }
+    free(acc);
+  }
+}
+
 /* eval_reduction for a rank-2 i32 input over one axis: the oracle folds in an i128 wrapped at 64 bits and the store
  * truncates to 32 (plan_eval.rs:530-545), which for Sum and Prod is wrapping 32-bit arithmetic; Max/Min take the
  * first element and then a strictly better one; And/Or/Xor are seeded by the first element (bit_fold); an empty fold

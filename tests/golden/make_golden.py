@@ -108,6 +108,9 @@ def golden_float_sum() -> dict:
         "max_f32_bits": [f32_bits(serial_extremum(r, True)) for r in rows],
         "min_f32_bits": [f32_bits(serial_extremum(r, False)) for r in rows],
         "col_sum_f32_bits": [f32_bits(documented([r[c] for r in rows], 1)) for c in range(96)],
+        # the corpus's transpose as a [96, 5] input reduced over its outer axis: each column of that input is a row
+        # of the corpus, so the documented order over the outer axis gives the row sums above
+        "col_documented_blocks": [1, 2, 8, 32, 16],
         "col_max_f32_bits": [f32_bits(serial_extremum([r[c] for r in rows], True)) for c in range(96)],
     }
 

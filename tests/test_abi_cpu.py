@@ -107,7 +107,7 @@ def test_dispatch_table_maps_each_lift():
     (_red("PROD", "F32"), "UnsupportedOp"),
     (_red("SUM", "F32", shape=(4, 8, 16), axes_mask=2), "UnsupportedPlanShape"),  # a middle axis
     (_red("SUM", "F32", axes_mask=1), "UnsupportedOp"),  # outer axis under the F32 policy: Auto only
-    (_red("SUM", "F32", axes_mask=1, accum="AUTO", block=4), "UnsupportedPlanShape"),  # outer Sum: serial order
+    (_red("SUM", "F32", axes_mask=1, accum="AUTO", block=512), "UnsupportedPlanShape"),  # outer block <= 256
     (_red("MEAN", "I32"), "UnsupportedOp"),  # the oracle has no integer Mean
     (_red("AND", "F32"), "UnsupportedOp"),  # bit folds are integer-only
     (_red("ARGMAX", "F32", "I64"), "UnsupportedDtype"),

@@ -48,6 +48,9 @@ def test_float_corpus_mean_max_min_columns():
     assert bits(ops.reduce2d(x, "min", 1).cpu()).tolist() == g["min_f32_bits"]
     assert bits(ops.reduce2d(x, "sum", 0).cpu()).tolist() == g["col_sum_f32_bits"]
     assert bits(ops.reduce2d(x, "max", 0).cpu()).tolist() == g["col_max_f32_bits"]
+    xt = torch.from_numpy(np.ascontiguousarray(xn.T)).cuda()  # the corpus's rows as columns
+    for b in g["col_documented_blocks"]:
+        assert bits(ops.reduce2d(xt, "sum", 0, block=b).cpu()).tolist() == g["documented_f32_bits"][str(b)], b
 
 
 SHAPES = [(1, 1), (3, 7), (17, 96), (64, 4097), (33, 8192), (1000, 5), (5, 1000), (300, 1024)]
@@ -96,9 +99,14 @@ def test_float_sum_mean_vs_oracle(rows, cols):
     rng = np.random.default_rng(rows * 3 + cols)
     xn = (rng.standard_normal((rows, cols)) * 10.0 ** rng.integers(-3, 4, (rows, 1))).astype(np.float32)
     x = torch.from_numpy(xn).cuda()
-    # outer axis: the serial order per column
+    # outer axis: the serial order per column (block 1) and the documented order of larger blocks
     assert np.array_equal(bits(ops.reduce2d(x, "sum", 0).cpu()), bits(orc.reduce2d_f32(xn, "sum", 0)))
     assert np.array_equal(bits(ops.reduce2d(x, "mean", 0).cpu()), bits(orc.reduce2d_f32(xn, "mean", 0)))
+    for b in (2, 16, 64, 256):
+        assert np.array_equal(bits(ops.reduce2d(x, "sum", 0, block=b).cpu()),
+                              bits(orc.col_sum_f32_documented(xn, b))), b
+        assert np.array_equal(bits(ops.reduce2d(x, "mean", 0, block=b).cpu()),
+                              bits(orc.col_sum_f32_documented(xn, b, mean=True))), b
     # last axis: the documented order for each block (block 1 is the serial order)
     for b in (1, 4, 256, 1024):
         assert np.array_equal(bits(ops.reduce2d(x, "mean", 1, block=b).cpu()),
@@ -146,6 +154,8 @@ def test_full_config_rows():
     for op in ("max", "min"):
         for axis in (0, 1):
             assert np.array_equal(bits(ops.reduce2d(x, op, axis).cpu()), bits(orc.reduce2d_f32(xn, op, axis, t)))
+    assert np.array_equal(bits(ops.reduce2d(x, "sum", 0, block=256).cpu()),
+                          bits(orc.col_sum_f32_documented(xn, 256, threads=t)))
     xi = rng.integers(-2**31, 2**31, (8192, 8192), dtype=np.int64).astype(np.int32)
     xit = torch.from_numpy(xi).cuda()
     for op in INT_OPS:

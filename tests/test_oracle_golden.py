@@ -89,6 +89,9 @@ def test_float_mean_max_min_and_columns():
     assert bits(orc.reduce2d_f32(x, "min", 1)) == g["min_f32_bits"]
     assert bits(orc.reduce2d_f32(x, "sum", 0)) == g["col_sum_f32_bits"]
     assert bits(orc.reduce2d_f32(x, "max", 0)) == g["col_max_f32_bits"]
+    xt = np.ascontiguousarray(x.T)  # the corpus's rows as the columns of a [96, 5] input
+    for b in g["col_documented_blocks"]:
+        assert bits(orc.col_sum_f32_documented(xt, b)) == g["documented_f32_bits"][str(b)], b
 
 
 def test_float_extremum_nan_and_zero_rules():

@@ -177,8 +177,8 @@ extern "C" int up_sm100_classify(const up_plan_desc* p, up_lowered* out) {
           return refuse(out, UP_LOWER_UNSUPPORTED_OP, "accumulation policy");
         const int b = p->block ? p->block : (axis == 1 ? 256 : 1);
         if (b < 1 || b > 1024 || (b & (b - 1))) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "block B");
-        if (summing && axis == 0 && b != 1)
-          return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "an outer-axis Sum/Mean folds in the serial order");
+        if (summing && axis == 0 && b > 256)
+          return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "an outer-axis Sum/Mean takes a block of at most 256");
         if (p->op == UP_OP_SUM && axis == 1) return accept(out, UP_K_ROW_SUM_F32, {p->accum, b});
         return accept(out, UP_K_REDUCE2D_F32, {p->op, axis, p->accum, b});
       }

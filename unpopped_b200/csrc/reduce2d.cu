@@ -9,11 +9,14 @@
 //    these is associative and commutative, so any combine order gives the oracle's bits.
 //  * f32 Max/Min keep the first element and replace it by a NaN or by a strictly better value: the result is the
 //    row's last NaN if it has one (widened through f64 and back, so with the quiet bit set), else the first
-//    element of the extreme value (so the first zero's sign when +0 and -0 tie). The kernels reduce a packed
-//    (order key, inverted index) word and a last-NaN index, both order-independent, then copy that element's bits.
+//    element of the extreme value (so the first zero's sign when +0 and -0 tie). The kernels keep the best value
+//    with its first index and the last NaN's index; merging those by value (ties to the lower index) is
+//    order-independent.
 //  * f32 Sum/Mean over the outer axis fold each column in the serial order in f64 (one thread per column: the
 //    order is the oracle's, not a tree), one rounding; Mean divides by the row count, so an empty Mean is 0/0.
 #include "common.cuh"
+
+#include <mutex>
 
 namespace up {
 namespace r2 {
@@ -133,109 +136,204 @@ __global__ void __launch_bounds__(kThreads) col_fold_i32_kernel(const int32_t* _
 }
 
 // ---- f32 Max/Min ----
-// Order key of a non-NaN f32 (-0 counted as +0); MIN ranks by the inverted key. The packed word puts the key above
-// the inverted index, so the greatest word is the best value at its first index; 0 means "no element".
-template <bool MAX>
-__device__ __forceinline__ uint64_t ext_pack(uint32_t u, uint32_t idx) {
-  if (u == 0x80000000u) u = 0;
-  const uint32_t key = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return ((uint64_t)(MAX ? key : ~key) << 32) | (uint64_t)(0xffffffffu - idx);
-}
-
-__device__ __forceinline__ bool f32_isnan_bits(uint32_t u) { return (u & 0x7fffffffu) > 0x7f800000u; }
+// The fold's state: the best value so far with its first index (idx = kNone: no non-NaN element yet) and the last
+// NaN's index. A thread takes its elements in ascending index order and replaces only on a strictly better value,
+// so it keeps the first of equal values (and of +0/-0). The value is the element itself, bits and all, so the
+// result needs no re-read unless it is a NaN. Two states combine by value, ties to the lower index.
+constexpr uint32_t kNone = 0xffffffffu;
 
 template <bool MAX>
-__device__ __forceinline__ void ext_take(uint32_t u, uint32_t idx, uint64_t& best, int64_t& nan_idx) {
-  if (f32_isnan_bits(u)) {
-    nan_idx = (int64_t)idx > nan_idx ? (int64_t)idx : nan_idx;
-  } else {
-    const uint64_t p = ext_pack<MAX>(u, idx);
-    best = p > best ? p : best;
+struct ExtState {
+  float m;
+  uint32_t idx;
+  int32_t nan_idx;
+  __device__ __forceinline__ void init() {
+    m = MAX ? -__int_as_float(0x7f800000) : __int_as_float(0x7f800000);
+    idx = kNone;
+    nan_idx = -1;
   }
-}
-
-// the result's bits from the fold's state: the last NaN (quiet bit set), else the best element, else 0 (empty)
-__device__ __forceinline__ uint32_t ext_result(const float* base, int64_t step, uint64_t best, int64_t nan_idx) {
-  if (nan_idx >= 0) return __float_as_uint(base[nan_idx * step]) | 0x00400000u;
-  if (best == 0) return 0u;
-  return __float_as_uint(base[(int64_t)(0xffffffffu - (uint32_t)best) * step]);
-}
+  __device__ __forceinline__ void take(float v, uint32_t i) {  // i ascending within a thread
+    const bool is_nan = v != v;
+    const bool take_v = !is_nan && ((MAX ? v > m : v < m) || idx == kNone);
+    m = take_v ? v : m;
+    idx = take_v ? i : idx;
+    nan_idx = is_nan ? (int32_t)i : nan_idx;
+  }
+  __device__ __forceinline__ void merge(float om, uint32_t oidx, int32_t onan) {
+    nan_idx = onan > nan_idx ? onan : nan_idx;
+    if (oidx == kNone) return;
+    const bool better = idx == kNone || (MAX ? om > m : om < m) || (om == m && oidx < idx);
+    m = better ? om : m;
+    idx = better ? oidx : idx;
+  }
+  __device__ __forceinline__ void warp_merge() {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, m, o);
+      const uint32_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      const int32_t on = __shfl_xor_sync(0xffffffffu, nan_idx, o);
+      merge(om, oi, on);
+    }
+  }
+  // the result's bits: the last NaN (quiet bit set), else the best element, else 0 (empty)
+  __device__ __forceinline__ uint32_t result(const float* base, int64_t step) const {
+    if (nan_idx >= 0) return __float_as_uint(base[(int64_t)nan_idx * step]) | 0x00400000u;
+    return idx == kNone ? 0u : __float_as_uint(m);
+  }
+};
 
 template <bool MAX, bool VEC>
 __global__ void __launch_bounds__(kThreads) row_extremum_f32_kernel(const float* __restrict__ x, int64_t rows,
                                                                      int64_t cols, int64_t stride,
                                                                      float* __restrict__ out) {
-  __shared__ uint64_t sbest[kThreads / 32];
-  __shared__ int64_t snan[kThreads / 32];
+  __shared__ float sm[kThreads / 32];
+  __shared__ uint32_t si[kThreads / 32];
+  __shared__ int32_t sn[kThreads / 32];
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const float* row = x + r * stride;
-    uint64_t best = 0;
-    int64_t nan_idx = -1;
+    ExtState<MAX> st;
+    st.init();
     if (VEC) {
       const int64_t nv = cols / 4;
-      for (int64_t i = threadIdx.x; i < nv; i += kThreads) {
+      int64_t i = threadIdx.x;
+      for (; i + 3 * kThreads < nv; i += 4 * kThreads) {
+        float4 f[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) f[u] = ld_nc_na_f4(row + 4 * (i + u * kThreads));
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t c = (uint32_t)(4 * (i + u * kThreads));
+          st.take(f[u].x, c);
+          st.take(f[u].y, c + 1);
+          st.take(f[u].z, c + 2);
+          st.take(f[u].w, c + 3);
+        }
+      }
+      for (; i < nv; i += kThreads) {
         const float4 f = ld_nc_na_f4(row + 4 * i);
         const uint32_t c = (uint32_t)(4 * i);
-        ext_take<MAX>(__float_as_uint(f.x), c, best, nan_idx);
-        ext_take<MAX>(__float_as_uint(f.y), c + 1, best, nan_idx);
-        ext_take<MAX>(__float_as_uint(f.z), c + 2, best, nan_idx);
-        ext_take<MAX>(__float_as_uint(f.w), c + 3, best, nan_idx);
+        st.take(f.x, c);
+        st.take(f.y, c + 1);
+        st.take(f.z, c + 2);
+        st.take(f.w, c + 3);
       }
     } else {
-      for (int64_t c = threadIdx.x; c < cols; c += kThreads)
-        ext_take<MAX>(__float_as_uint(__ldg(row + c)), (uint32_t)c, best, nan_idx);
+      for (int64_t c = threadIdx.x; c < cols; c += kThreads) st.take(__ldg(row + c), (uint32_t)c);
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const uint64_t b = __shfl_xor_sync(0xffffffffu, best, o);
-      const int64_t n = __shfl_xor_sync(0xffffffffu, nan_idx, o);
-      best = b > best ? b : best;
-      nan_idx = n > nan_idx ? n : nan_idx;
-    }
+    st.warp_merge();
+    const int w = threadIdx.x >> 5;
     if ((threadIdx.x & 31) == 0) {
-      sbest[threadIdx.x >> 5] = best;
-      snan[threadIdx.x >> 5] = nan_idx;
+      sm[w] = st.m;
+      si[w] = st.idx;
+      sn[w] = st.nan_idx;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-      for (int i = 1; i < kThreads / 32; ++i) {
-        best = sbest[i] > best ? sbest[i] : best;
-        nan_idx = snan[i] > nan_idx ? snan[i] : nan_idx;
-      }
-      best = sbest[0] > best ? sbest[0] : best;
-      nan_idx = snan[0] > nan_idx ? snan[0] : nan_idx;
-      out[r] = __uint_as_float(ext_result(row, 1, best, nan_idx));
+      for (int k = 1; k < kThreads / 32; ++k) st.merge(sm[k], si[k], sn[k]);
+      out[r] = __uint_as_float(st.result(row, 1));
     }
     __syncthreads();
   }
 }
 
-// f32 over the outer axis, one thread per column folding the rows in order: Sum/Mean in f64 (the serial order),
-// Max/Min by the packed rule.
+// f32 Max/Min over the outer axis: a CTA takes 32 columns (one per lane, coalesced across the row) and its 16 warps
+// split the rows (warp w folds rows w, w + 16, ... in order); the 16 partials of a column merge by value.
+constexpr int kColWarps = 16;
+template <bool MAX>
+__global__ void __launch_bounds__(32 * kColWarps) col_extremum_f32_kernel(const float* __restrict__ x, int64_t rows,
+                                                                          int64_t cols, int64_t stride,
+                                                                          float* __restrict__ out) {
+  __shared__ float sm[kColWarps][32];
+  __shared__ uint32_t si[kColWarps][32];
+  __shared__ int32_t sn[kColWarps][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t c = (int64_t)blockIdx.x * 32 + lane;
+  ExtState<MAX> st;
+  st.init();
+  if (c < cols) {
+    int64_t r = w;
+    for (; r + 3 * kColWarps < rows; r += 4 * kColWarps) {
+      float v[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) v[k] = __ldg(x + (r + k * kColWarps) * stride + c);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) st.take(v[k], (uint32_t)(r + k * kColWarps));
+    }
+    for (; r < rows; r += kColWarps) st.take(__ldg(x + r * stride + c), (uint32_t)r);
+  }
+  sm[w][lane] = st.m;
+  si[w][lane] = st.idx;
+  sn[w][lane] = st.nan_idx;
+  __syncthreads();
+  if (w == 0 && c < cols) {
+    for (int k = 1; k < kColWarps; ++k) st.merge(sm[k][lane], si[k][lane], sn[k][lane]);
+    out[c] = __uint_as_float(st.result(x + c, stride));
+  }
+}
+
+// f32 Sum/Mean over the outer axis, one thread per column folding the rows in order in f64 (the serial order; a
+// split of the rows would change the roundings).
 template <int OP>
 __global__ void __launch_bounds__(kThreads) col_f32_kernel(const float* __restrict__ x, int64_t rows, int64_t cols,
                                                             int64_t stride, float* __restrict__ out) {
+  static_assert(OP == UP_OP_SUM || OP == UP_OP_MEAN, "Sum or Mean");
   const int64_t c = (int64_t)blockIdx.x * kThreads + threadIdx.x;
   if (c >= cols) return;
-  if (OP == UP_OP_SUM || OP == UP_OP_MEAN) {
-    double acc = 0.0;
-    int64_t r = 0;
-    for (; r + 3 < rows; r += 4) {
-      float v[4];
+  double acc = 0.0;
+  int64_t r = 0;
+  for (; r + 3 < rows; r += 4) {
+    float v[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) v[u] = __ldg(x + (r + u) * stride + c);
+    for (int u = 0; u < 4; ++u) v[u] = __ldg(x + (r + u) * stride + c);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) acc += (double)v[u];
-    }
-    for (; r < rows; ++r) acc += (double)__ldg(x + r * stride + c);
-    out[c] = __double2float_rn(OP == UP_OP_MEAN ? acc / (double)rows : acc);
-  } else {
-    constexpr bool MAX = OP == UP_OP_MAX;
-    uint64_t best = 0;
-    int64_t nan_idx = -1;
-    for (int64_t r = 0; r < rows; ++r) ext_take<MAX>(__float_as_uint(__ldg(x + r * stride + c)), (uint32_t)r, best, nan_idx);
-    out[c] = __uint_as_float(ext_result(x + c, stride, best, nan_idx));
+    for (int u = 0; u < 4; ++u) acc += (double)v[u];
   }
+  for (; r < rows; ++r) acc += (double)__ldg(x + r * stride + c);
+  out[c] = __double2float_rn(OP == UP_OP_MEAN ? acc / (double)rows : acc);
+}
+
+// f32 Sum/Mean over the outer axis in the launched lift's documented order for a logical block of B threads
+// (kernel_lift/block_reduce.rs:13-30): logical thread t of column c folds rows t, t+B, t+2B, ... ascending into an
+// f64; then acc[t] += acc[t+s] for s = B/2 .. 1; Mean divides by the row count; one rounding. A CTA takes 32
+// columns (one per lane) and 16 warps; warp w holds logical threads w, w+16, ... (B/16 accumulators; B <= 256),
+// so each step loads B/16 rows per thread, all coalesced across the 32 columns. The tree runs in shared memory.
+constexpr int kDocWarps = 16, kDocMaxB = 256;
+template <bool MEAN>
+__global__ void __launch_bounds__(32 * kDocWarps) col_sum_f32_doc_kernel(const float* __restrict__ x, int64_t rows,
+                                                                         int64_t cols, int64_t stride, int B,
+                                                                         float* __restrict__ out) {
+  extern __shared__ double sacc[];  // [B][32]
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t c = (int64_t)blockIdx.x * 32 + lane;
+  const int J = B > kDocWarps ? B / kDocWarps : (w < B ? 1 : 0);  // logical threads of this warp
+  double acc[kDocMaxB / kDocWarps];
+#pragma unroll
+  for (int j = 0; j < kDocMaxB / kDocWarps; ++j) acc[j] = 0.0;
+  if (c < cols && J > 0) {
+    for (int64_t r0 = 0; r0 < rows; r0 += B) {
+      float v[kDocMaxB / kDocWarps];
+#pragma unroll
+      for (int j = 0; j < kDocMaxB / kDocWarps; ++j) {
+        const int64_t r = r0 + w + (int64_t)kDocWarps * j;
+        v[j] = (j < J && r < rows) ? __ldg(x + r * stride + c) : 0.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < kDocMaxB / kDocWarps; ++j)
+        if (j < J && r0 + w + (int64_t)kDocWarps * j < rows) acc[j] += (double)v[j];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kDocMaxB / kDocWarps; ++j)
+    if (j < J) sacc[(w + kDocWarps * j) * 32 + lane] = acc[j];
+  __syncthreads();
+  for (int sh = B >> 1; sh > 0; sh >>= 1) {
+    for (int i = threadIdx.x; i < sh * 32; i += 32 * kDocWarps) {
+      const int t = i >> 5, l = i & 31;
+      sacc[t * 32 + l] = sacc[t * 32 + l] + sacc[(t + sh) * 32 + l];
+    }
+    __syncthreads();
+  }
+  if (w == 0 && c < cols) out[c] = __double2float_rn(MEAN ? sacc[lane] / (double)rows : sacc[lane]);
 }
 
 template <int OP>
@@ -309,7 +407,7 @@ extern "C" int up_sm100_reduce2d_f32(const float* x, int64_t rows, int64_t cols,
       if (accum != UP_ACCUM_AUTO) return fail_with(UP_ERR_UNSUPPORTED, "reduce2d_f32: Mean is lowered for Auto");
       return row_mean_f32_auto(x, rows, cols, row_stride, block, out, stream);
     }
-    if (cols > 0xfffffffeLL) return UP_ERR_UNSUPPORTED;  // indices are packed in 32 bits
+    if (cols > 0x7fffffffLL) return UP_ERR_UNSUPPORTED;  // indices are 32-bit
     const int g = (int)(rows < (int64_t)sm_count() * 8 ? rows : (int64_t)sm_count() * 8);
     const bool vec = aligned(x, 16) && cols % 4 == 0 && row_stride % 4 == 0;
     if (op == UP_OP_MAX) {
@@ -322,17 +420,51 @@ extern "C" int up_sm100_reduce2d_f32(const float* x, int64_t rows, int64_t cols,
     note_launch();
     return check_launch();
   }
-  // axis 0: the serial order per column (Sum/Mean), so the accumulation policy must be Auto
+  // axis 0: Sum/Mean in the serial order (block 1) or the documented order of a logical block of up to 256
   if ((op == UP_OP_SUM || op == UP_OP_MEAN) && accum != UP_ACCUM_AUTO)
     return fail_with(UP_ERR_UNSUPPORTED, "reduce2d_f32: an outer-axis Sum/Mean is lowered for Auto");
-  if (rows > 0xfffffffeLL) return UP_ERR_UNSUPPORTED;
+  if ((op == UP_OP_SUM || op == UP_OP_MEAN) && block > 1) {
+    if (block > kDocMaxB || (block & (block - 1)) != 0)
+      return fail_with(UP_ERR_UNSUPPORTED, "reduce2d_f32: an outer-axis block is a power of two up to 256");
+    const size_t smem = (size_t)block * 32 * sizeof(double);
+    const unsigned g = (unsigned)((cols + 31) / 32);
+    {
+      static std::mutex mu;
+      static bool attr_set[64] = {false};
+      int dev = 0;
+      cudaError_t e = cudaGetDevice(&dev);
+      if (e != cudaSuccess) return cuda_status(e);
+      std::lock_guard<std::mutex> lk(mu);
+      if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        const int bytes = (int)((size_t)kDocMaxB * 32 * sizeof(double));
+        e = cudaFuncSetAttribute(col_sum_f32_doc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        if (e == cudaSuccess)
+          e = cudaFuncSetAttribute(col_sum_f32_doc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        if (e != cudaSuccess) return cuda_status(e);
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+      }
+    }
+    if (op == UP_OP_MEAN)
+      col_sum_f32_doc_kernel<true><<<g, 32 * kDocWarps, smem, s>>>(x, rows, cols, row_stride, block, out);
+    else
+      col_sum_f32_doc_kernel<false><<<g, 32 * kDocWarps, smem, s>>>(x, rows, cols, row_stride, block, out);
+    note_launch();
+    return check_launch();
+  }
+  if (rows > 0x7fffffffLL) return UP_ERR_UNSUPPORTED;
   const int64_t gx = (cols + kThreads - 1) / kThreads;
   if (gx > 0x7fffffff) return UP_ERR_UNSUPPORTED;
   switch (op) {
     case UP_OP_SUM: col_f32_kernel<UP_OP_SUM><<<(int)gx, kThreads, 0, s>>>(x, rows, cols, row_stride, out); break;
     case UP_OP_MEAN: col_f32_kernel<UP_OP_MEAN><<<(int)gx, kThreads, 0, s>>>(x, rows, cols, row_stride, out); break;
-    case UP_OP_MAX: col_f32_kernel<UP_OP_MAX><<<(int)gx, kThreads, 0, s>>>(x, rows, cols, row_stride, out); break;
-    default: col_f32_kernel<UP_OP_MIN><<<(int)gx, kThreads, 0, s>>>(x, rows, cols, row_stride, out); break;
+    case UP_OP_MAX:
+      col_extremum_f32_kernel<true><<<(unsigned)((cols + 31) / 32), 32 * kColWarps, 0, s>>>(x, rows, cols, row_stride,
+                                                                                         out);
+      break;
+    default:
+      col_extremum_f32_kernel<false><<<(unsigned)((cols + 31) / 32), 32 * kColWarps, 0, s>>>(x, rows, cols, row_stride,
+                                                                                          out);
+      break;
   }
   note_launch();
   return check_launch();
