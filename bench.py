@@ -410,6 +410,12 @@ def profile_cases(which: str):
         o = torch.empty(x.shape[0], device=dev)
         return lambda: ops.row_sum(x, "auto", block=1024, out=o)
 
+    @case("rowmax_f32")
+    def _():
+        x = wl.rowsum_input(device=dev)
+        o = torch.empty(x.shape[0], device=dev)
+        return lambda: ops.reduce2d(x, "max", 1, out=o)
+
     @case("argmax")
     def _():
         x = wl.argmax_input(rows=8192, device=dev)
@@ -450,7 +456,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--lifts", default="all", choices=["all", "none"])
     ap.add_argument("--profile", default=None,
-                    help="run only the small ncu case of one lift (scan, rowsum, rowsum_auto, argmax, gather, dequant, w4a16, all)")
+                    help="run only the small ncu case of one lift (scan, rowsum, rowsum_auto, rowmax_f32, argmax, gather, dequant, w4a16, all)")
     args = ap.parse_args()
     if args.profile:
         profile_cases(args.profile)
