@@ -12,30 +12,31 @@
 //    units are split evenly over one persistent CTA per SM (stream-K), so every SM streams the same share of
 //    W. Each k-block keeps its own accumulator (its own group scale), but a unit's hand-offs between the roles
 //    are paid once for UK k-blocks: measured, these hand-offs, not the data or the math, set the unit's time.
-//  * warp 26 (W loader): one thread brings each unit's W, 128 rows x 64 UK bytes, into a ring of shared-memory
+//  * warp 18 (W loader): one thread brings each unit's W, 128 rows x 64 UK bytes, into a ring of shared-memory
 //    stages with one TMA box (128-byte swizzled when a box row is 128 bytes; rows past N read as 0). The ring holds
 //    128 KiB, far ahead of use, and the load path of the SM stays free for everything else: the plain 16-byte loads
 //    this replaced put 32 rows' worth of sector requests behind every warp instruction.
-//  * warps 0..15 (dequant): warp w owns TMEM lane quarter w % 4 and k-quarter w / 4, so thread (w, lane) owns row
-//    32 (w % 4) + lane of the tile and 32 UK k of every unit: 16 UK bytes of W, read from the W stage (conflict
-//    free under the swizzle). It turns the nibbles into exact bf16 (a shift, one lop3 and one bf16x2 subtract per
+//  * warps 0..7 (dequant): warp w owns TMEM lane quarter w % 4 and k-quarters 2 (w / 4) and 2 (w / 4) + 1, so
+//    thread (w, lane) owns row 32 (w % 4) + lane of the tile and 64 UK k of every unit: 32 UK bytes of W, read from
+//    the W stage (conflict free under the swizzle). Each k-quarter is released to its issuer as soon as it is in
+//    tensor memory. (Sixteen warps, one k-quarter each, measured 1 % slower and left fewer registers per thread.) It turns the nibbles into exact bf16 (a shift, one lop3 and one bf16x2 subtract per
 //    pair, pairing k with k + 4) and stores them into tensor memory (tcgen05.st) as the MMA's A operand, whose k
 //    order inside each group of 8 is therefore 0,4,1,5,2,6,3,7.
-//  * warps 16..19 (MMA issuers): a single thread issues only about one tcgen05.mma per ~100 cycles, so four
+//  * warps 8..11 (MMA issuers): a single thread issues only about one tcgen05.mma per ~100 cycles, so four
 //    threads share a unit's 8 UK k-steps as pipelines: issuer g runs the 2 UK k-steps of k-quarter g into
 //    its k-block's accumulator after the issuer before it in that k-block has issued its own (an mbarrier
 //    hand-off between tcgen05.fence::before_thread_sync and ::after_thread_sync orders them), so each
 //    k-block ends in one accumulator while several units are in issue at once. (Four separate accumulators per unit were measured
 //    slower: the epilogue's reads of four times the tensor-memory data cost more than the hand-offs.)
-//  * warp 24 (activation loader): one thread brings each unit's [16 x 128 UK] activation tile into a ring of
+//  * warp 16 (activation loader): one thread brings each unit's [16 x 128 UK] activation tile into a ring of
 //    shared-memory stages with 2 UK TMA boxes, 128-byte swizzled as the MMA reads it; rows past M read as 0.
-//  * warp 27 (activation permuter): rewrites each landed 16-byte chunk (8 k) in place to the k order 0,4,1,5,2,6,
+//  * warp 19 (activation permuter): rewrites each landed 16-byte chunk (8 k) in place to the k order 0,4,1,5,2,6,
 //    3,7 of the A operand (the swizzle moves whole chunks, so it is unaffected), then releases the stage to the MMA.
-//  * warp 25 (scale loader): one thread brings each unit's scales, f16 groups [g0, g0 + 16) of its 128 rows with
+//  * warp 17 (scale loader): one thread brings each unit's scales, f16 groups [g0, g0 + 16) of its 128 rows with
 //    g0 = the unit's first group rounded down to a multiple of 8, into a ring of shared-memory slots with one TMA
 //    box. (A scale row stride that is not a multiple of 16 bytes cannot be a TMA tensor; then the warp's lanes load
 //    and store the same slot layout.) Loading them in the epilogue put a global-load latency on every unit.
-//  * warps 20..23 (epilogue): read the unit's accumulators (tcgen05.ld), scale each by scale[n][k-block] in
+//  * warps 12..15 (epilogue): read the unit's accumulators (tcgen05.ld), scale each by scale[n][k-block] in
 //    f32 and accumulate in registers, k-block by k-block. A tile finished inside one CTA is written as bf16;
 //    a tile split between CTAs writes f32 partials, and whichever CTA finishes it last (an atomic count)
 //    sums them in CTA order, writes bf16 and clears the partials — no CTA ever waits on another.
@@ -57,12 +58,12 @@ namespace w4 {
 constexpr int kTileN = 128;                      // W rows per tile = MMA M
 constexpr int kMmaN = 16;                        // activation rows = MMA N
 constexpr int kKB = 128;                         // k per unit
-constexpr int kDqWarps = 16;                     // warps 0..15
-constexpr int kIssuers = 4;                      // warps 16..19
-constexpr int kEpiWarps = 4;                     // warps 20..23
+constexpr int kDqWarps = 8;                      // warps 0..7
+constexpr int kIssuers = 4;                      // warps 8..11
+constexpr int kEpiWarps = 4;                     // warps 12..15
 constexpr int kIss0 = kDqWarps, kEpi0 = kIss0 + kIssuers, kXWarp = kEpi0 + kEpiWarps, kScWarp = kXWarp + 1;
 constexpr int kWWarp = kScWarp + 1, kXpWarp = kWWarp + 1;
-constexpr int kThreads = 32 * (kXpWarp + 1);     // 896
+constexpr int kThreads = 32 * (kXpWarp + 1);     // 640
 constexpr int kScRing = 8;                       // units of scales staged in shared memory
 constexpr int kScCols = 16;                      // f16 scales per row in a slot: groups [g0, g0 + 16), g0 % 8 == 0
 constexpr uint32_t kSleepNs = 64;                // pause between polls of a waiting dequant/epilogue/loader warp
@@ -301,8 +302,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
 
   if (warp < kDqWarps) {
-    // ---------------- dequant: row 32 (warp % 4) + lane, k-quarter warp / 4 ----------------
-    const int lq = warp & 3, kq = warp >> 2;
+    // ---------------- dequant: row 32 (warp % 4) + lane, k-quarters 2 (warp / 4) and 2 (warp / 4) + 1 ----------------
+    const int lq = warp & 3, kh = warp >> 2;  // k-half kh: k-quarters 2 kh and 2 kh + 1
     const int r = lq * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(lq * 32) << 16;
     // this thread's 16-byte chunks of its row in a W stage: chunk UK kq + h, 128-byte swizzled when UK = 2
@@ -317,13 +318,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
       }
-      uint4 cur[UK];
+      uint4 cur[2][UK];
 #pragma unroll
-      for (int h = 0; h < UK; ++h) {
-        const int c = UK * kq + h;
-        const int cs = UK == 2 ? (c ^ (r & 7)) : c;
-        cur[h] = *reinterpret_cast<const uint4*>(wrow + (size_t)(i % C::kWStages) * C::kWUnit + (cs << 4));
-      }
+      for (int qq = 0; qq < 2; ++qq)
+#pragma unroll
+        for (int h = 0; h < UK; ++h) {
+          const int c = UK * (2 * kh + qq) + h;
+          const int cs = UK == 2 ? (c ^ (r & 7)) : c;
+          cur[qq][h] = *reinterpret_cast<const uint4*>(wrow + (size_t)(i % C::kWStages) * C::kWUnit + (cs << 4));
+        }
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&w_empty[i % C::kWStages]);
       {
@@ -337,17 +340,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
 #pragma unroll
-        for (int h = 0; h < UK; ++h) {
-          uint32_t regs[16];
-          const uint32_t wd[4] = {cur[h].x, cur[h].y, cur[h].z, cur[h].w};
+        for (int qq = 0; qq < 2; ++qq) {
+          const int kq = 2 * kh + qq;
 #pragma unroll
-          for (int wi = 0; wi < 4; ++wi) nib8_to_bf16x2_k4(wd[wi], regs + 4 * wi);
-          tc::st_32x32b_x16(tmem + lane_addr + C::kACol0 + a * C::kACols + 16 * (UK * kq + h), regs);
+          for (int h = 0; h < UK; ++h) {
+            uint32_t regs[16];
+            const uint32_t wd[4] = {cur[qq][h].x, cur[qq][h].y, cur[qq][h].z, cur[qq][h].w};
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) nib8_to_bf16x2_k4(wd[wi], regs + 4 * wi);
+            tc::st_32x32b_x16(tmem + lane_addr + C::kACol0 + a * C::kACols + 16 * (UK * kq + h), regs);
+          }
+          tc::wait_st();
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&a_full[4 * a + kq]);
         }
-        tc::wait_st();
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&a_full[4 * a + kq]);
       }
     }
   } else if (warp < kEpi0) {
