@@ -92,6 +92,11 @@ typedef enum up_schedule {
 } up_schedule;
 
 /* Kernel ids: what `up_sm100_classify` maps a plan to and `up_sm100_launch` runs. */
+/* `WriteCombine` (crates/unpopped/src/ir.rs:2723-2732), in declaration order. */
+typedef enum up_write_combine {
+  UP_COMBINE_ASSIGN = 0, UP_COMBINE_ADD = 1, UP_COMBINE_MAX = 2, UP_COMBINE_MIN = 3
+} up_write_combine;
+
 typedef enum up_kernel_id {
   UP_K_NONE = -1,
   UP_K_ROW_SUM_F32 = 1,
@@ -101,7 +106,9 @@ typedef enum up_kernel_id {
   UP_K_DEQUANT_I4 = 5,
   UP_K_W4A16_GEMM = 6,
   UP_K_REDUCE2D_F32 = 7,  /* f32 Sum/Mean/Max/Min over the last or the outer axis of a rank-2 input */
-  UP_K_REDUCE2D_I32 = 8   /* i32 Sum/Prod/Max/Min/And/Or/Xor, same axes */
+  UP_K_REDUCE2D_I32 = 8,  /* i32 Sum/Prod/Max/Min/And/Or/Xor, same axes */
+  UP_K_SCATTER = 9,       /* scatter / index_add with an atomic combine over axis 0 */
+  UP_K_BINCOUNT = 10
 } up_kernel_id;
 
 /* A buffer argument: the reference's TypedBuffer / OperandDesc. `base` and `stride` count elements
@@ -136,6 +143,11 @@ typedef struct up_plan_desc {
   int32_t n_operands;    /* inputs then outputs, at most 8 */
   up_tensor operands[8]; /* shapes/strides/dtypes only; ptr may be NULL */
   char target[32];       /* TargetId token, e.g. "cuda:sm_100a" or "cuda:sm100a" */
+  /* appended: the data-dependent WRITE role (WriteIndex::ScatterIndexed, ir.rs:2787-2850) */
+  int32_t has_write_index; /* Strided with a scatter store */
+  int32_t scatter_axis;    /* the scattered axis of the destination */
+  int32_t combine;         /* up_write_combine */
+  int32_t count;           /* bincount: the input is its own index and the increment is the constant 1 */
 } up_plan_desc;
 
 /* What `Backend::lower` returns (`GeneratedKernel{name, source}` + launch metadata), or why it refused
@@ -227,6 +239,22 @@ UP_API int up_sm100_reduce2d_f32(const float* x, int64_t rows, int64_t cols, int
                                  int accum, int block, float* out, void* stream);
 UP_API int up_sm100_reduce2d_i32(const int32_t* x, int64_t rows, int64_t cols, int64_t row_stride, int axis,
                                  int op, int32_t* out, void* stream);
+
+/* The launched Scatter lift (`WriteIndex::ScatterIndexed`, ir.rs:2787-2850; the oracle's scatter store,
+ * oracle/plan_eval.rs:430-490) over axis 0 of a row-major destination [out_rows, cols]: for every element (i, j) of
+ * `updates` [n, cols], the target row t is ids[i * ids_stride + j] (`ids_stride` = the index's row stride: a
+ * full-shape index, torch `scatter_add`) or ids[i] (`ids_stride` 0: `index_add`), and
+ * out[t][j] = combine(out[t][j], updates[i][j]); targets outside [0, out_rows) are skipped. `combine`: ADD, MAX or
+ * MIN (ASSIGN is declined, as the reference's launched lift declines it). `dtype`: I32, U32, I64 (every combine;
+ * bit-exact, integer add wraps) or F32, F64 (ADD only; within the reassociation band gamma_(n-1) * sum|terms|).
+ * `index_dtype`: I32, I64 or U32. Strides in elements. */
+UP_API int up_sm100_scatter(const void* updates, int64_t n, int64_t cols, int64_t upd_stride, int dtype,
+                            const void* ids, int index_dtype, int64_t ids_stride, int combine, void* out,
+                            int64_t out_rows, int64_t out_stride, void* stream);
+
+/* bincount (`OpDef::bincount`; crates/unpopped/tests/kernel_bincount_agrees.rs:1-10): counts[x[i]] += 1 for every
+ * in-range x[i] (0 <= x[i] < bins); `counts` (I32) keeps its prior contents. `index_dtype`: I32, I64 or U32. */
+UP_API int up_sm100_bincount(const void* x, int64_t n, int index_dtype, int32_t* counts, int64_t bins, void* stream);
 
 /* Row max and argmax of a row-major bf16 matrix: Max is NaN-propagating (oracle/plan_contract.rs:179-210),
  * ArgMax is the first index of the extreme with NaN the greatest value (plan_contract.rs:213-245).

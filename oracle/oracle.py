@@ -44,6 +44,8 @@ def lib():
         L.orc_row_mean_f32_documented.argtypes = [P, I64, I64, I64, I64, P, I]
         L.orc_reduce2d_i32.argtypes = [P, I64, I64, I64, I, I, P, I]
         L.orc_col_sum_f32_documented.argtypes = [P, I64, I64, I64, I64, I, P, I]
+        L.orc_scatter.argtypes = [P, I64, I64, I, P, I, I64, I, P, I64]
+        L.orc_bincount.argtypes = [P, I64, I, P, I64]
         L.orc_scan_i32.argtypes = [P, P, I64, I64, I, I, I, ctypes.c_int32, I]
         L.orc_scan_i32_chunked.argtypes = [P, P, I64, I, I, I]
         L.orc_reduce_i32.argtypes = [P, I64, I]
@@ -133,6 +135,33 @@ def col_sum_f32_documented(x: np.ndarray, block: int, mean: bool = False, thread
     out = np.empty(cols, np.float32)
     lib().orc_col_sum_f32_documented(_p(x), rows, cols, cols, block, int(mean), _p(out), threads)
     return out
+
+
+_SCATTER_EK = {np.dtype(np.int32): 9, np.dtype(np.int64): 10, np.dtype(np.uint32): 23, np.dtype(np.float32): 2,
+               np.dtype(np.float64): 4}
+_INDEX_EK = {np.dtype(np.int32): 9, np.dtype(np.int64): 10, np.dtype(np.uint32): 23}
+COMBINE = {"add": 1, "max": 2, "min": 3}
+
+
+def scatter(updates: np.ndarray, ids: np.ndarray, out: np.ndarray, combine: str) -> np.ndarray:
+    """The scatter store over axis 0 in the serial source order (oracle/plan_eval.rs:430-490); `ids` is either
+    full-shape [n, cols] (scatter) or 1-D [n] (index_add). Returns a new array: `out` with the updates combined in."""
+    upd = np.ascontiguousarray(updates)
+    idx = np.ascontiguousarray(ids)
+    res = np.array(out, dtype=upd.dtype, copy=True, order="C")
+    n, cols = upd.shape
+    ids_stride = cols if idx.ndim == 2 else 0
+    lib().orc_scatter(_p(upd), n, cols, _SCATTER_EK[upd.dtype], _p(idx), _INDEX_EK[idx.dtype], ids_stride,
+                      COMBINE[combine], _p(res), res.shape[0])
+    return res
+
+
+def bincount(x: np.ndarray, counts: np.ndarray) -> np.ndarray:
+    """counts[x[i]] += 1 for every in-range x[i] (kernel_bincount_agrees.rs:1-10); returns a new array."""
+    xx = np.ascontiguousarray(x)
+    res = np.array(counts, dtype=np.int32, copy=True)
+    lib().orc_bincount(_p(xx), xx.size, _INDEX_EK[xx.dtype], _p(res), res.size)
+    return res
 
 
 def reduce2d_i32(x: np.ndarray, op: str, axis: int, threads: int = 1) -> np.ndarray:

@@ -285,6 +285,62 @@ void orc_reduce2d_i32(const int32_t* x, int64_t rows, int64_t cols, int64_t row_
   }
 }
 
+/* ---- scatter: oracle/plan_eval.rs:430-490 (the scatter store), ir.rs:2723-2850 ---------------------- */
+
+static int64_t orc_index_at(const void* ids, int kind, int64_t k) {
+  if (kind == ORC_EK_I64) return ((const int64_t*)ids)[k];
+  if (kind == ORC_EK_U32) return (int64_t)((const uint32_t*)ids)[k];
+  return (int64_t)((const int32_t*)ids)[k];
+}
+
+/* Serial in the source order (row-major over updates [n, cols]): the target row is t = ids[i*ids_stride + j] (a
+ * full-shape index) or ids[i] (ids_stride 0: index_add); a target outside [0, out_rows) is skipped; then
+ * out[t][j] = combine(out[t][j], upd[i][j]). Element kinds: 9 I32, 23 U32, 10 I64 (Add wraps at the width, Max/Min
+ * compare at the type's signedness); 2 F32, 4 F64 (Add in f64, stored at the dtype: one rounding per step).
+ * combine: 1 Add, 2 Max, 3 Min. */
+void orc_scatter(const void* upd, int64_t n, int64_t cols, int dtype, const void* ids, int index_dtype,
+                 int64_t ids_stride, int combine, void* out, int64_t out_rows) {
+  for (int64_t i = 0; i < n; ++i)
+    for (int64_t j = 0; j < cols; ++j) {
+      const int64_t t = orc_index_at(ids, index_dtype, ids_stride ? i * ids_stride + j : i);
+      if (t < 0 || t >= out_rows) continue;
+      const int64_t o = t * cols + j, u = i * cols + j;
+      if (dtype == 2) {
+        float* d = (float*)out;
+        d[o] = (float)((double)d[o] + (double)((const float*)upd)[u]);
+      } else if (dtype == 4) {
+        double* d = (double*)out;
+        d[o] = d[o] + ((const double*)upd)[u];
+      } else if (dtype == ORC_EK_I64) {
+        int64_t* d = (int64_t*)out;
+        const int64_t v = ((const int64_t*)upd)[u];
+        if (combine == 1) d[o] = (int64_t)((uint64_t)d[o] + (uint64_t)v);
+        else if (combine == 2) d[o] = v > d[o] ? v : d[o];
+        else d[o] = v < d[o] ? v : d[o];
+      } else if (dtype == ORC_EK_U32) {
+        uint32_t* d = (uint32_t*)out;
+        const uint32_t v = ((const uint32_t*)upd)[u];
+        if (combine == 1) d[o] = d[o] + v;
+        else if (combine == 2) d[o] = v > d[o] ? v : d[o];
+        else d[o] = v < d[o] ? v : d[o];
+      } else {
+        int32_t* d = (int32_t*)out;
+        const int32_t v = ((const int32_t*)upd)[u];
+        if (combine == 1) d[o] = (int32_t)((uint32_t)d[o] + (uint32_t)v);
+        else if (combine == 2) d[o] = v > d[o] ? v : d[o];
+        else d[o] = v < d[o] ? v : d[o];
+      }
+    }
+}
+
+/* bincount (crates/unpopped/tests/kernel_bincount_agrees.rs:1-10): counts[x[i]] += 1 for 0 <= x[i] < bins. */
+void orc_bincount(const void* x, int64_t n, int index_dtype, int32_t* counts, int64_t bins) {
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t v = orc_index_at(x, index_dtype, i);
+    if (v >= 0 && v < bins) counts[v] += 1;
+  }
+}
+
 /* ---- scans: oracle/plan_window.rs:10-238 ---------------------------------------------------------- */
 
 static inline int32_t orc_combine_i32(int op, int32_t a, int32_t b) {

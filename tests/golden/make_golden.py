@@ -322,6 +322,70 @@ def golden_dequant() -> dict:
     }
 
 
+# --- crates/unpopped/tests/kernel_parallel_scatter_agrees.rs, kernel_bincount_agrees.rs,
+#     kernel_parallel_float_scatter_band.rs -----------------------------------------------------------------------
+
+def golden_scatter() -> dict:
+    """The launched-scatter corpus (kernel_parallel_scatter_agrees.rs:19-56): updates [9, 4] = (i*7 % 11) - 5, a
+    full-shape index with duplicates and out-of-range targets, a destination [5, 4] pre-filled with i - 3; expected
+    by the scatter store's definition (oracle/plan_eval.rs:430-490): serial, skip targets outside [0, 5), integer
+    add/max/min. bincount's data (kernel_bincount_agrees.rs:26-34) into 6 zeroed bins. The float band corpus
+    (kernel_parallel_float_scatter_band.rs:24-100): updates, targets and initial values, with each cell's exact sum,
+    sum of magnitudes and term count."""
+    src, dst = (9, 4), (5, 4)
+    upd = [(i * 7 % 11) - 5 for i in range(src[0] * src[1])]
+    targets = [0, 4, 4, 1, 7, -2, 0, 2, 4, 3, 0, 1, 9, 2, 2, 4, 0, 1]
+    idx = [targets[(i * 5 + i // 4) % len(targets)] for i in range(src[0] * src[1])]
+    init = [i - 3 for i in range(dst[0] * dst[1])]
+    exp = {}
+    for name, f in (("add", lambda a, b: wrap32(a + b)), ("max", max), ("min", min)):
+        out = list(init)
+        for i in range(src[0] * src[1]):
+            t = idx[i]
+            if 0 <= t < dst[0]:
+                c = t * dst[1] + i % src[1]
+                out[c] = f(out[c], upd[i])
+        exp[name] = out
+    bc_data = [0, 2, 2, 0, 5, 1, 0, -1, 6, 9, 2, 1, -7, 0]
+    counts = [0] * 6
+    for v in bc_data:
+        if 0 <= v < 6:
+            counts[v] += 1
+    fsrc, fdst = (12, 3), (4, 3)
+
+    def f_update(i):
+        sign = -1.0 if (i * 7 + i // 5) % 3 == 0 else 1.0
+        return f32(sign * f32(1.0000001) * 2.0 ** (((i * 11) % 26) - 3))
+
+    def f_target(i):
+        return [0, 0, 1, 0, 0, 5, 1, 0, -1, 0, 1, 0][(i // fsrc[1]) % 12]
+
+    def f_init(i):
+        return f32(i * 0.375 - 2.0)
+
+    fu = [f_update(i) for i in range(fsrc[0] * fsrc[1])]
+    ft = [f_target(i) for i in range(fsrc[0] * fsrc[1])]
+    fi = [f_init(i) for i in range(fdst[0] * fdst[1])]
+    truth = []
+    for c in range(fdst[0] * fdst[1]):
+        total, mag, n = fi[c], abs(fi[c]), 1
+        for i in range(fsrc[0] * fsrc[1]):
+            t = ft[i]
+            if 0 <= t < fdst[0] and t * fdst[1] + i % fsrc[1] == c:
+                total += fu[i]
+                mag += abs(fu[i])
+                n += 1
+        truth.append([total, mag, n])
+    return {
+        "source": "crates/unpopped/tests/kernel_parallel_scatter_agrees.rs:19-56; kernel_bincount_agrees.rs:26-34; "
+                  "kernel_parallel_float_scatter_band.rs:24-107",
+        "src": list(src), "dst": list(dst), "updates": upd, "index": idx, "init": init, "expected": exp,
+        "bincount": {"x": bc_data, "bins": 6, "counts": counts},
+        "float_band": {"src": list(fsrc), "dst": list(fdst), "updates_f32_bits": [f32_bits(v) for v in fu],
+                       "targets": ft, "init_f32_bits": [f32_bits(v) for v in fi], "cell_sum_abs_n": truth},
+    }
+
+
 def main() -> None:
     out = {
         "float_sum_documented.json": golden_float_sum(),
@@ -329,6 +393,7 @@ def main() -> None:
         "scan_i32.json": golden_scan(),
         "gather_oob.json": golden_gather(),
         "dequant_kat.json": golden_dequant(),
+        "scatter.json": golden_scatter(),
     }
     for name, obj in out.items():
         with open(os.path.join(HERE, name), "w") as f:

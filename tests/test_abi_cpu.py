@@ -7,7 +7,7 @@ import re
 import pytest
 
 from unpopped_b200 import _lib
-from unpopped_b200._lib import OP
+from unpopped_b200._lib import COMBINE, OP
 from unpopped_b200.backend import CudaSm100, LowerError, Operand, Plan
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -74,6 +74,31 @@ def test_dispatch_table_maps_the_reduction_breadth():
         for mask, axis in ((0, 1), (2, 1), (1, 0)):
             k = b.lower(_red(op, "I32", axes_mask=mask))
             assert (k.name, k.scalars) == ("up_sm100_reduce2d_i32", (OP[op], axis)), (op, mask)
+
+
+def _scatter(dtype, index_shape, index_strides, combine="ADD", shape=(9, 4), out_rows=5, **kw):
+    return Plan("STRIDED", [Operand(dtype, shape), Operand("I32", index_shape, index_strides),
+                            Operand(dtype, (out_rows, shape[1]))], dtype=dtype, write_index=True, combine=combine, **kw)
+
+
+def test_dispatch_table_maps_scatter_and_bincount():
+    b = CudaSm100()
+    for combine in ("ADD", "MAX", "MIN"):
+        k = b.lower(_scatter("I32", (9, 4), (4, 1), combine))
+        assert (k.name, k.scalars) == ("up_sm100_scatter", (COMBINE[combine], 1))
+    k = b.lower(_scatter("I64", (9,), (1,)))  # index_add: one target per update row
+    assert (k.name, k.scalars) == ("up_sm100_scatter", (COMBINE["ADD"], 0))
+    assert b.lower(_scatter("F32", (9, 4), (4, 1))).name == "up_sm100_scatter"
+    bc = Plan("STRIDED", [Operand("I32", (14,)), Operand("I32", (6,))], dtype="I32", write_index=True, count=True)
+    assert b.lower(bc).name == "up_sm100_bincount"
+    for plan, variant in ((_scatter("I32", (9, 4), (4, 1), "ASSIGN"), "UnsupportedOp"),
+                          (_scatter("F32", (9, 4), (4, 1), "MAX"), "UnsupportedOp"),
+                          (_scatter("F16", (9, 4), (4, 1)), "UnsupportedDtype"),
+                          (_scatter("I32", (9, 4), (4, 1), scatter_axis=1), "UnsupportedPlanShape"),
+                          (_scatter("I32", (3, 4), (4, 1)), "UnsupportedPlanShape")):
+        with pytest.raises(LowerError) as e:
+            b.lower(plan)
+        assert e.value.variant == variant
 
 
 def test_dispatch_table_maps_each_lift():

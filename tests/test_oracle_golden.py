@@ -108,6 +108,34 @@ def test_float_extremum_nan_and_zero_rules():
     assert np.isnan(orc.reduce2d_f32(np.zeros((3, 0), np.float32), "mean", 1)).all()
 
 
+def test_scatter_corpus_and_bincount():
+    """The scatter store against the launched-scatter corpus (duplicates, out-of-range targets, a pre-filled
+    destination) for Add/Max/Min, and bincount's data."""
+    g = load("scatter.json")
+    src, dst = g["src"], g["dst"]
+    upd = np.array(g["updates"], np.int32).reshape(src)
+    idx = np.array(g["index"], np.int32).reshape(src)
+    init = np.array(g["init"], np.int32).reshape(dst)
+    for combine, exp in g["expected"].items():
+        assert orc.scatter(upd, idx, init, combine).reshape(-1).tolist() == exp, combine
+    b = g["bincount"]
+    for dt in (np.int32, np.int64):
+        assert orc.bincount(np.array(b["x"], dt), np.zeros(b["bins"], np.int32)).tolist() == b["counts"]
+
+
+def test_float_scatter_serial_sum_is_in_the_band():
+    """The serial f32 scatter-add of the band corpus lies inside gamma_(n-1) * sum|terms| of each cell's exact sum."""
+    f = load("scatter.json")["float_band"]
+    upd = np.array(f["updates_f32_bits"], np.uint32).view(np.float32).reshape(f["src"])
+    tgt = np.array(f["targets"], np.int32).reshape(f["src"])
+    init = np.array(f["init_f32_bits"], np.uint32).view(np.float32).reshape(f["dst"])
+    got = orc.scatter(upd, tgt, init, "add").reshape(-1)
+    u = 2.0 ** -24
+    for c, (total, mag, n) in enumerate(f["cell_sum_abs_n"]):
+        k = (n - 1) * u
+        assert abs(float(got[c]) - total) <= k / (1 - k) * mag, c
+
+
 def test_chunked_scan_equals_serial_scan():
     rng = np.random.default_rng(7)
     x = rng.integers(-(2**31), 2**31 - 1, size=100_003, dtype=np.int64).astype(np.int32)

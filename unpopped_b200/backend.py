@@ -13,7 +13,7 @@ import ctypes
 import dataclasses
 
 from . import _lib
-from ._lib import EK, KERNEL, LOWER_ERROR, OOB, OP, SCHED, UpLowered, UpPlanDesc, UpTensor
+from ._lib import COMBINE, EK, KERNEL, LOWER_ERROR, OOB, OP, SCHED, UpLowered, UpPlanDesc, UpTensor
 
 DTYPE_SUPPORT = {0: "Supported", 1: "Unsupported", 2: "NotExpressible"}
 TARGET = "cuda:sm_100a"
@@ -62,6 +62,10 @@ class Plan:
     exclusive: bool = False
     reverse: bool = False
     read_index: bool = False
+    write_index: bool = False  # a scatter store (WriteIndex::ScatterIndexed)
+    scatter_axis: int = 0
+    combine: str = "ADD"
+    count: bool = False  # bincount
     gather_axis: int = 0
     oob: str = "SKIP"
     index_dtype: str = "I32"
@@ -82,6 +86,10 @@ class Plan:
         p.exclusive = int(self.exclusive)
         p.reverse = int(self.reverse)
         p.has_read_index = int(self.read_index)
+        p.has_write_index = int(self.write_index)
+        p.scatter_axis = self.scatter_axis
+        p.combine = COMBINE[self.combine]
+        p.count = int(self.count)
         p.gather_axis = self.gather_axis
         p.oob = OOB[self.oob]
         p.index_dtype = EK[self.index_dtype]

@@ -80,6 +80,8 @@ static const char* k_name(int id) {
     case UP_K_W4A16_GEMM: return "up_sm100_w4a16_gemm";
     case UP_K_REDUCE2D_F32: return "up_sm100_reduce2d_f32";
     case UP_K_REDUCE2D_I32: return "up_sm100_reduce2d_i32";
+    case UP_K_SCATTER: return "up_sm100_scatter";
+    case UP_K_BINCOUNT: return "up_sm100_bincount";
     default: return "";
   }
 }
@@ -201,6 +203,34 @@ extern "C" int up_sm100_classify(const up_plan_desc* p, up_lowered* out) {
       return accept(out, UP_K_SCAN_I32, {p->op, p->exclusive ? 1 : 0, p->reverse ? 1 : 0});
     }
     case UP_SCHED_STRIDED: {
+      if (p->has_write_index) {
+        // scatter / index_add / bincount: operands (updates, ids, out) or, for bincount, (x, counts)
+        if (p->scatter_axis != 0) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "scatter along axis 0 only");
+        if (p->index_dtype != UP_EK_I32 && p->index_dtype != UP_EK_I64 && p->index_dtype != UP_EK_U32)
+          return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "index dtype");
+        if (p->combine == UP_COMBINE_ASSIGN)
+          return refuse(out, UP_LOWER_UNSUPPORTED_OP, "a launched Assign: repeated targets order the stores");
+        if (p->count) {
+          if (p->n_operands < 2 || ops[1].dtype != UP_EK_I32 || p->combine != UP_COMBINE_ADD)
+            return refuse(out, UP_LOWER_INADMISSIBLE_PLAN, "bincount adds into I32 counts");
+          return accept(out, UP_K_BINCOUNT, {});
+        }
+        if (p->n_operands < 3) return refuse(out, UP_LOWER_INADMISSIBLE_PLAN, "updates, ids and output");
+        const up_tensor &u = ops[0], &ix = ops[1], &o = ops[2];
+        if (u.rank != 2 || o.rank != 2 || u.stride[1] != 1 || o.stride[1] != 1 || u.shape[1] != o.shape[1])
+          return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "rank-2 updates and destination with contiguous rows");
+        const bool full = ix.rank == 2 && ix.stride[1] == 1 && ix.shape[0] == u.shape[0] && ix.shape[1] == u.shape[1];
+        const bool row = (ix.rank == 1 && ix.shape[0] == u.shape[0]) ||
+                         (ix.rank == 2 && ix.stride[1] == 0 && ix.shape[0] == u.shape[0]);
+        if (!full && !row) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "a full-shape or a 1-D row index");
+        const int dt = p->dtype;
+        const bool integer = dt == UP_EK_I32 || dt == UP_EK_U32 || dt == UP_EK_I64;
+        const bool fp = dt == UP_EK_F32 || dt == UP_EK_F64;
+        if (!integer && !fp) return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "scatter dtypes: I32, U32, I64, F32, F64");
+        if (fp && p->combine != UP_COMBINE_ADD)
+          return refuse(out, UP_LOWER_UNSUPPORTED_OP, "float Max/Min scatter: integers only");
+        return accept(out, UP_K_SCATTER, {p->combine, full ? 1 : 0});
+      }
       if (!p->has_read_index) return refuse(out, UP_LOWER_UNSUPPORTED_SCHEDULE, "only the gather form of Strided");
       if (p->gather_axis != 0) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "gather along axis 0 only");
       if (p->index_dtype != UP_EK_I32 && p->index_dtype != UP_EK_I64 && p->index_dtype != UP_EK_U32)
@@ -296,6 +326,24 @@ extern "C" int up_sm100_launch(int kernel_id, const up_tensor* ins, int n_in, co
                                           mx.ptr ? (float*)at(mx) : nullptr,
                                           (am.ptr && am.dtype == UP_EK_I32) ? (int32_t*)at(am) : nullptr,
                                           (am.ptr && am.dtype == UP_EK_I64) ? (int64_t*)at(am) : nullptr, stream);
+    }
+    case UP_K_SCATTER: {
+      if (n_in < 2 || n_out < 1) return UP_ERR_INVALID;
+      const up_tensor &u = ins[0], &ix = ins[1], &o = outs[0];
+      if (u.rank != 2 || o.rank != 2 || u.dtype != o.dtype) return UP_ERR_UNSUPPORTED;
+      const int64_t ids_stride = sc(1, 0) ? ix.stride[0] : 0;
+      const int64_t ids_elem_stride = (ix.rank >= 1 && !sc(1, 0)) ? ix.stride[0] : 1;
+      if (!sc(1, 0) && ids_elem_stride != 1) return UP_ERR_UNSUPPORTED;  // a 1-D index must be contiguous
+      return up_sm100_scatter(at(u), u.shape[0], u.shape[1], u.stride[0], u.dtype, at(ix), ix.dtype, ids_stride,
+                              (int)sc(0, UP_COMBINE_ADD), (void*)at(o), o.shape[0], o.stride[0], stream);
+    }
+    case UP_K_BINCOUNT: {
+      if (n_in < 1 || n_out < 1) return UP_ERR_INVALID;
+      const up_tensor &x = ins[0], &c = outs[0];
+      int64_t nx = 1;
+      for (int d = 0; d < x.rank; ++d) nx *= x.shape[d];
+      if (c.dtype != UP_EK_I32 || (x.rank > 1 && !dense_row_major(x))) return UP_ERR_UNSUPPORTED;
+      return up_sm100_bincount(at(x), nx, x.dtype, (int32_t*)at(c), c.rank >= 1 ? c.shape[0] : 1, stream);
     }
     case UP_K_SCAN_I32: {
       if (n_in < 1 || n_out < 1) return UP_ERR_INVALID;

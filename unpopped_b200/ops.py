@@ -13,7 +13,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import ACCUM, EK, OOB, OP, check
+from ._lib import ACCUM, COMBINE, EK, OOB, OP, check
 
 _OPS = {"sum": OP["SUM"], "max": OP["MAX"], "min": OP["MIN"]}
 _OOBS = {"skip": OOB["SKIP"], "clamp": OOB["CLAMP"], "zero_fill": OOB["ZERO_FILL"]}
@@ -99,6 +99,45 @@ def reduce2d(x: torch.Tensor, op: str, axis: int = 1, accum: str = "auto", block
         check(L.up_sm100_reduce2d_i32(x.data_ptr(), rows, cols, x.stride(0), axis, OP[op.upper()], out.data_ptr(),
                                       _stream(x)), "reduce2d_i32")
     return out
+
+
+_SC_EK = {torch.int32: EK["I32"], torch.int64: EK["I64"], torch.uint32: EK["U32"], torch.float32: EK["F32"],
+          torch.float64: EK["F64"]}
+
+
+def scatter(updates: torch.Tensor, ids: torch.Tensor, out: torch.Tensor, combine: str = "add") -> torch.Tensor:
+    """out[t][j] (combine)= updates[i][j] with t = ids[i][j] (a full-shape index, scatter) or ids[i] (1-D, index_add),
+    over axis 0; targets outside [0, out.shape[0]) are skipped. Updates `out` in place and returns it."""
+    for t, name in ((updates, "updates"), (ids, "ids"), (out, "out")):
+        _cuda(t, name)
+    if updates.dim() != 2 or out.dim() != 2 or updates.stride(1) != 1 or out.stride(1) != 1:
+        raise ValueError("scatter takes rank-2 updates and destination with contiguous rows")
+    if updates.dtype != out.dtype or updates.dtype not in _SC_EK or ids.dtype not in _IDX:
+        raise ValueError("scatter dtypes: updates/out I32, U32, I64, F32 or F64; ids I32, I64 or U32")
+    if ids.dim() == 2:
+        if ids.shape != updates.shape or ids.stride(1) != 1:
+            raise ValueError("a full-shape index has the updates' shape and contiguous rows")
+        ids_stride = ids.stride(0)
+    else:
+        if ids.dim() != 1 or ids.shape[0] != updates.shape[0] or ids.stride(0) != 1:
+            raise ValueError("a row index is 1-D, one per update row, contiguous")
+        ids_stride = 0
+    check(_lib.load().up_sm100_scatter(updates.data_ptr(), updates.shape[0], updates.shape[1], updates.stride(0),
+                                       _SC_EK[updates.dtype], ids.data_ptr(), _IDX[ids.dtype], ids_stride,
+                                       COMBINE[combine.upper()], out.data_ptr(), out.shape[0], out.stride(0),
+                                       _stream(out)), "scatter")
+    return out
+
+
+def bincount(x: torch.Tensor, counts: torch.Tensor) -> torch.Tensor:
+    """counts[x[i]] += 1 for every in-range x[i]; `counts` (int32) keeps its prior contents."""
+    _cuda(x, "x")
+    _cuda(counts, "counts")
+    if counts.dtype != torch.int32 or not counts.is_contiguous() or not x.is_contiguous() or x.dtype not in _IDX:
+        raise ValueError("bincount takes contiguous I32/I64/U32 values and contiguous int32 counts")
+    check(_lib.load().up_sm100_bincount(x.data_ptr(), x.numel(), _IDX[x.dtype], counts.data_ptr(), counts.numel(),
+                                        _stream(counts)), "bincount")
+    return counts
 
 
 def row_max_argmax(x: torch.Tensor, index_dtype=torch.int32, want_max: bool = True, want_argmax: bool = True):
