@@ -62,6 +62,17 @@ def gather_inputs(rows=1 << 20, dim=256, n=1 << 24, s=1.1, seed=SEED + 3, device
     return table, ids
 
 
+def zipf_ids(n: int, rows: int, s: float, seed: int, device="cuda") -> torch.Tensor:
+    """int32 [n] Zipf(s) over ranks 1..rows (inverse CDF), mapped through a seeded permutation of the rows."""
+    g = _gen(device, seed)
+    ranks = torch.arange(1, rows + 1, device=device, dtype=torch.float64)
+    cdf = torch.cumsum(ranks.pow(-s), 0)
+    cdf /= cdf[-1].clone()
+    u = torch.rand(n, generator=g, device=device, dtype=torch.float64)
+    r = torch.searchsorted(cdf, u).clamp_(max=rows - 1)
+    return torch.randperm(rows, generator=g, device=device)[r].to(torch.int32)
+
+
 def gather_bytes(ids: torch.Tensor, dim=256, elem=2):
     """(compulsory, logical) bytes: ids + output + each distinct table row once; logical reads every row."""
     n = ids.numel()
