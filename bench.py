@@ -293,14 +293,14 @@ def bench_lifts(ctx, K, W, hbm, bf16):
             "logical_GBps": round(ctx.world * logical / (ms * 1e-3) / 1e9, 1)})
     del table, ids, g_out
 
-    # the scatter lift: index_add of 2^20 i32 rows of 64 into 2^16 rows with Zipf(1.1) targets (atomic adds)
+    # the scatter lift: index_add of 2^20 i32 rows of 64 into 2^16 rows with uniform targets (atomic adds)
     g = torch.Generator(device="cpu").manual_seed(wl.SEED + 7)
     upd = torch.randint(-1000, 1000, (1 << 20, 64), dtype=torch.int32, generator=g).to(ctx.dev)
-    tid = wl.zipf_ids(1 << 20, 1 << 16, 1.1, wl.SEED + 8, device=ctx.dev)
+    tid = torch.randint(0, 1 << 16, (1 << 20,), dtype=torch.int32, generator=g).to(ctx.dev)
     dst = torch.zeros((1 << 16, 64), dtype=torch.int32, device=ctx.dev)
     sc_bytes = upd.numel() * 4 + tid.numel() * 4 + 2 * dst.numel() * 4
     ms, _, _ = ctx.timed(lambda i, kin: ops.scatter(upd, tid, dst, "add"), K, W)
-    record("index_add_i32_2p20x64_into_2p16", sc_bytes, ms, "scatter_kernel", 1,
+    record("index_add_i32_2p20x64_into_2p16_uniform", sc_bytes, ms, "scatter_kernel", 1,
            {"bytes_basis": "updates + ids read once, destination read and written once"})
     del upd, tid, dst
 
