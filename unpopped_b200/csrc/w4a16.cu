@@ -166,6 +166,28 @@ struct UnitCursor {
   __device__ __forceinline__ int gi_at(int h, int kpg) const { return gi + (sub + h) / kpg; }
 };
 
+// The order in which a CTA takes its units [lo, hi): first the units of its last tile when that tile is split with
+// the next CTA ([rot, hi), rot the tile's first unit), then [lo, rot). Both parts of every split tile are then done
+// early in both CTAs, so the split-tile fix-up (a chain of dependent global round trips) happens while other work
+// runs, and each CTA ends on whole tiles. Every role that needs a unit's position walks this same order.
+template <int UK>
+struct RotCursor {
+  UnitCursor<UK> c;
+  int64_t lo, rot, n_first, e;
+  __device__ __forceinline__ void init(int64_t lo_, int64_t hi_, int64_t rot_, int64_t G, int kpg) {
+    lo = lo_;
+    rot = rot_;
+    n_first = hi_ - rot_;
+    e = 0;
+    c.init(rot_, G, kpg);
+  }
+  __device__ __forceinline__ void next(int64_t G, int kpg) {
+    if (++e == n_first) c.init(lo, G, kpg);
+    else c.next((int)G, kpg);
+  }
+  __device__ __forceinline__ int64_t unit() const { return e < n_first ? rot + e : lo + (e - n_first); }
+};
+
 // The end of a tile segment in the epilogue (all kEpiWarps epilogue warps reach it together):
 // a whole tile is written as bf16. For a tile split between CTAs, each epilogue thread publishes its row's
 // 16 f32 partials; the epilogue warps meet on an mbarrier (seg_in, one arrival per warp), one thread counts
@@ -260,6 +282,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t P = gridDim.x;
   const int64_t lo = ((int64_t)blockIdx.x * U) / P, hi = (((int64_t)blockIdx.x + 1) * U) / P;
   const int64_t n_units = hi - lo;
+  // the first unit of this CTA's last tile when that tile starts inside the range and is cut by its end
+  const int64_t GUk = G / UK, t1s = (hi / GUk) * GUk;
+  const int64_t rot = (t1s > lo && t1s < hi) ? t1s : lo;
   const int Gi = (int)G, kpg = (int)(group / kKB);
 
   if (threadIdx.x == 0) {
@@ -409,8 +434,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = lq * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(lq * 32) << 16;
     const int64_t GU = G / UK;      // units per tile
-    UnitCursor<UK> ce;              // the unit being finished
-    ce.init(lo, G, kpg);
+    RotCursor<UK> ce;               // the unit being finished
+    ce.init(lo, hi, rot, G, kpg);
     float acc[kMmaN];
 #pragma unroll
     for (int j = 0; j < kMmaN; ++j) acc[j] = 0.f;
@@ -428,7 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float sc[UK];
 #pragma unroll
       for (int h = 0; h < UK; ++h)
-        sc[h] = __half2float(scs[((size_t)q * kTileN + r) * kScCols + (ce.gi_at(h, kpg) - (ce.gi & ~7))]);
+        sc[h] = __half2float(scs[((size_t)q * kTileN + r) * kScCols + (ce.c.gi_at(h, kpg) - (ce.c.gi & ~7))]);
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&sc_empty[q]);
       const bool good = tc::mbar_wait_sleepy(&mma_done[d], dph, wait_ns, abort_flag, kSleepNs);
@@ -437,8 +462,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc::fence_after_sync();
-      const int64_t t = ce.t, kb = ce.kb;
-      if (e == 0 || kb == 0) {
+      const int64_t t = ce.c.t, kb = ce.c.kb;
+      if (e == 0 || e == hi - rot || kb == 0) {  // a segment starts: the range's start, the wrap, a tile
         seg_kb0 = kb;
 #pragma unroll
         for (int j = 0; j < kMmaN; ++j) acc[j] = 0.f;
@@ -454,8 +479,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&d_empty[d]);
+      const int64_t u = ce.unit();
       ce.next(Gi, kpg);
-      const int64_t u = lo + e;
       if (u + 1 == hi || kb + UK == G)  // the segment [seg_kb0, kb + UK) of tile t ends here
         if (!finish_segment(acc, t, seg_kb0 == 0 && kb + UK == G, r, lane, M, N, U, GU, P, S_max, out, counters,
                             partials, seg_in, seg_out, s_last, nfix, wait_ns, abort_flag)) {
@@ -467,8 +492,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------- scale warp: stages each unit's scales, f16 groups [g0, g0 + 16) of its 128 rows, g0 = gi & ~7 -------
     // With a scale row stride of a multiple of 16 bytes one thread brings them in with one TMA box per unit;
     // otherwise the lanes load and store them (rows l, l + 32, l + 64, l + 96).
-    UnitCursor<UK> cs;
-    cs.init(lo, G, kpg);
+    RotCursor<UK> rs;
+    rs.init(lo, hi, rot, G, kpg);
+    const UnitCursor<UK>& cs = rs.c;
     if (scale_tma) {
       if (lane == 0) {
         tc::tma_prefetch_desc(&smap);
@@ -483,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc::mbar_arrive_expect_tx(&sc_full[q], (uint32_t)kScSlot);
           tc::tma_load_2d(scs + (size_t)q * kTileN * kScCols, &smap, &sc_full[q], cs.gi & ~7,
                           cs.t * kTileN);
-          cs.next(Gi, kpg);
+          rs.next(Gi, kpg);
           issued = i + 1;
         }
         for (int64_t j = issued > kScRing ? issued - kScRing : 0; j < issued; ++j)
@@ -509,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             slot[row * kScCols + (gi - (cs.gi & ~7))] = n < N ? scale[n * gpr + gi] : __ushort_as_half(0);
           }
         }
-        cs.next(Gi, kpg);
+        rs.next(Gi, kpg);
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&sc_full[q]);
       }
@@ -518,8 +544,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- W loader: one TMA box of 128 rows x 64 UK bytes per unit ----------------
     if (lane == 0) {
       tc::tma_prefetch_desc(&wmap);
-      UnitCursor<UK> cw;
-      cw.init(lo, G, kpg);
+      RotCursor<UK> rw;
+      rw.init(lo, hi, rot, G, kpg);
+      const UnitCursor<UK>& cw = rw.c;
       int64_t issued = 0;
       for (int64_t i = 0; i < n_units; ++i) {
         const int sw = (int)(i % C::kWStages);
@@ -530,7 +557,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc::mbar_arrive_expect_tx(&w_full[sw], C::kWUnit);
         tc::tma_load_2d(wst + (size_t)sw * C::kWUnit, &wmap, &w_full[sw], cw.kb * (kKB / 2), cw.t * kTileN);
-        cw.next(Gi, kpg);
+        rw.next(Gi, kpg);
         issued = i + 1;
       }
       // every issued load must land before this CTA's shared memory is released
@@ -565,8 +592,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- activation loader: 2 UK TMA boxes per unit ----------------
     if (lane == 0) {
       tc::tma_prefetch_desc(&xmap);
-      UnitCursor<UK> cx;
-      cx.init(lo, G, kpg);
+      RotCursor<UK> rx;
+      rx.init(lo, hi, rot, G, kpg);
+      const UnitCursor<UK>& cx = rx.c;
       int64_t issued = 0;
       for (int64_t i = 0; i < n_units; ++i) {
         const int s = (int)(i % kXStages);
@@ -579,7 +607,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int bx = 0; bx < 2 * UK; ++bx)
           tc::tma_load_2d(dst + bx * (kXBytes / 2), &xmap, &x_raw[s], cx.kb * kKB + bx * (kKB / 2), 0);
-        cx.next(Gi, kpg);
+        rx.next(Gi, kpg);
         issued = i + 1;
       }
       // every issued load must land before this CTA's shared memory is released
