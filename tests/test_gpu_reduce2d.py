@@ -53,7 +53,7 @@ def test_float_corpus_mean_max_min_columns():
         assert bits(ops.reduce2d(xt, "sum", 0, block=b).cpu()).tolist() == g["documented_f32_bits"][str(b)], b
 
 
-SHAPES = [(1, 1), (3, 7), (17, 96), (64, 4097), (33, 8192), (1000, 5), (5, 1000), (300, 1024)]
+SHAPES = [(1, 1), (3, 7), (17, 96), (64, 4097), (33, 8192), (1000, 5), (5, 1000), (300, 1024), (9, 12000)]
 
 
 @pytest.mark.parametrize("rows,cols", SHAPES)
@@ -112,6 +112,43 @@ def test_float_sum_mean_vs_oracle(rows, cols):
         assert np.array_equal(bits(ops.reduce2d(x, "mean", 1, block=b).cpu()),
                               bits(orc.row_mean_f32_documented(xn, b))), b
     assert np.array_equal(bits(ops.reduce2d(x, "mean", 1, block=1).cpu()), bits(orc.reduce2d_f32(xn, "mean", 1)))
+
+
+@pytest.mark.parametrize("cols", [96, 8192, 12000])
+def test_float_max_min_structured_rows(cols):
+    """Rows built to hit each branch of the chunked fold: all -inf / +inf, all NaN, +0 and -0 ties in either order,
+    the extreme value first, last and repeated, one NaN at the start or the end, and an extreme beside a NaN."""
+    rng = np.random.default_rng(cols)
+    rows = []
+    inf = np.float32(np.inf)
+    for fill in (-inf, inf, np.float32(np.nan), np.float32(0.0), np.float32(-0.0)):
+        rows.append(np.full(cols, fill, np.float32))
+    z = np.zeros(cols, np.float32)
+    z[::2] = -0.0
+    rows.append(z)
+    rows.append(-z)
+    for pos in (0, cols - 1, cols // 2, 3, cols - 4):
+        for v in (1e30, -1e30):
+            r = rng.standard_normal(cols).astype(np.float32)
+            r[pos] = v
+            rows.append(r)
+    r = rng.standard_normal(cols).astype(np.float32)
+    r[[5, cols // 3, cols - 2]] = 7.0
+    r[[9, cols // 2]] = -7.0
+    rows.append(r)
+    for pos in (0, cols - 1):
+        r = rng.standard_normal(cols).astype(np.float32)
+        r.view(np.uint32)[pos] = 0xffa00001  # a signalling-looking NaN with the sign bit
+        rows.append(r)
+    r = rng.standard_normal(cols).astype(np.float32)
+    r[10], r[11] = np.nan, 1e30
+    rows.append(r)
+    xn = np.stack(rows)
+    x = torch.from_numpy(xn).cuda()
+    for op in ("max", "min"):
+        for axis in (0, 1):
+            got = bits(ops.reduce2d(x, op, axis).cpu())
+            assert np.array_equal(got, bits(orc.reduce2d_f32(xn, op, axis))), (op, axis)
 
 
 def test_strided_views():

@@ -70,6 +70,33 @@ __global__ void __launch_bounds__(kThreads) row_fold_i32_kernel(const int32_t* _
                                                                  int64_t cols, int64_t stride,
                                                                  int32_t* __restrict__ out) {
   __shared__ int32_t part[kThreads / 32];
+  if (VEC && cols / 4 <= 8 * kThreads) {
+    // rows of at most 8 int4 per thread: the next row's loads are issued before this row is folded
+    const int64_t nv = cols / 4;
+    uint4 f[8];
+    auto load = [&](int64_t rr) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t i = threadIdx.x + (int64_t)u * kThreads;
+        if (rr < rows && i < nv) f[u] = ld_nc_na_v4(x + rr * stride + 4 * i);
+      }
+    };
+    int64_t r = blockIdx.x;
+    load(r);
+    for (; r < rows; r += gridDim.x) {
+      uint4 cur[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) cur[u] = f[u];
+      load(r + gridDim.x);
+      int32_t acc = ident<OP>();
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (threadIdx.x + (int64_t)u * kThreads < nv) acc = comb4<OP>(acc, cur[u]);
+      acc = block_comb<OP>(acc, part);
+      if (threadIdx.x == 0) out[r] = cols > 0 ? acc : (OP == UP_OP_PROD ? 1 : 0);
+    }
+    return;
+  }
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const int32_t* row = x + r * stride;
     int32_t acc = ident<OP>();
@@ -182,57 +209,171 @@ struct ExtState {
   }
 };
 
+// max.NaN / min.NaN: the larger (smaller) operand, NaN if either is NaN, so one tree over a chunk both finds the
+// chunk's extreme value and shows whether the chunk holds a NaN.
+template <bool MAX>
+__device__ __forceinline__ float pick_nan(float a, float b) {
+  float d;
+  if (MAX)
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  else
+    asm("min.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+
+// Folds U float4s (elements base[u] .. base[u] + 3, ascending in u; ok[u] false for a float4 outside the row) into
+// the state in index order, with the serial rule's result: the chunk's extreme value is found by one max.NaN tree;
+// a chunk with a NaN takes the serial path element by element; otherwise the state changes only when the chunk's
+// value is strictly better (or the state is empty), and then to the chunk's first element equal to it, so the first
+// of equal values (and of +0/-0) is kept. About 1.1 operations per element instead of the serial rule's seven.
+template <bool MAX, int U>
+__device__ __forceinline__ void fold_chunk(ExtState<MAX>& st, const float4 (&f)[U], const uint32_t (&base)[U],
+                                           const bool (&ok)[U]) {
+  const float fill = MAX ? -__int_as_float(0x7f800000) : __int_as_float(0x7f800000);
+  float q[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u)
+    q[u] = ok[u] ? pick_nan<MAX>(pick_nan<MAX>(f[u].x, f[u].y), pick_nan<MAX>(f[u].z, f[u].w)) : fill;
+#pragma unroll
+  for (int h = 1; h < U; h <<= 1)
+#pragma unroll
+    for (int u = 0; u + h < U; u += 2 * h) q[u] = pick_nan<MAX>(q[u], q[u + h]);
+  const float cm = q[0];
+  if (cm != cm) {
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (ok[u]) {
+        st.take(f[u].x, base[u]);
+        st.take(f[u].y, base[u] + 1);
+        st.take(f[u].z, base[u] + 2);
+        st.take(f[u].w, base[u] + 3);
+      }
+  } else if (st.idx == kNone || (MAX ? cm > st.m : cm < st.m)) {
+    bool found = false;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const float4 c = f[u];
+      if (!found && ok[u] && (c.x == cm || c.y == cm || c.z == cm || c.w == cm)) {
+        found = true;
+        st.idx = c.x == cm ? base[u] : c.y == cm ? base[u] + 1 : c.z == cm ? base[u] + 2 : base[u] + 3;
+        st.m = c.x == cm ? c.x : c.y == cm ? c.y : c.z == cm ? c.z : c.w;
+      }
+    }
+  }
+}
+
+// An order-preserving integer key of a non-NaN float, with +0 and -0 equal (ties between them go to the lower
+// index, as equal values do).
+__device__ __forceinline__ int32_t ext_key(float m) {
+  const int32_t b = m == 0.0f ? 0 : __float_as_int(m);
+  return b >= 0 ? b : (b ^ 0x7fffffff);
+}
+
+// Merges the 32 lanes' states into every lane with the warp's integer reductions: the best key, the lowest index
+// holding it, the last NaN; the value's bits come from the lane that holds the winning index.
+template <bool MAX>
+__device__ __forceinline__ void warp_reduce_ext(ExtState<MAX>& st) {
+  const int32_t none = MAX ? (int32_t)0x80000000 : 0x7fffffff;
+  const int32_t k = st.idx == kNone ? none : ext_key(st.m);
+  const int32_t wk = MAX ? __reduce_max_sync(0xffffffffu, k) : __reduce_min_sync(0xffffffffu, k);
+  const uint32_t wi = __reduce_min_sync(0xffffffffu, (st.idx != kNone && k == wk) ? st.idx : kNone);
+  const unsigned own = __ballot_sync(0xffffffffu, wi != kNone && st.idx == wi);
+  const float wm = __shfl_sync(0xffffffffu, st.m, own ? __ffs(own) - 1 : 0);
+  st.nan_idx = __reduce_max_sync(0xffffffffu, st.nan_idx);
+  st.m = wm;
+  st.idx = wi;
+}
+
+// f32 Max/Min over the last axis, a CTA per row (grid-stride). Rows of at most 8 float4 per thread keep the whole
+// share in registers and issue the next row's loads before folding this one; longer rows fold 4 float4 per step.
+// The block merge is one barrier per row: the warps' states go to a double-buffered slot and warp 0 merges them.
 template <bool MAX, bool VEC>
 __global__ void __launch_bounds__(kThreads) row_extremum_f32_kernel(const float* __restrict__ x, int64_t rows,
                                                                      int64_t cols, int64_t stride,
                                                                      float* __restrict__ out) {
-  __shared__ float sm[kThreads / 32];
-  __shared__ uint32_t si[kThreads / 32];
-  __shared__ int32_t sn[kThreads / 32];
+  constexpr int kW = kThreads / 32;
+  __shared__ float sm[2][kW];
+  __shared__ uint32_t si[2][kW];
+  __shared__ int32_t sn[2][kW];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int par = 0;
+  // the warp-merged state of this row to the slot; warp 0 merges the slots and writes the result
+  auto finish = [&](ExtState<MAX>& st, int64_t r) {
+    warp_reduce_ext<MAX>(st);
+    if (lane == 0) {
+      sm[par][w] = st.m;
+      si[par][w] = st.idx;
+      sn[par][w] = st.nan_idx;
+    }
+    __syncthreads();
+    if (w == 0) {
+      ExtState<MAX> b;
+      b.init();
+      if (lane < kW) {
+        b.m = sm[par][lane];
+        b.idx = si[par][lane];
+        b.nan_idx = sn[par][lane];
+      }
+      warp_reduce_ext<MAX>(b);
+      if (lane == 0) out[r] = __uint_as_float(b.result(x + r * stride, 1));
+    }
+    par ^= 1;  // the next row writes the other slot; this one is read before the next row's barrier
+  };
+  if (VEC && cols / 4 <= 8 * kThreads) {
+    const int64_t nv = cols / 4;
+    uint32_t base[8];
+    bool ok[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int64_t i = threadIdx.x + (int64_t)u * kThreads;
+      ok[u] = i < nv;
+      base[u] = (uint32_t)(4 * i);
+    }
+    float4 f[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) f[u] = make_float4(0.f, 0.f, 0.f, 0.f);  // a float4 outside the row is never folded
+    auto load = [&](int64_t rr) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (rr < rows && ok[u]) f[u] = ld_nc_na_f4(x + rr * stride + base[u]);
+    };
+    int64_t r = blockIdx.x;
+    load(r);
+    for (; r < rows; r += gridDim.x) {
+      float4 cur[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) cur[u] = f[u];
+      load(r + gridDim.x);
+      ExtState<MAX> st;
+      st.init();
+      fold_chunk<MAX, 8>(st, cur, base, ok);
+      finish(st, r);
+    }
+    return;
+  }
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const float* row = x + r * stride;
     ExtState<MAX> st;
     st.init();
     if (VEC) {
       const int64_t nv = cols / 4;
-      int64_t i = threadIdx.x;
-      for (; i + 3 * kThreads < nv; i += 4 * kThreads) {
+      for (int64_t i = threadIdx.x; i < nv; i += 4 * kThreads) {
         float4 f[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) f[u] = ld_nc_na_f4(row + 4 * (i + u * kThreads));
+        uint32_t base[4];
+        bool ok[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const uint32_t c = (uint32_t)(4 * (i + u * kThreads));
-          st.take(f[u].x, c);
-          st.take(f[u].y, c + 1);
-          st.take(f[u].z, c + 2);
-          st.take(f[u].w, c + 3);
+          const int64_t j = i + (int64_t)u * kThreads;
+          ok[u] = j < nv;
+          base[u] = (uint32_t)(4 * j);
+          f[u] = ok[u] ? ld_nc_na_f4(row + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-      }
-      for (; i < nv; i += kThreads) {
-        const float4 f = ld_nc_na_f4(row + 4 * i);
-        const uint32_t c = (uint32_t)(4 * i);
-        st.take(f.x, c);
-        st.take(f.y, c + 1);
-        st.take(f.z, c + 2);
-        st.take(f.w, c + 3);
+        fold_chunk<MAX, 4>(st, f, base, ok);
       }
     } else {
       for (int64_t c = threadIdx.x; c < cols; c += kThreads) st.take(__ldg(row + c), (uint32_t)c);
     }
-    st.warp_merge();
-    const int w = threadIdx.x >> 5;
-    if ((threadIdx.x & 31) == 0) {
-      sm[w] = st.m;
-      si[w] = st.idx;
-      sn[w] = st.nan_idx;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      for (int k = 1; k < kThreads / 32; ++k) st.merge(sm[k], si[k], sn[k]);
-      out[r] = __uint_as_float(st.result(row, 1));
-    }
-    __syncthreads();
+    finish(st, r);
   }
 }
 
@@ -340,8 +481,10 @@ template <int OP>
 int launch_i32(const int32_t* x, int64_t rows, int64_t cols, int64_t stride, int axis, int32_t* out, cudaStream_t s) {
   const int sms = sm_count();
   if (axis == 1) {
-    int64_t g = rows < (int64_t)sms * 8 ? rows : (int64_t)sms * 8;
     const bool vec = aligned(x, 16) && cols % 4 == 0 && stride % 4 == 0;
+    // rows held in registers with the next row's loads in flight need only two CTAs per SM (measured best)
+    const int64_t per_sm = vec && cols / 4 <= 8 * kThreads ? 2 : 8;
+    const int64_t g = rows < (int64_t)sms * per_sm ? rows : (int64_t)sms * per_sm;
     if (vec) row_fold_i32_kernel<OP, true><<<(int)g, kThreads, 0, s>>>(x, rows, cols, stride, out);
     else row_fold_i32_kernel<OP, false><<<(int)g, kThreads, 0, s>>>(x, rows, cols, stride, out);
     note_launch();
@@ -408,8 +551,9 @@ extern "C" int up_sm100_reduce2d_f32(const float* x, int64_t rows, int64_t cols,
       return row_mean_f32_auto(x, rows, cols, row_stride, block, out, stream);
     }
     if (cols > 0x7fffffffLL) return UP_ERR_UNSUPPORTED;  // indices are 32-bit
-    const int g = (int)(rows < (int64_t)sm_count() * 8 ? rows : (int64_t)sm_count() * 8);
     const bool vec = aligned(x, 16) && cols % 4 == 0 && row_stride % 4 == 0;
+    const int64_t per_sm = vec && cols / 4 <= 8 * kThreads ? 2 : 8;  // as for the i32 fold (measured best)
+    const int g = (int)(rows < (int64_t)sm_count() * per_sm ? rows : (int64_t)sm_count() * per_sm);
     if (op == UP_OP_MAX) {
       if (vec) row_extremum_f32_kernel<true, true><<<g, kThreads, 0, s>>>(x, rows, cols, row_stride, out);
       else row_extremum_f32_kernel<true, false><<<g, kThreads, 0, s>>>(x, rows, cols, row_stride, out);
