@@ -16,6 +16,7 @@
 //    order is the oracle's, not a tree), one rounding; Mean divides by the row count, so an empty Mean is 0/0.
 #include "common.cuh"
 
+#include <cooperative_groups.h>
 #include <mutex>
 
 namespace up {
@@ -412,6 +413,101 @@ __global__ void __launch_bounds__(32 * kColWarps) col_extremum_f32_kernel(const 
   }
 }
 
+// f32 Max/Min over the outer axis, 16-byte loads: a CTA takes a strip of 128 columns (a float4 per lane, 512 B of
+// each row per warp) and a cluster of 8 CTAs splits the rows into 8 ranges; warp w of a CTA folds rows w, w + 8, ...
+// of its range in order. Each lane folds a batch of 4 rows per column with one max.NaN tree and searches the batch
+// only when its value is strictly better (the serial rule as in fold_chunk). The 8 warps merge through shared
+// memory and the cluster's 8 CTAs through distributed shared memory into rank 0, which writes the strip.
+constexpr int kColStrip = 128, kColCluster = 8, kColVecWarps = 8;
+template <bool MAX>
+__device__ __forceinline__ void fold_col_batch(ExtState<MAX>& st, float a0, float a1, float a2, float a3,
+                                               uint32_t r, uint32_t step) {
+  const float cm = pick_nan<MAX>(pick_nan<MAX>(a0, a1), pick_nan<MAX>(a2, a3));
+  if (cm != cm) {
+    st.take(a0, r);
+    st.take(a1, r + step);
+    st.take(a2, r + 2 * step);
+    st.take(a3, r + 3 * step);
+  } else if (st.idx == kNone || (MAX ? cm > st.m : cm < st.m)) {
+    st.idx = a0 == cm ? r : a1 == cm ? r + step : a2 == cm ? r + 2 * step : r + 3 * step;
+    st.m = a0 == cm ? a0 : a1 == cm ? a1 : a2 == cm ? a2 : a3;
+  }
+}
+
+template <bool MAX>
+__global__ void __cluster_dims__(1, kColCluster, 1) __launch_bounds__(32 * kColVecWarps)
+    col_extremum_f32_vec_kernel(const float* __restrict__ x, int64_t rows, int64_t cols, int64_t stride,
+                                float* __restrict__ out) {
+  namespace cg = cooperative_groups;
+  __shared__ float sm[kColVecWarps][kColStrip];
+  __shared__ uint32_t si[kColVecWarps][kColStrip];
+  __shared__ int32_t sn[kColVecWarps][kColStrip];
+  __shared__ float cm_[kColStrip];
+  __shared__ uint32_t ci_[kColStrip];
+  __shared__ int32_t cn_[kColStrip];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t c0 = (int64_t)blockIdx.x * kColStrip + 4 * lane;
+  const int64_t per = (rows + kColCluster - 1) / kColCluster;
+  const int64_t r0 = (int64_t)blockIdx.y * per;
+  const int64_t r1 = r0 + per < rows ? r0 + per : rows;
+  ExtState<MAX> st[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) st[j].init();
+  if (c0 < cols) {
+    const float* base = x + c0;
+    int64_t r = r0 + w;
+    constexpr int S = kColVecWarps;
+    for (; r + 3 * S < r1; r += 4 * S) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = ld_nc_na_f4(base + (r + u * S) * stride);
+      fold_col_batch<MAX>(st[0], v[0].x, v[1].x, v[2].x, v[3].x, (uint32_t)r, S);
+      fold_col_batch<MAX>(st[1], v[0].y, v[1].y, v[2].y, v[3].y, (uint32_t)r, S);
+      fold_col_batch<MAX>(st[2], v[0].z, v[1].z, v[2].z, v[3].z, (uint32_t)r, S);
+      fold_col_batch<MAX>(st[3], v[0].w, v[1].w, v[2].w, v[3].w, (uint32_t)r, S);
+    }
+    for (; r < r1; r += S) {
+      const float4 v = ld_nc_na_f4(base + r * stride);
+      st[0].take(v.x, (uint32_t)r);
+      st[1].take(v.y, (uint32_t)r);
+      st[2].take(v.z, (uint32_t)r);
+      st[3].take(v.w, (uint32_t)r);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    sm[w][4 * lane + j] = st[j].m;
+    si[w][4 * lane + j] = st[j].idx;
+    sn[w][4 * lane + j] = st[j].nan_idx;
+  }
+  __syncthreads();
+  const int t = threadIdx.x;  // the strip's column t (threads 0 .. 127)
+  if (t < kColStrip) {
+    ExtState<MAX> a;
+    a.m = sm[0][t];
+    a.idx = si[0][t];
+    a.nan_idx = sn[0][t];
+    for (int k = 1; k < kColVecWarps; ++k) a.merge(sm[k][t], si[k][t], sn[k][t]);
+    cm_[t] = a.m;
+    ci_[t] = a.idx;
+    cn_[t] = a.nan_idx;
+  }
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();  // every CTA's strip states are visible to rank 0
+  if (cluster.block_rank() == 0 && t < kColStrip) {
+    ExtState<MAX> a;
+    a.m = cm_[t];
+    a.idx = ci_[t];
+    a.nan_idx = cn_[t];
+    for (unsigned q = 1; q < (unsigned)kColCluster; ++q)
+      a.merge(*cluster.map_shared_rank(&cm_[t], q), *cluster.map_shared_rank(&ci_[t], q),
+              *cluster.map_shared_rank(&cn_[t], q));
+    const int64_t c = (int64_t)blockIdx.x * kColStrip + t;
+    if (c < cols) out[c] = __uint_as_float(a.result(x + c, stride));
+  }
+  cluster.sync();  // rank 0 has read the other CTAs' shared memory before they exit
+}
+
 // f32 Sum/Mean over the outer axis, one thread per column folding the rows in order in f64 (the serial order; a
 // split of the rows would change the roundings).
 template <int OP>
@@ -602,12 +698,20 @@ extern "C" int up_sm100_reduce2d_f32(const float* x, int64_t rows, int64_t cols,
     case UP_OP_SUM: col_f32_kernel<UP_OP_SUM><<<(int)gx, kThreads, 0, s>>>(x, rows, cols, row_stride, out); break;
     case UP_OP_MEAN: col_f32_kernel<UP_OP_MEAN><<<(int)gx, kThreads, 0, s>>>(x, rows, cols, row_stride, out); break;
     case UP_OP_MAX:
-      col_extremum_f32_kernel<true><<<(unsigned)((cols + 31) / 32), 32 * kColWarps, 0, s>>>(x, rows, cols, row_stride,
-                                                                                         out);
-      break;
     default:
-      col_extremum_f32_kernel<false><<<(unsigned)((cols + 31) / 32), 32 * kColWarps, 0, s>>>(x, rows, cols, row_stride,
-                                                                                          out);
+      if (aligned(x, 16) && cols % 4 == 0 && row_stride % 4 == 0) {
+        const dim3 grid((unsigned)((cols + kColStrip - 1) / kColStrip), kColCluster);
+        if (op == UP_OP_MAX)
+          col_extremum_f32_vec_kernel<true><<<grid, 32 * kColVecWarps, 0, s>>>(x, rows, cols, row_stride, out);
+        else
+          col_extremum_f32_vec_kernel<false><<<grid, 32 * kColVecWarps, 0, s>>>(x, rows, cols, row_stride, out);
+      } else if (op == UP_OP_MAX) {
+        col_extremum_f32_kernel<true><<<(unsigned)((cols + 31) / 32), 32 * kColWarps, 0, s>>>(x, rows, cols,
+                                                                                           row_stride, out);
+      } else {
+        col_extremum_f32_kernel<false><<<(unsigned)((cols + 31) / 32), 32 * kColWarps, 0, s>>>(x, rows, cols,
+                                                                                            row_stride, out);
+      }
       break;
   }
   note_launch();
