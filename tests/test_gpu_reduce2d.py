@@ -102,7 +102,7 @@ def test_float_sum_mean_vs_oracle(rows, cols):
     # outer axis: the serial order per column (block 1) and the documented order of larger blocks
     assert np.array_equal(bits(ops.reduce2d(x, "sum", 0).cpu()), bits(orc.reduce2d_f32(xn, "sum", 0)))
     assert np.array_equal(bits(ops.reduce2d(x, "mean", 0).cpu()), bits(orc.reduce2d_f32(xn, "mean", 0)))
-    for b in (2, 16, 64, 256):
+    for b in (2, 16, 64, 128, 256):
         assert np.array_equal(bits(ops.reduce2d(x, "sum", 0, block=b).cpu()),
                               bits(orc.col_sum_f32_documented(xn, b))), b
         assert np.array_equal(bits(ops.reduce2d(x, "mean", 0, block=b).cpu()),
@@ -193,6 +193,8 @@ def test_full_config_rows():
             assert np.array_equal(bits(ops.reduce2d(x, op, axis).cpu()), bits(orc.reduce2d_f32(xn, op, axis, t)))
     assert np.array_equal(bits(ops.reduce2d(x, "sum", 0, block=256).cpu()),
                           bits(orc.col_sum_f32_documented(xn, 256, threads=t)))
+    for op in ("sum", "mean"):  # the serial order per column (block 1)
+        assert np.array_equal(bits(ops.reduce2d(x, op, 0).cpu()), bits(orc.reduce2d_f32(xn, op, 0, t))), op
     xi = rng.integers(-2**31, 2**31, (8192, 8192), dtype=np.int64).astype(np.int32)
     xit = torch.from_numpy(xi).cuda()
     for op in INT_OPS:

@@ -129,6 +129,24 @@ __global__ void col_init_i32_kernel(int32_t* __restrict__ out, int64_t cols) {
     out[c] = ident<OP>();
 }
 
+// A split's partial into out[c] with the op's atomic.
+template <int OP>
+__device__ __forceinline__ void col_combine_out(int32_t* o, int32_t acc) {
+  if (OP == UP_OP_SUM) atomicAdd(o, acc);
+  else if (OP == UP_OP_MAX) atomicMax(o, acc);
+  else if (OP == UP_OP_MIN) atomicMin(o, acc);
+  else if (OP == UP_OP_AND) atomicAnd(o, acc);
+  else if (OP == UP_OP_OR) atomicOr(o, acc);
+  else if (OP == UP_OP_XOR) atomicXor(o, acc);
+  else {  // Prod: no atomic multiply; a compare-and-swap loop (each retry sees a newer value, so it ends)
+    int32_t old = *reinterpret_cast<volatile int32_t*>(o), seen;
+    do {
+      seen = old;
+      old = atomicCAS(o, seen, comb<OP>(seen, acc));
+    } while (old != seen);
+  }
+}
+
 template <int OP>
 __global__ void __launch_bounds__(kThreads) col_fold_i32_kernel(const int32_t* __restrict__ x, int64_t rows,
                                                                  int64_t cols, int64_t stride, int64_t per_split,
@@ -147,20 +165,7 @@ __global__ void __launch_bounds__(kThreads) col_fold_i32_kernel(const int32_t* _
     for (int u = 0; u < 4; ++u) acc = comb<OP>(acc, v[u]);
   }
   for (; r < r1; ++r) acc = comb<OP>(acc, __ldg(x + r * stride + c));
-  int32_t* o = out + c;
-  if (OP == UP_OP_SUM) atomicAdd(o, acc);
-  else if (OP == UP_OP_MAX) atomicMax(o, acc);
-  else if (OP == UP_OP_MIN) atomicMin(o, acc);
-  else if (OP == UP_OP_AND) atomicAnd(o, acc);
-  else if (OP == UP_OP_OR) atomicOr(o, acc);
-  else if (OP == UP_OP_XOR) atomicXor(o, acc);
-  else {  // Prod: no atomic multiply; a compare-and-swap loop (each retry sees a newer value, so it ends)
-    int32_t old = *reinterpret_cast<volatile int32_t*>(o), seen;
-    do {
-      seen = old;
-      old = atomicCAS(o, seen, comb<OP>(seen, acc));
-    } while (old != seen);
-  }
+  col_combine_out<OP>(out + c, acc);
 }
 
 // ---- f32 Max/Min ----
@@ -529,12 +534,72 @@ __global__ void __launch_bounds__(kThreads) col_f32_kernel(const float* __restri
   out[c] = __double2float_rn(OP == UP_OP_MEAN ? acc / (double)rows : acc);
 }
 
+// The same serial order with the rows staged through shared memory, for 16-byte aligned rows whose width is a
+// multiple of 4: a CTA is one warp and 32 columns. The chain of f64 adds per column is inherently serial, so the
+// only parallelism is across columns; to keep enough bytes in flight the warp runs D stages of 32 rows x 128 B ahead
+// with 16-byte cp.async copies (lane l copies rows l/8, l/8 + 4, ... of columns 4(l%8) .. 4(l%8)+3), and lane l
+// adds column l of each staged row in order. Copies past the last row or column are zero-filled and never added.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sa), "l"(gmem), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <bool MEAN, int D>
+__global__ void __launch_bounds__(32) col_sum_f32_serial_kernel(const float* __restrict__ x, int64_t rows,
+                                                                int64_t cols, int64_t stride,
+                                                                float* __restrict__ out) {
+  extern __shared__ __align__(16) float stage[];  // [D][32 rows][32 columns]
+  const int lane = threadIdx.x;
+  const int64_t cb = (int64_t)blockIdx.x * 32;
+  const int lr = lane >> 3, lc = (lane & 7) * 4;
+  const bool cok = cb + lc < cols;
+  const int64_t nst = (rows + 31) / 32;
+  auto issue = [&](int64_t st) {
+    if (st < nst) {
+      float* b = stage + (size_t)(st % D) * 1024;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int rr = lr + 4 * k;
+        const int64_t r = st * 32 + rr;
+        const bool ok = cok && r < rows;
+        cp_async16(b + rr * 32 + lc, ok ? x + r * stride + cb + lc : x, ok ? 16 : 0);
+      }
+    }
+    cp_async_commit();  // an empty group past the end keeps the group count uniform
+  };
+#pragma unroll
+  for (int st = 0; st < D - 1; ++st) issue(st);
+  double acc = 0.0;
+  for (int64_t st = 0; st < nst; ++st) {
+    issue(st + D - 1);  // into the buffer read in the previous step
+    cp_async_wait<D - 1>();
+    __syncwarp();
+    const float* b = stage + (size_t)(st % D) * 1024 + lane;
+    if (st * 32 + 32 <= rows) {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) acc += (double)b[k * 32];
+    } else {
+      const int n = (int)(rows - st * 32);
+      for (int k = 0; k < n; ++k) acc += (double)b[k * 32];
+    }
+    __syncwarp();  // every lane has read the buffer before the next step refills it
+  }
+  cp_async_wait<0>();
+  if (cb + lane < cols) out[cb + lane] = __double2float_rn(MEAN ? acc / (double)rows : acc);
+}
+
 // f32 Sum/Mean over the outer axis in the launched lift's documented order for a logical block of B threads
 // (kernel_lift/block_reduce.rs:13-30): logical thread t of column c folds rows t, t+B, t+2B, ... ascending into an
 // f64; then acc[t] += acc[t+s] for s = B/2 .. 1; Mean divides by the row count; one rounding. A CTA takes 32
 // columns (one per lane) and 16 warps; warp w holds logical threads w, w+16, ... (B/16 accumulators; B <= 256),
 // so each step loads B/16 rows per thread, all coalesced across the 32 columns. The tree runs in shared memory.
 constexpr int kDocWarps = 16, kDocMaxB = 256;
+constexpr int kSerialStages = 12;  // 48 KB of rows in flight per 32 columns (measured best of 4, 8, 12)
 template <bool MEAN>
 __global__ void __launch_bounds__(32 * kDocWarps) col_sum_f32_doc_kernel(const float* __restrict__ x, int64_t rows,
                                                                          int64_t cols, int64_t stride, int B,
@@ -573,6 +638,132 @@ __global__ void __launch_bounds__(32 * kDocWarps) col_sum_f32_doc_kernel(const f
   if (w == 0 && c < cols) out[c] = __double2float_rn(MEAN ? sacc[lane] / (double)rows : sacc[lane]);
 }
 
+// The documented order with 16-byte loads, for B = 64, 128 or 256: a strip of 128 columns (a float4 per lane) per
+// CTA and a cluster of 8 CTAs per strip. Logical thread t = k + 8w + 64i lives in CTA rank k, warp w, slot i
+// (I = B/64 slots per lane), so each warp reads 512 B of every row it touches. The tree's levels s >= 64 pair
+// slots of one thread, s = 32, 16, 8 pair warps of one CTA (through shared memory) and s = 4, 2, 1 pair CTAs of the
+// cluster (rank 0 reads the other ranks' values through distributed shared memory), each as acc[t] + acc[t+s].
+template <bool MEAN, int I>
+__global__ void __cluster_dims__(1, kColCluster, 1) __launch_bounds__(256)
+    col_sum_f32_doc_vec_kernel(const float* __restrict__ x, int64_t rows, int64_t cols, int64_t stride,
+                               float* __restrict__ out) {
+  namespace cg = cooperative_groups;
+  constexpr int B = 64 * I, U = 8 / I;  // U steps of I rows in flight per lane
+  __shared__ double sw[8][kColStrip];
+  __shared__ double cs[kColStrip];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int k = (int)blockIdx.y;
+  const int64_t c0 = (int64_t)blockIdx.x * kColStrip + 4 * lane;
+  double acc[I][4];
+#pragma unroll
+  for (int i = 0; i < I; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
+  if (c0 < cols) {
+    const float* base = x + c0;
+    const int64_t M = (rows + B - 1) / B;
+    auto add = [&](int i, int64_t r, const float4 v) {
+      if (r < rows) {
+        acc[i][0] += (double)v.x;
+        acc[i][1] += (double)v.y;
+        acc[i][2] += (double)v.z;
+        acc[i][3] += (double)v.w;
+      }
+    };
+    int64_t m = 0;
+    for (; m + U <= M; m += U) {
+      float4 v[U][I];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int i = 0; i < I; ++i) {
+          const int64_t r = k + 8 * w + 64 * i + B * (m + u);
+          v[u][i] = r < rows ? ld_nc_na_f4(base + r * stride) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int i = 0; i < I; ++i) add(i, k + 8 * w + 64 * i + B * (m + u), v[u][i]);
+    }
+    for (; m < M; ++m) {
+#pragma unroll
+      for (int i = 0; i < I; ++i) {
+        const int64_t r = k + 8 * w + 64 * i + B * m;
+        if (r < rows) add(i, r, ld_nc_na_f4(base + r * stride));
+      }
+    }
+  }
+#pragma unroll
+  for (int h = I / 2; h >= 1; h >>= 1)  // levels s = 64h
+#pragma unroll
+    for (int i = 0; i < h; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = acc[i][j] + acc[i + h][j];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) sw[w][4 * lane + j] = acc[0][j];
+  __syncthreads();
+  const int t = threadIdx.x;  // the strip's column t (threads 0 .. 127)
+  if (t < kColStrip) {
+    double v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v[q] = sw[q][t];
+#pragma unroll
+    for (int h = 4; h >= 1; h >>= 1)  // levels s = 8h: warp q and q + h
+#pragma unroll
+      for (int q = 0; q < h; ++q) v[q] = v[q] + v[q + h];
+    cs[t] = v[0];
+  }
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();  // every CTA's values are visible to rank 0
+  if (cluster.block_rank() == 0 && t < kColStrip) {
+    double v[8];
+    v[0] = cs[t];
+#pragma unroll
+    for (unsigned q = 1; q < 8; ++q) v[q] = *cluster.map_shared_rank(&cs[t], q);
+#pragma unroll
+    for (int h = 4; h >= 1; h >>= 1)  // levels s = h: rank q and q + h
+#pragma unroll
+      for (int q = 0; q < h; ++q) v[q] = v[q] + v[q + h];
+    const int64_t c = (int64_t)blockIdx.x * kColStrip + t;
+    if (c < cols) out[c] = __double2float_rn(MEAN ? v[0] / (double)rows : v[0]);
+  }
+  cluster.sync();  // rank 0 has read the other CTAs' shared memory before they exit
+}
+
+// The same with 16-byte loads (a thread takes 4 adjacent columns, a CTA 1024 columns, 4 KB of each row).
+template <int OP>
+__global__ void __launch_bounds__(kThreads) col_fold_i32_vec_kernel(const int32_t* __restrict__ x, int64_t rows,
+                                                                     int64_t cols, int64_t stride, int64_t per_split,
+                                                                     int32_t* __restrict__ out) {
+  const int64_t c = ((int64_t)blockIdx.x * kThreads + threadIdx.x) * 4;
+  if (c >= cols) return;
+  const int64_t r0 = (int64_t)blockIdx.y * per_split;
+  const int64_t r1 = r0 + per_split < rows ? r0 + per_split : rows;
+  int32_t a[4] = {ident<OP>(), ident<OP>(), ident<OP>(), ident<OP>()};
+  int64_t r = r0;
+  for (; r + 3 < r1; r += 4) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = ld_nc_na_v4(x + (r + u) * stride + c);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      a[0] = comb<OP>(a[0], (int32_t)v[u].x);
+      a[1] = comb<OP>(a[1], (int32_t)v[u].y);
+      a[2] = comb<OP>(a[2], (int32_t)v[u].z);
+      a[3] = comb<OP>(a[3], (int32_t)v[u].w);
+    }
+  }
+  for (; r < r1; ++r) {
+    const uint4 v = ld_nc_na_v4(x + r * stride + c);
+    a[0] = comb<OP>(a[0], (int32_t)v.x);
+    a[1] = comb<OP>(a[1], (int32_t)v.y);
+    a[2] = comb<OP>(a[2], (int32_t)v.z);
+    a[3] = comb<OP>(a[3], (int32_t)v.w);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) col_combine_out<OP>(out + c + j, a[j]);
+}
+
 template <int OP>
 int launch_i32(const int32_t* x, int64_t rows, int64_t cols, int64_t stride, int axis, int32_t* out, cudaStream_t s) {
   const int sms = sm_count();
@@ -586,7 +777,8 @@ int launch_i32(const int32_t* x, int64_t rows, int64_t cols, int64_t stride, int
     note_launch();
     return check_launch();
   }
-  const int64_t gx = (cols + kThreads - 1) / kThreads;
+  const bool vec = aligned(x, 16) && cols % 4 == 0 && stride % 4 == 0;
+  const int64_t gx = vec ? (cols + 4 * kThreads - 1) / (4 * kThreads) : (cols + kThreads - 1) / kThreads;
   col_init_i32_kernel<OP><<<(int)(gx < 4096 ? gx : 4096), kThreads, 0, s>>>(out, cols);
   note_launch();
   if (rows == 0) {  // an empty fold stores 0 (1 for Prod): overwrite the identity
@@ -600,7 +792,11 @@ int launch_i32(const int32_t* x, int64_t rows, int64_t cols, int64_t stride, int
   if (splits < 1) splits = 1;
   const int64_t per = (rows + splits - 1) / splits;
   splits = (rows + per - 1) / per;
-  col_fold_i32_kernel<OP><<<dim3((unsigned)gx, (unsigned)splits), kThreads, 0, s>>>(x, rows, cols, stride, per, out);
+  if (vec)
+    col_fold_i32_vec_kernel<OP><<<dim3((unsigned)gx, (unsigned)splits), kThreads, 0, s>>>(x, rows, cols, stride, per,
+                                                                                         out);
+  else
+    col_fold_i32_kernel<OP><<<dim3((unsigned)gx, (unsigned)splits), kThreads, 0, s>>>(x, rows, cols, stride, per, out);
   note_launch();
   return check_launch();
 }
@@ -666,6 +862,21 @@ extern "C" int up_sm100_reduce2d_f32(const float* x, int64_t rows, int64_t cols,
   if ((op == UP_OP_SUM || op == UP_OP_MEAN) && block > 1) {
     if (block > kDocMaxB || (block & (block - 1)) != 0)
       return fail_with(UP_ERR_UNSUPPORTED, "reduce2d_f32: an outer-axis block is a power of two up to 256");
+    if (block >= 64 && aligned(x, 16) && cols % 4 == 0 && row_stride % 4 == 0) {
+      const dim3 grid((unsigned)((cols + kColStrip - 1) / kColStrip), kColCluster);
+      const bool mean = op == UP_OP_MEAN;
+      if (block == 64)
+        mean ? col_sum_f32_doc_vec_kernel<true, 1><<<grid, 256, 0, s>>>(x, rows, cols, row_stride, out)
+             : col_sum_f32_doc_vec_kernel<false, 1><<<grid, 256, 0, s>>>(x, rows, cols, row_stride, out);
+      else if (block == 128)
+        mean ? col_sum_f32_doc_vec_kernel<true, 2><<<grid, 256, 0, s>>>(x, rows, cols, row_stride, out)
+             : col_sum_f32_doc_vec_kernel<false, 2><<<grid, 256, 0, s>>>(x, rows, cols, row_stride, out);
+      else
+        mean ? col_sum_f32_doc_vec_kernel<true, 4><<<grid, 256, 0, s>>>(x, rows, cols, row_stride, out)
+             : col_sum_f32_doc_vec_kernel<false, 4><<<grid, 256, 0, s>>>(x, rows, cols, row_stride, out);
+      note_launch();
+      return check_launch();
+    }
     const size_t smem = (size_t)block * 32 * sizeof(double);
     const unsigned g = (unsigned)((cols + 31) / 32);
     {
@@ -695,8 +906,21 @@ extern "C" int up_sm100_reduce2d_f32(const float* x, int64_t rows, int64_t cols,
   const int64_t gx = (cols + kThreads - 1) / kThreads;
   if (gx > 0x7fffffff) return UP_ERR_UNSUPPORTED;
   switch (op) {
-    case UP_OP_SUM: col_f32_kernel<UP_OP_SUM><<<(int)gx, kThreads, 0, s>>>(x, rows, cols, row_stride, out); break;
-    case UP_OP_MEAN: col_f32_kernel<UP_OP_MEAN><<<(int)gx, kThreads, 0, s>>>(x, rows, cols, row_stride, out); break;
+    case UP_OP_SUM:
+    case UP_OP_MEAN:
+      if (aligned(x, 16) && cols % 4 == 0 && row_stride % 4 == 0) {
+        const size_t smem = (size_t)kSerialStages * 32 * 32 * sizeof(float);
+        const unsigned g = (unsigned)((cols + 31) / 32);
+        if (op == UP_OP_SUM)
+          col_sum_f32_serial_kernel<false, kSerialStages><<<g, 32, smem, s>>>(x, rows, cols, row_stride, out);
+        else
+          col_sum_f32_serial_kernel<true, kSerialStages><<<g, 32, smem, s>>>(x, rows, cols, row_stride, out);
+      } else if (op == UP_OP_SUM) {
+        col_f32_kernel<UP_OP_SUM><<<(int)gx, kThreads, 0, s>>>(x, rows, cols, row_stride, out);
+      } else {
+        col_f32_kernel<UP_OP_MEAN><<<(int)gx, kThreads, 0, s>>>(x, rows, cols, row_stride, out);
+      }
+      break;
     case UP_OP_MAX:
     default:
       if (aligned(x, 16) && cols % 4 == 0 && row_stride % 4 == 0) {
