@@ -108,7 +108,9 @@ typedef enum up_kernel_id {
   UP_K_REDUCE2D_F32 = 7,  /* f32 Sum/Mean/Max/Min over the last or the outer axis of a rank-2 input */
   UP_K_REDUCE2D_I32 = 8,  /* i32 Sum/Prod/Max/Min/And/Or/Xor, same axes */
   UP_K_SCATTER = 9,       /* scatter / index_add with an atomic combine over axis 0 */
-  UP_K_BINCOUNT = 10
+  UP_K_BINCOUNT = 10,
+  UP_K_REDUCE_F32 = 11,   /* f32 Sum/Mean/Max/Min over one run of adjacent axes of a rank-r input (any class) */
+  UP_K_REDUCE_I32 = 12    /* i32, the seven ops, same geometry */
 } up_kernel_id;
 
 /* A buffer argument: the reference's TypedBuffer / OperandDesc. `base` and `stride` count elements
@@ -239,6 +241,17 @@ UP_API int up_sm100_reduce2d_f32(const float* x, int64_t rows, int64_t cols, int
                                  int accum, int block, float* out, void* stream);
 UP_API int up_sm100_reduce2d_i32(const int32_t* x, int64_t rows, int64_t cols, int64_t row_stride, int axis,
                                  int op, int32_t* out, void* stream);
+
+/* The same ops over the middle axis of [outer, rows, cols] (rows contiguous; batch b at x + b·outer_stride) into
+ * out[outer][cols] (row stride out_stride): `ReduceAxisClass::Middle` (plan/types.rs:150-165), and every reduced
+ * set that flattens to one run of adjacent axes, which the oracle folds in row-major order over the reduced
+ * coordinates (oracle/plan_eval.rs:565-605), the order the flattened axis has. Each output cell is the outer-axis
+ * fold of up_sm100_reduce2d_* over its batch, with the same orders, bounds and refusals. */
+UP_API int up_sm100_reduce3d_f32(const float* x, int64_t outer, int64_t rows, int64_t cols, int64_t outer_stride,
+                                 int64_t row_stride, int op, int accum, int block, float* out, int64_t out_stride,
+                                 void* stream);
+UP_API int up_sm100_reduce3d_i32(const int32_t* x, int64_t outer, int64_t rows, int64_t cols, int64_t outer_stride,
+                                 int64_t row_stride, int op, int32_t* out, int64_t out_stride, void* stream);
 
 /* The launched Scatter lift (`WriteIndex::ScatterIndexed`, ir.rs:2787-2850; the oracle's scatter store,
  * oracle/plan_eval.rs:430-490) over axis 0 of a row-major destination [out_rows, cols]: for every element (i, j) of

@@ -76,6 +76,18 @@ def test_dispatch_table_maps_the_reduction_breadth():
             assert (k.name, k.scalars) == ("up_sm100_reduce2d_i32", (OP[op], axis)), (op, mask)
 
 
+def test_dispatch_table_maps_middle_and_multi_axis_reductions():
+    """Any rank, any one run of adjacent reduced axes: flattened to [A, R, C] at launch."""
+    b = CudaSm100()
+    for shape, mask in (((4, 8, 16), 2), ((4, 8, 16), 4), ((4, 8, 16), 3), ((2, 3, 4, 5), 6), ((2, 3, 4, 5), 12)):
+        k = b.lower(_red("SUM", "F32", shape=shape, axes_mask=mask, accum="AUTO"))
+        assert (k.name, k.scalars[:2]) == ("up_sm100_reduce3d_f32", (OP["SUM"], mask)), (shape, mask)
+        for op in ("MAX", "XOR"):
+            dt = "F32" if op == "MAX" else "I32"
+            k = b.lower(_red(op, dt, shape=shape, axes_mask=mask))
+            assert k.name == f"up_sm100_reduce3d_{dt.lower()}" and k.scalars[:2] == (OP[op], mask)
+
+
 def _scatter(dtype, index_shape, index_strides, combine="ADD", shape=(9, 4), out_rows=5, **kw):
     return Plan("STRIDED", [Operand(dtype, shape), Operand("I32", index_shape, index_strides),
                             Operand(dtype, (out_rows, shape[1]))], dtype=dtype, write_index=True, combine=combine, **kw)
@@ -130,7 +142,9 @@ def test_dispatch_table_maps_each_lift():
 @pytest.mark.parametrize("plan,variant", [
     (_red("SUM", "F64"), "UnsupportedDtype"),
     (_red("PROD", "F32"), "UnsupportedOp"),
-    (_red("SUM", "F32", shape=(4, 8, 16), axes_mask=2), "UnsupportedPlanShape"),  # a middle axis
+    (_red("SUM", "F32", shape=(4, 8, 16), axes_mask=2), "UnsupportedOp"),  # a middle axis: Auto only
+    (_red("MAX", "F32", shape=(4, 8, 16), axes_mask=5), "UnsupportedPlanShape"),  # axes 0 and 2: not one run
+    (_red("MAX", "I32", shape=(4, 8, 16), axes_mask=8), "UnsupportedPlanShape"),  # no such axis
     (_red("SUM", "F32", axes_mask=1), "UnsupportedOp"),  # outer axis under the F32 policy: Auto only
     (_red("SUM", "F32", axes_mask=1, accum="AUTO", block=512), "UnsupportedPlanShape"),  # outer block <= 256
     (_red("MEAN", "I32"), "UnsupportedOp"),  # the oracle has no integer Mean

@@ -80,6 +80,8 @@ static const char* k_name(int id) {
     case UP_K_W4A16_GEMM: return "up_sm100_w4a16_gemm";
     case UP_K_REDUCE2D_F32: return "up_sm100_reduce2d_f32";
     case UP_K_REDUCE2D_I32: return "up_sm100_reduce2d_i32";
+    case UP_K_REDUCE_F32: return "up_sm100_reduce3d_f32";
+    case UP_K_REDUCE_I32: return "up_sm100_reduce3d_i32";
     case UP_K_SCATTER: return "up_sm100_scatter";
     case UP_K_BINCOUNT: return "up_sm100_bincount";
     default: return "";
@@ -115,6 +117,63 @@ static bool dense_row_major(const up_tensor& t) {
     s *= t.shape[d];
   }
   return true;
+}
+
+// Axes [a, b) of t as one axis: its element count and the stride of its innermost non-unit axis (1 when all are
+// unit). False when they do not flatten (an axis's stride is not the next one's stride times its extent).
+static bool flat_run(const up_tensor& t, int a, int b, int64_t* n, int64_t* st) {
+  int64_t count = 1, expect = 0, inner = 1;
+  bool any = false;
+  for (int d = b - 1; d >= a; --d) {
+    count *= t.shape[d];
+    if (t.shape[d] == 1) continue;
+    if (any && t.stride[d] != expect) return false;
+    if (!any) inner = t.stride[d];
+    any = true;
+    expect = t.stride[d] * t.shape[d];
+  }
+  *n = count;
+  *st = inner;
+  return true;
+}
+
+// A reduction over one run of adjacent axes [i, j) of a rank-r input seen as [A, R, C]: A the kept leading axes
+// (batch stride sA), R the reduced run (step sR), C the kept trailing axes (contiguous). kind: 1 when C == 1 (a
+// last-axis reduction of A rows of R), 0 when A == 1 (the outer axis of [R, C]), 2 otherwise (the middle axis).
+struct RedGeo {
+  int kind;
+  int64_t A, R, C, sA, sR;
+};
+static bool reduction_geometry(const up_tensor& in, uint32_t mask, RedGeo* g) {
+  const int r = in.rank;
+  if (r < 1 || r > 8) return false;
+  if (mask == 0) mask = 1u << (r - 1);  // the legacy last-axis default (ir.rs:2094-2097)
+  if (mask >> r) return false;
+  int i = 0;
+  while (!(mask >> i & 1u)) ++i;
+  int j = i;
+  while (j < r && (mask >> j & 1u)) ++j;
+  if (mask >> j) return false;  // the reduced axes are not one run
+  int64_t sC = 1;
+  if (!flat_run(in, 0, i, &g->A, &g->sA) || !flat_run(in, i, j, &g->R, &g->sR) || !flat_run(in, j, r, &g->C, &sC))
+    return false;
+  if (g->C > 1 && sC != 1) return false;  // the kept trailing axes are contiguous
+  if (g->C == 1) {
+    if (g->R > 1 && g->sR != 1) return false;  // a last-axis reduction reads contiguous rows
+    if (g->A <= 1) g->sA = g->R;
+    g->kind = 1;
+  } else {
+    if (g->R <= 1) g->sR = g->C;
+    if (g->A <= 1) g->sA = g->R * g->sR;
+    g->kind = g->A == 1 ? 0 : 2;
+  }
+  return g->sA >= 0 && g->sR >= 0;
+}
+
+static int64_t numel(const up_tensor& t) {
+  int64_t n = 1;
+  for (int d = 0; d < t.rank; ++d) n *= t.shape[d];
+  return n;
 }
 
 }  // namespace up
@@ -155,11 +214,16 @@ extern "C" int up_sm100_classify(const up_plan_desc* p, up_lowered* out) {
       const up_tensor& in = ops[0];
       const bool last_axis = p->axes_mask == 0 || (in.rank >= 1 && p->axes_mask == (1u << (in.rank - 1)));
       const bool outer_axis = in.rank == 2 && p->axes_mask == 1u;  // axis 0 of a rank-2 input
-      if (!last_axis && !outer_axis)
-        return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "the last axis, or axis 0 of a rank-2 input, is reduced");
       if (!p->identity_body) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "body/post must be the identity");
-      if (!last_axis_contiguous(in)) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "rows must be contiguous");
-      const int axis = last_axis ? 1 : 0;
+      // rank 2 keeps the rank-2 kernels; any other rank, or a middle or multi-axis set, is flattened to [A, R, C]
+      const bool general = !(in.rank == 2 && (last_axis || outer_axis));
+      RedGeo geo{};
+      if (general && !reduction_geometry(in, p->axes_mask, &geo))
+        return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE,
+                      "the reduced axes are one run of adjacent axes, and the kept and reduced runs each flatten");
+      if (!general && !last_axis_contiguous(in))
+        return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "rows must be contiguous");
+      const int axis = general ? (geo.kind == 1 ? 1 : 0) : (last_axis ? 1 : 0);
       if (p->op == UP_OP_MAX || p->op == UP_OP_ARGMAX) {
         if (p->dtype == UP_EK_BF16 && axis == 1) {
           if (p->op == UP_OP_ARGMAX && p->out_dtype != UP_EK_I64 && p->out_dtype != UP_EK_I32)
@@ -181,6 +245,7 @@ extern "C" int up_sm100_classify(const up_plan_desc* p, up_lowered* out) {
         if (b < 1 || b > 1024 || (b & (b - 1))) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "block B");
         if (summing && axis == 0 && b > 256)
           return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "an outer-axis Sum/Mean takes a block of at most 256");
+        if (general) return accept(out, UP_K_REDUCE_F32, {p->op, p->axes_mask, p->accum, b});
         if (p->op == UP_OP_SUM && axis == 1) return accept(out, UP_K_ROW_SUM_F32, {p->accum, b});
         return accept(out, UP_K_REDUCE2D_F32, {p->op, axis, p->accum, b});
       }
@@ -188,6 +253,7 @@ extern "C" int up_sm100_classify(const up_plan_desc* p, up_lowered* out) {
         if (p->op != UP_OP_SUM && p->op != UP_OP_PROD && p->op != UP_OP_MAX && p->op != UP_OP_MIN &&
             p->op != UP_OP_AND && p->op != UP_OP_OR && p->op != UP_OP_XOR)
           return refuse(out, UP_LOWER_UNSUPPORTED_OP, "i32 reductions lowered: Sum, Prod, Max, Min, And, Or, Xor");
+        if (general) return accept(out, UP_K_REDUCE_I32, {p->op, p->axes_mask});
         return accept(out, UP_K_REDUCE2D_I32, {p->op, axis});
       }
       return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "reductions are lowered for f32, i32 and (Max/ArgMax) bf16");
@@ -315,6 +381,32 @@ extern "C" int up_sm100_launch(int kernel_id, const up_tensor* ins, int n_in, co
                                      stream);
       return up_sm100_reduce2d_i32(reinterpret_cast<const int32_t*>(at(x)), x.shape[0], x.shape[1], x.stride[0], axis,
                                    (int)sc(0, UP_OP_SUM), (int32_t*)at(y), stream);
+    }
+    case UP_K_REDUCE_F32:
+    case UP_K_REDUCE_I32: {
+      if (n_in < 1 || n_out < 1) return UP_ERR_INVALID;
+      const up_tensor &x = ins[0], &y = outs[0];
+      const bool f32 = kernel_id == UP_K_REDUCE_F32;
+      if (x.dtype != (f32 ? UP_EK_F32 : UP_EK_I32) || y.dtype != x.dtype) return UP_ERR_UNSUPPORTED;
+      RedGeo g{};
+      if (!reduction_geometry(x, (uint32_t)sc(1, 0), &g)) return UP_ERR_UNSUPPORTED;
+      if (!dense_row_major(y) || numel(y) != g.A * g.C) return UP_ERR_UNSUPPORTED;  // out [A, C], dense
+      const int op = (int)sc(0, UP_OP_SUM);
+      if (g.kind == 1) {  // A rows of R
+        if (f32 && op == UP_OP_SUM)
+          return up_sm100_row_sum_f32(reinterpret_cast<const float*>(at(x)), g.A, g.R, g.sA, (float*)at(y),
+                                      (int)sc(2, UP_ACCUM_AUTO), (int)sc(3, 256), stream);
+        if (f32)
+          return up_sm100_reduce2d_f32(reinterpret_cast<const float*>(at(x)), g.A, g.R, g.sA, 1, op,
+                                       (int)sc(2, UP_ACCUM_AUTO), (int)sc(3, 256), (float*)at(y), stream);
+        return up_sm100_reduce2d_i32(reinterpret_cast<const int32_t*>(at(x)), g.A, g.R, g.sA, 1, op, (int32_t*)at(y),
+                                     stream);
+      }
+      if (f32)
+        return up_sm100_reduce3d_f32(reinterpret_cast<const float*>(at(x)), g.A, g.R, g.C, g.sA, g.sR, op,
+                                     (int)sc(2, UP_ACCUM_AUTO), (int)sc(3, 1), (float*)at(y), g.C, stream);
+      return up_sm100_reduce3d_i32(reinterpret_cast<const int32_t*>(at(x)), g.A, g.R, g.C, g.sA, g.sR, op,
+                                   (int32_t*)at(y), g.C, stream);
     }
     case UP_K_ROW_MAX_ARGMAX_BF16: {
       if (n_in < 1 || n_out < 2) return UP_ERR_INVALID;

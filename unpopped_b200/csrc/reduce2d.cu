@@ -124,7 +124,8 @@ __global__ void __launch_bounds__(kThreads) row_fold_i32_kernel(const int32_t* _
 // ---- i32, outer axis: a thread per column (coalesced across the row), rows split over gridDim.y; the splits
 // combine into out with atomics (out holds the identity first). ----
 template <int OP>
-__global__ void col_init_i32_kernel(int32_t* __restrict__ out, int64_t cols) {
+__global__ void col_init_i32_kernel(int32_t* __restrict__ out, int64_t cols, int64_t ob) {
+  out += (int64_t)blockIdx.z * ob;
   for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < cols; c += (int64_t)gridDim.x * blockDim.x)
     out[c] = ident<OP>();
 }
@@ -150,7 +151,9 @@ __device__ __forceinline__ void col_combine_out(int32_t* o, int32_t acc) {
 template <int OP>
 __global__ void __launch_bounds__(kThreads) col_fold_i32_kernel(const int32_t* __restrict__ x, int64_t rows,
                                                                  int64_t cols, int64_t stride, int64_t per_split,
-                                                                 int32_t* __restrict__ out) {
+                                                                 int32_t* __restrict__ out, int64_t xb, int64_t ob) {
+  x += (int64_t)blockIdx.z * xb;  // batch z of a middle-axis reduction
+  out += (int64_t)blockIdx.z * ob;
   const int64_t c = (int64_t)blockIdx.x * kThreads + threadIdx.x;
   if (c >= cols) return;
   const int64_t r0 = (int64_t)blockIdx.y * per_split;
@@ -389,7 +392,9 @@ constexpr int kColWarps = 16;
 template <bool MAX>
 __global__ void __launch_bounds__(32 * kColWarps) col_extremum_f32_kernel(const float* __restrict__ x, int64_t rows,
                                                                           int64_t cols, int64_t stride,
-                                                                          float* __restrict__ out) {
+                                                                          float* __restrict__ out, int64_t xb, int64_t ob) {
+  x += (int64_t)blockIdx.z * xb;  // batch z of a middle-axis reduction
+  out += (int64_t)blockIdx.z * ob;
   __shared__ float sm[kColWarps][32];
   __shared__ uint32_t si[kColWarps][32];
   __shared__ int32_t sn[kColWarps][32];
@@ -442,7 +447,9 @@ __device__ __forceinline__ void fold_col_batch(ExtState<MAX>& st, float a0, floa
 template <bool MAX>
 __global__ void __cluster_dims__(1, kColCluster, 1) __launch_bounds__(32 * kColVecWarps)
     col_extremum_f32_vec_kernel(const float* __restrict__ x, int64_t rows, int64_t cols, int64_t stride,
-                                float* __restrict__ out) {
+                                float* __restrict__ out, int64_t xb, int64_t ob) {
+  x += (int64_t)blockIdx.z * xb;  // batch z of a middle-axis reduction
+  out += (int64_t)blockIdx.z * ob;
   namespace cg = cooperative_groups;
   __shared__ float sm[kColVecWarps][kColStrip];
   __shared__ uint32_t si[kColVecWarps][kColStrip];
@@ -517,7 +524,9 @@ __global__ void __cluster_dims__(1, kColCluster, 1) __launch_bounds__(32 * kColV
 // split of the rows would change the roundings).
 template <int OP>
 __global__ void __launch_bounds__(kThreads) col_f32_kernel(const float* __restrict__ x, int64_t rows, int64_t cols,
-                                                            int64_t stride, float* __restrict__ out) {
+                                                            int64_t stride, float* __restrict__ out, int64_t xb, int64_t ob) {
+  x += (int64_t)blockIdx.z * xb;  // batch z of a middle-axis reduction
+  out += (int64_t)blockIdx.z * ob;
   static_assert(OP == UP_OP_SUM || OP == UP_OP_MEAN, "Sum or Mean");
   const int64_t c = (int64_t)blockIdx.x * kThreads + threadIdx.x;
   if (c >= cols) return;
@@ -552,7 +561,9 @@ __device__ __forceinline__ void cp_async_wait() {
 template <bool MEAN, int D>
 __global__ void __launch_bounds__(32) col_sum_f32_serial_kernel(const float* __restrict__ x, int64_t rows,
                                                                 int64_t cols, int64_t stride,
-                                                                float* __restrict__ out) {
+                                                                float* __restrict__ out, int64_t xb, int64_t ob) {
+  x += (int64_t)blockIdx.z * xb;  // batch z of a middle-axis reduction
+  out += (int64_t)blockIdx.z * ob;
   extern __shared__ __align__(16) float stage[];  // [D][32 rows][32 columns]
   const int lane = threadIdx.x;
   const int64_t cb = (int64_t)blockIdx.x * 32;
@@ -603,7 +614,9 @@ constexpr int kSerialStages = 12;  // 48 KB of rows in flight per 32 columns (me
 template <bool MEAN>
 __global__ void __launch_bounds__(32 * kDocWarps) col_sum_f32_doc_kernel(const float* __restrict__ x, int64_t rows,
                                                                          int64_t cols, int64_t stride, int B,
-                                                                         float* __restrict__ out) {
+                                                                         float* __restrict__ out, int64_t xb, int64_t ob) {
+  x += (int64_t)blockIdx.z * xb;  // batch z of a middle-axis reduction
+  out += (int64_t)blockIdx.z * ob;
   extern __shared__ double sacc[];  // [B][32]
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int64_t c = (int64_t)blockIdx.x * 32 + lane;
@@ -646,7 +659,9 @@ __global__ void __launch_bounds__(32 * kDocWarps) col_sum_f32_doc_kernel(const f
 template <bool MEAN, int I>
 __global__ void __cluster_dims__(1, kColCluster, 1) __launch_bounds__(256)
     col_sum_f32_doc_vec_kernel(const float* __restrict__ x, int64_t rows, int64_t cols, int64_t stride,
-                               float* __restrict__ out) {
+                               float* __restrict__ out, int64_t xb, int64_t ob) {
+  x += (int64_t)blockIdx.z * xb;  // batch z of a middle-axis reduction
+  out += (int64_t)blockIdx.z * ob;
   namespace cg = cooperative_groups;
   constexpr int B = 64 * I, U = 8 / I;  // U steps of I rows in flight per lane
   __shared__ double sw[8][kColStrip];
@@ -734,7 +749,9 @@ __global__ void __cluster_dims__(1, kColCluster, 1) __launch_bounds__(256)
 template <int OP>
 __global__ void __launch_bounds__(kThreads) col_fold_i32_vec_kernel(const int32_t* __restrict__ x, int64_t rows,
                                                                      int64_t cols, int64_t stride, int64_t per_split,
-                                                                     int32_t* __restrict__ out) {
+                                                                     int32_t* __restrict__ out, int64_t xb, int64_t ob) {
+  x += (int64_t)blockIdx.z * xb;  // batch z of a middle-axis reduction
+  out += (int64_t)blockIdx.z * ob;
   const int64_t c = ((int64_t)blockIdx.x * kThreads + threadIdx.x) * 4;
   if (c >= cols) return;
   const int64_t r0 = (int64_t)blockIdx.y * per_split;
@@ -765,40 +782,149 @@ __global__ void __launch_bounds__(kThreads) col_fold_i32_vec_kernel(const int32_
 }
 
 template <int OP>
-int launch_i32(const int32_t* x, int64_t rows, int64_t cols, int64_t stride, int axis, int32_t* out, cudaStream_t s) {
+int launch_i32_rows(const int32_t* x, int64_t rows, int64_t cols, int64_t stride, int32_t* out, cudaStream_t s) {
   const int sms = sm_count();
-  if (axis == 1) {
-    const bool vec = aligned(x, 16) && cols % 4 == 0 && stride % 4 == 0;
-    // rows held in registers with the next row's loads in flight need only two CTAs per SM (measured best)
-    const int64_t per_sm = vec && cols / 4 <= 8 * kThreads ? 2 : 8;
-    const int64_t g = rows < (int64_t)sms * per_sm ? rows : (int64_t)sms * per_sm;
-    if (vec) row_fold_i32_kernel<OP, true><<<(int)g, kThreads, 0, s>>>(x, rows, cols, stride, out);
-    else row_fold_i32_kernel<OP, false><<<(int)g, kThreads, 0, s>>>(x, rows, cols, stride, out);
-    note_launch();
-    return check_launch();
-  }
   const bool vec = aligned(x, 16) && cols % 4 == 0 && stride % 4 == 0;
-  const int64_t gx = vec ? (cols + 4 * kThreads - 1) / (4 * kThreads) : (cols + kThreads - 1) / kThreads;
-  col_init_i32_kernel<OP><<<(int)(gx < 4096 ? gx : 4096), kThreads, 0, s>>>(out, cols);
-  note_launch();
-  if (rows == 0) {  // an empty fold stores 0 (1 for Prod): overwrite the identity
-    if (OP != UP_OP_PROD) cudaMemsetAsync(out, 0, sizeof(int32_t) * (size_t)cols, s);
-    return check_launch();
-  }
-  int64_t splits = ((int64_t)sms * 4 + gx - 1) / gx;
-  const int64_t max_splits = (rows + 63) / 64;
-  if (splits > max_splits) splits = max_splits;
-  if (splits > 65535) splits = 65535;
-  if (splits < 1) splits = 1;
-  const int64_t per = (rows + splits - 1) / splits;
-  splits = (rows + per - 1) / per;
-  if (vec)
-    col_fold_i32_vec_kernel<OP><<<dim3((unsigned)gx, (unsigned)splits), kThreads, 0, s>>>(x, rows, cols, stride, per,
-                                                                                         out);
-  else
-    col_fold_i32_kernel<OP><<<dim3((unsigned)gx, (unsigned)splits), kThreads, 0, s>>>(x, rows, cols, stride, per, out);
+  // rows held in registers with the next row's loads in flight need only two CTAs per SM (measured best)
+  const int64_t per_sm = vec && cols / 4 <= 8 * kThreads ? 2 : 8;
+  const int64_t g = rows < (int64_t)sms * per_sm ? rows : (int64_t)sms * per_sm;
+  if (vec) row_fold_i32_kernel<OP, true><<<(int)g, kThreads, 0, s>>>(x, rows, cols, stride, out);
+  else row_fold_i32_kernel<OP, false><<<(int)g, kThreads, 0, s>>>(x, rows, cols, stride, out);
   note_launch();
   return check_launch();
+}
+
+constexpr int64_t kMaxGridZ = 65535;
+
+// The middle axis of [outer, rows, cols] (outer 1: axis 0 of [rows, cols]) into out[outer][cols] (row stride ob);
+// batch b reads x + b * xb. Batches ride on gridDim.z, in chunks of at most 65535.
+template <int OP>
+int launch_i32_cols(const int32_t* x, int64_t outer, int64_t rows, int64_t cols, int64_t xb, int64_t stride,
+                    int32_t* out, int64_t ob, cudaStream_t s) {
+  const int sms = sm_count();
+  const bool vec = aligned(x, 16) && cols % 4 == 0 && stride % 4 == 0 && xb % 4 == 0;
+  const int64_t gx = vec ? (cols + 4 * kThreads - 1) / (4 * kThreads) : (cols + kThreads - 1) / kThreads;
+  for (int64_t b0 = 0; b0 < outer; b0 += kMaxGridZ) {
+    const int64_t nb = outer - b0 < kMaxGridZ ? outer - b0 : kMaxGridZ;
+    const int32_t* xs = x + b0 * xb;
+    int32_t* os = out + b0 * ob;
+    col_init_i32_kernel<OP><<<dim3((unsigned)(gx < 4096 ? gx : 4096), 1, (unsigned)nb), kThreads, 0, s>>>(os, cols, ob);
+    note_launch();
+    if (rows == 0) {  // an empty fold stores 0 (1 for Prod): overwrite the identity
+      if (OP != UP_OP_PROD) {
+        const cudaError_t e = cudaMemset2DAsync(os, sizeof(int32_t) * (size_t)ob, 0, sizeof(int32_t) * (size_t)cols,
+                                                (size_t)nb, s);
+        if (e != cudaSuccess) return cuda_status(e);
+      }
+      continue;
+    }
+    int64_t splits = ((int64_t)sms * 4 + gx * nb - 1) / (gx * nb);
+    const int64_t max_splits = (rows + 63) / 64;
+    if (splits > max_splits) splits = max_splits;
+    if (splits > 65535) splits = 65535;
+    if (splits < 1) splits = 1;
+    const int64_t per = (rows + splits - 1) / splits;
+    splits = (rows + per - 1) / per;
+    const dim3 grid((unsigned)gx, (unsigned)splits, (unsigned)nb);
+    if (vec)
+      col_fold_i32_vec_kernel<OP><<<grid, kThreads, 0, s>>>(xs, rows, cols, stride, per, os, xb, ob);
+    else
+      col_fold_i32_kernel<OP><<<grid, kThreads, 0, s>>>(xs, rows, cols, stride, per, os, xb, ob);
+    note_launch();
+    const int st = check_launch();
+    if (st != UP_OK) return st;
+  }
+  return check_launch();
+}
+
+template <int OP>
+int launch_i32(const int32_t* x, int64_t outer, int64_t rows, int64_t cols, int64_t xb, int64_t stride, int axis,
+               int32_t* out, int64_t ob, cudaStream_t s) {
+  if (axis == 1 && outer == 1) return launch_i32_rows<OP>(x, rows, cols, stride, out, s);
+  return launch_i32_cols<OP>(x, outer, rows, cols, xb, stride, out, ob, s);
+}
+
+// f32 over the middle axis of [outer, rows, cols] (outer 1: axis 0), as launch_i32_cols.
+int launch_f32_cols(const float* x, int64_t outer, int64_t rows, int64_t cols, int64_t xb, int64_t row_stride,
+                    int op, int accum, int block, float* out, int64_t ob, cudaStream_t s) {
+  const bool summing = op == UP_OP_SUM || op == UP_OP_MEAN;
+  // Sum/Mean in the serial order (block 1) or the documented order of a logical block of up to 256
+  if (summing && accum != UP_ACCUM_AUTO)
+    return fail_with(UP_ERR_UNSUPPORTED, "reduce2d_f32: an outer-axis Sum/Mean is lowered for Auto");
+  if (summing && block > 1 && (block > kDocMaxB || (block & (block - 1)) != 0))
+    return fail_with(UP_ERR_UNSUPPORTED, "reduce2d_f32: an outer-axis block is a power of two up to 256");
+  if (rows > 0x7fffffffLL) return UP_ERR_UNSUPPORTED;
+  const int64_t gx = (cols + kThreads - 1) / kThreads;
+  if (gx > 0x7fffffff) return UP_ERR_UNSUPPORTED;
+  const bool vec = aligned(x, 16) && cols % 4 == 0 && row_stride % 4 == 0 && xb % 4 == 0;
+  if (summing && block > 1 && !(block >= 64 && vec)) {
+    static std::mutex mu;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_status(e);
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+      const int bytes = (int)((size_t)kDocMaxB * 32 * sizeof(double));
+      e = cudaFuncSetAttribute(col_sum_f32_doc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(col_sum_f32_doc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+      if (e != cudaSuccess) return cuda_status(e);
+      if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+  }
+  const bool mean = op == UP_OP_MEAN;
+  for (int64_t b0 = 0; b0 < outer; b0 += kMaxGridZ) {
+    const unsigned nb = (unsigned)(outer - b0 < kMaxGridZ ? outer - b0 : kMaxGridZ);
+    const float* xs = x + b0 * xb;
+    float* os = out + b0 * ob;
+    if (summing && block > 1 && block >= 64 && vec) {
+      const dim3 grid((unsigned)((cols + kColStrip - 1) / kColStrip), kColCluster, nb);
+      if (block == 64)
+        mean ? col_sum_f32_doc_vec_kernel<true, 1><<<grid, 256, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob)
+             : col_sum_f32_doc_vec_kernel<false, 1><<<grid, 256, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob);
+      else if (block == 128)
+        mean ? col_sum_f32_doc_vec_kernel<true, 2><<<grid, 256, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob)
+             : col_sum_f32_doc_vec_kernel<false, 2><<<grid, 256, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob);
+      else
+        mean ? col_sum_f32_doc_vec_kernel<true, 4><<<grid, 256, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob)
+             : col_sum_f32_doc_vec_kernel<false, 4><<<grid, 256, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob);
+    } else if (summing && block > 1) {
+      const size_t smem = (size_t)block * 32 * sizeof(double);
+      const dim3 grid((unsigned)((cols + 31) / 32), 1, nb);
+      if (mean)
+        col_sum_f32_doc_kernel<true><<<grid, 32 * kDocWarps, smem, s>>>(xs, rows, cols, row_stride, block, os, xb, ob);
+      else
+        col_sum_f32_doc_kernel<false><<<grid, 32 * kDocWarps, smem, s>>>(xs, rows, cols, row_stride, block, os, xb, ob);
+    } else if (summing && vec) {
+      const size_t smem = (size_t)kSerialStages * 32 * 32 * sizeof(float);
+      const dim3 grid((unsigned)((cols + 31) / 32), 1, nb);
+      if (mean)
+        col_sum_f32_serial_kernel<true, kSerialStages><<<grid, 32, smem, s>>>(xs, rows, cols, row_stride, os, xb, ob);
+      else
+        col_sum_f32_serial_kernel<false, kSerialStages><<<grid, 32, smem, s>>>(xs, rows, cols, row_stride, os, xb, ob);
+    } else if (summing) {
+      const dim3 grid((unsigned)gx, 1, nb);
+      if (mean) col_f32_kernel<UP_OP_MEAN><<<grid, kThreads, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob);
+      else col_f32_kernel<UP_OP_SUM><<<grid, kThreads, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob);
+    } else if (vec) {
+      const dim3 grid((unsigned)((cols + kColStrip - 1) / kColStrip), kColCluster, nb);
+      if (op == UP_OP_MAX)
+        col_extremum_f32_vec_kernel<true><<<grid, 32 * kColVecWarps, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob);
+      else
+        col_extremum_f32_vec_kernel<false><<<grid, 32 * kColVecWarps, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob);
+    } else {
+      const dim3 grid((unsigned)((cols + 31) / 32), 1, nb);
+      if (op == UP_OP_MAX)
+        col_extremum_f32_kernel<true><<<grid, 32 * kColWarps, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob);
+      else
+        col_extremum_f32_kernel<false><<<grid, 32 * kColWarps, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob);
+    }
+    note_launch();
+    const int st = check_launch();
+    if (st != UP_OK) return st;
+  }
+  return UP_OK;
 }
 
 }  // namespace r2
@@ -807,24 +933,39 @@ int launch_i32(const int32_t* x, int64_t rows, int64_t cols, int64_t stride, int
 using namespace up;
 using namespace up::r2;
 
+static int reduce_i32(const int32_t* x, int64_t outer, int64_t rows, int64_t cols, int64_t xb, int64_t row_stride,
+                      int axis, int op, int32_t* out, int64_t ob, cudaStream_t s) {
+  if (rows > 65535LL * 0x7fffffffLL || cols > 0x7fffffffLL * kThreads) return UP_ERR_UNSUPPORTED;
+  switch (op) {
+    case UP_OP_SUM: return launch_i32<UP_OP_SUM>(x, outer, rows, cols, xb, row_stride, axis, out, ob, s);
+    case UP_OP_PROD: return launch_i32<UP_OP_PROD>(x, outer, rows, cols, xb, row_stride, axis, out, ob, s);
+    case UP_OP_MAX: return launch_i32<UP_OP_MAX>(x, outer, rows, cols, xb, row_stride, axis, out, ob, s);
+    case UP_OP_MIN: return launch_i32<UP_OP_MIN>(x, outer, rows, cols, xb, row_stride, axis, out, ob, s);
+    case UP_OP_AND: return launch_i32<UP_OP_AND>(x, outer, rows, cols, xb, row_stride, axis, out, ob, s);
+    case UP_OP_OR: return launch_i32<UP_OP_OR>(x, outer, rows, cols, xb, row_stride, axis, out, ob, s);
+    case UP_OP_XOR: return launch_i32<UP_OP_XOR>(x, outer, rows, cols, xb, row_stride, axis, out, ob, s);
+    default: return UP_ERR_UNSUPPORTED;
+  }
+}
+
 extern "C" int up_sm100_reduce2d_i32(const int32_t* x, int64_t rows, int64_t cols, int64_t row_stride, int axis,
                                      int op, int32_t* out, void* stream) {
   UP_CHECK_ARG(rows >= 0 && cols >= 0 && row_stride >= cols && (axis == 0 || axis == 1));
   UP_CHECK_ARG(out != nullptr || (axis == 1 ? rows : cols) == 0);
   if ((axis == 1 ? rows : cols) == 0) return UP_OK;
   UP_CHECK_ARG(x != nullptr || (axis == 1 ? cols : rows) == 0);
-  if (rows > 65535LL * 0x7fffffffLL || cols > 0x7fffffffLL * kThreads) return UP_ERR_UNSUPPORTED;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (op) {
-    case UP_OP_SUM: return launch_i32<UP_OP_SUM>(x, rows, cols, row_stride, axis, out, s);
-    case UP_OP_PROD: return launch_i32<UP_OP_PROD>(x, rows, cols, row_stride, axis, out, s);
-    case UP_OP_MAX: return launch_i32<UP_OP_MAX>(x, rows, cols, row_stride, axis, out, s);
-    case UP_OP_MIN: return launch_i32<UP_OP_MIN>(x, rows, cols, row_stride, axis, out, s);
-    case UP_OP_AND: return launch_i32<UP_OP_AND>(x, rows, cols, row_stride, axis, out, s);
-    case UP_OP_OR: return launch_i32<UP_OP_OR>(x, rows, cols, row_stride, axis, out, s);
-    case UP_OP_XOR: return launch_i32<UP_OP_XOR>(x, rows, cols, row_stride, axis, out, s);
-    default: return UP_ERR_UNSUPPORTED;
-  }
+  return reduce_i32(x, 1, rows, cols, 0, row_stride, axis, op, out, 0, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int up_sm100_reduce3d_i32(const int32_t* x, int64_t outer, int64_t rows, int64_t cols,
+                                     int64_t outer_stride, int64_t row_stride, int op, int32_t* out,
+                                     int64_t out_stride, void* stream) {
+  UP_CHECK_ARG(outer >= 0 && rows >= 0 && cols >= 0 && row_stride >= cols && out_stride >= cols);
+  UP_CHECK_ARG(outer <= 1 || outer_stride >= rows * row_stride);
+  if (outer == 0 || cols == 0) return UP_OK;
+  UP_CHECK_ARG(out != nullptr && (x != nullptr || rows == 0));
+  return reduce_i32(x, outer, rows, cols, outer_stride, row_stride, 0, op, out, out_stride,
+                    static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int up_sm100_reduce2d_f32(const float* x, int64_t rows, int64_t cols, int64_t row_stride, int axis, int op,
@@ -856,88 +997,17 @@ extern "C" int up_sm100_reduce2d_f32(const float* x, int64_t rows, int64_t cols,
     note_launch();
     return check_launch();
   }
-  // axis 0: Sum/Mean in the serial order (block 1) or the documented order of a logical block of up to 256
-  if ((op == UP_OP_SUM || op == UP_OP_MEAN) && accum != UP_ACCUM_AUTO)
-    return fail_with(UP_ERR_UNSUPPORTED, "reduce2d_f32: an outer-axis Sum/Mean is lowered for Auto");
-  if ((op == UP_OP_SUM || op == UP_OP_MEAN) && block > 1) {
-    if (block > kDocMaxB || (block & (block - 1)) != 0)
-      return fail_with(UP_ERR_UNSUPPORTED, "reduce2d_f32: an outer-axis block is a power of two up to 256");
-    if (block >= 64 && aligned(x, 16) && cols % 4 == 0 && row_stride % 4 == 0) {
-      const dim3 grid((unsigned)((cols + kColStrip - 1) / kColStrip), kColCluster);
-      const bool mean = op == UP_OP_MEAN;
-      if (block == 64)
-        mean ? col_sum_f32_doc_vec_kernel<true, 1><<<grid, 256, 0, s>>>(x, rows, cols, row_stride, out)
-             : col_sum_f32_doc_vec_kernel<false, 1><<<grid, 256, 0, s>>>(x, rows, cols, row_stride, out);
-      else if (block == 128)
-        mean ? col_sum_f32_doc_vec_kernel<true, 2><<<grid, 256, 0, s>>>(x, rows, cols, row_stride, out)
-             : col_sum_f32_doc_vec_kernel<false, 2><<<grid, 256, 0, s>>>(x, rows, cols, row_stride, out);
-      else
-        mean ? col_sum_f32_doc_vec_kernel<true, 4><<<grid, 256, 0, s>>>(x, rows, cols, row_stride, out)
-             : col_sum_f32_doc_vec_kernel<false, 4><<<grid, 256, 0, s>>>(x, rows, cols, row_stride, out);
-      note_launch();
-      return check_launch();
-    }
-    const size_t smem = (size_t)block * 32 * sizeof(double);
-    const unsigned g = (unsigned)((cols + 31) / 32);
-    {
-      static std::mutex mu;
-      static bool attr_set[64] = {false};
-      int dev = 0;
-      cudaError_t e = cudaGetDevice(&dev);
-      if (e != cudaSuccess) return cuda_status(e);
-      std::lock_guard<std::mutex> lk(mu);
-      if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        const int bytes = (int)((size_t)kDocMaxB * 32 * sizeof(double));
-        e = cudaFuncSetAttribute(col_sum_f32_doc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-        if (e == cudaSuccess)
-          e = cudaFuncSetAttribute(col_sum_f32_doc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-        if (e != cudaSuccess) return cuda_status(e);
-        if (dev >= 0 && dev < 64) attr_set[dev] = true;
-      }
-    }
-    if (op == UP_OP_MEAN)
-      col_sum_f32_doc_kernel<true><<<g, 32 * kDocWarps, smem, s>>>(x, rows, cols, row_stride, block, out);
-    else
-      col_sum_f32_doc_kernel<false><<<g, 32 * kDocWarps, smem, s>>>(x, rows, cols, row_stride, block, out);
-    note_launch();
-    return check_launch();
-  }
-  if (rows > 0x7fffffffLL) return UP_ERR_UNSUPPORTED;
-  const int64_t gx = (cols + kThreads - 1) / kThreads;
-  if (gx > 0x7fffffff) return UP_ERR_UNSUPPORTED;
-  switch (op) {
-    case UP_OP_SUM:
-    case UP_OP_MEAN:
-      if (aligned(x, 16) && cols % 4 == 0 && row_stride % 4 == 0) {
-        const size_t smem = (size_t)kSerialStages * 32 * 32 * sizeof(float);
-        const unsigned g = (unsigned)((cols + 31) / 32);
-        if (op == UP_OP_SUM)
-          col_sum_f32_serial_kernel<false, kSerialStages><<<g, 32, smem, s>>>(x, rows, cols, row_stride, out);
-        else
-          col_sum_f32_serial_kernel<true, kSerialStages><<<g, 32, smem, s>>>(x, rows, cols, row_stride, out);
-      } else if (op == UP_OP_SUM) {
-        col_f32_kernel<UP_OP_SUM><<<(int)gx, kThreads, 0, s>>>(x, rows, cols, row_stride, out);
-      } else {
-        col_f32_kernel<UP_OP_MEAN><<<(int)gx, kThreads, 0, s>>>(x, rows, cols, row_stride, out);
-      }
-      break;
-    case UP_OP_MAX:
-    default:
-      if (aligned(x, 16) && cols % 4 == 0 && row_stride % 4 == 0) {
-        const dim3 grid((unsigned)((cols + kColStrip - 1) / kColStrip), kColCluster);
-        if (op == UP_OP_MAX)
-          col_extremum_f32_vec_kernel<true><<<grid, 32 * kColVecWarps, 0, s>>>(x, rows, cols, row_stride, out);
-        else
-          col_extremum_f32_vec_kernel<false><<<grid, 32 * kColVecWarps, 0, s>>>(x, rows, cols, row_stride, out);
-      } else if (op == UP_OP_MAX) {
-        col_extremum_f32_kernel<true><<<(unsigned)((cols + 31) / 32), 32 * kColWarps, 0, s>>>(x, rows, cols,
-                                                                                           row_stride, out);
-      } else {
-        col_extremum_f32_kernel<false><<<(unsigned)((cols + 31) / 32), 32 * kColWarps, 0, s>>>(x, rows, cols,
-                                                                                            row_stride, out);
-      }
-      break;
-  }
-  note_launch();
-  return check_launch();
+  return launch_f32_cols(x, 1, rows, cols, 0, row_stride, op, accum, block, out, 0, s);
+}
+
+extern "C" int up_sm100_reduce3d_f32(const float* x, int64_t outer, int64_t rows, int64_t cols, int64_t outer_stride,
+                                     int64_t row_stride, int op, int accum, int block, float* out, int64_t out_stride,
+                                     void* stream) {
+  UP_CHECK_ARG(outer >= 0 && rows >= 0 && cols >= 0 && row_stride >= cols && out_stride >= cols);
+  UP_CHECK_ARG(outer <= 1 || outer_stride >= rows * row_stride);
+  if (op != UP_OP_SUM && op != UP_OP_MEAN && op != UP_OP_MAX && op != UP_OP_MIN) return UP_ERR_UNSUPPORTED;
+  if (outer == 0 || cols == 0) return UP_OK;
+  UP_CHECK_ARG(out != nullptr && (x != nullptr || rows == 0));
+  return launch_f32_cols(x, outer, rows, cols, outer_stride, row_stride, op, accum, block, out, out_stride,
+                         static_cast<cudaStream_t>(stream));
 }

@@ -101,6 +101,29 @@ def reduce2d(x: torch.Tensor, op: str, axis: int = 1, accum: str = "auto", block
     return out
 
 
+def reduce3d(x: torch.Tensor, op: str, accum: str = "auto", block: int = 1,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """Reduction of an [outer, rows, cols] f32 or i32 tensor over its middle axis into [outer, cols]; the rows and
+    the output rows are contiguous. Each output cell is the outer-axis fold of reduce2d over its batch."""
+    _cuda(x, "x")
+    if x.dim() != 3 or x.stride(2) != 1 or x.dtype not in (torch.float32, torch.int32):
+        raise ValueError("reduce3d takes a 3-D float32 or int32 tensor with contiguous rows")
+    outer, rows, cols = x.shape
+    if out is None:
+        out = torch.empty((outer, cols), dtype=x.dtype, device=x.device)
+    if out.dim() != 2 or tuple(out.shape) != (outer, cols) or out.stride(1) != 1:
+        raise ValueError("out is [outer, cols] with contiguous rows")
+    L = _lib.load()
+    if x.dtype == torch.float32:
+        check(L.up_sm100_reduce3d_f32(x.data_ptr(), outer, rows, cols, x.stride(0), x.stride(1), OP[op.upper()],
+                                      ACCUM[accum.upper()], block, out.data_ptr(), out.stride(0), _stream(x)),
+              "reduce3d_f32")
+    else:
+        check(L.up_sm100_reduce3d_i32(x.data_ptr(), outer, rows, cols, x.stride(0), x.stride(1), OP[op.upper()],
+                                      out.data_ptr(), out.stride(0), _stream(x)), "reduce3d_i32")
+    return out
+
+
 _SC_EK = {torch.int32: EK["I32"], torch.int64: EK["I64"], torch.uint32: EK["U32"], torch.float32: EK["F32"],
           torch.float64: EK["F64"]}
 
