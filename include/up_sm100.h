@@ -110,7 +110,8 @@ typedef enum up_kernel_id {
   UP_K_SCATTER = 9,       /* scatter / index_add with an atomic combine over axis 0 */
   UP_K_BINCOUNT = 10,
   UP_K_REDUCE_F32 = 11,   /* f32 Sum/Mean/Max/Min over one run of adjacent axes of a rank-r input (any class) */
-  UP_K_REDUCE_I32 = 12    /* i32, the seven ops, same geometry */
+  UP_K_REDUCE_I32 = 12,   /* i32, the seven ops, same geometry */
+  UP_K_ROW_REDUCE_F32 = 13 /* a RowReduce form (softmax, RMS norm, centred quotient) over f32 rows */
 } up_kernel_id;
 
 /* A buffer argument: the reference's TypedBuffer / OperandDesc. `base` and `stride` count elements
@@ -150,6 +151,9 @@ typedef struct up_plan_desc {
   int32_t scatter_axis;    /* the scattered axis of the destination */
   int32_t combine;         /* up_write_combine */
   int32_t count;           /* bincount: the input is its own index and the increment is the constant 1 */
+  /* appended: a RowReduce plan (Access::RowReduce, ir.rs; its stages and epilogue matched to a named form) */
+  int32_t row_reduce_form; /* up_row_reduce_form; 0 = not one of the lowered forms */
+  double eps;              /* the RMS norm's constant under the square root */
 } up_plan_desc;
 
 /* What `Backend::lower` returns (`GeneratedKernel{name, source}` + launch metadata), or why it refused
@@ -241,6 +245,24 @@ UP_API int up_sm100_reduce2d_f32(const float* x, int64_t rows, int64_t cols, int
                                  int accum, int block, float* out, void* stream);
 UP_API int up_sm100_reduce2d_i32(const int32_t* x, int64_t rows, int64_t cols, int64_t row_stride, int axis,
                                  int op, int32_t* out, void* stream);
+
+/* RowReduce forms, by the stages and epilogue of `Access::RowReduce` (crates/unpopped/src/ir.rs) they stand for:
+ * the forms of crates/unpopped/tests/kernel_parallel_row_reduce_agrees.rs:99-131. */
+typedef enum up_row_reduce_form {
+  UP_RR_NONE = 0,
+  UP_RR_SOFTMAX = 1,   /* stages Max(x), Sum(exp(x - r0)); epilogue exp(x - r0) / r1 */
+  UP_RR_RMS_NORM = 2,  /* stage Mean(x * x); epilogue x / sqrt(r0 + eps) */
+  UP_RR_CENTRED = 3    /* stages Mean(x), Max(x - r0); epilogue (x - r0) / r1 */
+} up_row_reduce_form;
+
+/* The launched RowReduce lift (`lift_row_reduce_opdef_launched`, kernel_lift/row_reduce_launched.rs:47-84) over
+ * the rows of a [rows, cols] f32 input (contiguous rows) into out (row stride out_stride), for logical block
+ * `block` (a power of two up to 1024). Expressions are evaluated in f64; Sum/Mean stages fold in the documented
+ * order of `block` (kernel_lift/block_reduce.rs:13-23); Max stages are NaN-keeping; each stage value is rounded
+ * once to f32 and the epilogue once on the store (row_reduce_launched.rs:1-24). The reference holds its softmax
+ * and RMS norm to a few ulps of its serial lift (kernel_parallel_row_reduce_agrees.rs:371-392). */
+UP_API int up_sm100_row_reduce_f32(const float* x, int64_t rows, int64_t cols, int64_t row_stride, int form,
+                                   int block, double eps, float* out, int64_t out_stride, void* stream);
 
 /* The same ops over the middle axis of [outer, rows, cols] (rows contiguous; batch b at x + b·outer_stride) into
  * out[outer][cols] (row stride out_stride): `ReduceAxisClass::Middle` (plan/types.rs:150-165), and every reduced

@@ -44,6 +44,7 @@ def lib():
         L.orc_row_mean_f32_documented.argtypes = [P, I64, I64, I64, I64, P, I]
         L.orc_reduce2d_i32.argtypes = [P, I64, I64, I64, I, I, P, I]
         L.orc_col_sum_f32_documented.argtypes = [P, I64, I64, I64, I64, I, P, I]
+        L.orc_row_reduce_f32.argtypes = [P, I64, I64, I64, I, I64, ctypes.c_double, P, I64, I]
         L.orc_scatter.argtypes = [P, I64, I64, I, P, I, I64, I, P, I64]
         L.orc_bincount.argtypes = [P, I64, I, P, I64]
         L.orc_scan_i32.argtypes = [P, P, I64, I64, I, I, I, ctypes.c_int32, I]
@@ -162,6 +163,20 @@ def bincount(x: np.ndarray, counts: np.ndarray) -> np.ndarray:
     res = np.array(counts, dtype=np.int32, copy=True)
     lib().orc_bincount(_p(xx), xx.size, _INDEX_EK[xx.dtype], _p(res), res.size)
     return res
+
+
+ROW_REDUCE_FORMS = {"softmax": 1, "rms_norm": 2, "centred": 3}
+
+
+def row_reduce_f32(x: np.ndarray, form: str, block: int, eps: float = 1e-3, threads: int = 1) -> np.ndarray:
+    """A RowReduce form (softmax, rms_norm, centred) over the last axis of a [rows, cols] f32 array, in the
+    launched lift's written order for a logical block of ``block`` (kernel_lift/row_reduce_launched.rs:1-24)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, cols = x.shape
+    out = np.empty_like(x)
+    lib().orc_row_reduce_f32(_p(x), rows, cols, cols, ROW_REDUCE_FORMS[form], block, ctypes.c_double(eps), _p(out),
+                             cols, threads)
+    return out
 
 
 def reduce2d_i32(x: np.ndarray, op: str, axis: int, threads: int = 1) -> np.ndarray:

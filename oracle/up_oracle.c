@@ -147,6 +147,70 @@ void orc_row_sum_f32_documented(const float* x, int64_t rows, int64_t cols, int6
   }
 }
 
+/* RowReduce forms (Access::RowReduce; kernel_lift/row_reduce_launched.rs:1-24, the oracle's eval_row_reduce,
+ * oracle/plan_contract.rs:265-360), in the launched lift's written order for a logical block of B threads:
+ * form 1 softmax (Max(x); Sum(exp(x - r0)); exp(x - r0) / r1), 2 RMS norm (Mean(x * x); x / sqrt(r0 + eps)),
+ * 3 centred quotient (Mean(x); Max(x - r0); (x - r0) / r1) — the forms of
+ * crates/unpopped/tests/kernel_parallel_row_reduce_agrees.rs:99-131. Every expression is evaluated in f64 from the
+ * f32 inputs and the f32 stage values; a Sum/Mean stage folds in the documented order (Mean divides the f64 total);
+ * a Max stage folds as the oracle does (take = !have || v is NaN || v > acc); each stage value is rounded once to
+ * f32, and the epilogue once on the store. */
+static double orc_doc_total(const double* pre, int64_t n, int64_t block, double* acc) {
+  for (int64_t t = 0; t < block; ++t) {
+    double a = 0.0;
+    for (int64_t c = t; c < n; c += block) a += pre[c];
+    acc[t] = a;
+  }
+  for (int64_t s = block / 2; s > 0; s /= 2)
+    for (int64_t t = 0; t < s; ++t) acc[t] += acc[t + s];
+  return acc[0];
+}
+
+static double orc_max_stage(const double* pre, int64_t n) {
+  double acc = 0.0;
+  int have = 0;
+  for (int64_t c = 0; c < n; ++c) {
+    const double v = pre[c];
+    if (!have || v != v || v > acc) acc = v;
+    have = 1;
+  }
+  return acc;
+}
+
+void orc_row_reduce_f32(const float* x, int64_t rows, int64_t cols, int64_t row_stride, int form, int64_t block,
+                        double eps, float* out, int64_t out_stride, int threads) {
+#pragma omp parallel num_threads(threads) if (threads > 1)
+  {
+    double* pre = (double*)malloc(sizeof(double) * (size_t)(cols > 0 ? cols : 1));
+    double* acc = (double*)malloc(sizeof(double) * (size_t)block);
+#pragma omp for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+      const float* row = x + r * row_stride;
+      float* o = out + r * out_stride;
+      if (form == 1) {
+        for (int64_t c = 0; c < cols; ++c) pre[c] = (double)row[c];
+        const float r0 = (float)orc_max_stage(pre, cols);
+        for (int64_t c = 0; c < cols; ++c) pre[c] = exp((double)row[c] - (double)r0);
+        const float r1 = (float)orc_doc_total(pre, cols, block, acc);
+        for (int64_t c = 0; c < cols; ++c) o[c] = (float)(pre[c] / (double)r1);
+      } else if (form == 2) {
+        for (int64_t c = 0; c < cols; ++c) pre[c] = (double)row[c] * (double)row[c];
+        const float r0 = (float)(orc_doc_total(pre, cols, block, acc) / (double)cols);
+        const double den = sqrt((double)r0 + eps);
+        for (int64_t c = 0; c < cols; ++c) o[c] = (float)((double)row[c] / den);
+      } else {
+        for (int64_t c = 0; c < cols; ++c) pre[c] = (double)row[c];
+        const float r0 = (float)(orc_doc_total(pre, cols, block, acc) / (double)cols);
+        for (int64_t c = 0; c < cols; ++c) pre[c] = (double)row[c] - (double)r0;
+        const float r1 = (float)orc_max_stage(pre, cols);
+        for (int64_t c = 0; c < cols; ++c) o[c] = (float)(pre[c] / (double)r1);
+      }
+    }
+    free(pre);
+    free(acc);
+  }
+}
+
 /* Max (extremum_fold, plan_contract.rs:179-210: take = !have || v is NaN || v > acc) and ArgMax
  * (arg_fold, plan_contract.rs:213-245: take = !have || (!acc.is_nan() && (v.is_nan() || v > acc)))
  * over a bf16 row, folded in f64. The max is stored as f32 (exact: bf16 is a subset). A NaN max is the

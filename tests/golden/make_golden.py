@@ -386,6 +386,79 @@ def golden_scatter() -> dict:
     }
 
 
+# --- crates/unpopped/tests/kernel_parallel_row_reduce_agrees.rs ---------------------------------------
+
+def row_reduce_corpus() -> list:
+    """`corpus` (row_reduce_agrees.rs:36-55): benign positives, a cancelling row, huge/tiny alternation, 0.1,
+    mixed signs; five rows of 96, generated column by column."""
+    rows, cols = 5, 96
+    s = [0x9E3779B97F4A7C15]
+    per_col = []
+    for c in range(cols):
+        big = 1.0e8 if c % 2 == 0 else -1.0e8
+        huge = 1.0e10 if c % 2 == 0 else -1.0e10
+        a = 1.0e-3 + 1.0e3 * lcg(s)
+        b = 1.0 + lcg(s) if c % 7 == 0 else big
+        h = huge * (1.0 + 1e-3 * lcg(s))
+        e = (lcg(s) - 0.5) * 2.0e5
+        per_col.append([a, b, h, 0.1, e])
+    return [[per_col[c][r] for c in range(cols)] for r in range(rows)]
+
+
+def row_reduce_gentle() -> list:
+    """`gentle` (row_reduce_agrees.rs:58-63): values in [-2, 4] for the transcendental epilogues."""
+    rows, cols = 5, 96
+    v = [((i * 7 + 3) % 19) * 0.37 - 2.0 for i in range(rows * cols)]
+    return [v[r * cols:(r + 1) * cols] for r in range(rows)]
+
+
+def centred_documented(xs: list, block: int) -> list:
+    """`centred_documented` (row_reduce_agrees.rs:330-339): stage 0 a documented mean, stage 1 the max of x - r0,
+    the epilogue (x - r0) / r1; stage values and the output are rounded to f32, the expressions between them are
+    not."""
+    r0 = documented(xs, block, mean=True)
+    r1 = f32(max(x - r0 for x in xs))
+    return [f32((x - r0) / r1) for x in xs]
+
+
+def serial_softmax(xs: list) -> list:
+    """The serial lift of `softmax` (row_reduce_agrees.rs:113-123; kernel_lift/row_reduce.rs:1-11): Max then an
+    ascending f64 Sum of exp(x - r0), each stage rounded once to f32; the epilogue in f64, rounded on the store."""
+    r0 = f32(max(xs))
+    e = [math.exp(x - r0) for x in xs]
+    acc = 0.0
+    for v in e:
+        acc = acc + v
+    r1 = f32(acc)
+    return [f32(v / r1) for v in e]
+
+
+def serial_rms_norm(xs: list, eps: float = 1.0e-3) -> list:
+    """The serial lift of `rms_norm` (row_reduce_agrees.rs:125-131): an ascending f64 Mean of x * x rounded to
+    f32, then x / sqrt(r0 + 1e-3) in f64, rounded on the store."""
+    acc = 0.0
+    for x in xs:
+        acc = acc + x * x
+    r0 = f32(acc / len(xs))
+    den = math.sqrt(r0 + eps)
+    return [f32(x / den) for x in xs]
+
+
+def golden_row_reduce() -> dict:
+    gentle = [[f32(x) for x in r] for r in row_reduce_gentle()]  # `at(F32, ...)`
+    corpus = [[f32(x) for x in r] for r in row_reduce_corpus()]
+    blocks = [1, 2, 8, 32, 128, 16]  # GEOMETRIES' block sizes (row_reduce_agrees.rs:29)
+    return {
+        "rows": 5, "cols": 96, "blocks": blocks,
+        "gentle_f32_bits": [[f32_bits(x) for x in r] for r in gentle],
+        "corpus_f32_bits": [[f32_bits(x) for x in r] for r in corpus],
+        "centred_f32_bits": {str(b): [[f32_bits(v) for v in centred_documented(r, b)] for r in gentle] for b in blocks},
+        "softmax_serial_f32_bits": [[f32_bits(v) for v in serial_softmax(r)] for r in gentle],
+        "rms_norm_serial_f32_bits": [[f32_bits(v) for v in serial_rms_norm(r)] for r in gentle],
+        "ulp_band": 4,  # transcendental_epilogues_stay_within_a_few_ulps_of_the_serial_lift (:371-392)
+    }
+
+
 def main() -> None:
     out = {
         "float_sum_documented.json": golden_float_sum(),
@@ -394,6 +467,7 @@ def main() -> None:
         "gather_oob.json": golden_gather(),
         "dequant_kat.json": golden_dequant(),
         "scatter.json": golden_scatter(),
+        "row_reduce.json": golden_row_reduce(),
     }
     for name, obj in out.items():
         with open(os.path.join(HERE, name), "w") as f:

@@ -88,6 +88,18 @@ def test_dispatch_table_maps_middle_and_multi_axis_reductions():
             assert k.name == f"up_sm100_reduce3d_{dt.lower()}" and k.scalars[:2] == (OP[op], mask)
 
 
+def test_dispatch_table_maps_row_reduce_forms():
+    b = CudaSm100()
+    for form in ("SOFTMAX", "RMS_NORM", "CENTRED"):
+        for shape in ((64, 96), (3, 4, 96)):
+            k = b.lower(Plan("ROW_REDUCE", [Operand("F32", shape), Operand("F32", shape)], row_reduce_form=form,
+                             block=128, eps=0.25))
+            assert k.name == "up_sm100_row_reduce_f32"
+            assert k.scalars[:2] == (_lib.ROW_REDUCE_FORM[form], 128)
+            assert ctypes.c_int64(k.scalars[2]).value == ctypes.cast(ctypes.pointer(ctypes.c_double(0.25)),
+                                                                      ctypes.POINTER(ctypes.c_int64)).contents.value
+
+
 def _scatter(dtype, index_shape, index_strides, combine="ADD", shape=(9, 4), out_rows=5, **kw):
     return Plan("STRIDED", [Operand(dtype, shape), Operand("I32", index_shape, index_strides),
                             Operand(dtype, (out_rows, shape[1]))], dtype=dtype, write_index=True, combine=combine, **kw)
@@ -153,6 +165,13 @@ def test_dispatch_table_maps_each_lift():
     (_red("ARGMAX", "BF16", "F32"), "InadmissiblePlan"),
     (_red("SUM", "F32", accum="AUTO", block=3), "UnsupportedPlanShape"),
     (Plan("SCAN", [Operand("F32", (8,)), Operand("F32", (8,))], dtype="F32"), "UnsupportedDtype"),
+    (Plan("ROW_REDUCE", [Operand("F32", (4, 8)), Operand("F32", (4, 8))]), "UnsupportedOp"),  # not a named form
+    (Plan("ROW_REDUCE", [Operand("I32", (4, 8)), Operand("I32", (4, 8))], dtype="I32", row_reduce_form="SOFTMAX"),
+     "UnsupportedDtype"),
+    (Plan("ROW_REDUCE", [Operand("F32", (8,)), Operand("F32", (8,))], row_reduce_form="SOFTMAX"),
+     "UnsupportedPlanShape"),  # no leading axis to stride blocks over
+    (Plan("ROW_REDUCE", [Operand("F32", (4, 8)), Operand("F32", (4, 8))], row_reduce_form="SOFTMAX", block=6),
+     "UnsupportedPlanShape"),
     (Plan("SCAN", [Operand("I32", (4, 8)), Operand("I32", (4, 8))], dtype="I32", scan_axis=0), "UnsupportedPlanShape"),
     (Plan("STRIDED", [Operand("F32", (8,)), Operand("F32", (8,))]), "UnsupportedSchedule"),
     (Plan("WINDOW", [Operand("F32", (8,)), Operand("F32", (8,))]), "UnsupportedSchedule"),

@@ -218,3 +218,28 @@ def test_w4a16_oracle_matches_direct_f64_sum():
     assert np.allclose(exact, direct, rtol=1e-14, atol=1e-14)
     assert np.allclose(abs_sum, np.abs(xf) @ np.abs(w * sf).T, rtol=1e-14)
     assert out.tolist() == [[orc.f64_to_bf16(v) for v in row] for row in exact]
+
+
+def _ulps(a, b):
+    """The f32 ulp distance between two arrays (the ordering key of row_reduce_agrees.rs:226-240)."""
+    ka = a.view(np.int32).astype(np.int64)
+    kb = b.view(np.int32).astype(np.int64)
+    ka = np.where(ka < 0, -(1 << 31) - ka, ka)
+    kb = np.where(kb < 0, -(1 << 31) - kb, kb)
+    return int(np.abs(ka - kb).max())
+
+
+def test_row_reduce_oracle_matches_the_reference_written_orders():
+    """The centred quotient in the written order is bit-exact for every block
+    (a_two_stage_op_follows_the_written_order_bit_for_bit); softmax and RMS norm equal the serial lift at block 1
+    and stay within the reference's few-ulp band at every other block."""
+    g = load("row_reduce.json")
+    x = np.array(g["gentle_f32_bits"], np.uint32).view(np.float32)
+    for b in g["blocks"]:
+        want = np.array(g["centred_f32_bits"][str(b)], np.uint32)
+        assert np.array_equal(orc.row_reduce_f32(x, "centred", b).view(np.uint32), want), b
+    for form, key in (("softmax", "softmax_serial_f32_bits"), ("rms_norm", "rms_norm_serial_f32_bits")):
+        want = np.array(g[key], np.uint32).view(np.float32)
+        assert np.array_equal(orc.row_reduce_f32(x, form, 1).view(np.uint32), want.view(np.uint32)), form
+        for b in g["blocks"]:
+            assert _ulps(orc.row_reduce_f32(x, form, b), want) <= g["ulp_band"], (form, b)

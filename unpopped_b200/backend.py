@@ -13,7 +13,7 @@ import ctypes
 import dataclasses
 
 from . import _lib
-from ._lib import COMBINE, EK, KERNEL, LOWER_ERROR, OOB, OP, SCHED, UpLowered, UpPlanDesc, UpTensor
+from ._lib import COMBINE, EK, KERNEL, LOWER_ERROR, OOB, OP, ROW_REDUCE_FORM, SCHED, UpLowered, UpPlanDesc, UpTensor
 
 DTYPE_SUPPORT = {0: "Supported", 1: "Unsupported", 2: "NotExpressible"}
 TARGET = "cuda:sm_100a"
@@ -66,6 +66,8 @@ class Plan:
     scatter_axis: int = 0
     combine: str = "ADD"
     count: bool = False  # bincount
+    row_reduce_form: str = "NONE"  # a RowReduce plan's named form: SOFTMAX, RMS_NORM or CENTRED
+    eps: float = 1e-3
     gather_axis: int = 0
     oob: str = "SKIP"
     index_dtype: str = "I32"
@@ -90,6 +92,8 @@ class Plan:
         p.scatter_axis = self.scatter_axis
         p.combine = COMBINE[self.combine]
         p.count = int(self.count)
+        p.row_reduce_form = ROW_REDUCE_FORM[self.row_reduce_form]
+        p.eps = self.eps
         p.gather_axis = self.gather_axis
         p.oob = OOB[self.oob]
         p.index_dtype = EK[self.index_dtype]

@@ -82,6 +82,7 @@ static const char* k_name(int id) {
     case UP_K_REDUCE2D_I32: return "up_sm100_reduce2d_i32";
     case UP_K_REDUCE_F32: return "up_sm100_reduce3d_f32";
     case UP_K_REDUCE_I32: return "up_sm100_reduce3d_i32";
+    case UP_K_ROW_REDUCE_F32: return "up_sm100_row_reduce_f32";
     case UP_K_SCATTER: return "up_sm100_scatter";
     case UP_K_BINCOUNT: return "up_sm100_bincount";
     default: return "";
@@ -258,6 +259,22 @@ extern "C" int up_sm100_classify(const up_plan_desc* p, up_lowered* out) {
       }
       return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "reductions are lowered for f32, i32 and (Max/ArgMax) bf16");
     }
+    case UP_SCHED_ROW_REDUCE: {
+      // Access::RowReduce: the lowered forms over f32 rows (kernel_lift/row_reduce_launched.rs:47-84)
+      if (p->n_operands < 2) return refuse(out, UP_LOWER_INADMISSIBLE_PLAN, "a row reduction has an input and an output");
+      if (p->dtype != UP_EK_F32) return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "row reductions are lowered for f32");
+      if (p->row_reduce_form < UP_RR_SOFTMAX || p->row_reduce_form > UP_RR_CENTRED)
+        return refuse(out, UP_LOWER_UNSUPPORTED_OP, "the stages and epilogue are softmax, RMS norm or the centred quotient");
+      const up_tensor& in = ops[0];
+      int64_t rows = 0, rstride = 0;
+      if (in.rank < 2 || !last_axis_contiguous(in) || !flat_run(in, 0, in.rank - 1, &rows, &rstride))
+        return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "a launched row reduction strides blocks over a leading axis");
+      const int b = p->block ? p->block : 256;
+      if (b < 1 || b > 1024 || (b & (b - 1))) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "block B");
+      int64_t eps_bits = 0;
+      std::memcpy(&eps_bits, &p->eps, sizeof(eps_bits));
+      return accept(out, UP_K_ROW_REDUCE_F32, {p->row_reduce_form, b, eps_bits});
+    }
     case UP_SCHED_SCAN: {
       if (p->n_operands < 2) return refuse(out, UP_LOWER_INADMISSIBLE_PLAN, "a scan has an input and an output");
       if (p->dtype != UP_EK_I32) return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "scans are lowered for i32");
@@ -407,6 +424,23 @@ extern "C" int up_sm100_launch(int kernel_id, const up_tensor* ins, int n_in, co
                                      (int)sc(2, UP_ACCUM_AUTO), (int)sc(3, 1), (float*)at(y), g.C, stream);
       return up_sm100_reduce3d_i32(reinterpret_cast<const int32_t*>(at(x)), g.A, g.R, g.C, g.sA, g.sR, op,
                                    (int32_t*)at(y), g.C, stream);
+    }
+    case UP_K_ROW_REDUCE_F32: {
+      if (n_in < 1 || n_out < 1) return UP_ERR_INVALID;
+      const up_tensor &x = ins[0], &y = outs[0];
+      if (x.dtype != UP_EK_F32 || y.dtype != UP_EK_F32 || x.rank < 2 || y.rank != x.rank) return UP_ERR_UNSUPPORTED;
+      int64_t rows = 0, xs = 0, yrows = 0, ys = 0;
+      if (!last_axis_contiguous(x) || !last_axis_contiguous(y) || !flat_run(x, 0, x.rank - 1, &rows, &xs) ||
+          !flat_run(y, 0, y.rank - 1, &yrows, &ys))
+        return UP_ERR_UNSUPPORTED;
+      const int64_t cols = x.shape[x.rank - 1];
+      if (yrows != rows || y.shape[y.rank - 1] != cols) return UP_ERR_UNSUPPORTED;
+      if (rows <= 1) xs = ys = cols;  // one row: its stride is never used
+      double eps = 0.0;
+      const int64_t eps_bits = sc(2, 0);
+      std::memcpy(&eps, &eps_bits, sizeof(eps));
+      return up_sm100_row_reduce_f32(reinterpret_cast<const float*>(at(x)), rows, cols, xs, (int)sc(0, 0),
+                                     (int)sc(1, 256), eps, (float*)at(y), ys, stream);
     }
     case UP_K_ROW_MAX_ARGMAX_BF16: {
       if (n_in < 1 || n_out < 2) return UP_ERR_INVALID;

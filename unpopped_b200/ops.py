@@ -101,6 +101,24 @@ def reduce2d(x: torch.Tensor, op: str, axis: int = 1, accum: str = "auto", block
     return out
 
 
+def row_reduce(x: torch.Tensor, form: str, block: int = 256, eps: float = 1e-3,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """A RowReduce form over the rows of a [rows, cols] f32 tensor (contiguous rows): "softmax", "rms_norm"
+    (x / sqrt(mean(x * x) + eps)) or "centred" ((x - mean) / max(x - mean)), for logical block `block`."""
+    _cuda(x, "x")
+    if x.dim() != 2 or x.stride(1) != 1 or x.dtype != torch.float32:
+        raise ValueError("row_reduce takes a 2-D float32 tensor with contiguous rows")
+    if out is None:
+        out = torch.empty_like(x, memory_format=torch.contiguous_format)
+    if out.shape != x.shape or out.stride(1) != 1 or out.dtype != torch.float32:
+        raise ValueError("out has x's shape with contiguous rows")
+    L = _lib.load()
+    check(L.up_sm100_row_reduce_f32(x.data_ptr(), x.shape[0], x.shape[1], x.stride(0),
+                                    _lib.ROW_REDUCE_FORM[form.upper()], block, eps, out.data_ptr(), out.stride(0),
+                                    _stream(x)), "row_reduce_f32")
+    return out
+
+
 def reduce3d(x: torch.Tensor, op: str, accum: str = "auto", block: int = 1,
              out: torch.Tensor | None = None) -> torch.Tensor:
     """Reduction of an [outer, rows, cols] f32 or i32 tensor over its middle axis into [outer, cols]; the rows and
