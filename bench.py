@@ -248,15 +248,33 @@ def bench_lifts(ctx, K, W, hbm, bf16):
     ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xs[i % R], "max", 1, out=out), K, W)
     record("rowmax_f32_8192x8192", wl.rowsum_bytes(), ms, "row_extremum_f32_kernel", R)
     ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xs[i % R], "max", 0, out=out), K, W)
-    record("colmax_f32_8192x8192", wl.rowsum_bytes(), ms, "col_extremum_f32_kernel", R)
+    record("colmax_f32_8192x8192", wl.rowsum_bytes(), ms, "col_extremum_f32_vec_kernel", R)
     ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xs[i % R], "sum", 0, block=256, out=out), K, W)
-    record("colsum_f32_documented_B256", wl.rowsum_bytes(), ms, "col_sum_f32_doc_kernel", R)
+    record("colsum_f32_documented_B256", wl.rowsum_bytes(), ms, "col_sum_f32_doc_vec_kernel", R)
+    # the serial order per column (block 1, the default): bound by the chain of 8192 dependent f64 adds
+    ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xs[i % R], "sum", 0, out=out), K, W)
+    record("colsum_f32_serial", wl.rowsum_bytes(), ms, "col_sum_f32_serial_kernel", R)
+    # its split-K variant (64 row chunks of f64 partials, added in chunk order): the parallel association
+    L = _lib.load()
+    ws = torch.empty(L.up_sm100_col_sum_splitk_workspace_bytes(8192, 8192, 64), dtype=torch.uint8,
+                     device=ctx.dev)
+    ms, _, _ = ctx.timed(lambda i, kin: _lib.check(L.up_sm100_col_sum_f32_splitk(
+        xs[i % R].data_ptr(), 8192, 8192, 8192, 64, 0, ws.data_ptr(), ws.numel(), out.data_ptr(),
+        torch.cuda.current_stream().cuda_stream), "splitk"), K, W)
+    record("colsum_f32_splitk64", wl.rowsum_bytes() + ws.numel() * 2, ms, "splitk_partial_kernel", R)
+    del ws
+    # the RowReduce lift on the same rows (a read and a write of every element)
+    o2 = torch.empty_like(xs[0])
+    for form in ("softmax", "rms_norm"):
+        ms, _, _ = ctx.timed(lambda i, kin: ops.row_reduce(xs[i % R], form, block=256, out=o2), K, W)
+        record(f"row_{form}_f32_B256", 2 * wl.rowsum_bytes(), ms, "row_reduce_f32_held_kernel", R)
+    del o2
     xi = [x.view(torch.int32) for x in xs]  # the same bytes read as i32
     oi = out.view(torch.int32)
     ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xi[i % R], "xor", 1, out=oi), K, W)
     record("rowxor_i32_8192x8192", wl.rowsum_bytes(), ms, "row_fold_i32_kernel", R)
     ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xi[i % R], "sum", 0, out=oi), K, W)
-    record("colsum_i32_8192x8192", wl.rowsum_bytes() + 8192 * 4, ms, "col_fold_i32_kernel", R)
+    record("colsum_i32_8192x8192", wl.rowsum_bytes() + 8192 * 4, ms, "col_fold_i32_vec_kernel", R)
     del xi, oi
     del xs, out
 

@@ -111,7 +111,8 @@ typedef enum up_kernel_id {
   UP_K_BINCOUNT = 10,
   UP_K_REDUCE_F32 = 11,   /* f32 Sum/Mean/Max/Min over one run of adjacent axes of a rank-r input (any class) */
   UP_K_REDUCE_I32 = 12,   /* i32, the seven ops, same geometry */
-  UP_K_ROW_REDUCE_F32 = 13 /* a RowReduce form (softmax, RMS norm, centred quotient) over f32 rows */
+  UP_K_ROW_REDUCE_F32 = 13, /* a RowReduce form (softmax, RMS norm, centred quotient) over f32 rows */
+  UP_K_COL_SUM_SPLITK = 14   /* the split-K variant of the outer-axis f32 Sum/Mean (needs a workspace) */
 } up_kernel_id;
 
 /* A buffer argument: the reference's TypedBuffer / OperandDesc. `base` and `stride` count elements
@@ -154,6 +155,8 @@ typedef struct up_plan_desc {
   /* appended: a RowReduce plan (Access::RowReduce, ir.rs; its stages and epilogue matched to a named form) */
   int32_t row_reduce_form; /* up_row_reduce_form; 0 = not one of the lowered forms */
   double eps;              /* the RMS norm's constant under the square root */
+  /* appended: the runtime selector's choice of the split-K variant (ondevice/README.md:185-218) */
+  int64_t splitk_chunks;   /* > 0: an outer-axis f32 Sum/Mean runs as split-K over this many row chunks */
 } up_plan_desc;
 
 /* What `Backend::lower` returns (`GeneratedKernel{name, source}` + launch metadata), or why it refused
@@ -263,6 +266,17 @@ typedef enum up_row_reduce_form {
  * and RMS norm to a few ulps of its serial lift (kernel_parallel_row_reduce_agrees.rs:371-392). */
 UP_API int up_sm100_row_reduce_f32(const float* x, int64_t rows, int64_t cols, int64_t row_stride, int form,
                                    int block, double eps, float* out, int64_t out_stride, void* stream);
+
+/* The split-K variant of the outer-axis f32 Sum/Mean (crates/unpopped/ondevice/README.md:185-218; the harness
+ * splitk_validate.cu:40-50): chunk c of chunk_rows = ceil(rows / n_chunks) rows is folded ascending into an f64
+ * partial from a 0.0 seed (in the workspace), then the partials are added in chunk order seeded from the first;
+ * Mean divides by rows; one rounding. Deterministic for a fixed n_chunks (the reference's ReassociatedDeterministic
+ * fidelity); n_chunks = 1 is the serial fold of up_sm100_reduce2d_f32 (axis 0, block 1) bit for bit. n_chunks is
+ * clamped to [1, rows]. `workspace` from up_sm100_col_sum_splitk_workspace_bytes, 8-byte aligned. */
+UP_API int up_sm100_col_sum_f32_splitk(const float* x, int64_t rows, int64_t cols, int64_t row_stride,
+                                       int64_t n_chunks, int mean, void* workspace, size_t workspace_bytes,
+                                       float* out, void* stream);
+UP_API size_t up_sm100_col_sum_splitk_workspace_bytes(int64_t rows, int64_t cols, int64_t n_chunks);
 
 /* The same ops over the middle axis of [outer, rows, cols] (rows contiguous; batch b at x + b·outer_stride) into
  * out[outer][cols] (row stride out_stride): `ReduceAxisClass::Middle` (plan/types.rs:150-165), and every reduced

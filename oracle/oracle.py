@@ -45,6 +45,7 @@ def lib():
         L.orc_reduce2d_i32.argtypes = [P, I64, I64, I64, I, I, P, I]
         L.orc_col_sum_f32_documented.argtypes = [P, I64, I64, I64, I64, I, P, I]
         L.orc_row_reduce_f32.argtypes = [P, I64, I64, I64, I, I64, ctypes.c_double, P, I64, I]
+        L.orc_col_sum_f32_splitk.argtypes = [P, I64, I64, I64, I64, I, P, I]
         L.orc_scatter.argtypes = [P, I64, I64, I, P, I, I64, I, P, I64]
         L.orc_bincount.argtypes = [P, I64, I, P, I64]
         L.orc_scan_i32.argtypes = [P, P, I64, I64, I, I, I, ctypes.c_int32, I]
@@ -163,6 +164,16 @@ def bincount(x: np.ndarray, counts: np.ndarray) -> np.ndarray:
     res = np.array(counts, dtype=np.int32, copy=True)
     lib().orc_bincount(_p(xx), xx.size, _INDEX_EK[xx.dtype], _p(res), res.size)
     return res
+
+
+def col_sum_f32_splitk(x: np.ndarray, n_chunks: int, mean: bool = False, threads: int = 1) -> np.ndarray:
+    """The split-K variant of the outer-axis Sum/Mean (ondevice/README.md:185-218): f64 chunk partials added in
+    chunk order."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, cols = x.shape
+    out = np.empty(cols, np.float32)
+    lib().orc_col_sum_f32_splitk(_p(x), rows, cols, cols, n_chunks, int(mean), _p(out), threads)
+    return out
 
 
 ROW_REDUCE_FORMS = {"softmax": 1, "rms_norm": 2, "centred": 3}

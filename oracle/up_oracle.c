@@ -147,6 +147,27 @@ void orc_row_sum_f32_documented(const float* x, int64_t rows, int64_t cols, int6
   }
 }
 
+/* The split-K variant of the outer-axis Sum/Mean (ondevice/README.md:185-218, splitk_validate.cu:40-50): f64
+ * partials over chunks of ceil(rows / n_chunks) rows, each folded ascending from 0.0, added in chunk order from
+ * the first; Mean divides by rows; one rounding. n_chunks clamped to [1, rows]. */
+void orc_col_sum_f32_splitk(const float* x, int64_t rows, int64_t cols, int64_t row_stride, int64_t n_chunks,
+                            int mean, float* out, int threads) {
+  if (n_chunks > rows) n_chunks = rows;
+  if (n_chunks < 1) n_chunks = 1;
+  const int64_t chunk_rows = rows > 0 ? (rows + n_chunks - 1) / n_chunks : 0;
+#pragma omp parallel for num_threads(threads) schedule(static) if (threads > 1)
+  for (int64_t c = 0; c < cols; ++c) {
+    double total = 0.0;
+    for (int64_t k = 0; k < n_chunks; ++k) {
+      double a = 0.0;
+      const int64_t r0 = k * chunk_rows, r1 = r0 + chunk_rows < rows ? r0 + chunk_rows : rows;
+      for (int64_t r = r0; r < r1; ++r) a += (double)x[r * row_stride + c];
+      total = k == 0 ? a : total + a;
+    }
+    out[c] = (float)(mean ? total / (double)rows : total);
+  }
+}
+
 /* RowReduce forms (Access::RowReduce; kernel_lift/row_reduce_launched.rs:1-24, the oracle's eval_row_reduce,
  * oracle/plan_contract.rs:265-360), in the launched lift's written order for a logical block of B threads:
  * form 1 softmax (Max(x); Sum(exp(x - r0)); exp(x - r0) / r1), 2 RMS norm (Mean(x * x); x / sqrt(r0 + eps)),

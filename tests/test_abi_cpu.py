@@ -100,6 +100,20 @@ def test_dispatch_table_maps_row_reduce_forms():
                                                                       ctypes.POINTER(ctypes.c_int64)).contents.value
 
 
+def test_splitk_variant_is_selected_only_for_the_outer_axis_sum():
+    b = CudaSm100()
+    k = b.lower(_red("SUM", "F32", axes_mask=1, accum="AUTO", splitk_chunks=16))
+    assert (k.name, k.scalars) == ("up_sm100_col_sum_f32_splitk", (0, 16))
+    k = b.lower(_red("MEAN", "F32", axes_mask=1, accum="AUTO", splitk_chunks=3))
+    assert (k.name, k.scalars) == ("up_sm100_col_sum_f32_splitk", (1, 3))
+    for plan in (_red("MAX", "F32", axes_mask=1, splitk_chunks=4), _red("SUM", "F32", accum="AUTO", splitk_chunks=4)):
+        with pytest.raises(LowerError) as e:
+            b.lower(plan)
+        assert e.value.variant == "UnsupportedPlanShape"
+    assert _lib.load().up_sm100_col_sum_splitk_workspace_bytes(100, 64, 3) == 3 * 64 * 8
+    assert _lib.load().up_sm100_col_sum_splitk_workspace_bytes(2, 64, 30) == 2 * 64 * 8  # at most one chunk per row
+
+
 def _scatter(dtype, index_shape, index_strides, combine="ADD", shape=(9, 4), out_rows=5, **kw):
     return Plan("STRIDED", [Operand(dtype, shape), Operand("I32", index_shape, index_strides),
                             Operand(dtype, (out_rows, shape[1]))], dtype=dtype, write_index=True, combine=combine, **kw)

@@ -243,3 +243,27 @@ def test_row_reduce_oracle_matches_the_reference_written_orders():
         assert np.array_equal(orc.row_reduce_f32(x, form, 1).view(np.uint32), want.view(np.uint32)), form
         for b in g["blocks"]:
             assert _ulps(orc.row_reduce_f32(x, form, b), want) <= g["ulp_band"], (form, b)
+
+
+def _splitk_harness_corpus():
+    """splitk_validate.cu:53-61: rows 100, cols 64, in[i] = ((i % 37) - 18) * 0.25, column 0 all -0.0."""
+    rows, cols = 100, 64
+    x = np.array([((i % 37) - 18) * 0.25 for i in range(rows * cols)], np.float32).reshape(rows, cols)
+    x[:, 0] = -0.0
+    return x
+
+
+def test_splitk_oracle_meets_the_reference_harness():
+    """The split-K harness's checks (splitk_validate.cu:53-125): ragged chunks against the f64 sum, the zero-seeded
+    fold maps an all -0 column to +0, and n_chunks = 1 is the serial fold bit for bit."""
+    x = _splitk_harness_corpus()
+    exact = x.astype(np.float64).sum(axis=0)
+    got = orc.col_sum_f32_splitk(x, 3)
+    denom = np.maximum(np.abs(exact), 1.0)
+    assert (np.abs(got.astype(np.float64) - exact) / denom).max() < 1e-5
+    assert got.view(np.uint32)[0] == 0x00000000
+    rng = np.random.default_rng(4)
+    y = (rng.standard_normal((333, 40)) * 10.0 ** rng.integers(-3, 4, (333, 1))).astype(np.float32)
+    for mean in (False, True):
+        serial = orc.reduce2d_f32(y, "mean" if mean else "sum", 0)
+        assert np.array_equal(orc.col_sum_f32_splitk(y, 1, mean).view(np.uint32), serial.view(np.uint32))

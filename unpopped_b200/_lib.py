@@ -29,7 +29,7 @@ SCHED = dict(VECTORIZED=0, SCALAR=1, STRIDED=2, REDUCTION=3, ROW_REDUCE=4, CONTR
              KERNEL_FN=100)
 KERNEL = dict(NONE=-1, ROW_SUM_F32=1, ROW_MAX_ARGMAX_BF16=2, SCAN_I32=3, GATHER_ROWS=4, DEQUANT_I4=5,
               W4A16_GEMM=6, REDUCE2D_F32=7, REDUCE2D_I32=8, SCATTER=9, BINCOUNT=10, REDUCE_F32=11, REDUCE_I32=12,
-              ROW_REDUCE_F32=13)
+              ROW_REDUCE_F32=13, COL_SUM_SPLITK=14)
 ROW_REDUCE_FORM = dict(NONE=0, SOFTMAX=1, RMS_NORM=2, CENTRED=3)
 # WriteCombine ordinals (crates/unpopped/src/ir.rs:2723-2732)
 COMBINE = dict(ASSIGN=0, ADD=1, MAX=2, MIN=3)
@@ -54,7 +54,7 @@ class UpPlanDesc(ctypes.Structure):
                 ("index_dtype", ctypes.c_int32), ("n_operands", ctypes.c_int32), ("operands", UpTensor * 8),
                 ("target", ctypes.c_char * 32), ("has_write_index", ctypes.c_int32), ("scatter_axis", ctypes.c_int32),
                 ("combine", ctypes.c_int32), ("count", ctypes.c_int32), ("row_reduce_form", ctypes.c_int32),
-                ("eps", ctypes.c_double)]
+                ("eps", ctypes.c_double), ("splitk_chunks", ctypes.c_int64)]
 
 
 class UpLowered(ctypes.Structure):
@@ -92,6 +92,8 @@ SIGNATURES = {
     "up_sm100_reduce3d_f32": ([_P, _I64, _I64, _I64, _I64, _I64, _I, _I, _I, _P, _I64, _P], _I),
     "up_sm100_reduce3d_i32": ([_P, _I64, _I64, _I64, _I64, _I64, _I, _P, _I64, _P], _I),
     "up_sm100_row_reduce_f32": ([_P, _I64, _I64, _I64, _I, _I, ctypes.c_double, _P, _I64, _P], _I),
+    "up_sm100_col_sum_f32_splitk": ([_P, _I64, _I64, _I64, _I64, _I, _P, ctypes.c_size_t, _P, _P], _I),
+    "up_sm100_col_sum_splitk_workspace_bytes": ([_I64, _I64, _I64], ctypes.c_size_t),
     "up_sm100_scatter": ([_P, _I64, _I64, _I64, _I, _P, _I, _I64, _I, _P, _I64, _I64, _P], _I),
     "up_sm100_bincount": ([_P, _I64, _I, _P, _I64, _P], _I),
     "up_sm100_reduce_i32": ([_P, _I64, _I, _P, _P], _I),

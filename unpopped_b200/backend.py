@@ -68,6 +68,7 @@ class Plan:
     count: bool = False  # bincount
     row_reduce_form: str = "NONE"  # a RowReduce plan's named form: SOFTMAX, RMS_NORM or CENTRED
     eps: float = 1e-3
+    splitk_chunks: int = 0  # > 0: the split-K variant of an outer-axis f32 Sum/Mean
     gather_axis: int = 0
     oob: str = "SKIP"
     index_dtype: str = "I32"
@@ -94,6 +95,7 @@ class Plan:
         p.count = int(self.count)
         p.row_reduce_form = ROW_REDUCE_FORM[self.row_reduce_form]
         p.eps = self.eps
+        p.splitk_chunks = self.splitk_chunks
         p.gather_axis = self.gather_axis
         p.oob = OOB[self.oob]
         p.index_dtype = EK[self.index_dtype]

@@ -83,6 +83,7 @@ static const char* k_name(int id) {
     case UP_K_REDUCE_F32: return "up_sm100_reduce3d_f32";
     case UP_K_REDUCE_I32: return "up_sm100_reduce3d_i32";
     case UP_K_ROW_REDUCE_F32: return "up_sm100_row_reduce_f32";
+    case UP_K_COL_SUM_SPLITK: return "up_sm100_col_sum_f32_splitk";
     case UP_K_SCATTER: return "up_sm100_scatter";
     case UP_K_BINCOUNT: return "up_sm100_bincount";
     default: return "";
@@ -246,6 +247,11 @@ extern "C" int up_sm100_classify(const up_plan_desc* p, up_lowered* out) {
         if (b < 1 || b > 1024 || (b & (b - 1))) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "block B");
         if (summing && axis == 0 && b > 256)
           return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "an outer-axis Sum/Mean takes a block of at most 256");
+        if (p->splitk_chunks > 0) {  // the runtime selector chose the split-K variant
+          if (general || axis != 0 || !summing)
+            return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "split-K is a variant of the outer-axis Sum/Mean");
+          return accept(out, UP_K_COL_SUM_SPLITK, {p->op == UP_OP_MEAN ? 1 : 0, p->splitk_chunks});
+        }
         if (general) return accept(out, UP_K_REDUCE_F32, {p->op, p->axes_mask, p->accum, b});
         if (p->op == UP_OP_SUM && axis == 1) return accept(out, UP_K_ROW_SUM_F32, {p->accum, b});
         return accept(out, UP_K_REDUCE2D_F32, {p->op, axis, p->accum, b});
@@ -359,6 +365,9 @@ extern "C" int up_sm100_workspace_bytes(int kernel_id, const up_tensor* ins, int
     int64_t rows = 1;
     for (int d = 0; d < ins[0].rank - 1; ++d) rows *= ins[0].shape[d];
     *bytes = up_sm100_scan_workspace_bytes(rows, ins[0].shape[ins[0].rank - 1]);
+  } else if (kernel_id == UP_K_COL_SUM_SPLITK) {
+    if (!ins || n_in < 1 || ins[0].rank != 2 || !scalars || n_scalars < 2) return UP_ERR_INVALID;
+    *bytes = up_sm100_col_sum_splitk_workspace_bytes(ins[0].shape[0], ins[0].shape[1], scalars[1]);
   } else if (kernel_id == UP_K_W4A16_GEMM) {
     if (!ins || n_in < 3 || !scalars || n_scalars < 1) return UP_ERR_INVALID;
     *bytes = up_sm100_w4a16_workspace_bytes(ins[2].shape[0], ins[0].shape[0], ins[0].shape[1], scalars[0]);
@@ -424,6 +433,14 @@ extern "C" int up_sm100_launch(int kernel_id, const up_tensor* ins, int n_in, co
                                      (int)sc(2, UP_ACCUM_AUTO), (int)sc(3, 1), (float*)at(y), g.C, stream);
       return up_sm100_reduce3d_i32(reinterpret_cast<const int32_t*>(at(x)), g.A, g.R, g.C, g.sA, g.sR, op,
                                    (int32_t*)at(y), g.C, stream);
+    }
+    case UP_K_COL_SUM_SPLITK: {
+      if (n_in < 1 || n_out < 1) return UP_ERR_INVALID;
+      const up_tensor &x = ins[0], &y = outs[0];
+      if (x.dtype != UP_EK_F32 || y.dtype != UP_EK_F32 || x.rank != 2 || x.stride[1] != 1) return UP_ERR_UNSUPPORTED;
+      if (!dense_row_major(y) || numel(y) != x.shape[1]) return UP_ERR_UNSUPPORTED;
+      return up_sm100_col_sum_f32_splitk(reinterpret_cast<const float*>(at(x)), x.shape[0], x.shape[1], x.stride[0],
+                                         sc(1, 1), (int)sc(0, 0), workspace, workspace_bytes, (float*)at(y), stream);
     }
     case UP_K_ROW_REDUCE_F32: {
       if (n_in < 1 || n_out < 1) return UP_ERR_INVALID;

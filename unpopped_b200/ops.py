@@ -119,6 +119,24 @@ def row_reduce(x: torch.Tensor, form: str, block: int = 256, eps: float = 1e-3,
     return out
 
 
+def col_sum_splitk(x: torch.Tensor, n_chunks: int, mean: bool = False,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """The split-K variant of the outer-axis f32 Sum (Mean) of a [rows, cols] tensor with contiguous rows: f64
+    partials over n_chunks row chunks, added in chunk order. Allocates its workspace."""
+    _cuda(x, "x")
+    if x.dim() != 2 or x.stride(1) != 1 or x.dtype != torch.float32:
+        raise ValueError("col_sum_splitk takes a 2-D float32 tensor with contiguous rows")
+    rows, cols = x.shape
+    if out is None:
+        out = torch.empty(cols, dtype=torch.float32, device=x.device)
+    L = _lib.load()
+    nb = L.up_sm100_col_sum_splitk_workspace_bytes(rows, cols, n_chunks)
+    ws = torch.empty(max(8, nb), dtype=torch.uint8, device=x.device)
+    check(L.up_sm100_col_sum_f32_splitk(x.data_ptr(), rows, cols, x.stride(0), n_chunks, int(mean), ws.data_ptr(),
+                                        ws.numel(), out.data_ptr(), _stream(x)), "col_sum_f32_splitk")
+    return out
+
+
 def reduce3d(x: torch.Tensor, op: str, accum: str = "auto", block: int = 1,
              out: torch.Tensor | None = None) -> torch.Tensor:
     """Reduction of an [outer, rows, cols] f32 or i32 tensor over its middle axis into [outer, cols]; the rows and
