@@ -445,6 +445,18 @@ def profile_cases(which: str):
         o = torch.empty(x.shape[0], device=dev)
         return lambda: ops.reduce2d(x, "max", 1, out=o)
 
+    @case("colmax_f32")
+    def _():
+        x = wl.rowsum_input(device=dev)
+        o = torch.empty(x.shape[1], device=dev)
+        return lambda: ops.reduce2d(x, "max", 0, out=o)
+
+    @case("row_rms_norm")
+    def _():
+        x = wl.rowsum_input(device=dev)
+        o = torch.empty_like(x)
+        return lambda: ops.row_reduce(x, "rms_norm", block=256, out=o)
+
     @case("argmax")
     def _():
         x = wl.argmax_input(rows=8192, device=dev)
@@ -468,7 +480,7 @@ def profile_cases(which: str):
         o = torch.empty(d.m, d.n, dtype=torch.bfloat16, device=dev)
         return lambda: ops.w4a16(d.w_packed, d.scale, d.x, d.group, out=o)
 
-    for name in (cases if which == "all" else [which]):
+    for name in (cases if which == "all" else which.split(",")):
         run = cases[name]()
         for _ in range(3):
             flush.zero_()
@@ -485,7 +497,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--lifts", default="all", choices=["all", "none"])
     ap.add_argument("--profile", default=None,
-                    help="run only the small ncu case of one lift (scan, rowsum, rowsum_auto, rowmax_f32, argmax, gather, dequant, w4a16, all)")
+                    help="run only the small ncu cases of these lifts, comma-separated (scan, rowsum, rowsum_auto, "
+                         "rowmax_f32, colmax_f32, row_rms_norm, argmax, gather, dequant, w4a16, all)")
     args = ap.parse_args()
     if args.profile:
         profile_cases(args.profile)
