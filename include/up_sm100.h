@@ -87,7 +87,7 @@ typedef enum up_accum { UP_ACCUM_AUTO = 0, UP_ACCUM_F32 = 1 } up_accum;
  * (`Backend::lower_kernel`, backend.rs:726-745) for the dequant GEMM. */
 typedef enum up_schedule {
   UP_SCHED_VECTORIZED = 0, UP_SCHED_SCALAR = 1, UP_SCHED_STRIDED = 2, UP_SCHED_REDUCTION = 3,
-  UP_SCHED_ROW_REDUCE = 4, UP_SCHED_CONTRACTION = 5, UP_SCHED_SCAN = 6, UP_SCHED_WINDOW = 7,
+  UP_SCHED_ROW_REDUCE = 4, UP_SCHED_CONTRACTION = 5, UP_SCHED_SCAN = 6, UP_SCHED_WINDOW = 7, UP_SCHED_IM2COL = 8,
   UP_SCHED_KERNEL_FN = 100
 } up_schedule;
 
@@ -112,7 +112,9 @@ typedef enum up_kernel_id {
   UP_K_REDUCE_F32 = 11,   /* f32 Sum/Mean/Max/Min over one run of adjacent axes of a rank-r input (any class) */
   UP_K_REDUCE_I32 = 12,   /* i32, the seven ops, same geometry */
   UP_K_ROW_REDUCE_F32 = 13, /* a RowReduce form (softmax, RMS norm, centred quotient) over f32 rows */
-  UP_K_COL_SUM_SPLITK = 14   /* the split-K variant of the outer-axis f32 Sum/Mean (needs a workspace) */
+  UP_K_COL_SUM_SPLITK = 14,  /* the split-K variant of the outer-axis f32 Sum/Mean (needs a workspace) */
+  UP_K_WINDOW = 15,          /* 1-D window pooling (Sum/Mean/Max/Min) along one axis, f32 or i32 */
+  UP_K_IM2COL = 16           /* the 2-D unfold of an NCHW input, raw bits */
 } up_kernel_id;
 
 /* A buffer argument: the reference's TypedBuffer / OperandDesc. `base` and `stride` count elements
@@ -157,6 +159,11 @@ typedef struct up_plan_desc {
   double eps;              /* the RMS norm's constant under the square root */
   /* appended: the runtime selector's choice of the split-K variant (ondevice/README.md:185-218) */
   int64_t splitk_chunks;   /* > 0: an outer-axis f32 Sum/Mean runs as split-K over this many row chunks */
+  /* appended: Schedule::Window (plan/types.rs; ir.rs:2206-2259) */
+  int32_t window_axis, window_size, window_stride, window_dilation, window_pad_lo, window_pad_hi;
+  int32_t count_include_pad;
+  /* appended: Schedule::Im2Col (ir.rs:2286-2324): (h, w) pairs */
+  int32_t im2col_kernel[2], im2col_stride[2], im2col_pad[2], im2col_dilation[2];
 } up_plan_desc;
 
 /* What `Backend::lower` returns (`GeneratedKernel{name, source}` + launch metadata), or why it refused
@@ -277,6 +284,23 @@ UP_API int up_sm100_col_sum_f32_splitk(const float* x, int64_t rows, int64_t col
                                        int64_t n_chunks, int mean, void* workspace, size_t workspace_bytes,
                                        float* out, void* stream);
 UP_API size_t up_sm100_col_sum_splitk_workspace_bytes(int64_t rows, int64_t cols, int64_t n_chunks);
+
+/* The Window lift (Access::Window, ir.rs:2206-2259) as 1-D pooling along one axis of a dense [outer, k_in, inner]
+ * input into [outer, k_out, inner]: output o folds the taps o·stride − pad_lo + kk·dilation (kk ascending) that
+ * fall inside [0, k_in), as the oracle does (oracle/plan_window.rs:249-475). f32: Sum/Mean in f64 with one rounding
+ * (Mean divides by `size` when count_include_pad, else by the valid taps), Max/Min from the first tap, strictly
+ * better replacing, the last NaN kept (quiet bit set). i32: Sum wrapping, Max, Min. A window with no in-bounds tap
+ * is refused (UP_ERR_UNSUPPORTED), as the reference's plan declines it. */
+UP_API int up_sm100_window(const void* x, int dtype, int64_t outer, int64_t k_in, int64_t inner, int op, int size,
+                           int stride, int dilation, int pad_lo, int count_include_pad, void* out, int64_t k_out,
+                           void* stream);
+
+/* The Im2Col lift (Access::Im2Col, ir.rs:2286-2324; oracle/plan_window.rs:483-535): a dense NCHW input of
+ * elem_bytes-sized elements (1, 2, 4 or 8) into [N, C·kh·kw, oH·oW], oH = (H + 2ph − dh(kh − 1) − 1)/sh + 1 (and the
+ * same for W). Cell (n, c·kh·kw + ki·kw + kj, oh·oW + ow) is a raw-bit copy of input (n, c, oh·sh − ph + ki·dh,
+ * ow·sw − pw + kj·dw), or zero bytes outside the input. */
+UP_API int up_sm100_im2col(const void* x, int elem_bytes, int64_t n, int64_t c, int64_t h, int64_t w, int kh, int kw,
+                           int sh, int sw, int ph, int pw, int dh, int dw, void* out, void* stream);
 
 /* The same ops over the middle axis of [outer, rows, cols] (rows contiguous; batch b at x + b·outer_stride) into
  * out[outer][cols] (row stride out_stride): `ReduceAxisClass::Middle` (plan/types.rs:150-165), and every reduced

@@ -46,6 +46,8 @@ def lib():
         L.orc_col_sum_f32_documented.argtypes = [P, I64, I64, I64, I64, I, P, I]
         L.orc_row_reduce_f32.argtypes = [P, I64, I64, I64, I, I64, ctypes.c_double, P, I64, I]
         L.orc_col_sum_f32_splitk.argtypes = [P, I64, I64, I64, I64, I, P, I]
+        L.orc_window.argtypes = [P, I, I64, I64, I64, I, I64, I64, I64, I64, I, P, I64]
+        L.orc_im2col.argtypes = [P, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, P]
         L.orc_scatter.argtypes = [P, I64, I64, I, P, I, I64, I, P, I64]
         L.orc_bincount.argtypes = [P, I64, I, P, I64]
         L.orc_scan_i32.argtypes = [P, P, I64, I64, I, I, I, ctypes.c_int32, I]
@@ -164,6 +166,41 @@ def bincount(x: np.ndarray, counts: np.ndarray) -> np.ndarray:
     res = np.array(counts, dtype=np.int32, copy=True)
     lib().orc_bincount(_p(xx), xx.size, _INDEX_EK[xx.dtype], _p(res), res.size)
     return res
+
+
+WINDOW_OPS = {"sum": 0, "mean": 1, "max": 2, "min": 3}
+
+
+def window(x: np.ndarray, op: str, size: int, stride: int = 1, dilation: int = 1, pad_lo: int = 0,
+           k_out: int | None = None, count_include_pad: bool = False, axis: int = -1) -> np.ndarray:
+    """Window pooling along `axis` of a float32 or int32 array (oracle/plan_window.rs:249-475); k_out defaults to
+    the symmetric-padding extent."""
+    x = np.ascontiguousarray(x)
+    assert x.dtype in (np.float32, np.int32)
+    axis = axis % x.ndim
+    k_in = x.shape[axis]
+    if k_out is None:
+        k_out = (k_in + 2 * pad_lo - dilation * (size - 1) - 1) // stride + 1
+    shape = list(x.shape)
+    shape[axis] = k_out
+    out = np.empty(shape, x.dtype)
+    outer = int(np.prod(x.shape[:axis], dtype=np.int64))
+    inner = int(np.prod(x.shape[axis + 1:], dtype=np.int64))
+    lib().orc_window(_p(x), 2 if x.dtype == np.float32 else 9, outer, k_in, inner, WINDOW_OPS[op], size, stride,
+                     dilation, pad_lo, int(count_include_pad), _p(out), k_out)
+    return out
+
+
+def im2col(x: np.ndarray, kernel, stride=(1, 1), pad=(0, 0), dilation=(1, 1)) -> np.ndarray:
+    """The 2-D unfold of an NCHW array into [N, C*kh*kw, oH*oW], raw bits (oracle/plan_window.rs:483-535)."""
+    x = np.ascontiguousarray(x)
+    n, c, h, w = x.shape
+    (kh, kw), (sh, sw), (ph, pw), (dh, dw) = kernel, stride, pad, dilation
+    oh = (h + 2 * ph - dh * (kh - 1) - 1) // sh + 1
+    ow = (w + 2 * pw - dw * (kw - 1) - 1) // sw + 1
+    out = np.empty((n, c * kh * kw, oh * ow), x.dtype)
+    lib().orc_im2col(_p(x), x.itemsize, n, c, h, w, kh, kw, sh, sw, ph, pw, dh, dw, _p(out))
+    return out
 
 
 def col_sum_f32_splitk(x: np.ndarray, n_chunks: int, mean: bool = False, threads: int = 1) -> np.ndarray:

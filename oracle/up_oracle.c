@@ -147,6 +147,78 @@ void orc_row_sum_f32_documented(const float* x, int64_t rows, int64_t cols, int6
   }
 }
 
+/* Window pooling (Access::Window; the oracle's eval_window, oracle/plan_window.rs:249-475) along the middle axis of
+ * a dense [outer, k_in, inner] input into [outer, k_out, inner]: output o folds the taps
+ * p = o*stride - pad_lo + kk*dilation (kk ascending) inside [0, k_in). f32 (dtype 2): Sum/Mean in f64, Mean over
+ * `size` or the valid taps, one rounding; Max/Min: take = !have || v is NaN || v better (the result widened and
+ * narrowed back as the oracle's f32 -> f64 -> f32 does: a NaN gets the quiet bit). i32 (dtype 9): Sum wraps, Max and
+ * Min from the first tap. op: 0 Sum, 1 Mean, 2 Max, 3 Min. */
+void orc_window(const void* x, int dtype, int64_t outer, int64_t k_in, int64_t inner, int op, int64_t size,
+                int64_t stride, int64_t dilation, int64_t pad_lo, int include_pad, void* out, int64_t k_out) {
+  for (int64_t b = 0; b < outer; ++b)
+    for (int64_t o = 0; o < k_out; ++o)
+      for (int64_t i = 0; i < inner; ++i) {
+        double acc = 0.0, best = 0.0;
+        uint32_t acc_i = 0;
+        int32_t best_i = 0;
+        int64_t cnt = 0;
+        int have = 0;
+        for (int64_t kk = 0; kk < size; ++kk) {
+          const int64_t p = o * stride - pad_lo + kk * dilation;
+          if (p < 0 || p >= k_in) continue;
+          const int64_t at = (b * k_in + p) * inner + i;
+          if (dtype == 2) {
+            const double v = (double)((const float*)x)[at];
+            if (op <= 1) {
+              acc += v;
+              ++cnt;
+            } else {
+              if (!have || v != v || (op == 2 ? v > best : v < best)) best = v;
+              have = 1;
+            }
+          } else {
+            const int32_t v = ((const int32_t*)x)[at];
+            if (op == 0) {
+              acc_i += (uint32_t)v;
+            } else {
+              if (!have || (op == 2 ? v > best_i : v < best_i)) best_i = v;
+              have = 1;
+            }
+          }
+        }
+        const int64_t dst = (b * k_out + o) * inner + i;
+        if (dtype == 2) {
+          float r;
+          if (op == 0) r = (float)acc;
+          else if (op == 1) r = (float)(acc / (double)(include_pad ? size : cnt));
+          else r = best != best ? bits_f32(f32_bits((float)best) | 0x00400000u) : (float)best;
+          ((float*)out)[dst] = r;
+        } else {
+          ((int32_t*)out)[dst] = op == 0 ? (int32_t)acc_i : best_i;
+        }
+      }
+}
+
+/* Im2Col (the oracle's eval_im2col, oracle/plan_window.rs:483-535): a dense NCHW input of `esz`-byte elements into
+ * [N, C*kh*kw, oH*oW]; a raw-bit copy, zero bytes outside the input. */
+void orc_im2col(const uint8_t* x, int64_t esz, int64_t n, int64_t c, int64_t h, int64_t w, int64_t kh, int64_t kw,
+                int64_t sh, int64_t sw, int64_t ph, int64_t pw, int64_t dh, int64_t dw, uint8_t* out) {
+  const int64_t oh_n = (h + 2 * ph - dh * (kh - 1) - 1) / sh + 1, ow_n = (w + 2 * pw - dw * (kw - 1) - 1) / sw + 1;
+  const int64_t total = n * c * kh * kw * oh_n * ow_n;
+  for (int64_t t = 0; t < total; ++t) {
+    const int64_t col = t % (oh_n * ow_n), row = t / (oh_n * ow_n);
+    const int64_t oh = col / ow_n, ow = col - oh * ow_n;
+    const int64_t patch = row % (c * kh * kw), nn = row / (c * kh * kw);
+    const int64_t cc = patch / (kh * kw), kij = patch - cc * (kh * kw);
+    const int64_t ki = kij / kw, kj = kij - ki * kw;
+    const int64_t ih = oh * sh - ph + ki * dh, iw = ow * sw - pw + kj * dw;
+    if (ih >= 0 && ih < h && iw >= 0 && iw < w)
+      memcpy(out + t * esz, x + (((nn * c + cc) * h + ih) * w + iw) * esz, (size_t)esz);
+    else
+      memset(out + t * esz, 0, (size_t)esz);
+  }
+}
+
 /* The split-K variant of the outer-axis Sum/Mean (ondevice/README.md:185-218, splitk_validate.cu:40-50): f64
  * partials over chunks of ceil(rows / n_chunks) rows, each folded ascending from 0.0, added in chunk order from
  * the first; Mean divides by rows; one rounding. n_chunks clamped to [1, rows]. */

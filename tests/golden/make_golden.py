@@ -459,6 +459,133 @@ def golden_row_reduce() -> dict:
     }
 
 
+# --- crates/unpopped/tests/kernel_window_agrees.rs, kernel_int_window_agrees.rs ------------------------
+
+WINDOW_VALUES = [1.0e8, 1.0, -1.0e8, 0.5, float("nan"), 2.0, -0.0, float("inf"), -3.0, 0.1, 0.25]  # VALUES (:52-64)
+
+
+def window_fold(row: list, op: str, size: int, stride: int, dilation: int, pad: int, include_pad: bool,
+                k_out: int, is_int: bool = False, bits: int = 32) -> list:
+    """The oracle's window fold (oracle/plan_window.rs:320-475): valid taps ascending; f64 Sum/Mean (Mean over size
+    or the valid taps), Max/Min take = !have || NaN || better; integer Sum wraps at the dtype's width."""
+    out = []
+    for o in range(k_out):
+        acc, cnt, have, best = 0, 0, False, 0
+        for kk in range(size):
+            p = o * stride - pad + kk * dilation
+            if p < 0 or p >= len(row):
+                continue
+            v = row[p]
+            if op in ("sum", "mean"):
+                acc = acc + v
+                cnt += 1
+            else:
+                better = (v > best) if op == "max" else (v < best)
+                if not have or (not is_int and v != v) or better:
+                    best = v
+                have = True
+        if op == "sum":
+            out.append(wrap_int(acc, bits) if is_int else acc)
+        elif op == "mean":
+            out.append(acc / (size if include_pad else cnt))
+        else:
+            out.append(best)
+    return out
+
+
+def wrap_int(v: int, bits: int) -> int:
+    v &= (1 << bits) - 1
+    return v - (1 << bits) if v >> (bits - 1) else v
+
+
+def golden_window() -> dict:
+    cases = {  # (rows, k_in, size, stride, dilation, pad, include_pad)
+        "base": (3, 9, 3, 2, 1, 1, False),             # BASE (:45-53)
+        "base_include_pad": (3, 9, 3, 2, 1, 1, True),  # the_two_mean_divisors_agree_and_differ (:140-150)
+        "dilated_strided": (2, 12, 3, 3, 2, 2, False),  # dilation_and_stride_agree (:152-166)
+        "no_padding": (3, 9, 3, 1, 1, 0, False),       # no_padding_agrees (:168-178)
+    }
+    res = {"values_f32_bits": [f32_bits(v) for v in WINDOW_VALUES], "cases": {}}
+    for name, (rows, k_in, size, stride, dil, pad, inc) in cases.items():
+        span = dil * (size - 1) + 1
+        k_out = (k_in + 2 * pad - span) // stride + 1
+        data = [[f32(WINDOW_VALUES[(r * k_in + c) % len(WINDOW_VALUES)]) for c in range(k_in)] for r in range(rows)]
+        res["cases"][name] = {
+            "geometry": [rows, k_in, size, stride, dil, pad, int(inc), k_out],
+            "expected_f32_bits": {op: [[f32_bits(v) for v in window_fold(r, op, size, stride, dil, pad, inc, k_out)]
+                                       for r in data] for op in ("sum", "mean", "max", "min")},
+        }
+    # a_nan_is_kept_by_max_and_min (:180-200) and the_accumulator_is_f64_and_ascending (:202-230, f32 part)
+    nan_row = [1.0, float("nan"), 5.0, 4.0, 3.0, 2.0, 7.0, 6.0, 8.0]
+    res["nan_row_f32_bits"] = [f32_bits(v) for v in nan_row]
+    res["nan_row_expected"] = {op: [f32_bits(v) for v in window_fold(nan_row, op, 3, 3, 1, 0, False, 3)]
+                               for op in ("max", "min")}
+    acc_row = [f32(v) for v in [1.0e16, 1.0, -1.0e16, 1.0, 0.1, 0.2, 0.3, 0.4, 0.5]]
+    res["ascending_row_f32_bits"] = [f32_bits(v) for v in acc_row]
+    res["ascending_sum_f32_bits"] = [f32_bits(v) for v in window_fold(acc_row, "sum", 9, 1, 1, 0, False, 1)]
+    # the integer corpus (kernel_int_window_agrees.rs:52-80): I32 values [hi, 1, -1, 2, hi, 3, lo, -5, -7, -7, 4]
+    ints = [I32_MAX, 1, -1, 2, I32_MAX, 3, I32_MIN, -5, -7, -7, 4]
+    res["int_values"] = ints
+    res["int_cases"] = {}
+    for name, (rows, k_in, size, stride, dil, pad) in {"base": (3, 9, 3, 2, 1, 1), "dilated": (3, 11, 3, 1, 2, 2)}.items():
+        span = dil * (size - 1) + 1
+        k_out = (k_in + 2 * pad - span) // stride + 1
+        data = [[ints[(r * k_in + c) % len(ints)] for c in range(k_in)] for r in range(rows)]
+        res["int_cases"][name] = {
+            "geometry": [rows, k_in, size, stride, dil, pad, 0, k_out],
+            "expected": {op: [window_fold(r, op, size, stride, dil, pad, False, k_out, True) for r in data]
+                         for op in ("sum", "max", "min")},
+        }
+    return res
+
+
+# --- crates/unpopped/tests/kernel_im2col_agrees.rs -----------------------------------------------------
+
+def im2col_value(i: int) -> float:
+    """`value` (kernel_im2col_agrees.rs:70-77): i + 1, with a NaN at 2 and a negative zero at 5."""
+    return float("nan") if i == 2 else (-0.0 if i == 5 else float(i + 1))
+
+
+def im2col_def(x: list, shape, kernel, stride, pad, dilation) -> list:
+    """The Im2Col definition (ir.rs:2286-2324): cell (n, c*kh*kw + ki*kw + kj, oh*oW + ow) copies input
+    (n, c, oh*sh - ph + ki*dh, ow*sw - pw + kj*dw), zero outside."""
+    n, c, h, w = shape
+    (kh, kw), (sh, sw), (ph, pw), (dh, dw) = kernel, stride, pad, dilation
+    oh_n = (h + 2 * ph - dh * (kh - 1) - 1) // sh + 1
+    ow_n = (w + 2 * pw - dw * (kw - 1) - 1) // sw + 1
+    out = []
+    for nn in range(n):
+        for cc in range(c):
+            for ki in range(kh):
+                for kj in range(kw):
+                    for oh in range(oh_n):
+                        for ow in range(ow_n):
+                            ih, iw = oh * sh - ph + ki * dh, ow * sw - pw + kj * dw
+                            ok = 0 <= ih < h and 0 <= iw < w
+                            out.append(x[((nn * c + cc) * h + ih) * w + iw] if ok else 0.0)
+    return out
+
+
+def golden_im2col() -> dict:
+    square = dict(shape=[1, 1, 3, 3], kernel=[3, 3], stride=[1, 1], pad=[1, 1], dilation=[1, 1])  # SQUARE (:123-130)
+    cases = {
+        "padded_3x3": square,
+        "batch_and_channels": dict(square, shape=[2, 3, 4, 4]),           # :142-150
+        "stride_two": dict(square, shape=[1, 2, 5, 5], stride=[2, 2]),      # :152-161
+        "dilation": dict(square, shape=[1, 1, 6, 6], dilation=[2, 2], pad=[2, 2]),  # :163-173
+        "rectangular": dict(shape=[1, 2, 5, 7], kernel=[2, 3], stride=[1, 2], pad=[0, 2], dilation=[2, 1]),  # :175-188
+    }
+    res = {}
+    for name, cs in cases.items():
+        n = 1
+        for d in cs["shape"]:
+            n *= d
+        x = [f32(im2col_value(i)) for i in range(n)]
+        out = im2col_def(x, cs["shape"], cs["kernel"], cs["stride"], cs["pad"], cs["dilation"])
+        res[name] = dict(cs, x_f32_bits=[f32_bits(v) for v in x], expected_f32_bits=[f32_bits(v) for v in out])
+    return res
+
+
 def main() -> None:
     out = {
         "float_sum_documented.json": golden_float_sum(),
@@ -468,6 +595,8 @@ def main() -> None:
         "dequant_kat.json": golden_dequant(),
         "scatter.json": golden_scatter(),
         "row_reduce.json": golden_row_reduce(),
+        "window.json": golden_window(),
+        "im2col.json": golden_im2col(),
     }
     for name, obj in out.items():
         with open(os.path.join(HERE, name), "w") as f:

@@ -114,6 +114,19 @@ def test_splitk_variant_is_selected_only_for_the_outer_axis_sum():
     assert _lib.load().up_sm100_col_sum_splitk_workspace_bytes(2, 64, 30) == 2 * 64 * 8  # at most one chunk per row
 
 
+def test_dispatch_table_maps_window_and_im2col():
+    b = CudaSm100()
+    k = b.lower(Plan("WINDOW", [Operand("F32", (3, 9)), Operand("F32", (3, 5))], op="MEAN", window=(1, 3, 2, 1, 1, 1),
+                     count_include_pad=True))
+    assert (k.name, k.scalars) == ("up_sm100_window", (OP["MEAN"], 3, 2, 1, 1, 1, 1))
+    k = b.lower(Plan("WINDOW", [Operand("I32", (4, 9, 5)), Operand("I32", (4, 3, 5))], dtype="I32", op="MAX",
+                     window=(1, 3, 3, 1, 0, 0)))
+    assert (k.name, k.scalars) == ("up_sm100_window", (OP["MAX"], 3, 3, 1, 0, 0, 1))
+    k = b.lower(Plan("IM2COL", [Operand("BF16", (2, 3, 5, 7)), Operand("BF16", (2, 18, 12))],
+                     im2col=((2, 3), (1, 2), (0, 2), (2, 1))))
+    assert (k.name, k.scalars) == ("up_sm100_im2col", (2, 3, 1, 2, 0, 2, 2, 1))
+
+
 def _scatter(dtype, index_shape, index_strides, combine="ADD", shape=(9, 4), out_rows=5, **kw):
     return Plan("STRIDED", [Operand(dtype, shape), Operand("I32", index_shape, index_strides),
                             Operand(dtype, (out_rows, shape[1]))], dtype=dtype, write_index=True, combine=combine, **kw)
@@ -188,7 +201,11 @@ def test_dispatch_table_maps_each_lift():
      "UnsupportedPlanShape"),
     (Plan("SCAN", [Operand("I32", (4, 8)), Operand("I32", (4, 8))], dtype="I32", scan_axis=0), "UnsupportedPlanShape"),
     (Plan("STRIDED", [Operand("F32", (8,)), Operand("F32", (8,))]), "UnsupportedSchedule"),
-    (Plan("WINDOW", [Operand("F32", (8,)), Operand("F32", (8,))]), "UnsupportedSchedule"),
+    (Plan("WINDOW", [Operand("F32", (8,)), Operand("F32", (8,))], op="PROD"), "UnsupportedOp"),  # Prod refused
+    (Plan("WINDOW", [Operand("I32", (8,)), Operand("I32", (8,))], dtype="I32", op="MEAN"), "UnsupportedOp"),
+    (Plan("WINDOW", [Operand("F64", (8,)), Operand("F64", (8,))], dtype="F64"), "UnsupportedDtype"),
+    (Plan("IM2COL", [Operand("F32", (1, 1, 4, 4)), Operand("F32", (9, 16))]), "UnsupportedPlanShape"),  # rank-2 out
+    (Plan("IM2COL", [Operand("I4", (1, 1, 4, 4)), Operand("I4", (1, 1, 16))]), "UnsupportedDtype"),
     (Plan("CONTRACTION", [Operand("F32", (8, 8)), Operand("F32", (8, 8))]), "UnsupportedSchedule"),
     (Plan("KERNEL_FN", [Operand("F32", (8,))]), "UnsupportedKernel"),
     (_red("SUM", "F32", target="cuda:sm90a"), "UnsupportedSchedule"),

@@ -267,3 +267,36 @@ def test_splitk_oracle_meets_the_reference_harness():
     for mean in (False, True):
         serial = orc.reduce2d_f32(y, "mean" if mean else "sum", 0)
         assert np.array_equal(orc.col_sum_f32_splitk(y, 1, mean).view(np.uint32), serial.view(np.uint32))
+
+
+def test_window_oracle_matches_the_reference_corpora():
+    """kernel_window_agrees.rs and kernel_int_window_agrees.rs: every pool over the padded, strided and dilated
+    geometries, the two Mean divisors, a NaN kept by Max/Min, the ascending f64 accumulator, wrapping integer sums."""
+    g = load("window.json")
+    vals = np.array(g["values_f32_bits"], np.uint32).view(np.float32)
+    for name, c in g["cases"].items():
+        rows, k_in, size, stride, dil, pad, inc, k_out = c["geometry"]
+        x = np.resize(vals, rows * k_in).reshape(rows, k_in)
+        for op, want in c["expected_f32_bits"].items():
+            got = orc.window(x, op, size, stride, dil, pad, k_out, bool(inc))
+            assert np.array_equal(got.view(np.uint32), np.array(want, np.uint32)), (name, op)
+    x = np.array(g["nan_row_f32_bits"], np.uint32).view(np.float32)[None]
+    for op, want in g["nan_row_expected"].items():
+        assert np.array_equal(orc.window(x, op, 3, 3).view(np.uint32)[0], np.array(want, np.uint32)), op
+    x = np.array(g["ascending_row_f32_bits"], np.uint32).view(np.float32)[None]
+    assert orc.window(x, "sum", 9).view(np.uint32)[0].tolist() == g["ascending_sum_f32_bits"]
+    ints = np.array(g["int_values"], np.int64).astype(np.int32)
+    for name, c in g["int_cases"].items():
+        rows, k_in, size, stride, dil, pad, _, k_out = c["geometry"]
+        x = np.resize(ints, rows * k_in).reshape(rows, k_in)
+        for op, want in c["expected"].items():
+            assert orc.window(x, op, size, stride, dil, pad, k_out).tolist() == want, (name, op)
+
+
+def test_im2col_oracle_matches_the_definition():
+    """kernel_im2col_agrees.rs: distinct values with a NaN and a -0 planted, over padding, batch and channels,
+    stride, dilation and a rectangular window."""
+    for name, c in load("im2col.json").items():
+        x = np.array(c["x_f32_bits"], np.uint32).view(np.float32).reshape(c["shape"])
+        got = orc.im2col(x, c["kernel"], c["stride"], c["pad"], c["dilation"])
+        assert got.view(np.uint32).reshape(-1).tolist() == c["expected_f32_bits"], name

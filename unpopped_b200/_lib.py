@@ -25,11 +25,11 @@ EK = dict(F16=0, BF16=1, F32=2, F32_STRICT=3, F64=4, I8=5, I16=6, U8=7, U16=8, I
 OP = dict(SUM=0, MEAN=1, MAX=2, MIN=3, PROD=4, AND=5, OR=6, XOR=7, MAXNUM=8, MINNUM=9, ARGMAX=10, ARGMIN=11)
 OOB = dict(SKIP=0, CLAMP=1, ZERO_FILL=2)
 ACCUM = dict(AUTO=0, F32=1)
-SCHED = dict(VECTORIZED=0, SCALAR=1, STRIDED=2, REDUCTION=3, ROW_REDUCE=4, CONTRACTION=5, SCAN=6, WINDOW=7,
+SCHED = dict(VECTORIZED=0, SCALAR=1, STRIDED=2, REDUCTION=3, ROW_REDUCE=4, CONTRACTION=5, SCAN=6, WINDOW=7, IM2COL=8,
              KERNEL_FN=100)
 KERNEL = dict(NONE=-1, ROW_SUM_F32=1, ROW_MAX_ARGMAX_BF16=2, SCAN_I32=3, GATHER_ROWS=4, DEQUANT_I4=5,
               W4A16_GEMM=6, REDUCE2D_F32=7, REDUCE2D_I32=8, SCATTER=9, BINCOUNT=10, REDUCE_F32=11, REDUCE_I32=12,
-              ROW_REDUCE_F32=13, COL_SUM_SPLITK=14)
+              ROW_REDUCE_F32=13, COL_SUM_SPLITK=14, WINDOW=15, IM2COL=16)
 ROW_REDUCE_FORM = dict(NONE=0, SOFTMAX=1, RMS_NORM=2, CENTRED=3)
 # WriteCombine ordinals (crates/unpopped/src/ir.rs:2723-2732)
 COMBINE = dict(ASSIGN=0, ADD=1, MAX=2, MIN=3)
@@ -54,7 +54,12 @@ class UpPlanDesc(ctypes.Structure):
                 ("index_dtype", ctypes.c_int32), ("n_operands", ctypes.c_int32), ("operands", UpTensor * 8),
                 ("target", ctypes.c_char * 32), ("has_write_index", ctypes.c_int32), ("scatter_axis", ctypes.c_int32),
                 ("combine", ctypes.c_int32), ("count", ctypes.c_int32), ("row_reduce_form", ctypes.c_int32),
-                ("eps", ctypes.c_double), ("splitk_chunks", ctypes.c_int64)]
+                ("eps", ctypes.c_double), ("splitk_chunks", ctypes.c_int64),
+                ("window_axis", ctypes.c_int32), ("window_size", ctypes.c_int32), ("window_stride", ctypes.c_int32),
+                ("window_dilation", ctypes.c_int32), ("window_pad_lo", ctypes.c_int32),
+                ("window_pad_hi", ctypes.c_int32), ("count_include_pad", ctypes.c_int32),
+                ("im2col_kernel", ctypes.c_int32 * 2), ("im2col_stride", ctypes.c_int32 * 2),
+                ("im2col_pad", ctypes.c_int32 * 2), ("im2col_dilation", ctypes.c_int32 * 2)]
 
 
 class UpLowered(ctypes.Structure):
@@ -94,6 +99,8 @@ SIGNATURES = {
     "up_sm100_row_reduce_f32": ([_P, _I64, _I64, _I64, _I, _I, ctypes.c_double, _P, _I64, _P], _I),
     "up_sm100_col_sum_f32_splitk": ([_P, _I64, _I64, _I64, _I64, _I, _P, ctypes.c_size_t, _P, _P], _I),
     "up_sm100_col_sum_splitk_workspace_bytes": ([_I64, _I64, _I64], ctypes.c_size_t),
+    "up_sm100_window": ([_P, _I, _I64, _I64, _I64, _I, _I, _I, _I, _I, _I, _P, _I64, _P], _I),
+    "up_sm100_im2col": ([_P, _I, _I64, _I64, _I64, _I64, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P], _I),
     "up_sm100_scatter": ([_P, _I64, _I64, _I64, _I, _P, _I, _I64, _I, _P, _I64, _I64, _P], _I),
     "up_sm100_bincount": ([_P, _I64, _I, _P, _I64, _P], _I),
     "up_sm100_reduce_i32": ([_P, _I64, _I, _P, _P], _I),

@@ -69,6 +69,9 @@ class Plan:
     row_reduce_form: str = "NONE"  # a RowReduce plan's named form: SOFTMAX, RMS_NORM or CENTRED
     eps: float = 1e-3
     splitk_chunks: int = 0  # > 0: the split-K variant of an outer-axis f32 Sum/Mean
+    window: tuple = (0, 1, 1, 1, 0, 0)  # Schedule::Window: (axis, size, stride, dilation, pad_lo, pad_hi)
+    count_include_pad: bool = False
+    im2col: tuple = ((1, 1), (1, 1), (0, 0), (1, 1))  # Schedule::Im2Col: kernel, stride, pad, dilation (h, w)
     gather_axis: int = 0
     oob: str = "SKIP"
     index_dtype: str = "I32"
@@ -96,6 +99,11 @@ class Plan:
         p.row_reduce_form = ROW_REDUCE_FORM[self.row_reduce_form]
         p.eps = self.eps
         p.splitk_chunks = self.splitk_chunks
+        (p.window_axis, p.window_size, p.window_stride, p.window_dilation, p.window_pad_lo,
+         p.window_pad_hi) = self.window
+        p.count_include_pad = int(self.count_include_pad)
+        for field, pair in zip(("im2col_kernel", "im2col_stride", "im2col_pad", "im2col_dilation"), self.im2col):
+            getattr(p, field)[0], getattr(p, field)[1] = pair
         p.gather_axis = self.gather_axis
         p.oob = OOB[self.oob]
         p.index_dtype = EK[self.index_dtype]

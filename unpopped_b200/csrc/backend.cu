@@ -84,6 +84,8 @@ static const char* k_name(int id) {
     case UP_K_REDUCE_I32: return "up_sm100_reduce3d_i32";
     case UP_K_ROW_REDUCE_F32: return "up_sm100_row_reduce_f32";
     case UP_K_COL_SUM_SPLITK: return "up_sm100_col_sum_f32_splitk";
+    case UP_K_WINDOW: return "up_sm100_window";
+    case UP_K_IM2COL: return "up_sm100_im2col";
     case UP_K_SCATTER: return "up_sm100_scatter";
     case UP_K_BINCOUNT: return "up_sm100_bincount";
     default: return "";
@@ -281,6 +283,37 @@ extern "C" int up_sm100_classify(const up_plan_desc* p, up_lowered* out) {
       std::memcpy(&eps_bits, &p->eps, sizeof(eps_bits));
       return accept(out, UP_K_ROW_REDUCE_F32, {p->row_reduce_form, b, eps_bits});
     }
+    case UP_SCHED_WINDOW: {
+      // Access::Window (ir.rs:2206-2259): 1-D pooling along one axis of a dense input, identity pre/post
+      if (p->n_operands < 2) return refuse(out, UP_LOWER_INADMISSIBLE_PLAN, "a window has an input and an output");
+      if (p->dtype != UP_EK_F32 && p->dtype != UP_EK_I32)
+        return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "windows are lowered for f32 and i32");
+      if (p->op != UP_OP_SUM && p->op != UP_OP_MEAN && p->op != UP_OP_MAX && p->op != UP_OP_MIN)
+        return refuse(out, UP_LOWER_UNSUPPORTED_OP, "window ops: Sum, Mean, Max, Min");
+      if (p->dtype == UP_EK_I32 && p->op == UP_OP_MEAN)
+        return refuse(out, UP_LOWER_UNSUPPORTED_OP, "an integer window Mean is not defined");
+      if (!p->identity_body) return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "pre/post must be the identity");
+      const up_tensor &in = ops[0], &o = ops[1];
+      if (p->window_axis < 0 || p->window_axis >= in.rank || o.rank != in.rank || !dense_row_major(in) ||
+          !dense_row_major(o))
+        return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "a dense input and output, the axis in range");
+      if (p->window_size < 1 || p->window_stride < 1 || p->window_dilation < 1 || p->window_pad_lo < 0)
+        return refuse(out, UP_LOWER_INADMISSIBLE_PLAN, "size, stride, dilation >= 1");
+      return accept(out, UP_K_WINDOW, {p->op, p->window_size, p->window_stride, p->window_dilation, p->window_pad_lo,
+                                       p->count_include_pad, p->window_axis});
+    }
+    case UP_SCHED_IM2COL: {
+      if (p->n_operands < 2) return refuse(out, UP_LOWER_INADMISSIBLE_PLAN, "im2col has an input and an output");
+      const up_tensor &in = ops[0], &o = ops[1];
+      const int bits = elem_bits(in.dtype);
+      if (bits < 8 || (bits != 8 && bits != 16 && bits != 32 && bits != 64))
+        return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "im2col moves elements of 1, 2, 4 or 8 bytes");
+      if (in.rank != 4 || o.rank != 3 || !dense_row_major(in) || !dense_row_major(o) || o.dtype != in.dtype)
+        return refuse(out, UP_LOWER_UNSUPPORTED_PLAN_SHAPE, "a dense NCHW input into a dense [N, C*kh*kw, oH*oW]");
+      return accept(out, UP_K_IM2COL, {p->im2col_kernel[0], p->im2col_kernel[1], p->im2col_stride[0],
+                                       p->im2col_stride[1], p->im2col_pad[0], p->im2col_pad[1],
+                                       p->im2col_dilation[0], p->im2col_dilation[1]});
+    }
     case UP_SCHED_SCAN: {
       if (p->n_operands < 2) return refuse(out, UP_LOWER_INADMISSIBLE_PLAN, "a scan has an input and an output");
       if (p->dtype != UP_EK_I32) return refuse(out, UP_LOWER_UNSUPPORTED_DTYPE, "scans are lowered for i32");
@@ -433,6 +466,40 @@ extern "C" int up_sm100_launch(int kernel_id, const up_tensor* ins, int n_in, co
                                      (int)sc(2, UP_ACCUM_AUTO), (int)sc(3, 1), (float*)at(y), g.C, stream);
       return up_sm100_reduce3d_i32(reinterpret_cast<const int32_t*>(at(x)), g.A, g.R, g.C, g.sA, g.sR, op,
                                    (int32_t*)at(y), g.C, stream);
+    }
+    case UP_K_WINDOW: {
+      if (n_in < 1 || n_out < 1) return UP_ERR_INVALID;
+      const up_tensor &x = ins[0], &y = outs[0];
+      const int axis = (int)sc(6, 0);
+      if (axis < 0 || axis >= x.rank || y.rank != x.rank || !dense_row_major(x) || !dense_row_major(y) ||
+          y.dtype != x.dtype)
+        return UP_ERR_UNSUPPORTED;
+      int64_t outer = 1, inner = 1;
+      for (int d = 0; d < axis; ++d) {
+        if (y.shape[d] != x.shape[d]) return UP_ERR_UNSUPPORTED;
+        outer *= x.shape[d];
+      }
+      for (int d = axis + 1; d < x.rank; ++d) {
+        if (y.shape[d] != x.shape[d]) return UP_ERR_UNSUPPORTED;
+        inner *= x.shape[d];
+      }
+      return up_sm100_window(at(x), x.dtype, outer, x.shape[axis], inner, (int)sc(0, UP_OP_SUM), (int)sc(1, 1),
+                             (int)sc(2, 1), (int)sc(3, 1), (int)sc(4, 0), (int)sc(5, 0), (void*)at(y), y.shape[axis],
+                             stream);
+    }
+    case UP_K_IM2COL: {
+      if (n_in < 1 || n_out < 1) return UP_ERR_INVALID;
+      const up_tensor &x = ins[0], &y = outs[0];
+      if (x.rank != 4 || y.rank != 3 || !dense_row_major(x) || !dense_row_major(y)) return UP_ERR_UNSUPPORTED;
+      const int kh = (int)sc(0, 1), kw = (int)sc(1, 1), sh = (int)sc(2, 1), sw = (int)sc(3, 1);
+      const int ph = (int)sc(4, 0), pw = (int)sc(5, 0), dh = (int)sc(6, 1), dw = (int)sc(7, 1);
+      if (kh < 1 || kw < 1 || sh < 1 || sw < 1 || dh < 1 || dw < 1) return UP_ERR_UNSUPPORTED;
+      const int64_t oh = (x.shape[2] + 2 * (int64_t)ph - (int64_t)dh * (kh - 1) - 1) / sh + 1;
+      const int64_t ow = (x.shape[3] + 2 * (int64_t)pw - (int64_t)dw * (kw - 1) - 1) / sw + 1;
+      if (y.shape[0] != x.shape[0] || y.shape[1] != x.shape[1] * kh * kw || y.shape[2] != oh * ow)
+        return UP_ERR_UNSUPPORTED;
+      return up_sm100_im2col(at(x), elem_bits(x.dtype) / 8, x.shape[0], x.shape[1], x.shape[2], x.shape[3], kh, kw, sh,
+                             sw, ph, pw, dh, dw, (void*)at(y), stream);
     }
     case UP_K_COL_SUM_SPLITK: {
       if (n_in < 1 || n_out < 1) return UP_ERR_INVALID;

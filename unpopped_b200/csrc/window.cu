@@ -1,0 +1,242 @@
+// window.cu — the Window lift (Access::Window, crates/unpopped/src/ir.rs:2206-2259) as 1-D pooling along one axis
+// of a dense [outer, k_in, inner] input into [outer, k_out, inner], and the Im2Col lift (Access::Im2Col,
+// ir.rs:2286-2324), the 2-D unfold of an NCHW input into [N, C·kh·kw, oH·oW].
+//
+// Window, as the oracle evaluates it (oracle/plan_window.rs:249-475): output o folds the taps
+// p = o·stride − pad_lo + kk·dilation, kk = 0 .. size−1 ascending, skipping taps outside [0, k_in):
+//  * f32 Sum/Mean fold in f64 and round once; Mean divides by `size` (count_include_pad) or by the valid taps;
+//  * f32 Max/Min take the first tap, then a strictly better one, and keep the last NaN (its bits with the quiet bit
+//    set, as the f32 -> f64 -> f32 conversions of the oracle leave them);
+//  * i32 Sum wraps at 32 bits; i32 Max/Min are exact. i32 Mean is not defined (the oracle asserts against it).
+// A window with no in-bounds tap is refused before launch (window_taps::check_window_taps; the reference's plan
+// declines it, window_without_real_tap_declines.rs).
+//
+// Im2Col (plan_window.rs:483-535): output cell (n, c·kh·kw + ki·kw + kj, oh·oW + ow) copies the raw bits of
+// input (n, c, oh·sh − ph + ki·dh, ow·sw − pw + kj·dw), or writes zero bytes where that falls outside the input.
+#include "common.cuh"
+
+namespace up {
+namespace win {
+
+constexpr int kThreads = 256;
+
+// One output of a window: the fold of its in-bounds taps (src points at tap position 0 of the output's line;
+// consecutive taps are `step` elements apart).
+template <int OP, bool INCLUDE_PAD>
+__device__ __forceinline__ float window_f32_one(const float* __restrict__ src, int64_t step, int64_t p0, int64_t k_in,
+                                                int size, int dilation) {
+  if (OP == UP_OP_SUM || OP == UP_OP_MEAN) {
+    double acc = 0.0;
+    int cnt = 0;
+    for (int kk = 0; kk < size; ++kk) {
+      const int64_t p = p0 + (int64_t)kk * dilation;
+      if (p < 0 || p >= k_in) continue;
+      acc += (double)__ldg(src + p * step);
+      ++cnt;
+    }
+    if (OP == UP_OP_MEAN) acc = acc / (double)(INCLUDE_PAD ? size : cnt);
+    return __double2float_rn(acc);
+  } else {
+    uint32_t best = 0, nan_bits = 0;
+    bool have = false, nan = false;
+    for (int kk = 0; kk < size; ++kk) {
+      const int64_t p = p0 + (int64_t)kk * dilation;
+      if (p < 0 || p >= k_in) continue;
+      const float v = __ldg(src + p * step);
+      if (v != v) {
+        nan = true;
+        nan_bits = __float_as_uint(v);
+      } else if (!have || (OP == UP_OP_MAX ? v > __uint_as_float(best) : v < __uint_as_float(best))) {
+        best = __float_as_uint(v);
+      }
+      have = have || v == v;
+    }
+    return __uint_as_float(nan ? (nan_bits | 0x00400000u) : best);
+  }
+}
+
+template <int OP>
+__device__ __forceinline__ int32_t window_i32_one(const int32_t* __restrict__ src, int64_t step, int64_t p0,
+                                                  int64_t k_in, int size, int dilation) {
+  uint32_t acc = 0;
+  bool have = false;
+  for (int kk = 0; kk < size; ++kk) {
+    const int64_t p = p0 + (int64_t)kk * dilation;
+    if (p < 0 || p >= k_in) continue;
+    const int32_t v = __ldg(src + p * step);
+    if (OP == UP_OP_SUM) acc += (uint32_t)v;  // wraps at 32 bits
+    else if (!have || (OP == UP_OP_MAX ? v > (int32_t)acc : v < (int32_t)acc)) acc = (uint32_t)v;
+    have = true;
+  }
+  return (int32_t)acc;
+}
+
+// A "line" is one (b, o) pair: `inner` contiguous outputs whose taps are `inner` apart. With inner == 1 a CTA
+// takes a row (b) and its threads the outputs o; with inner > 1 a CTA takes lines and its threads the inner index.
+// No per-element division.
+template <typename T, typename F>
+__device__ __forceinline__ void window_walk(const T* __restrict__ x, int64_t outer, int64_t k_in, int64_t inner,
+                                            int64_t k_out, int stride, int pad_lo, T* __restrict__ out, F one) {
+  if (inner == 1) {
+    for (int64_t b = blockIdx.x; b < outer; b += gridDim.x) {
+      const T* row = x + b * k_in;
+      T* orow = out + b * k_out;
+      for (int64_t o = threadIdx.x; o < k_out; o += kThreads) orow[o] = one(row, 1, o * stride - pad_lo);
+    }
+  } else {
+    // lines narrower than the CTA share it: lp lines per step, thread t on line t / inner, index t % inner
+    const int64_t lines = outer * k_out;
+    const int lp = inner < kThreads ? kThreads / (int)inner : 1;
+    const int sub = inner < kThreads ? (int)threadIdx.x / (int)inner : 0;
+    const int64_t i0 = inner < kThreads ? (int64_t)threadIdx.x - (int64_t)sub * inner : threadIdx.x;
+    if (sub >= lp) return;  // the threads past lp whole lines
+    for (int64_t line = (int64_t)blockIdx.x * lp + sub; line < lines; line += (int64_t)gridDim.x * lp) {
+      const int64_t b = line / k_out, o = line - b * k_out;
+      const T* base = x + b * k_in * inner;
+      T* orow = out + line * inner;
+      for (int64_t i = i0; i < inner; i += kThreads) orow[i] = one(base + i, inner, o * stride - pad_lo);
+    }
+  }
+}
+
+template <int OP, bool INCLUDE_PAD>
+__global__ void __launch_bounds__(kThreads) window_f32_kernel(const float* __restrict__ x, int64_t outer, int64_t k_in,
+                                                               int64_t inner, int64_t k_out, int size, int stride,
+                                                               int dilation, int pad_lo, float* __restrict__ out) {
+  window_walk<float>(x, outer, k_in, inner, k_out, stride, pad_lo, out, [&](const float* src, int64_t step, int64_t p0) {
+    return window_f32_one<OP, INCLUDE_PAD>(src, step, p0, k_in, size, dilation);
+  });
+}
+
+template <int OP>
+__global__ void __launch_bounds__(kThreads) window_i32_kernel(const int32_t* __restrict__ x, int64_t outer,
+                                                               int64_t k_in, int64_t inner, int64_t k_out, int size,
+                                                               int stride, int dilation, int pad_lo,
+                                                               int32_t* __restrict__ out) {
+  window_walk<int32_t>(x, outer, k_in, inner, k_out, stride, pad_lo, out,
+                       [&](const int32_t* src, int64_t step, int64_t p0) {
+                         return window_i32_one<OP>(src, step, p0, k_in, size, dilation);
+                       });
+}
+
+// A CTA per output row (n, c, ki, kj), decoded once; its threads walk the row's oH·oW cells with 32-bit
+// arithmetic (the row length fits: oH·oW < 2^31 is checked on the host).
+template <typename T>
+__global__ void __launch_bounds__(kThreads) im2col_kernel(const T* __restrict__ x, int64_t n, int64_t c, int64_t h,
+                                                           int64_t w, int kh, int kw, int sh, int sw, int ph, int pw,
+                                                           int dh, int dw, int64_t oh_n, int64_t ow_n,
+                                                           T* __restrict__ out) {
+  const int cols = (int)(oh_n * ow_n), own = (int)ow_n;
+  const int64_t rows = n * c * kh * kw;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const int64_t patch = row % (c * kh * kw), nn = row / (c * kh * kw);
+    const int64_t cc = patch / (kh * kw);
+    const int kij = (int)(patch - cc * (kh * kw));
+    const int ki = kij / kw, kj = kij - ki * kw;
+    const T* plane = x + (nn * c + cc) * h * w;
+    T* orow = out + row * cols;
+    const int ih0 = ki * dh - ph, iw0 = kj * dw - pw;
+    for (int col = threadIdx.x; col < cols; col += kThreads) {
+      const int oh = col / own, ow = col - oh * own;
+      const int ih = oh * sh + ih0, iw = ow * sw + iw0;
+      T v{};
+      if (ih >= 0 && ih < h && iw >= 0 && iw < w) v = __ldg(plane + (int64_t)ih * w + iw);
+      orow[col] = v;
+    }
+  }
+}
+
+inline int grid_for(int64_t units) {  // one unit (a row or a line) per CTA at a time, up to 16 CTAs per SM
+  const int64_t cap = (int64_t)sm_count() * 16;
+  return (int)(units < cap ? (units > 0 ? units : 1) : cap);
+}
+
+}  // namespace win
+}  // namespace up
+
+using namespace up;
+
+// True when every output window holds an in-bounds tap (window_taps::check_window_taps).
+static bool every_window_has_a_tap(int64_t k_in, int64_t k_out, int size, int stride, int dilation, int pad_lo) {
+  for (int64_t o = 0; o < k_out; ++o) {
+    const int64_t p0 = o * stride - pad_lo;
+    int64_t kk = p0 >= 0 ? 0 : (-p0 + dilation - 1) / dilation;  // the first tap at or after 0
+    if (kk >= size || p0 + kk * dilation >= k_in) return false;
+  }
+  return true;
+}
+
+extern "C" int up_sm100_window(const void* x, int dtype, int64_t outer, int64_t k_in, int64_t inner, int op, int size,
+                               int stride, int dilation, int pad_lo, int count_include_pad, void* out, int64_t k_out,
+                               void* stream) {
+  UP_CHECK_ARG(outer >= 0 && k_in >= 0 && inner >= 0 && k_out >= 0);
+  if (size < 1 || stride < 1 || dilation < 1 || pad_lo < 0)
+    return fail_with(UP_ERR_UNSUPPORTED, "window: size, stride and dilation >= 1, pad >= 0");
+  if (dtype != UP_EK_F32 && dtype != UP_EK_I32) return fail_with(UP_ERR_UNSUPPORTED, "window: f32 or i32");
+  if (op != UP_OP_SUM && op != UP_OP_MEAN && op != UP_OP_MAX && op != UP_OP_MIN)
+    return fail_with(UP_ERR_UNSUPPORTED, "window: Sum, Mean, Max or Min (Prod is refused)");
+  if (dtype == UP_EK_I32 && op == UP_OP_MEAN) return fail_with(UP_ERR_UNSUPPORTED, "window: an integer Mean");
+  const int64_t total = outer * k_out * inner;
+  if (total == 0) return UP_OK;
+  if (!every_window_has_a_tap(k_in, k_out, size, stride, dilation, pad_lo))
+    return fail_with(UP_ERR_UNSUPPORTED, "window: a window with no in-bounds tap");
+  UP_CHECK_ARG(x != nullptr && out != nullptr);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t lp = inner > 1 && inner < win::kThreads ? win::kThreads / inner : 1;
+  const int g = win::grid_for(inner == 1 ? outer : (outer * k_out + lp - 1) / lp);
+  if (dtype == UP_EK_F32) {
+    const float* xf = static_cast<const float*>(x);
+    float* of = static_cast<float*>(out);
+#define UP_WIN_F32(OP, INC) \
+  win::window_f32_kernel<OP, INC><<<g, win::kThreads, 0, s>>>(xf, outer, k_in, inner, k_out, size, stride, dilation, pad_lo, of)
+    switch (op) {
+      case UP_OP_SUM: UP_WIN_F32(UP_OP_SUM, false); break;
+      case UP_OP_MEAN:
+        if (count_include_pad) UP_WIN_F32(UP_OP_MEAN, true);
+        else UP_WIN_F32(UP_OP_MEAN, false);
+        break;
+      case UP_OP_MAX: UP_WIN_F32(UP_OP_MAX, false); break;
+      default: UP_WIN_F32(UP_OP_MIN, false); break;
+    }
+#undef UP_WIN_F32
+  } else {
+    const int32_t* xi = static_cast<const int32_t*>(x);
+    int32_t* oi = static_cast<int32_t*>(out);
+    if (op == UP_OP_SUM)
+      win::window_i32_kernel<UP_OP_SUM><<<g, win::kThreads, 0, s>>>(xi, outer, k_in, inner, k_out, size, stride, dilation, pad_lo, oi);
+    else if (op == UP_OP_MAX)
+      win::window_i32_kernel<UP_OP_MAX><<<g, win::kThreads, 0, s>>>(xi, outer, k_in, inner, k_out, size, stride, dilation, pad_lo, oi);
+    else
+      win::window_i32_kernel<UP_OP_MIN><<<g, win::kThreads, 0, s>>>(xi, outer, k_in, inner, k_out, size, stride, dilation, pad_lo, oi);
+  }
+  note_launch();
+  return check_launch();
+}
+
+extern "C" int up_sm100_im2col(const void* x, int elem_bytes, int64_t n, int64_t c, int64_t h, int64_t w, int kh,
+                               int kw, int sh, int sw, int ph, int pw, int dh, int dw, void* out, void* stream) {
+  UP_CHECK_ARG(n >= 0 && c >= 0 && h >= 0 && w >= 0);
+  if (kh < 1 || kw < 1 || sh < 1 || sw < 1 || dh < 1 || dw < 1 || ph < 0 || pw < 0)
+    return fail_with(UP_ERR_UNSUPPORTED, "im2col: kernel, stride and dilation >= 1, pad >= 0");
+  if (elem_bytes != 1 && elem_bytes != 2 && elem_bytes != 4 && elem_bytes != 8) return UP_ERR_UNSUPPORTED;
+  const int64_t oh = (h + 2 * (int64_t)ph - (int64_t)dh * (kh - 1) - 1) / sh + 1;
+  const int64_t ow = (w + 2 * (int64_t)pw - (int64_t)dw * (kw - 1) - 1) / sw + 1;
+  if (oh <= 0 || ow <= 0) return fail_with(UP_ERR_UNSUPPORTED, "im2col: the window is larger than the padded input");
+  const int64_t total = n * c * kh * kw * oh * ow;
+  if (total == 0) return UP_OK;
+  if (oh * ow > 0x7fffffffLL || h > 0x7fffffffLL || w > 0x7fffffffLL) return UP_ERR_UNSUPPORTED;
+  UP_CHECK_ARG(x != nullptr && out != nullptr);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int g = win::grid_for(n * c * kh * kw);
+#define UP_I2C(T) \
+  win::im2col_kernel<T><<<g, win::kThreads, 0, s>>>(static_cast<const T*>(x), n, c, h, w, kh, kw, sh, sw, ph, pw, dh, dw, oh, ow, static_cast<T*>(out))
+  switch (elem_bytes) {
+    case 1: UP_I2C(uint8_t); break;
+    case 2: UP_I2C(uint16_t); break;
+    case 4: UP_I2C(uint32_t); break;
+    default: UP_I2C(unsigned long long); break;
+  }
+#undef UP_I2C
+  note_launch();
+  return check_launch();
+}

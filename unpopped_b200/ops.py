@@ -137,6 +137,49 @@ def col_sum_splitk(x: torch.Tensor, n_chunks: int, mean: bool = False,
     return out
 
 
+def window(x: torch.Tensor, op: str, size: int, stride: int = 1, dilation: int = 1, pad_lo: int = 0,
+           pad_hi: int | None = None, count_include_pad: bool = False, axis: int = -1,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """1-D window pooling (sum, mean, max, min) of a dense f32 or i32 tensor along `axis`; the output extent is
+    (k_in + pad_lo + pad_hi - dilation*(size-1) - 1) // stride + 1 (pad_hi defaults to pad_lo)."""
+    _cuda(x, "x")
+    if not x.is_contiguous() or x.dtype not in (torch.float32, torch.int32):
+        raise ValueError("window takes a contiguous float32 or int32 tensor")
+    axis = axis % x.dim()
+    k_in = x.shape[axis]
+    ph = pad_lo if pad_hi is None else pad_hi
+    k_out = (k_in + pad_lo + ph - dilation * (size - 1) - 1) // stride + 1
+    shape = list(x.shape)
+    shape[axis] = max(k_out, 0)
+    if out is None:
+        out = torch.empty(shape, dtype=x.dtype, device=x.device)
+    outer = int(np.prod(x.shape[:axis], dtype=np.int64))
+    inner = int(np.prod(x.shape[axis + 1:], dtype=np.int64))
+    L = _lib.load()
+    check(L.up_sm100_window(x.data_ptr(), EK["F32"] if x.dtype == torch.float32 else EK["I32"], outer, k_in, inner,
+                            OP[op.upper()], size, stride, dilation, pad_lo, int(count_include_pad), out.data_ptr(),
+                            shape[axis], _stream(x)), "window")
+    return out
+
+
+def im2col(x: torch.Tensor, kernel: tuple, stride: tuple = (1, 1), pad: tuple = (0, 0), dilation: tuple = (1, 1),
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """The 2-D unfold of a contiguous NCHW tensor into [N, C*kh*kw, oH*oW], raw bits, zeros outside the input."""
+    _cuda(x, "x")
+    if x.dim() != 4 or not x.is_contiguous():
+        raise ValueError("im2col takes a contiguous NCHW tensor")
+    n, c, h, w = x.shape
+    (kh, kw), (sh, sw), (ph, pw), (dh, dw) = kernel, stride, pad, dilation
+    oh = (h + 2 * ph - dh * (kh - 1) - 1) // sh + 1
+    ow = (w + 2 * pw - dw * (kw - 1) - 1) // sw + 1
+    if out is None:
+        out = torch.empty((n, c * kh * kw, max(oh, 0) * max(ow, 0)), dtype=x.dtype, device=x.device)
+    L = _lib.load()
+    check(L.up_sm100_im2col(x.data_ptr(), x.element_size(), n, c, h, w, kh, kw, sh, sw, ph, pw, dh, dw,
+                            out.data_ptr(), _stream(x)), "im2col")
+    return out
+
+
 def reduce3d(x: torch.Tensor, op: str, accum: str = "auto", block: int = 1,
              out: torch.Tensor | None = None) -> torch.Tensor:
     """Reduction of an [outer, rows, cols] f32 or i32 tensor over its middle axis into [outer, cols]; the rows and
