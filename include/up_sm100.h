@@ -302,6 +302,16 @@ UP_API int up_sm100_window(const void* x, int dtype, int64_t outer, int64_t k_in
 UP_API int up_sm100_im2col(const void* x, int elem_bytes, int64_t n, int64_t c, int64_t h, int64_t w, int kh, int kw,
                            int sh, int sw, int ph, int pw, int dh, int dw, void* out, void* stream);
 
+/* Interface artifacts. The `KernelInterface` (crates/unpopped/src/kernel_interface.rs:196-230) of a kernel id as
+ * JSON: the entry symbol, the parameters (role, element kind, rank) in the generic launch's operand order and then
+ * its scalars, the launch geometry and dynamic shared memory, launch bounds, the cooperative flag, the capabilities
+ * the code requires, fidelity notes, the workspace it needs, and its revision hash. A NULL `buf` reports the length
+ * (without the terminating NUL) in `len`; UP_ERR_INVALID when `cap` is too small. */
+UP_API int up_sm100_kernel_interface(int kernel_id, char* buf, size_t cap, size_t* len);
+/* A kernel's source revision: FNV-1a 64 over its source file (`GeneratedKernel::revision_hash`, backend.rs:173-175,
+ * revision.rs), the third field of its link-registry row (link.rs:27-42). 0 for an unknown id. */
+UP_API uint64_t up_sm100_revision_hash(int kernel_id);
+
 /* The same ops over the middle axis of [outer, rows, cols] (rows contiguous; batch b at x + b·outer_stride) into
  * out[outer][cols] (row stride out_stride): `ReduceAxisClass::Middle` (plan/types.rs:150-165), and every reduced
  * set that flattens to one run of adjacent axes, which the oracle folds in row-major order over the reduced

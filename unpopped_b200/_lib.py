@@ -99,6 +99,8 @@ SIGNATURES = {
     "up_sm100_row_reduce_f32": ([_P, _I64, _I64, _I64, _I, _I, ctypes.c_double, _P, _I64, _P], _I),
     "up_sm100_col_sum_f32_splitk": ([_P, _I64, _I64, _I64, _I64, _I, _P, ctypes.c_size_t, _P, _P], _I),
     "up_sm100_col_sum_splitk_workspace_bytes": ([_I64, _I64, _I64], ctypes.c_size_t),
+    "up_sm100_kernel_interface": ([_I, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)], _I),
+    "up_sm100_revision_hash": ([_I], ctypes.c_uint64),
     "up_sm100_window": ([_P, _I, _I64, _I64, _I64, _I, _I, _I, _I, _I, _I, _P, _I64, _P], _I),
     "up_sm100_im2col": ([_P, _I, _I64, _I64, _I64, _I64, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P], _I),
     "up_sm100_scatter": ([_P, _I64, _I64, _I64, _I, _P, _I, _I64, _I, _P, _I64, _I64, _P], _I),

@@ -45,10 +45,20 @@ def _stale(target: str, deps) -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
+def revision_hash(path: str) -> int:
+    """FNV-1a 64 over a source file's bytes: the reference's revision hash (crates/unpopped/src/revision.rs)."""
+    h = 0xCBF29CE484222325
+    with open(path, "rb") as f:
+        for b in f.read():
+            h = ((h ^ b) * 0x100000001B3) & 0xFFFFFFFFFFFFFFFF
+    return h
+
+
 def _compile(src: str, extra) -> str:
     obj = os.path.join(OBJ, os.path.basename(src) + ".o")
     if _stale(obj, [src] + _headers()):
-        cmd = [nvcc()] + NVCC_FLAGS + list(extra) + ["-c", src, "-o", obj]
+        rev = f"-DUP_SOURCE_REVISION=0x{revision_hash(src):016x}ull"
+        cmd = [nvcc()] + NVCC_FLAGS + [rev] + list(extra) + ["-c", src, "-o", obj]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed on {os.path.basename(src)}:\n{r.stdout}\n{r.stderr}")

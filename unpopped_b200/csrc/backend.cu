@@ -601,3 +601,5 @@ extern "C" int up_sm100_launch(int kernel_id, const up_tensor* ins, int n_in, co
       return UP_ERR_UNSUPPORTED;
   }
 }
+
+UP_DEFINE_REVISION(backend)

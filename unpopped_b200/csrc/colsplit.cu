@@ -126,3 +126,5 @@ extern "C" int up_sm100_col_sum_f32_splitk(const float* x, int64_t rows, int64_t
   note_launch();
   return check_launch();
 }
+
+UP_DEFINE_REVISION(colsplit)

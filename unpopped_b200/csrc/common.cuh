@@ -71,6 +71,16 @@ __device__ __forceinline__ float4 ld_nc_na_f4(const float* p) {
 
 }  // namespace up
 
+// The source revision of a translation unit: FNV-1a 64 over its .cu file's text, the reference's revision hash
+// (crates/unpopped/src/revision.rs), passed in by the build as UP_SOURCE_REVISION.
+#ifndef UP_SOURCE_REVISION
+#define UP_SOURCE_REVISION 0ull
+#endif
+#define UP_DEFINE_REVISION(name) \
+  namespace up {                 \
+  uint64_t revision_##name() { return UP_SOURCE_REVISION; } \
+  }
+
 #define UP_CHECK_ARG(cond)         \
   do {                             \
     if (!(cond)) return UP_ERR_INVALID; \

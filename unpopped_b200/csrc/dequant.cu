@@ -143,3 +143,5 @@ extern "C" int up_sm100_dequant_i4_bf16(const uint8_t* w, const uint16_t* scale,
   note_launch();
   return check_launch();
 }
+
+UP_DEFINE_REVISION(dequant)

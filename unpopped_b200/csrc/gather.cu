@@ -115,3 +115,5 @@ extern "C" int up_sm100_gather_rows(const void* table, int64_t table_rows, int64
   note_launch();
   return check_launch();
 }
+
+UP_DEFINE_REVISION(gather)

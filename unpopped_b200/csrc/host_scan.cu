@@ -172,3 +172,5 @@ extern "C" int up_sm100_scan_i32_host(const int32_t* x, int32_t* y, int64_t rows
   if (status != UP_OK) return status;
   return up_sm100_workspace_status(st.ws, st.comp);  // a bounded device wait that ran out, if any
 }
+
+UP_DEFINE_REVISION(host_scan)

@@ -437,3 +437,5 @@ extern "C" int up_sm100_reduce_i32(const int32_t* x, int64_t n, int op, int32_t*
   }
   return check_launch();
 }
+
+UP_DEFINE_REVISION(reduce)

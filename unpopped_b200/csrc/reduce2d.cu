@@ -1011,3 +1011,5 @@ extern "C" int up_sm100_reduce3d_f32(const float* x, int64_t outer, int64_t rows
   return launch_f32_cols(x, outer, rows, cols, outer_stride, row_stride, op, accum, block, out, out_stride,
                          static_cast<cudaStream_t>(stream));
 }
+
+UP_DEFINE_REVISION(reduce2d)

@@ -436,3 +436,5 @@ extern "C" int up_sm100_row_reduce_f32(const float* x, int64_t rows, int64_t col
     default: return rr::launch<rr::kFormCentred>(x, rows, cols, row_stride, block, eps, out, out_stride, s);
   }
 }
+
+UP_DEFINE_REVISION(rowreduce)

@@ -873,3 +873,9 @@ extern "C" int up_sm100_scan_i32_noalloc(const int32_t* x, int32_t* y, int64_t r
   if (st != UP_OK || !sync) return st;
   return up_sm100_workspace_status(scratch, stream);
 }
+
+namespace up {
+size_t scan_persist_smem_bytes() { return kQSmem; }  // for the kernel interface
+}  // namespace up
+
+UP_DEFINE_REVISION(scan)

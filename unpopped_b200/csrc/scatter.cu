@@ -177,3 +177,5 @@ extern "C" int up_sm100_bincount(const void* x, int64_t n, int index_dtype, int3
   note_launch();
   return check_launch();
 }
+
+UP_DEFINE_REVISION(scatter)

@@ -763,3 +763,9 @@ extern "C" int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, cons
   note_launch();
   return check_launch();
 }
+
+namespace up {
+size_t w4a16_smem_bytes() { return w4::kSmemBytes; }  // for the kernel interface
+}  // namespace up
+
+UP_DEFINE_REVISION(w4a16)

@@ -240,3 +240,5 @@ extern "C" int up_sm100_im2col(const void* x, int elem_bytes, int64_t n, int64_t
   note_launch();
   return check_launch();
 }
+
+UP_DEFINE_REVISION(window)
