@@ -15,6 +15,8 @@
 // input (n, c, oh·sh − ph + ki·dh, ow·sw − pw + kj·dw), or writes zero bytes where that falls outside the input.
 #include "common.cuh"
 
+#include <mutex>
+
 namespace up {
 namespace win {
 
@@ -31,7 +33,7 @@ __device__ __forceinline__ float window_f32_one(const float* __restrict__ src, i
     for (int kk = 0; kk < size; ++kk) {
       const int64_t p = p0 + (int64_t)kk * dilation;
       if (p < 0 || p >= k_in) continue;
-      acc += (double)__ldg(src + p * step);
+      acc += (double)src[p * step];
       ++cnt;
     }
     if (OP == UP_OP_MEAN) acc = acc / (double)(INCLUDE_PAD ? size : cnt);
@@ -42,7 +44,7 @@ __device__ __forceinline__ float window_f32_one(const float* __restrict__ src, i
     for (int kk = 0; kk < size; ++kk) {
       const int64_t p = p0 + (int64_t)kk * dilation;
       if (p < 0 || p >= k_in) continue;
-      const float v = __ldg(src + p * step);
+      const float v = src[p * step];
       if (v != v) {
         nan = true;
         nan_bits = __float_as_uint(v);
@@ -63,7 +65,7 @@ __device__ __forceinline__ int32_t window_i32_one(const int32_t* __restrict__ sr
   for (int kk = 0; kk < size; ++kk) {
     const int64_t p = p0 + (int64_t)kk * dilation;
     if (p < 0 || p >= k_in) continue;
-    const int32_t v = __ldg(src + p * step);
+    const int32_t v = src[p * step];
     if (OP == UP_OP_SUM) acc += (uint32_t)v;  // wraps at 32 bits
     else if (!have || (OP == UP_OP_MAX ? v > (int32_t)acc : v < (int32_t)acc)) acc = (uint32_t)v;
     have = true;
@@ -97,6 +99,71 @@ __device__ __forceinline__ void window_walk(const T* __restrict__ x, int64_t out
       for (int64_t i = i0; i < inner; i += kThreads) orow[i] = one(base + i, inner, o * stride - pad_lo);
     }
   }
+}
+
+// The same fold over a row staged in shared memory, with 32-bit positions; an interior window (every tap inside the
+// row) skips the bounds checks.
+template <int OP, bool INCLUDE_PAD>
+__device__ __forceinline__ float window_f32_row(const float* __restrict__ row, int p0, int k_in, int size,
+                                                int dilation) {
+  const bool interior = p0 >= 0 && p0 + (size - 1) * dilation < k_in;
+  if (OP == UP_OP_SUM || OP == UP_OP_MEAN) {
+    double acc = 0.0;
+    int cnt = 0;
+    if (interior) {
+      for (int kk = 0, p = p0; kk < size; ++kk, p += dilation) acc += (double)row[p];
+      cnt = size;
+    } else {
+      for (int kk = 0, p = p0; kk < size; ++kk, p += dilation)
+        if (p >= 0 && p < k_in) {
+          acc += (double)row[p];
+          ++cnt;
+        }
+    }
+    if (OP == UP_OP_MEAN) acc = acc / (double)(INCLUDE_PAD ? size : cnt);
+    return __double2float_rn(acc);
+  } else {
+    uint32_t best = 0, nan_bits = 0;
+    bool have = false, nan = false;
+    for (int kk = 0, p = p0; kk < size; ++kk, p += dilation) {
+      if (!interior && (p < 0 || p >= k_in)) continue;
+      const float v = row[p];
+      if (v != v) {
+        nan = true;
+        nan_bits = __float_as_uint(v);
+      } else if (!have || (OP == UP_OP_MAX ? v > __uint_as_float(best) : v < __uint_as_float(best))) {
+        best = __float_as_uint(v);
+      }
+      have = have || v == v;
+    }
+    return __uint_as_float(nan ? (nan_bits | 0x00400000u) : best);
+  }
+}
+
+// Windows along the innermost axis with rows that fit in shared memory: the row is staged once (every load of it in
+// flight together) and the taps are read from shared memory.
+constexpr int64_t kRowStageBytes = 48 * 1024;
+template <typename T, typename F>
+__device__ __forceinline__ void window_rows_staged(const T* __restrict__ x, int64_t outer, int64_t k_in, int64_t k_out,
+                                                   int stride, int pad_lo, T* __restrict__ out, F one) {
+  __shared__ __align__(16) T srow[kRowStageBytes / sizeof(T)];
+  for (int64_t b = blockIdx.x; b < outer; b += gridDim.x) {
+    const T* row = x + b * k_in;
+    for (int64_t i = threadIdx.x; i < k_in; i += kThreads) srow[i] = __ldg(row + i);
+    __syncthreads();
+    T* orow = out + b * k_out;
+    for (int64_t o = threadIdx.x; o < k_out; o += kThreads) orow[o] = one(srow, 1, o * stride - pad_lo);
+    __syncthreads();  // the row is read before the next one is staged
+  }
+}
+
+template <int OP, bool INCLUDE_PAD>
+__global__ void __launch_bounds__(kThreads) window_f32_staged_kernel(const float* __restrict__ x, int64_t outer,
+                                                                      int64_t k_in, int64_t k_out, int size, int stride,
+                                                                      int dilation, int pad_lo, float* __restrict__ out) {
+  window_rows_staged<float>(x, outer, k_in, k_out, stride, pad_lo, out, [&](const float* src, int64_t, int64_t p0) {
+    return window_f32_row<OP, INCLUDE_PAD>(src, (int)p0, (int)k_in, size, dilation);
+  });
 }
 
 template <int OP, bool INCLUDE_PAD>
@@ -146,6 +213,34 @@ __global__ void __launch_bounds__(kThreads) im2col_kernel(const T* __restrict__ 
   }
 }
 
+// A CTA per input plane (n, c) that fits in shared memory: the plane is staged once, coalesced, then the CTA writes
+// the plane's kh·kw output rows from shared memory.
+constexpr int64_t kPlaneBytes = 96 * 1024;
+template <typename T>
+__global__ void __launch_bounds__(kThreads) im2col_plane_kernel(const T* __restrict__ x, int64_t planes, int h, int w,
+                                                                 int kh, int kw, int sh, int sw, int ph, int pw, int dh,
+                                                                 int dw, int oh_n, int ow_n, T* __restrict__ out) {
+  extern __shared__ __align__(16) unsigned char plane_raw[];
+  T* plane = reinterpret_cast<T*>(plane_raw);
+  const int hw = h * w, cols = oh_n * ow_n;
+  for (int64_t pl = blockIdx.x; pl < planes; pl += gridDim.x) {
+    const T* src = x + pl * hw;
+    for (int i = threadIdx.x; i < hw; i += kThreads) plane[i] = __ldg(src + i);
+    __syncthreads();
+    T* orow = out + pl * kh * kw * (int64_t)cols;
+    for (int r = 0; r < kh * kw; ++r, orow += cols) {
+      const int ki = r / kw, kj = r - ki * kw;
+      const int ih0 = ki * dh - ph, iw0 = kj * dw - pw;
+      for (int col = threadIdx.x; col < cols; col += kThreads) {
+        const int oh = col / ow_n, ow = col - oh * ow_n;
+        const int ih = oh * sh + ih0, iw = ow * sw + iw0;
+        orow[col] = (ih >= 0 && ih < h && iw >= 0 && iw < w) ? plane[ih * w + iw] : T{};
+      }
+    }
+    __syncthreads();  // the plane is read before the next one is staged
+  }
+}
+
 inline int grid_for(int64_t units) {  // one unit (a row or a line) per CTA at a time, up to 16 CTAs per SM
   const int64_t cap = (int64_t)sm_count() * 16;
   return (int)(units < cap ? (units > 0 ? units : 1) : cap);
@@ -184,7 +279,22 @@ extern "C" int up_sm100_window(const void* x, int dtype, int64_t outer, int64_t 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t lp = inner > 1 && inner < win::kThreads ? win::kThreads / inner : 1;
   const int g = win::grid_for(inner == 1 ? outer : (outer * k_out + lp - 1) / lp);
-  if (dtype == UP_EK_F32) {
+  if (dtype == UP_EK_F32 && inner == 1 && k_in * 4 <= win::kRowStageBytes) {
+    const float* xf = static_cast<const float*>(x);
+    float* of = static_cast<float*>(out);
+#define UP_WIN_S(OP, INC) \
+  win::window_f32_staged_kernel<OP, INC><<<g, win::kThreads, 0, s>>>(xf, outer, k_in, k_out, size, stride, dilation, pad_lo, of)
+    switch (op) {
+      case UP_OP_SUM: UP_WIN_S(UP_OP_SUM, false); break;
+      case UP_OP_MEAN:
+        if (count_include_pad) UP_WIN_S(UP_OP_MEAN, true);
+        else UP_WIN_S(UP_OP_MEAN, false);
+        break;
+      case UP_OP_MAX: UP_WIN_S(UP_OP_MAX, false); break;
+      default: UP_WIN_S(UP_OP_MIN, false); break;
+    }
+#undef UP_WIN_S
+  } else if (dtype == UP_EK_F32) {
     const float* xf = static_cast<const float*>(x);
     float* of = static_cast<float*>(out);
 #define UP_WIN_F32(OP, INC) \
@@ -228,6 +338,39 @@ extern "C" int up_sm100_im2col(const void* x, int elem_bytes, int64_t n, int64_t
   UP_CHECK_ARG(x != nullptr && out != nullptr);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int g = win::grid_for(n * c * kh * kw);
+  const int64_t plane_bytes = h * w * (int64_t)elem_bytes;
+  if (plane_bytes <= win::kPlaneBytes && oh * ow <= 0x7fffffffLL && kh * kw <= 0x7fff) {
+    static std::mutex mu;
+    static bool attr_set[64][4] = {{false}};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_status(e);
+    const int which = elem_bytes == 1 ? 0 : elem_bytes == 2 ? 1 : elem_bytes == 4 ? 2 : 3;
+    {
+      std::lock_guard<std::mutex> lk(mu);
+      if (dev >= 0 && dev < 64 && !attr_set[dev][which]) {
+        const int mx = (int)win::kPlaneBytes;
+        e = which == 0 ? cudaFuncSetAttribute(win::im2col_plane_kernel<uint8_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx)
+          : which == 1 ? cudaFuncSetAttribute(win::im2col_plane_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx)
+          : which == 2 ? cudaFuncSetAttribute(win::im2col_plane_kernel<uint32_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx)
+                       : cudaFuncSetAttribute(win::im2col_plane_kernel<unsigned long long>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+        if (e != cudaSuccess) return cuda_status(e);
+        attr_set[dev][which] = true;
+      }
+    }
+    const int gp = win::grid_for(n * c);
+#define UP_I2P(T) \
+  win::im2col_plane_kernel<T><<<gp, win::kThreads, (size_t)plane_bytes, s>>>(static_cast<const T*>(x), n * c, (int)h, (int)w, kh, kw, sh, sw, ph, pw, dh, dw, (int)oh, (int)ow, static_cast<T*>(out))
+    switch (elem_bytes) {
+      case 1: UP_I2P(uint8_t); break;
+      case 2: UP_I2P(uint16_t); break;
+      case 4: UP_I2P(uint32_t); break;
+      default: UP_I2P(unsigned long long); break;
+    }
+#undef UP_I2P
+    note_launch();
+    return check_launch();
+  }
 #define UP_I2C(T) \
   win::im2col_kernel<T><<<g, win::kThreads, 0, s>>>(static_cast<const T*>(x), n, c, h, w, kh, kw, sh, sw, ph, pw, dh, dw, oh, ow, static_cast<T*>(out))
   switch (elem_bytes) {
