@@ -469,6 +469,19 @@ __global__ void __cluster_dims__(1, kColCluster, 1) __launch_bounds__(32 * kColV
     const float* base = x + c0;
     int64_t r = r0 + w;
     constexpr int S = kColVecWarps;
+    for (; r + 7 * S < r1; r += 8 * S) {  // eight rows in flight, folded as two batches in row order
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = ld_nc_na_f4(base + (r + u * S) * stride);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t rh = (uint32_t)(r + 4 * h * S);
+        fold_col_batch<MAX>(st[0], v[4 * h].x, v[4 * h + 1].x, v[4 * h + 2].x, v[4 * h + 3].x, rh, S);
+        fold_col_batch<MAX>(st[1], v[4 * h].y, v[4 * h + 1].y, v[4 * h + 2].y, v[4 * h + 3].y, rh, S);
+        fold_col_batch<MAX>(st[2], v[4 * h].z, v[4 * h + 1].z, v[4 * h + 2].z, v[4 * h + 3].z, rh, S);
+        fold_col_batch<MAX>(st[3], v[4 * h].w, v[4 * h + 1].w, v[4 * h + 2].w, v[4 * h + 3].w, rh, S);
+      }
+    }
     for (; r + 3 * S < r1; r += 4 * S) {
       float4 v[4];
 #pragma unroll
