@@ -77,7 +77,7 @@ static const char* interface_body(int id) {
     case UP_K_BINCOUNT:
       return R"J({"entry_symbol":"up_sm100_bincount","params":[{"name":"x","role":"read","elem":"I32|I64|U32","rank":1},{"name":"counts","role":"readwrite","elem":"I32","rank":1}],"launch":{"block":[256,1,1],"grid":"grid-stride, up to 16 CTAs per SM","cluster":null,"dynamic_shared_bytes":0},"launch_bounds":{"max_threads":256,"min_blocks":0},"cooperative":false,"requires":["sm_100a","int32_atomics"],"fidelity_notes":[],"workspace":null})J";
     case UP_K_ROW_REDUCE_F32:
-      return R"J({"entry_symbol":"up_sm100_row_reduce_f32","params":[{"name":"x","role":"read","elem":"F32","rank":-1},{"name":"out","role":"write","elem":"F32","rank":-1},{"name":"form","role":"scalar","elem":"I32"},{"name":"block","role":"scalar","elem":"I32"},{"name":"eps","role":"scalar","elem":"F64"}],"launch":{"block":[256,1,1],"grid":"two CTAs per SM over row groups (rows of at most 32 elements per thread), else 8 per SM","cluster":null,"dynamic_shared_bytes":65536},"launch_bounds":{"max_threads":256,"min_blocks":0},"cooperative":false,"requires":["sm_100a","cp.async","fp64"],"fidelity_notes":["exp by Tang's table-driven method, within 2 f64 ulps of exp; softmax and RMS norm within 4 f32 ulps of the serial lift, as the reference states"],"workspace":null})J";
+      return R"J({"entry_symbol":"up_sm100_row_reduce_f32","params":[{"name":"x","role":"read","elem":"F32","rank":-1},{"name":"out","role":"write","elem":"F32","rank":-1},{"name":"form","role":"scalar","elem":"I32"},{"name":"block","role":"scalar","elem":"I32"},{"name":"eps","role":"scalar","elem":"F64"}],"launch":{"block":[256,1,1],"grid":"two CTAs per SM over row groups (rows of at most 32 elements per thread), else 8 per SM","cluster":null,"dynamic_shared_bytes":65536},"launch_bounds":{"max_threads":256,"min_blocks":0},"cooperative":false,"requires":["sm_100a","cp.async","fp64"],"fidelity_notes":["exp and sqrt are CUDA's f64 functions; softmax and RMS norm stay within 4 f32 ulps of the serial lift, as the reference states"],"workspace":null})J";
     case UP_K_COL_SUM_SPLITK:
       return R"J({"entry_symbol":"up_sm100_col_sum_f32_splitk","params":[{"name":"x","role":"read","elem":"F32","rank":2},{"name":"out","role":"write","elem":"F32","rank":1},{"name":"mean","role":"scalar","elem":"I32"},{"name":"n_chunks","role":"scalar","elem":"I64"}],"launch":{"block":[256,1,1],"grid":"partial: column strips x n_chunks; combine: a thread per column","cluster":null,"dynamic_shared_bytes":0},"launch_bounds":{"max_threads":256,"min_blocks":0},"cooperative":false,"requires":["sm_100a","fp64"],"fidelity_notes":["ReassociatedDeterministic: f64 chunk partials added in chunk order, a different association than the serial fold; n_chunks = 1 is the serial fold"],"workspace":"n_chunks x cols f64 partials: up_sm100_col_sum_splitk_workspace_bytes"})J";
     case UP_K_WINDOW:

@@ -200,56 +200,10 @@ __global__ void __launch_bounds__(kThreads) row_reduce_f32_kernel(const float* _
 }
 
 // ---- the register-resident form (at most 32 elements per thread) ----
-// Three exact shortcuts keep the f64 pipe and the conversion unit off the critical path:
-//  * f32 -> f64 widening by integer operations (exact for zeros and normal numbers, from the binary32 and binary64
-//    layouts: sign kept, exponent rebiased by 896, fraction moved up 29 bits), used when a warp vote finds no
-//    subnormal, infinity or NaN in the warp's cached values; otherwise the conversion instruction;
-//  * a quotient a / b rounded to f32 as RN(a * RN(1 / b)): that product is within 2 f64 ulps of the quotient, so
-//    its f32 rounding is the quotient's unless the product lies within 4 ulps of an f32 rounding midpoint or
-//    outside the f32 normal range, which take the exact division (div_round_f32);
-//  * exp by Tang's table-driven method (P. T. P. Tang, "Table-driven implementation of the exponential function in
-//    IEEE floating-point arithmetic", ACM TOMS 15(2), 1989): d = (32k + j) ln2/32 + r with |r| <= ln2/64, exp(d) =
-//    2^k · 2^(j/32) · p(r), p the degree-6 Taylor polynomial (truncation below 0.02 ulp), ln2/32 split in two
-//    (Cody-Waite) so k · L1 is exact; within 2 f64 ulps of exp, far inside what the f32 rounding can see. Below
-//    -700 (where 2^k would leave the normal range) it gives 0, which changes no stored bit (exp_table).
-constexpr double kExpInvL = 0x1.71547652b82fep+5;  // 32 / ln2
-constexpr double kExpL1 = 0x1.62e4200000000p-6;    // ln2 / 32, its low 32 fraction bits clear
-constexpr double kExpL2 = 0x1.fdf473de6af28p-27;   // ln2 / 32 - L1
-
-__device__ __forceinline__ double exp_table(double d, const double* tab) {
-  // Below -700, exp(d) < 2^-1009: it reaches the output as RN_f32(exp(d) / r1) = 0 (r1 >= 1, as the row's maximum
-  // contributes exp(0)), and in the sum it is absorbed by every partial of normal size it meets before the total,
-  // so 0 leaves every stored bit as exp would. A NaN stays a NaN.
-  if (!(d >= -700.0)) return d != d ? d : 0.0;
-  const double magic = 6755399441055744.0;  // 1.5 * 2^52: adding it rounds to an integer in the low word
-  const double t = fma(d, kExpInvL, magic);
-  const double kd = t - magic;
-  const int k = __double2loint(t);
-  double r = fma(-kd, kExpL1, d);
-  r = fma(-kd, kExpL2, r);
-  double q = 1.0 / 720.0;
-  q = fma(q, r, 1.0 / 120.0);
-  q = fma(q, r, 1.0 / 24.0);
-  q = fma(q, r, 1.0 / 6.0);
-  q = fma(q, r, 0.5);
-  q = fma(q, r, 1.0);
-  q = fma(q, r, 1.0);
-  const double v = tab[k & 31] * q;
-  return __hiloint2double(__double2hiint(v) + ((k >> 5) * (1 << 20)), __double2loint(v));
-}
-
-__device__ __forceinline__ bool widenable(float f) {
-  const uint32_t t = __float_as_uint(f) & 0x7fffffffu;
-  return t - 0x00800000u < 0x7f000000u || t == 0u;
-}
-
-__device__ __forceinline__ double widen_fast(float f) {  // a zero or a normal number
-  const uint32_t u = __float_as_uint(f);
-  const uint32_t t = u & 0x7fffffffu;
-  const uint32_t hi = t == 0u ? u : (((t >> 3) + 0x38000000u) | (u & 0x80000000u));
-  return __hiloint2double((int)hi, (int)(u << 29));
-}
-
+// A quotient a / b is rounded to f32 as RN(a * RN(1 / b)): that product is within 2 f64 ulps of the quotient, so its
+// f32 rounding is the quotient's unless the product lies within 4 ulps of an f32 rounding midpoint or outside the
+// f32 normal range, which take the exact division (div_round_f32). exp is CUDA's f64 exp; a table-driven exp
+// (Tang's method) and an integer f32 -> f64 widening both measured slower here.
 __device__ __noinline__ float div_exact_f32(double a, double b) { return __double2float_rn(a / b); }
 
 __device__ __forceinline__ float div_round_f32(double a, double b, double inv) {
@@ -276,12 +230,7 @@ __global__ void __launch_bounds__(kThreads) row_reduce_f32_held_kernel(const flo
   __shared__ double region[kThreads];
   __shared__ double wred[kThreads / 32];
   __shared__ double slot[kThreads];
-  __shared__ double tab[32];
   extern __shared__ __align__(16) float stage[];  // [2][kCache * kThreads]
-  if (FORM == kFormSoftmax) {
-    if (threadIdx.x < 32) tab[threadIdx.x] = exp2((double)threadIdx.x / 32.0);
-    __syncthreads();
-  }
   const int G = B / L;
   const int rpc = kThreads / G;
   const int grp = threadIdx.x / G, p = threadIdx.x - grp * G;
@@ -311,10 +260,6 @@ __global__ void __launch_bounds__(kThreads) row_reduce_f32_held_kernel(const flo
     const float* src = &stage[(it & 1) * kCache * kThreads + grp * kCache * G + p];
 #pragma unroll
     for (int k = 0; k < kCache; ++k) xv[k] = k < kn ? src[G * k] : 0.0f;
-    bool fine = true;
-#pragma unroll
-    for (int k = 0; k < kCache; ++k) fine &= widenable(xv[k]);
-    const bool alu = __all_sync(0xffffffffu, fine);  // every thread is here: the loop above is not divergent
     double acc[L];
 #pragma unroll
     for (int q = 0; q < L; ++q) acc[q] = 0.0;
@@ -325,13 +270,8 @@ __global__ void __launch_bounds__(kThreads) row_reduce_f32_held_kernel(const flo
         if (k < kn) asm("max.NaN.f32 %0, %0, %1;" : "+f"(m) : "f"(xv[k]));
       const double r0d = (double)(float)group_max((double)m, G, p, grp, wred, slot);
       double ev[kCache];
-      if (alu) {
 #pragma unroll
-        for (int k = 0; k < kCache; ++k) ev[k] = exp_table(widen_fast(xv[k]) - r0d, tab);
-      } else {
-#pragma unroll
-        for (int k = 0; k < kCache; ++k) ev[k] = exp((double)xv[k] - r0d);
-      }
+      for (int k = 0; k < kCache; ++k) ev[k] = exp((double)xv[k] - r0d);
 #pragma unroll
       for (int k = 0; k < kCache; ++k)
         if (k < kn) acc[k % L] += ev[k];
@@ -342,13 +282,8 @@ __global__ void __launch_bounds__(kThreads) row_reduce_f32_held_kernel(const flo
         if (k < kn) orow[p + (int64_t)G * k] = div_round_f32(ev[k], r1, inv);
     } else {
       double xd[kCache];
-      if (alu) {
 #pragma unroll
-        for (int k = 0; k < kCache; ++k) xd[k] = widen_fast(xv[k]);
-      } else {
-#pragma unroll
-        for (int k = 0; k < kCache; ++k) xd[k] = (double)xv[k];
-      }
+      for (int k = 0; k < kCache; ++k) xd[k] = (double)xv[k];
 #pragma unroll
       for (int k = 0; k < kCache; ++k)
         if (k < kn) acc[k % L] += FORM == kFormRmsNorm ? xd[k] * xd[k] : xd[k];
