@@ -141,3 +141,15 @@ def test_full_size_middle_axis():
     assert np.array_equal(bits(ops.reduce3d(x, "max").cpu()), bits(want_max))
     want_sum = np.stack([orc.col_sum_f32_documented(xn[a], 256, threads=t) for a in range(64)])
     assert np.array_equal(bits(ops.reduce3d(x, "sum", block=256).cpu()), bits(want_sum))
+
+
+def test_more_batches_than_one_launch_holds():
+    """70,000 batches run as two launches of at most 65,535 (the grid's z extent)."""
+    rng = np.random.default_rng(21)
+    xf = rng.standard_normal((70000, 3, 4)).astype(np.float32)
+    xi = rng.integers(-1000, 1000, (70000, 3, 4)).astype(np.int32)
+    for op in ("max", "sum"):
+        got = ops.reduce3d(torch.from_numpy(xf).cuda(), op).cpu().numpy()
+        assert np.array_equal(bits(got), bits(_middle_oracle(xf, op))), op
+    for op in ("xor", "min"):
+        assert np.array_equal(ops.reduce3d(torch.from_numpy(xi).cuda(), op).cpu().numpy(), _middle_oracle(xi, op)), op

@@ -141,3 +141,17 @@ def test_plans_through_the_backend():
                       im2col=((3, 3), (1, 1), (1, 1), (1, 1))))
     be.launch(k, [Operand("F32", (2, 3, 8, 8), ptr=im.data_ptr())], [Operand("F32", (2, 27, 64), ptr=o.data_ptr())])
     assert np.array_equal(bits(o.cpu().numpy()), bits(orc.im2col(im.cpu().numpy(), (3, 3), (1, 1), (1, 1), (1, 1))))
+
+
+def test_unstaged_paths():
+    """Rows longer than the shared-memory stage (innermost windows) and planes larger than it (im2col) take the
+    unstaged kernels."""
+    rng = np.random.default_rng(13)
+    xn = rng.standard_normal((3, 20000)).astype(np.float32)
+    x = torch.from_numpy(xn).cuda()
+    for op in ("max", "mean", "sum"):
+        got = ops.window(x, op, 3, 2, 1, 1).cpu().numpy()
+        assert np.array_equal(bits(got), bits(orc.window(xn, op, 3, 2, 1, 1))), op
+    im = rng.standard_normal((1, 2, 200, 200)).astype(np.float32)  # 160 KB planes
+    got = ops.im2col(torch.from_numpy(im).cuda(), (3, 3), (2, 2), (1, 1), (1, 1)).cpu().numpy()
+    assert np.array_equal(bits(got), bits(orc.im2col(im, (3, 3), (2, 2), (1, 1), (1, 1))))
