@@ -222,7 +222,7 @@ __device__ __forceinline__ void cp_async4(float* smem, const float* gmem) {
 
 // Rows are staged through shared memory by cp.async, the next rows' copies in flight while this row is computed:
 // two buffers of kCache * kThreads floats (each row group's row at grp * kCache * G).
-template <int FORM, int L>
+template <int FORM, int L, bool WHOLE>
 __global__ void __launch_bounds__(kThreads) row_reduce_f32_held_kernel(const float* __restrict__ x, int64_t rows,
                                                                         int64_t cols, int64_t stride, int B,
                                                                         double eps, float* __restrict__ out,
@@ -242,7 +242,7 @@ __global__ void __launch_bounds__(kThreads) row_reduce_f32_held_kernel(const flo
       float* dst = &stage[buf * kCache * kThreads + grp * kCache * G + p];
 #pragma unroll
       for (int k = 0; k < kCache; ++k)
-        if (k < K) cp_async4(dst + G * k, src + (int64_t)G * k);
+        if (WHOLE || k < K) cp_async4(dst + G * k, src + (int64_t)G * k);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(kThreads) row_reduce_f32_held_kernel(const flo
     float xv[kCache];
     const float* src = &stage[(it & 1) * kCache * kThreads + grp * kCache * G + p];
 #pragma unroll
-    for (int k = 0; k < kCache; ++k) xv[k] = k < kn ? src[G * k] : 0.0f;
+    for (int k = 0; k < kCache; ++k) xv[k] = WHOLE || k < kn ? src[G * k] : 0.0f;
     double acc[L];
 #pragma unroll
     for (int q = 0; q < L; ++q) acc[q] = 0.0;
@@ -267,46 +267,72 @@ __global__ void __launch_bounds__(kThreads) row_reduce_f32_held_kernel(const flo
       float m = -INFINITY;
 #pragma unroll
       for (int k = 0; k < kCache; ++k)
-        if (k < kn) asm("max.NaN.f32 %0, %0, %1;" : "+f"(m) : "f"(xv[k]));
+        if (WHOLE || k < kn) asm("max.NaN.f32 %0, %0, %1;" : "+f"(m) : "f"(xv[k]));
       const double r0d = (double)(float)group_max((double)m, G, p, grp, wred, slot);
       double ev[kCache];
 #pragma unroll
       for (int k = 0; k < kCache; ++k) ev[k] = exp((double)xv[k] - r0d);
 #pragma unroll
       for (int k = 0; k < kCache; ++k)
-        if (k < kn) acc[k % L] += ev[k];
+        if (WHOLE || k < kn) acc[k % L] += ev[k];
       const double r1 = (double)(float)group_tree<L>(acc, G, p, grp, region, slot);
       const double inv = 1.0 / r1;
 #pragma unroll
       for (int k = 0; k < kCache; ++k)
-        if (k < kn) orow[p + (int64_t)G * k] = div_round_f32(ev[k], r1, inv);
+        if (WHOLE ? live : k < kn) orow[p + (int64_t)G * k] = div_round_f32(ev[k], r1, inv);
     } else {
       double xd[kCache];
 #pragma unroll
       for (int k = 0; k < kCache; ++k) xd[k] = (double)xv[k];
 #pragma unroll
       for (int k = 0; k < kCache; ++k)
-        if (k < kn) acc[k % L] += FORM == kFormRmsNorm ? xd[k] * xd[k] : xd[k];
+        if (WHOLE || k < kn) acc[k % L] += FORM == kFormRmsNorm ? xd[k] * xd[k] : xd[k];
       const double r0d = (double)(float)(group_tree<L>(acc, G, p, grp, region, slot) / (double)cols);
       if (FORM == kFormRmsNorm) {
         const double den = sqrt(r0d + eps);
         const double inv = 1.0 / den;
 #pragma unroll
         for (int k = 0; k < kCache; ++k)
-          if (k < kn) orow[p + (int64_t)G * k] = div_round_f32(xd[k], den, inv);
+          if (WHOLE ? live : k < kn) orow[p + (int64_t)G * k] = div_round_f32(xd[k], den, inv);
       } else {
         double m = -INFINITY;
 #pragma unroll
         for (int k = 0; k < kCache; ++k)
-          if (k < kn) m = nan_max(m, xd[k] - r0d);
+          if (WHOLE || k < kn) m = nan_max(m, xd[k] - r0d);
         const double r1 = (double)(float)group_max(m, G, p, grp, wred, slot);
         const double inv = 1.0 / r1;
 #pragma unroll
         for (int k = 0; k < kCache; ++k)
-          if (k < kn) orow[p + (int64_t)G * k] = div_round_f32(xd[k] - r0d, r1, inv);
+          if (WHOLE ? live : k < kn) orow[p + (int64_t)G * k] = div_round_f32(xd[k] - r0d, r1, inv);
       }
     }
   }
+}
+
+// The held path's launch: the staged-row buffers need 64 KB of dynamic shared memory, an attribute set once per
+// device and instantiation.
+template <int FORM, int L, bool WHOLE>
+int launch_held(const float* x, int64_t rows, int64_t cols, int64_t stride, int B, double eps, float* out,
+                int64_t ostride, int64_t g, cudaStream_t s) {
+  constexpr size_t smem = 2 * sizeof(float) * kCache * kThreads;
+  static std::mutex mu;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+      e = cudaFuncSetAttribute(row_reduce_f32_held_kernel<FORM, L, WHOLE>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return cuda_status(e);
+      if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+  }
+  const int64_t held_cap = (int64_t)sm_count() * 2;  // two CTAs per SM: registers and the staged rows
+  row_reduce_f32_held_kernel<FORM, L, WHOLE><<<(int)(g < held_cap ? g : held_cap), kThreads, smem, s>>>(
+      x, rows, cols, stride, B, eps, out, ostride);
+  return UP_OK;
 }
 
 template <int FORM, int L>
@@ -318,24 +344,11 @@ int launch_form(const float* x, int64_t rows, int64_t cols, int64_t stride, int 
   const int64_t cap = (int64_t)sm_count() * 8;
   if (g > cap) g = cap;
   if (cols <= (int64_t)kCache * G) {
-    constexpr size_t smem = 2 * sizeof(float) * kCache * kThreads;
-    static std::mutex mu;
-    static bool attr_set[64] = {false};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return cuda_status(e);
-    {
-      std::lock_guard<std::mutex> lk(mu);
-      if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(row_reduce_f32_held_kernel<FORM, L>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem);
-        if (e != cudaSuccess) return cuda_status(e);
-        if (dev >= 0 && dev < 64) attr_set[dev] = true;
-      }
-    }
-    const int64_t held_cap = (int64_t)sm_count() * 2;  // two CTAs per SM: registers and the staged rows
-    row_reduce_f32_held_kernel<FORM, L><<<(int)(g < held_cap ? g : held_cap), kThreads, smem, s>>>(
-        x, rows, cols, stride, B, eps, out, ostride);
+    // A row that fills each thread's kCache slots exactly needs no per-slot bound.
+    const int rc = cols == (int64_t)kCache * G
+                       ? launch_held<FORM, L, true>(x, rows, cols, stride, B, eps, out, ostride, g, s)
+                       : launch_held<FORM, L, false>(x, rows, cols, stride, B, eps, out, ostride, g, s);
+    if (rc != UP_OK) return rc;
   } else
     row_reduce_f32_kernel<FORM, L, false><<<(int)g, kThreads, 0, s>>>(x, rows, cols, stride, B, eps, out, ostride);
   note_launch();
