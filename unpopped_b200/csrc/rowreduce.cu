@@ -310,26 +310,32 @@ __global__ void __launch_bounds__(kThreads) row_reduce_f32_held_kernel(const flo
 }
 
 // The held path's launch: the staged-row buffers need 64 KB of dynamic shared memory, an attribute set once per
-// device and instantiation.
+// device and instantiation; the grid is the CTAs that fit on every SM at once (two or three, by registers).
 template <int FORM, int L, bool WHOLE>
 int launch_held(const float* x, int64_t rows, int64_t cols, int64_t stride, int B, double eps, float* out,
                 int64_t ostride, int64_t g, cudaStream_t s) {
   constexpr size_t smem = 2 * sizeof(float) * kCache * kThreads;
   static std::mutex mu;
-  static bool attr_set[64] = {false};
+  static int per_sm[64] = {0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
+  int fit = 0;
   {
     std::lock_guard<std::mutex> lk(mu);
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    if (dev >= 0 && dev < 64) fit = per_sm[dev];
+    if (fit == 0) {
       e = cudaFuncSetAttribute(row_reduce_f32_held_kernel<FORM, L, WHOLE>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return cuda_status(e);
-      if (dev >= 0 && dev < 64) attr_set[dev] = true;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&fit, row_reduce_f32_held_kernel<FORM, L, WHOLE>, kThreads,
+                                                        smem);
+      if (e != cudaSuccess) return cuda_status(e);
+      if (fit < 1) fit = 1;
+      if (dev >= 0 && dev < 64) per_sm[dev] = fit;
     }
   }
-  const int64_t held_cap = (int64_t)sm_count() * 2;  // two CTAs per SM: registers and the staged rows
+  const int64_t held_cap = (int64_t)sm_count() * fit;
   row_reduce_f32_held_kernel<FORM, L, WHOLE><<<(int)(g < held_cap ? g : held_cap), kThreads, smem, s>>>(
       x, rows, cols, stride, B, eps, out, ostride);
   return UP_OK;
