@@ -272,7 +272,7 @@ def bench_lifts(ctx, K, W, hbm, bf16):
     # the Window lift (max pool 3/2, pad 1, along the last axis) and Im2Col (a 3x3 unfold of 32 x 64 x 56 x 56)
     ow = torch.empty((8192, 4096), device=ctx.dev)
     ms, _, _ = ctx.timed(lambda i, kin: ops.window(xs[i % R], "max", 3, 2, 1, 1, out=ow), K, W)
-    record("window_maxpool3s2_f32_8192x8192", wl.rowsum_bytes() + ow.numel() * 4, ms, "window_f32_kernel", R)
+    record("window_maxpool3s2_f32_8192x8192", wl.rowsum_bytes() + ow.numel() * 4, ms, "window_f32_staged_kernel", R)
     del ow
     xi = [x.view(torch.int32) for x in xs]  # the same bytes read as i32
     oi = out.view(torch.int32)
