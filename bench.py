@@ -462,6 +462,12 @@ def profile_cases(which: str):
         o = torch.empty_like(x)
         return lambda: ops.row_reduce(x, "rms_norm", block=256, out=o)
 
+    @case("window")
+    def _():
+        x = wl.rowsum_input(device=dev)
+        o = torch.empty((x.shape[0], x.shape[1] // 2), device=dev)
+        return lambda: ops.window(x, "max", 3, 2, 1, 1, out=o)
+
     @case("argmax")
     def _():
         x = wl.argmax_input(rows=8192, device=dev)
@@ -503,7 +509,7 @@ def main():
     ap.add_argument("--lifts", default="all", choices=["all", "none"])
     ap.add_argument("--profile", default=None,
                     help="run only the small ncu cases of these lifts, comma-separated (scan, rowsum, rowsum_auto, "
-                         "rowmax_f32, colmax_f32, row_rms_norm, argmax, gather, dequant, w4a16, all)")
+                         "rowmax_f32, colmax_f32, row_rms_norm, window, argmax, gather, dequant, w4a16, all)")
     args = ap.parse_args()
     if args.profile:
         profile_cases(args.profile)

@@ -103,17 +103,21 @@ __device__ __forceinline__ void window_walk(const T* __restrict__ x, int64_t out
 
 // The same fold over a row staged in shared memory, with 32-bit positions; an interior window (every tap inside the
 // row) skips the bounds checks.
-template <int OP, bool INCLUDE_PAD>
-__device__ __forceinline__ float window_f32_row(const float* __restrict__ row, int p0, int k_in, int size,
+// SZ > 0 fixes the window size at compile time (the common pooling sizes), so the tap loops unroll.
+template <int OP, bool INCLUDE_PAD, int SZ>
+__device__ __forceinline__ float window_f32_row(const float* __restrict__ row, int p0, int k_in, int size_rt,
                                                 int dilation) {
+  const int size = SZ > 0 ? SZ : size_rt;
   const bool interior = p0 >= 0 && p0 + (size - 1) * dilation < k_in;
   if (OP == UP_OP_SUM || OP == UP_OP_MEAN) {
     double acc = 0.0;
     int cnt = 0;
     if (interior) {
+#pragma unroll
       for (int kk = 0, p = p0; kk < size; ++kk, p += dilation) acc += (double)row[p];
       cnt = size;
     } else {
+#pragma unroll
       for (int kk = 0, p = p0; kk < size; ++kk, p += dilation)
         if (p >= 0 && p < k_in) {
           acc += (double)row[p];
@@ -125,6 +129,7 @@ __device__ __forceinline__ float window_f32_row(const float* __restrict__ row, i
   } else {
     uint32_t best = 0, nan_bits = 0;
     bool have = false, nan = false;
+#pragma unroll
     for (int kk = 0, p = p0; kk < size; ++kk, p += dilation) {
       if (!interior && (p < 0 || p >= k_in)) continue;
       const float v = row[p];
@@ -176,13 +181,27 @@ __device__ __forceinline__ void window_rows_staged(const T* __restrict__ x, int6
   }
 }
 
-template <int OP, bool INCLUDE_PAD>
+template <int OP, bool INCLUDE_PAD, int SZ>
 __global__ void __launch_bounds__(kThreads) window_f32_staged_kernel(const float* __restrict__ x, int64_t outer,
                                                                       int64_t k_in, int64_t k_out, int size, int stride,
                                                                       int dilation, int pad_lo, float* __restrict__ out) {
   window_rows_staged<float>(x, outer, k_in, k_out, stride, pad_lo, out, [&](const float* src, int64_t, int64_t p0) {
-    return window_f32_row<OP, INCLUDE_PAD>(src, (int)p0, (int)k_in, size, dilation);
+    return window_f32_row<OP, INCLUDE_PAD, SZ>(src, (int)p0, (int)k_in, size, dilation);
   });
+}
+
+template <int OP, bool INCLUDE_PAD>
+void launch_staged(const float* x, int64_t outer, int64_t k_in, int64_t k_out, int size, int stride, int dilation,
+                   int pad_lo, float* out, int g, cudaStream_t s) {
+  if (size == 2)
+    window_f32_staged_kernel<OP, INCLUDE_PAD, 2><<<g, kThreads, 0, s>>>(x, outer, k_in, k_out, size, stride, dilation,
+                                                                       pad_lo, out);
+  else if (size == 3)
+    window_f32_staged_kernel<OP, INCLUDE_PAD, 3><<<g, kThreads, 0, s>>>(x, outer, k_in, k_out, size, stride, dilation,
+                                                                       pad_lo, out);
+  else
+    window_f32_staged_kernel<OP, INCLUDE_PAD, 0><<<g, kThreads, 0, s>>>(x, outer, k_in, k_out, size, stride, dilation,
+                                                                       pad_lo, out);
 }
 
 template <int OP, bool INCLUDE_PAD>
@@ -301,8 +320,7 @@ extern "C" int up_sm100_window(const void* x, int dtype, int64_t outer, int64_t 
   if (dtype == UP_EK_F32 && inner == 1 && k_in * 4 <= win::kRowStageBytes) {
     const float* xf = static_cast<const float*>(x);
     float* of = static_cast<float*>(out);
-#define UP_WIN_S(OP, INC) \
-  win::window_f32_staged_kernel<OP, INC><<<g, win::kThreads, 0, s>>>(xf, outer, k_in, k_out, size, stride, dilation, pad_lo, of)
+#define UP_WIN_S(OP, INC) win::launch_staged<OP, INC>(xf, outer, k_in, k_out, size, stride, dilation, pad_lo, of, g, s)
     switch (op) {
       case UP_OP_SUM: UP_WIN_S(UP_OP_SUM, false); break;
       case UP_OP_MEAN:
