@@ -127,11 +127,27 @@ __device__ __forceinline__ float window_f32_row(const float* __restrict__ row, i
     if (OP == UP_OP_MEAN) acc = acc / (double)(INCLUDE_PAD ? size : cnt);
     return __double2float_rn(acc);
   } else {
+    if (interior) {
+      // Every tap is in bounds, so the first one seeds the fold. A NaN anywhere decides the result, so a NaN seed
+      // needs no later non-NaN value, and a NaN tap never wins the comparison.
+      float b = row[p0];
+      uint32_t nb = __float_as_uint(b);  // the last NaN's bits, read only when there is one
+      bool nan = b != b;
+#pragma unroll
+      for (int kk = 1, p = p0 + dilation; kk < size; ++kk, p += dilation) {
+        const float v = row[p];
+        const bool vn = v != v;
+        nb = vn ? __float_as_uint(v) : nb;
+        nan = nan || vn;
+        b = (OP == UP_OP_MAX ? v > b : v < b) ? v : b;
+      }
+      return __uint_as_float(nan ? (nb | 0x00400000u) : __float_as_uint(b));
+    }
     uint32_t best = 0, nan_bits = 0;
     bool have = false, nan = false;
 #pragma unroll
     for (int kk = 0, p = p0; kk < size; ++kk, p += dilation) {
-      if (!interior && (p < 0 || p >= k_in)) continue;
+      if (p < 0 || p >= k_in) continue;
       const float v = row[p];
       if (v != v) {
         nan = true;
