@@ -281,14 +281,19 @@ __global__ void __launch_bounds__(kThreads) im2col_plane_kernel(const T* __restr
     const T* src = x + pl * hw;
     for (int i = threadIdx.x; i < hw; i += kThreads) plane[i] = __ldg(src + i);
     __syncthreads();
-    T* orow = out + pl * kh * kw * (int64_t)cols;
-    for (int r = 0; r < kh * kw; ++r, orow += cols) {
-      const int ki = r / kw, kj = r - ki * kw;
-      const int ih0 = ki * dh - ph, iw0 = kj * dw - pw;
-      for (int col = threadIdx.x; col < cols; col += kThreads) {
-        const int oh = col / ow_n, ow = col - oh * ow_n;
-        const int ih = oh * sh + ih0, iw = ow * sw + iw0;
-        orow[col] = (ih >= 0 && ih < h && iw >= 0 && iw < w) ? plane[ih * w + iw] : T{};
+    // a thread decodes its cell (oh, ow) once and writes it in all kh·kw rows (each store coalesced across the warp)
+    T* const orow = out + pl * kh * kw * (int64_t)cols;
+    for (int col = threadIdx.x; col < cols; col += kThreads) {
+      const int oh = col / ow_n, ow = col - oh * ow_n;
+      const int ihb = oh * sh - ph, iwb = ow * sw - pw;
+      T* o = orow + col;
+      for (int ki = 0; ki < kh; ++ki) {
+        const int ih = ihb + ki * dh;
+        const bool in_h = ih >= 0 && ih < h;
+        for (int kj = 0; kj < kw; ++kj, o += cols) {
+          const int iw = iwb + kj * dw;
+          *o = (in_h && iw >= 0 && iw < w) ? plane[ih * w + iw] : T{};
+        }
       }
     }
     __syncthreads();  // the plane is read before the next one is staged
