@@ -24,12 +24,15 @@ constexpr int kThreads = 256;
 
 // One output of a window: the fold of its in-bounds taps (src points at tap position 0 of the output's line;
 // consecutive taps are `step` elements apart).
-template <int OP, bool INCLUDE_PAD>
+// SZ > 0 fixes the window size at compile time, so the tap loops unroll.
+template <int OP, bool INCLUDE_PAD, int SZ>
 __device__ __forceinline__ float window_f32_one(const float* __restrict__ src, int64_t step, int64_t p0, int64_t k_in,
-                                                int size, int dilation) {
+                                                int size_rt, int dilation) {
+  const int size = SZ > 0 ? SZ : size_rt;
   if (OP == UP_OP_SUM || OP == UP_OP_MEAN) {
     double acc = 0.0;
     int cnt = 0;
+#pragma unroll
     for (int kk = 0; kk < size; ++kk) {
       const int64_t p = p0 + (int64_t)kk * dilation;
       if (p < 0 || p >= k_in) continue;
@@ -39,8 +42,27 @@ __device__ __forceinline__ float window_f32_one(const float* __restrict__ src, i
     if (OP == UP_OP_MEAN) acc = acc / (double)(INCLUDE_PAD ? size : cnt);
     return __double2float_rn(acc);
   } else {
+    if (p0 >= 0 && p0 + (int64_t)(size - 1) * dilation < k_in) {
+      // an interior window: the first tap seeds a branch-free fold (as window_f32_row below)
+      const int64_t tstep = (int64_t)dilation * step;
+      const float* q = src + p0 * step;
+      float b = *q;
+      uint32_t nb = __float_as_uint(b);
+      bool nan = b != b;
+#pragma unroll
+      for (int kk = 1; kk < size; ++kk) {
+        q += tstep;
+        const float v = *q;
+        const bool vn = v != v;
+        nb = vn ? __float_as_uint(v) : nb;
+        nan = nan || vn;
+        b = (OP == UP_OP_MAX ? v > b : v < b) ? v : b;
+      }
+      return __uint_as_float(nan ? (nb | 0x00400000u) : __float_as_uint(b));
+    }
     uint32_t best = 0, nan_bits = 0;
     bool have = false, nan = false;
+#pragma unroll
     for (int kk = 0; kk < size; ++kk) {
       const int64_t p = p0 + (int64_t)kk * dilation;
       if (p < 0 || p >= k_in) continue;
@@ -220,13 +242,27 @@ void launch_staged(const float* x, int64_t outer, int64_t k_in, int64_t k_out, i
                                                                        pad_lo, out);
 }
 
-template <int OP, bool INCLUDE_PAD>
+template <int OP, bool INCLUDE_PAD, int SZ>
 __global__ void __launch_bounds__(kThreads) window_f32_kernel(const float* __restrict__ x, int64_t outer, int64_t k_in,
                                                                int64_t inner, int64_t k_out, int size, int stride,
                                                                int dilation, int pad_lo, float* __restrict__ out) {
   window_walk<float>(x, outer, k_in, inner, k_out, stride, pad_lo, out, [&](const float* src, int64_t step, int64_t p0) {
-    return window_f32_one<OP, INCLUDE_PAD>(src, step, p0, k_in, size, dilation);
+    return window_f32_one<OP, INCLUDE_PAD, SZ>(src, step, p0, k_in, size, dilation);
   });
+}
+
+template <int OP, bool INCLUDE_PAD>
+void launch_lines(const float* x, int64_t outer, int64_t k_in, int64_t inner, int64_t k_out, int size, int stride,
+                  int dilation, int pad_lo, float* out, int g, cudaStream_t s) {
+  if (size == 2)
+    window_f32_kernel<OP, INCLUDE_PAD, 2><<<g, kThreads, 0, s>>>(x, outer, k_in, inner, k_out, size, stride, dilation,
+                                                                pad_lo, out);
+  else if (size == 3)
+    window_f32_kernel<OP, INCLUDE_PAD, 3><<<g, kThreads, 0, s>>>(x, outer, k_in, inner, k_out, size, stride, dilation,
+                                                                pad_lo, out);
+  else
+    window_f32_kernel<OP, INCLUDE_PAD, 0><<<g, kThreads, 0, s>>>(x, outer, k_in, inner, k_out, size, stride, dilation,
+                                                                pad_lo, out);
 }
 
 template <int OP>
@@ -356,7 +392,7 @@ extern "C" int up_sm100_window(const void* x, int dtype, int64_t outer, int64_t 
     const float* xf = static_cast<const float*>(x);
     float* of = static_cast<float*>(out);
 #define UP_WIN_F32(OP, INC) \
-  win::window_f32_kernel<OP, INC><<<g, win::kThreads, 0, s>>>(xf, outer, k_in, inner, k_out, size, stride, dilation, pad_lo, of)
+  win::launch_lines<OP, INC>(xf, outer, k_in, inner, k_out, size, stride, dilation, pad_lo, of, g, s)
     switch (op) {
       case UP_OP_SUM: UP_WIN_F32(UP_OP_SUM, false); break;
       case UP_OP_MEAN:
