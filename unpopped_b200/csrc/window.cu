@@ -114,11 +114,21 @@ __device__ __forceinline__ void window_walk(const T* __restrict__ x, int64_t out
     const int sub = inner < kThreads ? (int)threadIdx.x / (int)inner : 0;
     const int64_t i0 = inner < kThreads ? (int64_t)threadIdx.x - (int64_t)sub * inner : threadIdx.x;
     if (sub >= lp) return;  // the threads past lp whole lines
-    for (int64_t line = (int64_t)blockIdx.x * lp + sub; line < lines; line += (int64_t)gridDim.x * lp) {
-      const int64_t b = line / k_out, o = line - b * k_out;
+    // (b, o) of the line advance by a fixed step: one division per thread, not one per line
+    const int64_t step = (int64_t)gridDim.x * lp;
+    const int64_t db = step / k_out, dr = step - db * k_out;
+    int64_t line = (int64_t)blockIdx.x * lp + sub;
+    int64_t b = line / k_out, o = line - b * k_out;
+    for (; line < lines; line += step) {
       const T* base = x + b * k_in * inner;
       T* orow = out + line * inner;
       for (int64_t i = i0; i < inner; i += kThreads) orow[i] = one(base + i, inner, o * stride - pad_lo);
+      o += dr;
+      b += db;
+      if (o >= k_out) {
+        o -= k_out;
+        ++b;
+      }
     }
   }
 }
