@@ -81,7 +81,7 @@ static const char* interface_body(int id) {
     case UP_K_COL_SUM_SPLITK:
       return R"J({"entry_symbol":"up_sm100_col_sum_f32_splitk","params":[{"name":"x","role":"read","elem":"F32","rank":2},{"name":"out","role":"write","elem":"F32","rank":1},{"name":"mean","role":"scalar","elem":"I32"},{"name":"n_chunks","role":"scalar","elem":"I64"}],"launch":{"block":[256,1,1],"grid":"partial: column strips x n_chunks; combine: a thread per column","cluster":null,"dynamic_shared_bytes":0},"launch_bounds":{"max_threads":256,"min_blocks":0},"cooperative":false,"requires":["sm_100a","fp64"],"fidelity_notes":["ReassociatedDeterministic: f64 chunk partials added in chunk order, a different association than the serial fold; n_chunks = 1 is the serial fold"],"workspace":"n_chunks x cols f64 partials: up_sm100_col_sum_splitk_workspace_bytes"})J";
     case UP_K_WINDOW:
-      return R"J({"entry_symbol":"up_sm100_window","params":[{"name":"x","role":"read","elem":"F32|I32","rank":-1},{"name":"out","role":"write","elem":"F32|I32","rank":-1},{"name":"op","role":"scalar","elem":"I32"},{"name":"size","role":"scalar","elem":"I32"},{"name":"stride","role":"scalar","elem":"I32"},{"name":"dilation","role":"scalar","elem":"I32"},{"name":"pad_lo","role":"scalar","elem":"I32"},{"name":"count_include_pad","role":"scalar","elem":"I32"},{"name":"axis","role":"scalar","elem":"I32"}],"launch":{"block":[256,1,1],"grid":"a CTA per row (innermost axis; the row staged by cp.async into 48 KiB of static shared memory) or per group of lines, up to 16 per SM","cluster":null,"dynamic_shared_bytes":0},"launch_bounds":{"max_threads":256,"min_blocks":0},"cooperative":false,"requires":["sm_100a","cp.async"],"fidelity_notes":[],"workspace":null})J";
+      return R"J({"entry_symbol":"up_sm100_window","params":[{"name":"x","role":"read","elem":"F32|I32","rank":-1},{"name":"out","role":"write","elem":"F32|I32","rank":-1},{"name":"op","role":"scalar","elem":"I32"},{"name":"size","role":"scalar","elem":"I32"},{"name":"stride","role":"scalar","elem":"I32"},{"name":"dilation","role":"scalar","elem":"I32"},{"name":"pad_lo","role":"scalar","elem":"I32"},{"name":"count_include_pad","role":"scalar","elem":"I32"},{"name":"axis","role":"scalar","elem":"I32"}],"launch":{"block":[256,1,1],"grid":"a CTA per row (innermost axis; the row staged by cp.async into 32 KiB of static shared memory) or per group of lines, up to 16 per SM","cluster":null,"dynamic_shared_bytes":0},"launch_bounds":{"max_threads":256,"min_blocks":0},"cooperative":false,"requires":["sm_100a","cp.async"],"fidelity_notes":[],"workspace":null})J";
     case UP_K_IM2COL:
       return R"J({"entry_symbol":"up_sm100_im2col","params":[{"name":"x","role":"read","elem":"any","rank":4},{"name":"out","role":"write","elem":"any","rank":3},{"name":"kh","role":"scalar","elem":"I32"},{"name":"kw","role":"scalar","elem":"I32"},{"name":"sh","role":"scalar","elem":"I32"},{"name":"sw","role":"scalar","elem":"I32"},{"name":"ph","role":"scalar","elem":"I32"},{"name":"pw","role":"scalar","elem":"I32"},{"name":"dh","role":"scalar","elem":"I32"},{"name":"dw","role":"scalar","elem":"I32"}],"launch":{"block":[256,1,1],"grid":"a CTA per input plane staged in dynamic shared memory (the plane's bytes, at most 96 KiB), else a CTA per output row; up to 16 per SM","cluster":null,"dynamic_shared_bytes":0},"launch_bounds":{"max_threads":256,"min_blocks":0},"cooperative":false,"requires":["sm_100a"],"fidelity_notes":[],"workspace":null})J";
     default: return nullptr;

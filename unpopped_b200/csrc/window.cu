@@ -195,9 +195,10 @@ __device__ __forceinline__ float window_f32_row(const float* __restrict__ row, i
 
 // Windows along the innermost axis with rows that fit in shared memory: the row is staged once with cp.async
 // (16-byte copies when the rows are 16-byte aligned, else 4-byte ones; no copy waits on a register, so every copy
-// of the row is in flight together) and the taps are read from shared memory. One 48 KB buffer keeps four CTAs on
-// an SM, whose folds cover each other's staging; two buffers per CTA (three CTAs) measured slower.
-constexpr int64_t kRowStageBytes = 48 * 1024;
+// of the row is in flight together) and the taps are read from shared memory. One 32 KiB buffer (rows up to 8,192
+// f32) keeps six CTAs on an SM, whose folds cover each other's staging: faster than 48 KiB (four CTAs) and than two
+// buffers per CTA. Longer rows take the line path.
+constexpr int64_t kRowStageBytes = 32 * 1024;
 __device__ __forceinline__ void stage_copy16(void* smem, const void* gmem) {
   const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
