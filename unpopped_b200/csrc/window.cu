@@ -326,7 +326,14 @@ __global__ void __launch_bounds__(kThreads) im2col_plane_kernel(const T* __restr
   const int hw = h * w, cols = oh_n * ow_n;
   for (int64_t pl = blockIdx.x; pl < planes; pl += gridDim.x) {
     const T* src = x + pl * hw;
-    for (int i = threadIdx.x; i < hw; i += kThreads) plane[i] = __ldg(src + i);
+    const int bytes = hw * (int)sizeof(T);
+    if ((((uintptr_t)src | (uintptr_t)bytes) & 15) == 0) {  // 16-byte cp.async: every copy of the plane in flight
+      for (int i = threadIdx.x; i < bytes / 16; i += kThreads)
+        stage_copy16(plane_raw + 16 * i, reinterpret_cast<const unsigned char*>(src) + 16 * i);
+      asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    } else {
+      for (int i = threadIdx.x; i < hw; i += kThreads) plane[i] = __ldg(src + i);
+    }
     __syncthreads();
     // a thread decodes its cell (oh, ow) once and writes it in all kh·kw rows (each store coalesced across the warp)
     T* const orow = out + pl * kh * kw * (int64_t)cols;
