@@ -350,7 +350,14 @@ UP_API int up_sm100_row_max_argmax_bf16(const uint16_t* x, int64_t rows, int64_t
  * the element (the first is the identity: 0, INT32_MIN, INT32_MAX); `reverse` runs from the row's end.
  * `carry_in` (device pointer to one int32, or NULL) is combined in front of every row — the carry of a
  * scan sharded over several GPUs. Single-pass decoupled look-back; `workspace` from
- * up_sm100_scan_workspace_bytes, zero-filled before its first use. */
+ * up_sm100_scan_workspace_bytes, zero-filled before its first use (the launches keep it usable: look-back flags
+ * are tagged per launch, and the first launch on a workspace after the 30-bit tag wraps, once in 2^30 launches,
+ * clears the flags with a stream-ordered memset first). Shapes beyond 2^31 - 2 tiles return UP_ERR_UNSUPPORTED
+ * (up_sm100_scan_workspace_bytes then answers SIZE_MAX). Rows that are 16-byte aligned and whole 16-byte chunks
+ * long run as one persistent CTA per SM, which needs every CTA resident at once: a kernel running concurrently
+ * on other streams can keep one off the device, and the scan then returns UP_ERR_DEVICE_TIMEOUT (through
+ * up_sm100_workspace_status) after the wait limit instead of completing. Other rows take tiles from an atomic
+ * ticket and complete whatever runs beside them. */
 UP_API int up_sm100_scan_i32(const int32_t* x, int32_t* y, int64_t rows, int64_t k, int op, int exclusive,
                       int reverse, const int32_t* carry_in, void* workspace, size_t workspace_bytes,
                       void* stream);
@@ -361,12 +368,13 @@ UP_API size_t up_sm100_scan_workspace_bytes(int64_t rows, int64_t k);
  * device array (256 KiB per device), so nothing is allocated or freed. It holds at most 32768 tiles:
  * rows * ceil(k / 8192) <= 32768, one row of up to 2^28 elements. Larger shapes return
  * UP_ERR_UNSUPPORTED with the reason in up_sm100_last_error. The first call on each device does set-up
- * (looks up the array's address, sets the kernel's shared-memory size); make it before any stream
- * capture. Every call on a device shares the array, so calls that overlap in time (other streams, other
- * host threads) race; serialize them. `sync` != 0 waits for the scan and returns UP_ERR_DEVICE_TIMEOUT
- * if its look-back ran out of time. The timeout flag is sticky: the report also covers any earlier
- * unreported call on this device, and reporting clears it. `sync` == 0 returns once the scan is
- * enqueued. */
+ * (looks up the array's address and sets the shared-memory size of every scan kernel variant), and so does
+ * the first call after a cudaDeviceReset (a new context); make that call before any stream capture. Every
+ * call on a device shares the array, so calls that overlap in time (other streams, other host threads)
+ * race; serialize them. `sync` != 0 waits for the scan (cudaStreamSynchronize, which fails under stream
+ * capture: pass 0 there) and returns UP_ERR_DEVICE_TIMEOUT if its look-back ran out of time. The timeout
+ * flag is sticky: the report also covers any earlier unreported call on this device, and reporting clears
+ * it. `sync` == 0 returns once the scan is enqueued. */
 UP_API int up_sm100_scan_i32_noalloc(const int32_t* x, int32_t* y, int64_t rows, int64_t k, int op,
                                      int exclusive, int reverse, const int32_t* carry_in, int sync,
                                      void* stream);
@@ -415,6 +423,9 @@ UP_API void up_sm100_set_wait_limit_ns(uint64_t ns);
 /* When nonzero, the next scan launches make tile 0 withhold its look-back flag, so every other tile's wait
  * runs out: the host-visible error path of a bounded wait, without hanging or faulting the GPU. */
 UP_API void up_sm100_set_test_withhold_flag(int enable);
+/* Makes `next` the 64-bit launch count the next scan uses (its flags carry the low 30 bits). Tests use it to
+ * cross a wrap of the 30-bit tag without 2^30 launches. */
+UP_API void up_sm100_set_test_scan_epoch(uint64_t next);
 /* Number of kernels this library has launched since load (all entry points). */
 UP_API uint64_t up_sm100_launch_count(void);
 /* Last CUDA error text seen by the library (static storage). */

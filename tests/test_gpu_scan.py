@@ -130,3 +130,49 @@ def test_reduce_i32_matches_oracle():
         for op in OPS:
             assert int(ops.reduce_i32(xt, op).item()) == orc.reduce_i32(x, OPS[op]), (n, op)
     assert int(ops.reduce_i32(torch.empty(0, dtype=torch.int32, device="cuda"), "max").item()) == -(2 ** 31)
+
+
+def test_epoch_wrap_clears_flags_left_by_the_earlier_cycle():
+    """The flags carry the low 30 bits of the launch count. A launch exactly 2^30 launches after another one has
+    the same tag, so the first launch on a workspace after the wrap must clear what the earlier cycle left: here
+    a large scan writes flags at tag T, the count jumps to T + 2^30, and a smaller scan on the same workspace
+    must leave every flag it does not write at zero, and every scan stays exact."""
+    L = _lib.load()
+    rng = np.random.default_rng(21)
+    big, small = (1 << 22) + 16, (1 << 20) + 4  # 513 and 129 tiles of 8192
+    ws = torch.zeros(L.up_sm100_scan_workspace_bytes(1, big), dtype=torch.uint8, device="cuda")
+    tag = (1 << 30) - 3
+    xb = torch.from_numpy(rng.integers(-9, 9, size=big).astype(np.int32)).cuda()
+    xs = torch.from_numpy(rng.integers(-9, 9, size=small).astype(np.int32)).cuda()
+    L.up_sm100_set_test_scan_epoch(tag)
+    y = ops.scan(xb, "sum", ws=ws)
+    assert ops.workspace_status(ws) == _lib.UP_OK
+    assert np.array_equal(y.cpu().numpy(), orc.scan_i32(xb.cpu().numpy(), orc.OP_SUM, False))
+    flags = ws[64:].view(torch.int64)
+    assert int((flags != 0).sum()) == 513
+    L.up_sm100_set_test_scan_epoch(tag + (1 << 30))  # the same 30-bit tag, one cycle later
+    y = ops.scan(xs, "max", ws=ws)
+    assert ops.workspace_status(ws) == _lib.UP_OK
+    assert np.array_equal(y.cpu().numpy(), orc.scan_i32(xs.cpu().numpy(), orc.OP_MAX, False))
+    flags = ws[64:].view(torch.int64)
+    assert int((flags[129:] != 0).sum()) == 0  # cleared before the scan, and not written by it
+    for _ in range(2):  # later launches of the new cycle do not clear again, and stay exact
+        y = ops.scan(xb, "sum", True, ws=ws)
+        assert ops.workspace_status(ws) == _lib.UP_OK
+        assert np.array_equal(y.cpu().numpy(), orc.scan_i32(xb.cpu().numpy(), orc.OP_SUM, True))
+
+
+def test_general_form_takes_tiles_by_ticket_and_resets_the_ticket():
+    """Unaligned input takes the one-tile-per-CTA form, whose CTAs take their tiles from a ticket counter in the
+    workspace header; the CTA with the last ticket sets it back to zero for the next launch."""
+    L = _lib.load()
+    rng = np.random.default_rng(8)
+    base = torch.from_numpy(rng.integers(-(2 ** 31), 2 ** 31 - 1, size=(1 << 21) + 3, dtype=np.int64)
+                            .astype(np.int32)).cuda()
+    x = base[1:]  # a 4-byte offset
+    ws = torch.zeros(L.up_sm100_scan_workspace_bytes(1, x.numel()), dtype=torch.uint8, device="cuda")
+    for op, excl, rev in (("sum", False, False), ("min", True, True), ("max", False, True)):
+        y = ops.scan(x, op, excl, rev, ws=ws)
+        assert ops.workspace_status(ws) == _lib.UP_OK
+        assert int(ws[:4].view(torch.int32).item()) == 0
+        assert np.array_equal(y.cpu().numpy(), orc.scan_i32(x.cpu().numpy(), OPS[op], excl, rev))

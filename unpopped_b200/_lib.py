@@ -112,6 +112,7 @@ SIGNATURES = {
     "up_sm100_w4a16_workspace_bytes": ([_I64, _I64, _I64, _I64], _SZ),
     "up_sm100_set_wait_limit_ns": ([_U64], None),
     "up_sm100_set_test_withhold_flag": ([_I], None),
+    "up_sm100_set_test_scan_epoch": ([_U64], None),
     "up_sm100_launch_count": ([], _U64),
     "up_sm100_last_error": ([], ctypes.c_char_p),
 }

@@ -6,10 +6,13 @@
 // plan outside the table below is declined with a typed LowerError, never run some other way.
 #include "common.cuh"
 
+#include <cuda.h>
+
 #include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 namespace up {
 
@@ -38,6 +41,54 @@ int fail_with(int status, const char* text) {
 uint64_t wait_limit_ns() { return g_wait_ns.load(std::memory_order_relaxed); }
 
 int take_withhold_flag() { return g_withhold.exchange(0); }
+
+uint64_t context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static std::once_flag once;
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(p);
+  });
+  if (get_current == nullptr || get_id == nullptr) return 0;
+  cudaFree(nullptr);  // makes the device's primary context current if no context is yet
+  CUcontext c = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&c) != CUDA_SUCCESS || c == nullptr || get_id(c, &id) != CUDA_SUCCESS) return 0;
+  return (uint64_t)id;
+}
+
+cudaError_t ensure_smem_attr(const void* func, int bytes) {
+  struct Entry {
+    const void* func;
+    uint64_t ctx;
+    int bytes;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> done;
+  const uint64_t ctx = context_id();
+  std::lock_guard<std::mutex> lk(mu);
+  if (ctx != 0)
+    for (const Entry& en : done)
+      if (en.func == func && en.ctx == ctx && en.bytes >= bytes) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess || ctx == 0) return e;
+  for (Entry& en : done)
+    if (en.func == func && en.ctx == ctx) {
+      en.bytes = bytes;
+      return e;
+    }
+  done.push_back({func, ctx, bytes});
+  return e;
+}
 
 int sm_count() {
   int dev = 0;

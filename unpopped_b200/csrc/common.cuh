@@ -20,6 +20,13 @@ uint64_t wait_limit_ns();
 int take_withhold_flag();         // returns and clears the scan test hook
 int sm_count();                   // SMs of the current device (cached per device)
 int fail_with(int status, const char* text);  // records `text` as the last error, returns `status`
+// A number that identifies the current CUDA context for the life of the process (cuCtxGetId); 0 when the driver
+// cannot say. A cudaDeviceReset ends the primary context, and the next one gets a new number, so host caches of
+// per-context state (function attributes, symbol addresses, allocations) key on it instead of the device index.
+uint64_t context_id();
+// Raises `func`'s dynamic shared-memory limit to at least `bytes` in the current context. The attribute belongs to
+// the context, so this runs the CUDA call once per context and kernel, and again after a device reset.
+cudaError_t ensure_smem_attr(const void* func, int bytes);
 int row_mean_f32_auto(const float* x, int64_t rows, int64_t cols, int64_t row_stride, int block, float* out,
                       void* stream);  // reduce.cu: the Auto row sum divided by cols
 

@@ -41,6 +41,7 @@ struct Chunk {
 
 struct Streamer {
   bool ready = false;
+  uint64_t ctx = 0;  // the context the slots and streams belong to
   cudaStream_t h2d = nullptr, comp = nullptr, d2h = nullptr;
   int32_t* xs = nullptr;  // kSlots x kSlotElems
   int32_t* ys = nullptr;
@@ -53,8 +54,12 @@ struct Streamer {
 std::mutex g_mu;
 Streamer g_st[64];
 
+// Allocates the slots, streams and events once per device and context. After a cudaDeviceReset the old ones died
+// with their context, so a new context starts from nothing.
 int setup(Streamer& st) {
-  if (st.ready) return UP_OK;
+  const uint64_t ctx = context_id();
+  if (st.ready && (ctx == 0 || st.ctx == ctx)) return UP_OK;
+  st = Streamer{};
   cudaError_t e = cudaSuccess;
   auto ok = [&](cudaError_t r) {
     if (e == cudaSuccess) e = r;
@@ -77,6 +82,7 @@ int setup(Streamer& st) {
   ok(cudaDeviceSynchronize());
   if (e != cudaSuccess) return cuda_status(e);
   st.ready = true;
+  st.ctx = ctx;
   return UP_OK;
 }
 

@@ -871,20 +871,10 @@ int launch_f32_cols(const float* x, int64_t outer, int64_t rows, int64_t cols, i
   if (gx > 0x7fffffff) return UP_ERR_UNSUPPORTED;
   const bool vec = aligned(x, 16) && cols % 4 == 0 && row_stride % 4 == 0 && xb % 4 == 0;
   if (summing && block > 1 && !(block >= 64 && vec)) {
-    static std::mutex mu;
-    static bool attr_set[64] = {false};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    const int bytes = (int)((size_t)kDocMaxB * 32 * sizeof(double));
+    cudaError_t e = ensure_smem_attr((const void*)col_sum_f32_doc_kernel<true>, bytes);
+    if (e == cudaSuccess) e = ensure_smem_attr((const void*)col_sum_f32_doc_kernel<false>, bytes);
     if (e != cudaSuccess) return cuda_status(e);
-    std::lock_guard<std::mutex> lk(mu);
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-      const int bytes = (int)((size_t)kDocMaxB * 32 * sizeof(double));
-      e = cudaFuncSetAttribute(col_sum_f32_doc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-      if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(col_sum_f32_doc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-      if (e != cudaSuccess) return cuda_status(e);
-      if (dev >= 0 && dev < 64) attr_set[dev] = true;
-    }
   }
   const bool mean = op == UP_OP_MEAN;
   for (int64_t b0 = 0; b0 < outer; b0 += kMaxGridZ) {

@@ -321,13 +321,12 @@ int launch_held(const float* x, int64_t rows, int64_t cols, int64_t stride, int 
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
   int fit = 0;
+  e = ensure_smem_attr((const void*)row_reduce_f32_held_kernel<FORM, L, WHOLE>, (int)smem);
+  if (e != cudaSuccess) return cuda_status(e);
   {
     std::lock_guard<std::mutex> lk(mu);
     if (dev >= 0 && dev < 64) fit = per_sm[dev];
     if (fit == 0) {
-      e = cudaFuncSetAttribute(row_reduce_f32_held_kernel<FORM, L, WHOLE>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return cuda_status(e);
       e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&fit, row_reduce_f32_held_kernel<FORM, L, WHOLE>, kThreads,
                                                         smem);
       if (e != cudaSuccess) return cuda_status(e);

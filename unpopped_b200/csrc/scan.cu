@@ -16,15 +16,18 @@
 //
 // Look-back flags: one 64-bit word per tile = epoch(30) | status(2) | value(32), written and read with
 // relaxed gpu-scope atomics (the value travels inside the flag word). Status: 1 = aggregate of this tile,
-// 2 = inclusive prefix through this tile, 3 = aborted. The epoch is a per-launch number chosen on the host,
-// so flags of earlier launches are never mistaken for this one's and the workspace needs zero-filling only
-// once. Every wait is bounded by a globaltimer deadline; a wait that runs out sets the workspace error word
-// and publishes "aborted", which the tiles that wait on it propagate at once.
+// 2 = inclusive prefix through this tile, 3 = aborted. The epoch is the low 30 bits of a per-launch 64-bit
+// count kept on the host, so flags of earlier launches are never mistaken for this one's and the workspace
+// needs zero-filling only once. When the count passes a multiple of 2^30 the tags repeat: the first launch
+// on each workspace after that clears its flags (a stream-ordered memset) before it runs. Every wait is
+// bounded by a globaltimer deadline; a wait that runs out sets the workspace error word and publishes
+// "aborted", which the tiles that wait on it propagate at once.
 #include "common.cuh"
 #include "tc.cuh"
 
 #include <atomic>
 #include <mutex>
+#include <vector>
 
 namespace up {
 
@@ -36,8 +39,9 @@ constexpr int kTileBytes = kScanTile * 4;                        // 64 KiB
 constexpr size_t kScanSmem = kTileBytes;
 
 struct ScanHeader {
-  uint32_t reserved0, reserved1, reserved2;
-  uint32_t error;  // byte 12: set when a bounded wait ran out
+  uint32_t ticket;  // the general form's next tile; the CTA that takes the last tile sets it back to 0
+  uint32_t reserved1, reserved2;
+  uint32_t error;   // byte 12: set when a bounded wait ran out
   uint32_t pad[12];
 };
 static_assert(sizeof(ScanHeader) == 64, "header is one 64-byte line");
@@ -112,8 +116,10 @@ struct TileView {
 // is read with element loads into shared memory in scan order; in shared memory, warp w owns 2048 elements
 // and lane l handles the 16-byte chunks i*32 + l (i = 0..15), which keeps every access conflict-free.
 // Pass 1 folds the tile; the aggregate goes out as a look-back flag; warp 0 walks back 32 predecessors
-// per step until an inclusive prefix; pass 2 rescans with the prefix and writes the result. CTAs are
-// dispatched in index order, so a tile only ever waits on tiles whose CTAs have started.
+// per step until an inclusive prefix; pass 2 rescans with the prefix and writes the result. A CTA takes its
+// tile from a ticket counter in the workspace header, not from blockIdx.x: tickets go out in the order CTAs
+// start, so a tile only ever waits on tiles whose CTAs are already running, whatever order the hardware
+// dispatches CTAs in and however many SMs other work holds.
 template <int OP>
 __global__ void __launch_bounds__(kScanThreads) scan_i32_kernel(const int32_t* __restrict__ x,
                                                                 int32_t* __restrict__ y, int64_t k,
@@ -126,9 +132,16 @@ __global__ void __launch_bounds__(kScanThreads) scan_i32_kernel(const int32_t* _
   __shared__ int32_t s_warp_tot[kScanThreads / 32];
   __shared__ int32_t s_prefix;
   __shared__ int s_abort;
+  __shared__ uint32_t s_ticket;
 
+  if (threadIdx.x == 0) {
+    const uint32_t tk = atomicAdd(&hdr->ticket, 1u);
+    if (tk == gridDim.x - 1) atomicExch(&hdr->ticket, 0u);  // every CTA has its tile: ready for the next launch
+    s_ticket = tk;
+  }
+  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t t = blockIdx.x;
+  const int64_t t = s_ticket;
   const int64_t row = t / tiles_per_row;
   const int64_t q = t - row * tiles_per_row;
   const int64_t lo = q * kScanTile;
@@ -274,8 +287,12 @@ __global__ void __launch_bounds__(kScanThreads) scan_i32_kernel(const int32_t* _
 //    it reads is an aggregate, which depends only on its own tile's data: there is no chain of prefixes across
 //    CTAs, and this warp runs ahead of the rescans as far as the aggregates allow, so the round trips to L2
 //    overlap the scanning instead of stalling it.
-// Forward progress: every CTA is resident (one per SM, grid <= SMs); a tile's aggregate needs only its data,
-// and a stage is refilled only after its tile's rescan, whose prefix needs aggregates of smaller tiles only.
+// Forward progress: every CTA is resident (one per SM, grid <= SMs; the host checks that one CTA fits on an SM
+// before it launches this form); a tile's aggregate needs only its data, and a stage is refilled only after its
+// tile's rescan, whose prefix needs aggregates of smaller tiles only. Work that holds SMs while this kernel runs
+// (a concurrent kernel, a context limited to part of the GPU) can keep a CTA off the device until the others
+// finish; they cannot finish without it, so their bounded waits run out and the launch reports
+// UP_ERR_DEVICE_TIMEOUT with a partly written output, not a hang.
 // Aborts: a wait that runs out (or an aborted tile in a window) makes the CTA publish "aborted" for its
 // remaining tiles, stop loading, let the loads in flight land, and exit; the error word is set.
 constexpr int kQTile = 8192;                        // elements per tile
@@ -683,16 +700,67 @@ __global__ void __launch_bounds__(kQThreads, 1)
   if (!ok && threadIdx.x == 0) abort_from(j);
 }
 
-static std::atomic<uint32_t> g_epoch{0};
+// ---- per-launch epochs ----
+//
+// The flags carry the low 30 bits of a 64-bit launch count. Within one span of 2^30 launches (a "cycle") the tags
+// are distinct, so a flag left by an earlier launch never matches a later one. Across a cycle boundary they
+// repeat, so the first launch on a workspace in each cycle after the first clears the workspace's flags first.
+// Workspaces cleared in the current cycle are remembered by address and size (a larger size clears again).
+static std::mutex g_epoch_mu;
+static uint64_t g_epoch64 = 0;
+static uint64_t g_epoch_cycle = 0;
+struct ClearedWs {
+  const void* ws;
+  size_t bytes;
+};
+static std::vector<ClearedWs> g_cleared;
+
+static cudaError_t launch_epoch(void* workspace, size_t workspace_bytes, cudaStream_t s, uint32_t* epoch) {
+  std::lock_guard<std::mutex> lk(g_epoch_mu);
+  const uint64_t e = ++g_epoch64;
+  const uint64_t cycle = e >> 30;
+  *epoch = (uint32_t)(e & 0x3fffffffu);
+  if (cycle != g_epoch_cycle) {
+    g_epoch_cycle = cycle;
+    g_cleared.clear();
+  }
+  if (cycle == 0) return cudaSuccess;  // the caller's zero-fill holds no tag of this cycle
+  for (const ClearedWs& c : g_cleared)
+    if (c.ws == workspace && c.bytes >= workspace_bytes) return cudaSuccess;
+  // the flags only: the header keeps an unreported error word, and its ticket is already zero
+  const cudaError_t r = cudaMemsetAsync(static_cast<char*>(workspace) + sizeof(ScanHeader), 0,
+                                        workspace_bytes - sizeof(ScanHeader), s);
+  if (r != cudaSuccess) return r;
+  for (ClearedWs& c : g_cleared)
+    if (c.ws == workspace) {
+      c.bytes = workspace_bytes;
+      return cudaSuccess;
+    }
+  g_cleared.push_back({workspace, workspace_bytes});
+  return cudaSuccess;
+}
+
+// rows x ceil(k / tile) into *out when it is at most `cap`, without overflowing on any int64 extents.
+static bool tile_count(int64_t rows, int64_t k, int64_t tile, int64_t cap, int64_t* out) {
+  if (rows <= 0 || k <= 0) {
+    *out = 0;
+    return true;
+  }
+  const int64_t per_row = (k - 1) / tile + 1;
+  if (per_row > cap / rows) return false;
+  *out = rows * per_row;
+  return true;
+}
+constexpr int64_t kMaxScanTiles = 0x7ffffffeLL;  // a grid dimension and a 32-bit ticket
 
 }  // namespace up
 
 using namespace up;
 
 extern "C" size_t up_sm100_scan_workspace_bytes(int64_t rows, int64_t k) {
-  if (rows <= 0 || k <= 0) return sizeof(ScanHeader);
   // one flag per tile of the persistent form (8192 elements); the one-tile-per-CTA form needs fewer
-  const int64_t tiles = rows * ((k + kQTile - 1) / kQTile);
+  int64_t tiles = 0;
+  if (!tile_count(rows, k, kQTile, kMaxScanTiles, &tiles)) return SIZE_MAX;  // refused by up_sm100_scan_i32
   return sizeof(ScanHeader) + (size_t)tiles * sizeof(uint64_t);
 }
 
@@ -700,19 +768,8 @@ template <int OP>
 static cudaError_t launch_scan(unsigned grid, cudaStream_t s, const int32_t* x, int32_t* y, int64_t k, int64_t tpr,
                                int exclusive, int reverse, const int32_t* carry_in, ScanHeader* hdr, uint64_t* flags,
                                uint32_t epoch, uint64_t wns, int withhold) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  cudaError_t e = ensure_smem_attr((const void*)scan_i32_kernel<OP>, (int)kScanSmem);
   if (e != cudaSuccess) return e;
-  static std::mutex mu;
-  static bool attr_set[64] = {false};
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-      e = cudaFuncSetAttribute(scan_i32_kernel<OP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kScanSmem);
-      if (e != cudaSuccess) return e;
-      if (dev >= 0 && dev < 64) attr_set[dev] = true;
-    }
-  }
   scan_i32_kernel<OP><<<grid, kScanThreads, kScanSmem, s>>>(x, y, k, tpr, exclusive, reverse, carry_in, hdr, flags,
                                                             epoch, wns, withhold);
   return cudaGetLastError();
@@ -723,20 +780,8 @@ static cudaError_t launch_scan_persist_dir(unsigned grid, cudaStream_t s, const 
                                            int64_t tpr, int64_t tiles, int exclusive, const int32_t* carry_in,
                                            ScanHeader* hdr, uint64_t* flags, uint32_t epoch, uint64_t wns,
                                            int withhold) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  cudaError_t e = ensure_smem_attr((const void*)scan_i32_persist_kernel<OP, REV>, (int)kQSmem);
   if (e != cudaSuccess) return e;
-  static std::mutex mu;
-  static bool attr_set[64] = {false};
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-      e = cudaFuncSetAttribute(scan_i32_persist_kernel<OP, REV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)kQSmem);
-      if (e != cudaSuccess) return e;
-      if (dev >= 0 && dev < 64) attr_set[dev] = true;
-    }
-  }
   scan_i32_persist_kernel<OP, REV><<<grid, kQThreads, kQSmem, s>>>(x, y, k, tpr, tiles, exclusive, carry_in, hdr,
                                                                    flags, epoch, wns, withhold);
   return cudaGetLastError();
@@ -753,6 +798,60 @@ static cudaError_t launch_scan_persist(unsigned grid, cudaStream_t s, const int3
                                                       epoch, wns, withhold);
 }
 
+namespace up {
+// Sets every scan kernel's shared-memory limit in the current context, and answers whether one CTA of the
+// persistent form fits on an SM (it needs 197 KiB of shared memory and 576 threads; a context whose carveout or
+// register budget is smaller cannot hold it, and the scan then takes the general form).
+static cudaError_t scan_setup(bool* persistent_fits) {
+  const void* general[3] = {(const void*)scan_i32_kernel<UP_OP_SUM>, (const void*)scan_i32_kernel<UP_OP_MAX>,
+                            (const void*)scan_i32_kernel<UP_OP_MIN>};
+  const void* persist[6] = {
+      (const void*)scan_i32_persist_kernel<UP_OP_SUM, false>, (const void*)scan_i32_persist_kernel<UP_OP_SUM, true>,
+      (const void*)scan_i32_persist_kernel<UP_OP_MAX, false>, (const void*)scan_i32_persist_kernel<UP_OP_MAX, true>,
+      (const void*)scan_i32_persist_kernel<UP_OP_MIN, false>, (const void*)scan_i32_persist_kernel<UP_OP_MIN, true>};
+  for (const void* f : general) {
+    const cudaError_t e = ensure_smem_attr(f, (int)kScanSmem);
+    if (e != cudaSuccess) return e;
+  }
+  bool fits = true;
+  for (const void* f : persist) {
+    cudaError_t e = ensure_smem_attr(f, (int)kQSmem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, f, kQThreads, kQSmem);
+    if (e != cudaSuccess) return e;
+    fits = fits && per_sm >= 1;
+  }
+  *persistent_fits = fits;
+  return cudaSuccess;
+}
+
+// scan_setup once per context: whether the persistent form can run here.
+static int persistent_form_fits(bool* fits) {
+  static std::mutex mu;
+  static uint64_t ctx_done[64] = {0};
+  static bool fit[64] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  const uint64_t ctx = context_id();
+  std::lock_guard<std::mutex> lk(mu);
+  if (dev >= 0 && dev < 64 && ctx != 0 && ctx_done[dev] == ctx) {
+    *fits = fit[dev];
+    return UP_OK;
+  }
+  bool f = false;
+  e = scan_setup(&f);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (dev >= 0 && dev < 64) {
+    ctx_done[dev] = ctx;
+    fit[dev] = f;
+  }
+  *fits = f;
+  return UP_OK;
+}
+}  // namespace up
+
 extern "C" int up_sm100_scan_i32(const int32_t* x, int32_t* y, int64_t rows, int64_t k, int op, int exclusive,
                                  int reverse, const int32_t* carry_in, void* workspace, size_t workspace_bytes,
                                  void* stream) {
@@ -761,21 +860,26 @@ extern "C" int up_sm100_scan_i32(const int32_t* x, int32_t* y, int64_t rows, int
   if (rows == 0 || k == 0) return UP_OK;
   UP_CHECK_ARG(x != nullptr && y != nullptr && workspace != nullptr);
   UP_CHECK_ARG(aligned(workspace, 64));
-  const int64_t tpr = (k + kScanTile - 1) / kScanTile;
-  const int64_t tiles = rows * tpr;
-  if (rows * ((k + kQTile - 1) / kQTile) >= (int64_t)0x7fffffff) return UP_ERR_UNSUPPORTED;
+  int64_t qtiles = 0, tiles = 0;
+  if (!tile_count(rows, k, kQTile, kMaxScanTiles, &qtiles) || !tile_count(rows, k, kScanTile, kMaxScanTiles, &tiles))
+    return fail_with(UP_ERR_UNSUPPORTED, "scan_i32: more than 2^31 - 2 tiles");
   if (workspace_bytes < up_sm100_scan_workspace_bytes(rows, k)) return UP_ERR_INVALID;
+  const int64_t tpr = tiles / rows;
   auto* hdr = static_cast<ScanHeader*>(workspace);
   auto* flags = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + sizeof(ScanHeader));
+  bool fits = false;
+  int st = persistent_form_fits(&fits);
+  if (st != UP_OK) return st;
   // bulk copies need 16-byte aligned rows of whole 16-byte chunks
-  const int bulk = aligned(x, 16) && aligned(y, 16) && (k % 4 == 0);
-  const int withhold = take_withhold_flag();
-  const uint32_t epoch = ++g_epoch;
+  const int bulk = fits && aligned(x, 16) && aligned(y, 16) && (k % 4 == 0);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t epoch = 0;
+  cudaError_t e = launch_epoch(workspace, workspace_bytes, s, &epoch);
+  if (e != cudaSuccess) return cuda_status(e);
+  const int withhold = take_withhold_flag();
   const uint64_t wns = wait_limit_ns();
-  cudaError_t e;
   if (bulk) {
-    const int64_t qtpr = (k + kQTile - 1) / kQTile, qtiles = rows * qtpr;
+    const int64_t qtpr = qtiles / rows;
     int64_t grid = sm_count();
     if (grid > kQMaxGrid) grid = kQMaxGrid;
     if (grid > qtiles) grid = qtiles;
@@ -805,6 +909,11 @@ extern "C" int up_sm100_scan_i32(const int32_t* x, int32_t* y, int64_t rows, int
   return cuda_status(e);
 }
 
+extern "C" void up_sm100_set_test_scan_epoch(uint64_t next) {
+  std::lock_guard<std::mutex> lk(g_epoch_mu);
+  g_epoch64 = next - 1;
+}
+
 extern "C" int up_sm100_workspace_status(void* workspace, void* stream) {
   UP_CHECK_ARG(workspace != nullptr);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -827,26 +936,35 @@ extern "C" int up_sm100_workspace_status(void* workspace, void* stream) {
 //
 // The look-back flags and the error word live in one file-scope device array instead of a caller's
 // workspace. Each device holds its own copy of the array, zero from module load. What must be zero is
-// the error word, and it is cleared again whenever a timeout is reported. The flags are epoch-tagged,
-// so they never need clearing. Every call on a device uses the same array: calls that overlap in time
-// race, through concurrent streams or host threads, and must be serialized by the caller.
+// the error word, and it is cleared again whenever a timeout is reported; the flags are epoch-tagged
+// (and cleared by the launch that follows a wrap of the tag, as for any workspace). Every call on a device
+// uses the same array: calls that overlap in time race, through concurrent streams or host threads, and
+// must be serialized by the caller.
 namespace up {
 constexpr int64_t kNoAllocMaxTiles = 32768;  // rows x ceil(k / 8192) tiles, e.g. one row of 2^28 elements
 static __device__ __align__(256) uint64_t g_noalloc_scratch[sizeof(ScanHeader) / 8 + kNoAllocMaxTiles];
 static std::mutex g_noalloc_mu;
 static void* g_noalloc_ptr[64] = {};
+static uint64_t g_noalloc_ctx[64] = {};
 
-// The device address of this device's copy of the scratch, looked up once per device (with it current).
-static cudaError_t noalloc_scratch(int dev, void** out) {
+// Set-up, once per device and context, with that device current: the device address of this device's copy of
+// the scratch, and every scan kernel's shared-memory limit. A cudaDeviceReset ends the context the address
+// belongs to; the next call sees a new context and does the set-up again.
+static int noalloc_setup(int dev, void** out) {
+  const uint64_t ctx = context_id();
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  if (ctx == 0 || g_noalloc_ctx[dev] != ctx || g_noalloc_ptr[dev] == nullptr) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess) return cuda_status(e);
+    bool fits = false;
+    const int st = persistent_form_fits(&fits);
+    if (st != UP_OK) return st;
     g_noalloc_ptr[dev] = p;
+    g_noalloc_ctx[dev] = ctx;
   }
   *out = g_noalloc_ptr[dev];
-  return cudaSuccess;
+  return UP_OK;
 }
 }  // namespace up
 
@@ -856,8 +974,8 @@ extern "C" int up_sm100_scan_i32_noalloc(const int32_t* x, int32_t* y, int64_t r
   UP_CHECK_ARG(rows >= 0 && k >= 0);
   if (op != UP_OP_SUM && op != UP_OP_MAX && op != UP_OP_MIN) return UP_ERR_UNSUPPORTED;
   if (rows == 0 || k == 0) return UP_OK;
-  const int64_t tpr = (k + kQTile - 1) / kQTile;
-  if (rows > kNoAllocMaxTiles || rows * tpr > kNoAllocMaxTiles)
+  int64_t tiles = 0;
+  if (!tile_count(rows, k, kQTile, kNoAllocMaxTiles, &tiles))
     return fail_with(UP_ERR_UNSUPPORTED,
                      "up_sm100_scan_i32_noalloc: rows * ceil(k / 8192) exceeds the built-in scratch's 32768 "
                      "tiles; use up_sm100_scan_i32 with a workspace");
@@ -866,10 +984,10 @@ extern "C" int up_sm100_scan_i32_noalloc(const int32_t* x, int32_t* y, int64_t r
   if (e != cudaSuccess) return cuda_status(e);
   if (dev < 0 || dev >= 64) return fail_with(UP_ERR_UNSUPPORTED, "up_sm100_scan_i32_noalloc: device index >= 64");
   void* scratch = nullptr;
-  e = noalloc_scratch(dev, &scratch);
-  if (e != cudaSuccess) return cuda_status(e);
-  const int st = up_sm100_scan_i32(x, y, rows, k, op, exclusive, reverse, carry_in, scratch,
-                                   sizeof(g_noalloc_scratch), stream);
+  int st = noalloc_setup(dev, &scratch);
+  if (st != UP_OK) return st;
+  st = up_sm100_scan_i32(x, y, rows, k, op, exclusive, reverse, carry_in, scratch, sizeof(g_noalloc_scratch),
+                         stream);
   if (st != UP_OK || !sync) return st;
   return up_sm100_workspace_status(scratch, stream);
 }

@@ -736,19 +736,9 @@ extern "C" int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, cons
     if (sr != CUDA_SUCCESS) return fail_with(UP_ERR_CUDA, "cuTensorMapEncodeTiled refused the scale tensor map");
   }
   {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    cudaError_t e = ensure_smem_attr((const void*)w4a16_kernel<1>, (int)kSmemBytes);
+    if (e == cudaSuccess) e = ensure_smem_attr((const void*)w4a16_kernel<2>, (int)kSmemBytes);
     if (e != cudaSuccess) return cuda_status(e);
-    static std::mutex mu;
-    static bool attr_set[64] = {false};
-    std::lock_guard<std::mutex> lk(mu);
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-      e = cudaFuncSetAttribute(w4a16_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
-      if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(w4a16_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
-      if (e != cudaSuccess) return cuda_status(e);
-      if (dev >= 0 && dev < 64) attr_set[dev] = true;
-    }
   }
   auto* base = static_cast<char*>(workspace);
   auto* hdr = reinterpret_cast<WsHeader*>(base);

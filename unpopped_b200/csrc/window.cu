@@ -452,24 +452,13 @@ extern "C" int up_sm100_im2col(const void* x, int elem_bytes, int64_t n, int64_t
   const int g = win::grid_for(n * c * kh * kw);
   const int64_t plane_bytes = h * w * (int64_t)elem_bytes;
   if (plane_bytes <= win::kPlaneBytes && oh * ow <= 0x7fffffffLL && kh * kw <= 0x7fff) {
-    static std::mutex mu;
-    static bool attr_set[64][4] = {{false}};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    const int mx = (int)win::kPlaneBytes;
+    const cudaError_t e =
+        elem_bytes == 1   ? ensure_smem_attr((const void*)win::im2col_plane_kernel<uint8_t>, mx)
+        : elem_bytes == 2 ? ensure_smem_attr((const void*)win::im2col_plane_kernel<uint16_t>, mx)
+        : elem_bytes == 4 ? ensure_smem_attr((const void*)win::im2col_plane_kernel<uint32_t>, mx)
+                          : ensure_smem_attr((const void*)win::im2col_plane_kernel<unsigned long long>, mx);
     if (e != cudaSuccess) return cuda_status(e);
-    const int which = elem_bytes == 1 ? 0 : elem_bytes == 2 ? 1 : elem_bytes == 4 ? 2 : 3;
-    {
-      std::lock_guard<std::mutex> lk(mu);
-      if (dev >= 0 && dev < 64 && !attr_set[dev][which]) {
-        const int mx = (int)win::kPlaneBytes;
-        e = which == 0 ? cudaFuncSetAttribute(win::im2col_plane_kernel<uint8_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx)
-          : which == 1 ? cudaFuncSetAttribute(win::im2col_plane_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx)
-          : which == 2 ? cudaFuncSetAttribute(win::im2col_plane_kernel<uint32_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx)
-                       : cudaFuncSetAttribute(win::im2col_plane_kernel<unsigned long long>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
-        if (e != cudaSuccess) return cuda_status(e);
-        attr_set[dev][which] = true;
-      }
-    }
     const int gp = win::grid_for(n * c);
 #define UP_I2P(T) \
   win::im2col_plane_kernel<T><<<gp, win::kThreads, (size_t)plane_bytes, s>>>(static_cast<const T*>(x), n * c, (int)h, (int)w, kh, kw, sh, sw, ph, pw, dh, dw, (int)oh, (int)ow, static_cast<T*>(out))
