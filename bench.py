@@ -366,6 +366,127 @@ def cpu_scan_baseline():
             "sample": f"full config: 2^28 int32 inclusive add-scan, serial C restatement of eval_scan, {reps} passes"}
 
 
+def _best_time(fn, min_s=0.4, max_reps=5):
+    """Best wall time of `fn` over a few repetitions (at least two, or `min_s` seconds)."""
+    best, reps, t_all = float("inf"), 0, time.perf_counter()
+    while reps < 2 or (time.perf_counter() - t_all < min_s and reps < max_reps):
+        t0 = time.perf_counter()
+        fn()
+        best = min(best, time.perf_counter() - t0)
+        reps += 1
+    return best
+
+
+def cpu_baselines():
+    """Each config lift's CPU baselines, timed on this host on a bounded sample of the config's own workload
+    (seeded, same distributions): the oracle restatement on 1 core and with OpenMP on every core, and the serial C
+    the reference's C99 emitter writes for the lift (oracle/c99_forms.c) on 1 core: the serial lift, and for the
+    row sum and the scan also the launched lift's serialized thread loop. GB/s over the algorithmic bytes of the
+    sample, as on the GPU. Returns ({config: {baseline: GB/s}}, {config: sample description}, threads)."""
+    import numpy as np
+    import torch
+
+    import oracle as orc
+    from unpopped_b200 import workloads as wl
+
+    T = orc.max_threads()
+    res, samples = {}, {}
+
+    def gbs(nbytes, secs):
+        return round(nbytes / secs / 1e9, 2)
+
+    # config 1: the full 8192 x 8192 row sum
+    x = wl.rowsum_input(device="cpu").numpy()
+    nb = wl.rowsum_bytes()
+    res["cfg1"] = {"oracle_1c": gbs(nb, _best_time(lambda: orc.row_sum_f32(x, 1))),
+                   f"omp_{T}c": gbs(nb, _best_time(lambda: orc.row_sum_f32(x, T))),
+                   "c99_1c": gbs(nb, _best_time(lambda: orc.c99_row_sum(x))),
+                   "c99_launched_1c": gbs(nb, _best_time(lambda: orc.c99_row_sum(x, 256)))}
+    samples["cfg1"] = "full 8192x8192 f32; c99_launched = the block-tree lift at B=256, serialized"
+    del x
+    # config 2: 2^26 of the 2^28 scan elements
+    n = 1 << 26
+    x = wl.scan_input(n=n, device="cpu").numpy()
+    y = np.empty_like(x)
+    nb = wl.scan_bytes(n)
+    res["cfg2"] = {"oracle_1c": gbs(nb, _best_time(lambda: orc.lib().orc_scan_i32(
+                       orc._p(x), orc._p(y), 1, n, orc.OP_SUM, 0, 0, 0, 1))),
+                   f"omp_{T}c": gbs(nb, _best_time(lambda: orc.scan_i32_chunked(x, orc.OP_SUM, False, T))),
+                   "c99_1c": gbs(nb, _best_time(lambda: orc.c99_scan(x, orc.OP_SUM, False))),
+                   "c99_launched_1c": gbs(nb, _best_time(lambda: orc.c99_scan(x, orc.OP_SUM, False, 1024)))}
+    samples["cfg2"] = "2^26 int32 inclusive add (1/4 of the config); c99_launched = the 3-phase lift at B=1024"
+    del x, y
+    # config 3: the first 2^20 of the 2^24 Zipf ids into the full 2^20 x 256 table
+    table, ids = wl.gather_inputs(device="cpu")
+    tb = table.view(torch.int16).numpy().view(np.uint16)
+    ids = ids[:1 << 20].contiguous().numpy()
+    comp, _, _ = wl.gather_bytes(torch.from_numpy(ids))
+    out = np.zeros((ids.size, 256), np.uint16)
+    res["cfg3"] = {"oracle_1c": gbs(comp, _best_time(lambda: orc.gather_rows(tb, ids, orc.OOB_ZERO_FILL, out, 1))),
+                   f"omp_{T}c": gbs(comp, _best_time(lambda: orc.gather_rows(tb, ids, orc.OOB_ZERO_FILL, out, T))),
+                   "c99_1c": gbs(comp, _best_time(lambda: orc.c99_gather(tb, ids, orc.OOB_ZERO_FILL, out)))}
+    samples["cfg3"] = "2^20 of the 2^24 Zipf ids, full table; compulsory bytes of the sample"
+    del table, tb, ids, out
+    # config 4: 2048 of the 32768 rows
+    rows = 2048
+    xb = wl.argmax_input(rows=rows, device="cpu").view(torch.int16).numpy().view(np.uint16)
+    nb = wl.argmax_bytes(rows=rows)
+    res["cfg4"] = {"oracle_1c": gbs(nb, _best_time(lambda: orc.row_max_argmax_bf16(xb, 1))),
+                   f"omp_{T}c": gbs(nb, _best_time(lambda: orc.row_max_argmax_bf16(xb, T))),
+                   "c99_1c": gbs(nb, _best_time(lambda: orc.c99_row_max_argmax(xb)))}
+    samples["cfg4"] = "2048 of the 32768 rows x 32000 bf16"
+    del xb
+    # config 5: 256 of the 28672 weight rows (all 16 activation rows, full K)
+    nr = 256
+    d = wl.w4a16_inputs(n=nr, device="cpu")
+    w = d.w_packed.numpy()
+    sc = d.scale.view(torch.int16).numpy().view(np.uint16)
+    xa = d.x.view(torch.int16).numpy().view(np.uint16)
+    nb = wl.w4a16_bytes(n=nr)
+    res["cfg5"] = {"oracle_1c": gbs(nb, _best_time(lambda: orc.w4a16(w, sc, xa, d.m, nr, d.k, d.group, 1))),
+                   f"omp_{T}c": gbs(nb, _best_time(lambda: orc.w4a16(w, sc, xa, d.m, nr, d.k, d.group, T))),
+                   "c99_1c": gbs(nb, _best_time(lambda: orc.c99_w4a16(w, sc, xa, d.m, nr, d.k, d.group)))}
+    samples["cfg5"] = "256 of the 28672 weight rows, M=16, K=8192; the oracle's products are exact f64"
+    return res, samples, T
+
+
+# The config lifts, by their names in `bench_lifts`, in the order of BASELINE.json's configs.
+CONFIG_LIFTS = {
+    "rowsum_f32_8192x8192": ("cfg1_rowsum_f32", "cfg1"),
+    "rowsum_f32_auto_f64order_B1024": ("cfg1_rowsum_auto_B1024", None),
+    "scan_excl_add_i32_2p28": ("cfg2_scan_excl_add", None),
+    "scan_incl_max_i32_2p28": ("cfg2_scan_incl_max", None),
+    "gather_rows_bf16_zipf1.1": ("cfg3_gather_zipf", "cfg3"),
+    "max_argmax_bf16_32768x32000": ("cfg4_max_argmax", "cfg4"),
+    "dequant_i4_g128_bf16_28672x8192": ("cfg5_dequant", None),
+    "w4a16_gemm_16x28672x8192_g128": ("cfg5_w4a16", "cfg5"),
+}
+
+
+def config_block(lifts, head, cpu_cfg):
+    """The five configurations, compact, for the end of the JSON line: GB/s (aggregate), ms per step, fraction of
+    measured HBM per GPU, and the CPU baselines (GB/s) where measured."""
+    out = {}
+
+    def put(key, rec, cfg):
+        e = {"GBps": rec["value"], "ms": rec["ms_per_step"], "frac": rec["frac_of_hbm"]}
+        if "tflops" in rec:
+            e["TFLOPs"] = rec["tflops"]
+        if cfg and cfg in cpu_cfg:
+            e["cpu"] = cpu_cfg[cfg]
+        out[key] = e
+
+    for name in ("rowsum_f32_8192x8192", "rowsum_f32_auto_f64order_B1024"):
+        if name in lifts:
+            put(CONFIG_LIFTS[name][0], lifts[name], CONFIG_LIFTS[name][1])
+    put("cfg2_scan_incl_add", dict(value=head["value"], ms_per_step=head["ms_per_step"],
+                                   frac_of_hbm=head["frac_of_hbm"]), "cfg2")
+    for name, (key, cfg) in CONFIG_LIFTS.items():
+        if name in lifts and not key.startswith("cfg1"):
+            put(key, lifts[name], cfg)
+    return out
+
+
 def scan_config(world):
     """The headline workload's `config`, shared by both arms of the bench."""
     return {"workload": "configs[1]: inclusive add-scan over 2^28 int32 per GPU (1 GiB in, 1 GiB out)"
@@ -564,6 +685,9 @@ def main():
     clocks = clk.stop()
 
     cpu = cpu_scan_baseline() if (ctx.rank == 0 and ctx.world == 1) else None
+    cpu_cfg, cpu_samples, cpu_threads = ({}, {}, None)
+    if ctx.rank == 0 and ctx.world == 1 and args.lifts == "all":
+        cpu_cfg, cpu_samples, cpu_threads = cpu_baselines()
     traffic = ncu_traffic("scan_i32_persist_kernel_incl_add.md")
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": ctx.world, "steps": K, "warmup": W,
@@ -578,10 +702,16 @@ def main():
         "gpu_launches": launches,
         "clocks": clocks,
         "cpu_baseline": cpu,
-        "lifts": lifts,
     }
+    if lifts:
+        line["lifts"] = {k: [v["value"], v["frac_of_hbm"]] for k, v in lifts.items() if k not in CONFIG_LIFTS}
+        line["lifts_unit"] = "[GB/s aggregate, fraction of measured HBM per GPU]"
+        if cpu_samples:
+            line["cpu_samples"] = dict(cpu_samples, threads=cpu_threads, unit="GB/s of the sample's algorithmic bytes")
+        head = {"value": round(value, 1), "ms_per_step": round(ms, 4), "frac_of_hbm": round(achieved / hbm, 4)}
+        line["configs"] = config_block(lifts, head, cpu_cfg)
     if ctx.rank == 0:
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line, separators=(",", ":")), flush=True)
     if ctx.world > 1:
         ctx.barrier()
         ctx.dist.destroy_process_group()

@@ -24,9 +24,8 @@ _lib = None
 
 def build(force: bool = False) -> str:
     """Compile liborc.so with the committed Makefile (gcc, strict FP, OpenMP)."""
-    if force or not os.path.exists(_LIB_PATH) or (
-        os.path.getmtime(_LIB_PATH) < os.path.getmtime(os.path.join(_HERE, "up_oracle.c"))
-    ):
+    srcs = [os.path.join(_HERE, f) for f in ("up_oracle.c", "c99_forms.c", "Makefile")]
+    if force or not os.path.exists(_LIB_PATH) or any(os.path.getmtime(_LIB_PATH) < os.path.getmtime(f) for f in srcs):
         subprocess.run(["make", "-s", "-C", _HERE, "liborc.so"], check=True)
     return _LIB_PATH
 
@@ -75,6 +74,18 @@ def lib():
         L.orc_i4_value.argtypes = [P, I64]
         L.orc_i4_value.restype = I
         L.orc_max_threads.restype = I
+        # c99_forms.c: (pointer, shape array, stride array, base) per buffer, as the C99 emitter passes them
+        B4 = [P, P, P, ctypes.c_longlong]
+        L.c99_row_sum_serial.argtypes = B4 + B4
+        L.c99_row_sum_launched.argtypes = B4 + B4 + [ctypes.c_uint, ctypes.c_uint]
+        L.c99_scan_serial.argtypes = B4 + B4 + [I, I]
+        L.c99_scan_launched.argtypes = B4 + B4 + [I, I, ctypes.c_uint]
+        L.c99_gather_rows_u16.argtypes = B4 + B4 + B4 + [I]
+        L.c99_row_max_argmax_bf16.argtypes = B4 + [P, ctypes.c_longlong, P, ctypes.c_longlong]
+        L.c99_w4a16.argtypes = [P, P, P, I64, I64, I64, I64, P]
+        for f in ("c99_row_sum_serial", "c99_row_sum_launched", "c99_scan_serial", "c99_scan_launched",
+                  "c99_gather_rows_u16", "c99_row_max_argmax_bf16", "c99_w4a16"):
+            getattr(L, f).restype = I
         _lib = L
     return _lib
 
@@ -346,3 +357,75 @@ def bf16_to_f64(b: int) -> float:
 def i4_value(packed: np.ndarray, idx: int) -> int:
     p = np.ascontiguousarray(packed, dtype=np.uint8)
     return int(lib().orc_i4_value(_p(p), idx))
+
+
+# ---- the C99 emitter's serial forms (c99_forms.c): a timed CPU baseline, checked against the oracle ----
+
+def _buf(a: np.ndarray):
+    """(pointer, shape array, stride array, base 0) of a C-contiguous array, in the emitter's argument ABI; the
+    arrays are returned too so that they outlive the call."""
+    assert a.flags["C_CONTIGUOUS"]
+    shape = np.array(a.shape, np.int64)
+    stride = np.array([st // a.itemsize for st in a.strides], np.int64)
+    return (_p(a), _p(shape), _p(stride), 0), (shape, stride)
+
+
+def c99_row_sum(x: np.ndarray, block: int | None = None) -> np.ndarray:
+    """The serial reduction lift's C (block None) or the launched block-tree lift's serialized C (a block B)."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty(x.shape[0], np.float32)
+    a, keep_a = _buf(x)
+    b, keep_b = _buf(out)
+    if block is None:
+        st = lib().c99_row_sum_serial(*a, *b)
+    else:
+        st = lib().c99_row_sum_launched(*a, *b, block, max(1, x.shape[0]))
+    assert st == 0
+    return out
+
+
+def c99_scan(x: np.ndarray, op: int, exclusive: bool, block: int | None = None) -> np.ndarray:
+    """The serial scan lift's C (block None) or the launched three-phase lift's serialized C, over a 1-D row."""
+    x = np.ascontiguousarray(x, np.int32).reshape(-1)
+    y = np.empty_like(x)
+    a, keep_a = _buf(x)
+    b, keep_b = _buf(y)
+    if block is None:
+        st = lib().c99_scan_serial(*a, *b, op, int(exclusive))
+    else:
+        st = lib().c99_scan_launched(*a, *b, op, int(exclusive), block)
+    assert st == 0
+    return y
+
+
+def c99_gather(table_u16: np.ndarray, ids: np.ndarray, oob: int, out: np.ndarray) -> np.ndarray:
+    """The gather lift's per-cell C over 2-byte elements and i32 ids; `out` (pre-filled) is updated in place."""
+    t = np.ascontiguousarray(table_u16).view(np.uint16)
+    i = np.ascontiguousarray(ids, np.int32)
+    assert out.dtype.itemsize == 2 and out.flags["C_CONTIGUOUS"]
+    o = out.view(np.uint16)
+    a, ka = _buf(t)
+    b, kb = _buf(i)
+    c, kc = _buf(o)
+    assert lib().c99_gather_rows_u16(*a, *b, *c, oob) == 0
+    return out
+
+
+def c99_row_max_argmax(x_bits: np.ndarray):
+    """The kernel-layer arg loop's C over bf16 rows: (max f32, argmax i64)."""
+    x = np.ascontiguousarray(x_bits, np.uint16)
+    mx = np.empty(x.shape[0], np.float32)
+    am = np.empty(x.shape[0], np.int64)
+    a, ka = _buf(x)
+    assert lib().c99_row_max_argmax_bf16(*a, _p(mx), 0, _p(am), 0) == 0
+    return mx, am
+
+
+def c99_w4a16(w_packed, scale_f16_bits, x_bf16_bits, m, n, k, group) -> np.ndarray:
+    """The dequant GEMM KernelFn's serialized C (one thread per output cell, f32 accumulator): bf16 bits [m, n]."""
+    w = np.ascontiguousarray(w_packed, np.uint8)
+    s = np.ascontiguousarray(scale_f16_bits, np.uint16)
+    x = np.ascontiguousarray(x_bf16_bits, np.uint16)
+    out = np.empty((m, n), np.uint16)
+    assert lib().c99_w4a16(_p(w), _p(s), _p(x), m, n, k, group, _p(out)) == 0
+    return out

@@ -439,6 +439,20 @@ static const char* at(const up_tensor& t) {
   return static_cast<const char*>(t.ptr) + (int64_t)((t.base * (int64_t)bits) / 8);
 }
 
+// An output of `n` elements written contiguously: its elements must be exactly those, densely laid out.
+static bool dense_vector(const up_tensor& t, int64_t n) {
+  int64_t c = 1;
+  for (int d = 0; d < t.rank; ++d) c *= t.shape[d];
+  return c == n && (n <= 1 || dense_row_major(t));
+}
+
+static bool same_shape(const up_tensor& a, const up_tensor& b) {
+  if (a.rank != b.rank) return false;
+  for (int d = 0; d < a.rank; ++d)
+    if (a.shape[d] != b.shape[d]) return false;
+  return true;
+}
+
 extern "C" int up_sm100_workspace_bytes(int kernel_id, const up_tensor* ins, int n_in, const up_tensor* outs, int n_out,
                                         const int64_t* scalars, int n_scalars, size_t* bytes) {
   (void)outs; (void)n_out;
@@ -469,7 +483,7 @@ extern "C" int up_sm100_launch(int kernel_id, const up_tensor* ins, int n_in, co
       if (n_in < 1 || n_out < 1) return UP_ERR_INVALID;
       const up_tensor &x = ins[0], &y = outs[0];
       if (x.dtype != UP_EK_F32 || y.dtype != UP_EK_F32 || x.rank != 2 || x.stride[1] != 1) return UP_ERR_UNSUPPORTED;
-      if (y.shape[0] != x.shape[0] || (y.rank == 1 && y.stride[0] != 1)) return UP_ERR_UNSUPPORTED;
+      if (!dense_vector(y, x.shape[0])) return UP_ERR_UNSUPPORTED;
       return up_sm100_row_sum_f32(reinterpret_cast<const float*>(at(x)), x.shape[0], x.shape[1], x.stride[0],
                                   (float*)at(y), (int)sc(0, UP_ACCUM_F32), (int)sc(1, 256), stream);
     }
@@ -483,8 +497,7 @@ extern "C" int up_sm100_launch(int kernel_id, const up_tensor* ins, int n_in, co
         return UP_ERR_UNSUPPORTED;
       if (axis != 0 && axis != 1) return UP_ERR_INVALID;
       const int64_t n_out_elems = axis == 1 ? x.shape[0] : x.shape[1];
-      const int64_t y_count = y.rank == 2 ? y.shape[0] * y.shape[1] : (y.rank == 1 ? y.shape[0] : 1);
-      if (y_count != n_out_elems || (y.rank >= 1 && y.stride[y.rank - 1] != 1)) return UP_ERR_UNSUPPORTED;
+      if (!dense_vector(y, n_out_elems)) return UP_ERR_UNSUPPORTED;
       if (f32)
         return up_sm100_reduce2d_f32(reinterpret_cast<const float*>(at(x)), x.shape[0], x.shape[1], x.stride[0], axis,
                                      (int)sc(0, UP_OP_SUM), (int)sc(2, UP_ACCUM_AUTO), (int)sc(3, 256), (float*)at(y),
@@ -581,8 +594,9 @@ extern "C" int up_sm100_launch(int kernel_id, const up_tensor* ins, int n_in, co
       if (n_in < 1 || n_out < 2) return UP_ERR_INVALID;
       const up_tensor &x = ins[0], &mx = outs[0], &am = outs[1];
       if (x.dtype != UP_EK_BF16 || x.rank != 2 || x.stride[1] != 1) return UP_ERR_UNSUPPORTED;
-      if (mx.ptr && mx.dtype != UP_EK_F32) return UP_ERR_UNSUPPORTED;
-      if (am.ptr && am.dtype != UP_EK_I32 && am.dtype != UP_EK_I64) return UP_ERR_UNSUPPORTED;
+      if (mx.ptr && (mx.dtype != UP_EK_F32 || !dense_vector(mx, x.shape[0]))) return UP_ERR_UNSUPPORTED;
+      if (am.ptr && ((am.dtype != UP_EK_I32 && am.dtype != UP_EK_I64) || !dense_vector(am, x.shape[0])))
+        return UP_ERR_UNSUPPORTED;
       return up_sm100_row_max_argmax_bf16(reinterpret_cast<const uint16_t*>(at(x)), x.shape[0], x.shape[1], x.stride[0],
                                           mx.ptr ? (float*)at(mx) : nullptr,
                                           (am.ptr && am.dtype == UP_EK_I32) ? (int32_t*)at(am) : nullptr,
@@ -610,7 +624,7 @@ extern "C" int up_sm100_launch(int kernel_id, const up_tensor* ins, int n_in, co
       if (n_in < 1 || n_out < 1) return UP_ERR_INVALID;
       const up_tensor &x = ins[0], &y = outs[0];
       if (x.dtype != UP_EK_I32 || y.dtype != UP_EK_I32 || x.rank < 1) return UP_ERR_UNSUPPORTED;
-      if (!dense_row_major(x) || !dense_row_major(y)) return UP_ERR_UNSUPPORTED;
+      if (!dense_row_major(x) || !dense_row_major(y) || !same_shape(x, y)) return UP_ERR_UNSUPPORTED;
       int64_t rows = 1;
       for (int d = 0; d < x.rank - 1; ++d) rows *= x.shape[d];
       return up_sm100_scan_i32(reinterpret_cast<const int32_t*>(at(x)), (int32_t*)at(y), rows, x.shape[x.rank - 1],
@@ -620,9 +634,13 @@ extern "C" int up_sm100_launch(int kernel_id, const up_tensor* ins, int n_in, co
     case UP_K_GATHER_ROWS: {
       if (n_in < 2 || n_out < 1) return UP_ERR_INVALID;
       const up_tensor &tab = ins[0], &ids = ins[1], &o = outs[0];
-      if (tab.rank < 1 || tab.dtype != o.dtype || !dense_row_major(tab) || !dense_row_major(o)) return UP_ERR_UNSUPPORTED;
+      if (tab.rank < 1 || tab.dtype != o.dtype || !dense_row_major(tab) || !dense_row_major(o) || o.rank != tab.rank)
+        return UP_ERR_UNSUPPORTED;
       int64_t row_elems = 1;
-      for (int d = 1; d < tab.rank; ++d) row_elems *= tab.shape[d];
+      for (int d = 1; d < tab.rank; ++d) {
+        if (o.shape[d] != tab.shape[d]) return UP_ERR_UNSUPPORTED;
+        row_elems *= tab.shape[d];
+      }
       const int64_t row_bytes = row_elems * (int64_t)elem_bits(tab.dtype) / 8;
       const int64_t n = o.shape[0];
       if (ids.rank < 1 || ids.shape[0] != n || ids.stride[0] != 1) return UP_ERR_UNSUPPORTED;
@@ -634,6 +652,10 @@ extern "C" int up_sm100_launch(int kernel_id, const up_tensor* ins, int n_in, co
       const up_tensor &w = ins[0], &s = ins[1], &o = outs[0];
       if (w.dtype != UP_EK_I4 || s.dtype != UP_EK_F16 || o.dtype != UP_EK_BF16) return UP_ERR_UNSUPPORTED;
       if (!dense_row_major(w) || !dense_row_major(s) || !dense_row_major(o) || w.base % 2) return UP_ERR_UNSUPPORTED;
+      const int64_t group = sc(0, 128);
+      if (w.rank != 2 || s.rank != 2 || !same_shape(w, o) || group <= 0 || w.shape[1] % group ||
+          s.shape[0] != w.shape[0] || s.shape[1] != w.shape[1] / group)
+        return UP_ERR_UNSUPPORTED;
       return up_sm100_dequant_i4_bf16(reinterpret_cast<const uint8_t*>(at(w)), reinterpret_cast<const uint16_t*>(at(s)),
                                       w.shape[0], w.shape[1], sc(0, 128), (uint16_t*)at(o), stream);
     }
@@ -643,6 +665,11 @@ extern "C" int up_sm100_launch(int kernel_id, const up_tensor* ins, int n_in, co
       if (w.dtype != UP_EK_I4 || s.dtype != UP_EK_F16 || x.dtype != UP_EK_BF16 || o.dtype != UP_EK_BF16)
         return UP_ERR_UNSUPPORTED;
       if (!dense_row_major(w) || !dense_row_major(s) || !dense_row_major(x) || !dense_row_major(o) || w.base % 2)
+        return UP_ERR_UNSUPPORTED;
+      const int64_t group = sc(0, 128);
+      if (w.rank != 2 || s.rank != 2 || x.rank != 2 || o.rank != 2 || group <= 0 || w.shape[1] % group ||
+          s.shape[0] != w.shape[0] || s.shape[1] != w.shape[1] / group || x.shape[1] != w.shape[1] ||
+          o.shape[0] != x.shape[0] || o.shape[1] != w.shape[0])
         return UP_ERR_UNSUPPORTED;
       return up_sm100_w4a16_gemm(reinterpret_cast<const uint8_t*>(at(w)), reinterpret_cast<const uint16_t*>(at(s)),
                                  reinterpret_cast<const uint16_t*>(at(x)), x.shape[0], w.shape[0], w.shape[1], sc(0, 128),
