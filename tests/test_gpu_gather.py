@@ -86,3 +86,36 @@ def test_full_zipf_config():
     t_np = table.view(torch.int16).cpu().numpy().view(np.uint16)
     want = orc.gather_rows(t_np, ids[sel].cpu().numpy(), orc.OOB_ZERO_FILL)
     assert np.array_equal(out[sel].view(torch.int16).cpu().numpy().view(np.uint16), want)
+
+
+# Many runs of 32 rows per warp over a multi-wave grid: 16-byte aligned rows of 16 B to 8 KiB (one chunk per lane
+# and fewer, one, two and sixteen), n leaving a partial last run, and 20 % of the ids out of range (negative, past
+# the end, extreme).
+@pytest.mark.parametrize("row_bytes", [16, 48, 512, 1024, 8192])
+@pytest.mark.parametrize("policy", list(POLICIES))
+def test_large_n_every_policy(row_bytes, policy):
+    rng = np.random.default_rng(row_bytes + len(policy))
+    V = 3000
+    n = 148 * 4 * 16 * 3 + 5 if row_bytes <= 1024 else 148 * 4 * 16 + 3
+    words = row_bytes // 4
+    table = rng.integers(0, 2 ** 32, size=(V, words), dtype=np.uint64).astype(np.uint32)
+    for idx in ("i32", "i64", "u32"):
+        ids = _pool_ids(rng, n, V)
+        if idx == "u32":
+            ids = np.where(ids < 0, 2 ** 32 - 5, ids).astype(np.uint32)
+        else:
+            ids = ids.astype(np.int32 if idx == "i32" else np.int64)
+        prefill = rng.integers(0, 2 ** 32, size=(n, words), dtype=np.uint64).astype(np.uint32)
+        want = orc.gather_rows(table, ids, POLICIES[policy], out=prefill.copy())
+        out = torch.from_numpy(prefill.view(np.int32).copy()).cuda()
+        ops.gather_rows(torch.from_numpy(table.view(np.int32)).cuda(), torch.from_numpy(ids).cuda(), policy, out=out)
+        assert np.array_equal(out.cpu().numpy().view(np.uint32), want), idx
+
+
+def test_zipf_2p20_all_in_range_and_repeat():
+    """Zipf ids of the benchmark's distribution at 2^20 ids: plain row indexing, the same bits on a second call."""
+    table, ids = workloads.gather_inputs(n=1 << 20, device="cuda")
+    a = ops.gather_rows(table, ids, "skip")
+    b = ops.gather_rows(table, ids, "zero_fill")
+    assert torch.equal(a.view(torch.int16), table.view(torch.int16)[ids.long()])
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
