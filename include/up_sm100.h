@@ -416,7 +416,61 @@ UP_API int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, const ui
                         size_t workspace_bytes, void* stream);
 UP_API size_t up_sm100_w4a16_workspace_bytes(int64_t m, int64_t n, int64_t k, int64_t group);
 
+/* ---- Several GPUs of one node ------------------------------------------------------------------------
+ *
+ * The reference models a launch over several devices as the same kernel run per device on its slice of the
+ * launch (crates/unpopped/src/oracle/kernel_launch.rs:100-129, run_launch_devices; crates/unpopped/src/exec.rs:
+ * 119-143, LaunchShape::devices). A communicator joins the ranks of one node (at most 8), one GPU each; each rank
+ * calls up_sm100_launch_multi with its own shard, and the library runs the lift's exchange step (NCCL over
+ * NVLink, or peer stores for the block-cyclic scan). NCCL is loaded at run time (libnccl.so.2); without it these
+ * entry points return UP_ERR_COMM. Calls on one communicator are collectives: every rank makes the same calls
+ * in the same order, each on one stream of its own. */
+typedef struct up_comm up_comm;
+
+/* A new NCCL unique id (128 bytes) for a multi-process communicator: one rank makes it and the host's own channel
+ * (a store, MPI, torch.distributed) carries it to the others. */
+UP_API int up_sm100_comm_unique_id(unsigned char id[128]);
+/* Joins this process, on the current device, as `rank` of `nranks` (1..8) to the communicator named by `id`.
+ * Blocks until every rank has joined. */
+UP_API int up_sm100_comm_init_rank(int nranks, int rank, const unsigned char id[128], up_comm** comm);
+/* One process driving `n_gpus` devices: comms[i] is rank i on devs[i] (ncclCommInitAll); peer access is enabled
+ * between the devices. A call on comms[i] needs devs[i] current. The collective exchanges (the contiguous-shard
+ * scan, W4A16) need one process per GPU; the block-cyclic scan and the row-parallel lifts run either way. */
+UP_API int up_sm100_comm_init(int n_gpus, const int* devs, up_comm** comms);
+UP_API int up_sm100_comm_destroy(up_comm* comm);
+UP_API int up_sm100_comm_rank(const up_comm* comm, int* rank, int* nranks);
+
+/* Workspace of up_sm100_launch_multi on this rank's operands (the W4A16 GEMM adds room for the output slices). */
+UP_API int up_sm100_workspace_bytes_multi(int kernel_id, const up_tensor* ins, int n_in, const up_tensor* outs,
+                                          int n_out, const int64_t* scalars, int n_scalars, const up_comm* comm,
+                                          size_t* bytes);
+/* This rank's shard of a lift, with the lift's exchange step, on `stream` (the communicator's device current).
+ * Operands are this rank's, as for up_sm100_launch:
+ *  SCAN_I32:            ins {x i32, this rank's shard}, outs {y}; scalars {op, exclusive, reverse, layout}.
+ *                       layout 0: the global array is the shards in rank order. Each rank folds its shard, the
+ *                       ranks all-gather the totals (NCCL), and each scans with the fold of the totals before it
+ *                       (after it, reverse): two passes over the data. layout 1: block-cyclic. The global array
+ *                       is a sequence of stripes of 148 x 8192 elements, stripe s on rank s % G as that rank's
+ *                       local stripe s / G. One pass: each rank's CTA 0 stores its local stripes' aggregates into
+ *                       the other ranks' memory over NVLink, and the look-back adds those that sit before each
+ *                       tile. Forward only; shards of at least 148 x 8192 elements, 16-byte aligned, whole 16-byte
+ *                       chunks, the same size on every rank; every rank on its own GPU. Either layout is bit-exact
+ *                       to the single-GPU scan of the global array. Status after the fact:
+ *                       up_sm100_workspace_status on this rank's workspace.
+ *  W4A16_GEMM:          ins {w i4 [Nl, K] (this rank's weight rows), scale f16 [Nl, K/group], x bf16 [M, K]},
+ *                       outs {out bf16 [M, G * Nl]}, scalars {group}: the rank's slice, then an NCCL all-gather of
+ *                       every slice into the whole output on every rank (rank g's rows are columns g*Nl ..).
+ *  ROW_SUM_F32, ROW_MAX_ARGMAX_BF16, GATHER_ROWS, DEQUANT_I4: independent (output) rows; each rank runs its
+ *                       shard as up_sm100_launch does, with no collective. */
+UP_API int up_sm100_launch_multi(int kernel_id, const up_tensor* ins, int n_in, const up_tensor* outs, int n_out,
+                                 const int64_t* scalars, int n_scalars, void* workspace, size_t workspace_bytes,
+                                 void* stream, up_comm* comm);
+
 /* ---- Test and tuning hooks ----------------------------------------------------------------------- */
+
+/* Makes `launches` the block-cyclic launch count of `comm` (its low 30 bits tag the stripe words), so that a test
+ * can cross a wrap of the tag; every rank must set the same value. */
+UP_API void up_sm100_comm_set_test_launches(up_comm* comm, uint64_t launches);
 
 /* Bound, in nanoseconds, of every device-side wait (default 1e9). */
 UP_API void up_sm100_set_wait_limit_ns(uint64_t ns);

@@ -113,6 +113,16 @@ SIGNATURES = {
     "up_sm100_set_wait_limit_ns": ([_U64], None),
     "up_sm100_set_test_withhold_flag": ([_I], None),
     "up_sm100_set_test_scan_epoch": ([_U64], None),
+    "up_sm100_comm_unique_id": ([_P], _I),
+    "up_sm100_comm_init_rank": ([_I, _I, _P, ctypes.POINTER(ctypes.c_void_p)], _I),
+    "up_sm100_comm_init": ([_I, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_void_p)], _I),
+    "up_sm100_comm_destroy": ([_P], _I),
+    "up_sm100_comm_rank": ([_P, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)], _I),
+    "up_sm100_workspace_bytes_multi": ([_I, ctypes.POINTER(UpTensor), _I, ctypes.POINTER(UpTensor), _I,
+                                        ctypes.POINTER(ctypes.c_int64), _I, _P, ctypes.POINTER(_SZ)], _I),
+    "up_sm100_launch_multi": ([_I, ctypes.POINTER(UpTensor), _I, ctypes.POINTER(UpTensor), _I,
+                               ctypes.POINTER(ctypes.c_int64), _I, _P, _SZ, _P, _P], _I),
+    "up_sm100_comm_set_test_launches": ([_P, _U64], None),
     "up_sm100_launch_count": ([], _U64),
     "up_sm100_last_error": ([], ctypes.c_char_p),
 }

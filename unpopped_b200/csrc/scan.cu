@@ -23,6 +23,7 @@
 // bounded by a globaltimer deadline; a wait that runs out sets the workspace error word and publishes
 // "aborted", which the tiles that wait on it propagate at once.
 #include "common.cuh"
+#include "multi.cuh"
 #include "tc.cuh"
 
 #include <atomic>
@@ -369,17 +370,27 @@ struct QCursor {
   }
 };
 
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 // What pass 1 leaves for pass 2 of one tile, per thread.
 struct QFold {
   int32_t cp[kQRowChunks];  // slot i: exclusive prefix, within this thread's row, of chunk (i + R) mod 4
   int32_t texcl;            // exclusive prefix of this thread's row within its warp
 };
 
-template <int OP, bool REV>
+template <int OP, bool REV, bool MULTI = false>
 __global__ void __launch_bounds__(kQThreads, 1)
     scan_i32_persist_kernel(const int32_t* __restrict__ x, int32_t* __restrict__ y, int64_t k, int64_t tiles_per_row,
                             int64_t n_tiles, int exclusive, const int32_t* carry_in, ScanHeader* hdr, uint64_t* flags,
-                            uint32_t epoch, uint64_t wait_ns, int withhold) {
+                            uint32_t epoch, uint64_t wait_ns, int withhold, MultiScan ms) {
+  static_assert(!(MULTI && REV), "the block-cyclic form scans forward");
   constexpr bool reverse = REV;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)kQStages * kQTileBytes);  // [stages] data landed
@@ -489,57 +500,101 @@ __global__ void __launch_bounds__(kQThreads, 1)
     // ---------------- look-back warp ----------------
     const int32_t cin = carry_in ? *carry_in : id;
     int32_t pre_prev = id;
+    // Folds the m aggregates flags[t - m .. t - 1] into *sum once all have been published (bounded wait). False
+    // when one of them is aborted, the CTA is aborting, or the wait ran out.
+    auto window = [&](int64_t t, int m, int32_t* sum) -> bool {
+      *sum = id;
+      if (m <= 0) return true;
+      const uint64_t t0 = globaltimer_ns();
+      while (true) {
+        uint64_t f[kQMaxWin];
+#pragma unroll
+        for (int i = 0; i < kQMaxWin; ++i) {  // all loads first: one round trip
+          const int d = lane + 32 * i + 1;
+          f[i] = d <= m ? ld_relaxed_u64(flags + (t - d)) : 0;
+        }
+        bool ready = true, err = false;
+#pragma unroll
+        for (int i = 0; i < kQMaxWin; ++i) {
+          const int d = lane + 32 * i + 1;
+          if (d <= m) {
+            const uint32_t st = flag_status(f[i], epoch);
+            ready = ready && st == kFlagAgg;
+            err = err || st == kFlagErr;
+          }
+        }
+        if (__any_sync(0xffffffffu, err) || __shfl_sync(0xffffffffu, *s_abort, 0)) return false;
+        if (__all_sync(0xffffffffu, ready)) {
+          int32_t v = id;
+#pragma unroll
+          for (int i = 0; i < kQMaxWin; ++i) {
+            const int d = lane + 32 * i + 1;
+            if (d <= m) v = comb<OP>(v, (int32_t)(uint32_t)f[i]);
+          }
+          *sum = warp_reduce<OP>(v);
+          return true;
+        }
+        if (__shfl_sync(0xffffffffu, globaltimer_ns() - t0 > wait_ns, 0)) return false;
+        __nanosleep(32);
+      }
+    };
+    // MULTI: folds the other ranks' stripe aggregates of global stripes [lo, hi) (at most kMaxRanks - 1 of them)
+    // once all have arrived (bounded wait). The ops are commutative, so their order does not matter.
+    auto remote = [&](int64_t lo, int64_t hi, int32_t* sum) -> bool {
+      *sum = id;
+      const int n = (int)(hi - lo);
+      if (n <= 0) return true;
+      const uint64_t t0 = globaltimer_ns();
+      while (true) {
+        const uint64_t f = lane < n ? ld_relaxed_sys_u64(ms.sflags + lo + lane) : 0;
+        const uint32_t st = lane < n ? flag_status(f, ms.tag) : kFlagAgg;
+        if (__any_sync(0xffffffffu, st == kFlagErr) || __shfl_sync(0xffffffffu, *s_abort, 0)) return false;
+        if (__all_sync(0xffffffffu, st == kFlagAgg)) {
+          *sum = warp_reduce<OP>(lane < n ? (int32_t)(uint32_t)f : id);
+          return true;
+        }
+        if (__shfl_sync(0xffffffffu, globaltimer_ns() - t0 > wait_ns, 0)) return false;
+        __nanosleep(64);
+      }
+    };
+    // MULTI, CTA 0: sends the aggregate of local stripe `ls` to every other rank (global stripe ls * G + r), or
+    // "aborted" for local stripes ls onward, so that no rank waits for them.
+    auto publish_stripe = [&](int64_t ls, int32_t agg, bool aborted) {
+      if (!MULTI || b != 0) return;
+      const int64_t n_stripes = (n_tiles + P - 1) / P;
+      for (int64_t q = ls; q < (aborted ? n_stripes : ls + 1); ++q)
+        if (lane < ms.G && lane != ms.r)
+          st_relaxed_sys_u64(ms.peers[lane] + q * ms.G + ms.r,
+                             make_flag(ms.tag, aborted ? kFlagErr : kFlagAgg, aborted ? 0 : agg));
+    };
     QCursor c;
     c.init(b, tiles_per_row);
     for (int64_t j = 0; j < n_mine; ++j, c.next(P, tiles_per_row)) {
       int32_t pre = cin;
+      bool good = true;
       if (c.q != 0) {
         const bool chain = j > 0 && c.q >= P;  // this CTA's previous tile is in the same row
         const int m = (int)(chain ? P : c.q);  // aggregates to add: tiles t - m .. t - 1
-        const int32_t base = chain ? pre_prev : cin;
-        const uint64_t t0 = globaltimer_ns();
-        bool bad = false;
-        while (true) {
-          uint64_t f[kQMaxWin];
-#pragma unroll
-          for (int i = 0; i < kQMaxWin; ++i) {  // all loads first: one round trip
-            const int d = lane + 32 * i + 1;
-            f[i] = d <= m ? ld_relaxed_u64(flags + (c.t - d)) : 0;
-          }
-          bool ready = true, err = false;
-#pragma unroll
-          for (int i = 0; i < kQMaxWin; ++i) {
-            const int d = lane + 32 * i + 1;
-            if (d <= m) {
-              const uint32_t st = flag_status(f[i], epoch);
-              ready = ready && st == kFlagAgg;
-              err = err || st == kFlagErr;
-            }
-          }
-          if (__any_sync(0xffffffffu, err) || __shfl_sync(0xffffffffu, *s_abort, 0)) {
-            bad = true;
-            break;
-          }
-          if (__all_sync(0xffffffffu, ready)) {
-            int32_t s = id;
-#pragma unroll
-            for (int i = 0; i < kQMaxWin; ++i) {
-              const int d = lane + 32 * i + 1;
-              if (d <= m) s = comb<OP>(s, (int32_t)(uint32_t)f[i]);
-            }
-            pre = comb<OP>(base, warp_reduce<OP>(s));
-            break;
-          }
-          if (__shfl_sync(0xffffffffu, globaltimer_ns() - t0 > wait_ns, 0)) {
-            bad = true;
-            break;
-          }
-          __nanosleep(32);
+        int32_t sum = id;
+        good = window(c.t, m, &sum);
+        if (good) {
+          pre = comb<OP>(chain ? pre_prev : cin, sum);
+          // CTA 0's window of P tiles is exactly its previous local stripe: publish it before waiting on anyone
+          if (MULTI && chain) publish_stripe(j - 1, sum, false);
         }
-        if (bad) {
-          if (lane == 0) abort_from(j);
-          return;
-        }
+      }
+      if (MULTI && good) {
+        // the other ranks' stripes between this CTA's previous tile and this one: local stripe j - 1's successors
+        // on ranks r + 1 .. G - 1 and local stripe j's predecessors on ranks 0 .. r - 1 (for j = 0, the latter)
+        const int64_t lo = j == 0 ? 0 : (j - 1) * ms.G + ms.r + 1, hi = j * ms.G + ms.r;
+        int32_t rs = id;
+        good = remote(lo, hi, &rs);
+        if (good) pre = comb<OP>(pre, rs);
+      }
+      if (!good) {
+        if (lane == 0) abort_from(j);
+        publish_stripe(j > 0 ? j - 1 : 0, 0, true);
+        return;
       }
       pre_prev = pre;
       if (lane == 0) {
@@ -551,6 +606,13 @@ __global__ void __launch_bounds__(kQThreads, 1)
         tc::mbar_arrive(&pfull[j % kQRing]);
       }
       __syncwarp();
+    }
+    if (MULTI && b == 0 && n_mine > 0) {
+      // the last local stripe (tiles (n_mine - 1) * P .. n_tiles - 1) has no next tile of CTA 0 to close it
+      const int64_t last = (n_mine - 1) * P;
+      int32_t sum = id;
+      if (window(n_tiles, (int)(n_tiles - last), &sum)) publish_stripe(n_mine - 1, sum, false);
+      else publish_stripe(n_mine - 1, 0, true);
     }
     return;
   }
@@ -783,7 +845,7 @@ static cudaError_t launch_scan_persist_dir(unsigned grid, cudaStream_t s, const 
   cudaError_t e = ensure_smem_attr((const void*)scan_i32_persist_kernel<OP, REV>, (int)kQSmem);
   if (e != cudaSuccess) return e;
   scan_i32_persist_kernel<OP, REV><<<grid, kQThreads, kQSmem, s>>>(x, y, k, tpr, tiles, exclusive, carry_in, hdr,
-                                                                   flags, epoch, wns, withhold);
+                                                                   flags, epoch, wns, withhold, MultiScan{});
   return cudaGetLastError();
 }
 
@@ -908,6 +970,59 @@ extern "C" int up_sm100_scan_i32(const int32_t* x, int32_t* y, int64_t rows, int
   note_launch();
   return cuda_status(e);
 }
+
+namespace up {
+// One rank's pass of a scan over an array sharded block-cyclically across a communicator's ranks (stripes of
+// kStripeTiles tiles of 8192 elements, stripe s on rank s % G): a single pass over the shard, with the cross-GPU
+// look-back through the stripe words in `m`. Forward scans of one 16-byte aligned row of whole 16-byte chunks and
+// at least kStripeTiles tiles, on a device that holds kStripeTiles persistent CTAs at once. Every rank launches it
+// with the same k, op and exclusive flag.
+int scan_i32_block_cyclic(const int32_t* x, int32_t* y, int64_t k, int op, int exclusive, const int32_t* carry_in,
+                          void* workspace, size_t workspace_bytes, const MultiScan& m, cudaStream_t s) {
+  if (op != UP_OP_SUM && op != UP_OP_MAX && op != UP_OP_MIN) return UP_ERR_UNSUPPORTED;
+  if (x == nullptr || y == nullptr || workspace == nullptr || !aligned(workspace, 64)) return UP_ERR_INVALID;
+  if (!aligned(x, 16) || !aligned(y, 16) || k % 4 != 0)
+    return fail_with(UP_ERR_UNSUPPORTED, "block-cyclic scan: 16-byte aligned shards of whole 16-byte chunks");
+  int64_t tiles = 0;
+  if (!tile_count(1, k, kQTile, kMaxScanTiles, &tiles) || tiles < kStripeTiles)
+    return fail_with(UP_ERR_UNSUPPORTED, "block-cyclic scan: a shard holds at least 148 tiles of 8192 elements");
+  if (workspace_bytes < up_sm100_scan_workspace_bytes(1, k)) return UP_ERR_INVALID;
+  bool fits = false;
+  int st = persistent_form_fits(&fits);
+  if (st != UP_OK) return st;
+  if (!fits || sm_count() < kStripeTiles)
+    return fail_with(UP_ERR_UNSUPPORTED, "block-cyclic scan: the device must hold 148 persistent CTAs at once");
+  auto* hdr = static_cast<ScanHeader*>(workspace);
+  auto* flags = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + sizeof(ScanHeader));
+  uint32_t epoch = 0;
+  cudaError_t e = launch_epoch(workspace, workspace_bytes, s, &epoch);
+  if (e != cudaSuccess) return cuda_status(e);
+  const void* fn = op == UP_OP_SUM   ? (const void*)scan_i32_persist_kernel<UP_OP_SUM, false, true>
+                   : op == UP_OP_MAX ? (const void*)scan_i32_persist_kernel<UP_OP_MAX, false, true>
+                                     : (const void*)scan_i32_persist_kernel<UP_OP_MIN, false, true>;
+  e = ensure_smem_attr(fn, (int)kQSmem);
+  if (e != cudaSuccess) return cuda_status(e);
+  const uint64_t wns = wait_limit_ns();
+  const int withhold = take_withhold_flag();
+  if (op == UP_OP_SUM)
+    scan_i32_persist_kernel<UP_OP_SUM, false, true><<<kStripeTiles, kQThreads, kQSmem, s>>>(
+        x, y, k, tiles, tiles, exclusive, carry_in, hdr, flags, epoch, wns, withhold, m);
+  else if (op == UP_OP_MAX)
+    scan_i32_persist_kernel<UP_OP_MAX, false, true><<<kStripeTiles, kQThreads, kQSmem, s>>>(
+        x, y, k, tiles, tiles, exclusive, carry_in, hdr, flags, epoch, wns, withhold, m);
+  else
+    scan_i32_persist_kernel<UP_OP_MIN, false, true><<<kStripeTiles, kQThreads, kQSmem, s>>>(
+        x, y, k, tiles, tiles, exclusive, carry_in, hdr, flags, epoch, wns, withhold, m);
+  note_launch();
+  return check_launch();
+}
+
+// Stripe words a block-cyclic scan of a shard of k elements needs on each of G ranks: one per global stripe.
+int64_t block_cyclic_stripe_words(int64_t k, int G) {
+  const int64_t tiles = (k + kQTile - 1) / kQTile;
+  return ((tiles + kStripeTiles - 1) / kStripeTiles) * G;
+}
+}  // namespace up
 
 extern "C" void up_sm100_set_test_scan_epoch(uint64_t next) {
   std::lock_guard<std::mutex> lk(g_epoch_mu);
