@@ -134,6 +134,11 @@ class Ctx:
             torch.cuda.set_device(self.local)
         self.dev = torch.device("cuda", self.local)
         self.sleep_cycles = 1_000_000  # ~0.5 ms at the B200's 1.9 GHz SM clock
+        self.comm = None
+        if self.world > 1:
+            from unpopped_b200 import dist as udist
+
+            self.comm = udist.Comm()  # the library's communicator (NCCL inside libunpopped_sm100)
 
     def barrier(self):
         if self.world > 1:
@@ -188,36 +193,19 @@ def copies_for(nbytes: int, l2_bytes: int = 126 << 20) -> int:
     return max(1, -(-(2 * l2_bytes) // max(1, nbytes)) + 1) if nbytes < 4 * l2_bytes else 1
 
 
-def make_scan_step(ctx, x, y, ws_kind="scan"):
-    """One step of the (possibly sharded) inclusive add-scan; records the scan kernel's own events."""
-    from unpopped_b200 import ops
+def make_scan_step(ctx, x, y, layout="block_cyclic"):
+    """One step of the (possibly sharded) inclusive add-scan. At N > 1 it goes through the library's communicator
+    (up_sm100_launch_multi): "block_cyclic" is one kernel per step (the cross-GPU look-back over NVLink),
+    "contiguous" folds the shard, all-gathers the totals and scans."""
+    from unpopped_b200 import dist as udist, ops
 
-    torch = ctx.torch
     if ctx.world == 1:
         def step(i, kin):  # one kernel: the step time is the kernel time
             ops.scan(x, "sum", out=y)
         return step
 
-    total = torch.empty(1, dtype=torch.int32, device=ctx.dev)
-    totals = torch.empty(ctx.world, dtype=torch.int32, device=ctx.dev)
-    carry = torch.empty(1, dtype=torch.int32, device=ctx.dev)
-
     def step(i, kin):
-        ops.reduce_i32(x, "sum", out=total)
-        ctx.dist.all_gather_into_tensor(totals, total)
-        # the carry is the wrapped sum of the lower ranks' totals
-        if ctx.rank == 0:
-            carry.zero_()
-        else:
-            ops.reduce_i32(totals[:ctx.rank], "sum", out=carry)
-        if kin is not None:
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            ops.scan(x, "sum", carry=carry, out=y)
-            b.record()
-            kin.append((a, b))
-        else:
-            ops.scan(x, "sum", carry=carry, out=y)
+        udist.sharded_scan(x, "sum", layout=layout, comm=ctx.comm, out=y)
     return step
 
 
@@ -450,6 +438,16 @@ def cpu_baselines():
     return res, samples, T
 
 
+def scan_ws_status(ctx):
+    """The sharded scan's workspace status on this rank (a bounded wait that ran out shows here)."""
+    from unpopped_b200 import _lib
+
+    ws = ctx.comm._ws.get(_lib.KERNEL["SCAN_I32"])
+    if ws is not None:
+        _lib.check(_lib.load().up_sm100_workspace_status(ws.data_ptr(), ctx.torch.cuda.current_stream().cuda_stream),
+                   "sharded scan")
+
+
 # The config lifts, by their names in `bench_lifts`, in the order of BASELINE.json's configs.
 CONFIG_LIFTS = {
     "rowsum_f32_8192x8192": ("cfg1_rowsum_f32", "cfg1"),
@@ -490,7 +488,8 @@ def config_block(lifts, head, cpu_cfg):
 def scan_config(world):
     """The headline workload's `config`, shared by both arms of the bench."""
     return {"workload": "configs[1]: inclusive add-scan over 2^28 int32 per GPU (1 GiB in, 1 GiB out)"
-                        + ("; shards combined by an all-gather of per-GPU totals" if world > 1 else ""),
+                        + ("; block-cyclic shards (148 x 8192-element stripes round-robin over the GPUs), one "
+                           "pass with the cross-GPU look-back over NVLink" if world > 1 else ""),
             "lift": "scan_incl_add_i32", "elements_per_gpu": SCAN_N,
             "l2": "input (1 GiB per GPU) larger than the 126 MB L2; no flush", "parallelism": f"sharded x{world}"}
 
@@ -652,10 +651,12 @@ def main():
     x = wl.scan_input(device=ctx.dev, seed=wl.SEED + 2 + ctx.rank)
     y = torch.empty_like(x)
     step = make_scan_step(ctx, x, y)
-    ms, kms, launches = ctx.timed(step, K, W, inner=ctx.world > 1)
-    if kms is None:
-        kms = ms
-    ops.check_workspace("scan", ctx.dev)
+    ms, kms, launches = ctx.timed(step, K, W)
+    kms = ms  # one kernel per step at any N
+    if ctx.world == 1:
+        ops.check_workspace("scan", ctx.dev)
+    else:
+        scan_ws_status(ctx)
     nbytes = wl.scan_bytes()
     value = ctx.world * nbytes / (ms * 1e-3) / 1e9
     achieved = nbytes / (kms * 1e-3) / 1e9
@@ -669,15 +670,22 @@ def main():
             ops.scan_host(xh, "sum", out=yh)
         api = "up_sm100_scan_i32_host (pinned host buffers, copies overlapped with the scan)"
     else:
-        # sharded: the carry needs every shard's total first, so the shard is copied in whole
+        # sharded: every rank copies its shard in, runs the block-cyclic scan and copies its result out
         def e2e_step(i, kin):
             x.copy_(xh, non_blocking=True)
             step(i, None)
             yh.copy_(y, non_blocking=True)
-        api = "copy in, sharded up_sm100_scan_i32 (reduce, all-gather of totals, scan), copy out"
+        api = "copy in, up_sm100_launch_multi block-cyclic scan (one pass, cross-GPU look-back), copy out"
     e_ms, _, _ = ctx.timed(e2e_step, max(3, K // 4), 3, head_start=ctx.world > 1)
     e2e = {"value": round(ctx.world * nbytes / (e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
            "h2d_bytes_per_step": xh.numel() * 4, "d2h_bytes_per_step": yh.numel() * 4, "api": api}
+    contiguous = None
+    if ctx.world > 1:
+        # the two-pass layout over contiguous shards (fold, all-gather of totals, scan), for comparison
+        c_ms, _, _ = ctx.timed(make_scan_step(ctx, x, y, "contiguous"), K, W)
+        scan_ws_status(ctx)
+        contiguous = {"value": round(ctx.world * nbytes / (c_ms * 1e-3) / 1e9, 1), "ms_per_step": round(c_ms, 4),
+                      "frac_of_hbm": round(nbytes / (c_ms * 1e-3) / 1e9 / hbm, 4)}
     del xh, yh, x, y
     torch.cuda.empty_cache()
 
@@ -710,10 +718,14 @@ def main():
             line["cpu_samples"] = dict(cpu_samples, threads=cpu_threads, unit="GB/s of the sample's algorithmic bytes")
         head = {"value": round(value, 1), "ms_per_step": round(ms, 4), "frac_of_hbm": round(achieved / hbm, 4)}
         line["configs"] = config_block(lifts, head, cpu_cfg)
+    if contiguous is not None:
+        line["scan_contiguous_two_pass"] = contiguous
     if ctx.rank == 0:
         print(json.dumps(line, separators=(",", ":")), flush=True)
     if ctx.world > 1:
+        torch.cuda.synchronize()
         ctx.barrier()
+        ctx.comm.close()
         ctx.dist.destroy_process_group()
 
 

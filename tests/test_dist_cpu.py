@@ -192,3 +192,121 @@ def test_a_rank_that_leaves_ends_the_exchange_with_an_error():
             p.kill()
     assert got[1] == "left"
     assert got[0].startswith("error:"), got[0]
+
+
+def _block_cyclic_worker(rank, world, port, n_local, q):
+    try:
+        _init(rank, world, port)
+        from unpopped_b200.dist import block_cyclic_index, sharded_scan
+
+        g = torch.Generator().manual_seed(11)
+        glob = torch.randint(-(2 ** 31), 2 ** 31 - 1, (world * n_local,), generator=g, dtype=torch.int32)
+        x = glob[block_cyclic_index(n_local, world)[rank]].contiguous()
+        res = {}
+        for op in OPS:
+            for ex in (False, True):
+                res[(op, ex)] = sharded_scan(x, op, ex, layout="block_cyclic", local=cpu_local()).numpy()
+        q.put((rank, res))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_block_cyclic_layout_is_the_global_scan(world):
+    """The block-cyclic layout (stripes of 148 x 8192 elements dealt round-robin, a partial last stripe): every
+    rank's result, put back at its global positions, is the scan of the global array."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+
+    from unpopped_b200.dist import STRIPE_ELEMS, block_cyclic_index
+
+    n_local = 2 * STRIPE_ELEMS + 8192 * 3 + 4
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_block_cyclic_worker, args=(r, world, port, n_local, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        assert isinstance(got[r], dict), got[r]
+    g = torch.Generator().manual_seed(11)
+    glob = torch.randint(-(2 ** 31), 2 ** 31 - 1, (world * n_local,), generator=g, dtype=torch.int32).numpy()
+    idx = block_cyclic_index(n_local, world).numpy()
+    for (op, ex) in got[0]:
+        want = orc.scan_i32(glob, OPS[op], ex)
+        for r in range(world):
+            assert np.array_equal(got[r][(op, ex)], want[idx[r]]), (op, ex, r)
+
+
+def test_block_cyclic_index_is_a_permutation_in_stripes():
+    from unpopped_b200.dist import STRIPE_ELEMS, block_cyclic_index
+
+    for world in (1, 2, 3, 8):
+        n_local = STRIPE_ELEMS + 17 * 4
+        idx = block_cyclic_index(n_local, world)
+        assert sorted(idx.reshape(-1).tolist()[:0]) == []
+        flat = idx.reshape(-1)
+        assert torch.unique(flat).numel() == flat.numel()
+        # rank r's first stripe is global stripe r
+        for r in range(world):
+            assert int(idx[r, 0]) == r * STRIPE_ELEMS
+
+
+def _comm_args_worker(rank, world, port, q):
+    """A communicator cannot form without a GPU: every entry point answers with a status, none crashes."""
+    try:
+        _init(rank, world, port)
+        import ctypes
+
+        from unpopped_b200 import _lib
+
+        L = _lib.load()
+        uid = (ctypes.c_ubyte * 128)()
+        out = {"uid": L.up_sm100_comm_unique_id(uid) if rank == 0 else 0}
+        box = [bytes(uid)]
+        dist.broadcast_object_list(box, src=0)
+        uid = (ctypes.c_ubyte * 128).from_buffer_copy(box[0])
+        c = ctypes.c_void_p()
+        out["init_bad_rank"] = L.up_sm100_comm_init_rank(world, world, uid, ctypes.byref(c))
+        out["init_bad_size"] = L.up_sm100_comm_init_rank(0, 0, uid, ctypes.byref(c))
+        out["init_too_many"] = L.up_sm100_comm_init_rank(9, 0, uid, ctypes.byref(c))
+        out["init_null"] = L.up_sm100_comm_init_rank(world, rank, uid, None)
+        out["init_no_gpu"] = L.up_sm100_comm_init_rank(world, rank, uid, ctypes.byref(c))
+        t = _lib.UpTensor()
+        out["launch_no_comm"] = L.up_sm100_launch_multi(_lib.KERNEL["SCAN_I32"], ctypes.byref(t), 1, ctypes.byref(t),
+                                                        1, None, 0, None, 0, None, None)
+        n = ctypes.c_size_t(0)
+        out["ws_no_comm"] = L.up_sm100_workspace_bytes_multi(_lib.KERNEL["SCAN_I32"], ctypes.byref(t), 1,
+                                                             ctypes.byref(t), 1, None, 0, None, ctypes.byref(n))
+        out["rank_null"] = L.up_sm100_comm_rank(None, None, None)
+        out["destroy_null"] = L.up_sm100_comm_destroy(None)
+        out["uid_null"] = L.up_sm100_comm_unique_id(None)
+        q.put((rank, out))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, repr(e)))
+
+
+def test_communicator_argument_errors_on_gloo_ranks():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_comm_args_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        out = got[r]
+        assert isinstance(out, dict), out
+        for key in ("init_bad_rank", "init_bad_size", "init_too_many", "init_null", "launch_no_comm", "ws_no_comm",
+                    "rank_null", "destroy_null", "uid_null"):
+            assert out[key] == 7, (key, out[key])  # UP_ERR_INVALID
+        assert out["init_no_gpu"] in (5, 6), out  # UP_ERR_CUDA or UP_ERR_COMM: no device in this container
+    assert got[0]["uid"] in (0, 6)  # NCCL may or may not make an id without a network interface

@@ -108,11 +108,14 @@ def _desc(t: torch.Tensor, ek: str, shape=None):
 
 
 def block_cyclic_index(n_local: int, world: int) -> torch.Tensor:
-    """The global positions of every rank's n_local elements under the block-cyclic layout (local stripe k of rank
-    r is global stripe k * world + r), as a [world, n_local] int64 tensor."""
+    """The global positions of every rank's n_local elements under the block-cyclic layout, as a [world, n_local]
+    int64 tensor. Local stripe k of rank r is global stripe k * world + r; every stripe of a round has the same size
+    (full, or the shards' common remainder in the last round), so it starts at k * world * S + r * size_k."""
     pos = torch.arange(n_local, dtype=torch.int64)
     k, off = pos // STRIPE_ELEMS, pos % STRIPE_ELEMS
-    return torch.stack([(k * world + r) * STRIPE_ELEMS + off for r in range(world)])
+    last = (n_local - 1) // STRIPE_ELEMS if n_local > 0 else 0
+    size_k = torch.where(k == last, torch.full_like(k, n_local - last * STRIPE_ELEMS), torch.full_like(k, STRIPE_ELEMS))
+    return torch.stack([k * world * STRIPE_ELEMS + r * size_k + off for r in range(world)])
 
 
 def shard_carry(totals: torch.Tensor, rank: int, op: str, reverse: bool, local: Local) -> torch.Tensor:
