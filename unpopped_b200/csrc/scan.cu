@@ -304,6 +304,8 @@ constexpr int kQCompute = kQTile / (4 * kQRowChunks);  // 512 compute threads
 constexpr int kQCWarps = kQCompute / 32;            // 16
 constexpr int kQCopyWarp = kQCWarps, kQLookWarp = kQCWarps + 1;
 constexpr int kQThreads = kQCompute + 64;           // + copy warp + look-back warp
+constexpr int kQPubWarp = kQLookWarp + 1;           // block-cyclic form: CTA 0's stripe publisher
+constexpr int kQThreadsMulti = kQThreads + 32;
 constexpr int kQFold = 3;                           // tiles folded ahead of the rescan
 constexpr int kQRing = 5;                           // prefix and warp-total ring (>= kQFold + 2)
 constexpr int kQMaxWin = 5;                         // look-back flags per lane: grids of up to 160 CTAs
@@ -386,7 +388,7 @@ struct QFold {
 };
 
 template <int OP, bool REV, bool MULTI = false>
-__global__ void __launch_bounds__(kQThreads, 1)
+__global__ void __launch_bounds__(MULTI ? kQThreadsMulti : kQThreads, 1)
     scan_i32_persist_kernel(const int32_t* __restrict__ x, int32_t* __restrict__ y, int64_t k, int64_t tiles_per_row,
                             int64_t n_tiles, int exclusive, const int32_t* carry_in, ScanHeader* hdr, uint64_t* flags,
                             uint32_t epoch, uint64_t wait_ns, int withhold, MultiScan ms) {
@@ -438,6 +440,77 @@ __global__ void __launch_bounds__(kQThreads, 1)
     *s_abort = 1;
     for (int64_t jj = from; jj < n_mine; ++jj) st_relaxed_u64(flags + b + jj * P, make_flag(epoch, kFlagErr, 0));
   };
+
+  // Folds the m aggregates flags[t - m .. t - 1] into *sum once all have been published (bounded wait). False
+  // when one of them is aborted, the CTA is aborting, or the wait ran out.
+  auto window = [&](int64_t t, int m, int32_t* sum) -> bool {
+    *sum = id;
+    if (m <= 0) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+      uint64_t f[kQMaxWin];
+#pragma unroll
+      for (int i = 0; i < kQMaxWin; ++i) {  // all loads first: one round trip
+        const int d = lane + 32 * i + 1;
+        f[i] = d <= m ? ld_relaxed_u64(flags + (t - d)) : 0;
+      }
+      bool ready = true, err = false;
+#pragma unroll
+      for (int i = 0; i < kQMaxWin; ++i) {
+        const int d = lane + 32 * i + 1;
+        if (d <= m) {
+          const uint32_t st = flag_status(f[i], epoch);
+          ready = ready && st == kFlagAgg;
+          err = err || st == kFlagErr;
+        }
+      }
+      if (__any_sync(0xffffffffu, err) || __shfl_sync(0xffffffffu, *s_abort, 0)) return false;
+      if (__all_sync(0xffffffffu, ready)) {
+        int32_t v = id;
+#pragma unroll
+        for (int i = 0; i < kQMaxWin; ++i) {
+          const int d = lane + 32 * i + 1;
+          if (d <= m) v = comb<OP>(v, (int32_t)(uint32_t)f[i]);
+        }
+        *sum = warp_reduce<OP>(v);
+        return true;
+      }
+      if (__shfl_sync(0xffffffffu, globaltimer_ns() - t0 > wait_ns, 0)) return false;
+      __nanosleep(32);
+    }
+  };
+
+  // MULTI, CTA 0: sends the aggregate of local stripe `ls` to every other rank (global stripe ls * G + r), or
+  // "aborted" for local stripes ls onward, so that no rank waits for them.
+  auto publish_stripe = [&](int64_t ls, int32_t agg, bool aborted) {
+    if (!MULTI || b != 0) return;
+    const int64_t n_stripes = (n_tiles + P - 1) / P;
+    for (int64_t q = ls; q < (aborted ? n_stripes : ls + 1); ++q)
+      if (lane < ms.G && lane != ms.r)
+        st_relaxed_sys_u64(ms.peers[lane] + q * ms.G + ms.r,
+                           make_flag(ms.tag, aborted ? kFlagErr : kFlagAgg, aborted ? 0 : agg));
+  };
+
+  if (MULTI && warp == kQPubWarp) {
+    // ---------------- stripe publisher (block-cyclic form, CTA 0) ----------------
+    // A stripe's aggregate depends only on its tiles' aggregates, which the compute warps of every CTA publish as
+    // soon as they fold a tile (three tiles ahead of the rescans). Publishing it from here, not from the look-back
+    // warp (whose loop also waits on the other ranks), keeps every cross-GPU dependency on data alone: no rank's
+    // publication ever waits for another rank.
+    if (b == 0) {
+      const int64_t n_stripes = (n_tiles + P - 1) / P;
+      for (int64_t q = 0; q < n_stripes; ++q) {
+        const int64_t hi = (q + 1) * P < n_tiles ? (q + 1) * P : n_tiles;
+        int32_t sum = id;
+        if (!window(hi, (int)(hi - q * P), &sum)) {
+          publish_stripe(q, 0, true);
+          break;
+        }
+        publish_stripe(q, sum, false);
+      }
+    }
+    return;
+  }
 
   if (warp == kQCopyWarp) {
     // ---------------- copy warp ----------------
@@ -500,44 +573,6 @@ __global__ void __launch_bounds__(kQThreads, 1)
     // ---------------- look-back warp ----------------
     const int32_t cin = carry_in ? *carry_in : id;
     int32_t pre_prev = id;
-    // Folds the m aggregates flags[t - m .. t - 1] into *sum once all have been published (bounded wait). False
-    // when one of them is aborted, the CTA is aborting, or the wait ran out.
-    auto window = [&](int64_t t, int m, int32_t* sum) -> bool {
-      *sum = id;
-      if (m <= 0) return true;
-      const uint64_t t0 = globaltimer_ns();
-      while (true) {
-        uint64_t f[kQMaxWin];
-#pragma unroll
-        for (int i = 0; i < kQMaxWin; ++i) {  // all loads first: one round trip
-          const int d = lane + 32 * i + 1;
-          f[i] = d <= m ? ld_relaxed_u64(flags + (t - d)) : 0;
-        }
-        bool ready = true, err = false;
-#pragma unroll
-        for (int i = 0; i < kQMaxWin; ++i) {
-          const int d = lane + 32 * i + 1;
-          if (d <= m) {
-            const uint32_t st = flag_status(f[i], epoch);
-            ready = ready && st == kFlagAgg;
-            err = err || st == kFlagErr;
-          }
-        }
-        if (__any_sync(0xffffffffu, err) || __shfl_sync(0xffffffffu, *s_abort, 0)) return false;
-        if (__all_sync(0xffffffffu, ready)) {
-          int32_t v = id;
-#pragma unroll
-          for (int i = 0; i < kQMaxWin; ++i) {
-            const int d = lane + 32 * i + 1;
-            if (d <= m) v = comb<OP>(v, (int32_t)(uint32_t)f[i]);
-          }
-          *sum = warp_reduce<OP>(v);
-          return true;
-        }
-        if (__shfl_sync(0xffffffffu, globaltimer_ns() - t0 > wait_ns, 0)) return false;
-        __nanosleep(32);
-      }
-    };
     // MULTI: folds the other ranks' stripe aggregates of global stripes [lo, hi) (at most kMaxRanks - 1 of them)
     // once all have arrived (bounded wait). The ops are commutative, so their order does not matter.
     auto remote = [&](int64_t lo, int64_t hi, int32_t* sum) -> bool {
@@ -557,16 +592,6 @@ __global__ void __launch_bounds__(kQThreads, 1)
         __nanosleep(64);
       }
     };
-    // MULTI, CTA 0: sends the aggregate of local stripe `ls` to every other rank (global stripe ls * G + r), or
-    // "aborted" for local stripes ls onward, so that no rank waits for them.
-    auto publish_stripe = [&](int64_t ls, int32_t agg, bool aborted) {
-      if (!MULTI || b != 0) return;
-      const int64_t n_stripes = (n_tiles + P - 1) / P;
-      for (int64_t q = ls; q < (aborted ? n_stripes : ls + 1); ++q)
-        if (lane < ms.G && lane != ms.r)
-          st_relaxed_sys_u64(ms.peers[lane] + q * ms.G + ms.r,
-                             make_flag(ms.tag, aborted ? kFlagErr : kFlagAgg, aborted ? 0 : agg));
-    };
     QCursor c;
     c.init(b, tiles_per_row);
     for (int64_t j = 0; j < n_mine; ++j, c.next(P, tiles_per_row)) {
@@ -577,11 +602,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
         const int m = (int)(chain ? P : c.q);  // aggregates to add: tiles t - m .. t - 1
         int32_t sum = id;
         good = window(c.t, m, &sum);
-        if (good) {
-          pre = comb<OP>(chain ? pre_prev : cin, sum);
-          // CTA 0's window of P tiles is exactly its previous local stripe: publish it before waiting on anyone
-          if (MULTI && chain) publish_stripe(j - 1, sum, false);
-        }
+        if (good) pre = comb<OP>(chain ? pre_prev : cin, sum);
       }
       if (MULTI && good) {
         // the other ranks' stripes between this CTA's previous tile and this one: local stripe j - 1's successors
@@ -591,9 +612,8 @@ __global__ void __launch_bounds__(kQThreads, 1)
         good = remote(lo, hi, &rs);
         if (good) pre = comb<OP>(pre, rs);
       }
-      if (!good) {
+      if (!good) {  // the publisher sees the abort and marks this rank's remaining stripes for the others
         if (lane == 0) abort_from(j);
-        publish_stripe(j > 0 ? j - 1 : 0, 0, true);
         return;
       }
       pre_prev = pre;
@@ -606,13 +626,6 @@ __global__ void __launch_bounds__(kQThreads, 1)
         tc::mbar_arrive(&pfull[j % kQRing]);
       }
       __syncwarp();
-    }
-    if (MULTI && b == 0 && n_mine > 0) {
-      // the last local stripe (tiles (n_mine - 1) * P .. n_tiles - 1) has no next tile of CTA 0 to close it
-      const int64_t last = (n_mine - 1) * P;
-      int32_t sum = id;
-      if (window(n_tiles, (int)(n_tiles - last), &sum)) publish_stripe(n_mine - 1, sum, false);
-      else publish_stripe(n_mine - 1, 0, true);
     }
     return;
   }
@@ -1002,16 +1015,20 @@ int scan_i32_block_cyclic(const int32_t* x, int32_t* y, int64_t k, int op, int e
                                      : (const void*)scan_i32_persist_kernel<UP_OP_MIN, false, true>;
   e = ensure_smem_attr(fn, (int)kQSmem);
   if (e != cudaSuccess) return cuda_status(e);
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kQThreadsMulti, kQSmem);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (per_sm < 1) return fail_with(UP_ERR_UNSUPPORTED, "block-cyclic scan: its CTA does not fit on an SM");
   const uint64_t wns = wait_limit_ns();
   const int withhold = take_withhold_flag();
   if (op == UP_OP_SUM)
-    scan_i32_persist_kernel<UP_OP_SUM, false, true><<<kStripeTiles, kQThreads, kQSmem, s>>>(
+    scan_i32_persist_kernel<UP_OP_SUM, false, true><<<kStripeTiles, kQThreadsMulti, kQSmem, s>>>(
         x, y, k, tiles, tiles, exclusive, carry_in, hdr, flags, epoch, wns, withhold, m);
   else if (op == UP_OP_MAX)
-    scan_i32_persist_kernel<UP_OP_MAX, false, true><<<kStripeTiles, kQThreads, kQSmem, s>>>(
+    scan_i32_persist_kernel<UP_OP_MAX, false, true><<<kStripeTiles, kQThreadsMulti, kQSmem, s>>>(
         x, y, k, tiles, tiles, exclusive, carry_in, hdr, flags, epoch, wns, withhold, m);
   else
-    scan_i32_persist_kernel<UP_OP_MIN, false, true><<<kStripeTiles, kQThreads, kQSmem, s>>>(
+    scan_i32_persist_kernel<UP_OP_MIN, false, true><<<kStripeTiles, kQThreadsMulti, kQSmem, s>>>(
         x, y, k, tiles, tiles, exclusive, carry_in, hdr, flags, epoch, wns, withhold, m);
   note_launch();
   return check_launch();
