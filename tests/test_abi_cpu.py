@@ -240,3 +240,19 @@ def test_workspace_sizes():
     ins = (_lib.UpTensor * 1)(Operand("I32", (4, 40000)).to_c())
     assert L.up_sm100_workspace_bytes(_lib.KERNEL["SCAN_I32"], ins, 1, ins, 1, None, 0, ctypes.byref(n)) == 0
     assert n.value == 64 + 8 * 4 * 5
+
+
+# The reference's cross-emitter corpus (crates/unpopped/src/launch_cases.rs:140-180): four launched elementwise kernels,
+# each with two inputs and one output of one dtype. This backend's kernel layer takes only the dequant-GEMM function,
+# so its conformance answer for every case is the typed UnsupportedKernel decline, never an approximation.
+LAUNCH_CASES = [("fma_shape_f32", "F32", (5, 7)), ("div_f32", "F32", (6, 5)), ("sub_i32", "I32", (3, 11)),
+                ("add_u32", "U32", (37,))]
+
+
+@pytest.mark.parametrize("name,dtype,shape", LAUNCH_CASES)
+def test_launch_cases_corpus_is_declined_with_unsupported_kernel(name, dtype, shape):
+    b = CudaSm100()
+    plan = Plan("KERNEL_FN", [Operand(dtype, shape), Operand(dtype, shape), Operand(dtype, shape)], dtype=dtype)
+    with pytest.raises(LowerError) as e:
+        b.lower(plan)
+    assert e.value.variant == "UnsupportedKernel", name
