@@ -313,6 +313,12 @@ constexpr int kQMaxGrid = 32 * kQMaxWin;
 constexpr size_t kQSmem = (size_t)kQStages * kQTileBytes + 256;
 static_assert(kQRing >= kQFold + 2, "warp-total ring");
 static_assert(kQStages >= kQFold + 2, "stages");
+// The block-cyclic form folds one tile further ahead (its rescans also wait on other GPUs' stripes, whose arrival
+// the fold look-ahead hides), with a seventh stage so that two tiles still load ahead of the folds.
+constexpr int kQStagesMulti = 7, kQFoldMulti = 4, kQRingMulti = 6;
+constexpr size_t kQSmemMulti = (size_t)kQStagesMulti * kQTileBytes + 256;
+static_assert(kQRingMulti >= kQFoldMulti + 2 && kQStagesMulti >= kQFoldMulti + 2, "block-cyclic pipeline");
+static_assert(kQSmemMulti <= 227 * 1024 - 1024, "block-cyclic stages fit the opt-in shared memory");
 
 // Barrier `id` over `n` threads that also returns whether any of them passed `v`.
 __device__ __forceinline__ bool named_bar_or(int id, int n, bool v) {
@@ -393,14 +399,17 @@ __global__ void __launch_bounds__(MULTI ? kQThreadsMulti : kQThreads, 1)
                             int64_t n_tiles, int exclusive, const int32_t* carry_in, ScanHeader* hdr, uint64_t* flags,
                             uint32_t epoch, uint64_t wait_ns, int withhold, MultiScan ms) {
   static_assert(!(MULTI && REV), "the block-cyclic form scans forward");
+  constexpr int STAGES = MULTI ? kQStagesMulti : kQStages;  // shared-memory tile stages
+  constexpr int FOLD = MULTI ? kQFoldMulti : kQFold;        // tiles folded ahead of the rescan
+  constexpr int RING = MULTI ? kQRingMulti : kQRing;        // prefix and warp-total ring
   constexpr bool reverse = REV;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)kQStages * kQTileBytes);  // [stages] data landed
-  uint64_t* done = full + kQStages;      // [stages] rescanned (one arrival per compute warp)
-  uint64_t* pfull = done + kQStages;     // [ring] prefix delivered (look-back lane 0)
-  uint64_t* pempty = pfull + kQRing;     // [ring] prefix consumed (one arrival per compute warp)
-  __shared__ int32_t s_wt[kQRing][kQCWarps];
-  __shared__ int32_t s_prefix[kQRing];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)STAGES * kQTileBytes);  // [stages] data landed
+  uint64_t* done = full + STAGES;      // [stages] rescanned (one arrival per compute warp)
+  uint64_t* pfull = done + STAGES;     // [ring] prefix delivered (look-back lane 0)
+  uint64_t* pempty = pfull + RING;     // [ring] prefix consumed (one arrival per compute warp)
+  __shared__ int32_t s_wt[RING][kQCWarps];
+  __shared__ int32_t s_prefix[RING];
   __shared__ int s_abort_mem;
   volatile int* s_abort = &s_abort_mem;
 
@@ -410,11 +419,11 @@ __global__ void __launch_bounds__(MULTI ? kQThreadsMulti : kQThreads, 1)
   const int32_t id = ident<OP>();
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kQStages; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&done[s], kQCWarps);
     }
-    for (int s = 0; s < kQRing; ++s) {
+    for (int s = 0; s < RING; ++s) {
       tc::mbar_init(&pfull[s], 1);
       tc::mbar_init(&pempty[s], kQCWarps);
     }
@@ -431,9 +440,9 @@ __global__ void __launch_bounds__(MULTI ? kQThreadsMulti : kQThreads, 1)
     const int64_t lo = c.q * kQTile;
     return c.row * k + (reverse ? (k - lo - cnt) : lo);
   };
-  auto stage = [&](int64_t j) { return smem + (size_t)(j % kQStages) * kQTileBytes; };
-  auto sphase = [&](int64_t j) { return (uint32_t)((j / kQStages) & 1); };
-  auto rphase = [&](int64_t j) { return (uint32_t)((j / kQRing) & 1); };
+  auto stage = [&](int64_t j) { return smem + (size_t)(j % STAGES) * kQTileBytes; };
+  auto sphase = [&](int64_t j) { return (uint32_t)((j / STAGES) & 1); };
+  auto rphase = [&](int64_t j) { return (uint32_t)((j / RING) & 1); };
   // Marks this CTA's tiles from `from` on as aborted, so that no other CTA waits for them.
   auto abort_from = [&](int64_t from) {
     if (!*s_abort) atomicOr(&hdr->error, 1u);
@@ -531,9 +540,9 @@ __global__ void __launch_bounds__(MULTI ? kQThreadsMulti : kQThreads, 1)
       bool ok = true;
       while (issued < n_mine && !*s_abort) {
         const int64_t j = issued;
-        if (j >= kQStages) {  // the stage's previous tile must be rescanned and sent out first
-          const int64_t jo = j - kQStages;
-          if (!tc::mbar_wait(&done[jo % kQStages], sphase(jo), wait_ns, s_abort)) {
+        if (j >= STAGES) {  // the stage's previous tile must be rescanned and sent out first
+          const int64_t jo = j - STAGES;
+          if (!tc::mbar_wait(&done[jo % STAGES], sphase(jo), wait_ns, s_abort)) {
             ok = false;
             break;
           }
@@ -543,7 +552,7 @@ __global__ void __launch_bounds__(MULTI ? kQThreadsMulti : kQThreads, 1)
         }
         const int cnt = count_of(lc);
         const uint32_t bytes = (uint32_t)cnt * 4u;
-        uint64_t* bar = &full[j % kQStages];
+        uint64_t* bar = &full[j % STAGES];
         tc::mbar_arrive_expect_tx(bar, bytes);
         const char* src = reinterpret_cast<const char*>(x + start_of(lc, cnt));
         for (uint32_t off = 0; off < bytes; off += 16384u)
@@ -552,7 +561,7 @@ __global__ void __launch_bounds__(MULTI ? kQThreadsMulti : kQThreads, 1)
         issued = j + 1;
       }
       for (int64_t jo = stored; ok && jo < issued && !*s_abort; ++jo) {
-        if (!tc::mbar_wait(&done[jo % kQStages], sphase(jo), wait_ns, s_abort)) {
+        if (!tc::mbar_wait(&done[jo % STAGES], sphase(jo), wait_ns, s_abort)) {
           ok = false;
           break;
         }
@@ -561,8 +570,8 @@ __global__ void __launch_bounds__(MULTI ? kQThreadsMulti : kQThreads, 1)
       if (!ok && !*s_abort) abort_from(stored);
       if (*s_abort) {
         // loads still in flight must land before this CTA's shared memory is released
-        for (int64_t j = (issued > kQStages ? issued - kQStages : 0); j < issued; ++j)
-          tc::mbar_wait(&full[j % kQStages], sphase(j), wait_ns, nullptr);
+        for (int64_t j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j)
+          tc::mbar_wait(&full[j % STAGES], sphase(j), wait_ns, nullptr);
       }
       asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
@@ -618,12 +627,12 @@ __global__ void __launch_bounds__(MULTI ? kQThreadsMulti : kQThreads, 1)
       }
       pre_prev = pre;
       if (lane == 0) {
-        if (j >= kQRing && !tc::mbar_wait(&pempty[j % kQRing], rphase(j - kQRing), wait_ns, s_abort)) {
+        if (j >= RING && !tc::mbar_wait(&pempty[j % RING], rphase(j - RING), wait_ns, s_abort)) {
           abort_from(j);
           return;
         }
-        s_prefix[j % kQRing] = pre;
-        tc::mbar_arrive(&pfull[j % kQRing]);
+        s_prefix[j % RING] = pre;
+        tc::mbar_arrive(&pfull[j % RING]);
       }
       __syncwarp();
     }
@@ -670,7 +679,7 @@ __global__ void __launch_bounds__(MULTI ? kQThreadsMulti : kQThreads, 1)
     const int32_t inc = warp_incl_scan<OP>(run, lane);
     st.texcl = __shfl_up_sync(0xffffffffu, inc, 1);
     if (lane == 0) st.texcl = id;
-    if (lane == 31) s_wt[j % kQRing][warp] = inc;
+    if (lane == 31) s_wt[j % RING][warp] = inc;
   };
   // After the barrier that follows fold_math: the tile's aggregate goes out as its look-back flag, and the
   // warp totals are replaced by their exclusive prefixes, which the tile's rescan reads one per warp.
@@ -679,25 +688,25 @@ __global__ void __launch_bounds__(MULTI ? kQThreadsMulti : kQThreads, 1)
       int32_t run = id;
 #pragma unroll
       for (int w = 0; w < kQCWarps; ++w) {
-        const int32_t v = s_wt[j % kQRing][w];
-        s_wt[j % kQRing][w] = run;
+        const int32_t v = s_wt[j % RING][w];
+        s_wt[j % RING][w] = run;
         run = comb<OP>(run, v);
       }
       if (!(withhold && t == 0)) st_relaxed_u64(flags + t, make_flag(epoch, kFlagAgg, run));
     }
   };
 
-  QFold st[kQFold + 1];  // st[0]: the tile to rescan next; st[i]: the tile folded i tiles after it
+  QFold st[FOLD + 1];  // st[0]: the tile to rescan next; st[i]: the tile folded i tiles after it
   int64_t j = 0;
   bool ok = true;
-  // prologue: fold the first kQFold tiles (unrolled, so the states stay in registers)
+  // prologue: fold the first FOLD tiles (unrolled, so the states stay in registers)
 #pragma unroll
-  for (int jf = 0; jf < kQFold; ++jf) {
+  for (int jf = 0; jf < FOLD; ++jf) {
     if (ok && jf < n_mine) {
       const int cnt = count_of(fc);
       const int64_t t = fc.t;
       fc.next(P, tiles_per_row);
-      const bool landed = tc::mbar_wait(&full[jf % kQStages], sphase(jf), wait_ns, s_abort);
+      const bool landed = tc::mbar_wait(&full[jf % STAGES], sphase(jf), wait_ns, s_abort);
       int32_t v[kQRowChunks][4];
       load_row(jf, cnt, v);
       fold_math(jf, v, st[jf]);
@@ -705,23 +714,23 @@ __global__ void __launch_bounds__(MULTI ? kQThreadsMulti : kQThreads, 1)
       else publish(jf, t);
     }
   }
-  // Steady state: iteration j folds tile j + kQFold (publishing its aggregate as early as possible), then
+  // Steady state: iteration j folds tile j + FOLD (publishing its aggregate as early as possible), then
   // rescans tile j. One barrier per iteration; it also settles whether any warp's wait for the previous
   // prefix ran out (such a warp releases nothing and has flagged the abort).
   bool good_prev = true;
   for (; ok && j < n_mine; ++j) {
-    const bool fold_next = j + kQFold < n_mine;
-    const int64_t jf = j + kQFold;
+    const bool fold_next = j + FOLD < n_mine;
+    const int64_t jf = j + FOLD;
     bool good_f = true;
     int64_t ft = 0;
     if (fold_next) {
       const int fcnt = count_of(fc);
       ft = fc.t;
       fc.next(P, tiles_per_row);
-      good_f = tc::mbar_wait(&full[jf % kQStages], sphase(jf), wait_ns, s_abort);
+      good_f = tc::mbar_wait(&full[jf % STAGES], sphase(jf), wait_ns, s_abort);
       int32_t fv[kQRowChunks][4];
       load_row(jf, fcnt, fv);
-      fold_math(jf, fv, st[kQFold]);
+      fold_math(jf, fv, st[FOLD]);
     }
     if (named_bar_or(1, kQCompute, !good_f || !good_prev || *s_abort)) {
       ok = false;
@@ -732,11 +741,11 @@ __global__ void __launch_bounds__(MULTI ? kQThreadsMulti : kQThreads, 1)
     // pass 2 of tile j
     const int rcnt = count_of(rc);
     rc.next(P, tiles_per_row);
-    const bool gr = tc::mbar_wait(&pfull[j % kQRing], rphase(j), wait_ns, s_abort);
+    const bool gr = tc::mbar_wait(&pfull[j % RING], rphase(j), wait_ns, s_abort);
     int32_t rv[kQRowChunks][4];
     load_row(j, rcnt, rv);
-    const int32_t pre = s_prefix[j % kQRing];
-    const int32_t wpre = s_wt[j % kQRing][warp];  // exclusive prefix of this warp's rows (see publish)
+    const int32_t pre = s_prefix[j % RING];
+    const int32_t wpre = s_wt[j % RING][warp];  // exclusive prefix of this warp's rows (see publish)
     const int32_t base = comb<OP>(comb<OP>(pre, wpre), st[0].texcl);
     int4* wbuf = reinterpret_cast<int4*>(stage(j));
     const int nch = rcnt >> 2;
@@ -762,15 +771,15 @@ __global__ void __launch_bounds__(MULTI ? kQThreadsMulti : kQThreads, 1)
     const bool wgood = __all_sync(0xffffffffu, gr);
     if (lane == 0) {
       if (wgood) {  // one arrival per warp
-        tc::mbar_arrive(&done[j % kQStages]);
-        tc::mbar_arrive(&pempty[j % kQRing]);
+        tc::mbar_arrive(&done[j % STAGES]);
+        tc::mbar_arrive(&pempty[j % RING]);
       } else {
         abort_from(j);  // stops the copy and look-back warps; the next barrier stops the compute warps
       }
     }
     good_prev = wgood;
 #pragma unroll
-    for (int q = 0; q < kQFold; ++q) st[q] = st[q + 1];
+    for (int q = 0; q < FOLD; ++q) st[q] = st[q + 1];
   }
   if (!ok && threadIdx.x == 0) abort_from(j);
 }
@@ -1013,22 +1022,22 @@ int scan_i32_block_cyclic(const int32_t* x, int32_t* y, int64_t k, int op, int e
   const void* fn = op == UP_OP_SUM   ? (const void*)scan_i32_persist_kernel<UP_OP_SUM, false, true>
                    : op == UP_OP_MAX ? (const void*)scan_i32_persist_kernel<UP_OP_MAX, false, true>
                                      : (const void*)scan_i32_persist_kernel<UP_OP_MIN, false, true>;
-  e = ensure_smem_attr(fn, (int)kQSmem);
+  e = ensure_smem_attr(fn, (int)kQSmemMulti);
   if (e != cudaSuccess) return cuda_status(e);
   int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kQThreadsMulti, kQSmem);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kQThreadsMulti, kQSmemMulti);
   if (e != cudaSuccess) return cuda_status(e);
   if (per_sm < 1) return fail_with(UP_ERR_UNSUPPORTED, "block-cyclic scan: its CTA does not fit on an SM");
   const uint64_t wns = wait_limit_ns();
   const int withhold = take_withhold_flag();
   if (op == UP_OP_SUM)
-    scan_i32_persist_kernel<UP_OP_SUM, false, true><<<kStripeTiles, kQThreadsMulti, kQSmem, s>>>(
+    scan_i32_persist_kernel<UP_OP_SUM, false, true><<<kStripeTiles, kQThreadsMulti, kQSmemMulti, s>>>(
         x, y, k, tiles, tiles, exclusive, carry_in, hdr, flags, epoch, wns, withhold, m);
   else if (op == UP_OP_MAX)
-    scan_i32_persist_kernel<UP_OP_MAX, false, true><<<kStripeTiles, kQThreadsMulti, kQSmem, s>>>(
+    scan_i32_persist_kernel<UP_OP_MAX, false, true><<<kStripeTiles, kQThreadsMulti, kQSmemMulti, s>>>(
         x, y, k, tiles, tiles, exclusive, carry_in, hdr, flags, epoch, wns, withhold, m);
   else
-    scan_i32_persist_kernel<UP_OP_MIN, false, true><<<kStripeTiles, kQThreadsMulti, kQSmem, s>>>(
+    scan_i32_persist_kernel<UP_OP_MIN, false, true><<<kStripeTiles, kQThreadsMulti, kQSmemMulti, s>>>(
         x, y, k, tiles, tiles, exclusive, carry_in, hdr, flags, epoch, wns, withhold, m);
   note_launch();
   return check_launch();
