@@ -313,9 +313,9 @@ constexpr int kQMaxGrid = 32 * kQMaxWin;
 constexpr size_t kQSmem = (size_t)kQStages * kQTileBytes + 256;
 static_assert(kQRing >= kQFold + 2, "warp-total ring");
 static_assert(kQStages >= kQFold + 2, "stages");
-// The block-cyclic form folds one tile further ahead (its rescans also wait on other GPUs' stripes, whose arrival
-// the fold look-ahead hides), with a seventh stage so that two tiles still load ahead of the folds.
-constexpr int kQStagesMulti = 7, kQFoldMulti = 4, kQRingMulti = 6;
+// The pipeline depths of the block-cyclic form (the same as the single-GPU form: folding a fourth tile ahead over
+// seven stages measured no faster on two GPUs, 0.466 against 0.458 ms per 2^28-element shard).
+constexpr int kQStagesMulti = 6, kQFoldMulti = 3, kQRingMulti = 5;
 constexpr size_t kQSmemMulti = (size_t)kQStagesMulti * kQTileBytes + 256;
 static_assert(kQRingMulti >= kQFoldMulti + 2 && kQStagesMulti >= kQFoldMulti + 2, "block-cyclic pipeline");
 static_assert(kQSmemMulti <= 227 * 1024 - 1024, "block-cyclic stages fit the opt-in shared memory");
@@ -582,23 +582,51 @@ __global__ void __launch_bounds__(MULTI ? kQThreadsMulti : kQThreads, 1)
     // ---------------- look-back warp ----------------
     const int32_t cin = carry_in ? *carry_in : id;
     int32_t pre_prev = id;
-    // MULTI: folds the other ranks' stripe aggregates of global stripes [lo, hi) (at most kMaxRanks - 1 of them)
-    // once all have arrived (bounded wait). The ops are commutative, so their order does not matter.
-    auto remote = [&](int64_t lo, int64_t hi, int32_t* sum) -> bool {
+      // MULTI: `window` and the other ranks' stripe aggregates of global stripes [lo, hi) (at most kMaxRanks - 1)
+    // in one round trip: both sets of loads are issued together and tested together (bounded wait). The ops are
+    // commutative, so the stripes fold in any order.
+    auto window_remote = [&](int64_t t, int m, int64_t lo, int64_t hi, int32_t* sum, int32_t* rsum) -> bool {
       *sum = id;
+      *rsum = id;
       const int n = (int)(hi - lo);
-      if (n <= 0) return true;
       const uint64_t t0 = globaltimer_ns();
       while (true) {
-        const uint64_t f = lane < n ? ld_relaxed_sys_u64(ms.sflags + lo + lane) : 0;
-        const uint32_t st = lane < n ? flag_status(f, ms.tag) : kFlagAgg;
-        if (__any_sync(0xffffffffu, st == kFlagErr) || __shfl_sync(0xffffffffu, *s_abort, 0)) return false;
-        if (__all_sync(0xffffffffu, st == kFlagAgg)) {
-          *sum = warp_reduce<OP>(lane < n ? (int32_t)(uint32_t)f : id);
+        uint64_t f[kQMaxWin];
+#pragma unroll
+        for (int i = 0; i < kQMaxWin; ++i) {
+          const int d = lane + 32 * i + 1;
+          f[i] = d <= m ? ld_relaxed_u64(flags + (t - d)) : 0;
+        }
+        const uint64_t g = lane < n ? ld_relaxed_sys_u64(ms.sflags + lo + lane) : 0;
+        bool ready = true, err = false;
+#pragma unroll
+        for (int i = 0; i < kQMaxWin; ++i) {
+          const int d = lane + 32 * i + 1;
+          if (d <= m) {
+            const uint32_t st = flag_status(f[i], epoch);
+            ready = ready && st == kFlagAgg;
+            err = err || st == kFlagErr;
+          }
+        }
+        if (lane < n) {
+          const uint32_t st = flag_status(g, ms.tag);
+          ready = ready && st == kFlagAgg;
+          err = err || st == kFlagErr;
+        }
+        if (__any_sync(0xffffffffu, err) || __shfl_sync(0xffffffffu, *s_abort, 0)) return false;
+        if (__all_sync(0xffffffffu, ready)) {
+          int32_t v = id;
+#pragma unroll
+          for (int i = 0; i < kQMaxWin; ++i) {
+            const int d = lane + 32 * i + 1;
+            if (d <= m) v = comb<OP>(v, (int32_t)(uint32_t)f[i]);
+          }
+          *sum = warp_reduce<OP>(v);
+          *rsum = warp_reduce<OP>(lane < n ? (int32_t)(uint32_t)g : id);
           return true;
         }
         if (__shfl_sync(0xffffffffu, globaltimer_ns() - t0 > wait_ns, 0)) return false;
-        __nanosleep(64);
+        __nanosleep(32);
       }
     };
     QCursor c;
@@ -606,20 +634,21 @@ __global__ void __launch_bounds__(MULTI ? kQThreadsMulti : kQThreads, 1)
     for (int64_t j = 0; j < n_mine; ++j, c.next(P, tiles_per_row)) {
       int32_t pre = cin;
       bool good = true;
-      if (c.q != 0) {
-        const bool chain = j > 0 && c.q >= P;  // this CTA's previous tile is in the same row
-        const int m = (int)(chain ? P : c.q);  // aggregates to add: tiles t - m .. t - 1
-        int32_t sum = id;
-        good = window(c.t, m, &sum);
-        if (good) pre = comb<OP>(chain ? pre_prev : cin, sum);
-      }
-      if (MULTI && good) {
+      const bool chain = j > 0 && c.q >= P;        // this CTA's previous tile is in the same row
+      const int m = c.q == 0 ? 0 : (int)(chain ? P : c.q);  // aggregates to add: tiles t - m .. t - 1
+      if (!MULTI) {
+        if (m > 0) {
+          int32_t sum = id;
+          good = window(c.t, m, &sum);
+          if (good) pre = comb<OP>(chain ? pre_prev : cin, sum);
+        }
+      } else {
         // the other ranks' stripes between this CTA's previous tile and this one: local stripe j - 1's successors
         // on ranks r + 1 .. G - 1 and local stripe j's predecessors on ranks 0 .. r - 1 (for j = 0, the latter)
         const int64_t lo = j == 0 ? 0 : (j - 1) * ms.G + ms.r + 1, hi = j * ms.G + ms.r;
-        int32_t rs = id;
-        good = remote(lo, hi, &rs);
-        if (good) pre = comb<OP>(pre, rs);
+        int32_t sum = id, rs = id;
+        good = window_remote(c.t, m, lo, hi, &sum, &rs);
+        if (good) pre = comb<OP>(m > 0 ? comb<OP>(chain ? pre_prev : cin, sum) : cin, rs);
       }
       if (!good) {  // the publisher sees the abort and marks this rank's remaining stripes for the others
         if (lane == 0) abort_from(j);
