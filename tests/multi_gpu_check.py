@@ -36,8 +36,8 @@ def main():
     comm = udist.Comm()
     checks = {}
 
-    def gen(seed):
-        return torch.Generator(device="cpu").manual_seed(seed)
+    def gen(seed):  # the same stream on every rank (same device type, same seed)
+        return torch.Generator(device=dev).manual_seed(seed)
 
     def agree(name, ok):
         t = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
@@ -46,7 +46,7 @@ def main():
 
     # ---- scan over contiguous shards ----
     n = (1 << 22) + 12
-    full = torch.randint(-(2 ** 31), 2 ** 31 - 1, (world * n,), generator=gen(1), dtype=torch.int32).to(dev)
+    full = torch.randint(-(2 ** 31), 2 ** 31 - 1, (world * n,), generator=gen(1), dtype=torch.int32, device=dev)
     mine = full[rank * n:(rank + 1) * n].contiguous()
     for op, ex, rev in (("sum", False, False), ("sum", True, False), ("max", False, False), ("sum", False, True),
                         ("min", True, True)):
@@ -56,8 +56,8 @@ def main():
 
     # ---- block-cyclic scan ----
     for n_local, seed in ((3 * udist.STRIPE_ELEMS + 8192 * 5 + 4, 2), (1 << 28, 3)):
-        glob = torch.randint(0, 16, (world * n_local,), generator=gen(seed), dtype=torch.int32).to(dev)
-        idx = udist.block_cyclic_index(n_local, world)[rank].to(dev)
+        glob = torch.randint(0, 16, (world * n_local,), generator=gen(seed), dtype=torch.int32, device=dev)
+        idx = udist.block_cyclic_index(n_local, world, rank, dev)
         x = glob[idx].contiguous()
         cases = (("sum", False), ("sum", True), ("max", False), ("min", True)) if n_local < (1 << 28) else \
             (("sum", False),)
@@ -81,7 +81,7 @@ def main():
     agree("w4a16_split_rows", torch.equal(out.view(torch.int16), want.view(torch.int16)))
 
     # ---- row-parallel lifts on row shards ----
-    xs = torch.randn(4096 * world, 8192, generator=gen(6)).to(dev)[rank * 4096:(rank + 1) * 4096].contiguous()
+    xs = torch.randn(4096 * world, 8192, generator=gen(6), device=dev)[rank * 4096:(rank + 1) * 4096].contiguous()
     rs = torch.empty(4096, device=dev)
     udist.sharded_rows("ROW_SUM_F32", [(xs, "F32")], [(rs, "F32")], [1, 256], comm, dev)
     agree("row_sum_shard", torch.equal(rs.view(torch.int32), ops.row_sum(xs, "f32").view(torch.int32)))
@@ -99,8 +99,8 @@ def main():
 
     # ---- failure detection across GPUs: a withheld flag, bounded waits, the error reported on every rank ----
     n_local = 2 * udist.STRIPE_ELEMS
-    glob = torch.randint(0, 16, (world * n_local,), generator=gen(9), dtype=torch.int32).to(dev)
-    idx = udist.block_cyclic_index(n_local, world)[rank].to(dev)
+    glob = torch.randint(0, 16, (world * n_local,), generator=gen(9), dtype=torch.int32, device=dev)
+    idx = udist.block_cyclic_index(n_local, world, rank, dev)
     x = glob[idx].contiguous()
     udist.sharded_scan(x, "sum", layout="block_cyclic", comm=comm)  # the workspace for this shape exists
     ws = comm._ws[_lib.KERNEL["SCAN_I32"]]

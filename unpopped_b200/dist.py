@@ -107,14 +107,17 @@ def _desc(t: torch.Tensor, ek: str, shape=None):
     return Operand(ek, shape, ptr=t.data_ptr()).to_c()
 
 
-def block_cyclic_index(n_local: int, world: int) -> torch.Tensor:
-    """The global positions of every rank's n_local elements under the block-cyclic layout, as a [world, n_local]
-    int64 tensor. Local stripe k of rank r is global stripe k * world + r; every stripe of a round has the same size
-    (full, or the shards' common remainder in the last round), so it starts at k * world * S + r * size_k."""
-    pos = torch.arange(n_local, dtype=torch.int64)
+def block_cyclic_index(n_local: int, world: int, rank: int | None = None, device="cpu") -> torch.Tensor:
+    """The global positions of a rank's n_local elements under the block-cyclic layout (int64 [n_local]), or of
+    every rank's ([world, n_local]) when `rank` is None. Local stripe k of rank r is global stripe k * world + r;
+    every stripe of a round has the same size (full, or the shards' common remainder in the last round), so it starts
+    at k * world * S + r * size_k."""
+    pos = torch.arange(n_local, dtype=torch.int64, device=device)
     k, off = pos // STRIPE_ELEMS, pos % STRIPE_ELEMS
     last = (n_local - 1) // STRIPE_ELEMS if n_local > 0 else 0
     size_k = torch.where(k == last, torch.full_like(k, n_local - last * STRIPE_ELEMS), torch.full_like(k, STRIPE_ELEMS))
+    if rank is not None:
+        return k * world * STRIPE_ELEMS + rank * size_k + off
     return torch.stack([k * world * STRIPE_ELEMS + r * size_k + off for r in range(world)])
 
 
