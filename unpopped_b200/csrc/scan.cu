@@ -313,9 +313,9 @@ constexpr int kQMaxGrid = 32 * kQMaxWin;
 constexpr size_t kQSmem = (size_t)kQStages * kQTileBytes + 256;
 static_assert(kQRing >= kQFold + 2, "warp-total ring");
 static_assert(kQStages >= kQFold + 2, "stages");
-// The pipeline depths of the block-cyclic form (the same as the single-GPU form: folding a fourth tile ahead over
-// seven stages measured no faster on two GPUs, 0.466 against 0.458 ms per 2^28-element shard).
-constexpr int kQStagesMulti = 6, kQFoldMulti = 3, kQRingMulti = 5;
+// The block-cyclic form folds one tile further ahead: its rescans also wait for other GPUs' stripe aggregates, and
+// the fold look-ahead is the slack that hides their arrival. A seventh stage keeps two tiles loading ahead.
+constexpr int kQStagesMulti = 7, kQFoldMulti = 4, kQRingMulti = 6;
 constexpr size_t kQSmemMulti = (size_t)kQStagesMulti * kQTileBytes + 256;
 static_assert(kQRingMulti >= kQFoldMulti + 2 && kQStagesMulti >= kQFoldMulti + 2, "block-cyclic pipeline");
 static_assert(kQSmemMulti <= 227 * 1024 - 1024, "block-cyclic stages fit the opt-in shared memory");
