@@ -239,9 +239,7 @@ def _w4a16_bound_check(d, got_bits):
     gv = (got_bits.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
     a = np.abs(exact)
     ulp = 2.0 ** (np.floor(np.log2(np.maximum(a, 2.0 ** -126))) - 7)
-    G = d.k // 128
-    dd = d.k + 2 * G + 2
-    bound = 0.5 * ulp + dd * U32 / (1 - dd * U32) * abs_sum
+    bound = 0.5 * ulp + 2.0 * U32 * abs_sum  # the bar of tests/test_gpu_w4a16.py
     assert np.all(np.abs(gv - exact) <= bound)
 
 

@@ -2,9 +2,13 @@
 the oracle restatement, from small shapes that exercise split tiles up to the full 16 x 28672 x 8192 config.
 
 W4A16 tolerance (f32 accumulation against the exact f64 sum, one bf16 rounding):
-  |got - exact| <= 1/2 ulp_bf16(|exact|) + gamma_(K + 2G + 2) * sum_k |x * w * s|,  u = 2^-24, G = K/128,
-counting one rounding per tensor-core accumulate step, the scale multiply and add per k-block, and the
-split-tile partial sum.
+  |got - exact| <= 1/2 ulp_bf16(|exact|) + C * u * sum_k |x * w * s|,  u = 2^-24, C = 2,
+and at least 99 % of the outputs are the correctly rounded bf16 of the exact sum. The a-priori bound of an f32
+accumulation in this order, gamma_(K + 2G + 2) (one rounding per tensor-core accumulate step, the scale multiply and
+add per k-block, and the split-tile partial sum; about 8,322 u at K = 8192), is far looser than what the kernel does:
+measured, the error beyond the half ulp is at most 0.107 u * sum|x w s| on the full 16 x 28672 x 8192 config and
+0.133 u on 7 x 38400 x 256, and 99.99 % of outputs are correctly rounded. C = 2 leaves a 15x margin over that and still
+fails any change that loses f32 accumulation (a bf16 partial alone is 2^-9 relative, 32768 u).
 """
 import numpy as np
 import pytest
@@ -15,15 +19,12 @@ from unpopped_b200 import _lib, ops, workloads
 
 pytestmark = pytest.mark.gpu
 U32 = 2.0 ** -24
+ACC_C = 2.0  # the accumulation allowance, in units of u * sum|x w s| (see the module docstring)
 
 
 @pytest.fixture(scope="module", autouse=True)
 def _cuda():
     assert torch.cuda.is_available(), "these tests need the B200"
-
-
-def gamma(d):
-    return d * U32 / (1 - d * U32)
 
 
 def ulp_bf16(v):
@@ -62,13 +63,12 @@ def _check_w4a16(d, got, threads=1):
                                     _np(d.x.view(torch.int16), np.uint16), d.m, d.n, d.k, d.group, threads=threads)
     g = _np(got.view(torch.int16), np.uint16).astype(np.uint32)
     gv = (g << 16).view(np.float32).astype(np.float64)
-    G = d.k // 128
-    bound = 0.5 * ulp_bf16(exact) + gamma(d.k + 2 * G + 2) * abs_sum
+    bound = 0.5 * ulp_bf16(exact) + ACC_C * U32 * abs_sum
     err = np.abs(gv - exact)
     bad = err > bound
     assert not bad.any(), (int(bad.sum()), float((err / bound).max()))
-    # most outputs are the correctly rounded value itself
-    assert np.mean(g == out) > 0.9
+    # and nearly every output is the correctly rounded value itself
+    assert np.mean(g == out) >= 0.99
 
 
 @pytest.mark.parametrize("m,n,k", [(16, 128, 128), (16, 256, 1024), (1, 384, 512), (5, 1024, 2048),
