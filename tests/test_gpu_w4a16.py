@@ -73,7 +73,9 @@ def _check_w4a16(d, got, threads=1):
 
 @pytest.mark.parametrize("m,n,k", [(16, 128, 128), (16, 256, 1024), (1, 384, 512), (5, 1024, 2048),
                                    (16, 2048, 4096), (16, 200, 256), (7, 128 * 300, 256),
-                                   (16, 1000, 640), (3, 512, 384)])  # odd k-block counts: one-k-block units
+                                   (16, 1000, 640), (3, 512, 384),  # odd k-block counts: one-k-block units
+                                   # many units a CTA (about 8), so every ring wraps several times per issuer
+                                   (16, 9216, 4096), (5, 4096, 128 * 33)])
 def test_w4a16_vs_oracle(m, n, k):
     d = workloads.w4a16_inputs(n=n, k=k, m=m, group=128, seed=m * n + k)
     got = ops.w4a16(d.w_packed, d.scale, d.x, 128)

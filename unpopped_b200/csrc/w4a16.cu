@@ -18,19 +18,19 @@
 //    this replaced put 32 rows' worth of sector requests behind every warp instruction.
 //  * warps 0..7 (dequant): warp w owns TMEM lane quarter w % 4 and k-quarters 2 (w / 4) and 2 (w / 4) + 1, so
 //    thread (w, lane) owns row 32 (w % 4) + lane of the tile and 64 UK k of every unit: 32 UK bytes of W, read from
-//    the W stage (conflict free under the swizzle). Each k-quarter is released to its issuer as soon as it is in
-//    tensor memory. (Sixteen warps, one k-quarter each, measured 1 % slower and left fewer registers per thread.) It turns the nibbles into exact bf16 (a shift, one lop3 and one bf16x2 subtract per
+//    the W stage (conflict free under the swizzle). (Sixteen warps, one k-quarter each, measured 1 % slower and left
+//    fewer registers per thread.) It turns the nibbles into exact bf16 (a shift, one lop3 and one bf16x2 subtract per
 //    pair, pairing k with k + 4) and stores them into tensor memory (tcgen05.st) as the MMA's A operand, whose k
 //    order inside each group of 8 is therefore 0,4,1,5,2,6,3,7.
-//  * warps 8..11 (MMA issuers): a single thread issues only about one tcgen05.mma per ~100 cycles, so four
-//    threads share a unit's 8 UK k-steps as pipelines: issuer g runs the 2 UK k-steps of k-quarter g into
-//    its k-block's accumulator after the issuer before it in that k-block has issued its own (an mbarrier
-//    hand-off between tcgen05.fence::before_thread_sync and ::after_thread_sync orders them), so each
-//    k-block ends in one accumulator while several units are in issue at once. (Four separate accumulators per unit were measured
-//    slower: the epilogue's reads of four times the tensor-memory data cost more than the hand-offs.)
+//  * warps 8..10 (MMA issuers): one thread issues a tcgen05.mma of this shape about every 49 cycles (measured; four
+//    issuing threads reach one per 12 cycles), so three threads take the units in turn (unit i to issuer i % 3), each
+//    issuing all 8 UK k-steps of its unit into one accumulator per k-block and committing the unit's barriers. No
+//    issuer waits for another: chaining them inside a unit (an mbarrier hand-off per k-quarter) put four hand-off
+//    latencies on every unit. Every ring the issuers wait on (A and D slots in tensor memory, activation stages) is at
+//    least three deep, so no parity wait can meet a barrier two phases behind.
 //  * warp 16 (activation loader): one thread brings each unit's [16 x 128 UK] activation tile into a ring of
 //    shared-memory stages with 2 UK TMA boxes, 128-byte swizzled as the MMA reads it; rows past M read as 0.
-//  * warp 19 (activation permuter): rewrites each landed 16-byte chunk (8 k) in place to the k order 0,4,1,5,2,6,
+//  * warp 11 (activation permuter): rewrites each landed 16-byte chunk (8 k) in place to the k order 0,4,1,5,2,6,
 //    3,7 of the A operand (the swizzle moves whole chunks, so it is unaffected), then releases the stage to the MMA.
 //  * warp 17 (scale loader): one thread brings each unit's scales, f16 groups [g0, g0 + 16) of its 128 rows with
 //    g0 = the unit's first group rounded down to a multiple of 8, into a ring of shared-memory slots with one TMA
@@ -59,7 +59,8 @@ constexpr int kTileN = 128;                      // W rows per tile = MMA M
 constexpr int kMmaN = 16;                        // activation rows = MMA N
 constexpr int kKB = 128;                         // k per unit
 constexpr int kDqWarps = 8;                      // warps 0..7
-constexpr int kIssuers = 4;                      // warps 8..11
+constexpr int kIssuers = 4;                      // warps 8..11: two pairs
+constexpr int kPairs = kIssuers / 2;             // units in issue at once
 constexpr int kEpiWarps = 4;                     // warps 12..15
 constexpr int kIss0 = kDqWarps, kEpi0 = kIss0 + kIssuers, kXWarp = kEpi0 + kEpiWarps, kScWarp = kXWarp + 1;
 constexpr int kWWarp = kScWarp + 1, kXpWarp = kWWarp + 1;
@@ -74,28 +75,42 @@ constexpr int kTmemCols = 512;
 template <int UK>
 struct Cfg {
   static constexpr int kACols = 64 * UK;               // A (dequantized W) columns per unit
-  static constexpr int kDCols = kMmaN * UK;            // accumulator columns per unit: one 16-column block per k-block
-  static constexpr int kRing = UK == 1 ? 6 : 3;        // units in flight between dequant, MMA and epilogue
+  // accumulator columns per unit: one 16-column block per half of the unit (64 UK k: a k-block when UK = 2)
+  static constexpr int kDCols = 2 * kMmaN;
+  static constexpr int kRing = UK == 1 ? 5 : 3;        // A slots: units in flight between dequant and MMA
   static constexpr int kACol0 = 0;
   static constexpr int kDCol0 = kRing * kACols;
+  // D slots: the accumulators take the columns the A slots leave, so the epilogue runs one or more units behind the
+  // MMAs without holding back an A slot (4 for two k-blocks a unit, 8 for one)
+  static constexpr int kDRing = (kTmemCols - kDCol0) / kDCols;
   static constexpr int kXUnit = kXBytes * UK;          // activation bytes per unit
-  static constexpr int kXStages = 8 / UK;              // 32 KiB of activation stages either way
-  static constexpr int kChain = kIssuers / UK;         // issuers chained into one k-block's accumulator
+  static constexpr int kXStages = 12 / UK;             // 48 KiB of activation stages either way
   static constexpr int kWRow = 64 * UK;                // bytes of one W row in a unit
   static constexpr int kWUnit = kTileN * kWRow;        // W bytes per unit (one TMA box of 128 rows)
   static constexpr int kWStages = 16 / UK;             // 128 KiB of W in flight either way
-  // mbarriers: x_full, x_empty [kXStages]; a_full [kRing][4]; mma_done, d_empty [kRing]; hand [kIssuers][kRing];
-  // seg_in, seg_out; then the TMEM address word, the abort word and the fix-up verdict
+  // mbarriers: x_full, x_empty, x_raw [kXStages]; a_full [kRing][2]; mma_done [kRing]; d_done, d_empty [kDRing];
+  // drain [kIssuers]; sc_full, sc_empty [kScRing]; w_full, w_empty [kWStages]; seg_in, seg_out; then the TMEM address
+  // word, the abort word and the fix-up verdict
   static constexpr int kNumBars =
-      3 * kXStages + 4 * kRing + 2 * kRing + kIssuers * kRing + 2 * kScRing + 2 * kWStages + 2;
-  static_assert(kDCol0 + kRing * kDCols <= kTmemCols, "tensor memory");
+      3 * kXStages + 3 * kRing + 2 * kDRing + kIssuers + 2 * kScRing + 2 * kWStages + 2;
+  static_assert(kDRing >= kRing && kDCol0 + kDRing * kDCols <= kTmemCols, "tensor memory");
+  // Issuer pair p takes units p, p + kPairs, ...; for unit i an issuer waits on ring slots for the phase of unit i (or
+  // of i - depth), which is only sound while the slot's phase before that has completed. The issuer's previous unit,
+  // i - kPairs, already saw every unit up to it through, so a ring at least kPairs deep is enough.
+  static_assert(kRing >= kPairs && kDRing >= kPairs && kXStages >= kPairs, "ring shallower than the issuer pairs");
 };
 constexpr int kBarBytes = 2048;
 constexpr size_t kWBytes = (size_t)16 * kTileN * 64;  // the W ring: Cfg<UK>::kWStages * kWUnit for either UK
 static_assert(Cfg<1>::kNumBars * 8 + 12 <= kBarBytes && Cfg<2>::kNumBars * 8 + 12 <= kBarBytes, "barrier region");
 constexpr size_t kScSlot = (size_t)kTileN * kScCols * 2;  // one TMA box of 128 rows x 16 f16
 constexpr size_t kScBytes = kScRing * kScSlot;
-constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + (size_t)8 * kXBytes + kWBytes + kScBytes + kBarBytes;
+// Each scale slot carries its unit's header, written by the scale warp with the scales: {tile, segment flags,
+// the slot columns of the unit's UK scale groups (16 bits each), 0}. The epilogue then keeps no unit cursor.
+constexpr size_t kHdrBytes = kScRing * sizeof(int4);
+constexpr uint32_t kSegStart = 1u, kSegEnd = 2u, kSegWhole = 4u;  // header flags: a tile segment starts / ends here;
+                                                                   // the segment is the whole tile
+constexpr size_t kSmemBytes =
+    1024 /*alignment slack*/ + (size_t)12 * kXBytes + kWBytes + kScBytes + kHdrBytes + kBarBytes;
 static_assert(kEpi0 % 4 == 0, "epilogue warp e reads TMEM lane quarter e % 4");
 
 struct WsHeader {
@@ -138,6 +153,7 @@ __device__ __forceinline__ void nib8_to_bf16x2_k4(uint32_t w, uint32_t* out) {
 // dominate the loops. G (k-blocks per tile) is a multiple of UK.
 template <int UK>
 struct UnitCursor {
+  static_assert(UK == 1 || UK == 2, "one or two k-blocks a unit");
   int t, kb, sub, gi;  // sub = kb % (group / 128)
   __device__ __forceinline__ void init(int64_t u, int64_t G, int kpg) {
     const int64_t GU = G / UK;
@@ -162,8 +178,8 @@ struct UnitCursor {
         ++gi;
       }
   }
-  // scale-group index of k-block kb + h of the unit
-  __device__ __forceinline__ int gi_at(int h, int kpg) const { return gi + (sub + h) / kpg; }
+  // scale-group index of k-block kb + h of the unit (h < UK <= 2 and sub < kpg, so (sub + h) / kpg is 0 or 1)
+  __device__ __forceinline__ int gi_at(int h, int kpg) const { return gi + (sub + h == kpg ? 1 : 0); }
 };
 
 // The order in which a CTA takes its units [lo, hi): first the units of its last tile when that tile is split with
@@ -259,15 +275,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kRing = C::kRing, kXStages = C::kXStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* xs = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* wst = xs + (size_t)kXStages * C::kXUnit;  // [kWStages] W boxes (1024-byte aligned: 32 KiB after xs)
+  uint8_t* wst = xs + (size_t)kXStages * C::kXUnit;  // [kWStages] W boxes (1024-byte aligned: 48 KiB after xs)
   __half* scs = reinterpret_cast<__half*>(wst + kWBytes);  // [kScRing][128][kScCols] f16 scales
-  uint64_t* x_full = reinterpret_cast<uint64_t*>(wst + kWBytes + kScBytes);  // [kXStages]: TMA landed
-  uint64_t* x_empty = x_full + kXStages;        // [kXStages]: the stage's MMAs completed (chain ends' commits)
-  uint64_t* a_full = x_empty + kXStages;        // [kRing][4]: k-quarter q of the unit's A is in TMEM (4 warps)
-  uint64_t* mma_done = a_full + 4 * kRing;      // [kRing]: all of the unit's MMAs completed
-  uint64_t* d_empty = mma_done + kRing;         // [kRing]: the epilogue has read the unit's accumulators
-  uint64_t* hand = d_empty + kRing;             // [kIssuers][kRing]: issuer g has issued the unit's k-quarter g
-  uint64_t* sc_full = hand + kIssuers * kRing;  // [kScRing]: the scale warp has written the unit's scales
+  int4* sc_hdr = reinterpret_cast<int4*>(wst + kWBytes + kScBytes);  // [kScRing] unit headers
+  uint64_t* x_full = reinterpret_cast<uint64_t*>(wst + kWBytes + kScBytes + kHdrBytes);  // [kXStages]: TMA landed
+  uint64_t* x_empty = x_full + kXStages;        // [kXStages]: the stage's MMAs completed (the issuer's commit)
+  uint64_t* a_full = x_empty + kXStages;        // [kRing][2]: half h of the unit's A is in TMEM (4 dequant warps)
+  uint64_t* mma_done = a_full + 2 * kRing;      // [kRing]: all of the unit's MMAs completed (its A slot is free)
+  uint64_t* d_done = mma_done + kRing;          // [kDRing]: the same, by D slot (the epilogue may read it)
+  uint64_t* d_empty = d_done + C::kDRing;       // [kDRing]: the epilogue has read the unit's accumulators
+  uint64_t* drain = d_empty + C::kDRing;        // [kIssuers]: an unwinding issuer's MMAs completed
+  uint64_t* sc_full = drain + kIssuers;         // [kScRing]: the scale warp has written the unit's scales
   uint64_t* sc_empty = sc_full + kScRing;       // [kScRing]: every epilogue warp has read them
   uint64_t* w_full = sc_empty + kScRing;        // [kWStages]: the unit's W box has landed
   uint64_t* w_empty = w_full + C::kWStages;     // [kWStages]: every dequant warp has read it
@@ -290,13 +308,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kXStages; ++s) {
       tc::mbar_init(&x_full[s], 1);
-      tc::mbar_init(&x_empty[s], UK);
+      tc::mbar_init(&x_empty[s], 2);
     }
     for (int a = 0; a < kRing; ++a) {
-      for (int q = 0; q < 4; ++q) tc::mbar_init(&a_full[4 * a + q], 4);
-      tc::mbar_init(&mma_done[a], UK);
-      tc::mbar_init(&d_empty[a], kEpiWarps);
-      for (int g = 0; g < kIssuers; ++g) tc::mbar_init(&hand[g * kRing + a], 1);
+      for (int h = 0; h < 2; ++h) tc::mbar_init(&a_full[2 * a + h], kDqWarps / 2);
+      tc::mbar_init(&mma_done[a], 2);
+    }
+    for (int g = 0; g < kIssuers; ++g) tc::mbar_init(&drain[g], 1);
+    for (int d = 0; d < C::kDRing; ++d) {
+      tc::mbar_init(&d_done[d], 2);
+      tc::mbar_init(&d_empty[d], kEpiWarps);
     }
     for (int q = 0; q < kScRing; ++q) {
       tc::mbar_init(&sc_full[q], 1);
@@ -331,74 +352,84 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lq = warp & 3, kh = warp >> 2;  // k-half kh: k-quarters 2 kh and 2 kh + 1
     const int r = lq * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(lq * 32) << 16;
-    // this thread's 16-byte chunks of its row in a W stage: chunk UK kq + h, 128-byte swizzled when UK = 2
-    const uint8_t* wrow = wst + (size_t)r * C::kWRow;
-    bool ok = true;
-    for (int64_t i = 0; ok && i < n_units; ++i) {
-      {
-        const int sw = (int)(i % C::kWStages);
-        if (!__all_sync(0xffffffffu, tc::mbar_wait(&w_full[sw], (uint32_t)((i / C::kWStages) & 1), wait_ns,
-                                                   abort_flag))) {
-          give_up();
-          break;
-        }
+    // this thread's 16-byte chunks of its row in a W stage: chunk UK kq + h, 128-byte swizzled when UK = 2. The
+    // loop keeps its ring positions as 32-bit counters advanced by increments: the integer pipe is the one the
+    // nibble conversion fills, so the loop's own arithmetic is kept off it.
+    uint32_t coff[2][UK];  // byte offsets of the chunks inside a W stage
+#pragma unroll
+    for (int qq = 0; qq < 2; ++qq)
+#pragma unroll
+      for (int h = 0; h < UK; ++h) {
+        const int c = UK * (2 * kh + qq) + h;
+        coff[qq][h] = (uint32_t)(r * C::kWRow + ((UK == 2 ? (c ^ (r & 7)) : c) << 4));
+      }
+    const uint32_t a_base = tmem + lane_addr + C::kACol0 + 16 * (UK * 2 * kh);  // this warp's columns of A slot 0
+    int sw = 0, a = 0;
+    uint32_t wph = 0, aph = 0;
+    const int nu = (int)n_units;
+    for (int i = 0; i < nu; ++i) {
+      if (!__all_sync(0xffffffffu, tc::mbar_wait(&w_full[sw], wph, wait_ns, abort_flag))) {
+        give_up();
+        break;
       }
       uint4 cur[2][UK];
+      const uint8_t* stage = wst + (size_t)sw * C::kWUnit;
+#pragma unroll
+      for (int qq = 0; qq < 2; ++qq)
+#pragma unroll
+        for (int h = 0; h < UK; ++h) cur[qq][h] = *reinterpret_cast<const uint4*>(stage + coff[qq][h]);
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&w_empty[sw]);
+      if (++sw == C::kWStages) {
+        sw = 0;
+        wph ^= 1u;
+      }
+      // the A stage is free once the unit kRing earlier has been multiplied
+      const bool good = tc::mbar_wait(&mma_done[a], aph ^ 1u, wait_ns, abort_flag);
+      if (!__all_sync(0xffffffffu, good)) {  // warp-uniform: the tcgen05 ops below are .sync.aligned
+        give_up();
+        break;
+      }
 #pragma unroll
       for (int qq = 0; qq < 2; ++qq)
 #pragma unroll
         for (int h = 0; h < UK; ++h) {
-          const int c = UK * (2 * kh + qq) + h;
-          const int cs = UK == 2 ? (c ^ (r & 7)) : c;
-          cur[qq][h] = *reinterpret_cast<const uint4*>(wrow + (size_t)(i % C::kWStages) * C::kWUnit + (cs << 4));
+          uint32_t regs[16];
+          const uint32_t wd[4] = {cur[qq][h].x, cur[qq][h].y, cur[qq][h].z, cur[qq][h].w};
+#pragma unroll
+          for (int wi = 0; wi < 4; ++wi) nib8_to_bf16x2_k4(wd[wi], regs + 4 * wi);
+          tc::st_32x32b_x16(a_base + a * C::kACols + 16 * (UK * qq + h), regs);
         }
+      tc::wait_st();
+      tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&w_empty[i % C::kWStages]);
-      {
-        const int a = (int)(i % kRing);
-        const uint32_t aph = (uint32_t)((i / kRing) & 1);
-        // the A stage is free once the unit kRing earlier has been multiplied
-        const bool good = tc::mbar_wait_sleepy(&mma_done[a], aph ^ 1u, wait_ns, abort_flag, kSleepNs);
-        if (!__all_sync(0xffffffffu, good)) {  // warp-uniform: the tcgen05 ops below are .sync.aligned
-          give_up();
-          ok = false;
-          break;
-        }
-#pragma unroll
-        for (int qq = 0; qq < 2; ++qq) {
-          const int kq = 2 * kh + qq;
-#pragma unroll
-          for (int h = 0; h < UK; ++h) {
-            uint32_t regs[16];
-            const uint32_t wd[4] = {cur[qq][h].x, cur[qq][h].y, cur[qq][h].z, cur[qq][h].w};
-#pragma unroll
-            for (int wi = 0; wi < 4; ++wi) nib8_to_bf16x2_k4(wd[wi], regs + 4 * wi);
-            tc::st_32x32b_x16(tmem + lane_addr + C::kACol0 + a * C::kACols + 16 * (UK * kq + h), regs);
-          }
-          tc::wait_st();
-          tc::fence_before_sync();
-          __syncwarp();
-          if (lane == 0) tc::mbar_arrive(&a_full[4 * a + kq]);
-        }
+      if (lane == 0) tc::mbar_arrive(&a_full[2 * a + kh]);  // this warp's k-quarters are half kh of the unit
+      if (++a == kRing) {
+        a = 0;
+        aph ^= 1u;
       }
     }
   } else if (warp < kEpi0) {
-    // ------- MMA issuers: issuer g runs the 2 UK k-steps of k-quarter g, in its k-block's chain -------
-    const int g = warp - kIss0;
-    const int hk = (UK * g) / 4;          // the k-block (accumulator) of this issuer's k-steps
-    const int pos = g % C::kChain;        // place in that k-block's chain
+    // ------- MMA issuers: pair p takes units p, p + 2, ...; issuer h of the pair the 4 UK k-steps of half h -------
+    const int g = warp - kIss0, p = g >> 1, hh = g & 1;
     if (lane == 0) {
       constexpr uint32_t idesc = tc::idesc_bf16_f32(kTileN, kMmaN);
-      int64_t issued = 0;
-      for (int64_t i = 0; i < n_units; ++i) {
-        const int a = (int)(i % kRing), s = (int)(i % kXStages);
-        const uint32_t rph = (uint32_t)((i / kRing) & 1), xph = (uint32_t)((i / kXStages) & 1);
-        // the first issuer of a chain starts the accumulator once the epilogue has read the slot's previous
-        // unit; the others add to it after the issuer before them
-        const bool ready = tc::mbar_wait(&a_full[4 * a + g], rph, wait_ns, abort_flag) &&
+      bool issued = false;
+      // ring positions of unit i, advanced by kPairs units a step
+      int a = p, s = p, dsl = p;
+      uint32_t rph = 0, xph = 0, dph = 0;
+      auto step = [](int& slot, uint32_t& ph, int depth) {
+        if ((slot += kPairs) >= depth) {
+          slot -= depth;
+          ph ^= 1u;
+        }
+      };
+      const int nu = (int)n_units;
+      for (int i = p; i < nu; i += kPairs, step(a, rph, kRing), step(s, xph, kXStages), step(dsl, dph, C::kDRing)) {
+        // the half's A and the unit's activations are in place and the epilogue has read the D slot's previous unit
+        const bool ready = tc::mbar_wait(&a_full[2 * a + hh], rph, wait_ns, abort_flag) &&
                            tc::mbar_wait(&x_full[s], xph, wait_ns, abort_flag) &&
-                           (pos == 0 ? tc::mbar_wait(&d_empty[a], rph ^ 1u, wait_ns, abort_flag)
-                                     : tc::mbar_wait(&hand[(g - 1) * kRing + a], rph, wait_ns, abort_flag));
+                           tc::mbar_wait(&d_empty[dsl], dph ^ 1u, wait_ns, abort_flag);
         if (!ready) {
           give_up();
           break;
@@ -406,83 +437,90 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::fence_after_sync();
         const uint32_t xaddr = tc::smem_u32(xs + (size_t)s * C::kXUnit);
 #pragma unroll
-        for (int jj = 0; jj < 2 * UK; ++jj) {
-          const int j = 2 * UK * g + jj;  // k-step: 16 k = 32 bytes of a 128-byte swizzle atom row
+        for (int jj = 0; jj < 4 * UK; ++jj) {
+          const int j = 4 * UK * hh + jj;  // k-step j: 16 k = 32 bytes of a 128-byte swizzle atom row
           const uint64_t bdesc = tc::sdesc_kmajor_sw128(xaddr + (uint32_t)((j >> 2) * 2048 + (j & 3) * 32));
-          tc::mma_ts_bf16(tmem + C::kDCol0 + a * C::kDCols + hk * kMmaN, tmem + C::kACol0 + a * C::kACols + j * 8,
-                          bdesc, idesc, (pos > 0 || jj > 0) ? 1u : 0u);
+          tc::mma_ts_bf16(tmem + C::kDCol0 + dsl * C::kDCols + hh * kMmaN, tmem + C::kACol0 + a * C::kACols + j * 8,
+                          bdesc, idesc, jj > 0 ? 1u : 0u);
         }
-        if (pos + 1 < C::kChain) {
-          tc::fence_before_sync();
-          tc::mbar_arrive(&hand[g * kRing + a]);
-        } else {
-          // a chain's MMAs run in issue order, so its last issuer's completing covers all of them
-          tc::commit(&mma_done[a]);
-          tc::commit(&x_empty[s]);
-        }
-        issued = i + 1;
+        // the commits arrive once this thread's MMAs so far (so its half of the unit) have completed
+        tc::commit(&mma_done[a]);
+        tc::commit(&d_done[dsl]);
+        tc::commit(&x_empty[s]);
+        issued = true;
       }
-      // Unwinding after an abort: the MMAs already issued must finish before TMEM is released.
-      if (*abort_flag && issued > 0) {
-        const int64_t i = issued - 1;
-        tc::mbar_wait(&mma_done[i % kRing], (uint32_t)((i / kRing) & 1), wait_ns, nullptr);
+      // Unwinding after an abort: this issuer's MMAs must finish before TMEM is released.
+      if (*abort_flag && issued) {
+        tc::commit(&drain[g]);
+        tc::mbar_wait(&drain[g], 0u, wait_ns, nullptr);
       }
     }
-  } else if (warp < kXWarp) {
+  } else if (warp >= kEpi0 && warp < kXWarp) {
     // ---------------- epilogue: row 32 (warp % 4) + lane, all 16 activation rows ----------------
+    // Per unit: the scale slot (its header says the tile, where segments start and end and which scale columns to
+    // take), then the accumulators; ring positions advance by increments (no 64-bit division in the loop).
     const int lq = warp & 3;
     const int r = lq * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(lq * 32) << 16;
-    const int64_t GU = G / UK;      // units per tile
-    RotCursor<UK> ce;               // the unit being finished
-    ce.init(lo, hi, rot, G, kpg);
+    const int64_t GU = G / UK;  // units per tile
     float acc[kMmaN];
 #pragma unroll
     for (int j = 0; j < kMmaN; ++j) acc[j] = 0.f;
-    int64_t seg_kb0 = 0;
     uint32_t nfix = 0;
-    for (int64_t e = 0; e < n_units; ++e) {
-      const int d = (int)(e % kRing);
-      const uint32_t dph = (uint32_t)((e / kRing) & 1);
-      // this row's scales of the unit, staged by the scale warp; the slot is released once they are read
-      const int q = (int)(e % kScRing);
-      if (!__all_sync(0xffffffffu, tc::mbar_wait(&sc_full[q], (uint32_t)((e / kScRing) & 1), wait_ns, abort_flag))) {
+    int d = 0, q = 0;
+    uint32_t dph = 0, qph = 0;
+    const int nu = (int)n_units;
+    for (int e = 0; e < nu; ++e) {
+      if (!__all_sync(0xffffffffu, tc::mbar_wait(&sc_full[q], qph, wait_ns, abort_flag))) {
         give_up();
         break;
       }
+      const int4 hd = sc_hdr[q];
       float sc[UK];
 #pragma unroll
       for (int h = 0; h < UK; ++h)
-        sc[h] = __half2float(scs[((size_t)q * kTileN + r) * kScCols + (ce.c.gi_at(h, kpg) - (ce.c.gi & ~7))]);
+        sc[h] = __half2float(scs[((size_t)q * kTileN + r) * kScCols + ((hd.z >> (16 * h)) & 0xffff)]);
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&sc_empty[q]);
-      const bool good = tc::mbar_wait_sleepy(&mma_done[d], dph, wait_ns, abort_flag, kSleepNs);
+      if (++q == kScRing) {
+        q = 0;
+        qph ^= 1u;
+      }
+      const bool good = tc::mbar_wait(&d_done[d], dph, wait_ns, abort_flag);
       if (!__all_sync(0xffffffffu, good)) {
         give_up();
         break;
       }
       tc::fence_after_sync();
-      const int64_t t = ce.c.t, kb = ce.c.kb;
-      if (e == 0 || e == hi - rot || kb == 0) {  // a segment starts: the range's start, the wrap, a tile
-        seg_kb0 = kb;
+      if (hd.y & kSegStart) {  // a segment starts: the range's start, the wrap, a tile
 #pragma unroll
         for (int j = 0; j < kMmaN; ++j) acc[j] = 0.f;
       }
-#pragma unroll
-      for (int h = 0; h < UK; ++h) {  // k-block by k-block, in k order
-        uint32_t dv[kMmaN];
-        tc::ld_32x32b_x16(tmem + lane_addr + C::kDCol0 + d * C::kDCols + h * kMmaN, dv);
+      {
+        uint32_t dv[2][kMmaN];  // the unit's two half accumulators
+        tc::ld_32x32b_x16(tmem + lane_addr + C::kDCol0 + d * C::kDCols, dv[0]);
+        tc::ld_32x32b_x16(tmem + lane_addr + C::kDCol0 + d * C::kDCols + kMmaN, dv[1]);
         tc::wait_ld();
+        if (UK == 2) {  // the halves are the k-blocks: each its own scale, in k order
 #pragma unroll
-        for (int j = 0; j < kMmaN; ++j) acc[j] = fmaf(sc[h], __uint_as_float(dv[j]), acc[j]);
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int j = 0; j < kMmaN; ++j) acc[j] = fmaf(sc[h], __uint_as_float(dv[h][j]), acc[j]);
+        } else {  // both halves of the one k-block, summed, then scaled
+#pragma unroll
+          for (int j = 0; j < kMmaN; ++j)
+            acc[j] = fmaf(sc[0], __uint_as_float(dv[0][j]) + __uint_as_float(dv[1][j]), acc[j]);
+        }
       }
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&d_empty[d]);
-      const int64_t u = ce.unit();
-      ce.next(Gi, kpg);
-      if (u + 1 == hi || kb + UK == G)  // the segment [seg_kb0, kb + UK) of tile t ends here
-        if (!finish_segment(acc, t, seg_kb0 == 0 && kb + UK == G, r, lane, M, N, U, GU, P, S_max, out, counters,
+      if (++d == C::kDRing) {
+        d = 0;
+        dph ^= 1u;
+      }
+      if (hd.y & kSegEnd)  // the segment ends here: write the tile, or publish this CTA's part of it
+        if (!finish_segment(acc, hd.x, (hd.y & kSegWhole) != 0, r, lane, M, N, U, GU, P, S_max, out, counters,
                             partials, seg_in, seg_out, s_last, nfix, wait_ns, abort_flag)) {
           give_up();
           break;
@@ -495,6 +533,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     RotCursor<UK> rs;
     rs.init(lo, hi, rot, G, kpg);
     const UnitCursor<UK>& cs = rs.c;
+    int seg_kb0 = 0;
+    // the unit's header: a segment starts at the range's start, at the wrap and at a tile's first unit, and ends at
+    // the range's end and at a tile's last unit
+    auto header = [&](int64_t i) {
+      const int64_t u = rs.unit();
+      const bool start = i == 0 || i == rs.n_first || cs.kb == 0;
+      if (start) seg_kb0 = cs.kb;
+      const bool end = u + 1 == hi || cs.kb + UK == Gi;
+      const uint32_t flags = (start ? kSegStart : 0u) | (end ? kSegEnd : 0u) |
+                             (end && seg_kb0 == 0 && cs.kb + UK == Gi ? kSegWhole : 0u);
+      const int g0 = cs.gi & ~7;
+      int cols = cs.gi_at(0, kpg) - g0;
+      if (UK == 2) cols |= (cs.gi_at(1, kpg) - g0) << 16;
+      return make_int4(cs.t, (int)flags, cols, 0);
+    };
     if (scale_tma) {
       if (lane == 0) {
         tc::tma_prefetch_desc(&smap);
@@ -506,6 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             give_up();
             break;
           }
+          sc_hdr[q] = header(i);  // published by the arrive (release) below
           tc::mbar_arrive_expect_tx(&sc_full[q], (uint32_t)kScSlot);
           tc::tma_load_2d(scs + (size_t)q * kTileN * kScCols, &smap, &sc_full[q], cs.gi & ~7,
                           cs.t * kTileN);
@@ -525,6 +579,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         __half* slot = scs + (size_t)q * kTileN * kScCols;
+        const int4 hd = header(i);
+        if (lane == 0) sc_hdr[q] = hd;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int row = lane + 32 * j;
@@ -588,7 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&x_full[s]);
     }
-  } else {
+  } else if (warp == kXWarp) {
     // ---------------- activation loader: 2 UK TMA boxes per unit ----------------
     if (lane == 0) {
       tc::tma_prefetch_desc(&xmap);
@@ -694,6 +750,7 @@ extern "C" int up_sm100_w4a16_gemm(const uint8_t* w, const uint16_t* scale, cons
   // TMA boxes of W rows (K/2 bytes, a multiple of 64) and of activation rows (2K bytes)
   if (!aligned(w, 16) || !aligned(x, 16) || !aligned(workspace, 256)) return UP_ERR_INVALID;
   const Plan p = make_plan(n, k);
+  if (p.U / p.P + 1 > 0x7fffffff) return UP_ERR_UNSUPPORTED;  // a CTA counts its units in 32 bits
   if (workspace_bytes < p.bytes) return UP_ERR_INVALID;
   auto enc = encode_fn();
   if (enc == nullptr) return fail_with(UP_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
