@@ -54,11 +54,15 @@ def test_reference_window_corpora():
             assert ops.window(x, op, size, stride, dil, pad).cpu().numpy().tolist() == want, (name, op)
 
 
-GEOMS = [(3, 1, 1, 0), (3, 2, 1, 1), (5, 3, 2, 2), (1, 1, 1, 0), (7, 4, 3, 3), (2, 2, 1, 0), (9, 1, 1, 4)]
+GEOMS = [(3, 1, 1, 0), (3, 2, 1, 1), (5, 3, 2, 2), (1, 1, 1, 0), (7, 4, 3, 3), (2, 2, 1, 0), (9, 1, 1, 4),
+         (2, 1, 1, 1), (3, 1, 1, 2)]
 
 
+# (2, 3000, 4), (3, 37, 8), (2, 10, 16) and (2, 4, 3, 64) along axis 1 take the column kernel (inner a multiple of 4
+# floats) for sizes 2 and 3 at strides 1 and 2: short axes whose output count is not a multiple of 4, and padding
+# in the first and last windows
 @pytest.mark.parametrize("shape,axis", [((4, 1000), 1), ((6, 50, 33), 1), ((3, 40, 7, 5), 2), ((200,), 0),
-                                        ((2, 3000, 4), 1)])
+                                        ((2, 3000, 4), 1), ((3, 37, 8), 1), ((2, 10, 16), 1), ((2, 4, 3, 64), 1)])
 @pytest.mark.parametrize("geom", GEOMS)
 def test_window_vs_oracle(shape, axis, geom):
     size, stride, dil, pad = geom
