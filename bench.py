@@ -262,6 +262,13 @@ def bench_lifts(ctx, K, W, hbm, bf16):
     ms, _, _ = ctx.timed(lambda i, kin: ops.window(xs[i % R], "max", 3, 2, 1, 1, out=ow), K, W)
     record("window_maxpool3s2_f32_8192x8192", wl.rowsum_bytes() + ow.numel() * 4, ms, "window_f32_staged_kernel", R)
     del ow
+    # the same bytes as 64 x 8192 x 128, pooled along the middle axis (the column kernel)
+    om = torch.empty((64, 4096, 128), device=ctx.dev)
+    ms, _, _ = ctx.timed(lambda i, kin: ops.window(xs[i % R].view(64, 8192, 128), "max", 3, 2, 1, 1, axis=1, out=om),
+                         K, W)
+    record("window_maxpool3s2_f32_middle_64x8192x128", wl.rowsum_bytes() + om.numel() * 4, ms,
+           "window_f32_cols_ext_kernel", R)
+    del om
     xi = [x.view(torch.int32) for x in xs]  # the same bytes read as i32
     oi = out.view(torch.int32)
     ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xi[i % R], "xor", 1, out=oi), K, W)
@@ -588,6 +595,12 @@ def profile_cases(which: str):
         o = torch.empty((x.shape[0], x.shape[1] // 2), device=dev)
         return lambda: ops.window(x, "max", 3, 2, 1, 1, out=o)
 
+    @case("window_mid")
+    def _():
+        x = torch.randn(64, 8192, 128, device=dev)
+        o = torch.empty(64, 4096, 128, device=dev)
+        return lambda: ops.window(x, "max", 3, 2, 1, 1, axis=1, out=o)
+
     @case("argmax")
     def _():
         x = wl.argmax_input(rows=8192, device=dev)
@@ -629,7 +642,7 @@ def main():
     ap.add_argument("--lifts", default="all", choices=["all", "none"])
     ap.add_argument("--profile", default=None,
                     help="run only the small ncu cases of these lifts, comma-separated (scan, rowsum, rowsum_auto, "
-                         "rowmax_f32, colmax_f32, row_rms_norm, window, argmax, gather, dequant, w4a16, all)")
+                         "rowmax_f32, colmax_f32, row_rms_norm, window, window_mid, argmax, gather, dequant, w4a16, all)")
     args = ap.parse_args()
     if args.profile:
         profile_cases(args.profile)
