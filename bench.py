@@ -583,6 +583,12 @@ def profile_cases(which: str):
         o = torch.empty(x.shape[1], device=dev)
         return lambda: ops.reduce2d(x, "max", 0, out=o)
 
+    @case("row_softmax")
+    def _():
+        x = wl.rowsum_input(device=dev)
+        o = torch.empty_like(x)
+        return lambda: ops.row_reduce(x, "softmax", block=256, out=o)
+
     @case("row_rms_norm")
     def _():
         x = wl.rowsum_input(device=dev)
@@ -642,7 +648,7 @@ def main():
     ap.add_argument("--lifts", default="all", choices=["all", "none"])
     ap.add_argument("--profile", default=None,
                     help="run only the small ncu cases of these lifts, comma-separated (scan, rowsum, rowsum_auto, "
-                         "rowmax_f32, colmax_f32, row_rms_norm, window, window_mid, argmax, gather, dequant, w4a16, all)")
+                         "rowmax_f32, colmax_f32, row_softmax, row_rms_norm, window, window_mid, argmax, gather, dequant, w4a16, all)")
     args = ap.parse_args()
     if args.profile:
         profile_cases(args.profile)
