@@ -103,7 +103,10 @@ def test_reference_im2col_corpus():
 @pytest.mark.parametrize("case", [((2, 3, 9, 11), (3, 3), (1, 1), (1, 1), (1, 1)),
                                   ((1, 4, 16, 16), (5, 5), (2, 2), (2, 2), (1, 1)),
                                   ((3, 2, 7, 13), (2, 3), (1, 2), (0, 2), (2, 1)),
-                                  ((1, 1, 1, 1), (1, 1), (1, 1), (0, 0), (1, 1))])
+                                  ((1, 1, 1, 1), (1, 1), (1, 1), (0, 0), (1, 1)),
+                                  # output rows of 12 and 16 cells: the 16-byte-store path for the types they divide
+                                  ((2, 3, 10, 12), (3, 3), (1, 1), (1, 1), (1, 1)),
+                                  ((1, 2, 9, 16), (3, 3), (1, 1), (2, 2), (2, 2))])
 def test_im2col_vs_oracle(dtype, case):
     shape, k, s, p, d = case
     rng = np.random.default_rng(sum(shape))

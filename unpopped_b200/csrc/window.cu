@@ -473,9 +473,11 @@ __global__ void __launch_bounds__(kThreads) im2col_kernel(const T* __restrict__ 
 }
 
 // A CTA per input plane (n, c) that fits in shared memory: the plane is staged once, coalesced, then the CTA writes
-// the plane's kh·kw output rows from shared memory.
+// the plane's kh·kw output rows from shared memory. With VEC > 1 (an output row width that is a multiple of VEC
+// elements of 16 / sizeof(T)), a thread takes VEC consecutive cells of one output row and writes each of its kh·kw
+// rows' cells with one 16-byte evict-first store: the output is the bulk of the traffic and is not read again.
 constexpr int64_t kPlaneBytes = 96 * 1024;
-template <typename T>
+template <typename T, int VEC>
 __global__ void __launch_bounds__(kThreads) im2col_plane_kernel(const T* __restrict__ x, int64_t planes, int h, int w,
                                                                  int kh, int kw, int sh, int sw, int ph, int pw, int dh,
                                                                  int dw, int oh_n, int ow_n, T* __restrict__ out) {
@@ -495,6 +497,32 @@ __global__ void __launch_bounds__(kThreads) im2col_plane_kernel(const T* __restr
     __syncthreads();
     // a thread decodes its cell (oh, ow) once and writes it in all kh·kw rows (each store coalesced across the warp)
     T* const orow = out + pl * kh * kw * (int64_t)cols;
+    if constexpr (VEC > 1) {
+      static_assert(VEC * sizeof(T) == 16, "one 16-byte store per vector of cells");
+      for (int col = threadIdx.x * VEC; col < cols; col += kThreads * VEC) {
+        const int oh = col / ow_n, ow = col - oh * ow_n;  // the VEC cells share oh: ow_n is a multiple of VEC
+        const int ihb = oh * sh - ph, iwb = ow * sw - pw;
+        T* o = orow + col;
+        for (int ki = 0; ki < kh; ++ki) {
+          const int ih = ihb + ki * dh;
+          const bool in_h = ih >= 0 && ih < h;
+          for (int kj = 0; kj < kw; ++kj, o += cols) {
+            union {
+              T e[VEC];
+              uint4 v;
+            } pk;
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) {
+              const int iw = iwb + v * sw + kj * dw;
+              pk.e[v] = (in_h && iw >= 0 && iw < w) ? plane[ih * w + iw] : T{};
+            }
+            st_cs_v4(o, pk.v);
+          }
+        }
+      }
+      __syncthreads();  // the plane is read before the next one is staged
+      continue;
+    }
     for (int col = threadIdx.x; col < cols; col += kThreads) {
       const int oh = col / ow_n, ow = col - oh * ow_n;
       const int ihb = oh * sh - ph, iwb = ow * sw - pw;
@@ -612,22 +640,26 @@ extern "C" int up_sm100_im2col(const void* x, int elem_bytes, int64_t n, int64_t
   const int64_t plane_bytes = h * w * (int64_t)elem_bytes;
   if (plane_bytes <= win::kPlaneBytes && oh * ow <= 0x7fffffffLL && kh * kw <= 0x7fff) {
     const int mx = (int)win::kPlaneBytes;
-    const cudaError_t e =
-        elem_bytes == 1   ? ensure_smem_attr((const void*)win::im2col_plane_kernel<uint8_t>, mx)
-        : elem_bytes == 2 ? ensure_smem_attr((const void*)win::im2col_plane_kernel<uint16_t>, mx)
-        : elem_bytes == 4 ? ensure_smem_attr((const void*)win::im2col_plane_kernel<uint32_t>, mx)
-                          : ensure_smem_attr((const void*)win::im2col_plane_kernel<unsigned long long>, mx);
-    if (e != cudaSuccess) return cuda_status(e);
+    // 16-byte stores of 16 / elem_bytes cells when every output row holds whole vectors
+    const bool vec = ow % (16 / elem_bytes) == 0 && aligned(out, 16);
     const int gp = win::grid_for(n * c);
-#define UP_I2P(T) \
-  win::im2col_plane_kernel<T><<<gp, win::kThreads, (size_t)plane_bytes, s>>>(static_cast<const T*>(x), n * c, (int)h, (int)w, kh, kw, sh, sw, ph, pw, dh, dw, (int)oh, (int)ow, static_cast<T*>(out))
+    cudaError_t e = cudaSuccess;
+#define UP_I2P(T, V)                                                                                                 \
+  do {                                                                                                               \
+    e = ensure_smem_attr((const void*)win::im2col_plane_kernel<T, V>, mx);                                          \
+    if (e == cudaSuccess)                                                                                            \
+      win::im2col_plane_kernel<T, V><<<gp, win::kThreads, (size_t)plane_bytes, s>>>(                                \
+          static_cast<const T*>(x), n * c, (int)h, (int)w, kh, kw, sh, sw, ph, pw, dh, dw, (int)oh, (int)ow,       \
+          static_cast<T*>(out));                                                                                     \
+  } while (0)
     switch (elem_bytes) {
-      case 1: UP_I2P(uint8_t); break;
-      case 2: UP_I2P(uint16_t); break;
-      case 4: UP_I2P(uint32_t); break;
-      default: UP_I2P(unsigned long long); break;
+      case 1: if (vec) UP_I2P(uint8_t, 16); else UP_I2P(uint8_t, 1); break;
+      case 2: if (vec) UP_I2P(uint16_t, 8); else UP_I2P(uint16_t, 1); break;
+      case 4: if (vec) UP_I2P(uint32_t, 4); else UP_I2P(uint32_t, 1); break;
+      default: if (vec) UP_I2P(unsigned long long, 2); else UP_I2P(unsigned long long, 1); break;
     }
 #undef UP_I2P
+    if (e != cudaSuccess) return cuda_status(e);
     note_launch();
     return check_launch();
   }
