@@ -269,6 +269,12 @@ def bench_lifts(ctx, K, W, hbm, bf16):
     record("window_maxpool3s2_f32_middle_64x8192x128", wl.rowsum_bytes() + om.numel() * 4, ms,
            "window_f32_cols_ext_kernel", R)
     del om
+    # Im2Col: the 3x3, pad 1 unfold of 32 x 64 x 56 x 56 f32 (a ResNet stem's first layer), 9x its input in writes
+    ximg = [torch.randn(32, 64, 56, 56, device=ctx.dev) for _ in range(R)]
+    oimg = torch.empty((32, 64 * 9, 56 * 56), device=ctx.dev)
+    ms, _, _ = ctx.timed(lambda i, kin: ops.im2col(ximg[i % R], (3, 3), (1, 1), (1, 1), out=oimg), K, W)
+    record("im2col_3x3_f32_32x64x56x56", ximg[0].numel() * 4 + oimg.numel() * 4, ms, "im2col_plane_kernel", R)
+    del ximg, oimg
     xi = [x.view(torch.int32) for x in xs]  # the same bytes read as i32
     oi = out.view(torch.int32)
     ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xi[i % R], "xor", 1, out=oi), K, W)
