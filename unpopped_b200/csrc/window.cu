@@ -520,19 +520,18 @@ __global__ void __launch_bounds__(kThreads) im2col_plane_kernel(const T* __restr
           }
         }
       }
-      __syncthreads();  // the plane is read before the next one is staged
-      continue;
-    }
-    for (int col = threadIdx.x; col < cols; col += kThreads) {
-      const int oh = col / ow_n, ow = col - oh * ow_n;
-      const int ihb = oh * sh - ph, iwb = ow * sw - pw;
-      T* o = orow + col;
-      for (int ki = 0; ki < kh; ++ki) {
-        const int ih = ihb + ki * dh;
-        const bool in_h = ih >= 0 && ih < h;
-        for (int kj = 0; kj < kw; ++kj, o += cols) {
-          const int iw = iwb + kj * dw;
-          *o = (in_h && iw >= 0 && iw < w) ? plane[ih * w + iw] : T{};
+    } else {
+      for (int col = threadIdx.x; col < cols; col += kThreads) {
+        const int oh = col / ow_n, ow = col - oh * ow_n;
+        const int ihb = oh * sh - ph, iwb = ow * sw - pw;
+        T* o = orow + col;
+        for (int ki = 0; ki < kh; ++ki) {
+          const int ih = ihb + ki * dh;
+          const bool in_h = ih >= 0 && ih < h;
+          for (int kj = 0; kj < kw; ++kj, o += cols) {
+            const int iw = iwb + kj * dw;
+            *o = (in_h && iw >= 0 && iw < w) ? plane[ih * w + iw] : T{};
+          }
         }
       }
     }
