@@ -238,7 +238,7 @@ def bench_lifts(ctx, K, W, hbm, bf16):
     ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xs[i % R], "max", 0, out=out), K, W)
     record("colmax_f32_8192x8192", wl.rowsum_bytes(), ms, "col_extremum_f32_vec_kernel", R)
     ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xs[i % R], "sum", 0, block=256, out=out), K, W)
-    record("colsum_f32_documented_B256", wl.rowsum_bytes(), ms, "col_sum_f32_doc_vec_kernel", R)
+    record("colsum_f32_documented_B256", wl.rowsum_bytes(), ms, "col_sum_f32_doc_vec4_kernel", R)
     # the serial order per column (block 1, the default): bound by the chain of 8192 dependent f64 adds
     ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xs[i % R], "sum", 0, out=out), K, W)
     record("colsum_f32_serial", wl.rowsum_bytes(), ms, "col_sum_f32_serial_kernel", R)

@@ -669,14 +669,17 @@ __global__ void __launch_bounds__(32 * kDocWarps) col_sum_f32_doc_kernel(const f
 // (I = B/64 slots per lane), so each warp reads 512 B of every row it touches. The tree's levels s >= 64 pair
 // slots of one thread, s = 32, 16, 8 pair warps of one CTA (through shared memory) and s = 4, 2, 1 pair CTAs of the
 // cluster (rank 0 reads the other ranks' values through distributed shared memory), each as acc[t] + acc[t+s].
+//
+// Occupancy sets the wave count: 8,192 columns are 512 CTAs, so the CTAs an SM holds decide whether they run as one
+// wave. With four slots a lane (B = 256) the kernel keeps four rows in flight under a cap of four CTAs per SM (64
+// registers, a few spilled): one wave, 1.09x faster than eight rows at two CTAs per SM (110 registers, 1.7 waves).
 template <bool MEAN, int I>
-__global__ void __cluster_dims__(1, kColCluster, 1) __launch_bounds__(256)
-    col_sum_f32_doc_vec_kernel(const float* __restrict__ x, int64_t rows, int64_t cols, int64_t stride,
-                               float* __restrict__ out, int64_t xb, int64_t ob) {
+__device__ __forceinline__ void col_sum_doc_vec_body(const float* __restrict__ x, int64_t rows, int64_t cols,
+                                                     int64_t stride, float* __restrict__ out, int64_t xb, int64_t ob) {
   x += (int64_t)blockIdx.z * xb;  // batch z of a middle-axis reduction
   out += (int64_t)blockIdx.z * ob;
   namespace cg = cooperative_groups;
-  constexpr int B = 64 * I, U = 8 / I;  // U steps of I rows in flight per lane
+  constexpr int B = 64 * I, U = I == 4 ? 1 : 8 / I;  // U steps of I rows in flight per lane
   __shared__ double sw[8][kColStrip];
   __shared__ double cs[kColStrip];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -756,6 +759,19 @@ __global__ void __cluster_dims__(1, kColCluster, 1) __launch_bounds__(256)
     if (c < cols) out[c] = __double2float_rn(MEAN ? v[0] / (double)rows : v[0]);
   }
   cluster.sync();  // rank 0 has read the other CTAs' shared memory before they exit
+}
+
+template <bool MEAN, int I>
+__global__ void __cluster_dims__(1, kColCluster, 1) __launch_bounds__(256)
+    col_sum_f32_doc_vec_kernel(const float* __restrict__ x, int64_t rows, int64_t cols, int64_t stride,
+                               float* __restrict__ out, int64_t xb, int64_t ob) {
+  col_sum_doc_vec_body<MEAN, I>(x, rows, cols, stride, out, xb, ob);
+}
+template <bool MEAN>
+__global__ void __cluster_dims__(1, kColCluster, 1) __launch_bounds__(256, 4)
+    col_sum_f32_doc_vec4_kernel(const float* __restrict__ x, int64_t rows, int64_t cols, int64_t stride,
+                                float* __restrict__ out, int64_t xb, int64_t ob) {
+  col_sum_doc_vec_body<MEAN, 4>(x, rows, cols, stride, out, xb, ob);
 }
 
 // The same with 16-byte loads (a thread takes 4 adjacent columns, a CTA 1024 columns, 4 KB of each row).
@@ -890,8 +906,8 @@ int launch_f32_cols(const float* x, int64_t outer, int64_t rows, int64_t cols, i
         mean ? col_sum_f32_doc_vec_kernel<true, 2><<<grid, 256, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob)
              : col_sum_f32_doc_vec_kernel<false, 2><<<grid, 256, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob);
       else
-        mean ? col_sum_f32_doc_vec_kernel<true, 4><<<grid, 256, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob)
-             : col_sum_f32_doc_vec_kernel<false, 4><<<grid, 256, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob);
+        mean ? col_sum_f32_doc_vec4_kernel<true><<<grid, 256, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob)
+             : col_sum_f32_doc_vec4_kernel<false><<<grid, 256, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob);
     } else if (summing && block > 1) {
       const size_t smem = (size_t)block * 32 * sizeof(double);
       const dim3 grid((unsigned)((cols + 31) / 32), 1, nb);
