@@ -267,7 +267,7 @@ def bench_lifts(ctx, K, W, hbm, bf16):
     ms, _, _ = ctx.timed(lambda i, kin: ops.window(xs[i % R].view(64, 8192, 128), "max", 3, 2, 1, 1, axis=1, out=om),
                          K, W)
     record("window_maxpool3s2_f32_middle_64x8192x128", wl.rowsum_bytes() + om.numel() * 4, ms,
-           "window_f32_cols_ext_kernel", R)
+           "window_f32_lines_staged_kernel", R)
     del om
     # Im2Col: the 3x3, pad 1 unfold of 32 x 64 x 56 x 56 f32 (a ResNet stem's first layer), 9x its input in writes
     ximg = [torch.randn(32, 64, 56, 56, device=ctx.dev) for _ in range(R)]

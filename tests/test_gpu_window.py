@@ -58,11 +58,13 @@ GEOMS = [(3, 1, 1, 0), (3, 2, 1, 1), (5, 3, 2, 2), (1, 1, 1, 0), (7, 4, 3, 3), (
          (2, 1, 1, 1), (3, 1, 1, 2)]
 
 
-# (2, 3000, 4), (3, 37, 8), (2, 10, 16) and (2, 4, 3, 64) along axis 1 take the column kernel (inner a multiple of 4
-# floats) for sizes 2 and 3 at strides 1 and 2: short axes whose output count is not a multiple of 4, and padding
-# in the first and last windows
+# Inner extents that are a multiple of 4 floats take the staged kernel when a tile of 8 outputs fits its 32 KiB
+# buffer ((2, 3000, 4), (3, 37, 8), (2, 10, 16), (2, 4, 3, 64), and (2, 21, 768) at stride 1), else the column
+# kernel for sizes 2 and 3 at strides 1 and 2 ((2, 9, 4096), and (2, 21, 768) at stride 2): short axes whose output
+# count is not a multiple of the tile, and padding in the first and last windows
 @pytest.mark.parametrize("shape,axis", [((4, 1000), 1), ((6, 50, 33), 1), ((3, 40, 7, 5), 2), ((200,), 0),
-                                        ((2, 3000, 4), 1), ((3, 37, 8), 1), ((2, 10, 16), 1), ((2, 4, 3, 64), 1)])
+                                        ((2, 3000, 4), 1), ((3, 37, 8), 1), ((2, 10, 16), 1), ((2, 4, 3, 64), 1),
+                                        ((2, 21, 768), 1), ((2, 9, 4096), 1)])
 @pytest.mark.parametrize("geom", GEOMS)
 def test_window_vs_oracle(shape, axis, geom):
     size, stride, dil, pad = geom
