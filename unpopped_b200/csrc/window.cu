@@ -794,7 +794,8 @@ extern "C" int up_sm100_im2col(const void* x, int elem_bytes, int64_t n, int64_t
   if (oh <= 0 || ow <= 0) return fail_with(UP_ERR_UNSUPPORTED, "im2col: the window is larger than the padded input");
   const int64_t total = n * c * kh * kw * oh * ow;
   if (total == 0) return UP_OK;
-  if (oh * ow > 0x7fffffffLL || h > 0x7fffffffLL || w > 0x7fffffffLL) return UP_ERR_UNSUPPORTED;
+  // 32-bit cell loops step by up to kThreads * 16 cells past the row's end: keep that headroom below 2^31
+  if (oh * ow > 0x7fffffffLL - 16 * win::kThreads || h > 0x7fffffffLL || w > 0x7fffffffLL) return UP_ERR_UNSUPPORTED;
   UP_CHECK_ARG(x != nullptr && out != nullptr);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int g = win::grid_for(n * c * kh * kw);
