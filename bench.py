@@ -613,6 +613,18 @@ def profile_cases(which: str):
         o = torch.empty(64, 4096, 128, device=dev)
         return lambda: ops.window(x, "max", 3, 2, 1, 1, axis=1, out=o)
 
+    @case("im2col")
+    def _():
+        x = torch.randn(32, 64, 56, 56, device=dev)
+        o = torch.empty(32, 64 * 9, 56 * 56, device=dev)
+        return lambda: ops.im2col(x, (3, 3), (1, 1), (1, 1), out=o)
+
+    @case("colsum_doc")
+    def _():
+        x = wl.rowsum_input(device=dev)
+        o = torch.empty(x.shape[1], device=dev)
+        return lambda: ops.reduce2d(x, "sum", 0, block=256, out=o)
+
     @case("argmax")
     def _():
         x = wl.argmax_input(rows=8192, device=dev)
@@ -654,7 +666,7 @@ def main():
     ap.add_argument("--lifts", default="all", choices=["all", "none"])
     ap.add_argument("--profile", default=None,
                     help="run only the small ncu cases of these lifts, comma-separated (scan, rowsum, rowsum_auto, "
-                         "rowmax_f32, colmax_f32, row_softmax, row_rms_norm, window, window_mid, argmax, gather, dequant, w4a16, all)")
+                         "rowmax_f32, colmax_f32, colsum_doc, im2col, row_softmax, row_rms_norm, window, window_mid, argmax, gather, dequant, w4a16, all)")
     args = ap.parse_args()
     if args.profile:
         profile_cases(args.profile)
