@@ -91,6 +91,31 @@ def test_integer_scatter_vs_oracle(dtype, index_dtype, form):
         assert np.array_equal(got, orc.scatter(upd, ids, init, combine)), combine
 
 
+@pytest.mark.parametrize("dtype", [np.int32, np.uint32])
+@pytest.mark.parametrize("cols", [4, 64, 256, 260])
+def test_index_add_whole_rows(dtype, cols):
+    """index_add of whole rows (one target per source row): duplicates, a hot row, out-of-range targets."""
+    rng = np.random.default_rng(cols * 7 + (dtype == np.uint32))
+    n, rows = 20000, 200
+    if dtype == np.uint32:
+        upd = rng.integers(0, 2**32, (n, cols), dtype=np.uint64).astype(np.uint32)
+        init = rng.integers(0, 2**32, (rows, cols), dtype=np.uint64).astype(np.uint32)
+    else:
+        upd = rng.integers(-2**31, 2**31, (n, cols), dtype=np.int64).astype(np.int32)
+        init = rng.integers(-2**31, 2**31, (rows, cols), dtype=np.int64).astype(np.int32)
+    ids = rng.integers(-5, rows + 5, n).astype(np.int32)
+    ids[::3] = 7  # a third of the rows go to one target
+    for combine in ("add", "max", "min"):
+        out = torch.from_numpy(init.view(np.int32).copy()).cuda()
+        tu = torch.from_numpy(upd.view(np.int32)).cuda()
+        if dtype == np.uint32:
+            ops.scatter(tu.view(torch.uint32), torch.from_numpy(ids).cuda(), out.view(torch.uint32), combine)
+        else:
+            ops.scatter(tu, torch.from_numpy(ids).cuda(), out, combine)
+        got = out.cpu().numpy().view(dtype)
+        assert np.array_equal(got, orc.scatter(upd, ids, init, combine)), combine
+
+
 def test_float_scatter_integer_valued_is_exact():
     """f32 and f64 adds of integer-valued data inside 2^24 are exact in every order."""
     rng = np.random.default_rng(3)
