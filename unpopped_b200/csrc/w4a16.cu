@@ -18,26 +18,31 @@
 //    this replaced put 32 rows' worth of sector requests behind every warp instruction.
 //  * warps 0..7 (dequant): warp w owns TMEM lane quarter w % 4 and k-quarters 2 (w / 4) and 2 (w / 4) + 1, so
 //    thread (w, lane) owns row 32 (w % 4) + lane of the tile and 64 UK k of every unit: 32 UK bytes of W, read from
-//    the W stage (conflict free under the swizzle). (Sixteen warps, one k-quarter each, measured 1 % slower and left
+//    the W stage (conflict free under the swizzle). (Sixteen warps, one k-quarter each, measured 4 % slower and left
 //    fewer registers per thread.) It turns the nibbles into exact bf16 (a shift, one lop3 and one bf16x2 subtract per
 //    pair, pairing k with k + 4) and stores them into tensor memory (tcgen05.st) as the MMA's A operand, whose k
-//    order inside each group of 8 is therefore 0,4,1,5,2,6,3,7.
-//  * warps 8..10 (MMA issuers): one thread issues a tcgen05.mma of this shape about every 49 cycles (measured; four
-//    issuing threads reach one per 12 cycles), so three threads take the units in turn (unit i to issuer i % 3), each
-//    issuing all 8 UK k-steps of its unit into one accumulator per k-block and committing the unit's barriers. No
-//    issuer waits for another: chaining them inside a unit (an mbarrier hand-off per k-quarter) put four hand-off
-//    latencies on every unit. Every ring the issuers wait on (A and D slots in tensor memory, activation stages) is at
-//    least three deep, so no parity wait can meet a barrier two phases behind.
+//    order inside each group of 8 is therefore 0,4,1,5,2,6,3,7. The four warps of k-half h (w / 4 = h) release
+//    half h of the unit's A together (one barrier per half).
+//  * warps 8..11 (MMA issuers): one thread issues a tcgen05.mma of this shape about every 49 cycles alone (measured;
+//    four issuing threads reach one per 12 cycles), so the issuers work in two pairs: pair p takes units p, p + 2,
+//    ..., and issuer h of the pair issues the 4 UK k-steps of half h into its own accumulator (a k-block's when
+//    UK = 2) and commits the unit's barriers (counts of two). No issuer waits for another: chaining issuers inside a
+//    unit (an mbarrier hand-off per k-quarter) put four hand-off latencies on every unit. Every ring an issuer waits
+//    on (A and D slots in tensor memory, activation stages) is at least as deep as the number of pairs, so no parity
+//    wait can meet a barrier two phases behind.
 //  * warp 16 (activation loader): one thread brings each unit's [16 x 128 UK] activation tile into a ring of
 //    shared-memory stages with 2 UK TMA boxes, 128-byte swizzled as the MMA reads it; rows past M read as 0.
-//  * warp 11 (activation permuter): rewrites each landed 16-byte chunk (8 k) in place to the k order 0,4,1,5,2,6,
+//  * warp 19 (activation permuter): rewrites each landed 16-byte chunk (8 k) in place to the k order 0,4,1,5,2,6,
 //    3,7 of the A operand (the swizzle moves whole chunks, so it is unaffected), then releases the stage to the MMA.
 //  * warp 17 (scale loader): one thread brings each unit's scales, f16 groups [g0, g0 + 16) of its 128 rows with
 //    g0 = the unit's first group rounded down to a multiple of 8, into a ring of shared-memory slots with one TMA
 //    box. (A scale row stride that is not a multiple of 16 bytes cannot be a TMA tensor; then the warp's lanes load
-//    and store the same slot layout.) Loading them in the epilogue put a global-load latency on every unit.
-//  * warps 12..15 (epilogue): read the unit's accumulators (tcgen05.ld), scale each by scale[n][k-block] in
-//    f32 and accumulate in registers, k-block by k-block. A tile finished inside one CTA is written as bf16;
+//    and store the same slot layout.) Loading them in the epilogue put a global-load latency on every unit. Beside
+//    each unit's scales it writes the unit's header: the tile, where tile segments start and end, and the slot
+//    columns of the unit's scales.
+//  * warps 12..15 (epilogue): read the unit's two half accumulators (tcgen05.ld), scale each k-block by
+//    scale[n][k-block] in f32 (for UK = 1, the two halves of the one k-block are summed first) and accumulate in
+//    registers, unit by unit as the headers say. A tile finished inside one CTA is written as bf16;
 //    a tile split between CTAs writes f32 partials, and whichever CTA finishes it last (an atomic count)
 //    sums them in CTA order, writes bf16 and clears the partials — no CTA ever waits on another.
 // Every mbarrier wait is bounded; a wait that runs out sets the workspace error word and the CTA unwinds.
