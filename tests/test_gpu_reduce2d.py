@@ -114,6 +114,73 @@ def test_float_sum_mean_vs_oracle(rows, cols):
     assert np.array_equal(bits(ops.reduce2d(x, "mean", 1, block=1).cpu()), bits(orc.reduce2d_f32(xn, "mean", 1)))
 
 
+def _serial_columns(rng, rows, cols):
+    """Columns for the outer-axis Sum in the serial order, one kind per column in turn: N(0,1) and U[0,1) (chunks
+    stay exact), a few values near 2^-40 among N(0,1) ones, sums of ones with tiny and large values (partial sums
+    at full precision that cross binades), exponents over 40 binades, subnormals beside normals, NaN/±Inf/±0
+    specials, and all -0 (the sum is +0)."""
+    kinds = []
+    for c in range(cols):
+        k = c % 8
+        if k == 0:
+            v = rng.standard_normal(rows)
+        elif k == 1:
+            v = rng.random(rows)
+        elif k == 2:
+            v = rng.standard_normal(rows)
+            v[rng.random(rows) < 0.01] = rng.choice([2.0 ** -40, -3.0 * 2.0 ** -45, 2.0 ** -30], 1)[0]
+        elif k == 3:
+            v = np.where(rng.random(rows) < 0.7, 1.0, rng.choice([2.0 ** -28, 2.0 ** -52, 3.0 * 2.0 ** 24], rows))
+        elif k == 4:
+            v = (rng.random(rows) - 0.5) * 2.0 ** rng.integers(-20, 20, rows)
+        elif k == 5:
+            v = rng.standard_normal(rows) * np.where(rng.random(rows) < 0.5, 2.0 ** -135, 1.0)
+        elif k == 6:
+            v = _specials(rng, rows, 1)[:, 0]  # kept in f32: the NaN payloads stay as drawn
+        else:
+            v = np.full(rows, -0.0)
+        kinds.append(v if v.dtype == np.float32 else v.astype(np.float32))
+    return np.ascontiguousarray(np.stack(kinds, axis=1))
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 33), (63, 40), (64, 32), (65, 31), (1023, 70), (1024, 64), (1025, 96),
+                                       (3000, 257), (8192, 100), (8193, 16), (20000, 12), (20000, 9)])
+def test_outer_sum_serial_order_exact_and_rounding_chunks(rows, cols):
+    """The outer-axis Sum/Mean in the serial order, bit for bit, on columns whose chunks are added out of order (no
+    add rounds) and columns that round and take the value-by-value fold, at row counts on both sides of the 64-row
+    chunk, the 1,024-row segment and the 8,192-row round of the cluster form (widths that are a multiple of 4 on
+    16-byte aligned rows); NaN results match as NaN. A strided, unaligned view takes the 32-column form."""
+    rng = np.random.default_rng(rows * 7 + cols)
+    xn = _serial_columns(rng, rows, cols)
+    wide = np.zeros((rows, cols + 5), np.float32)
+    wide[:, 3:3 + cols] = xn
+    wt = torch.from_numpy(wide).cuda()
+    for x in (torch.from_numpy(xn).cuda(), wt[:, 3:3 + cols]):
+        for op in ("sum", "mean"):
+            got = ops.reduce2d(x, op, 0).cpu().numpy()
+            want = orc.reduce2d_f32(xn, op, 0)
+            nan = np.isnan(want)
+            assert np.array_equal(np.isnan(got), nan), op
+            assert np.array_equal(bits(got)[~nan], bits(want)[~nan]), op
+
+
+@pytest.mark.parametrize("dist", ["normal", "uniform", "ones_and_tiny"])
+def test_outer_sum_serial_order_full_strips(dist):
+    """8,192 x 8,192 in the cluster form: N(0,1) (the all-exact round), U[0,1) (a few chunks round) and unit values
+    with a tiny one in every 50 (most rounds fall back to rank order), bit for bit against the serial fold."""
+    rng = np.random.default_rng(5)
+    if dist == "normal":
+        xn = rng.standard_normal((8192, 8192), dtype=np.float32)
+    elif dist == "uniform":
+        xn = rng.random((8192, 8192), dtype=np.float32)
+    else:
+        xn = np.where(rng.random((8192, 8192)) < 0.02, np.float32(2.0 ** -35), np.float32(1.0)).astype(np.float32)
+    x = torch.from_numpy(xn).cuda()
+    t = orc.max_threads()
+    for op in ("sum", "mean"):
+        assert np.array_equal(bits(ops.reduce2d(x, op, 0).cpu()), bits(orc.reduce2d_f32(xn, op, 0, t))), op
+
+
 @pytest.mark.parametrize("cols", [96, 8192, 12000])
 def test_float_max_min_structured_rows(cols):
     """Rows built to hit each branch of the chunked fold: all -inf / +inf, all NaN, +0 and -0 ties in either order,

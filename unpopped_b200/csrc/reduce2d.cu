@@ -12,8 +12,9 @@
 //    element of the extreme value (so the first zero's sign when +0 and -0 tie). The kernels keep the best value
 //    with its first index and the last NaN's index; merging those by value (ties to the lower index) is
 //    order-independent.
-//  * f32 Sum/Mean over the outer axis fold each column in the serial order in f64 (one thread per column: the
-//    order is the oracle's, not a tree), one rounding; Mean divides by the row count, so an empty Mean is 0/0.
+//  * f32 Sum/Mean over the outer axis fold each column in the serial order in f64, one rounding (the kernels add
+//    runs of values out of order only where no add of the serial fold can round); Mean divides by the row count,
+//    so an empty Mean is 0/0.
 #include "common.cuh"
 
 #include <cooperative_groups.h>
@@ -533,88 +534,309 @@ __global__ void __cluster_dims__(1, kColCluster, 1) __launch_bounds__(32 * kColV
   cluster.sync();  // rank 0 has read the other CTAs' shared memory before they exit
 }
 
-// f32 Sum/Mean over the outer axis, one thread per column folding the rows in order in f64 (the serial order; a
-// split of the rows would change the roundings).
-template <int OP>
-__global__ void __launch_bounds__(kThreads) col_f32_kernel(const float* __restrict__ x, int64_t rows, int64_t cols,
-                                                            int64_t stride, float* __restrict__ out, int64_t xb, int64_t ob) {
-  x += (int64_t)blockIdx.z * xb;  // batch z of a middle-axis reduction
-  out += (int64_t)blockIdx.z * ob;
-  static_assert(OP == UP_OP_SUM || OP == UP_OP_MEAN, "Sum or Mean");
-  const int64_t c = (int64_t)blockIdx.x * kThreads + threadIdx.x;
-  if (c >= cols) return;
-  double acc = 0.0;
-  int64_t r = 0;
-  for (; r + 3 < rows; r += 4) {
-    float v[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) v[u] = __ldg(x + (r + u) * stride + c);
-#pragma unroll
-    for (int u = 0; u < 4; ++u) acc += (double)v[u];
-  }
-  for (; r < rows; ++r) acc += (double)__ldg(x + r * stride + c);
-  out[c] = __double2float_rn(OP == UP_OP_MEAN ? acc / (double)rows : acc);
+// f32 Sum/Mean over the outer axis in the serial order per column: s = (((0 + x0) + x1) + ...) in f64, one rounding
+// to f32 (plan_eval.rs:566-645). Folded directly, each column is a chain of 8,192 dependent f64 adds with the
+// loads in front of them. The kernels below get the same bits with a short chain:
+//  * Exactness. Every f32 is an integer multiple of its ulp, 2^(max(e,1) - 150) for exponent field e. If all the
+//    values added since the last inexact step are multiples of 2^q, so is every partial sum, and a partial sum
+//    below 2^(q+53) in magnitude is a multiple of 2^q with at most 53 significant bits: representable, so the add
+//    that made it did not round. While no add rounds, the serial fold is the exact sum, and any order of adding a
+//    run of values gives the same bits.
+//  * Chunks. Producer warps read each column in chunks of 64 rows and summarise a chunk in three numbers: T, its
+//    sum in f64 in a tree (exact whenever it is used); L = 2^(q + 53) for q the smallest ulp exponent of its
+//    nonzero values; and H, a bound of the magnitude of every prefix sum of the chunk: the running f32 prefix's
+//    largest magnitude plus 2^-17 · B, where B bounds the sum of |x| (f32 adds of |x|, rounded up by a factor
+//    1 + 2^-15). A 64-value f32 prefix is off by at most 64 · 2^-24 · B = 2^-18 · B. If B < L fails (a NaN, an
+//    infinity, an overflow, or a tree that may round), H is +inf.
+//  * The chain walks a column's chunks in order with the running sum s and lim, the minimum of the L seen since the
+//    last anchor. The serial fold's partial sums inside a chunk are s + (a prefix), at most |s| + H in magnitude,
+//    so if |s| + H < lim each is a multiple of 2^q below 2^(q+53), as is each partial sum of the tree (at most
+//    B < L): the chunk adds no rounding, and s + T is exact. Otherwise the chunk is re-read and folded value by
+//    value in f64, as the serial fold does; s then anchors lim at 2^(lowbit(s) + 53), lowbit(s) the place of its
+//    lowest set bit. A NaN or infinite s fails the comparison, so the rest of such a column takes the serial fold
+//    too (NaN payloads propagate as they do there).
+// On N(0,1) data about 0.002 % of chunks take the serial fold and on U[0,1) about 0.04 %; on data whose exponents
+// spread over 30 binades or more nearly all do, and the kernels then run at about the speed of the plain fold.
+constexpr int kSpecChunk = 64;
+
+__device__ __forceinline__ double pow2_biased(uint32_t e) { return __longlong_as_double((long long)e << 52); }
+__device__ __forceinline__ double f64_inf() { return __longlong_as_double(0x7ff0000000000000ll); }
+
+// 2^(lowbit(s) + 53) for a finite nonzero s, +inf otherwise.
+__device__ __forceinline__ double spec_anchor(double s) {
+  const uint64_t u = (uint64_t)__double_as_longlong(s);
+  const uint32_t ex = (uint32_t)(u >> 52) & 0x7ffu;
+  const uint64_t m = u & ((1ull << 52) - 1);
+  if ((u << 1) == 0 || ex == 0x7ffu) return f64_inf();
+  const uint64_t sig = ex ? (m | (1ull << 52)) : m;
+  const uint32_t le = (ex ? ex : 1u) + (uint32_t)(__ffsll((long long)sig) - 1) + 1u;
+  return pow2_biased(le < 2046u ? le : 2046u);
 }
 
-// The same serial order with the rows staged through shared memory, for 16-byte aligned rows whose width is a
-// multiple of 4: a CTA is one warp and 32 columns. The chain of f64 adds per column is inherently serial, so the
-// only parallelism is across columns; to keep enough bytes in flight the warp runs D stages of 32 rows x 128 B ahead
-// with 16-byte cp.async copies (lane l copies rows l/8, l/8 + 4, ... of columns 4(l%8) .. 4(l%8)+3), and lane l
-// adds column l of each staged row in order. Copies past the last row or column are zero-filled and never added.
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
-  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sa), "l"(gmem), "r"(src_bytes) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+// One value into a chunk summary. mn keeps the minimum of (bits << 1) - 2: the sign drops out, and both zeros wrap
+// to the top so they never count.
+__device__ __forceinline__ void spec_acc(float v, double& t, float& b, float& pre, float& hi, uint32_t& mn) {
+  t += (double)v;
+  b += fabsf(v);
+  pre += v;
+  hi = fmaxf(hi, fabsf(pre));
+  mn = min(mn, (__float_as_uint(v) << 1) - 2u);
 }
 
-template <bool MEAN, int D>
-__global__ void __launch_bounds__(32) col_sum_f32_serial_kernel(const float* __restrict__ x, int64_t rows,
-                                                                int64_t cols, int64_t stride,
-                                                                float* __restrict__ out, int64_t xb, int64_t ob) {
+// L and H of a chunk from its accumulators.
+__device__ __forceinline__ void spec_finish(float b, float hi, uint32_t mn, double& lc, float& h) {
+  const float bsum = b * 1.000030517578125f;    // 1 + 2^-15
+  const float err = bsum * 7.62939453125e-06f;  // 2^-17
+  lc = mn >= 0xfffffffeu ? f64_inf() : pow2_biased(max((mn + 2u) >> 24, 1u) + 926u);
+  h = (double)bsum < lc ? hi + err : __int_as_float(0x7f800000);
+}
+
+// The serial fold of one chunk's rows (a chunk that may round), and the anchor after it.
+__device__ __forceinline__ void spec_serial_chunk(const float* __restrict__ xc, int64_t r0, int64_t rows,
+                                                  int64_t stride, double& s, double& lim) {
+  float v[kSpecChunk];
+#pragma unroll
+  for (int k = 0; k < kSpecChunk; ++k) v[k] = r0 + k < rows ? __ldg(xc + (r0 + k) * stride) : 0.f;
+#pragma unroll
+  for (int k = 0; k < kSpecChunk; ++k)
+    if (r0 + k < rows) s += (double)v[k];
+  lim = spec_anchor(s);
+}
+
+// The form for any row alignment: a CTA takes 32 columns (lane l: column 32·blockIdx.x + l); warps 1..8 summarise
+// segments of 16 chunks, warp 0 walks them, and a segment's summaries are double-buffered in shared memory so the
+// chain walks segment i - 1 while the producers summarise segment i. The chain adds a segment's chunks
+// speculatively and checks all of them beside it; a lane with a failed check goes back to the segment's start.
+constexpr int kSpecSeg = 16, kSpecProducers = 8;
+
+template <bool MEAN>
+__global__ void __launch_bounds__(32 * (kSpecProducers + 1), 2)
+    col_sum_f32_serial_spec_kernel(const float* __restrict__ x, int64_t rows, int64_t cols, int64_t stride,
+                                   float* __restrict__ out, int64_t xb, int64_t ob) {
   x += (int64_t)blockIdx.z * xb;  // batch z of a middle-axis reduction
   out += (int64_t)blockIdx.z * ob;
-  extern __shared__ __align__(16) float stage[];  // [D][32 rows][32 columns]
-  const int lane = threadIdx.x;
-  const int64_t cb = (int64_t)blockIdx.x * 32;
-  const int lr = lane >> 3, lc = (lane & 7) * 4;
-  const bool cok = cb + lc < cols;
-  const int64_t nst = (rows + 31) / 32;
-  auto issue = [&](int64_t st) {
-    if (st < nst) {
-      float* b = stage + (size_t)(st % D) * 1024;
+  __shared__ double s_t[2][kSpecSeg][32], s_l[2][kSpecSeg][32];
+  __shared__ float s_h[2][kSpecSeg][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t col = (int64_t)blockIdx.x * 32 + lane;
+  const bool cok = col < cols;
+  const float* __restrict__ xc = x + (cok ? col : 0);
+  const int64_t nseg = (rows + kSpecChunk * kSpecSeg - 1) / (kSpecChunk * kSpecSeg);
+  double s = 0.0, lim = f64_inf();  // the chain's state (warp 0)
+  for (int64_t i = 0; i <= nseg; ++i) {
+    if (warp > 0) {
+      if (i < nseg) {
+        const int bb = (int)(i & 1);
+        for (int j = warp - 1; j < kSpecSeg; j += kSpecProducers) {
+          const int64_t r0 = (i * kSpecSeg + j) * kSpecChunk;
+          float v[kSpecChunk];
+          if (cok && r0 + kSpecChunk <= rows) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int rr = lr + 4 * k;
-        const int64_t r = st * 32 + rr;
-        const bool ok = cok && r < rows;
-        cp_async16(b + rr * 32 + lc, ok ? x + r * stride + cb + lc : x, ok ? 16 : 0);
+            for (int k = 0; k < kSpecChunk; ++k) v[k] = __ldg(xc + (r0 + k) * stride);
+          } else {
+#pragma unroll
+            for (int k = 0; k < kSpecChunk; ++k) v[k] = (cok && r0 + k < rows) ? __ldg(xc + (r0 + k) * stride) : 0.f;
+          }
+          double t[8] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0};
+          float b = 0.f, pre = 0.f, hi = 0.f;
+          uint32_t mn = 0xffffffffu;
+#pragma unroll
+          for (int k = 0; k < kSpecChunk; ++k) spec_acc(v[k], t[k & 7], b, pre, hi, mn);
+          double lc;
+          float h;
+          spec_finish(b, hi, mn, lc, h);
+          s_t[bb][j][lane] = ((t[0] + t[1]) + (t[2] + t[3])) + ((t[4] + t[5]) + (t[6] + t[7]));
+          s_l[bb][j][lane] = lc;
+          s_h[bb][j][lane] = h;
+        }
+      }
+    } else if (i > 0) {
+      const int bb = (int)((i - 1) & 1);
+      const double s0 = s, l0 = lim;
+      bool ok = true;
+#pragma unroll
+      for (int j = 0; j < kSpecSeg; ++j) {
+        lim = fmin(lim, s_l[bb][j][lane]);
+        ok &= fabs(s) + (double)s_h[bb][j][lane] < lim;
+        s += s_t[bb][j][lane];
+      }
+      if (!ok) {
+        s = s0;
+        lim = l0;
+        for (int j = 0; j < kSpecSeg; ++j) {
+          lim = fmin(lim, s_l[bb][j][lane]);
+          if (fabs(s) + (double)s_h[bb][j][lane] < lim)
+            s += s_t[bb][j][lane];
+          else
+            spec_serial_chunk(xc, ((i - 1) * kSpecSeg + j) * kSpecChunk, rows, stride, s, lim);
+        }
       }
     }
-    cp_async_commit();  // an empty group past the end keeps the group count uniform
-  };
-#pragma unroll
-  for (int st = 0; st < D - 1; ++st) issue(st);
-  double acc = 0.0;
-  for (int64_t st = 0; st < nst; ++st) {
-    issue(st + D - 1);  // into the buffer read in the previous step
-    cp_async_wait<D - 1>();
-    __syncwarp();
-    const float* b = stage + (size_t)(st % D) * 1024 + lane;
-    if (st * 32 + 32 <= rows) {
-#pragma unroll
-      for (int k = 0; k < 32; ++k) acc += (double)b[k * 32];
-    } else {
-      const int n = (int)(rows - st * 32);
-      for (int k = 0; k < n; ++k) acc += (double)b[k * 32];
-    }
-    __syncwarp();  // every lane has read the buffer before the next step refills it
+    __syncthreads();  // segment i is summarised and segment i - 1 walked before either buffer is reused
   }
-  cp_async_wait<0>();
-  if (cb + lane < cols) out[cb + lane] = __double2float_rn(MEAN ? acc / (double)rows : acc);
+  if (warp == 0 && cok) out[col] = __double2float_rn(MEAN ? s / (double)rows : s);
+}
+
+// The form for 16-byte aligned rows whose width is a multiple of 4, which reads 512 bytes of a row per warp (a float4
+// per lane): a CTA takes a strip of 128 columns and a cluster of kStripCluster CTAs splits the rows. Chunks go in
+// rounds of kStripCluster · kStripCap; in each round rank k summarises its share of the round's chunks into shared
+// memory (all 8 warps, a lane's 4 columns at once). Then, one column per lane of warps 0..3:
+//  1. each rank adds its own chunks' T in order (SL) and takes the minimum of their L (ML), noting whether every
+//     partial sum of SL stayed below ML (then SL is exact);
+//  2. rank k starts from the round's carry plus SL of ranks 0..k-1 (read through distributed shared memory), with
+//     lim the minimum of the carry's and their ML, and walks its chunks with the checks;
+//  3. if every check of every rank held and every SL used was exact, each start was the serial fold's own, and
+//     rank kStripCluster-1's result is the next carry. Otherwise the ranks go in order: rank k takes the carry from
+//     rank k-1 and keeps its own result if its speculative start equals that carry bit for bit, else walks again
+//     from the carry (re-reading any chunk that may round).
+constexpr int kStripCols = 128, kStripCluster = 4, kStripCap = 32, kStripWarps = 8, kStripSub = 16;
+constexpr int kStripSmem = kStripCap * kStripCols * (8 + 8 + 4) + 4 * kStripCols * 8 + 16;
+
+template <bool MEAN>
+__global__ void __cluster_dims__(1, kStripCluster, 1) __launch_bounds__(32 * kStripWarps, 2)
+    col_sum_f32_serial_strip_kernel(const float* __restrict__ x, int64_t rows, int64_t cols, int64_t stride,
+                                    float* __restrict__ out, int64_t xb, int64_t ob) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  x += (int64_t)blockIdx.z * xb;  // batch z of a middle-axis reduction
+  out += (int64_t)blockIdx.z * ob;
+  extern __shared__ __align__(16) unsigned char strip_smem[];
+  double* s_t = reinterpret_cast<double*>(strip_smem);  // [kStripCap][128] chunk sums T
+  double* s_l = s_t + kStripCap * kStripCols;            // [kStripCap][128] chunk limits L
+  double* s_carry = s_l + kStripCap * kStripCols;        // [2][128]: s and lim handed to this rank
+  double* s_part = s_carry + 2 * kStripCols;             // [2][128]: this rank's SL and ML
+  float* s_h = reinterpret_cast<float*>(s_part + 2 * kStripCols);  // [kStripCap][128] prefix bounds H
+  int* s_fail = reinterpret_cast<int*>(s_h + kStripCap * kStripCols);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t c0 = (int64_t)blockIdx.x * kStripCols;
+  const bool pok = c0 + 4 * lane < cols;  // a producer lane's 4 columns (cols is a multiple of 4)
+  const int ccol = 32 * warp + lane;      // a chain lane's column (warps 0..3)
+  const bool cok = warp < 4 && c0 + ccol < cols;
+  const float* __restrict__ xq = x + c0 + (cok ? ccol : 0);
+  if (threadIdx.x < kStripCols) {
+    s_carry[threadIdx.x] = 0.0;
+    s_carry[kStripCols + threadIdx.x] = f64_inf();
+  }
+  cluster.sync();  // every CTA of the cluster runs and holds its initial carry before any hand-off
+  const float* __restrict__ xp = x + c0 + 4 * lane;
+  const int64_t nchunks = (rows + kSpecChunk - 1) / kSpecChunk;
+  const int64_t per_round = (int64_t)kStripCluster * kStripCap;
+  for (int64_t g0 = 0; g0 < nchunks; g0 += per_round) {
+    const int64_t nch = min(per_round, nchunks - g0);
+    const int64_t share = (nch + kStripCluster - 1) / kStripCluster;
+    const int64_t mb = g0 + min(nch, (int64_t)rank * share);  // this rank's first chunk
+    const int me = (int)(g0 + min(nch, (int64_t)(rank + 1) * share) - mb);
+    for (int j = warp; j < me; j += kStripWarps) {
+      const int64_t r0 = (mb + j) * kSpecChunk;
+      double t[4][2] = {{0.0, 0.0}, {0.0, 0.0}, {0.0, 0.0}, {0.0, 0.0}};
+      float b[4] = {0.f, 0.f, 0.f, 0.f}, pre[4] = {0.f, 0.f, 0.f, 0.f}, hi[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t mn[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+      for (int sb = 0; sb < kSpecChunk; sb += kStripSub) {
+        float4 v[kStripSub];
+        const bool full = pok && r0 + sb + kStripSub <= rows;
+#pragma unroll
+        for (int k = 0; k < kStripSub; ++k) {
+          const int64_t r = r0 + sb + k;
+          v[k] = (full || (pok && r < rows)) ? ld_nc_na_f4(xp + r * stride) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < kStripSub; ++k) {
+          spec_acc(v[k].x, t[0][k & 1], b[0], pre[0], hi[0], mn[0]);
+          spec_acc(v[k].y, t[1][k & 1], b[1], pre[1], hi[1], mn[1]);
+          spec_acc(v[k].z, t[2][k & 1], b[2], pre[2], hi[2], mn[2]);
+          spec_acc(v[k].w, t[3][k & 1], b[3], pre[3], hi[3], mn[3]);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int at = j * kStripCols + 4 * lane + c;
+        double lc;
+        float h;
+        spec_finish(b[c], hi[c], mn[c], lc, h);
+        s_t[at] = t[c][0] + t[c][1];
+        s_l[at] = lc;
+        s_h[at] = h;
+      }
+    }
+    __syncthreads();
+    // 1. this rank's SL and ML
+    double si = 0.0, li = 0.0, so = 0.0, lo = 0.0;  // the speculative start and result
+    bool exact = true, wok = true;                  // SL exact (or unused); every check of the walk held
+    if (cok) {
+      double sl = 0.0, ml = f64_inf(), mx = 0.0;
+#pragma unroll 4
+      for (int j = 0; j < me; ++j) {
+        ml = fmin(ml, s_l[j * kStripCols + ccol]);
+        sl += s_t[j * kStripCols + ccol];
+        mx = fmax(mx, fabs(sl));
+      }
+      s_part[ccol] = sl;
+      s_part[kStripCols + ccol] = ml;
+      exact = rank == kStripCluster - 1 || mx < ml;  // SL is used by later ranks only
+    }
+    cluster.sync();
+    // 2. the speculative start and the checked walk
+    if (cok) {
+      const double* c0r = cluster.map_shared_rank(s_carry, 0);
+      double s = c0r[ccol], lim = c0r[kStripCols + ccol];
+      for (int q = 0; q < rank; ++q) {
+        const double* pr = cluster.map_shared_rank(s_part, q);
+        s += pr[ccol];
+        lim = fmin(lim, pr[kStripCols + ccol]);
+      }
+      si = s;
+      li = lim;
+#pragma unroll 4
+      for (int j = 0; j < me; ++j) {
+        lim = fmin(lim, s_l[j * kStripCols + ccol]);
+        wok &= fabs(s) + (double)s_h[j * kStripCols + ccol] < lim;
+        s += s_t[j * kStripCols + ccol];
+      }
+      so = s;
+      lo = lim;
+    }
+    const int fail = __syncthreads_or(cok && !(exact && wok));
+    if (threadIdx.x == 0) *s_fail = fail;
+    cluster.sync();
+    bool any = false;
+    for (int q = 0; q < kStripCluster; ++q) any |= *cluster.map_shared_rank(s_fail, q) != 0;
+    if (!any) {
+      // 3. every start was the serial fold's own: the last rank's result carries
+      if (rank == kStripCluster - 1 && cok) {
+        double* dst = cluster.map_shared_rank(s_carry, 0);
+        dst[ccol] = so;
+        dst[kStripCols + ccol] = lo;
+      }
+      cluster.sync();
+    } else {
+      for (int p = 0; p < kStripCluster; ++p) {
+        if (rank == p && cok) {
+          double s = s_carry[ccol], lim = s_carry[kStripCols + ccol];
+          if (!(wok && __double_as_longlong(s) == __double_as_longlong(si) &&
+                __double_as_longlong(lim) == __double_as_longlong(li))) {
+            for (int j = 0; j < me; ++j) {
+              lim = fmin(lim, s_l[j * kStripCols + ccol]);
+              if (fabs(s) + (double)s_h[j * kStripCols + ccol] < lim)
+                s += s_t[j * kStripCols + ccol];
+              else
+                spec_serial_chunk(xq, (mb + j) * kSpecChunk, rows, stride, s, lim);
+            }
+            so = s;
+            lo = lim;
+          }
+          double* dst = cluster.map_shared_rank(s_carry, (p + 1) % kStripCluster);
+          dst[ccol] = so;
+          dst[kStripCols + ccol] = lo;
+        }
+        cluster.sync();  // the hand-off is visible before the next rank reads it
+      }
+    }
+  }
+  if (rank == 0 && cok) {
+    const double s = s_carry[ccol];
+    out[c0 + ccol] = __double2float_rn(MEAN ? s / (double)rows : s);
+  }
 }
 
 // f32 Sum/Mean over the outer axis in the launched lift's documented order for a logical block of B threads
@@ -623,7 +845,6 @@ __global__ void __launch_bounds__(32) col_sum_f32_serial_kernel(const float* __r
 // columns (one per lane) and 16 warps; warp w holds logical threads w, w+16, ... (B/16 accumulators; B <= 256),
 // so each step loads B/16 rows per thread, all coalesced across the 32 columns. The tree runs in shared memory.
 constexpr int kDocWarps = 16, kDocMaxB = 256;
-constexpr int kSerialStages = 12;  // 48 KB of rows in flight per 32 columns (measured best of 4, 8, 12)
 template <bool MEAN>
 __global__ void __launch_bounds__(32 * kDocWarps) col_sum_f32_doc_kernel(const float* __restrict__ x, int64_t rows,
                                                                          int64_t cols, int64_t stride, int B,
@@ -886,6 +1107,11 @@ int launch_f32_cols(const float* x, int64_t outer, int64_t rows, int64_t cols, i
   const int64_t gx = (cols + kThreads - 1) / kThreads;
   if (gx > 0x7fffffff) return UP_ERR_UNSUPPORTED;
   const bool vec = aligned(x, 16) && cols % 4 == 0 && row_stride % 4 == 0 && xb % 4 == 0;
+  if (summing && block == 1 && vec) {
+    cudaError_t e = ensure_smem_attr((const void*)col_sum_f32_serial_strip_kernel<true>, kStripSmem);
+    if (e == cudaSuccess) e = ensure_smem_attr((const void*)col_sum_f32_serial_strip_kernel<false>, kStripSmem);
+    if (e != cudaSuccess) return cuda_status(e);
+  }
   if (summing && block > 1 && !(block >= 64 && vec)) {
     const int bytes = (int)((size_t)kDocMaxB * 32 * sizeof(double));
     cudaError_t e = ensure_smem_attr((const void*)col_sum_f32_doc_kernel<true>, bytes);
@@ -916,16 +1142,21 @@ int launch_f32_cols(const float* x, int64_t outer, int64_t rows, int64_t cols, i
       else
         col_sum_f32_doc_kernel<false><<<grid, 32 * kDocWarps, smem, s>>>(xs, rows, cols, row_stride, block, os, xb, ob);
     } else if (summing && vec) {
-      const size_t smem = (size_t)kSerialStages * 32 * 32 * sizeof(float);
+      const dim3 grid((unsigned)((cols + kStripCols - 1) / kStripCols), kStripCluster, nb);
+      if (mean)
+        col_sum_f32_serial_strip_kernel<true><<<grid, 32 * kStripWarps, kStripSmem, s>>>(xs, rows, cols, row_stride,
+                                                                                      os, xb, ob);
+      else
+        col_sum_f32_serial_strip_kernel<false><<<grid, 32 * kStripWarps, kStripSmem, s>>>(xs, rows, cols, row_stride,
+                                                                                       os, xb, ob);
+    } else if (summing) {
       const dim3 grid((unsigned)((cols + 31) / 32), 1, nb);
       if (mean)
-        col_sum_f32_serial_kernel<true, kSerialStages><<<grid, 32, smem, s>>>(xs, rows, cols, row_stride, os, xb, ob);
+        col_sum_f32_serial_spec_kernel<true><<<grid, 32 * (kSpecProducers + 1), 0, s>>>(xs, rows, cols, row_stride, os,
+                                                                                       xb, ob);
       else
-        col_sum_f32_serial_kernel<false, kSerialStages><<<grid, 32, smem, s>>>(xs, rows, cols, row_stride, os, xb, ob);
-    } else if (summing) {
-      const dim3 grid((unsigned)gx, 1, nb);
-      if (mean) col_f32_kernel<UP_OP_MEAN><<<grid, kThreads, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob);
-      else col_f32_kernel<UP_OP_SUM><<<grid, kThreads, 0, s>>>(xs, rows, cols, row_stride, os, xb, ob);
+        col_sum_f32_serial_spec_kernel<false><<<grid, 32 * (kSpecProducers + 1), 0, s>>>(xs, rows, cols, row_stride,
+                                                                                        os, xb, ob);
     } else if (vec) {
       const dim3 grid((unsigned)((cols + kColStrip - 1) / kColStrip), kColCluster, nb);
       if (op == UP_OP_MAX)
