@@ -542,16 +542,15 @@ __global__ void __cluster_dims__(1, kColCluster, 1) __launch_bounds__(32 * kColV
 //    below 2^(q+53) in magnitude is a multiple of 2^q with at most 53 significant bits: representable, so the add
 //    that made it did not round. While no add rounds, the serial fold is the exact sum, and any order of adding a
 //    run of values gives the same bits.
-//  * Chunks. Producer warps read each column in chunks of 64 rows and summarise a chunk in three numbers: T, its
-//    sum in f64 in a tree (exact whenever it is used); L = 2^(q + 53) for q the smallest ulp exponent of its
-//    nonzero values; and H, a bound of the magnitude of every prefix sum of the chunk: the running f32 prefix's
-//    largest magnitude plus 2^-17 · B, where B bounds the sum of |x| (f32 adds of |x|, rounded up by a factor
-//    1 + 2^-15). A 64-value f32 prefix is off by at most 64 · 2^-24 · B = 2^-18 · B. If B < L fails (a NaN, an
-//    infinity, an overflow, or a tree that may round), H is +inf.
+//  * Chunks. Producer warps read each column in chunks of 64 rows and summarise a chunk in three numbers: L =
+//    2^(q + 53) for q the smallest ulp exponent of its nonzero values; T, its prefix sum in f64 in row order; and
+//    H, the largest magnitude of those prefix sums, rounded up to f32. If H < L, no add of the prefix rounded (the
+//    first that did would have made a partial sum of magnitude at least L, since L is a power of two and rounding
+//    is monotone), so T and H are exact. Otherwise, or if T is a NaN or infinite, H is +inf.
 //  * The chain walks a column's chunks in order with the running sum s and lim, the minimum of the L seen since the
 //    last anchor. The serial fold's partial sums inside a chunk are s + (a prefix), at most |s| + H in magnitude,
-//    so if |s| + H < lim each is a multiple of 2^q below 2^(q+53), as is each partial sum of the tree (at most
-//    B < L): the chunk adds no rounding, and s + T is exact. Otherwise the chunk is re-read and folded value by
+//    so if |s| + H < lim each is a multiple of 2^q below 2^(q+53): the chunk adds no rounding, and s + T is
+//    exact. Otherwise the chunk is re-read and folded value by
 //    value in f64, as the serial fold does; s then anchors lim at 2^(lowbit(s) + 53), lowbit(s) the place of its
 //    lowest set bit. A NaN or infinite s fails the comparison, so the rest of such a column takes the serial fold
 //    too (NaN payloads propagate as they do there).
@@ -575,32 +574,49 @@ __device__ __forceinline__ double spec_anchor(double s) {
 
 // One value into a chunk summary. mn keeps the minimum of (bits << 1) - 2: the sign drops out, and both zeros wrap
 // to the top so they never count.
-__device__ __forceinline__ void spec_acc(float v, double& t, float& b, float& pre, float& hi, uint32_t& mn) {
-  t += (double)v;
-  b += fabsf(v);
-  pre += v;
-  hi = fmaxf(hi, fabsf(pre));
+__device__ __forceinline__ void spec_acc(float v, double& pre, double& hi, uint32_t& mn) {
+  pre += (double)v;
+  hi = fmax(hi, fabs(pre));
   mn = min(mn, (__float_as_uint(v) << 1) - 2u);
 }
 
-// L and H of a chunk from its accumulators.
-__device__ __forceinline__ void spec_finish(float b, float hi, uint32_t mn, double& lc, float& h) {
-  const float bsum = b * 1.000030517578125f;    // 1 + 2^-15
-  const float err = bsum * 7.62939453125e-06f;  // 2^-17
+// L and H of a chunk from its accumulators (T is the prefix itself).
+__device__ __forceinline__ void spec_finish(double pre, double hi, uint32_t mn, double& lc, float& h) {
   lc = mn >= 0xfffffffeu ? f64_inf() : pow2_biased(max((mn + 2u) >> 24, 1u) + 926u);
-  h = (double)bsum < lc ? hi + err : __int_as_float(0x7f800000);
+  h = (hi < lc && pre - pre == 0.0) ? __double2float_ru(hi) : __int_as_float(0x7f800000);
 }
 
-// The serial fold of one chunk's rows (a chunk that may round), and the anchor after it.
-__device__ __forceinline__ void spec_serial_chunk(const float* __restrict__ xc, int64_t r0, int64_t rows,
-                                                  int64_t stride, double& s, double& lim) {
-  float v[kSpecChunk];
+// The serial fold of chunk rows [r0, r0 + 64) for every lane of the warp with `slow` set (chunks that may round),
+// and the anchor after it. The whole warp loads each such column's chunk, two rows a lane, so its 64 loads are in
+// flight together, and passes the values to the owning lane in row order. col_of(f) is lane f's column base. Every
+// lane of the warp calls this with the same r0.
+template <class ColOf>
+__device__ __forceinline__ void spec_serial_chunks_warp(bool slow, ColOf col_of, int64_t r0, int64_t rows,
+                                                        int64_t stride, double& s, double& lim) {
+  const int lane = threadIdx.x & 31;
+  unsigned m = __ballot_sync(0xffffffffu, slow);
+  while (m) {
+    const int f = __ffs(m) - 1;
+    m &= m - 1;
+    const float* __restrict__ xc = col_of(f);
+    const float a = r0 + lane < rows ? __ldg(xc + (r0 + lane) * stride) : 0.f;
+    const float b = r0 + 32 + lane < rows ? __ldg(xc + (r0 + 32 + lane) * stride) : 0.f;
+    double acc = s;
 #pragma unroll
-  for (int k = 0; k < kSpecChunk; ++k) v[k] = r0 + k < rows ? __ldg(xc + (r0 + k) * stride) : 0.f;
+    for (int k = 0; k < 32; ++k) {
+      const float v = __shfl_sync(0xffffffffu, a, k);
+      if (r0 + k < rows) acc += (double)v;
+    }
 #pragma unroll
-  for (int k = 0; k < kSpecChunk; ++k)
-    if (r0 + k < rows) s += (double)v[k];
-  lim = spec_anchor(s);
+    for (int k = 0; k < 32; ++k) {
+      const float v = __shfl_sync(0xffffffffu, b, k);
+      if (r0 + 32 + k < rows) acc += (double)v;
+    }
+    if (lane == f) {
+      s = acc;
+      lim = spec_anchor(acc);
+    }
+  }
 }
 
 // The form for any row alignment: a CTA takes 32 columns (lane l: column 32·blockIdx.x + l); warps 1..8 summarise
@@ -637,15 +653,14 @@ __global__ void __launch_bounds__(32 * (kSpecProducers + 1), 2)
 #pragma unroll
             for (int k = 0; k < kSpecChunk; ++k) v[k] = (cok && r0 + k < rows) ? __ldg(xc + (r0 + k) * stride) : 0.f;
           }
-          double t[8] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0};
-          float b = 0.f, pre = 0.f, hi = 0.f;
+          double pre = 0.0, hi = 0.0;
           uint32_t mn = 0xffffffffu;
 #pragma unroll
-          for (int k = 0; k < kSpecChunk; ++k) spec_acc(v[k], t[k & 7], b, pre, hi, mn);
+          for (int k = 0; k < kSpecChunk; ++k) spec_acc(v[k], pre, hi, mn);
           double lc;
           float h;
-          spec_finish(b, hi, mn, lc, h);
-          s_t[bb][j][lane] = ((t[0] + t[1]) + (t[2] + t[3])) + ((t[4] + t[5]) + (t[6] + t[7]));
+          spec_finish(pre, hi, mn, lc, h);
+          s_t[bb][j][lane] = pre;
           s_l[bb][j][lane] = lc;
           s_h[bb][j][lane] = h;
         }
@@ -660,15 +675,23 @@ __global__ void __launch_bounds__(32 * (kSpecProducers + 1), 2)
         ok &= fabs(s) + (double)s_h[bb][j][lane] < lim;
         s += s_t[bb][j][lane];
       }
-      if (!ok) {
-        s = s0;
-        lim = l0;
+      if (__any_sync(0xffffffffu, !ok)) {  // the lanes with a failed check walk the segment again
+        if (!ok) {
+          s = s0;
+          lim = l0;
+        }
+        const float* xb0 = x + (int64_t)blockIdx.x * 32;
         for (int j = 0; j < kSpecSeg; ++j) {
-          lim = fmin(lim, s_l[bb][j][lane]);
-          if (fabs(s) + (double)s_h[bb][j][lane] < lim)
-            s += s_t[bb][j][lane];
-          else
-            spec_serial_chunk(xc, ((i - 1) * kSpecSeg + j) * kSpecChunk, rows, stride, s, lim);
+          bool slow = false;
+          if (!ok) {
+            lim = fmin(lim, s_l[bb][j][lane]);
+            if (fabs(s) + (double)s_h[bb][j][lane] < lim)
+              s += s_t[bb][j][lane];
+            else
+              slow = true;
+          }
+          spec_serial_chunks_warp(slow, [&](int f) { return xb0 + f; }, ((i - 1) * kSpecSeg + j) * kSpecChunk, rows,
+                                  stride, s, lim);
         }
       }
     }
@@ -681,14 +704,17 @@ __global__ void __launch_bounds__(32 * (kSpecProducers + 1), 2)
 // per lane): a CTA takes a strip of 128 columns and a cluster of kStripCluster CTAs splits the rows. Chunks go in
 // rounds of kStripCluster · kStripCap; in each round rank k summarises its share of the round's chunks into shared
 // memory (all 8 warps, a lane's 4 columns at once). Then, one column per lane of warps 0..3:
-//  1. each rank adds its own chunks' T in order (SL) and takes the minimum of their L (ML), noting whether every
-//     partial sum of SL stayed below ML (then SL is exact);
+//  1. each rank adds its own chunks' T in order (SL) and takes the minimum of their L (ML), the largest |partial
+//     sum| of SL (MX) and the largest H (HM);
 //  2. rank k starts from the round's carry plus SL of ranks 0..k-1 (read through distributed shared memory), with
-//     lim the minimum of the carry's and their ML, and walks its chunks with the checks;
-//  3. if every check of every rank held and every SL used was exact, each start was the serial fold's own, and
+//     lim the minimum of the carry's and their ML. From a start s, every partial sum of the serial fold over the
+//     rank's rows is at most |s| + MX + HM in magnitude (the partial sums at chunk starts are s + a partial sum of
+//     SL), so if that bound (taken with upward-rounded adds) is below min(lim, ML), no add of the rank's rows
+//     rounds and s + SL is exact: one test for the whole rank. Otherwise the rank walks its chunks with the checks;
+//  3. if every rank's test held and every SL used was exact, each start was the serial fold's own, and
 //     rank kStripCluster-1's result is the next carry. Otherwise the ranks go in order: rank k takes the carry from
-//     rank k-1 and keeps its own result if its speculative start equals that carry bit for bit, else walks again
-//     from the carry (re-reading any chunk that may round).
+//     rank k-1 and keeps its own result if its speculative start equals that carry bit for bit; else it tries the
+//     one test from the carry, and only then walks from the carry (re-reading any chunk that may round).
 constexpr int kStripCols = 128, kStripCluster = 4, kStripCap = 32, kStripWarps = 8, kStripSub = 16;
 constexpr int kStripSmem = kStripCap * kStripCols * (8 + 8 + 4) + 4 * kStripCols * 8 + 16;
 
@@ -713,7 +739,6 @@ __global__ void __cluster_dims__(1, kStripCluster, 1) __launch_bounds__(32 * kSt
   const bool pok = c0 + 4 * lane < cols;  // a producer lane's 4 columns (cols is a multiple of 4)
   const int ccol = 32 * warp + lane;      // a chain lane's column (warps 0..3)
   const bool cok = warp < 4 && c0 + ccol < cols;
-  const float* __restrict__ xq = x + c0 + (cok ? ccol : 0);
   if (threadIdx.x < kStripCols) {
     s_carry[threadIdx.x] = 0.0;
     s_carry[kStripCols + threadIdx.x] = f64_inf();
@@ -729,8 +754,7 @@ __global__ void __cluster_dims__(1, kStripCluster, 1) __launch_bounds__(32 * kSt
     const int me = (int)(g0 + min(nch, (int64_t)(rank + 1) * share) - mb);
     for (int j = warp; j < me; j += kStripWarps) {
       const int64_t r0 = (mb + j) * kSpecChunk;
-      double t[4][2] = {{0.0, 0.0}, {0.0, 0.0}, {0.0, 0.0}, {0.0, 0.0}};
-      float b[4] = {0.f, 0.f, 0.f, 0.f}, pre[4] = {0.f, 0.f, 0.f, 0.f}, hi[4] = {0.f, 0.f, 0.f, 0.f};
+      double pre[4] = {0.0, 0.0, 0.0, 0.0}, hi[4] = {0.0, 0.0, 0.0, 0.0};
       uint32_t mn[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
       for (int sb = 0; sb < kSpecChunk; sb += kStripSub) {
         float4 v[kStripSub];
@@ -742,10 +766,10 @@ __global__ void __cluster_dims__(1, kStripCluster, 1) __launch_bounds__(32 * kSt
         }
 #pragma unroll
         for (int k = 0; k < kStripSub; ++k) {
-          spec_acc(v[k].x, t[0][k & 1], b[0], pre[0], hi[0], mn[0]);
-          spec_acc(v[k].y, t[1][k & 1], b[1], pre[1], hi[1], mn[1]);
-          spec_acc(v[k].z, t[2][k & 1], b[2], pre[2], hi[2], mn[2]);
-          spec_acc(v[k].w, t[3][k & 1], b[3], pre[3], hi[3], mn[3]);
+          spec_acc(v[k].x, pre[0], hi[0], mn[0]);
+          spec_acc(v[k].y, pre[1], hi[1], mn[1]);
+          spec_acc(v[k].z, pre[2], hi[2], mn[2]);
+          spec_acc(v[k].w, pre[3], hi[3], mn[3]);
         }
       }
 #pragma unroll
@@ -753,8 +777,8 @@ __global__ void __cluster_dims__(1, kStripCluster, 1) __launch_bounds__(32 * kSt
         const int at = j * kStripCols + 4 * lane + c;
         double lc;
         float h;
-        spec_finish(b[c], hi[c], mn[c], lc, h);
-        s_t[at] = t[c][0] + t[c][1];
+        spec_finish(pre[c], hi[c], mn[c], lc, h);
+        s_t[at] = pre[c];
         s_l[at] = lc;
         s_h[at] = h;
       }
@@ -762,19 +786,68 @@ __global__ void __cluster_dims__(1, kStripCluster, 1) __launch_bounds__(32 * kSt
     __syncthreads();
     // 1. this rank's SL and ML
     double si = 0.0, li = 0.0, so = 0.0, lo = 0.0;  // the speculative start and result
-    bool exact = true, wok = true;                  // SL exact (or unused); every check of the walk held
+    double sl = 0.0, ml = f64_inf(), mx = 0.0, hm = 0.0;
+    bool exact = true, wok = true;                  // SL exact (or unused); the rank's test or walk held
     if (cok) {
-      double sl = 0.0, ml = f64_inf(), mx = 0.0;
+      float h = 0.f;
 #pragma unroll 4
       for (int j = 0; j < me; ++j) {
         ml = fmin(ml, s_l[j * kStripCols + ccol]);
+        h = fmaxf(h, s_h[j * kStripCols + ccol]);
         sl += s_t[j * kStripCols + ccol];
         mx = fmax(mx, fabs(sl));
       }
+      hm = (double)h;
       s_part[ccol] = sl;
       s_part[kStripCols + ccol] = ml;
       exact = rank == kStripCluster - 1 || mx < ml;  // SL is used by later ranks only
     }
+    // the whole rank from start s without a rounding add (see 2. above)
+    auto rank_exact = [&](double s, double lim) {
+      return __dadd_ru(__dadd_ru(fabs(s), mx), hm) < fmin(lim, ml);
+    };
+    // The chunk-by-chunk walk from (s, lim) for lanes with `act`, 8 chunks at a time without branches; with FOLD,
+    // a block with a failed check is walked again chunk by chunk and folds the chunks that may round. Every lane of
+    // the warp calls it. Returns whether every check held.
+    auto walk = [&](double& s, double& lim, bool act, bool fold) {
+      bool good = true;
+      const float* xw = x + c0 + 32 * warp;
+      for (int j0 = 0; j0 < me; j0 += 8) {
+        double s1 = s, l1 = lim;
+        bool okb = true;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (j0 + u < me) {
+            const int at = (j0 + u) * kStripCols + ccol;
+            l1 = fmin(l1, s_l[at]);
+            okb &= fabs(s1) + (double)s_h[at] < l1;
+            s1 += s_t[at];
+          }
+        }
+        if (act && (okb || !fold)) {
+          s = s1;
+          lim = l1;
+        }
+        good &= okb;
+        const bool redo = fold && act && !okb;
+        if (__any_sync(0xffffffffu, redo)) {
+          for (int u = 0; u < 8 && j0 + u < me; ++u) {
+            bool slow = false;
+            if (redo) {
+              const int at = (j0 + u) * kStripCols + ccol;
+              lim = fmin(lim, s_l[at]);
+              if (fabs(s) + (double)s_h[at] < lim)
+                s += s_t[at];
+              else
+                slow = true;
+            }
+            spec_serial_chunks_warp(slow, [&](int f) { return xw + f; }, (mb + j0 + u) * kSpecChunk, rows, stride, s,
+                                    lim);
+          }
+        }
+      }
+      return good;
+    };
     cluster.sync();
     // 2. the speculative start and the checked walk
     if (cok) {
@@ -787,14 +860,24 @@ __global__ void __cluster_dims__(1, kStripCluster, 1) __launch_bounds__(32 * kSt
       }
       si = s;
       li = lim;
-#pragma unroll 4
-      for (int j = 0; j < me; ++j) {
-        lim = fmin(lim, s_l[j * kStripCols + ccol]);
-        wok &= fabs(s) + (double)s_h[j * kStripCols + ccol] < lim;
-        s += s_t[j * kStripCols + ccol];
+      const bool whole = rank_exact(s, lim);
+      if (whole) {
+        s += sl;
+        lim = fmin(lim, ml);
       }
       so = s;
       lo = lim;
+      wok = whole;
+    }
+    if (warp < 4 && __any_sync(0xffffffffu, cok && !wok)) {
+      const bool act = cok && !wok;
+      double s = si, lim = li;
+      const bool good = walk(s, lim, act, false);
+      if (act) {
+        so = s;
+        lo = lim;
+        wok = good;
+      }
     }
     const int fail = __syncthreads_or(cok && !(exact && wok));
     if (threadIdx.x == 0) *s_fail = fail;
@@ -811,23 +894,29 @@ __global__ void __cluster_dims__(1, kStripCluster, 1) __launch_bounds__(32 * kSt
       cluster.sync();
     } else {
       for (int p = 0; p < kStripCluster; ++p) {
-        if (rank == p && cok) {
+        if (rank == p && warp < 4) {
           double s = s_carry[ccol], lim = s_carry[kStripCols + ccol];
-          if (!(wok && __double_as_longlong(s) == __double_as_longlong(si) &&
-                __double_as_longlong(lim) == __double_as_longlong(li))) {
-            for (int j = 0; j < me; ++j) {
-              lim = fmin(lim, s_l[j * kStripCols + ccol]);
-              if (fabs(s) + (double)s_h[j * kStripCols + ccol] < lim)
-                s += s_t[j * kStripCols + ccol];
-              else
-                spec_serial_chunk(xq, (mb + j) * kSpecChunk, rows, stride, s, lim);
-            }
-            so = s;
-            lo = lim;
+          // a lane whose speculative start was the carry keeps its result; the others take the rank's test from the
+          // carry, and walk from it if that fails
+          bool again = cok && !(wok && __double_as_longlong(s) == __double_as_longlong(si) &&
+                                __double_as_longlong(lim) == __double_as_longlong(li));
+          if (again && rank_exact(s, lim)) {
+            so = s + sl;
+            lo = fmin(lim, ml);
+            again = false;
           }
-          double* dst = cluster.map_shared_rank(s_carry, (p + 1) % kStripCluster);
-          dst[ccol] = so;
-          dst[kStripCols + ccol] = lo;
+          if (__any_sync(0xffffffffu, again)) {
+            walk(s, lim, again, true);
+            if (again) {
+              so = s;
+              lo = lim;
+            }
+          }
+          if (cok) {
+            double* dst = cluster.map_shared_rank(s_carry, (p + 1) % kStripCluster);
+            dst[ccol] = so;
+            dst[kStripCols + ccol] = lo;
+          }
         }
         cluster.sync();  // the hand-off is visible before the next rank reads it
       }
