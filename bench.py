@@ -239,9 +239,9 @@ def bench_lifts(ctx, K, W, hbm, bf16):
     record("colmax_f32_8192x8192", wl.rowsum_bytes(), ms, "col_extremum_f32_vec_kernel", R)
     ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xs[i % R], "sum", 0, block=256, out=out), K, W)
     record("colsum_f32_documented_B256", wl.rowsum_bytes(), ms, "col_sum_f32_doc_vec4_kernel", R)
-    # the serial order per column (block 1, the default): bound by the chain of 8192 dependent f64 adds
+    # the serial order per column (block 1, the default): runs of rows added out of order where no add can round
     ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xs[i % R], "sum", 0, out=out), K, W)
-    record("colsum_f32_serial", wl.rowsum_bytes(), ms, "col_sum_f32_serial_kernel", R)
+    record("colsum_f32_serial", wl.rowsum_bytes(), ms, "col_sum_f32_serial_strip_kernel", R)
     # its split-K variant (64 row chunks of f64 partials, added in chunk order): the parallel association
     L = _lib.load()
     ws = torch.empty(L.up_sm100_col_sum_splitk_workspace_bytes(8192, 8192, 64), dtype=torch.uint8,
@@ -625,6 +625,12 @@ def profile_cases(which: str):
         o = torch.empty(x.shape[1], device=dev)
         return lambda: ops.reduce2d(x, "sum", 0, block=256, out=o)
 
+    @case("colsum_serial")
+    def _():
+        x = wl.rowsum_input(device=dev)
+        o = torch.empty(x.shape[1], device=dev)
+        return lambda: ops.reduce2d(x, "sum", 0, out=o)
+
     @case("argmax")
     def _():
         x = wl.argmax_input(rows=8192, device=dev)
@@ -666,7 +672,7 @@ def main():
     ap.add_argument("--lifts", default="all", choices=["all", "none"])
     ap.add_argument("--profile", default=None,
                     help="run only the small ncu cases of these lifts, comma-separated (scan, rowsum, rowsum_auto, "
-                         "rowmax_f32, colmax_f32, colsum_doc, im2col, row_softmax, row_rms_norm, window, window_mid, argmax, gather, dequant, w4a16, all)")
+                         "rowmax_f32, colmax_f32, colsum_doc, colsum_serial, im2col, row_softmax, row_rms_norm, window, window_mid, argmax, gather, dequant, w4a16, all)")
     args = ap.parse_args()
     if args.profile:
         profile_cases(args.profile)
