@@ -50,6 +50,79 @@ def test_auto_sum_matches_golden_documented_order():
     assert ops.row_sum(x, accum="auto", block=1).cpu().numpy().view(np.uint32).tolist() == g["serial_f32_bits"]
 
 
+def _serial_rows(rng, rows, cols):
+    """Rows for the serial-order row sum (block 1), one kind per row in turn: N(0,1) and U[0,1) (chunks stay
+    exact), a few values near 2^-40 among N(0,1) ones, ones with tiny and large values (partial sums at full
+    precision that cross binades), exponents over 40 binades, subnormals beside normals, NaN/±Inf/±0 specials, and
+    all -0 (the sum is +0)."""
+    out = np.empty((rows, cols), np.float32)
+    for r in range(rows):
+        k = r % 8
+        if k == 0:
+            v = rng.standard_normal(cols)
+        elif k == 1:
+            v = rng.random(cols)
+        elif k == 2:
+            v = rng.standard_normal(cols)
+            v[rng.random(cols) < 0.01] = rng.choice([2.0 ** -40, -3.0 * 2.0 ** -45, 2.0 ** -30], 1)[0]
+        elif k == 3:
+            v = np.where(rng.random(cols) < 0.7, 1.0, rng.choice([2.0 ** -28, 2.0 ** -52, 3.0 * 2.0 ** 24], cols))
+        elif k == 4:
+            v = (rng.random(cols) - 0.5) * 2.0 ** rng.integers(-20, 20, cols)
+        elif k == 5:
+            v = rng.standard_normal(cols) * np.where(rng.random(cols) < 0.5, 2.0 ** -135, 1.0)
+        elif k == 6:
+            v = rng.standard_normal(cols).astype(np.float32)
+            pick = rng.random(cols)
+            v[pick < 0.02] = 0.0
+            v[(pick >= 0.02) & (pick < 0.04)] = -0.0
+            v[(pick >= 0.04) & (pick < 0.045)] = np.inf
+            v[(pick >= 0.045) & (pick < 0.05)] = -np.inf
+            nan_at = pick > 0.995
+            vb = v.view(np.uint32)
+            vb[nan_at] = (rng.integers(1, 1 << 22, cols).astype(np.uint32) | np.uint32(0x7f800000))[nan_at]
+        else:
+            v = np.full(cols, -0.0)
+        out[r] = v if v.dtype == np.float32 else v.astype(np.float32)
+    return out
+
+
+def _same_or_both_nan(got, want):
+    nan = np.isnan(want)
+    assert np.array_equal(np.isnan(got), nan)
+    assert np.array_equal(got.view(np.uint32)[~nan], want.view(np.uint32)[~nan])
+
+
+@pytest.mark.parametrize("rows,cols", [(8, 1), (8, 63), (8, 64), (16, 65), (16, 2047), (16, 2048), (16, 2049),
+                                       (24, 8192), (9, 20000), (3, 100003)])
+def test_auto_sum_serial_order_exact_and_rounding_chunks(rows, cols):
+    """Block 1 (the serial order) bit for bit against the oracle's serial fold, on rows whose chunks are added out
+    of order (no add rounds) and rows that round and take the value-by-value fold, at lengths on both sides of the
+    64-value chunk and the 2,048-value segment; Sum and Mean; a view one column in (unaligned rows) as well."""
+    rng = np.random.default_rng(rows * 11 + cols)
+    xn = _serial_rows(rng, rows, cols)
+    wide = np.zeros((rows, cols + 3), np.float32)
+    wide[:, 1:1 + cols] = xn
+    wt = torch.from_numpy(wide).cuda()
+    for x in (torch.from_numpy(xn).cuda(), wt[:, 1:1 + cols]):
+        _same_or_both_nan(ops.row_sum(x, accum="auto", block=1).cpu().numpy(), orc.row_sum_f32(xn))
+        _same_or_both_nan(ops.reduce2d(x, "mean", 1, block=1).cpu().numpy(), orc.reduce2d_f32(xn, "mean", 1))
+
+
+@pytest.mark.parametrize("dist", ["normal", "uniform", "ones_and_tiny"])
+def test_auto_sum_serial_order_full_rows(dist):
+    """8,192 rows of 8,192: N(0,1), U[0,1) and unit values with a tiny one in every 50, bit for bit."""
+    rng = np.random.default_rng(6)
+    if dist == "normal":
+        xn = rng.standard_normal((8192, 8192), dtype=np.float32)
+    elif dist == "uniform":
+        xn = rng.random((8192, 8192), dtype=np.float32)
+    else:
+        xn = np.where(rng.random((8192, 8192)) < 0.02, np.float32(2.0 ** -35), np.float32(1.0)).astype(np.float32)
+    got = ops.row_sum(torch.from_numpy(xn).cuda(), accum="auto", block=1).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), orc.row_sum_f32(xn, orc.max_threads()).view(np.uint32))
+
+
 @pytest.mark.parametrize("rows,cols", [(1, 1), (3, 7), (17, 96), (5, 1000), (64, 4097), (33, 8192)])
 @pytest.mark.parametrize("block", [1, 2, 4, 32, 128, 256, 1024])
 def test_auto_sum_bit_exact_vs_oracle(rows, cols, block):

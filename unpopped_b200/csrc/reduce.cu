@@ -5,6 +5,9 @@
 // oracle/plan_contract.rs:146-245). All kernels are HBM-streaming: 128-bit loads through the read-only
 // path with no L1 allocation, fixed-order warp/block combines, one CTA per row.
 #include "common.cuh"
+#include "spec.cuh"
+
+#include <algorithm>
 
 #include <cuda_bf16.h>
 
@@ -126,6 +129,96 @@ __global__ void row_sum_auto_kernel(const float* __restrict__ x, int64_t rows, i
     // Mean divides the f64 total by the extent before the one rounding (block_reduce.rs:13-23)
     if (lr < rpc && p == 0 && r < rows) out[r] = __double2float_rn(mean ? s[0] / (double)cols : s[0]);
     __syncthreads();
+  }
+}
+
+// ===================================================================================================
+// Row sum, UP_ACCUM_AUTO at block 1: the serial order, which is the plan oracle's fold (plan_eval.rs:566-645),
+// s = ((0 + x0) + x1) + ... in f64 with one rounding, by the chunk rule of spec.cuh. A warp takes a row, 32 chunks
+// (2,048 values) at a time, lane l summarising chunk l from contiguous loads. If |s| plus the sum of the segment's
+// H (both sums rounded up) is below min(lim, the smallest L of the segment), every partial sum of the fold over the
+// segment (at most |s| + the H of the chunks so far) is exact, and s += the warp sum of its T (exact in any order).
+// Otherwise the warp walks the segment's chunks in order, each lane's summary passed by shuffles, and folds the
+// chunks that may round value by value (the warp loads the chunk, two values a lane, and adds them in order). s
+// and lim are the same in every lane of the warp.
+// ===================================================================================================
+template <bool MEAN, bool VEC>
+__global__ void __launch_bounds__(256) row_sum_serial_spec_kernel(const float* __restrict__ x, int64_t rows,
+                                                                  int64_t cols, int64_t stride,
+                                                                  float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t w0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = w0; r < rows; r += nw) {
+    const float* __restrict__ row = x + r * stride;
+    double s = 0.0, lim = f64_inf();
+    for (int64_t c0 = 0; c0 < cols; c0 += 32 * kSpecChunk) {
+      const int64_t cb = c0 + (int64_t)kSpecChunk * lane;
+      double pre = 0.0, hi = 0.0;
+      uint32_t mn = 0xffffffffu;
+      if (VEC && cb + kSpecChunk <= cols) {
+        float4 v[kSpecChunk / 4];
+#pragma unroll
+        for (int k = 0; k < kSpecChunk / 4; ++k) v[k] = ld_nc_na_f4(row + cb + 4 * k);
+#pragma unroll
+        for (int k = 0; k < kSpecChunk / 4; ++k) {
+          spec_acc(v[k].x, pre, hi, mn);
+          spec_acc(v[k].y, pre, hi, mn);
+          spec_acc(v[k].z, pre, hi, mn);
+          spec_acc(v[k].w, pre, hi, mn);
+        }
+      } else {
+        float v[kSpecChunk];
+#pragma unroll
+        for (int k = 0; k < kSpecChunk; ++k) v[k] = cb + k < cols ? __ldg(row + cb + k) : 0.f;
+#pragma unroll
+        for (int k = 0; k < kSpecChunk; ++k) spec_acc(v[k], pre, hi, mn);
+      }
+      double lc;
+      float h;
+      spec_finish(pre, hi, mn, lc, h);
+      double hs = (double)h, ml = lc, ts = pre;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        hs = __dadd_ru(hs, __shfl_xor_sync(0xffffffffu, hs, o));
+        ml = fmin(ml, __shfl_xor_sync(0xffffffffu, ml, o));
+        ts += __shfl_xor_sync(0xffffffffu, ts, o);
+      }
+      hs = __shfl_sync(0xffffffffu, hs, 0);  // lane 0's values decide for the whole warp
+      ml = __shfl_sync(0xffffffffu, ml, 0);
+      ts = __shfl_sync(0xffffffffu, ts, 0);
+      const double l2 = fmin(lim, ml);
+      if (__dadd_ru(fabs(s), hs) < l2) {
+        s += ts;
+        lim = l2;
+      } else {
+        const int nch = (int)min((int64_t)32, (cols - c0 + kSpecChunk - 1) / kSpecChunk);
+        for (int j = 0; j < nch; ++j) {
+          const double tj = __shfl_sync(0xffffffffu, pre, j), lj = __shfl_sync(0xffffffffu, lc, j);
+          const float hj = __shfl_sync(0xffffffffu, h, j);
+          lim = fmin(lim, lj);
+          if (fabs(s) + (double)hj < lim) {
+            s += tj;
+          } else {
+            const int64_t rb = c0 + (int64_t)kSpecChunk * j;
+            const float a = rb + lane < cols ? __ldg(row + rb + lane) : 0.f;
+            const float b = rb + 32 + lane < cols ? __ldg(row + rb + 32 + lane) : 0.f;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+              const float v = __shfl_sync(0xffffffffu, a, k);
+              if (rb + k < cols) s += (double)v;
+            }
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+              const float v = __shfl_sync(0xffffffffu, b, k);
+              if (rb + 32 + k < cols) s += (double)v;
+            }
+            lim = spec_anchor(s);
+          }
+        }
+      }
+    }
+    if (lane == 0) out[r] = __double2float_rn(MEAN ? s / (double)cols : s);
   }
 }
 
@@ -349,7 +442,15 @@ static int launch_row_sum_auto(const float* x, int64_t rows, int64_t cols, int64
                                float* out, cudaStream_t s) {
   if (block < 1 || block > 1024 || (block & (block - 1)) != 0) return UP_ERR_UNSUPPORTED;
   const bool vec = aligned(x, 16) && (cols % 4 == 0) && (row_stride % 4 == 0);
-  if (vec && block >= 4) {
+  if (block == 1) {  // the serial order: a warp per row
+    const int64_t g = std::min<int64_t>((rows + 7) / 8, (int64_t)sm_count() * 16);
+    if (vec)
+      mean ? row_sum_serial_spec_kernel<true, true><<<(int)g, 256, 0, s>>>(x, rows, cols, row_stride, out)
+           : row_sum_serial_spec_kernel<false, true><<<(int)g, 256, 0, s>>>(x, rows, cols, row_stride, out);
+    else
+      mean ? row_sum_serial_spec_kernel<true, false><<<(int)g, 256, 0, s>>>(x, rows, cols, row_stride, out)
+           : row_sum_serial_spec_kernel<false, false><<<(int)g, 256, 0, s>>>(x, rows, cols, row_stride, out);
+  } else if (vec && block >= 4) {
     const int P = block / 4, threads = 256, rpc = threads / P;
     const int64_t g = (rows + rpc - 1) / rpc;
     const size_t smem = (size_t)rpc * block * sizeof(double);

@@ -16,6 +16,7 @@
 //    runs of values out of order only where no add of the serial fold can round); Mean divides by the row count,
 //    so an empty Mean is 0/0.
 #include "common.cuh"
+#include "spec.cuh"
 
 #include <cooperative_groups.h>
 #include <mutex>
@@ -556,36 +557,6 @@ __global__ void __cluster_dims__(1, kColCluster, 1) __launch_bounds__(32 * kColV
 //    too (NaN payloads propagate as they do there).
 // On N(0,1) data about 0.002 % of chunks take the serial fold and on U[0,1) about 0.04 %; on data whose exponents
 // spread over 30 binades or more nearly all do, and the kernels then run at about the speed of the plain fold.
-constexpr int kSpecChunk = 64;
-
-__device__ __forceinline__ double pow2_biased(uint32_t e) { return __longlong_as_double((long long)e << 52); }
-__device__ __forceinline__ double f64_inf() { return __longlong_as_double(0x7ff0000000000000ll); }
-
-// 2^(lowbit(s) + 53) for a finite nonzero s, +inf otherwise.
-__device__ __forceinline__ double spec_anchor(double s) {
-  const uint64_t u = (uint64_t)__double_as_longlong(s);
-  const uint32_t ex = (uint32_t)(u >> 52) & 0x7ffu;
-  const uint64_t m = u & ((1ull << 52) - 1);
-  if ((u << 1) == 0 || ex == 0x7ffu) return f64_inf();
-  const uint64_t sig = ex ? (m | (1ull << 52)) : m;
-  const uint32_t le = (ex ? ex : 1u) + (uint32_t)(__ffsll((long long)sig) - 1) + 1u;
-  return pow2_biased(le < 2046u ? le : 2046u);
-}
-
-// One value into a chunk summary. mn keeps the minimum of (bits << 1) - 2: the sign drops out, and both zeros wrap
-// to the top so they never count.
-__device__ __forceinline__ void spec_acc(float v, double& pre, double& hi, uint32_t& mn) {
-  pre += (double)v;
-  hi = fmax(hi, fabs(pre));
-  mn = min(mn, (__float_as_uint(v) << 1) - 2u);
-}
-
-// L and H of a chunk from its accumulators (T is the prefix itself).
-__device__ __forceinline__ void spec_finish(double pre, double hi, uint32_t mn, double& lc, float& h) {
-  lc = mn >= 0xfffffffeu ? f64_inf() : pow2_biased(max((mn + 2u) >> 24, 1u) + 926u);
-  h = (hi < lc && pre - pre == 0.0) ? __double2float_ru(hi) : __int_as_float(0x7f800000);
-}
-
 // The serial fold of chunk rows [r0, r0 + 64) for every lane of the warp with `slow` set (chunks that may round),
 // and the anchor after it. The whole warp loads each such column's chunk, two rows a lane, so its 64 loads are in
 // flight together, and passes the values to the owning lane in row order. col_of(f) is lane f's column base. Every
