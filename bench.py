@@ -232,6 +232,9 @@ def bench_lifts(ctx, K, W, hbm, bf16):
     record("rowsum_f32_8192x8192", wl.rowsum_bytes(), ms, "row_sum_f32_kernel", R)
     ms, _, _ = ctx.timed(lambda i, kin: ops.row_sum(xs[i % R], "auto", 1024, out=out), K, W)
     record("rowsum_f32_auto_f64order_B1024", wl.rowsum_bytes(), ms, "row_sum_auto_kernel", R)
+    # block 1, the serial order: runs of values added out of order where no add can round
+    ms, _, _ = ctx.timed(lambda i, kin: ops.row_sum(xs[i % R], "auto", 1, out=out), K, W)
+    record("rowsum_f32_serial", wl.rowsum_bytes(), ms, "row_sum_serial_spec_kernel", R)
     # the reduction breadth on the same input: f32 Max over the last axis, and Max over the outer axis
     ms, _, _ = ctx.timed(lambda i, kin: ops.reduce2d(xs[i % R], "max", 1, out=out), K, W)
     record("rowmax_f32_8192x8192", wl.rowsum_bytes(), ms, "row_extremum_f32_kernel", R)
