@@ -628,6 +628,12 @@ def profile_cases(which: str):
         o = torch.empty(x.shape[1], device=dev)
         return lambda: ops.reduce2d(x, "sum", 0, block=256, out=o)
 
+    @case("rowsum_serial")
+    def _():
+        x = wl.rowsum_input(device=dev)
+        o = torch.empty(x.shape[0], device=dev)
+        return lambda: ops.row_sum(x, "auto", 1, out=o)
+
     @case("colsum_serial")
     def _():
         x = wl.rowsum_input(device=dev)
@@ -675,7 +681,7 @@ def main():
     ap.add_argument("--lifts", default="all", choices=["all", "none"])
     ap.add_argument("--profile", default=None,
                     help="run only the small ncu cases of these lifts, comma-separated (scan, rowsum, rowsum_auto, "
-                         "rowmax_f32, colmax_f32, colsum_doc, colsum_serial, im2col, row_softmax, row_rms_norm, window, window_mid, argmax, gather, dequant, w4a16, all)")
+                         "rowsum_serial, rowmax_f32, colmax_f32, colsum_doc, colsum_serial, im2col, row_softmax, row_rms_norm, window, window_mid, argmax, gather, dequant, w4a16, all)")
     args = ap.parse_args()
     if args.profile:
         profile_cases(args.profile)
