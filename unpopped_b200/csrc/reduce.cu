@@ -140,10 +140,11 @@ __global__ void row_sum_auto_kernel(const float* __restrict__ x, int64_t rows, i
 // segment (at most |s| + the H of the chunks so far) is exact, and s += the warp sum of its T (exact in any order).
 // Otherwise the warp walks the segment's chunks in order, each lane's summary passed by shuffles, and folds the
 // chunks that may round value by value (the warp loads the chunk, two values a lane, and adds them in order). s
-// and lim are the same in every lane of the warp.
+// and lim are the same in every lane of the warp. A float4 lane loads its chunk in two halves, which fits three CTAs
+// an SM (79 registers) and keeps more warps' loads in flight.
 // ===================================================================================================
 template <bool MEAN, bool VEC>
-__global__ void __launch_bounds__(256) row_sum_serial_spec_kernel(const float* __restrict__ x, int64_t rows,
+__global__ void __launch_bounds__(256, VEC ? 3 : 2) row_sum_serial_spec_kernel(const float* __restrict__ x, int64_t rows,
                                                                   int64_t cols, int64_t stride,
                                                                   float* __restrict__ out) {
   const int lane = threadIdx.x & 31;
@@ -157,15 +158,18 @@ __global__ void __launch_bounds__(256) row_sum_serial_spec_kernel(const float* _
       double pre = 0.0, hi = 0.0;
       uint32_t mn = 0xffffffffu;
       if (VEC && cb + kSpecChunk <= cols) {
-        float4 v[kSpecChunk / 4];
+#pragma unroll 1
+        for (int h0 = 0; h0 < kSpecChunk / 4; h0 += 8) {  // two halves of 8 float4
+          float4 v[8];
 #pragma unroll
-        for (int k = 0; k < kSpecChunk / 4; ++k) v[k] = ld_nc_na_f4(row + cb + 4 * k);
+          for (int k = 0; k < 8; ++k) v[k] = ld_nc_na_f4(row + cb + 4 * (h0 + k));
 #pragma unroll
-        for (int k = 0; k < kSpecChunk / 4; ++k) {
-          spec_acc(v[k].x, pre, hi, mn);
-          spec_acc(v[k].y, pre, hi, mn);
-          spec_acc(v[k].z, pre, hi, mn);
-          spec_acc(v[k].w, pre, hi, mn);
+          for (int k = 0; k < 8; ++k) {
+            spec_acc(v[k].x, pre, hi, mn);
+            spec_acc(v[k].y, pre, hi, mn);
+            spec_acc(v[k].z, pre, hi, mn);
+            spec_acc(v[k].w, pre, hi, mn);
+          }
         }
       } else {
         float v[kSpecChunk];
