@@ -1,0 +1,129 @@
+"""CPU check of the chunk rule behind the serial-order Sum kernels (unpopped_b200/csrc/spec.cuh).
+
+A numpy restatement of the row kernel's decisions must give the plain serial f64 fold's bits
+(oracle/plan_eval.rs:566-645: s = ((0 + x0) + x1) + ..., one rounding) on data built to stress it. The row kernel
+works in segments of 32 chunks of 64 values, with one test per segment from the running sum and a chunk-by-chunk
+walk with value-by-value folds where the test fails. Here the segment test uses exact rational arithmetic, the
+weakest bound the rule allows (the kernel's upward-rounded sums pass less often). This tests the rule, not the CUDA
+code; the GPU tests compare the kernels with the oracle.
+"""
+import math
+from fractions import Fraction
+
+import numpy as np
+import pytest
+
+CHUNK = 64
+SEGMENT = 32 * CHUNK
+
+
+def _summary(v):
+    """(T, H, L) of one chunk: the f64 prefix sum in fold order, its largest magnitude rounded up to f32 (+inf
+    unless it is below L and T is finite), and 2^(q + 53) for q the smallest ulp exponent of the nonzero values."""
+    pre = np.cumsum(np.concatenate(([0.0], v.astype(np.float64))))[1:]  # the fold's own partial sums from +0
+    t = float(pre[-1])
+    hi = float(np.max(np.abs(pre)))
+    bits = v.view(np.uint32)
+    nz = bits[(bits & 0x7FFFFFFF) != 0]
+    if nz.size == 0:
+        lim = math.inf
+    else:
+        e = max(int(((nz >> 23) & 0xFF).min()), 1)
+        lim = 2.0 ** (e - 150 + 53)
+    if hi < lim and math.isfinite(t):
+        h = np.float32(hi)
+        if float(h) < hi:
+            h = np.nextafter(h, np.float32(np.inf))
+        h = float(h)
+    else:
+        h = math.inf
+    return t, h, lim
+
+
+def _anchor(s):
+    """2^(lowbit(s) + 53) for a finite nonzero s, +inf otherwise."""
+    if s == 0.0 or not math.isfinite(s):
+        return math.inf
+    m, e = math.frexp(s)
+    mant = int(abs(m) * 2.0 ** 53)
+    tz = (mant & -mant).bit_length() - 1
+    return 2.0 ** min(e - 53 + tz + 53, 1023)
+
+
+def _spec_row(v, counts):
+    s, lim = 0.0, math.inf
+    n = v.size
+    for c0 in range(0, n, SEGMENT):
+        chunks = [v[c0 + j:min(c0 + j + CHUNK, n)] for j in range(0, SEGMENT, CHUNK) if c0 + j < n]
+        summ = [_summary(c) for c in chunks]
+        l2 = min([lim] + [x[2] for x in summ])
+        ok = math.isfinite(s) and all(math.isfinite(x[1]) for x in summ)
+        if ok and math.isfinite(l2):
+            ok = Fraction(abs(s)) + sum(Fraction(x[1]) for x in summ) < Fraction(l2)
+        if ok:
+            ts = float(np.sum(np.array([x[0] for x in summ])))  # pairwise: any order is exact here
+            s += ts
+            lim = l2
+            counts["segments"] += 1
+            continue
+        for (t, h, lc), c in zip(summ, chunks):
+            lim = min(lim, lc)
+            if abs(s) + h < lim:
+                s += t
+            else:
+                for x in c:
+                    s += float(x)
+                lim = _anchor(s)
+                counts["folds"] += 1
+    return s
+
+
+def _rows(rng, kind, n):
+    if kind == "normal":
+        return rng.standard_normal(n)
+    if kind == "uniform":
+        return rng.random(n)
+    if kind == "tiny":
+        v = rng.standard_normal(n)
+        v[rng.random(n) < 0.01] = rng.choice([2.0 ** -40, -3.0 * 2.0 ** -45, 2.0 ** -30], 1)[0]
+        return v
+    if kind == "binades":
+        return np.where(rng.random(n) < 0.7, 1.0, rng.choice([2.0 ** -28, 2.0 ** -52, 3.0 * 2.0 ** 24], n))
+    if kind == "spread":
+        return (rng.random(n) - 0.5) * 2.0 ** rng.integers(-20, 20, n)
+    if kind == "subnormal":
+        return rng.standard_normal(n) * np.where(rng.random(n) < 0.5, 2.0 ** -135, 1.0)
+    if kind == "zeros":
+        return np.where(rng.random(n) < 0.5, -0.0, 0.0)
+    v = rng.standard_normal(n).astype(np.float32)  # specials
+    pick = rng.random(n)
+    v[pick < 0.02] = 0.0
+    v[(pick >= 0.02) & (pick < 0.04)] = -0.0
+    v[(pick >= 0.04) & (pick < 0.042)] = np.inf
+    v[(pick >= 0.042) & (pick < 0.044)] = -np.inf
+    v.view(np.uint32)[pick > 0.998] = np.uint32(0x7FC00001)
+    return v
+
+
+KINDS = ["normal", "uniform", "tiny", "binades", "spread", "subnormal", "zeros", "specials"]
+
+
+@pytest.mark.parametrize("kind", KINDS)
+def test_chunk_rule_gives_the_serial_fold(kind):
+    rng = np.random.default_rng(KINDS.index(kind) + 40)
+    counts = {"segments": 0, "folds": 0}
+    for n in (1, 63, 64, 65, 2047, 2048, 2049, 9000):
+        for _ in range(6):
+            v = np.ascontiguousarray(_rows(rng, kind, n), dtype=np.float32)
+            with np.errstate(invalid="ignore"):  # inf - inf in the specials rows is part of the fold
+                want = float(np.cumsum(np.concatenate(([0.0], v.astype(np.float64))))[-1])  # from +0, as the fold
+                got = _spec_row(v, counts)
+            if math.isnan(want):
+                assert math.isnan(got), (kind, n)
+            else:
+                assert np.float64(got).tobytes() == np.float64(want).tobytes(), (kind, n, got, want)
+    # the data reaches the branch it was built for
+    if kind in ("normal", "uniform", "zeros"):
+        assert counts["segments"] > 0
+    if kind in ("tiny", "binades", "spread", "specials"):
+        assert counts["folds"] > 0
