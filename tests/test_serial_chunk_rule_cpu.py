@@ -127,3 +127,101 @@ def test_chunk_rule_gives_the_serial_fold(kind):
         assert counts["segments"] > 0
     if kind in ("tiny", "binades", "spread", "specials"):
         assert counts["folds"] > 0
+
+
+def _walk(s, lim, chunks, summ, counts):
+    """The chain over chunks in order from (s, lim): add T where |s| + H < lim, else fold the chunk's values."""
+    for (t, h, lc), c in zip(summ, chunks):
+        lim = min(lim, lc)
+        if abs(s) + h < lim:
+            s += t
+        else:
+            for x in c:
+                s += float(x)
+            lim = _anchor(s)
+            counts["folds"] += 1
+    return s, lim
+
+
+def _rank_exact(s, lim, part):
+    """One test for a whole rank from start s: |s| + MX + HM below min(lim, ML), in exact rationals."""
+    sl, ml, mx, hm = part
+    if not (math.isfinite(s) and math.isfinite(mx) and math.isfinite(hm)):
+        return False
+    bound = min(lim, ml)
+    return math.isinf(bound) or Fraction(abs(s)) + Fraction(mx) + Fraction(hm) < Fraction(bound)
+
+
+def _spec_column(v, counts, ranks=4, cap=32):
+    """The cluster column kernel's round protocol for one column: each round's chunks split over `ranks`; each
+    rank's SL (its T added in order), ML, MX (largest |partial| of SL) and HM (largest H); speculative starts from
+    the carry plus SL of earlier ranks; if every rank's one test holds and every SL used is exact, the last rank's
+    result carries, else the ranks go in order, keeping a result whose speculative start was the carry."""
+    n = v.size
+    chunks = [v[i:min(i + CHUNK, n)] for i in range(0, n, CHUNK)]
+    summ = [_summary(c) for c in chunks]
+    s, lim = 0.0, math.inf
+    per_round = ranks * cap
+    for g0 in range(0, len(chunks), per_round):
+        nch = min(per_round, len(chunks) - g0)
+        share = -(-nch // ranks)
+        spans = [(g0 + min(nch, k * share), g0 + min(nch, (k + 1) * share)) for k in range(ranks)]
+        parts = []
+        for a, b in spans:
+            sl, ml, mx, hm = 0.0, math.inf, 0.0, 0.0
+            for t, h, lc in summ[a:b]:
+                ml = min(ml, lc)
+                hm = max(hm, h)
+                sl += t
+                mx = max(mx, abs(sl))  # a NaN partial is dropped, as fmax drops it
+            parts.append((sl, ml, mx, hm))
+        spec = []  # per rank: start, start lim, result, result lim, walk held, SL exact
+        for k, (a, b) in enumerate(spans):
+            si, li = s, lim
+            for q in range(k):
+                si += parts[q][0]
+                li = min(li, parts[q][1])
+            if _rank_exact(si, li, parts[k]):
+                so, lo, wok = si + parts[k][0], min(li, parts[k][1]), True
+            else:
+                so, lo, wok = si, li, True
+                for t, h, lc in summ[a:b]:
+                    lo = min(lo, lc)
+                    wok &= abs(so) + h < lo
+                    so += t
+            exact = k == ranks - 1 or parts[k][2] < parts[k][1]
+            spec.append((si, li, so, lo, wok, exact))
+        if all(w and e for (_, _, _, _, w, e) in spec):
+            s, lim = spec[-1][2], spec[-1][3]
+            counts["segments"] += 1
+            continue
+        for k, (a, b) in enumerate(spans):  # rank order from the true carry
+            si, li, so, lo, wok, _ = spec[k]
+            same = wok and np.float64(s).tobytes() == np.float64(si).tobytes() and lim == li
+            if same:
+                s, lim = so, lo
+            elif _rank_exact(s, lim, parts[k]):
+                s, lim = s + parts[k][0], min(lim, parts[k][1])
+            else:
+                s, lim = _walk(s, lim, chunks[a:b], summ[a:b], counts)
+    return s
+
+
+@pytest.mark.parametrize("kind", KINDS)
+def test_cluster_round_protocol_gives_the_serial_fold(kind):
+    rng = np.random.default_rng(KINDS.index(kind) + 80)
+    counts = {"segments": 0, "folds": 0}
+    for n in (1, 64, 65, 1000, 8192, 8193, 20000):
+        for _ in range(4):
+            v = np.ascontiguousarray(_rows(rng, kind, n), dtype=np.float32)
+            with np.errstate(invalid="ignore"):
+                want = float(np.cumsum(np.concatenate(([0.0], v.astype(np.float64))))[-1])
+                got = _spec_column(v, counts)
+            if math.isnan(want):
+                assert math.isnan(got), (kind, n)
+            else:
+                assert np.float64(got).tobytes() == np.float64(want).tobytes(), (kind, n, got, want)
+    if kind in ("normal", "uniform", "zeros"):
+        assert counts["segments"] > 0
+    if kind in ("tiny", "binades", "spread", "specials"):
+        assert counts["folds"] > 0
